@@ -1,0 +1,492 @@
+/*
+ * hbf_oracle.c -- CPU restatement of the HBFSim batched access-timing path.
+ *
+ * TEST INFRASTRUCTURE ONLY (see hbf_oracle.h).  Plain C, single file, built by
+ * oracle/Makefile into oracle/libhbf_oracle.so.  The shipped library never
+ * links or loads it.
+ */
+#include "hbf_oracle.h"
+
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define U64MAX UINT64_MAX
+
+/* hbf_device.cuh:946-950 */
+uint64_t or_saturating_add(uint64_t left, uint64_t right)
+{
+    return right > U64MAX - left ? U64MAX : left + right;
+}
+
+/* hbf_device.cuh:952-957 */
+uint64_t or_saturating_multiply(uint64_t left, uint32_t right)
+{
+    return right != 0 && left > U64MAX / right ? U64MAX : left * right;
+}
+
+/* hbf_device.cuh:746-757 (64-bit wrapping arithmetic, as the reference) */
+uint64_t or_fast_transfer_ns(uint32_t bytes, uint64_t bandwidth)
+{
+    if (bytes == 0 || bandwidth == 0) return 0;
+    const uint64_t numerator = (uint64_t)bytes * 1000000000ULL;
+    return (numerator + bandwidth - 1) / bandwidth;
+}
+
+/* hbf_device.cuh:797-817: the later of latency and transfer, not the sum */
+uint64_t or_fast_service_ns(uint64_t base_latency, uint32_t bytes,
+                            uint64_t bandwidth)
+{
+    const uint64_t transfer = or_fast_transfer_ns(bytes, bandwidth);
+    return transfer > base_latency ? transfer : base_latency;
+}
+
+/* hbf_device.cuh:826-841: upper-bound binary search on sorted bases */
+uint32_t or_find_range_index(const or_range* ranges, uint32_t count,
+                             uint64_t address)
+{
+    uint32_t first = 0, last = count;
+    while (first < last) {
+        const uint32_t middle = first + (last - first) / 2;
+        if (ranges[middle].base <= address) first = middle + 1;
+        else last = middle;
+    }
+    return first == 0 ? count : first - 1;
+}
+
+/* hbf_device.cuh:843-862 */
+int or_access_supported(const or_range* r, uint64_t address, uint32_t bytes,
+                        uint32_t op)
+{
+    if (bytes == 0 || op > 1 || (r->mode != 1 && r->mode != 2) ||
+        r->page_bytes == 0 || r->page_bytes > UINT32_MAX ||
+        r->length > U64MAX - r->base || address < r->base ||
+        address - r->base >= r->length || bytes > U64MAX - address ||
+        address + bytes > r->base + r->length ||
+        (r->permissions & (1u << op)) == 0)
+        return 0;
+    const uint64_t offset = address - r->base;
+    const uint64_t last_offset = offset + bytes - 1;
+    return offset / r->page_bytes == last_offset / r->page_bytes;
+}
+
+/* hbf_device.cuh:873-884 */
+int or_range_overlaps(const or_range* r, uint64_t address, uint32_t bytes)
+{
+    if (bytes == 0 || r->length == 0 || r->base > U64MAX - r->length ||
+        address > U64MAX - bytes)
+        return 0;
+    return address < r->base + r->length && r->base < address + bytes;
+}
+
+/* hbf_device.cuh:929-944 */
+int or_media_descriptor(const or_range* r, uint64_t address, uint32_t bytes,
+                        uint32_t op, uint64_t* logical_address,
+                        uint32_t* media_bytes)
+{
+    if (!or_access_supported(r, address, bytes, op)) return 0;
+    const uint64_t page_offset =
+        ((address - r->base) / r->page_bytes) * r->page_bytes;
+    if (page_offset > U64MAX - r->file_offset) return 0;
+    *logical_address = r->file_offset + page_offset;
+    *media_bytes = (uint32_t)r->page_bytes;
+    return 1;
+}
+
+/* hbf_device.cuh:729-744 */
+static uint64_t or_fast_hash(uint64_t value)
+{
+    value += 0x9e3779b97f4a7c15ULL;
+    value = (value ^ (value >> 30)) * 0xbf58476d1ce4e5b9ULL;
+    value = (value ^ (value >> 27)) * 0x94d049bb133111ebULL;
+    return value ^ (value >> 31);
+}
+
+int or_hybrid_reference_sample(uint64_t sequence, uint32_t warmup,
+                               uint64_t threshold, uint64_t key)
+{
+    return sequence < warmup ||
+           (threshold != 0 && or_fast_hash(sequence ^ key) <= threshold);
+}
+
+/* Classification of one access, restating the order of checks in
+ * __hbfsim_resolve (hbf_device.cu:997-1003 zero bytes, 1083-1127 lookup,
+ * straddle into the successor range and bypass, 1152-1179 media descriptor).
+ * Capacity-mode ranges go through the capacity path, not the timing batch. */
+static uint32_t or_classify(const or_range* ranges, uint32_t count,
+                            uint64_t address, uint32_t bytes, uint32_t op,
+                            uint32_t* range_index, uint64_t* media)
+{
+    *range_index = count;
+    *media = 0;
+    if (bytes == 0) return OR_STATUS_UNSUPPORTED;
+    const uint32_t index = or_find_range_index(ranges, count, address);
+    if (index == count || address < ranges[index].base ||
+        address - ranges[index].base >= ranges[index].length) {
+        const uint32_t successor = index == count ? 0u : index + 1u;
+        if (successor < count &&
+            or_range_overlaps(&ranges[successor], address, bytes))
+            return OR_STATUS_UNSUPPORTED;
+        return OR_STATUS_BYPASS;
+    }
+    uint32_t media_bytes = 0;
+    if (!or_media_descriptor(&ranges[index], address, bytes, op, media,
+                             &media_bytes))
+        return OR_STATUS_UNSUPPORTED;
+    if (ranges[index].mode != 1) return OR_STATUS_UNSUPPORTED;
+    *range_index = index;
+    return OR_STATUS_MODELED;
+}
+
+/* Stripe decode (builder-fixed semantics; parity unpinned).
+ *   m  = file_offset + (address - base)         media byte offset
+ *   u  = m / stripe_bytes                        stripe unit
+ *   u is split as a mixed-radix number in the profile's allocation order,
+ *   fastest letter first (CWDP: channel, way, die, plane), radices
+ *   C = stacks * channels_per_stack, W = 1, D = dies, P = planes.  The rest is
+ *   the row inside the plane.  Global channel g: stack = g % stacks,
+ *   channel-in-stack = g / stacks (the page-stripe placement of
+ *   src/ucie/stack_router.cpp:205-218).  Page inside the plane =
+ *   (row * stripe + m % stripe) / page_bytes. */
+static void or_decode_one(const or_geometry* g, uint64_t m, or_decoded* d)
+{
+    uint64_t radix[4];
+    radix[0] = (uint64_t)g->stacks * g->channels_per_stack;
+    radix[1] = 1;
+    radix[2] = g->dies_per_channel;
+    radix[3] = g->planes_per_die;
+    uint64_t digit[4] = {0, 0, 0, 0};
+    uint64_t u = m / g->stripe_bytes;
+    for (int k = 0; k < 4; ++k) {
+        const int letter = g->order[k];
+        digit[letter] = u % radix[letter];
+        u /= radix[letter];
+    }
+    d->channel = (uint32_t)digit[0];
+    d->stack = (uint32_t)(digit[0] % g->stacks);
+    d->die = (uint32_t)digit[2];
+    d->plane = (uint32_t)digit[3];
+    d->page = (u * g->stripe_bytes + m % g->stripe_bytes) / g->page_bytes;
+}
+
+void or_decode_batch(const or_range* ranges, uint32_t count,
+                     const or_geometry* g, const uint64_t* address,
+                     const uint32_t* bytes, const uint8_t* op, uint64_t n,
+                     or_decoded* out)
+{
+    for (uint64_t i = 0; i < n; ++i) {
+        or_decoded d;
+        memset(&d, 0, sizeof d);
+        uint64_t media = 0;
+        d.status = or_classify(ranges, count, address[i], bytes[i], op[i],
+                               &d.range_index, &media);
+        d.media_address = media;
+        if (d.status == OR_STATUS_MODELED) {
+            const or_range* r = &ranges[d.range_index];
+            or_decode_one(g, r->file_offset + (address[i] - r->base), &d);
+            if (g->shard_count > 1 &&
+                d.channel % g->shard_count != g->shard_rank)
+                d.status = OR_STATUS_FOREIGN;
+        }
+        out[i] = d;
+    }
+}
+
+/* ceil(bytes * 1e9 / bandwidth), exact (128-bit). */
+static uint64_t or_channel_transfer_ns(uint32_t bytes, uint64_t bandwidth)
+{
+    if (bytes == 0 || bandwidth == 0) return 0;
+    const unsigned __int128 num = (unsigned __int128)bytes * 1000000000ULL;
+    const unsigned __int128 q = (num + bandwidth - 1) / bandwidth;
+    return q > U64MAX ? U64MAX : (uint64_t)q;
+}
+
+/* ---- ordering: (arrival, index), stable ---- */
+static const uint64_t* g_sort_arrival;
+static int or_cmp_index(const void* a, const void* b)
+{
+    const uint64_t ia = *(const uint64_t*)a, ib = *(const uint64_t*)b;
+    const uint64_t aa = g_sort_arrival[ia], ab = g_sort_arrival[ib];
+    if (aa != ab) return aa < ab ? -1 : 1;
+    return ia < ib ? -1 : (ia > ib ? 1 : 0);
+}
+
+static uint64_t* or_arrival_order(const uint64_t* arrival, uint64_t n)
+{
+    uint64_t* order = (uint64_t*)malloc(sizeof(uint64_t) * (n ? n : 1));
+    if (!order) return NULL;
+    int sorted = 1;
+    for (uint64_t i = 0; i < n; ++i) {
+        order[i] = i;
+        if (i && arrival[i] < arrival[i - 1]) sorted = 0;
+    }
+    if (!sorted) {
+        g_sort_arrival = arrival;
+        qsort(order, n, sizeof(uint64_t), or_cmp_index);
+    }
+    return order;
+}
+
+/* FAST model step: hbf_device.cu:883-910 (tail CAS loop and target), with the
+ * access's arrival tick in place of %globaltimer. */
+static uint64_t or_fast_step(uint64_t* tail, uint64_t arrival, uint64_t x,
+                             uint64_t latency_scaled)
+{
+    const uint64_t start = *tail > arrival ? *tail : arrival;
+    *tail = or_saturating_add(start, x);
+    const uint64_t latency_target = or_saturating_add(arrival, latency_scaled);
+    return latency_target > *tail ? latency_target : *tail;
+}
+
+/* DIE model step (builder-fixed semantics, parity unpinned):
+ *   start = max(arrival, channel_free, die_free[d])
+ *   channel_free = start + X          (channel carries command + data)
+ *   die_free[d]  = channel_free + T   (die runs tR / tPROG)
+ *   done = die_free[d]                                        */
+static uint64_t or_die_step(uint64_t* chan, uint64_t* die, uint64_t arrival,
+                            uint64_t x, uint64_t t)
+{
+    uint64_t start = arrival;
+    if (*chan > start) start = *chan;
+    if (*die > start) start = *die;
+    *chan = or_saturating_add(start, x);
+    *die = or_saturating_add(*chan, t);
+    return *die;
+}
+
+typedef struct or_job {
+    const or_range* ranges;
+    const or_geometry* g;
+    const or_timing* t;
+    const uint64_t* chan_bw;
+    const uint64_t* t_read;
+    const uint64_t* t_prog;
+    const uint32_t* bytes;
+    const uint8_t* op;
+    const uint64_t* arrival;
+    const or_decoded* dec;
+    const uint64_t* order;      /* modeled accesses in (arrival, index) order */
+    uint64_t order_n;
+    uint64_t* state;
+    uint64_t* done;
+    uint64_t* latency;
+    uint32_t channel_begin, channel_end;  /* local channels this job owns */
+    uint64_t latency_sum;
+    uint64_t max_done;
+    uint64_t fast_modeled_ns;
+} or_job;
+
+static void or_run_job(or_job* j)
+{
+    const or_geometry* g = j->g;
+    const or_timing* t = j->t;
+    const uint32_t dies = g->dies_per_channel;
+    const uint32_t shards = g->shard_count ? g->shard_count : 1;
+    for (uint64_t k = 0; k < j->order_n; ++k) {
+        const uint64_t i = j->order[k];
+        const or_decoded* d = &j->dec[i];
+        const uint64_t a = j->arrival[i];
+        uint64_t done;
+        if (t->model == OR_MODEL_FAST) {
+            const or_range* r = &j->ranges[d->range_index];
+            const uint64_t base = j->op[i] ? t->program_latency_ns
+                                           : t->read_latency_ns;
+            const uint64_t x = or_saturating_multiply(
+                or_fast_transfer_ns((uint32_t)r->page_bytes,
+                                    t->aggregate_bandwidth),
+                t->time_scale);
+            done = or_fast_step(&j->state[0], a, x,
+                                or_saturating_multiply(base, t->time_scale));
+            j->fast_modeled_ns += or_fast_service_ns(
+                base, (uint32_t)r->page_bytes, t->aggregate_bandwidth);
+        } else {
+            const uint32_t c = d->channel / shards;
+            if (c < j->channel_begin || c >= j->channel_end) continue;
+            uint64_t* st = &j->state[(uint64_t)c * (dies + 1)];
+            const uint64_t x = or_saturating_multiply(
+                or_channel_transfer_ns(j->bytes[i], j->chan_bw[c]),
+                t->time_scale);
+            const uint64_t top = j->op[i] ? j->t_prog[d->stack]
+                                          : j->t_read[d->stack];
+            const uint64_t tt = or_saturating_multiply(top, t->time_scale);
+            done = or_die_step(&st[0], &st[1 + d->die], a, x, tt);
+        }
+        j->done[i] = done;
+        j->latency[i] = done - a;
+        j->latency_sum = or_saturating_add(j->latency_sum, done - a);
+        if (done > j->max_done) j->max_done = done;
+    }
+}
+
+static void* or_thread_main(void* arg)
+{
+    or_run_job((or_job*)arg);
+    return NULL;
+}
+
+int or_run_batch_threads(const or_range* ranges, uint32_t count,
+                         const or_geometry* g, const or_timing* t,
+                         const uint64_t* chan_bw, const uint64_t* t_read,
+                         const uint64_t* t_prog, const uint64_t* address,
+                         const uint32_t* bytes, const uint8_t* op,
+                         const uint64_t* arrival, uint64_t n, uint64_t* state,
+                         uint64_t* done, uint64_t* latency, uint8_t* status,
+                         or_stats* stats, int threads)
+{
+    memset(stats, 0, sizeof *stats);
+    or_decoded* dec = (or_decoded*)malloc(sizeof(or_decoded) * (n ? n : 1));
+    if (!dec) return -1;
+    or_decode_batch(ranges, count, g, address, bytes, op, n, dec);
+    uint64_t* order = or_arrival_order(arrival, n);
+    if (!order) { free(dec); return -1; }
+    uint64_t m = 0;
+    for (uint64_t k = 0; k < n; ++k) {
+        const uint64_t i = order[k];
+        status[i] = (uint8_t)dec[i].status;
+        done[i] = arrival[i];
+        latency[i] = 0;
+        switch (dec[i].status) {
+        case OR_STATUS_MODELED: order[m++] = i; break;
+        case OR_STATUS_BYPASS: stats->bypass++; break;
+        case OR_STATUS_FOREIGN: stats->foreign++; break;
+        default: stats->unsupported++; break;
+        }
+    }
+    stats->modeled = m;
+    const uint32_t shards = g->shard_count ? g->shard_count : 1;
+    const uint32_t channels_total = g->stacks * g->channels_per_stack;
+    const uint32_t local = (channels_total + shards - 1) / shards;
+    if (t->model == OR_MODEL_FAST || threads <= 1) threads = 1;
+    if ((uint32_t)threads > local) threads = (int)local;
+    or_job* jobs = (or_job*)calloc((size_t)threads, sizeof(or_job));
+    pthread_t* tids = (pthread_t*)calloc((size_t)threads, sizeof(pthread_t));
+    for (int k = 0; k < threads; ++k) {
+        or_job* j = &jobs[k];
+        j->ranges = ranges; j->g = g; j->t = t; j->chan_bw = chan_bw;
+        j->t_read = t_read; j->t_prog = t_prog; j->bytes = bytes; j->op = op;
+        j->arrival = arrival; j->dec = dec; j->order = order; j->order_n = m;
+        j->state = state; j->done = done; j->latency = latency;
+        j->channel_begin = (uint32_t)((uint64_t)local * k / threads);
+        j->channel_end = (uint32_t)((uint64_t)local * (k + 1) / threads);
+        if (t->model == OR_MODEL_FAST) { j->channel_begin = 0; j->channel_end = ~0u; }
+    }
+    if (threads == 1) {
+        or_run_job(&jobs[0]);
+    } else {
+        for (int k = 0; k < threads; ++k)
+            pthread_create(&tids[k], NULL, or_thread_main, &jobs[k]);
+        for (int k = 0; k < threads; ++k) pthread_join(tids[k], NULL);
+    }
+    for (int k = 0; k < threads; ++k) {
+        stats->latency_sum = or_saturating_add(stats->latency_sum,
+                                               jobs[k].latency_sum);
+        if (jobs[k].max_done > stats->max_done)
+            stats->max_done = jobs[k].max_done;
+        stats->fast_modeled_ns += jobs[k].fast_modeled_ns;
+    }
+    free(jobs); free(tids); free(order); free(dec);
+    return 0;
+}
+
+int or_run_batch(const or_range* ranges, uint32_t count, const or_geometry* g,
+                 const or_timing* t, const uint64_t* chan_bw,
+                 const uint64_t* t_read, const uint64_t* t_prog,
+                 const uint64_t* address, const uint32_t* bytes,
+                 const uint8_t* op, const uint64_t* arrival, uint64_t n,
+                 uint64_t* state, uint64_t* done, uint64_t* latency,
+                 uint8_t* status, or_stats* stats)
+{
+    return or_run_batch_threads(ranges, count, g, t, chan_bw, t_read, t_prog,
+                                address, bytes, op, arrival, n, state, done,
+                                latency, status, stats, 1);
+}
+
+/* ---- exact LRU (adapters/vllm_capacity/placement_policy.py:68-93) with the
+ * dirty tracking of CapacityPageService::resolve
+ * (src/host_service/capacity_page_service.cpp:97-210): a write marks the page
+ * dirty whether it hit or missed; an evicted dirty page must be programmed. */
+typedef struct { uint64_t key; int64_t node; } or_slot;
+
+static uint64_t or_mix(uint64_t x) { return or_fast_hash(x); }
+
+void or_lru_run(const uint64_t* pages, const uint8_t* writes, uint64_t n,
+                uint64_t frames, uint8_t* hit, uint64_t* victim,
+                uint8_t* victim_dirty)
+{
+    if (frames == 0) {
+        for (uint64_t i = 0; i < n; ++i) {
+            hit[i] = 0; victim[i] = U64MAX; victim_dirty[i] = 0;
+        }
+        return;
+    }
+    uint64_t cap = 16;
+    while (cap < frames * 2 + 16) cap <<= 1;
+    or_slot* table = (or_slot*)malloc(sizeof(or_slot) * cap);
+    for (uint64_t k = 0; k < cap; ++k) table[k].node = -1;
+    /* nodes: doubly linked list, head = most recent */
+    uint64_t* key = (uint64_t*)malloc(sizeof(uint64_t) * frames);
+    int64_t* prev = (int64_t*)malloc(sizeof(int64_t) * frames);
+    int64_t* next = (int64_t*)malloc(sizeof(int64_t) * frames);
+    uint8_t* dirty = (uint8_t*)malloc(frames);
+    int64_t head = -1, tail = -1;
+    uint64_t used = 0;
+    const uint64_t mask = cap - 1;
+#define OR_UNLINK(x) do { \
+        if (prev[x] >= 0) next[prev[x]] = next[x]; else head = next[x]; \
+        if (next[x] >= 0) prev[next[x]] = prev[x]; else tail = prev[x]; } while (0)
+#define OR_PUSH_FRONT(x) do { prev[x] = -1; next[x] = head; \
+        if (head >= 0) { prev[head] = x; } \
+        head = x; \
+        if (tail < 0) { tail = x; } } while (0)
+    for (uint64_t i = 0; i < n; ++i) {
+        const uint64_t p = pages[i];
+        uint64_t h = or_mix(p) & mask;
+        while (table[h].node >= 0 && table[h].key != p) h = (h + 1) & mask;
+        victim[i] = U64MAX;
+        victim_dirty[i] = 0;
+        if (table[h].node >= 0) {
+            const int64_t x = table[h].node;
+            hit[i] = 1;
+            if (writes[i]) dirty[x] = 1;
+            OR_UNLINK(x);
+            OR_PUSH_FRONT(x);
+            continue;
+        }
+        hit[i] = 0;
+        int64_t x;
+        if (used < frames) {
+            x = (int64_t)used++;
+        } else {
+            x = tail;
+            victim[i] = key[x];
+            victim_dirty[i] = dirty[x];
+            OR_UNLINK(x);
+            /* delete key[x] from the table (backward-shift deletion) */
+            uint64_t d = or_mix(key[x]) & mask;
+            while (table[d].key != key[x] || table[d].node != x)
+                d = (d + 1) & mask;
+            uint64_t hole = d, probe = (d + 1) & mask;
+            table[hole].node = -1;
+            while (table[probe].node >= 0) {
+                const uint64_t ideal = or_mix(table[probe].key) & mask;
+                const int moves = ((probe - ideal) & mask) >= ((probe - hole) & mask);
+                if (moves) {
+                    table[hole] = table[probe];
+                    table[probe].node = -1;
+                    hole = probe;
+                }
+                probe = (probe + 1) & mask;
+            }
+            h = or_mix(p) & mask;
+            while (table[h].node >= 0) h = (h + 1) & mask;
+        }
+        key[x] = p;
+        dirty[x] = writes[i] ? 1 : 0;
+        table[h].key = p;
+        table[h].node = x;
+        OR_PUSH_FRONT(x);
+    }
+#undef OR_UNLINK
+#undef OR_PUSH_FRONT
+    free(table); free(key); free(prev); free(next); free(dirty);
+}

@@ -1,0 +1,156 @@
+/*
+ * hbf_oracle.h -- CPU restatement of the HBFSim batched access-timing path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  Nothing in the shipped library links, loads or
+ * calls this code.  It is the checker that the CUDA path is compared against
+ * (tests/, __graft_entry__.smoke(), and bench.py's cpu_baseline leg only).
+ *
+ * Every function cites the reference file:line it restates.  Paths are
+ * relative to the HBFSim source tree.
+ *
+ * Parity status:
+ *   - range lookup / media descriptor / fast model arithmetic: pinned to the
+ *     reference (src/cuda_runtime/device/hbf_device.cuh) by golden vectors
+ *     produced from the reference headers compiled here (oracle/Makefile).
+ *   - per-die max-plus model, stripe decode, refresh/throttle scaling: the
+ *     reference has no implementation (MQSim is an absent submodule), so the
+ *     semantics are fixed by this build and written out below.  PARITY
+ *     UNPINNED for those parts.
+ */
+#ifndef HBF_ORACLE_H
+#define HBF_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Per-access status codes written by the batch path. */
+enum {
+    OR_STATUS_MODELED = 1,      /* timed by the model (reference: Ready)      */
+    OR_STATUS_UNSUPPORTED = 6,  /* rejected (reference: Unsupported)          */
+    OR_STATUS_BYPASS = 8,       /* outside every range: native HBM, untimed  */
+    OR_STATUS_FOREIGN = 9       /* belongs to another shard's channels       */
+};
+
+enum { OR_MODEL_FAST = 1, OR_MODEL_DIE = 3 };
+
+/* One registered range (the fields of SharedRangeRecord that the path reads,
+ * hbf_device.cuh:105-118). */
+typedef struct or_range {
+    uint64_t base;
+    uint64_t length;
+    uint64_t file_offset;
+    uint32_t range_id;
+    uint32_t mode;         /* 1 timing, 2 capacity */
+    uint32_t permissions;  /* bit0 read, bit1 write */
+    uint32_t reserved;
+    uint64_t page_bytes;
+} or_range;
+
+typedef struct or_geometry {
+    uint32_t stacks;
+    uint32_t channels_per_stack;
+    uint32_t dies_per_channel;
+    uint32_t planes_per_die;
+    uint32_t stripe_bytes;     /* power of two */
+    uint32_t page_bytes;
+    uint8_t order[4];          /* fastest-varying first: 0=C 1=W 2=D 3=P */
+    uint32_t shard_rank;       /* channel g belongs to shard g % shard_count */
+    uint32_t shard_count;
+} or_geometry;
+
+typedef struct or_timing {
+    uint32_t model;                 /* OR_MODEL_FAST or OR_MODEL_DIE */
+    uint32_t time_scale;
+    uint64_t read_latency_ns;
+    uint64_t program_latency_ns;
+    uint64_t aggregate_bandwidth;   /* bytes/s, FAST model */
+    uint64_t page_bytes;            /* FAST model transfer size */
+} or_timing;
+
+typedef struct or_decoded {
+    uint64_t media_address;  /* page-aligned media address (media_descriptor) */
+    uint64_t page;           /* page index inside the plane */
+    uint32_t status;
+    uint32_t range_index;
+    uint32_t stack;
+    uint32_t channel;        /* global channel, 0 .. stacks*channels-1 */
+    uint32_t die;
+    uint32_t plane;
+} or_decoded;
+
+typedef struct or_stats {
+    uint64_t modeled;
+    uint64_t bypass;
+    uint64_t unsupported;
+    uint64_t foreign;
+    uint64_t fast_modeled_ns;   /* sum of fast_service_ns (FAST model) */
+    uint64_t latency_sum;       /* saturating sum of latency, modeled only */
+    uint64_t max_done;          /* simulated time after the batch */
+} or_stats;
+
+/* ---- reference arithmetic (hbf_device.cuh) ---- */
+uint64_t or_saturating_add(uint64_t a, uint64_t b);
+uint64_t or_saturating_multiply(uint64_t a, uint32_t b);
+uint64_t or_fast_transfer_ns(uint32_t bytes, uint64_t bandwidth);
+uint64_t or_fast_service_ns(uint64_t base_latency, uint32_t bytes,
+                            uint64_t bandwidth);
+uint32_t or_find_range_index(const or_range* ranges, uint32_t count,
+                             uint64_t address);
+int or_access_supported(const or_range* r, uint64_t address, uint32_t bytes,
+                        uint32_t op);
+int or_range_overlaps(const or_range* r, uint64_t address, uint32_t bytes);
+int or_media_descriptor(const or_range* r, uint64_t address, uint32_t bytes,
+                        uint32_t op, uint64_t* logical_address,
+                        uint32_t* media_bytes);
+int or_hybrid_reference_sample(uint64_t sequence, uint32_t warmup,
+                               uint64_t threshold, uint64_t key);
+
+/* ---- classification + decode of a whole batch ---- */
+void or_decode_batch(const or_range* ranges, uint32_t count,
+                     const or_geometry* g, const uint64_t* address,
+                     const uint32_t* bytes, const uint8_t* op, uint64_t n,
+                     or_decoded* out);
+
+/* ---- timing ----
+ * state layout (uint64 each):
+ *   FAST: state[0] = fast channel tail
+ *   DIE : per local channel c: state[c*(D+1)] = channel free,
+ *         state[c*(D+1)+1+d] = die d free.
+ * chan_bw[c]: effective channel bandwidth of local channel c (DIE only).
+ * t_read[s], t_prog[s]: die op times of stack s, already throttled (DIE).
+ */
+int or_run_batch(const or_range* ranges, uint32_t count, const or_geometry* g,
+                 const or_timing* t, const uint64_t* chan_bw,
+                 const uint64_t* t_read, const uint64_t* t_prog,
+                 const uint64_t* address, const uint32_t* bytes,
+                 const uint8_t* op, const uint64_t* arrival, uint64_t n,
+                 uint64_t* state, uint64_t* done, uint64_t* latency,
+                 uint8_t* status, or_stats* stats);
+
+/* Multithreaded variant of the DIE model, sharded by channel over host
+ * threads (channels are independent).  Same results as or_run_batch. */
+int or_run_batch_threads(const or_range* ranges, uint32_t count,
+                         const or_geometry* g, const or_timing* t,
+                         const uint64_t* chan_bw, const uint64_t* t_read,
+                         const uint64_t* t_prog, const uint64_t* address,
+                         const uint32_t* bytes, const uint8_t* op,
+                         const uint64_t* arrival, uint64_t n, uint64_t* state,
+                         uint64_t* done, uint64_t* latency, uint8_t* status,
+                         or_stats* stats, int threads);
+
+/* ---- capacity mode: exact LRU over frames (placement_policy.py:68-93) ----
+ * pages[i]: logical page of access i, writes[i]: 1 for a write.
+ * Outputs per access: hit (1/0), victim page (UINT64_MAX if none),
+ * victim_dirty (1 if the evicted page had been written while resident). */
+void or_lru_run(const uint64_t* pages, const uint8_t* writes, uint64_t n,
+                uint64_t frames, uint8_t* hit, uint64_t* victim,
+                uint8_t* victim_dirty);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,171 @@
+"""Regenerate the golden fixtures in this directory from the HBFSim reference.
+
+Run in a container that holds the HBFSim source tree (default
+/root/reference, override with HBFSIM_REFERENCE):
+
+    make -C oracle            # builds oracle/_ref/ref_goldens from reference sources
+    python tests/golden/make_goldens.py
+
+Fixtures written:
+  device_goldens.jsonl   range lookup / access_supported / media_descriptor,
+                         fast_transfer_ns, fast_service_ns (device and host),
+                         saturating arithmetic, hybrid sampler bit and
+                         fast-model traces, all computed by the reference's own
+                         functions (src/cuda_runtime/device/hbf_device.cuh,
+                         src/hybrid/calibrator.cpp).
+  thermal_goldens.json   layered RC grids built by the reference exporter
+                         (tools/eq3_layered_export.py discretize()/network())
+                         and advanced by the reference ThermalModel
+                         (src/eq3_thermal/thermal.cpp, backward Euler with
+                         dense Cholesky).
+
+Nothing at test time reads the reference tree: the tests read only these
+fixtures.
+"""
+from __future__ import annotations
+
+import importlib.util
+import json
+import os
+import random
+import subprocess
+import sys
+import tempfile
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+REF = Path(os.environ.get("HBFSIM_REFERENCE", "/root/reference"))
+REF_BIN = REPO / "oracle" / "_ref" / "ref_goldens"
+
+
+def load_exporter():
+    path = REF / "tools" / "eq3_layered_export.py"
+    spec = importlib.util.spec_from_file_location("eq3_layered_export", path)
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
+def device_goldens() -> None:
+    out = subprocess.run([str(REF_BIN), "device"], check=True,
+                         capture_output=True, text=True).stdout
+    (HERE / "device_goldens.jsonl").write_text(out)
+
+
+def layered_ir(stack: dict) -> dict:
+    """The layer-stack description used by this build, written as the
+    exporter's package IR: one full-footprint component per layer."""
+    nx, ny, cell = stack["nx"], stack["ny"], stack["cell_m"]
+    z = 0.0
+    components, materials = [], {}
+    for index, layer in enumerate(stack["layers"]):
+        name = f"mat{index}"
+        materials[name] = {"cv_j_m3_k": layer["cv_j_m3_k"],
+                           "k_xyz_w_m_k": layer["k_xyz_w_m_k"]}
+        components.append({"id": f"layer{index:02d}", "material": name,
+                           "xyz_m": [0.0, 0.0, z],
+                           "size_m": [nx * cell, ny * cell, layer["thickness_m"]],
+                           "powered": True, "physical_type": "HBF"})
+        z += layer["thickness_m"]
+    return {"package_size_m": [nx * cell, ny * cell, z],
+            "components": components, "materials": materials,
+            "boundaries": {"bottom": stack["bottom"], "top": stack["top"],
+                           "initial_temperature_k": stack["initial_k"]}}
+
+
+def thermal_case(exporter, stack: dict, steps: int, dt: float, seed: int) -> dict:
+    ir = layered_ir(stack)
+    grid = exporter.discretize(ir, stack["cell_m"])
+    edges, boundaries = exporter.network(ir, grid)
+    cells = grid["cells"]
+    rng = random.Random(seed)
+    n = len(cells)
+    powers = []
+    for _ in range(steps):
+        row = [0.0] * n
+        for i in range(n):
+            if rng.random() < 0.4:
+                row[i] = rng.uniform(0.0, 0.05)
+        powers.append(row)
+    lines = [f"nodes {n}"]
+    for c, (g, t) in zip(cells, boundaries):
+        lines.append(f"{c['capacity_j_k']!r} {g!r} {t!r} {stack['initial_k']!r} 0")
+    lines.append(f"edges {len(edges)}")
+    lines += [f"{i} {j} {g!r}" for i, j, g in edges]
+    lines.append(f"steps {steps} {dt!r}")
+    lines += [" ".join(repr(p) for p in row) for row in powers]
+    with tempfile.NamedTemporaryFile("w", suffix=".net", delete=False) as f:
+        f.write("\n".join(lines) + "\n")
+        path = f.name
+    try:
+        out = subprocess.run([str(REF_BIN), "thermal", path], check=True,
+                             capture_output=True, text=True).stdout
+    finally:
+        os.unlink(path)
+    temps = [[float(v) for v in line.split()[2:]] for line in out.splitlines()]
+    return {"stack": stack, "dt": dt, "steps": steps, "power_w": powers,
+            "temperature_k": temps, "shape": grid["shape"],
+            "edge_count": len(edges)}
+
+
+def thermal_goldens() -> None:
+    exporter = load_exporter()
+    silicon = {"cv_j_m3_k": 1.66e6, "k_xyz_w_m_k": [148.0, 148.0, 148.0]}
+    nand = {"cv_j_m3_k": 1.75e6, "k_xyz_w_m_k": [110.0, 110.0, 35.0]}
+    cases = []
+    stack_a = {"nx": 6, "ny": 5, "cell_m": 1.0e-3, "initial_k": 318.15,
+               "layers": [dict(silicon, thickness_m=100e-6),
+                          dict(nand, thickness_m=50e-6),
+                          dict(nand, thickness_m=50e-6)],
+               "bottom": {"h_w_m2_k": 0.0, "ambient_k": 318.15},
+               "top": {"h_w_m2_k": 2.0e4, "ambient_k": 318.15}}
+    cases.append(thermal_case(exporter, stack_a, steps=6, dt=1e-3, seed=1))
+    stack_b = {"nx": 8, "ny": 8, "cell_m": 0.5e-3, "initial_k": 330.0,
+               "layers": [dict(silicon, thickness_m=80e-6)] +
+                         [dict(nand, thickness_m=40e-6) for _ in range(4)],
+               "bottom": {"h_w_m2_k": 500.0, "ambient_k": 310.0},
+               "top": {"h_w_m2_k": 1.5e4, "ambient_k": 318.15}}
+    cases.append(thermal_case(exporter, stack_b, steps=5, dt=2e-3, seed=2))
+    (HERE / "thermal_goldens.json").write_text(json.dumps(cases))
+
+
+def lru_goldens() -> None:
+    """Exact-LRU victims from the reference's offline policy
+    (adapters/vllm_capacity/placement_policy.py LruCache)."""
+    sys.path.insert(0, str(REF / "adapters" / "vllm_capacity"))
+    from placement_policy import LruCache  # noqa: E402  (reference code)
+    rng = random.Random(7)
+    cases = []
+    for frames, universe, length in ((0, 5, 40), (1, 4, 60), (2, 3, 50),
+                                     (16, 40, 3000), (100, 150, 6000),
+                                     (64, 1000, 4000)):
+        keys = []
+        for _ in range(length):
+            if rng.random() < 0.5 and keys:
+                keys.append(keys[-1 - rng.randrange(min(len(keys), 32))])
+            else:
+                keys.append(rng.randrange(universe))
+        cache = LruCache(frames)
+        hits, victims = [], []
+        for position, key in enumerate(keys):
+            result = cache.access((0, key), position)
+            hits.append(1 if result.hit else 0)
+            victims.append(-1 if result.evicted is None else result.evicted[1])
+        cases.append({"frames": frames, "keys": keys, "hits": hits,
+                      "victims": victims})
+    (HERE / "lru_goldens.json").write_text(json.dumps(cases))
+
+
+def main() -> int:
+    if not REF_BIN.exists():
+        print("build oracle/_ref/ref_goldens first (make -C oracle)", file=sys.stderr)
+        return 2
+    device_goldens()
+    thermal_goldens()
+    lru_goldens()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
