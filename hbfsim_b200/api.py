@@ -1,0 +1,223 @@
+"""Python host side of the B200 access-timing path.
+
+`Context` mirrors the reference C API (include/hbfsim/api.h:92-107) call for
+call -- context_create, register_device, flush, get_stats, unregister,
+context_destroy -- and adds the batch exports of include/hbfsim/batch_v1.h.
+Errors raise HbfsimError carrying the hbfsim_error code, the way the
+reference vLLM loader turns a non-zero status into an exception
+(adapters/vllm/hbfsim_loader.py:287-380).  torch is used only to hand device
+buffers and streams to the library.
+"""
+from __future__ import annotations
+
+import ctypes
+import tempfile
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib
+from ._lib import HbfsimError, check
+
+__all__ = ["Context", "HbfsimError", "BatchResult"]
+
+
+@dataclass
+class BatchResult:
+    done_ns: object
+    latency_ns: object
+    status: object
+
+
+def _ptr(t) -> int:
+    if t is None:
+        return 0
+    if isinstance(t, np.ndarray):
+        return t.ctypes.data
+    return t.data_ptr()
+
+
+class Context:
+    """One hbfsim context bound to the current CUDA device."""
+
+    def __init__(self, profile_path: str, report_dir: str | None = None,
+                 mode: int = _lib.MODEL_DIE, ring_capacity: int = 64,
+                 request_timeout_ns: int = 1_000_000_000):
+        self._lib = _lib.load()
+        self._tmp = None
+        if report_dir is None:
+            self._tmp = tempfile.TemporaryDirectory(prefix="hbfsim-report-")
+            report_dir = self._tmp.name
+        opts = _lib.Options(str(profile_path).encode(), str(report_dir).encode(),
+                            mode, ring_capacity, request_timeout_ns)
+        handle = ctypes.c_void_p()
+        check(self._lib.hbfsim_context_create(ctypes.byref(opts), ctypes.byref(handle)),
+              "hbfsim_context_create")
+        self.handle = handle
+        self.mode = mode
+
+    # ---- reference API -------------------------------------------------
+    def register_device(self, base: int, length: int, mode: int = _lib.RANGE_TIMING,
+                        permissions: int = _lib.READ_WRITE, cache_policy: int = 0,
+                        stream_id: int = 0) -> None:
+        o = _lib.RangeOptions(mode, permissions, cache_policy, stream_id)
+        check(self._lib.hbfsim_register_device(self.handle, ctypes.c_void_p(base),
+                                               length, ctypes.byref(o)),
+              "hbfsim_register_device")
+
+    def unregister(self, base: int) -> None:
+        check(self._lib.hbfsim_unregister(self.handle, ctypes.c_void_p(base)),
+              "hbfsim_unregister")
+
+    def flush(self) -> None:
+        check(self._lib.hbfsim_flush(self.handle), "hbfsim_flush")
+
+    def get_stats(self) -> dict:
+        s = _lib.Stats()
+        check(self._lib.hbfsim_get_stats(self.handle, ctypes.byref(s)), "hbfsim_get_stats")
+        return {f: getattr(s, f) for f, _ in _lib.Stats._fields_}
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self._lib.hbfsim_context_destroy(self.handle)
+            self.handle = None
+        if self._tmp is not None:
+            self._tmp.cleanup()
+            self._tmp = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- batch_v1 -------------------------------------------------------
+    def set_geometry(self, stacks: int = 1, stripe_bytes: int = 0, shard_rank: int = 0,
+                     shard_count: int = 1) -> None:
+        g = _lib.GeometryV1(ctypes.sizeof(_lib.GeometryV1), 1, stacks, stripe_bytes,
+                            shard_rank, shard_count)
+        check(self._lib.hbfsim_set_geometry_v1(self.handle, ctypes.byref(g)),
+              "hbfsim_set_geometry_v1")
+
+    @staticmethod
+    def _batch(count, address, nbytes, op, arrival, done, latency, status):
+        return _lib.AccessBatchV1(ctypes.sizeof(_lib.AccessBatchV1), 1, count,
+                                  _ptr(address), _ptr(nbytes), _ptr(op), _ptr(arrival),
+                                  _ptr(done), _ptr(latency), _ptr(status))
+
+    def submit(self, address, nbytes, op, arrival, out: BatchResult | None = None,
+               stream=None) -> BatchResult:
+        """Time a batch held in device tensors (uint64/int64 address and
+        arrival, int32 bytes, uint8 op).  Asynchronous on `stream`."""
+        import torch
+        n = address.numel()
+        if out is None:
+            dev = address.device
+            out = BatchResult(torch.empty(n, dtype=torch.int64, device=dev),
+                              torch.empty(n, dtype=torch.int64, device=dev),
+                              torch.empty(n, dtype=torch.uint8, device=dev))
+        b = self._batch(n, address, nbytes, op, arrival, out.done_ns, out.latency_ns,
+                        out.status)
+        s = stream.cuda_stream if stream is not None else torch.cuda.current_stream().cuda_stream
+        check(self._lib.hbfsim_submit_access_batch_v1(self.handle, ctypes.byref(b),
+                                                      ctypes.c_void_p(s)),
+              "hbfsim_submit_access_batch_v1")
+        return out
+
+    def submit_host(self, address, nbytes, op, arrival, out: BatchResult | None = None
+                    ) -> BatchResult:
+        """Time a batch held in host memory (numpy arrays or pinned CPU
+        tensors); copies are pipelined inside the library.  Synchronous."""
+        n = int(address.shape[0])
+        if out is None:
+            out = BatchResult(np.empty(n, np.uint64), np.empty(n, np.uint64),
+                              np.empty(n, np.uint8))
+        b = self._batch(n, address, nbytes, op, arrival, out.done_ns, out.latency_ns,
+                        out.status)
+        check(self._lib.hbfsim_submit_access_batch_host_v1(self.handle, ctypes.byref(b)),
+              "hbfsim_submit_access_batch_host_v1")
+        return out
+
+    def reset_state(self, stream=None) -> None:
+        """Idle every die and channel at tick 0 (asynchronous on `stream`)."""
+        import torch
+        s = stream.cuda_stream if stream is not None else torch.cuda.current_stream().cuda_stream
+        check(self._lib.hbfsim_reset_state_v1(self.handle, ctypes.c_void_p(s)),
+              "hbfsim_reset_state_v1")
+
+    def set_profiling(self, enable: bool) -> None:
+        check(self._lib.hbfsim_set_profiling_v1(self.handle, 1 if enable else 0),
+              "hbfsim_set_profiling_v1")
+
+    def kernel_times(self) -> dict:
+        """{slot: (launches, total_ms)} since the last call; synchronizes."""
+        k = _lib.KernelTimesV1(ctypes.sizeof(_lib.KernelTimesV1), 1)
+        check(self._lib.hbfsim_get_kernel_times_v1(self.handle, ctypes.byref(k)),
+              "hbfsim_get_kernel_times_v1")
+        return {name: (k.launches[i], k.total_ms[i]) for i, name in enumerate(_lib.KERNEL_SLOTS)}
+
+    def simulated_time(self) -> int:
+        v = ctypes.c_uint64()
+        check(self._lib.hbfsim_get_simulated_time_v1(self.handle, ctypes.byref(v)),
+              "hbfsim_get_simulated_time_v1")
+        return v.value
+
+    def batch_stats(self) -> dict:
+        s = _lib.BatchStatsV1(ctypes.sizeof(_lib.BatchStatsV1), 1)
+        check(self._lib.hbfsim_get_batch_stats_v1(self.handle, ctypes.byref(s)),
+              "hbfsim_get_batch_stats_v1")
+        return {f: getattr(s, f) for f, _ in _lib.BatchStatsV1._fields_[2:]}
+
+    def decode(self, address, nbytes, op, stream=None):
+        """Range lookup + stripe decode of device tensors; returns a uint8
+        device tensor viewed as hbfsim_decoded_v1 records (40 bytes each)."""
+        import torch
+        n = address.numel()
+        out = torch.empty(n * ctypes.sizeof(_lib.DecodedV1), dtype=torch.uint8,
+                          device=address.device)
+        s = stream.cuda_stream if stream is not None else torch.cuda.current_stream().cuda_stream
+        check(self._lib.hbfsim_decode_batch_v1(self.handle, _ptr(address), _ptr(nbytes),
+                                               _ptr(op), n, _ptr(out), ctypes.c_void_p(s)),
+              "hbfsim_decode_batch_v1")
+        return out
+
+    def set_channel_factors(self, refresh_permille=None, throttle_permille=None,
+                            admit_after_ns=None) -> None:
+        r = None if refresh_permille is None else np.ascontiguousarray(refresh_permille, np.uint32)
+        t = None if throttle_permille is None else np.ascontiguousarray(throttle_permille, np.uint32)
+        a = None if admit_after_ns is None else np.ascontiguousarray(admit_after_ns, np.uint64)
+        check(self._lib.hbfsim_set_channel_factors_v1(self.handle, _ptr(r), _ptr(t), _ptr(a)),
+              "hbfsim_set_channel_factors_v1")
+
+    def channel_factors(self, channels: int, stacks: int):
+        r = np.zeros(channels, np.uint32)
+        t = np.zeros(stacks, np.uint32)
+        a = np.zeros(stacks, np.uint64)
+        check(self._lib.hbfsim_get_channel_factors_v1(self.handle, _ptr(r), _ptr(t), _ptr(a)),
+              "hbfsim_get_channel_factors_v1")
+        return r, t, a
+
+    def state_words(self) -> int:
+        return int(self._lib.hbfsim_state_words_v1(self.handle))
+
+    def get_state(self) -> np.ndarray:
+        w = np.zeros(self.state_words(), np.uint64)
+        check(self._lib.hbfsim_get_state_v1(self.handle, _ptr(w), w.size), "hbfsim_get_state_v1")
+        return w
+
+    def set_state(self, words: np.ndarray) -> None:
+        w = np.ascontiguousarray(words, np.uint64)
+        check(self._lib.hbfsim_set_state_v1(self.handle, _ptr(w), w.size), "hbfsim_set_state_v1")
+
+    def die_activity(self, dies_total: int):
+        rb = np.zeros(dies_total, np.uint64)
+        wr = np.zeros(dies_total, np.uint64)
+        check(self._lib.hbfsim_get_die_activity_v1(self.handle, _ptr(rb), _ptr(wr), dies_total),
+              "hbfsim_get_die_activity_v1")
+        return rb, wr

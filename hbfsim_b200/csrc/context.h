@@ -1,0 +1,97 @@
+// context.h -- the hbfsim_context object behind the C ABI (internal).
+#pragma once
+
+#include "../../include/hbfsim/batch_v1.h"
+#include "profile.h"
+#include "timing.h"
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+namespace hbfb {
+struct ThermalState;  // thermal.cu
+}
+
+struct hbfsim_context {
+    hbfb::Profile profile;
+    std::string report_dir;
+    std::uint32_t mode = 0;            // hbfsim_options.mode
+    std::uint64_t request_timeout_ns = 0;
+    int device = 0;
+    int sm_count = 148;
+    cudaStream_t stream = nullptr;
+    std::mutex mu;
+
+    // ranges (host copy sorted by base; device copy mirrors it)
+    std::vector<hbfb::DevRange> ranges;
+    std::uint64_t next_file_offset = 0;
+    std::uint32_t next_range_id = 1;
+    hbfb::DevRange* d_ranges = nullptr;
+    std::uint32_t d_range_capacity = 0;
+
+    // geometry
+    std::uint32_t stacks = 1;
+    std::uint32_t stripe_bytes = 0;
+    std::uint32_t shard_rank = 0;
+    std::uint32_t shard_count = 1;
+    std::uint32_t channels_total = 0;  // stacks * profile.channels
+    std::uint32_t C = 0;               // local channels (state rows)
+    std::uint32_t D = 0;               // dies per channel (die model)
+    std::uint32_t K = 0;               // state words per channel
+    std::uint8_t order[4] = {0, 1, 2, 3};
+
+    // timing state, double-buffered: batches read cur, write 1-cur
+    std::uint64_t* d_state[2] = {nullptr, nullptr};
+    int cur = 0;
+    std::uint64_t state_words_allocated = 0;
+
+    // per-batch scratch
+    hbfb::i64* d_agg = nullptr;
+    hbfb::i64* d_incoming = nullptr;
+    std::uint64_t scratch_ctas = 0;
+    std::uint32_t* d_error = nullptr;
+    std::uint64_t* d_last_arrival = nullptr;
+    hbfb::DevCounters* d_counters = nullptr;
+    std::uint64_t errors_reported = 0;
+
+    // channel factor tables (device, per local channel) + host inputs
+    std::uint64_t* d_chan_bw = nullptr;
+    hbfb::i64* d_t_read = nullptr;
+    hbfb::i64* d_t_prog = nullptr;
+    hbfb::i64* d_admit = nullptr;
+    std::vector<std::uint32_t> refresh_permille;   // per local channel
+    std::vector<std::uint32_t> throttle_permille;  // per stack
+    std::vector<std::uint64_t> admit_after;        // per stack
+    std::uint64_t x_max = 0;   // largest transfer tick of any access (scaled)
+    std::uint64_t t_max = 0;   // largest die op tick (scaled, throttled)
+    std::uint64_t admit_max = 0;
+
+    // per-die activity since the last epoch (die model), index c*D+d
+    unsigned long long* d_die_read_bytes = nullptr;
+    unsigned long long* d_die_writes = nullptr;
+
+    // host-buffer pipeline
+    cudaStream_t copy_in = nullptr;
+    cudaStream_t copy_out = nullptr;
+    void* d_stage[2] = {nullptr, nullptr};
+    std::uint64_t stage_capacity = 0;  // accesses per stage
+
+    hbfb::ThermalState* thermal = nullptr;
+
+    // launch profiling (event pairs per kernel slot)
+    bool profiling = false;
+    struct Mark {
+        int slot;
+        cudaEvent_t begin;
+        cudaEvent_t end;
+    };
+    std::vector<Mark> marks;
+    std::vector<cudaEvent_t> event_pool;
+    hbfb::LaunchHooks hooks();
+};
+
+namespace hbfb {
+// thermal.cu
+void thermal_destroy(ThermalState* t);
+}

@@ -1,0 +1,1017 @@
+// timing.cu -- B200 kernels for the batched HBF access-timing path.
+//
+// One batch is timed by three launches on one stream:
+//
+//   pass 1  (timing_pass_kernel<..., 1>)  every CTA owns a contiguous range of
+//           tiles.  Per tile: stage the SoA inputs in shared memory, run the
+//           range lookup + stripe decode (A1/A2), partition the tile by local
+//           channel with a stable in-SMEM counting sort, and build the max-plus
+//           matrix of every piece (<= L consecutive accesses of one channel).
+//           The pieces are folded into the CTA's range aggregate R_b
+//           (per channel a K x (K+1) max-plus affine map, K = state words).
+//   scan    (range_scan_kernel)  one CTA applies R_0, R_1, ... to the
+//           context's die/channel state and writes each CTA's incoming state.
+//   pass 2  (timing_pass_kernel<..., 2>)  every CTA re-stages its tiles,
+//           propagates its incoming state through the pieces (one max-plus
+//           matrix-vector product per piece) and replays each piece from its
+//           exact incoming state, writing completion tick, latency and status.
+//
+// Why max-plus: both timing models are max-plus affine in the per-channel
+// state (see the step functions below), so a chunk of accesses is summarized
+// exactly by a K x (K+1) matrix, and chunks compose associatively.  Column r
+// of a piece's matrix is the piece replayed from the unit state e_r (r < K,
+// arrivals ignored) or from the all-NEG state with real arrivals (r == K).
+//
+// Integer, bit-exact: the host proves every tick stays below 2^60, so signed
+// 64-bit max-plus arithmetic equals the reference's saturating unsigned
+// arithmetic; batches that fail the proof run the sequential kernel instead.
+#include "timing.h"
+
+namespace hbfb {
+
+// ---------------------------------------------------------------- helpers
+__device__ __forceinline__ i64 imax(i64 a, i64 b) { return a > b ? a : b; }
+
+__device__ __forceinline__ u64 sat_add_u64(u64 a, u64 b)
+{
+    return b > ~u64{0} - a ? ~u64{0} : a + b;
+}
+
+__device__ __forceinline__ u64 sat_mul_u64(u64 a, u32 b)
+{
+    return b != 0 && a > ~u64{0} / b ? ~u64{0} : a * b;
+}
+
+// ceil(n / d) for n < 2^63, d >= 1, quotient below 2^40: a double estimate
+// corrected by integer checks (the estimate is within one of the quotient).
+__device__ __forceinline__ u64 ceil_div_u64(u64 n, u64 d)
+{
+    u64 q = static_cast<u64>(static_cast<double>(n) / static_cast<double>(d));
+#pragma unroll 1
+    for (int k = 0; k < 3 && q * d > n; ++k) --q;
+#pragma unroll 1
+    for (int k = 0; k < 3 && n - q * d >= d; ++k) ++q;
+    return q + (n != q * d ? 1u : 0u);
+}
+
+// hbf_device.cuh:826-841 -- upper-bound binary search on the sorted bases.
+__device__ __forceinline__ u32 find_range_index(const DevRange* r, u32 count,
+                                                u64 address)
+{
+    u32 first = 0, last = count;
+    while (first < last) {
+        const u32 middle = first + (last - first) / 2;
+        if (__ldg(&r[middle].base) <= address) first = middle + 1;
+        else last = middle;
+    }
+    return first == 0 ? count : first - 1;
+}
+
+// hbf_device.cuh:873-884
+__device__ __forceinline__ bool range_overlaps(const DevRange& r, u64 a,
+                                               u32 bytes)
+{
+    if (bytes == 0 || r.length == 0 || r.base > ~u64{0} - r.length ||
+        a > ~u64{0} - bytes)
+        return false;
+    return a < r.base + r.length && r.base < a + bytes;
+}
+
+struct Decoded {
+    u32 status;
+    u32 range_index;
+    u32 channel;   // global
+    u32 local;     // local channel (this shard)
+    u32 stack;
+    u32 die;
+    u32 plane;
+    u64 media;
+    u64 page;
+};
+
+// Classification in the order of __hbfsim_resolve (hbf_device.cu:997-1003
+// zero bytes, 1083-1127 lookup / straddle / bypass, 1152-1179 media
+// descriptor via access_supported hbf_device.cuh:843-862 and 929-944),
+// followed by the stripe decode.  Page sizes are powers of two (profile
+// validation), so the page arithmetic uses the range's page shift.
+__device__ __forceinline__ Decoded classify_decode(const DecodeParams& p,
+                                                   u64 a, u32 bytes, u32 op,
+                                                   bool want_geometry)
+{
+    Decoded d{};
+    d.range_index = p.range_count;
+    if (bytes == 0) { d.status = kUnsupported; return d; }
+    const u32 index = find_range_index(p.ranges, p.range_count, a);
+    DevRange r;
+    if (index != p.range_count) r = p.ranges[index];
+    if (index == p.range_count || a < r.base || a - r.base >= r.length) {
+        const u32 successor = index == p.range_count ? 0u : index + 1u;
+        if (successor < p.range_count &&
+            range_overlaps(p.ranges[successor], a, bytes))
+            d.status = kUnsupported;
+        else
+            d.status = kBypass;
+        return d;
+    }
+    // access_supported (hbf_device.cuh:843-862)
+    const u32 shift = r.reserved;
+    if (op > 1 || (r.mode != 1 && r.mode != 2) || r.page_bytes == 0 ||
+        r.page_bytes > 0xffffffffull || r.length > ~u64{0} - r.base ||
+        bytes > ~u64{0} - a || a + bytes > r.base + r.length ||
+        (r.permissions & (1u << op)) == 0) {
+        d.status = kUnsupported;
+        return d;
+    }
+    const u64 offset = a - r.base;
+    if ((offset >> shift) != ((offset + bytes - 1) >> shift)) {
+        d.status = kUnsupported;
+        return d;
+    }
+    const u64 page_offset = (offset >> shift) << shift;
+    if (page_offset > ~u64{0} - r.file_offset || r.mode != 1) {
+        d.status = kUnsupported;
+        return d;
+    }
+    d.media = r.file_offset + page_offset;
+    d.range_index = index;
+    d.status = kModeled;
+    if (!want_geometry) return d;
+    // stripe decode: mixed radix in allocation order, fastest letter first
+    const u64 m = r.file_offset + offset;
+    u32 u = static_cast<u32>(m >> p.stripe_shift);  // host: m>>shift < 2^32
+    u32 digit[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const u32 letter = p.order[k];
+        const u32 q = fastdiv_q(u, p.radix[letter]);
+        digit[letter] = u - q * p.radix[letter].d;
+        u = q;
+    }
+    d.channel = digit[0];
+    d.die = digit[2];
+    d.plane = digit[3];
+    const u32 sq = fastdiv_q(d.channel, p.stack_div);
+    d.stack = d.channel - sq * p.stack_div.d;
+    const u64 stripe_mask = (u64{1} << p.stripe_shift) - 1;
+    d.page = ((static_cast<u64>(u) << p.stripe_shift) + (m & stripe_mask)) >>
+             shift;
+    const u32 lq = fastdiv_q(d.channel, p.shard_div);
+    d.local = lq;
+    if (p.shard_count > 1 && d.channel - lq * p.shard_div.d != p.shard_rank)
+        d.status = kForeign;
+    return d;
+}
+
+// ---------------------------------------------------------------- kernels
+struct PassArgs {
+    DecodeParams dp;
+    TimingParams tp;
+    const u64* address;
+    const u32* bytes;
+    const u8* op;
+    const u64* arrival;
+    u64* done;
+    u64* latency;
+    u8* status;
+    u64 n;
+    u32 tiles_per_cta;
+    u32 vec;        // all SoA pointers 16-byte aligned: vector loads/stores
+    u32 T;          // tile size (multiple of 32 * warps)
+    u32 L;          // piece length
+    u32 C;          // local channels
+    u32 K;          // state words per channel
+    u32 group_channels;  // channels per piece-matrix group
+    u32 pm_capacity;     // piece slots in shared memory per group
+    // shared memory offsets (bytes)
+    u32 off_addr, off_arr, off_bytes, off_op, off_ord, off_key, off_rank;
+    u32 off_wcnt, off_seg, off_pbase, off_pchan, off_pm, off_pin, off_die;
+    u32 off_chan, off_act, off_red;
+    // global scratch
+    i64* agg;        // [ctas][C][K][K+1]  (pass 1 out)
+    i64* incoming;   // [ctas][C][K]       (pass 2 in, carried in place)
+    u32* error;      // device error bits of this batch
+    const u64* last_arrival;  // last arrival of the previous batch
+    const u64* state_in;      // carried state (checked against the tick limit)
+    DevCounters* counters;
+};
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+
+struct ChanInfo {  // per local channel, staged in shared memory
+    i64 t_read;
+    i64 t_prog;
+    i64 admit;
+    u64 bw;
+};
+
+template <int MODEL>
+struct StepModel;
+
+// FAST model, hbf_device.cu:883-910: one tail for the whole device.
+//   tail' = max(tail, a) + X ;  done = max(a + L_op, tail')
+template <>
+struct StepModel<kModelFast> {
+    static __device__ __forceinline__ i64 step(i64& chan, i64* /*die*/,
+                                               u32 /*stride*/, i64 a, u32 info,
+                                               const ChanInfo&,
+                                               const TimingParams& tp)
+    {
+        chan = imax(chan, a) + tp.fast_x;
+        const i64 lat = (info >> 28) & 1u ? tp.fast_l_prog : tp.fast_l_read;
+        return imax(a + lat, chan);
+    }
+};
+
+// DIE model (north-star recurrence, builder-fixed details):
+//   start = max(a, channel_free, die_free[d]); channel_free = start + X;
+//   die_free[d] = channel_free + T_op; done = die_free[d]
+template <>
+struct StepModel<kModelDie> {
+    static __device__ __forceinline__ i64 step(i64& chan, i64* die,
+                                               u32 stride, i64 a, u32 info,
+                                               const ChanInfo& ci,
+                                               const TimingParams&)
+    {
+        const i64 x = static_cast<i64>(info & 0xffffffu);
+        const u32 d = (info >> 24) & 15u;
+        const i64 t = (info >> 28) & 1u ? ci.t_prog : ci.t_read;
+        i64* slot = die + d * stride;
+        const i64 start = imax(imax(a, chan), *slot);
+        chan = start + x;
+        const i64 done = chan + t;
+        *slot = done;
+        return done;
+    }
+};
+
+__device__ __forceinline__ u32 lane_id() { return threadIdx.x & 31u; }
+
+// Exclusive scan of `count` u32 values in shared memory by warp 0.
+__device__ void warp0_exclusive_scan(u32* v, u32 count, u32* total)
+{
+    if (threadIdx.x >= 32) return;
+    u32 carry = 0;
+    for (u32 base = 0; base < count; base += 32) {
+        const u32 i = base + lane_id();
+        const u32 x = i < count ? v[i] : 0u;
+        u32 s = x;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const u32 y = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane_id() >= static_cast<u32>(o)) s += y;
+        }
+        if (i < count) v[i] = carry + s - x;
+        carry += __shfl_sync(0xffffffffu, s, 31);
+    }
+    if (lane_id() == 0 && total) *total = carry;
+}
+
+template <int MODEL, int PASS>
+__global__ void __launch_bounds__(kThreads, 2)
+timing_pass_kernel(const PassArgs args)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    const PassArgs& A = args;
+    const u32 tid = threadIdx.x;
+    const u32 warp = tid >> 5;
+    const u32 lane = tid & 31u;
+    const u32 T = A.T, L = A.L, C = A.C, K = A.K;
+
+    u64* s_addr = reinterpret_cast<u64*>(smem + A.off_addr);   // -> done
+    u64* s_arr = reinterpret_cast<u64*>(smem + A.off_arr);     // -> latency
+    u32* s_bytes = reinterpret_cast<u32*>(smem + A.off_bytes); // -> xinfo
+    u8* s_op = smem + A.off_op;                                // -> status
+    u16* s_ord = reinterpret_cast<u16*>(smem + A.off_ord);
+    u16* s_key = reinterpret_cast<u16*>(smem + A.off_key);
+    u16* s_rank = reinterpret_cast<u16*>(smem + A.off_rank);
+    u32* s_wcnt = reinterpret_cast<u32*>(smem + A.off_wcnt);   // [W][C+1]
+    u32* s_seg = reinterpret_cast<u32*>(smem + A.off_seg);     // [C+2]
+    u32* s_pbase = reinterpret_cast<u32*>(smem + A.off_pbase); // [C+2]
+    u16* s_pchan = reinterpret_cast<u16*>(smem + A.off_pchan);
+    i64* s_pm = reinterpret_cast<i64*>(smem + A.off_pm);       // [P][K][K+1]
+    i64* s_pin = reinterpret_cast<i64*>(smem + A.off_pin);     // [P][K]
+    i64* s_die = reinterpret_cast<i64*>(smem + A.off_die);     // [16][threads]
+    ChanInfo* s_chan = reinterpret_cast<ChanInfo*>(smem + A.off_chan);
+    unsigned long long* s_act =
+        reinterpret_cast<unsigned long long*>(smem + A.off_act); // [C*D][2]
+    unsigned long long* s_red =
+        reinterpret_cast<unsigned long long*>(smem + A.off_red);
+
+    if (PASS == 2 && *A.error != 0) return;  // pass 1 refused the batch
+
+    const u32 KK = K + 1;
+    const u32 D = A.tp.dies;
+    for (u32 c = tid; c < C; c += kThreads) {
+        ChanInfo ci{};
+        if (MODEL == kModelDie) {
+            ci.t_read = A.tp.chan_t_read[c];
+            ci.t_prog = A.tp.chan_t_prog[c];
+            ci.admit = A.tp.chan_admit[c];
+            ci.bw = A.tp.chan_bw[c];
+        }
+        s_chan[c] = ci;
+    }
+    const bool activity = PASS == 2 && MODEL == kModelDie &&
+                          A.tp.die_read_bytes != nullptr;
+    if (activity)
+        for (u32 k = tid; k < 2 * C * D; k += kThreads) s_act[k] = 0;
+
+    i64* agg = A.agg + static_cast<u64>(blockIdx.x) * C * K * KK;
+    i64* carry = A.incoming + static_cast<u64>(blockIdx.x) * C * K;
+    if (PASS == 1 && blockIdx.x == 0) {
+        // the parallel path needs every carried tick below 2^59
+        for (u32 k = tid; k < C * K; k += kThreads)
+            if (A.state_in[k] >= kArrivalLimit) atomicOr(A.error, kErrNeedSeq);
+    }
+    if (PASS == 1) {
+        // R_b starts as the identity map: out_i = in_i
+        for (u32 k = tid; k < C * K * KK; k += kThreads) {
+            const u32 col = k % KK, row = (k / KK) % K;
+            agg[k] = col == row ? 0 : kNeg;
+        }
+    }
+    __syncthreads();
+
+    // per-thread statistics (pass 2)
+    unsigned long long st_modeled = 0, st_bypass = 0, st_unsup = 0,
+                       st_foreign = 0, st_lat = 0, st_max = 0, st_fast = 0;
+
+    const u64 tile_first = static_cast<u64>(blockIdx.x) * A.tiles_per_cta;
+    for (u32 tt = 0; tt < A.tiles_per_cta; ++tt) {
+        const u64 start = (tile_first + tt) * T;
+        if (start >= A.n) break;
+        const u32 nt = static_cast<u32>(A.n - start < T ? A.n - start : T);
+
+        // ---- stage inputs (16-byte vector loads for full tiles)
+        if (nt == T && A.vec) {
+            const uint4* g_addr = reinterpret_cast<const uint4*>(A.address + start);
+            const uint4* g_arr = reinterpret_cast<const uint4*>(A.arrival + start);
+            const uint4* g_bytes = reinterpret_cast<const uint4*>(A.bytes + start);
+            const uint4* g_op = reinterpret_cast<const uint4*>(A.op + start);
+            uint4* d_addr = reinterpret_cast<uint4*>(s_addr);
+            uint4* d_arr = reinterpret_cast<uint4*>(s_arr);
+            uint4* d_bytes = reinterpret_cast<uint4*>(s_bytes);
+            uint4* d_op = reinterpret_cast<uint4*>(s_op);
+            for (u32 k = tid; k < T / 2; k += kThreads) {
+                d_addr[k] = __ldcs(g_addr + k);
+                d_arr[k] = __ldcs(g_arr + k);
+            }
+            for (u32 k = tid; k < T / 4; k += kThreads) d_bytes[k] = __ldcs(g_bytes + k);
+            for (u32 k = tid; k < T / 16; k += kThreads) d_op[k] = __ldcs(g_op + k);
+        } else {
+            for (u32 k = tid; k < nt; k += kThreads) {
+                s_addr[k] = A.address[start + k];
+                s_arr[k] = A.arrival[start + k];
+                s_bytes[k] = A.bytes[start + k];
+                s_op[k] = A.op[start + k];
+            }
+        }
+        for (u32 k = tid; k < kWarps * (C + 1); k += kThreads) s_wcnt[k] = 0;
+        __syncthreads();
+
+        // ---- decode + stable ranking by local channel (warp-contiguous)
+        const u32 chunk = T / kWarps;
+        bool unsorted = false;
+        for (u32 j = 0; j < chunk; j += 32) {
+            const u32 e = warp * chunk + j + lane;
+            u32 key = C;
+            if (e < nt) {
+                const u64 a = s_addr[e];
+                const u32 b = s_bytes[e];
+                const u32 o = s_op[e];
+                const u64 arr = s_arr[e];
+                if (PASS == 1) {
+                    const u64 prev = e > 0 ? s_arr[e - 1]
+                                 : (start > 0 ? A.arrival[start - 1] : *A.last_arrival);
+                    if (arr < prev) unsorted = true;
+                    if (arr >= kArrivalLimit) atomicOr(A.error, kErrNeedSeq);
+                }
+                const Decoded d = classify_decode(A.dp, a, b, o, MODEL == kModelDie);
+                u32 info = (o & 1u) << 28;
+                if (d.status == kModeled) {
+                    key = MODEL == kModelDie ? d.local : 0u;
+                    if (MODEL == kModelDie) {
+                        const u64 x = sat_mul_u64(
+                            ceil_div_u64(static_cast<u64>(b) * 1000000000ull,
+                                         s_chan[key].bw),
+                            A.tp.time_scale);
+                        if (x > 0xffffffull) atomicOr(A.error, kErrNeedSeq);
+                        info |= static_cast<u32>(x & 0xffffffull) | (d.die << 24);
+                        if (activity) {
+                            if (o) atomicAdd(&s_act[2 * (key * D + d.die) + 1], 1ull);
+                            else atomicAdd(&s_act[2 * (key * D + d.die)],
+                                           static_cast<unsigned long long>(b));
+                        }
+                    }
+                    if (PASS == 2) ++st_modeled;
+                } else if (PASS == 2) {
+                    s_addr[e] = arr;  // done = arrival
+                    s_arr[e] = 0;     // latency 0
+                    if (d.status == kBypass) ++st_bypass;
+                    else if (d.status == kForeign) ++st_foreign;
+                    else ++st_unsup;
+                }
+                s_bytes[e] = info;
+                s_op[e] = static_cast<u8>(d.status);
+            }
+            const u32 peers = __match_any_sync(0xffffffffu, key);
+            const u32 before = __popc(peers & ((1u << lane) - 1u));
+            const u32 base = s_wcnt[warp * (C + 1) + key];
+            __syncwarp();
+            if (before == 0) s_wcnt[warp * (C + 1) + key] = base + __popc(peers);
+            if (e < nt) {
+                s_key[e] = static_cast<u16>(key);
+                s_rank[e] = static_cast<u16>(base + before);
+            }
+            __syncwarp();
+        }
+        if (PASS == 1 && unsorted) atomicOr(A.error, kErrUnsorted);
+        __syncthreads();
+
+        // ---- segment offsets: key-major, warp-minor
+        for (u32 c = tid; c < C; c += kThreads) {
+            u32 total = 0;
+            for (u32 w = 0; w < kWarps; ++w) total += s_wcnt[w * (C + 1) + c];
+            s_seg[c] = total;
+            s_pbase[c] = (total + L - 1) / L;
+        }
+        __syncthreads();
+        warp0_exclusive_scan(s_seg, C, &s_seg[C]);
+        warp0_exclusive_scan(s_pbase, C, &s_pbase[C]);
+        __syncthreads();
+        for (u32 c = tid; c < C; c += kThreads) {
+            u32 running = s_seg[c];
+            for (u32 w = 0; w < kWarps; ++w) {
+                const u32 cnt = s_wcnt[w * (C + 1) + c];
+                s_wcnt[w * (C + 1) + c] = running;
+                running += cnt;
+            }
+            for (u32 p = s_pbase[c]; p < s_pbase[c + 1]; ++p)
+                s_pchan[p] = static_cast<u16>(c);
+        }
+        __syncthreads();
+        for (u32 j = 0; j < chunk; j += 32) {
+            const u32 e = warp * chunk + j + lane;
+            if (e < nt) {
+                const u32 key = s_key[e];
+                if (key < C) s_ord[s_wcnt[warp * (C + 1) + key] + s_rank[e]] = static_cast<u16>(e);
+            }
+        }
+        __syncthreads();
+
+        // ---- channel groups: piece matrices, fold / propagate, replay
+        for (u32 cg0 = 0; cg0 < C; cg0 += A.group_channels) {
+            const u32 cg1 = cg0 + A.group_channels < C ? cg0 + A.group_channels : C;
+            const u32 p0 = s_pbase[cg0];
+            const u32 np = s_pbase[cg1] - p0;
+            if (np == 0) continue;
+
+            // phase A: column r of piece p = replay from unit state e_r
+            for (u32 q = tid; q < np * KK; q += kThreads) {
+                const u32 pl = q % np, r = q / np;
+                const u32 pg = p0 + pl;
+                const u32 c = s_pchan[pg];
+                const u32 first = s_seg[c] + (pg - s_pbase[c]) * L;
+                const u32 seg_end = s_seg[c + 1];
+                const u32 last = first + L < seg_end ? first + L : seg_end;
+                const ChanInfo ci = s_chan[c];
+                i64 chan = r == 0 ? 0 : kNeg;
+                i64* die = s_die + tid;
+                for (u32 j = 1; j < K; ++j) die[(j - 1) * kThreads] = r == j ? 0 : kNeg;
+                const bool real = r == K;
+                for (u32 k = first; k < last; ++k) {
+                    const u32 e = s_ord[k];
+                    const i64 a = real ? imax(static_cast<i64>(s_arr[e]), ci.admit) : kNeg;
+                    StepModel<MODEL>::step(chan, die, kThreads, a, s_bytes[e], ci, A.tp);
+                }
+                i64* col = s_pm + static_cast<u64>(pl) * K * KK + r;
+                col[0] = chan;
+                for (u32 j = 1; j < K; ++j) col[j * KK] = die[(j - 1) * kThreads];
+            }
+            __syncthreads();
+
+            if (PASS == 1) {
+                // fold this group's pieces into R_b, one thread per (c, r)
+                for (u32 q = tid; q < (cg1 - cg0) * KK; q += kThreads) {
+                    const u32 c = cg0 + q / KK, r = q % KK;
+                    if (s_pbase[c] == s_pbase[c + 1]) continue;
+                    i64 v[17];
+                    i64* col = agg + static_cast<u64>(c) * K * KK + r;
+                    for (u32 i = 0; i < K; ++i) v[i] = col[i * KK];
+                    v[K] = r == K ? 0 : kNeg;
+                    for (u32 pg = s_pbase[c]; pg < s_pbase[c + 1]; ++pg) {
+                        const i64* M = s_pm + static_cast<u64>(pg - p0) * K * KK;
+                        i64 w[16];
+                        for (u32 i = 0; i < K; ++i) {
+                            i64 best = kNeg;  // clamp: -inf stays -inf
+                            for (u32 j = 0; j <= K; ++j) best = imax(best, M[i * KK + j] + v[j]);
+                            w[i] = best;
+                        }
+                        for (u32 i = 0; i < K; ++i) v[i] = w[i];
+                    }
+                    for (u32 i = 0; i < K; ++i) col[i * KK] = v[i];
+                }
+                __syncthreads();
+            } else {
+                // propagate the carried state through the pieces
+                for (u32 c = cg0 + tid; c < cg1; c += kThreads) {
+                    i64 v[17];
+                    i64* cv = carry + static_cast<u64>(c) * K;
+                    for (u32 i = 0; i < K; ++i) v[i] = cv[i];
+                    v[K] = 0;
+                    for (u32 pg = s_pbase[c]; pg < s_pbase[c + 1]; ++pg) {
+                        i64* pin = s_pin + static_cast<u64>(pg - p0) * K;
+                        for (u32 i = 0; i < K; ++i) pin[i] = v[i];
+                        const i64* M = s_pm + static_cast<u64>(pg - p0) * K * KK;
+                        i64 w[16];
+                        for (u32 i = 0; i < K; ++i) {
+                            i64 best = kNeg;
+                            for (u32 j = 0; j <= K; ++j) best = imax(best, M[i * KK + j] + v[j]);
+                            w[i] = best;
+                        }
+                        for (u32 i = 0; i < K; ++i) v[i] = w[i];
+                    }
+                    for (u32 i = 0; i < K; ++i) cv[i] = v[i];
+                }
+                __syncthreads();
+                // phase C: replay every piece from its exact incoming state
+                for (u32 pl = tid; pl < np; pl += kThreads) {
+                    const u32 pg = p0 + pl;
+                    const u32 c = s_pchan[pg];
+                    const u32 first = s_seg[c] + (pg - s_pbase[c]) * L;
+                    const u32 seg_end = s_seg[c + 1];
+                    const u32 last = first + L < seg_end ? first + L : seg_end;
+                    const ChanInfo ci = s_chan[c];
+                    const i64* pin = s_pin + static_cast<u64>(pl) * K;
+                    i64 chan = pin[0];
+                    i64* die = s_die + tid;
+                    for (u32 j = 1; j < K; ++j) die[(j - 1) * kThreads] = pin[j];
+                    for (u32 k = first; k < last; ++k) {
+                        const u32 e = s_ord[k];
+                        const u32 info = s_bytes[e];
+                        const u64 arr = s_arr[e];
+                        const i64 a = imax(static_cast<i64>(arr), ci.admit);
+                        const i64 done = StepModel<MODEL>::step(chan, die, kThreads, a,
+                                                                info, ci, A.tp);
+                        const u64 ud = static_cast<u64>(done);
+                        s_addr[e] = ud;
+                        s_arr[e] = ud - arr;
+                        st_lat += ud - arr;
+                        st_max = ud > st_max ? ud : st_max;
+                        if (MODEL == kModelFast)
+                            st_fast += (info >> 28) & 1u ? A.tp.fast_service_prog
+                                                         : A.tp.fast_service_read;
+                    }
+                }
+                __syncthreads();
+            }
+        }
+
+        if (PASS == 2) {
+            // ---- write the tile's results
+            if (nt == T && A.vec) {
+                uint4* g_done = reinterpret_cast<uint4*>(A.done + start);
+                uint4* g_lat = reinterpret_cast<uint4*>(A.latency + start);
+                uint4* g_st = reinterpret_cast<uint4*>(A.status + start);
+                const uint4* d_done = reinterpret_cast<const uint4*>(s_addr);
+                const uint4* d_lat = reinterpret_cast<const uint4*>(s_arr);
+                const uint4* d_st = reinterpret_cast<const uint4*>(s_op);
+                for (u32 k = tid; k < T / 2; k += kThreads) {
+                    __stcs(g_done + k, d_done[k]);
+                    __stcs(g_lat + k, d_lat[k]);
+                }
+                for (u32 k = tid; k < T / 16; k += kThreads) __stcs(g_st + k, d_st[k]);
+            } else {
+                for (u32 k = tid; k < nt; k += kThreads) {
+                    A.done[start + k] = s_addr[k];
+                    A.latency[start + k] = s_arr[k];
+                    A.status[start + k] = s_op[k];
+                }
+            }
+        }
+        __syncthreads();
+    }
+
+    if (PASS == 2) {
+        if (activity) {
+            for (u32 k = tid; k < C * D; k += kThreads) {
+                if (s_act[2 * k]) atomicAdd(&A.tp.die_read_bytes[k], s_act[2 * k]);
+                if (s_act[2 * k + 1]) atomicAdd(&A.tp.die_writes[k], s_act[2 * k + 1]);
+            }
+        }
+        // block-reduce the statistics, one atomic each per CTA
+        unsigned long long vals[7] = {st_modeled, st_bypass, st_unsup, st_foreign,
+                                      st_lat, st_max, st_fast};
+#pragma unroll
+        for (int k = 0; k < 7; ++k) {
+            unsigned long long v = vals[k];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long y = __shfl_down_sync(0xffffffffu, v, o);
+                v = k == 5 ? (y > v ? y : v) : v + y;
+            }
+            if (lane == 0) s_red[k * kWarps + warp] = v;
+        }
+        __syncthreads();
+        if (tid < 7) {
+            unsigned long long v = 0;
+            for (u32 w = 0; w < kWarps; ++w) {
+                const unsigned long long y = s_red[tid * kWarps + w];
+                v = tid == 5 ? (y > v ? y : v) : v + y;
+            }
+            unsigned long long* dst = &A.counters->modeled;
+            if (tid == 5) atomicMax(&A.counters->max_done, v);
+            else if (v) atomicAdd(tid == 6 ? &A.counters->fast_modeled_ns : dst + tid, v);
+        }
+    }
+}
+
+// Sequential scan of the CTA range aggregates: incoming_b = R_{b-1} ...
+// R_0 (state).  One CTA; thread (c, i) owns state word i of channel c.
+struct ScanArgs {
+    const i64* agg;     // [ctas][C][K][K+1]
+    i64* incoming;      // [ctas][C][K]
+    const u64* state_in;
+    u64* state_out;
+    const u32* error;
+    u64* last_arrival;
+    const u64* arrival;
+    u64 n;
+    u32 ctas, C, K;
+    DevCounters* counters;
+};
+
+__global__ void __launch_bounds__(1024) range_scan_kernel(const ScanArgs a)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    i64* v = reinterpret_cast<i64*>(smem);           // [C][K]
+    i64* w = v + static_cast<u64>(a.C) * a.K;         // [C][K]
+    const u32 words = a.C * a.K;
+    const u32 KK = a.K + 1;
+    const u32 err = *a.error;
+    if (!(err & kErrUnsorted) && (err & kErrNeedSeq)) return;  // sequential path
+    for (u32 k = threadIdx.x; k < words; k += blockDim.x)
+        v[k] = static_cast<i64>(a.state_in[k]);
+    __syncthreads();
+    if (err & kErrUnsorted) {
+        for (u32 k = threadIdx.x; k < words; k += blockDim.x) a.state_out[k] = a.state_in[k];
+        if (threadIdx.x == 0) atomicAdd(&a.counters->errors, 1ull);
+        if (threadIdx.x == 0) atomicOr(&a.counters->error_code, static_cast<unsigned long long>(*a.error));
+        return;
+    }
+    for (u32 b = 0; b < a.ctas; ++b) {
+        const i64* R = a.agg + static_cast<u64>(b) * a.C * a.K * KK;
+        i64* in = a.incoming + static_cast<u64>(b) * words;
+        for (u32 k = threadIdx.x; k < words; k += blockDim.x) {
+            in[k] = v[k];
+            const u32 c = k / a.K, i = k % a.K;
+            const i64* row = R + (static_cast<u64>(c) * a.K + i) * KK;
+            const i64* vc = v + static_cast<u64>(c) * a.K;
+            i64 best = row[a.K];
+            for (u32 j = 0; j < a.K; ++j) best = imax(best, row[j] + vc[j]);
+            w[k] = best;
+        }
+        __syncthreads();
+        for (u32 k = threadIdx.x; k < words; k += blockDim.x) v[k] = w[k];
+        __syncthreads();
+    }
+    for (u32 k = threadIdx.x; k < words; k += blockDim.x)
+        a.state_out[k] = static_cast<u64>(v[k]);
+    if (threadIdx.x == 0) {
+        if (a.n) *a.last_arrival = a.arrival[a.n - 1];
+        atomicAdd(&a.counters->batches, 1ull);
+    }
+}
+
+// Exact sequential fallback with the reference's saturating unsigned
+// arithmetic, for batches whose ticks may approach 2^64.  One thread per
+// local channel walks the whole batch in order.
+struct SeqArgs {
+    DecodeParams dp;
+    TimingParams tp;
+    const u64* address;
+    const u32* bytes;
+    const u8* op;
+    const u64* arrival;
+    u64* done;
+    u64* latency;
+    u8* status;
+    u64 n;
+    u32 C, K;
+    const u64* state_in;
+    u64* state_out;
+    u32* error;
+    u64* last_arrival;
+    DevCounters* counters;
+};
+
+template <int MODEL>
+__global__ void sequential_kernel(const SeqArgs a)
+{
+    const u32 c = blockIdx.x * blockDim.x + threadIdx.x;
+    const u32 flags = *a.error;
+    if ((flags & kErrUnsorted) || !(flags & kErrNeedSeq) || c >= a.C) return;
+    u64 st[17];
+    for (u32 k = 0; k < a.K; ++k) st[k] = a.state_in[static_cast<u64>(c) * a.K + k];
+    unsigned long long n_mod = 0, n_byp = 0, n_uns = 0, n_for = 0, lat = 0,
+                       mx = 0, fast = 0;
+    for (u64 i = 0; i < a.n; ++i) {
+        const u64 arr = a.arrival[i];
+        const Decoded d = classify_decode(a.dp, a.address[i], a.bytes[i], a.op[i],
+                                          MODEL == kModelDie);
+        const u32 key = MODEL == kModelDie ? d.local : 0u;
+        if (d.status != kModeled) {
+            if (c == 0) {
+                a.done[i] = arr;
+                a.latency[i] = 0;
+                a.status[i] = static_cast<u8>(d.status);
+                if (d.status == kBypass) ++n_byp;
+                else if (d.status == kForeign) ++n_for;
+                else ++n_uns;
+            }
+            continue;
+        }
+        if (key != c) continue;
+        u64 done;
+        if (MODEL == kModelFast) {
+            const u64 x = static_cast<u64>(a.tp.fast_x);  // host: already saturated
+            const u64 lat_op = static_cast<u64>(a.op[i] ? a.tp.fast_l_prog : a.tp.fast_l_read);
+            const u64 s = st[0] > arr ? st[0] : arr;
+            st[0] = sat_add_u64(s, x);
+            const u64 lt = sat_add_u64(arr, lat_op);
+            done = lt > st[0] ? lt : st[0];
+            fast += a.op[i] ? a.tp.fast_service_prog : a.tp.fast_service_read;
+        } else {
+            const u64 bw = a.tp.chan_bw[c];
+            const u64 num = static_cast<u64>(a.bytes[i]) * 1000000000ull;
+            const u64 x = sat_mul_u64(num / bw + (num % bw != 0), a.tp.time_scale);
+            const u64 top = static_cast<u64>(a.op[i] ? a.tp.chan_t_prog[c] : a.tp.chan_t_read[c]);
+            u64 s = arr;
+            const u64 admit = static_cast<u64>(a.tp.chan_admit[c]);
+            if (admit > s) s = admit;
+            if (st[0] > s) s = st[0];
+            if (st[1 + d.die] > s) s = st[1 + d.die];
+            st[0] = sat_add_u64(s, x);
+            st[1 + d.die] = sat_add_u64(st[0], top);
+            done = st[1 + d.die];
+        }
+        a.done[i] = done;
+        a.latency[i] = done - arr;
+        a.status[i] = kModeled;
+        ++n_mod;
+        lat += done - arr;
+        mx = done > mx ? done : mx;
+    }
+    for (u32 k = 0; k < a.K; ++k) a.state_out[static_cast<u64>(c) * a.K + k] = st[k];
+    atomicAdd(&a.counters->modeled, n_mod);
+    if (c == 0) {
+        atomicAdd(&a.counters->bypass, n_byp);
+        atomicAdd(&a.counters->foreign, n_for);
+        atomicAdd(&a.counters->unsupported, n_uns);
+        atomicAdd(&a.counters->batches, 1ull);
+        if (a.n) *a.last_arrival = a.arrival[a.n - 1];
+    }
+    atomicAdd(&a.counters->latency_sum, lat);
+    atomicAdd(&a.counters->fast_modeled_ns, fast);
+    atomicMax(&a.counters->max_done, mx);
+}
+
+// Decode-only kernel (A1 + A2), one thread per access.
+struct DecodeOut {
+    u64 media_address;
+    u64 page;
+    u32 status;
+    u32 range_index;
+    u32 stack;
+    u32 channel;
+    u32 die;
+    u32 plane;
+};
+static_assert(sizeof(DecodeOut) == 40, "decoded record layout");
+
+__global__ void decode_kernel(const DecodeParams p, const u64* address,
+                              const u32* bytes, const u8* op, u64 n,
+                              DecodeOut* out)
+{
+    const u64 i = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const Decoded d = classify_decode(p, address[i], bytes[i], op[i], true);
+    DecodeOut o{};
+    o.status = d.status;
+    o.range_index = d.range_index;
+    o.media_address = d.media;
+    if (d.status == kModeled || d.status == kForeign) {
+        o.page = d.page;
+        o.stack = d.stack;
+        o.channel = d.channel;
+        o.die = d.die;
+        o.plane = d.plane;
+    }
+    out[i] = o;
+}
+
+// ---------------------------------------------------------------- host side
+struct Launch {
+    PassArgs pass;
+    u32 ctas;
+    u32 smem_bytes;
+};
+
+static u32 align_up(u32 v, u32 a) { return (v + a - 1) / a * a; }
+
+// Shared-memory layout for a tile of T accesses with C channels, K words.
+static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
+                  u32 group_channels)
+{
+    u32 off = 0;
+    auto take = [&](u32 bytes) {
+        off = align_up(off, 16);
+        const u32 at = off;
+        off += bytes;
+        return at;
+    };
+    const u32 pm_capacity = T / L + group_channels;
+    a.T = T;
+    a.L = L;
+    a.C = C;
+    a.K = K;
+    a.group_channels = group_channels;
+    a.pm_capacity = pm_capacity;
+    a.off_addr = take(8 * T);
+    a.off_arr = take(8 * T);
+    a.off_bytes = take(4 * T);
+    a.off_op = take(T);
+    a.off_ord = take(2 * T);
+    a.off_key = take(2 * T);
+    a.off_rank = take(2 * T);
+    a.off_wcnt = take(4 * kWarps * (C + 1));
+    a.off_seg = take(4 * (C + 2));
+    a.off_pbase = take(4 * (C + 2));
+    a.off_pchan = take(2 * (T / L + C + 1));
+    a.off_pm = take(8 * pm_capacity * K * (K + 1));
+    a.off_pin = take(8 * pm_capacity * K);
+    a.off_die = take(8 * 16 * kThreads);
+    a.off_chan = take(static_cast<u32>(sizeof(ChanInfo)) * C);
+    a.off_act = take(16 * C * (dies ? dies : 1));
+    a.off_red = take(8 * 8 * kWarps);
+    return align_up(off, 16);
+}
+
+}  // namespace hbfb
+
+// ---------------------------------------------------------------- C++ entry
+// (called by context.cu; not part of the C ABI)
+namespace hbfb {
+
+int plan_batch(u64 n, u32 C, u32 K, u32 dies, int sm_count, BatchPlan* plan)
+{
+    const u32 L = 32;
+    const u32 smem_limit = 110 * 1024;  // two CTAs per SM
+    u32 T = 2048;
+    u32 group = C;
+    PassArgs probe{};
+    for (;;) {
+        const u32 bytes = layout(probe, T, L, C, K, dies, group);
+        if (bytes <= smem_limit) break;
+        if (group > 8) group = (group + 1) / 2;
+        else if (T > 512) T /= 2;
+        else return -1;
+    }
+    const u64 tiles = (n + T - 1) / T;
+    const u64 max_ctas = static_cast<u64>(sm_count) * 2;
+    u64 ctas = tiles < max_ctas ? tiles : max_ctas;
+    if (ctas == 0) ctas = 1;
+    const u64 per = (tiles + ctas - 1) / ctas;
+    ctas = (tiles + per - 1) / per;
+    if (ctas == 0) ctas = 1;
+    plan->T = T;
+    plan->L = L;
+    plan->C = C;
+    plan->K = K;
+    plan->group_channels = group;
+    plan->ctas = static_cast<u32>(ctas);
+    plan->tiles_per_cta = static_cast<u32>(per ? per : 1);
+    plan->smem_bytes = layout(probe, T, L, C, K, dies, group);
+    return 0;
+}
+
+static const u32 kSeqFlagHost = kErrNeedSeq;
+
+// Launch sequence of one batch: pass 1, range scan, pass 2, then the
+// sequential kernel, which returns at once unless the error word asks for it
+// (set by the host when its tick bound fails, or by pass 1 on the device).
+cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
+                         const BatchIO& io, const BatchPlan& plan,
+                         const BatchScratch& s, bool force_sequential,
+                         cudaStream_t stream, const LaunchHooks& hooks)
+{
+    const u32 initial = force_sequential ? kErrNeedSeq : 0u;
+    cudaError_t err = cudaMemsetAsync(s.error, 0, sizeof(u32), stream);
+    if (err != cudaSuccess) return err;
+    if (initial) {
+        err = cudaMemcpyAsync(s.error, &kSeqFlagHost, sizeof(u32),
+                              cudaMemcpyHostToDevice, stream);
+        if (err != cudaSuccess) return err;
+    }
+    if (!force_sequential) {
+        PassArgs a{};
+        layout(a, plan.T, plan.L, plan.C, plan.K, tp.dies, plan.group_channels);
+        a.dp = dp;
+        a.tp = tp;
+        a.address = io.address;
+        a.bytes = io.bytes;
+        a.op = io.op;
+        a.arrival = io.arrival;
+        a.done = io.done;
+        a.latency = io.latency;
+        a.status = io.status;
+        a.n = io.n;
+        a.tiles_per_cta = plan.tiles_per_cta;
+        a.vec = io.aligned ? 1u : 0u;
+        a.agg = s.agg;
+        a.incoming = s.incoming;
+        a.error = s.error;
+        a.last_arrival = s.last_arrival;
+        a.state_in = s.state_in;
+        a.counters = s.counters;
+        const bool fast = tp.model == kModelFast;
+        auto p1 = fast ? timing_pass_kernel<kModelFast, 1> : timing_pass_kernel<kModelDie, 1>;
+        auto p2 = fast ? timing_pass_kernel<kModelFast, 2> : timing_pass_kernel<kModelDie, 2>;
+        for (auto k : {p1, p2}) {
+            err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(plan.smem_bytes));
+            if (err != cudaSuccess) return err;
+        }
+        hooks(kSlotPass1, 0, stream);
+        p1<<<plan.ctas, kThreads, plan.smem_bytes, stream>>>(a);
+        hooks(kSlotPass1, 1, stream);
+        ScanArgs sa{};
+        sa.agg = s.agg;
+        sa.incoming = s.incoming;
+        sa.state_in = s.state_in;
+        sa.state_out = s.state_out;
+        sa.error = s.error;
+        sa.last_arrival = s.last_arrival;
+        sa.arrival = io.arrival;
+        sa.n = io.n;
+        sa.ctas = plan.ctas;
+        sa.C = plan.C;
+        sa.K = plan.K;
+        sa.counters = s.counters;
+        const u32 scan_smem = 2 * 8 * plan.C * plan.K;
+        err = cudaFuncSetAttribute(range_scan_kernel,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(scan_smem));
+        if (err != cudaSuccess) return err;
+        hooks(kSlotScan, 0, stream);
+        range_scan_kernel<<<1, 1024, scan_smem, stream>>>(sa);
+        hooks(kSlotScan, 1, stream);
+        hooks(kSlotPass2, 0, stream);
+        p2<<<plan.ctas, kThreads, plan.smem_bytes, stream>>>(a);
+        hooks(kSlotPass2, 1, stream);
+    }
+    SeqArgs q{};
+    q.dp = dp;
+    q.tp = tp;
+    q.address = io.address;
+    q.bytes = io.bytes;
+    q.op = io.op;
+    q.arrival = io.arrival;
+    q.done = io.done;
+    q.latency = io.latency;
+    q.status = io.status;
+    q.n = io.n;
+    q.C = plan.C;
+    q.K = plan.K;
+    q.state_in = s.state_in;
+    q.state_out = s.state_out;
+    q.error = s.error;
+    q.last_arrival = s.last_arrival;
+    q.counters = s.counters;
+    const u32 threads = 64;
+    const u32 blocks = (plan.C + threads - 1) / threads;
+    hooks(kSlotSequential, 0, stream);
+    if (tp.model == kModelFast)
+        sequential_kernel<kModelFast><<<blocks, threads, 0, stream>>>(q);
+    else
+        sequential_kernel<kModelDie><<<blocks, threads, 0, stream>>>(q);
+    hooks(kSlotSequential, 1, stream);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_decode(const DecodeParams& dp, const u64* address,
+                          const u32* bytes, const u8* op, u64 n, void* out,
+                          cudaStream_t stream, const LaunchHooks& hooks)
+{
+    if (n == 0) return cudaSuccess;
+    const u32 threads = 256;
+    const u64 blocks = (n + threads - 1) / threads;
+    hooks(kSlotDecode, 0, stream);
+    decode_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+        dp, address, bytes, op, n, static_cast<DecodeOut*>(out));
+    hooks(kSlotDecode, 1, stream);
+    return cudaGetLastError();
+}
+
+}  // namespace hbfb

@@ -1,0 +1,64 @@
+// timing.h -- host-side entry points of the timing kernels (timing.cu).
+#pragma once
+
+#include "common.h"
+
+#include <cuda_runtime.h>
+
+namespace hbfb {
+
+struct BatchPlan {
+    u32 T, L, C, K, group_channels, ctas, tiles_per_cta, smem_bytes;
+};
+
+struct BatchIO {
+    const u64* address;
+    const u32* bytes;
+    const u8* op;
+    const u64* arrival;
+    u64* done;
+    u64* latency;
+    u8* status;
+    u64 n;
+    bool aligned;
+};
+
+struct BatchScratch {
+    i64* agg;
+    i64* incoming;
+    u32* error;
+    u64* last_arrival;
+    DevCounters* counters;
+    const u64* state_in;
+    u64* state_out;
+};
+
+// Optional launch markers (profiling): mark(slot, 0) before a launch and
+// mark(slot, 1) after it, on the launching stream.
+struct LaunchHooks {
+    void* owner = nullptr;
+    void (*mark)(void* owner, int slot, int phase, cudaStream_t stream) = nullptr;
+    void operator()(int slot, int phase, cudaStream_t s) const
+    {
+        if (mark) mark(owner, slot, phase, s);
+    }
+};
+
+enum KernelSlot : int {
+    kSlotPass1 = 0, kSlotScan = 1, kSlotPass2 = 2, kSlotSequential = 3,
+    kSlotDecode = 4, kSlotThermal = 5, kSlotController = 6, kSlotOther = 7,
+};
+
+// Tile size, channel grouping and grid for a batch of n accesses.
+int plan_batch(u64 n, u32 C, u32 K, u32 dies, int sm_count, BatchPlan* plan);
+
+cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
+                         const BatchIO& io, const BatchPlan& plan,
+                         const BatchScratch& s, bool force_sequential,
+                         cudaStream_t stream, const LaunchHooks& hooks = {});
+
+cudaError_t launch_decode(const DecodeParams& dp, const u64* address,
+                          const u32* bytes, const u8* op, u64 n, void* out,
+                          cudaStream_t stream, const LaunchHooks& hooks = {});
+
+}  // namespace hbfb

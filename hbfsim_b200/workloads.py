@@ -1,0 +1,178 @@
+"""Synthetic workloads shaped like the BASELINE configs (seeded, reproducible).
+
+No public dataset or model weights are involved: traces are generated from a
+seed with the shapes, sizes and value distributions of the configs, and the
+media profiles below follow the legacy profile schema
+(configs/schema/hbf-profile.schema.json) unchanged.
+
+c0  timing-only trace: 1,048,576 accesses on one 64 GiB range; 95 % reads;
+    128 B (80 %) or 4 KiB (20 %), 128-B aligned; 70 % of accesses in
+    sequential 16 KiB runs (128 steps of 128 B) from uniform starts, 30 %
+    uniform; exponential arrival gaps of mean 2 ns (rounded to whole ns);
+    1 stack x 16 channels x 4 dies x 4 planes, 16 KiB page, tR 3000 ns,
+    tPROG 200000 ns, 8 GB/s per channel, 4 KiB striping.  A 4 KiB access that
+    would cross a 16 KiB page is moved down to end at the page boundary.
+c1  MoE weight-streaming decode shaped like Qwen3-30B-A3B: 48 layers x 128
+    experts of 3*(2048*768) bf16 laid out contiguously in a 60 GiB range;
+    8 decode steps x 32 tokens; each token picks 8 distinct experts from
+    Zipf(1.1) over a per-layer random permutation; every weight byte of the
+    union of experts of a layer-step is read in 1 KiB reads.  Attention
+    weights (4096*2048 bf16 per layer) live in HBM: they are read too, as
+    bypass accesses outside the HBF range.  Arrival process (fixed by this
+    build): one 1 KiB read per ns, i.e. arrival = access index.  Profile as
+    c0 with 4 stacks (64 channels).
+"""
+from __future__ import annotations
+
+import json
+import os
+from dataclasses import dataclass, field
+from pathlib import Path
+
+import numpy as np
+
+GIB = 1 << 30
+RANGE_BASE = 0x7F00_0000_0000   # synthetic device address of the HBF range
+HBM_BASE = 0x7E00_0000_0000     # synthetic address of HBM-resident weights
+
+
+def c0_profile() -> dict:
+    return {
+        "name": "baseline-c0",
+        "capacity_bytes": 64 * GIB,
+        "page_bytes": 16384,
+        "read_latency_ns": 3000,
+        "program_latency_ns": 200000,
+        "channels": 16,
+        "dies_per_channel": 4,
+        "planes_per_die": 4,
+        "pages_per_block": 256,
+        "channel_width_bits": 8,
+        "channel_transfer_rate_mtps": 8000,
+        "queue_depth": 128,
+        "aggregate_bandwidth_bytes_per_s": 128_000_000_000,
+        "hbm_cache_bytes": 0,
+        "reference_sample_rate": 0.0,
+        "reference_warmup_requests": 0,
+        "time_scale": 1,
+        "timing_tolerance_ns": 10000,
+    }
+
+
+def c4_profile() -> dict:
+    p = c0_profile()
+    p.update(name="baseline-c4", dies_per_channel=8, capacity_bytes=128 * GIB)
+    return p
+
+
+@dataclass
+class Workload:
+    name: str
+    profile: dict
+    stacks: int
+    stripe_bytes: int
+    range_base: int
+    range_length: int
+    extra: dict = field(default_factory=dict)
+
+    def write_profile(self, directory: str | os.PathLike) -> str:
+        path = Path(directory) / f"{self.profile['name']}.json"
+        path.write_text(json.dumps(self.profile, indent=2))
+        return str(path)
+
+    @property
+    def channels_total(self) -> int:
+        return self.stacks * self.profile["channels"]
+
+    @property
+    def dies(self) -> int:
+        return self.profile["dies_per_channel"]
+
+
+def c0_workload() -> Workload:
+    return Workload("c0", c0_profile(), 1, 4096, RANGE_BASE, 64 * GIB)
+
+
+def c1_workload() -> Workload:
+    return Workload("c1", c0_profile(), 4, 4096, RANGE_BASE, 60 * GIB)
+
+
+def c0_trace(n: int = 1 << 20, seed: int = 0, range_length: int = 64 * GIB,
+             base: int = RANGE_BASE):
+    """Returns (address u64, bytes u32, op u8, arrival u64) numpy arrays."""
+    rng = np.random.default_rng(seed)
+    run = 128                                   # 16 KiB / 128 B
+    blocks = (n + run - 1) // run
+    sequential = rng.random(blocks) < 0.7
+    starts = rng.integers(0, (range_length - 16384) // 128, blocks, dtype=np.int64) * 128
+    uniform = rng.integers(0, (range_length - 4096) // 128, n, dtype=np.int64) * 128
+    i = np.arange(n, dtype=np.int64)
+    b = i // run
+    offset = np.where(sequential[b], starts[b] + (i % run) * 128, uniform)
+    size = np.where(rng.random(n) < 0.8, 128, 4096).astype(np.int64)
+    in_page = offset % 16384
+    over = np.maximum(in_page + size - 16384, 0)
+    offset = offset - over
+    op = (rng.random(n) < 0.05).astype(np.uint8)
+    gaps = np.rint(rng.exponential(2.0, n)).astype(np.uint64)
+    arrival = np.cumsum(gaps, dtype=np.uint64)
+    address = (offset + base).astype(np.uint64)
+    return address, size.astype(np.uint32), op, arrival
+
+
+EXPERT_BYTES = 3 * 2048 * 768 * 2
+ATTN_BYTES = 4096 * 2048 * 2
+READ_BYTES = 1024
+
+
+def c1_segments(seed: int = 0, steps: int = 8, layers: int = 48, experts: int = 128,
+                batch: int = 32, topk: int = 8, zipf_s: float = 1.1):
+    """Read segments of the MoE decode trace, in issue order.
+
+    Returns (base u64[S], count i64[S]): segment k is `count[k]` consecutive
+    1 KiB reads starting at `base[k]`.  Per layer-step: the layer's attention
+    weights (HBM, bypass) then the union of selected experts (HBF), in
+    ascending expert id."""
+    rng = np.random.default_rng(seed)
+    ranks = np.arange(1, experts + 1, dtype=np.float64)
+    p = ranks ** -zipf_s
+    p /= p.sum()
+    perms = np.stack([rng.permutation(experts) for _ in range(layers)])
+    bases, counts = [], []
+    for _ in range(steps):
+        for layer in range(layers):
+            chosen = set()
+            for _ in range(batch):
+                picks = rng.choice(experts, size=topk, replace=False, p=p)
+                chosen.update(int(perms[layer][r]) for r in picks)
+            bases.append(HBM_BASE + layer * ATTN_BYTES)
+            counts.append(ATTN_BYTES // READ_BYTES)
+            for e in sorted(chosen):
+                bases.append(RANGE_BASE + (layer * experts + e) * EXPERT_BYTES)
+                counts.append(EXPERT_BYTES // READ_BYTES)
+    return np.array(bases, dtype=np.uint64), np.array(counts, dtype=np.int64)
+
+
+def expand_segments(bases, counts, device=None):
+    """Expand read segments into SoA arrays.  With `device` set the expansion
+    runs in torch on that device (int64 tensors carry the u64 bit patterns);
+    otherwise numpy arrays are returned."""
+    n = int(counts.sum())
+    starts = np.concatenate([[0], np.cumsum(counts)[:-1]]).astype(np.int64)
+    if device is None:
+        seg_base = np.repeat(bases.astype(np.int64), counts)
+        seg_start = np.repeat(starts, counts)
+        idx = np.arange(n, dtype=np.int64)
+        address = (seg_base + (idx - seg_start) * READ_BYTES).astype(np.uint64)
+        return (address, np.full(n, READ_BYTES, np.uint32), np.zeros(n, np.uint8),
+                idx.astype(np.uint64))
+    import torch
+    c = torch.as_tensor(counts, device=device)
+    seg_base = torch.repeat_interleave(torch.as_tensor(bases.astype(np.int64), device=device), c)
+    seg_start = torch.repeat_interleave(torch.as_tensor(starts, device=device), c)
+    idx = torch.arange(n, dtype=torch.int64, device=device)
+    address = seg_base + (idx - seg_start) * READ_BYTES
+    del seg_base, seg_start
+    nbytes = torch.full((n,), READ_BYTES, dtype=torch.int32, device=device)
+    op = torch.zeros(n, dtype=torch.uint8, device=device)
+    return address, nbytes, op, idx

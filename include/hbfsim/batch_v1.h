@@ -1,0 +1,260 @@
+/*
+ * hbfsim/batch_v1.h -- additive, versioned exports for batched access timing
+ * on B200.  None of these exist in the reference C API; each struct carries
+ * struct_size and version the way hbfsim_capacity_stats_v1 does
+ * (reference include/hbfsim/api.h:66-90), so later versions can grow them.
+ *
+ * Every entry point returns an hbfsim_error code and never throws.  Device
+ * pointers are plain CUDA device addresses; `stream` is a cudaStream_t passed
+ * as void* (NULL = the context's own stream).  Calls on one context are
+ * serialized by the context; contexts are independent.
+ *
+ * Reference interfaces replaced, per entry point:
+ *   hbfsim_submit_access_batch_v1   the per-access device helper
+ *       __hbfsim_resolve (src/cuda_runtime/device/hbf_device.cu:963-1344)
+ *       and its fast-model step resolve_fast_or_hybrid (hbf_device.cu:765-960),
+ *       run over a whole batch instead of one instrumented load at a time
+ *   hbfsim_decode_batch_v1          find_range_index / media_descriptor
+ *       (hbf_device.cuh:826-944) plus the stripe decode of
+ *       src/ucie/bank_layout.cpp:59-72 and src/ucie/stack_router.cpp:52-59
+ *   hbfsim_get_simulated_time_v1    the modeled clock the reference reads
+ *       from fast_channel_tail_ns (hbf_device.cuh:70) / MQSim's engine.now
+ *   hbfsim_advance_epoch_v1         ThermalModel::advance_to
+ *       (src/eq3_thermal/thermal.cpp:242-311) on the eq3 layered grid
+ *       (tools/eq3_layered_export.py:48-114) plus the control sample of
+ *       CpuService (src/eq3_thermal/cpu_service.cpp:221-283)
+ *   hbfsim_submit_capacity_batch_v1 CapacityPageService::resolve
+ *       (src/host_service/capacity_page_service.cpp:97-210) with exact LRU
+ *       (adapters/vllm_capacity/placement_policy.py:68-93) and the
+ *       program-then-read media actions (request_dispatcher.cpp:107-126,
+ *       294-298)
+ */
+#ifndef HBFSIM_BATCH_V1_H
+#define HBFSIM_BATCH_V1_H
+
+#include "api.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* hbfsim_options.mode value selecting the per-die max-plus model. */
+#define HBFSIM_MODEL_DIE_V1 3u
+
+/* Per-access status written by the batch path. */
+enum hbfsim_access_status_v1 {
+    HBFSIM_ACCESS_MODELED = 1,      /* timed (reference RequestStatus::Ready) */
+    HBFSIM_ACCESS_UNSUPPORTED = 6,  /* rejected (RequestStatus::Unsupported)  */
+    HBFSIM_ACCESS_BYPASS = 8,       /* outside every range: native, untimed   */
+    HBFSIM_ACCESS_FOREIGN = 9       /* another shard's channel                */
+};
+
+/* ---- geometry: stacks, striping and channel sharding ---- */
+#define HBFSIM_GEOMETRY_V1_VERSION 1u
+typedef struct hbfsim_geometry_v1 {
+    uint32_t struct_size;
+    uint32_t version;
+    uint32_t stacks;         /* UCIe stack_count; profile channels are per stack */
+    uint32_t stripe_bytes;   /* power of two, >= 512; 0 = page_bytes           */
+    uint32_t shard_rank;     /* this context owns channels g % shard_count == rank */
+    uint32_t shard_count;    /* 1 = no sharding                                 */
+    uint32_t reserved[2];
+} hbfsim_geometry_v1;
+
+/* Must be called before the first batch (defaults: 1 stack, page striping,
+ * 1 shard). */
+int hbfsim_set_geometry_v1(hbfsim_context* context,
+                           const hbfsim_geometry_v1* geometry);
+
+/* ---- access batches ---- */
+#define HBFSIM_ACCESS_BATCH_V1_VERSION 1u
+typedef struct hbfsim_access_batch_v1 {
+    uint32_t struct_size;
+    uint32_t version;
+    uint64_t count;
+    const uint64_t* address;     /* device address of the access            */
+    const uint32_t* bytes;       /* access size                             */
+    const uint8_t* operation;    /* 0 read, 1 write                         */
+    const uint64_t* arrival_ns;  /* simulated arrival tick, non-decreasing  */
+    uint64_t* done_ns;           /* out: completion tick                    */
+    uint64_t* latency_ns;        /* out: done - arrival                     */
+    uint8_t* status;             /* out: hbfsim_access_status_v1            */
+} hbfsim_access_batch_v1;
+
+/* Times one batch with the context's model, continuing from the die/channel
+ * state the previous batch left.  All pointers are device pointers.  Runs
+ * asynchronously on `stream`; results are valid once the stream reaches the
+ * end of the call.  Arrivals must be non-decreasing within a batch and must
+ * not go below the previous batch's; a violation is recorded on the device,
+ * leaves the context state unchanged, and is returned by the next
+ * hbfsim_flush. */
+int hbfsim_submit_access_batch_v1(hbfsim_context* context,
+                                  const hbfsim_access_batch_v1* batch,
+                                  void* stream);
+
+/* The same call with HOST pointers: copies in, times, copies out, pipelined
+ * over chunks on the context's streams.  Synchronous. */
+int hbfsim_submit_access_batch_host_v1(hbfsim_context* context,
+                                       const hbfsim_access_batch_v1* batch);
+
+/* Returns the timing state to idle -- every die and channel free at tick 0,
+ * no arrival seen yet -- without touching ranges, factors or counters.
+ * Asynchronous on `stream`; replaces the carried state the way
+ * hbfsim_set_state_v1 does, without a host round trip. */
+int hbfsim_reset_state_v1(hbfsim_context* context, void* stream);
+
+/* Simulated time: the latest completion tick modeled so far. Synchronizes. */
+int hbfsim_get_simulated_time_v1(hbfsim_context* context, uint64_t* ns);
+
+#define HBFSIM_BATCH_STATS_V1_VERSION 1u
+typedef struct hbfsim_batch_stats_v1 {
+    uint32_t struct_size;
+    uint32_t version;
+    uint64_t modeled;
+    uint64_t bypass;
+    uint64_t unsupported;
+    uint64_t foreign;
+    uint64_t latency_sum_ns;   /* wrapping sum over modeled accesses */
+    uint64_t max_done_ns;
+    uint64_t fast_modeled_ns;  /* sum of fast_service_ns (FAST model) */
+    uint64_t batches;
+    uint64_t device_errors;    /* batches refused on the device */
+} hbfsim_batch_stats_v1;
+
+int hbfsim_get_batch_stats_v1(hbfsim_context* context,
+                              hbfsim_batch_stats_v1* out);
+
+/* ---- launch profiling ----
+ * When enabled, every kernel launch of the context is bracketed by CUDA
+ * events on its launching stream; hbfsim_get_kernel_times_v1 synchronizes,
+ * adds up the device time of each kernel kind and clears the record.
+ * Slots: 0 pass 1, 1 range scan, 2 pass 2, 3 sequential, 4 decode,
+ *        5 thermal step, 6 epoch controller, 7 other. */
+#define HBFSIM_KERNEL_SLOTS_V1 8
+#define HBFSIM_KERNEL_TIMES_V1_VERSION 1u
+typedef struct hbfsim_kernel_times_v1 {
+    uint32_t struct_size;
+    uint32_t version;
+    uint64_t launches[HBFSIM_KERNEL_SLOTS_V1];
+    double total_ms[HBFSIM_KERNEL_SLOTS_V1];
+} hbfsim_kernel_times_v1;
+
+int hbfsim_set_profiling_v1(hbfsim_context* context, int enable);
+int hbfsim_get_kernel_times_v1(hbfsim_context* context,
+                               hbfsim_kernel_times_v1* out);
+
+/* ---- decode only (range lookup + stripe decode) ---- */
+typedef struct hbfsim_decoded_v1 {
+    uint64_t media_address;  /* page-aligned media address */
+    uint64_t page;           /* page index inside the plane */
+    uint32_t status;
+    uint32_t range_index;
+    uint32_t stack;
+    uint32_t channel;        /* global channel */
+    uint32_t die;
+    uint32_t plane;
+} hbfsim_decoded_v1;
+
+int hbfsim_decode_batch_v1(hbfsim_context* context, const uint64_t* address,
+                           const uint32_t* bytes, const uint8_t* operation,
+                           uint64_t count, hbfsim_decoded_v1* out,
+                           void* stream);
+
+/* ---- refresh / throttle factors (per epoch) ----
+ * refresh_permille[c]: share of local channel c's bandwidth taken by refresh
+ *   (0..999); effective bandwidth = floor(bw * (1000 - r) / 1000).
+ * throttle_permille[s]: die op-time multiplier of stack s (>= 1000).
+ * admit_after_ns[s]: no access of stack s starts before this tick.
+ * Any pointer may be NULL to leave that table unchanged.  Host pointers. */
+int hbfsim_set_channel_factors_v1(hbfsim_context* context,
+                                  const uint32_t* refresh_permille,
+                                  const uint32_t* throttle_permille,
+                                  const uint64_t* admit_after_ns);
+
+/* ---- state checkpoint: raw little-endian die/channel state ----
+ * Layout: local channel c, state[c*(D+1)] = channel free, then die d free.
+ * FAST model: one word, the channel tail.  words = size of the buffer. */
+int hbfsim_get_state_v1(hbfsim_context* context, uint64_t* host_words,
+                        uint64_t words);
+int hbfsim_set_state_v1(hbfsim_context* context, const uint64_t* host_words,
+                        uint64_t words);
+uint64_t hbfsim_state_words_v1(hbfsim_context* context);
+
+/* ---- eq3 thermal grid and epoch controller ---- */
+#define HBFSIM_THERMAL_MAX_LAYERS 32
+#define HBFSIM_THERMAL_CONFIG_V1_VERSION 1u
+typedef struct hbfsim_thermal_layer_v1 {
+    double thickness_m;
+    double cv_j_m3_k;
+    double k_xyz_w_m_k[3];
+} hbfsim_thermal_layer_v1;
+
+typedef struct hbfsim_thermal_config_v1 {
+    uint32_t struct_size;
+    uint32_t version;
+    uint32_t nx, ny;            /* cells per layer (uniform square mesh) */
+    uint32_t layer_count;       /* bottom (index 0) to top              */
+    uint32_t reserved0;
+    double cell_m;
+    hbfsim_thermal_layer_v1 layers[HBFSIM_THERMAL_MAX_LAYERS];
+    double bottom_h_w_m2_k, bottom_ambient_k;
+    double top_h_w_m2_k, top_ambient_k;
+    double initial_k;
+    /* per-die power law: idle W + J per byte read + J per write access */
+    double die_idle_w;
+    double read_j_per_byte;
+    double write_j_per_access;
+    /* refresh law: base permille, doubling every refresh_step_k above
+     * refresh_onset_k; capped at refresh_cap_permille */
+    double refresh_onset_k;
+    double refresh_step_k;
+    uint32_t refresh_base_permille;
+    uint32_t refresh_cap_permille;
+    /* throttle (hysteresis levels Normal/Light/Severe/Shutdown on the hottest
+     * die of a stack, cpu_service.cpp:221-247) */
+    double light_k, severe_k, shutdown_k, hysteresis_k;
+    uint32_t light_permille, severe_permille;
+    uint32_t reserved1[2];
+    /* floorplan: die (global channel g, die d) heats layers
+     * [z0, z0+z_count) over the rectangle [x0,x1) x [y0,y1) in cells.
+     * Arrays of length channels_total * dies, indexed g * dies + d.
+     * Host pointers; copied at configure time. */
+    const uint32_t* die_z0;
+    const uint32_t* die_z_count;
+    const uint32_t* die_x0;
+    const uint32_t* die_x1;
+    const uint32_t* die_y0;
+    const uint32_t* die_y1;
+} hbfsim_thermal_config_v1;
+
+int hbfsim_thermal_configure_v1(hbfsim_context* context,
+                                const hbfsim_thermal_config_v1* config);
+
+/* Closes one epoch of `epoch_s` seconds: die activity recorded by the batches
+ * since the previous epoch becomes power, the grid takes one backward-Euler
+ * step, and the refresh / throttle factors of the next epoch are derived from
+ * the new die temperatures.  Activity counters are then cleared. */
+int hbfsim_advance_epoch_v1(hbfsim_context* context, double epoch_s,
+                            void* stream);
+
+/* Host copies of the grid temperatures (nx*ny*layers, K, cell index
+ * z*nx*ny + y*nx + x) and of per-die mean temperatures. */
+int hbfsim_get_temperatures_v1(hbfsim_context* context, double* out,
+                               uint64_t count);
+int hbfsim_get_die_temperatures_v1(hbfsim_context* context, double* out,
+                                   uint64_t count);
+/* Per-die activity since the last epoch: read bytes and write count, local
+ * die index c*D+d.  Host copies. */
+int hbfsim_get_die_activity_v1(hbfsim_context* context, uint64_t* read_bytes,
+                               uint64_t* writes, uint64_t count);
+/* Factors currently in force (host copies; NULL to skip). */
+int hbfsim_get_channel_factors_v1(hbfsim_context* context,
+                                  uint32_t* refresh_permille,
+                                  uint32_t* throttle_permille,
+                                  uint64_t* admit_after_ns);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HBFSIM_BATCH_V1_H */

@@ -244,9 +244,9 @@ static uint64_t or_fast_step(uint64_t* tail, uint64_t arrival, uint64_t x,
  *   die_free[d]  = channel_free + T   (die runs tR / tPROG)
  *   done = die_free[d]                                        */
 static uint64_t or_die_step(uint64_t* chan, uint64_t* die, uint64_t arrival,
-                            uint64_t x, uint64_t t)
+                            uint64_t admit, uint64_t x, uint64_t t)
 {
-    uint64_t start = arrival;
+    uint64_t start = arrival > admit ? arrival : admit;
     if (*chan > start) start = *chan;
     if (*die > start) start = *die;
     *chan = or_saturating_add(start, x);
@@ -261,6 +261,7 @@ typedef struct or_job {
     const uint64_t* chan_bw;
     const uint64_t* t_read;
     const uint64_t* t_prog;
+    const uint64_t* admit;
     const uint32_t* bytes;
     const uint8_t* op;
     const uint64_t* arrival;
@@ -309,7 +310,8 @@ static void or_run_job(or_job* j)
             const uint64_t top = j->op[i] ? j->t_prog[d->stack]
                                           : j->t_read[d->stack];
             const uint64_t tt = or_saturating_multiply(top, t->time_scale);
-            done = or_die_step(&st[0], &st[1 + d->die], a, x, tt);
+            const uint64_t adm = j->admit ? j->admit[d->stack] : 0;
+            done = or_die_step(&st[0], &st[1 + d->die], a, adm, x, tt);
         }
         j->done[i] = done;
         j->latency[i] = done - a;
@@ -324,19 +326,60 @@ static void* or_thread_main(void* arg)
     return NULL;
 }
 
+typedef struct or_decode_job {
+    const or_range* ranges;
+    uint32_t count;
+    const or_geometry* g;
+    const uint64_t* address;
+    const uint32_t* bytes;
+    const uint8_t* op;
+    uint64_t begin, end;
+    or_decoded* out;
+} or_decode_job;
+
+static void* or_decode_main(void* arg)
+{
+    or_decode_job* j = (or_decode_job*)arg;
+    or_decode_batch(j->ranges, j->count, j->g, j->address + j->begin,
+                    j->bytes + j->begin, j->op + j->begin, j->end - j->begin,
+                    j->out + j->begin);
+    return NULL;
+}
+
 int or_run_batch_threads(const or_range* ranges, uint32_t count,
                          const or_geometry* g, const or_timing* t,
                          const uint64_t* chan_bw, const uint64_t* t_read,
-                         const uint64_t* t_prog, const uint64_t* address,
+                         const uint64_t* t_prog, const uint64_t* admit,
+                         const uint64_t* address,
                          const uint32_t* bytes, const uint8_t* op,
                          const uint64_t* arrival, uint64_t n, uint64_t* state,
                          uint64_t* done, uint64_t* latency, uint8_t* status,
                          or_stats* stats, int threads)
 {
     memset(stats, 0, sizeof *stats);
+    if (threads < 1) threads = 1;
     or_decoded* dec = (or_decoded*)malloc(sizeof(or_decoded) * (n ? n : 1));
     if (!dec) return -1;
-    or_decode_batch(ranges, count, g, address, bytes, op, n, dec);
+    /* decode: independent per access, split over the threads */
+    {
+        or_decode_job* dj = (or_decode_job*)calloc((size_t)threads, sizeof(or_decode_job));
+        pthread_t* tid = (pthread_t*)calloc((size_t)threads, sizeof(pthread_t));
+        for (int k = 0; k < threads; ++k) {
+            dj[k].ranges = ranges; dj[k].count = count; dj[k].g = g;
+            dj[k].address = address; dj[k].bytes = bytes; dj[k].op = op;
+            dj[k].begin = n * (uint64_t)k / (uint64_t)threads;
+            dj[k].end = n * (uint64_t)(k + 1) / (uint64_t)threads;
+            dj[k].out = dec;
+        }
+        if (threads == 1) {
+            or_decode_main(&dj[0]);
+        } else {
+            for (int k = 0; k < threads; ++k)
+                pthread_create(&tid[k], NULL, or_decode_main, &dj[k]);
+            for (int k = 0; k < threads; ++k) pthread_join(tid[k], NULL);
+        }
+        free(dj); free(tid);
+    }
     uint64_t* order = or_arrival_order(arrival, n);
     if (!order) { free(dec); return -1; }
     uint64_t m = 0;
@@ -356,14 +399,15 @@ int or_run_batch_threads(const or_range* ranges, uint32_t count,
     const uint32_t shards = g->shard_count ? g->shard_count : 1;
     const uint32_t channels_total = g->stacks * g->channels_per_stack;
     const uint32_t local = (channels_total + shards - 1) / shards;
-    if (t->model == OR_MODEL_FAST || threads <= 1) threads = 1;
+    if (t->model == OR_MODEL_FAST) threads = 1;
     if ((uint32_t)threads > local) threads = (int)local;
     or_job* jobs = (or_job*)calloc((size_t)threads, sizeof(or_job));
     pthread_t* tids = (pthread_t*)calloc((size_t)threads, sizeof(pthread_t));
     for (int k = 0; k < threads; ++k) {
         or_job* j = &jobs[k];
         j->ranges = ranges; j->g = g; j->t = t; j->chan_bw = chan_bw;
-        j->t_read = t_read; j->t_prog = t_prog; j->bytes = bytes; j->op = op;
+        j->t_read = t_read; j->t_prog = t_prog; j->admit = admit;
+        j->bytes = bytes; j->op = op;
         j->arrival = arrival; j->dec = dec; j->order = order; j->order_n = m;
         j->state = state; j->done = done; j->latency = latency;
         j->channel_begin = (uint32_t)((uint64_t)local * k / threads);
@@ -391,13 +435,13 @@ int or_run_batch_threads(const or_range* ranges, uint32_t count,
 int or_run_batch(const or_range* ranges, uint32_t count, const or_geometry* g,
                  const or_timing* t, const uint64_t* chan_bw,
                  const uint64_t* t_read, const uint64_t* t_prog,
-                 const uint64_t* address, const uint32_t* bytes,
+                 const uint64_t* admit, const uint64_t* address, const uint32_t* bytes,
                  const uint8_t* op, const uint64_t* arrival, uint64_t n,
                  uint64_t* state, uint64_t* done, uint64_t* latency,
                  uint8_t* status, or_stats* stats)
 {
     return or_run_batch_threads(ranges, count, g, t, chan_bw, t_read, t_prog,
-                                address, bytes, op, arrival, n, state, done,
+                                admit, address, bytes, op, arrival, n, state, done,
                                 latency, status, stats, 1);
 }
 

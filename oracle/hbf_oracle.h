@@ -122,11 +122,12 @@ void or_decode_batch(const or_range* ranges, uint32_t count,
  *         state[c*(D+1)+1+d] = die d free.
  * chan_bw[c]: effective channel bandwidth of local channel c (DIE only).
  * t_read[s], t_prog[s]: die op times of stack s, already throttled (DIE).
+ * admit[s]: no access of stack s starts before this tick (DIE; NULL = 0).
  */
 int or_run_batch(const or_range* ranges, uint32_t count, const or_geometry* g,
                  const or_timing* t, const uint64_t* chan_bw,
                  const uint64_t* t_read, const uint64_t* t_prog,
-                 const uint64_t* address, const uint32_t* bytes,
+                 const uint64_t* admit, const uint64_t* address, const uint32_t* bytes,
                  const uint8_t* op, const uint64_t* arrival, uint64_t n,
                  uint64_t* state, uint64_t* done, uint64_t* latency,
                  uint8_t* status, or_stats* stats);
@@ -136,7 +137,8 @@ int or_run_batch(const or_range* ranges, uint32_t count, const or_geometry* g,
 int or_run_batch_threads(const or_range* ranges, uint32_t count,
                          const or_geometry* g, const or_timing* t,
                          const uint64_t* chan_bw, const uint64_t* t_read,
-                         const uint64_t* t_prog, const uint64_t* address,
+                         const uint64_t* t_prog, const uint64_t* admit,
+                         const uint64_t* address,
                          const uint32_t* bytes, const uint8_t* op,
                          const uint64_t* arrival, uint64_t n, uint64_t* state,
                          uint64_t* done, uint64_t* latency, uint8_t* status,

@@ -89,8 +89,8 @@ def _load() -> ctypes.CDLL:
     lib.or_decode_batch.restype = None
     lib.or_decode_batch.argtypes = [p, u32, p, p, p, p, u64, p]
     lib.or_run_batch_threads.restype = ctypes.c_int
-    lib.or_run_batch_threads.argtypes = [p, u32, p, p, p, p, p, p, p, p, p, u64,
-                                         p, p, p, p, p, ctypes.c_int]
+    lib.or_run_batch_threads.argtypes = [p, u32, p, p, p, p, p, p, p, p, p, p,
+                                         u64, p, p, p, p, p, ctypes.c_int]
     lib.or_lru_run.restype = None
     lib.or_lru_run.argtypes = [p, p, u64, u64, p, p, p]
     return lib
@@ -138,7 +138,7 @@ def decode(ranges, count, geometry, address, nbytes, op) -> np.ndarray:
 
 
 def run_batch(ranges, count, geometry, timing, chan_bw, t_read, t_prog, address,
-              nbytes, op, arrival, state, threads=1):
+              nbytes, op, arrival, state, threads=1, admit=None):
     """Returns (done, latency, status, stats dict); updates `state` in place."""
     n = address.size
     done = np.zeros(n, np.uint64)
@@ -148,7 +148,7 @@ def run_batch(ranges, count, geometry, timing, chan_bw, t_read, t_prog, address,
     rc = LIB.or_run_batch_threads(
         ctypes.cast(ranges, ctypes.c_void_p), count, ctypes.byref(geometry),
         ctypes.byref(timing), _ptr(chan_bw), _ptr(t_read), _ptr(t_prog),
-        _ptr(address), _ptr(nbytes), _ptr(op), _ptr(arrival), n, _ptr(state),
+        None if admit is None else _ptr(admit), _ptr(address), _ptr(nbytes), _ptr(op), _ptr(arrival), n, _ptr(state),
         _ptr(done), _ptr(latency), _ptr(status), ctypes.byref(stats), threads)
     if rc != 0:
         raise MemoryError("oracle allocation failed")

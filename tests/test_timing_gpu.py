@@ -1,0 +1,257 @@
+"""Parity of the CUDA timing path with the CPU oracle (bit-exact).
+
+Every test runs the same seeded trace through libhbfsim_b200.so (C ABI) and
+through oracle/libhbf_oracle.so and requires identical completion ticks,
+latencies, statuses, carried state and counters.
+"""
+import numpy as np
+import pytest
+
+import hbf_oracle as ho
+from helpers import OracleRun, Setup, assert_same, gpu_run, make_context, to_device
+from hbfsim_b200 import workloads as wl
+
+pytestmark = pytest.mark.gpu
+GIB = 1 << 30
+
+
+@pytest.fixture
+def tmp(tmp_path):
+    return str(tmp_path)
+
+
+def c0_setup(model=3, **kw):
+    s = Setup(profile=wl.c0_profile(), model=model, **kw)
+    s.ranges = [(wl.RANGE_BASE, 64 * GIB, 1, 3)]
+    return s
+
+
+@pytest.mark.parametrize("model", [1, 3])
+@pytest.mark.parametrize("n", [1, 31, 2048, 2049, 70001])
+def test_c0_small_batches(tmp, model, n):
+    s = c0_setup(model)
+    ctx = make_context(s, tmp)
+    arrays = wl.c0_trace(n, seed=n)
+    ora = OracleRun(s)
+    want = ora.run(*arrays)
+    assert_same(gpu_run(ctx, arrays), want, f"model {model} n {n}")
+    assert np.array_equal(ctx.get_state(), ora.state)
+    st = ctx.batch_stats()
+    assert st["modeled"] == want[3]["modeled"]
+    assert st["max_done_ns"] == want[3]["max_done"]
+    assert st["latency_sum_ns"] == want[3]["latency_sum"]
+    if model == 1:
+        assert ctx.get_stats()["fast_modeled_ns"] == want[3]["fast_modeled_ns"]
+    ctx.close()
+
+
+@pytest.mark.parametrize("model", [1, 3])
+def test_c0_full_config(tmp, model):
+    """BASELINE config 0 at its full size: 1,048,576 accesses."""
+    s = c0_setup(model)
+    ctx = make_context(s, tmp)
+    arrays = wl.c0_trace(1 << 20, seed=0)
+    ora = OracleRun(s)
+    want = ora.run(*arrays, threads=8)
+    assert_same(gpu_run(ctx, arrays), want, "c0 full")
+    assert np.array_equal(ctx.get_state(), ora.state)
+    assert ctx.simulated_time() == want[3]["max_done"]
+    ctx.close()
+
+
+def test_batches_carry_state(tmp):
+    """Splitting a trace into ragged batches gives the single-batch result."""
+    s = c0_setup(3)
+    ctx = make_context(s, tmp)
+    arrays = wl.c0_trace(50000, seed=5)
+    ora = OracleRun(s)
+    want = ora.run(*arrays)
+    got = []
+    for lo, hi in [(0, 1), (1, 4097), (4097, 4100), (4100, 33333), (33333, 50000)]:
+        got.append(gpu_run(ctx, tuple(a[lo:hi] for a in arrays)))
+    cat = tuple(np.concatenate([g[k] for g in got]) for k in range(3))
+    assert_same(cat, want, "batched")
+    assert np.array_equal(ctx.get_state(), ora.state)
+
+
+def test_statuses_multi_range(tmp):
+    """Bypass, straddle, cross-page, permission, bad op, zero bytes and a
+    capacity-mode range, across several ranges with gaps."""
+    s = Setup(profile=wl.c0_profile(), model=3, stacks=2, stripe=8192)
+    page = 16384
+    base = 1 << 40
+    s.ranges = [(base, 5 * page + 100, 1, 3), (base + 8 * page, 3 * page, 1, 1),
+                (base + 16 * page, 2 * page, 2, 3), (base + 20 * page, 40 * page, 1, 2)]
+    ctx = make_context(s, tmp)
+    rng = np.random.default_rng(11)
+    n = 20000
+    addr = base - page + rng.integers(0, 64 * page, n).astype(np.uint64)
+    nbytes = rng.choice(np.array([0, 1, 8, 128, 4096, 9000], np.uint32), n)
+    op = rng.choice(np.array([0, 1, 2], np.uint8), n, p=[0.6, 0.35, 0.05])
+    arrival = np.cumsum(rng.integers(0, 50, n)).astype(np.uint64)
+    ora = OracleRun(s)
+    want = ora.run(addr, nbytes, op, arrival)
+    got = gpu_run(ctx, (addr, nbytes, op, arrival))
+    assert_same(got, want, "statuses")
+    kinds = set(np.unique(got[2]).tolist())
+    assert {1, 6, 8} <= kinds
+
+
+def test_misaligned_buffers(tmp):
+    s = c0_setup(3)
+    ctx = make_context(s, tmp)
+    import torch
+    arrays = wl.c0_trace(9000, seed=3)
+    dev = to_device(arrays)
+    sl = tuple(t[1:] for t in dev)  # 8/4/1-byte offsets: scalar path
+    out = ctx.submit(*sl)
+    torch.cuda.synchronize()
+    ora = OracleRun(s)
+    want = ora.run(*(a[1:] for a in arrays))
+    got = (out.done_ns.cpu().numpy().view(np.uint64), out.latency_ns.cpu().numpy().view(np.uint64),
+           out.status.cpu().numpy())
+    assert_same(got, want, "misaligned")
+
+
+def test_unsorted_batch_refused(tmp):
+    s = c0_setup(3)
+    ctx = make_context(s, tmp)
+    arrays = wl.c0_trace(5000, seed=1)
+    gpu_run(ctx, arrays)
+    before = ctx.get_state()
+    bad = list(arrays)
+    bad[3] = bad[3].copy()
+    bad[3][100], bad[3][101] = bad[3][101] + 5, bad[3][100]
+    gpu_run(ctx, tuple(bad))
+    from hbfsim_b200 import HbfsimError
+    with pytest.raises(HbfsimError):
+        ctx.flush()
+    assert np.array_equal(ctx.get_state(), before)
+    assert ctx.batch_stats()["device_errors"] == 1
+    # a batch that goes back in time relative to the previous batch
+    gpu_run(ctx, tuple(a[:10] for a in arrays))
+    with pytest.raises(HbfsimError):
+        ctx.flush()
+
+
+@pytest.mark.parametrize("model", [1, 3])
+def test_saturating_sequential_path(tmp, model):
+    """Arrivals near 2^64 take the exact saturating kernel."""
+    s = c0_setup(model)
+    ctx = make_context(s, tmp)
+    addr, nbytes, op, _ = wl.c0_trace(3000, seed=9)
+    arrival = (np.uint64(2**64 - 400_000) +
+               np.cumsum(np.full(3000, 100, np.uint64))).astype(np.uint64)
+    op[-100:] = 1  # writes: a + tPROG passes 2^64 and saturates
+    ora = OracleRun(s)
+    want = ora.run(addr, nbytes, op, arrival)
+    assert_same(gpu_run(ctx, (addr, nbytes, op, arrival)), want, "saturating")
+    assert (want[0] == np.uint64(2**64 - 1)).any()
+    assert np.array_equal(ctx.get_state(), ora.state)
+
+
+def test_refresh_throttle_admit_factors(tmp):
+    s = c0_setup(3, stacks=2)
+    ctx = make_context(s, tmp)
+    rng = np.random.default_rng(4)
+    refresh = rng.integers(0, 400, s.local_channels).astype(np.uint32)
+    throttle = np.array([1000, 1750], np.uint32)
+    admit = np.array([0, 150_000], np.uint64)
+    ctx.set_channel_factors(refresh, throttle, admit)
+    arrays = wl.c0_trace(40000, seed=8)
+    ora = OracleRun(s, refresh, throttle, admit)
+    assert_same(gpu_run(ctx, arrays), ora.run(*arrays), "factors")
+    r, t, a = ctx.channel_factors(s.local_channels, s.stacks)
+    assert np.array_equal(r, refresh) and np.array_equal(t, throttle) and np.array_equal(a, admit)
+
+
+def test_channel_shards_partition_the_trace(tmp):
+    """Each shard times only its channels; the union equals the unsharded run."""
+    arrays = wl.c0_trace(30000, seed=12)
+    full = OracleRun(c0_setup(3, stacks=4)).run(*arrays)
+    merged_done = np.zeros_like(full[0])
+    seen = np.zeros(full[0].size, bool)
+    for rank in range(3):
+        s = c0_setup(3, stacks=4, shard_rank=rank, shard_count=3)
+        ctx = make_context(s, f"{tmp}/r{rank}")
+        got = gpu_run(ctx, arrays)
+        assert_same(got, OracleRun(s).run(*arrays), f"shard {rank}")
+        mine = got[2] == 1
+        merged_done[mine] = got[0][mine]
+        assert not (seen & mine).any()
+        seen |= mine
+        ctx.close()
+    modeled = full[2] == 1
+    assert np.array_equal(seen, modeled)
+    assert np.array_equal(merged_done[modeled], full[0][modeled])
+
+
+@pytest.mark.parametrize("order,stacks,stripe", [("CWDP", 1, 4096), ("DPCW", 4, 512),
+                                                 ("PCDW", 2, 16384), ("WDCP", 3, 2048)])
+def test_decode_matches_oracle(tmp, order, stacks, stripe):
+    import torch
+    p = wl.c0_profile()
+    p["plane_allocation_scheme"] = order
+    s = Setup(profile=p, model=3, stacks=stacks, stripe=stripe)
+    s.ranges = [(wl.RANGE_BASE, 60 * GIB, 1, 3), (wl.RANGE_BASE + 80 * GIB, GIB, 1, 1)]
+    ctx = make_context(s, tmp)
+    rng = np.random.default_rng(2)
+    n = 50000
+    addr = (wl.RANGE_BASE + rng.integers(0, 82 * GIB, n)).astype(np.uint64)
+    nbytes = rng.choice(np.array([1, 128, 4096], np.uint32), n)
+    op = rng.integers(0, 2, n).astype(np.uint8)
+    dev = to_device((addr, nbytes, op, np.zeros(n, np.uint64)))
+    raw = ctx.decode(dev[0], dev[1], dev[2])
+    torch.cuda.synchronize()
+    dt = np.dtype([("media_address", "<u8"), ("page", "<u8"), ("status", "<u4"),
+                   ("range_index", "<u4"), ("stack", "<u4"), ("channel", "<u4"),
+                   ("die", "<u4"), ("plane", "<u4")])
+    got = np.frombuffer(raw.cpu().numpy().tobytes(), dtype=dt)
+    ora = OracleRun(s)
+    want = ho.decode(ora.ranges, ora.count, ora.geometry, addr, nbytes, op)
+    for f in ("status", "media_address"):
+        assert np.array_equal(got[f], want[f]), f
+    m = want["status"] == 1
+    for f in ("range_index", "stack", "channel", "die", "plane", "page"):
+        assert np.array_equal(got[f][m], want[f][m]), f
+
+
+def test_c1_slice_parity(tmp):
+    """A slice of the MoE decode trace (config 1 shape, 4 stacks)."""
+    s = Setup(profile=wl.c0_profile(), model=3, stacks=4, stripe=4096)
+    s.ranges = [(wl.RANGE_BASE, 60 * GIB, 1, 1)]
+    ctx = make_context(s, tmp)
+    bases, counts = wl.c1_segments(seed=1, steps=1, layers=3)
+    arrays = wl.expand_segments(bases, counts)
+    want = OracleRun(s).run(*arrays, threads=8)
+    got = gpu_run(ctx, arrays)
+    assert_same(got, want, "c1 slice")
+    assert (got[2] == 8).sum() == 3 * 16384  # attention weights bypass to HBM
+
+
+def test_checkpoint_resume_bit_exact(tmp):
+    s = c0_setup(3)
+    arrays = wl.c0_trace(20000, seed=21)
+    first = tuple(a[:9000] for a in arrays)
+    second = tuple(a[9000:] for a in arrays)
+    ctx = make_context(s, tmp)
+    gpu_run(ctx, first)
+    saved = ctx.get_state()
+    r1 = gpu_run(ctx, second)
+    ctx2 = make_context(s, f"{tmp}/b")
+    ctx2.set_state(saved)
+    # the resumed context must also know the last arrival ordering
+    r2 = gpu_run(ctx2, second)
+    assert_same(r2, (r1[0], r1[1], r1[2]), "resume")
+
+
+def test_host_buffer_path_matches_device_path(tmp):
+    import torch
+    s = c0_setup(3)
+    arrays = wl.c0_trace(300000, seed=30)
+    ctx = make_context(s, tmp)
+    want = OracleRun(s).run(*arrays)
+    pinned = [torch.from_numpy(a.view({8: np.int64, 4: np.int32, 1: np.uint8}[a.itemsize]))
+              .pin_memory() for a in arrays]
+    out = ctx.submit_host(*pinned)
+    assert_same((out.done_ns, out.latency_ns, out.status), want, "host path")
