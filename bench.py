@@ -128,9 +128,9 @@ def remap_to_shard(address, rank: int, world: int, range_base: int):
     return torch.where(inside, range_base + u2 * STRIPE + w, address)
 
 
-def make_trace(device, rank: int, world: int, seed: int = 0):
+def make_trace(device, rank: int, world: int, seed: int = 0, decode_steps: int = 8):
     from hbfsim_b200 import workloads as wl
-    bases, counts = wl.c1_segments(seed=seed)
+    bases, counts = wl.c1_segments(seed=seed, steps=decode_steps)
     address, nbytes, op, arrival = wl.expand_segments(bases, counts, device=device)
     address = remap_to_shard(address, rank, world, wl.RANGE_BASE)
     return address, nbytes, op, arrival, (bases, counts)
@@ -229,6 +229,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-steps", type=int, default=8,
+                    help="config-1 decode steps in the trace (8 = the full config; "
+                         "fewer only for small profiling captures)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
@@ -250,7 +253,8 @@ def main():
 
     tmp = tempfile.mkdtemp(prefix=f"hbfsim-bench-{rank}-")
     t_gen = time.perf_counter()
-    address, nbytes, op, arrival, segments = make_trace(device, rank, world)
+    address, nbytes, op, arrival, segments = make_trace(device, rank, world,
+                                                        decode_steps=args.decode_steps)
     n = address.numel()
     torch.cuda.synchronize()
     log(f"[rank {rank}] trace: {n} accesses generated in {time.perf_counter() - t_gen:.1f} s")
@@ -321,6 +325,36 @@ def main():
     path_gbs = (IN_BYTES + OUT_BYTES) * n / (ms * 1e-3) / 1e9
 
     # end to end through the host-buffer C-ABI call, pinned host memory
+    if args.e2e_steps <= 0:
+        e2e_rate, same = None, None
+    else:
+        e2e_rate, same = run_e2e(ctx, address, nbytes, op, arrival, out, stream, args,
+                                 world, device, n)
+    ctx.flush()
+    st = ctx.batch_stats()
+    counts = torch.bincount(out.status.to(torch.int64), minlength=10)
+    tot = torch.stack([counts[1], counts[8], counts[6], counts[9]])
+    if world > 1:
+        dist.all_reduce(tot)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, cores, sample = cpu_sample_rate(segments)
+        cpu = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+    if rank == 0:
+        emit(args, world, n, ms_max, e2e_rate, same, kernels, launches, dominant, achieved,
+             peak, peak_kind, traffic, alg, path_gbs, cpu, clocks, tot)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_e2e(ctx, address, nbytes, op, arrival, out, stream, args, world, device, n):
+    import torch
+    import torch.distributed as dist
+    from hbfsim_b200 import BatchResult
     host = [t.cpu().pin_memory() for t in (address, nbytes, op, arrival)]
     host_out = BatchResult(torch.empty(n, dtype=torch.int64).pin_memory(),
                            torch.empty(n, dtype=torch.int64).pin_memory(),
@@ -340,61 +374,47 @@ def main():
     e2e_t = torch.tensor([statistics.median(e2e_times)], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
-    e2e_rate = n * world / float(e2e_t.item())
     # the host path must agree with the device path
     same = torch.equal(host_out.done_ns, out.done_ns.cpu())
+    return n * world / float(e2e_t.item()), bool(same)
 
-    ctx.flush()
-    st = ctx.batch_stats()
-    per = max(1, st["batches"])  # counters are cumulative over every batch run
-    tot = torch.tensor([st["modeled"] // per, st["bypass"] // per,
-                        st["unsupported"] // per, st["foreign"] // per],
-                       dtype=torch.int64, device=device)
-    if world > 1:
-        dist.all_reduce(tot)
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, cores, sample = cpu_sample_rate(segments)
-        cpu = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
-
-    if rank == 0:
-        value = n * world / (ms_max * 1e-3)
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "u64", "data": "synthetic",
-            "config": {
-                "workload": "c1: MoE weight-streaming decode trace shaped like Qwen3-30B-A3B "
-                            "(48 layers x 128 experts, 8 steps x 32 tokens, top-8 Zipf(1.1), "
-                            "1 KiB reads) on 4 stacks x 16 channels x 4 dies x 4 planes per GPU",
-                "timing_model": "per-die max-plus (hbfsim mode 3)",
-                "accesses_per_gpu": n, "stripe_bytes": STRIPE,
-                "parallelism": f"channel shards x{world}",
-                "l2": "inputs 5.9 GB per GPU, larger than L2 (no flush needed)"},
-            "e2e": {"value": e2e_rate, "unit": UNIT, "h2d_bytes_per_step": IN_BYTES * n,
-                    "d2h_bytes_per_step": OUT_BYTES * n, "matches_device_path": bool(same)},
-            "roofline": {"bound": "hbm", "kernel": f"timing_pass_kernel ({dominant})",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic,
-                         "peak_source": peak_kind,
-                         "algorithmic_bytes_per_access": alg[dominant]},
-            "roofline_path": {"achieved": path_gbs, "frac": path_gbs / peak,
-                              "note": "38 B/access over the whole batch (3 launches)"},
-            "kernels": kernels,
-            "gpu_launches": launches,
-            "cpu_baseline": cpu,
-            "clocks": clocks,
-            "per_step_totals": {"modeled": int(tot[0]), "bypass": int(tot[1]),
-                       "unsupported": int(tot[2]), "foreign": int(tot[3])},
-        }
-        print(json.dumps(line), flush=True)
-    ctx.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
+def emit(args, world, n, ms_max, e2e_rate, same, kernels, launches, dominant, achieved,
+         peak, peak_kind, traffic, alg, path_gbs, cpu, clocks, tot):
+    value = n * world / (ms_max * 1e-3)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "u64", "data": "synthetic",
+        "config": {
+            "workload": "c1: MoE weight-streaming decode trace shaped like Qwen3-30B-A3B "
+                        "(48 layers x 128 experts, %d decode steps x 32 tokens, top-8 "
+                        "Zipf(1.1), 1 KiB reads) on 4 stacks x 16 channels x 4 dies x 4 "
+                        "planes per GPU" % args.decode_steps,
+            "timing_model": "per-die max-plus (hbfsim mode 3)",
+            "accesses_per_gpu": n, "stripe_bytes": STRIPE,
+            "parallelism": f"channel shards x{world}",
+            "l2": "inputs %.1f GB per GPU, larger than L2 (no flush needed)"
+                  % (n * IN_BYTES / 1e9)},
+        "e2e": None if e2e_rate is None else {
+            "value": e2e_rate, "unit": UNIT, "h2d_bytes_per_step": IN_BYTES * n,
+            "d2h_bytes_per_step": OUT_BYTES * n, "matches_device_path": same},
+        "roofline": {"bound": "hbm", "kernel": f"{dominant}",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "peak_source": peak_kind,
+                     "algorithmic_bytes_per_access": alg[dominant]},
+        "roofline_path": {"achieved": path_gbs, "frac": path_gbs / peak,
+                          "note": "38 B/access over the whole batch (all launches)"},
+        "kernels": kernels,
+        "gpu_launches": launches,
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+        "per_step_totals": {"modeled": int(tot[0]), "bypass": int(tot[1]),
+                            "unsupported": int(tot[2]), "foreign": int(tot[3])},
+    }
+    print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

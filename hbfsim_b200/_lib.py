@@ -139,6 +139,9 @@ SIGNATURES = {
     "hbfsim_advance_epoch_v1": (i32, [vp, dbl, vp]),
     "hbfsim_get_temperatures_v1": (i32, [vp, vp, u64]),
     "hbfsim_get_die_temperatures_v1": (i32, [vp, vp, u64]),
+    "hbfsim_advance_epoch_global_v1": (i32, [vp, dbl, vp, vp, vp]),
+    "hbfsim_copy_die_activity_v1": (i32, [vp, vp, vp, vp]),
+    "hbfsim_get_thermal_factors_v1": (i32, [vp, vp, vp, vp, vp]),
 }
 
 

@@ -29,6 +29,18 @@ class BatchResult:
     status: object
 
 
+CUDA_STREAM_LEGACY = 0x1  # cudaStreamLegacy: the legacy default stream
+
+
+def _stream_handle(stream) -> int:
+    """cudaStream_t for the C ABI.  torch reports the legacy default stream
+    as 0, which the C ABI reads as "the context's own stream", so map it to
+    cudaStreamLegacy to keep the caller's stream ordering."""
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream or CUDA_STREAM_LEGACY
+
+
 def _ptr(t) -> int:
     if t is None:
         return 0
@@ -124,7 +136,7 @@ class Context:
                               torch.empty(n, dtype=torch.uint8, device=dev))
         b = self._batch(n, address, nbytes, op, arrival, out.done_ns, out.latency_ns,
                         out.status)
-        s = stream.cuda_stream if stream is not None else torch.cuda.current_stream().cuda_stream
+        s = _stream_handle(stream)
         check(self._lib.hbfsim_submit_access_batch_v1(self.handle, ctypes.byref(b),
                                                       ctypes.c_void_p(s)),
               "hbfsim_submit_access_batch_v1")
@@ -147,7 +159,7 @@ class Context:
     def reset_state(self, stream=None) -> None:
         """Idle every die and channel at tick 0 (asynchronous on `stream`)."""
         import torch
-        s = stream.cuda_stream if stream is not None else torch.cuda.current_stream().cuda_stream
+        s = _stream_handle(stream)
         check(self._lib.hbfsim_reset_state_v1(self.handle, ctypes.c_void_p(s)),
               "hbfsim_reset_state_v1")
 
@@ -181,7 +193,7 @@ class Context:
         n = address.numel()
         out = torch.empty(n * ctypes.sizeof(_lib.DecodedV1), dtype=torch.uint8,
                           device=address.device)
-        s = stream.cuda_stream if stream is not None else torch.cuda.current_stream().cuda_stream
+        s = _stream_handle(stream)
         check(self._lib.hbfsim_decode_batch_v1(self.handle, _ptr(address), _ptr(nbytes),
                                                _ptr(op), n, _ptr(out), ctypes.c_void_p(s)),
               "hbfsim_decode_batch_v1")

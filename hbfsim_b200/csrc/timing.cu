@@ -203,7 +203,39 @@ struct ChanInfo {  // per local channel, staged in shared memory
     i64 t_prog;
     i64 admit;
     u64 bw;
+    u32 x_shift;   // transfer = ceil(bytes / 2^x_shift) when x_exact
+    u32 x_exact;   // 1e9 / bw reduces to 1 / 2^x_shift
 };
+
+// ceil(bytes * 1e9 / bw) * time_scale for one access of a channel.
+__device__ __forceinline__ u64 transfer_ticks(u32 bytes, const ChanInfo& ci, u32 scale)
+{
+    u64 x;
+    if (ci.x_exact)
+        x = (static_cast<u64>(bytes) + (u64{1} << ci.x_shift) - 1) >> ci.x_shift;
+    else
+        x = ceil_div_u64(static_cast<u64>(bytes) * 1000000000ull, ci.bw);
+    return sat_mul_u64(x, scale);
+}
+
+__device__ ChanInfo stage_channel(const TimingParams& tp, u32 c, bool die)
+{
+    ChanInfo ci{};
+    if (!die) return ci;
+    ci.t_read = tp.chan_t_read[c];
+    ci.t_prog = tp.chan_t_prog[c];
+    ci.admit = tp.chan_admit[c];
+    ci.bw = tp.chan_bw[c];
+    // reduce 1e9 / bw: exact shift when the quotient is 1 / 2^s
+    u64 a = 1000000000ull, b = ci.bw;
+    while (b) { const u64 r = a % b; a = b; b = r; }
+    const u64 num = 1000000000ull / a, den = ci.bw / a;
+    if (num == 1 && (den & (den - 1)) == 0) {
+        ci.x_exact = 1;
+        ci.x_shift = 63 - __clzll(den);
+    }
+    return ci;
+}
 
 template <int MODEL>
 struct StepModel;
@@ -245,6 +277,31 @@ struct StepModel<kModelDie> {
     }
 };
 
+// The same DIE step with the die state in registers (D known at compile
+// time): the die slot is read through a select chain and written with
+// predicated moves, so the loop-carried chain never goes through memory.
+template <int D>
+struct DieRegs {
+    i64 chan;
+    i64 die[D];
+    __device__ __forceinline__ i64 step(i64 a, u32 info, const ChanInfo& ci)
+    {
+        const i64 x = static_cast<i64>(info & 0xffffffu);
+        const u32 d = (info >> 24) & 15u;
+        const i64 t = (info >> 28) & 1u ? ci.t_prog : ci.t_read;
+        i64 cur = die[0];
+#pragma unroll
+        for (int j = 1; j < D; ++j) cur = d == static_cast<u32>(j) ? die[j] : cur;
+        const i64 start = imax(imax(a, chan), cur);
+        chan = start + x;
+        const i64 done = chan + t;
+#pragma unroll
+        for (int j = 0; j < D; ++j)
+            if (d == static_cast<u32>(j)) die[j] = done;
+        return done;
+    }
+};
+
 __device__ __forceinline__ u32 lane_id() { return threadIdx.x & 31u; }
 
 // Exclusive scan of `count` u32 values in shared memory by warp 0.
@@ -267,6 +324,245 @@ __device__ void warp0_exclusive_scan(u32* v, u32 count, u32* total)
     if (lane_id() == 0 && total) *total = carry;
 }
 
+// Shared-memory views of one tile.
+struct TileSmem {
+    u64* addr;    // -> done
+    u64* arr;     // -> latency
+    u32* bytes;   // -> packed info (transfer ticks | die << 24 | op << 28)
+    u8* op;       // -> status
+    u16* ord;     // channel-sorted order of modeled accesses
+    u16* key;
+    u16* rank;
+    u32* wcnt;    // [warps][C+1]
+    u32* seg;     // [C+2] segment starts
+    ChanInfo* chan;
+    unsigned long long* act;  // [C*D][2]
+    unsigned long long* red;
+};
+
+__device__ __forceinline__ TileSmem tile_views(unsigned char* smem, const PassArgs& A)
+{
+    TileSmem s;
+    s.addr = reinterpret_cast<u64*>(smem + A.off_addr);
+    s.arr = reinterpret_cast<u64*>(smem + A.off_arr);
+    s.bytes = reinterpret_cast<u32*>(smem + A.off_bytes);
+    s.op = smem + A.off_op;
+    s.ord = reinterpret_cast<u16*>(smem + A.off_ord);
+    s.key = reinterpret_cast<u16*>(smem + A.off_key);
+    s.rank = reinterpret_cast<u16*>(smem + A.off_rank);
+    s.wcnt = reinterpret_cast<u32*>(smem + A.off_wcnt);
+    s.seg = reinterpret_cast<u32*>(smem + A.off_seg);
+    s.chan = reinterpret_cast<ChanInfo*>(smem + A.off_chan);
+    s.act = reinterpret_cast<unsigned long long*>(smem + A.off_act);
+    s.red = reinterpret_cast<unsigned long long*>(smem + A.off_red);
+    return s;
+}
+
+// Pass-2 statistics of one thread.
+struct Stats7 {
+    unsigned long long modeled = 0, bypass = 0, unsup = 0, foreign = 0, lat = 0,
+                       max = 0, fast = 0;
+};
+
+// Stage one tile, decode it, and build the channel-sorted order in s.ord
+// with segment starts in s.seg (stable: warps own contiguous chunks, lanes
+// are ranked in index order with __match_any_sync).
+template <int MODEL, int PASS>
+__device__ __forceinline__ void load_decode_partition(const PassArgs& A, const TileSmem& s,
+                                                      u64 start, u32 nt, bool activity,
+                                                      Stats7& st)
+{
+    const u32 tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
+    const u32 T = A.T, C = A.C, D = A.tp.dies;
+    if (nt == T && A.vec) {
+        const uint4* g_addr = reinterpret_cast<const uint4*>(A.address + start);
+        const uint4* g_arr = reinterpret_cast<const uint4*>(A.arrival + start);
+        const uint4* g_bytes = reinterpret_cast<const uint4*>(A.bytes + start);
+        const uint4* g_op = reinterpret_cast<const uint4*>(A.op + start);
+        uint4* d_addr = reinterpret_cast<uint4*>(s.addr);
+        uint4* d_arr = reinterpret_cast<uint4*>(s.arr);
+        uint4* d_bytes = reinterpret_cast<uint4*>(s.bytes);
+        uint4* d_op = reinterpret_cast<uint4*>(s.op);
+        for (u32 k = tid; k < T / 2; k += kThreads) {
+            d_addr[k] = __ldcs(g_addr + k);
+            d_arr[k] = __ldcs(g_arr + k);
+        }
+        for (u32 k = tid; k < T / 4; k += kThreads) d_bytes[k] = __ldcs(g_bytes + k);
+        for (u32 k = tid; k < T / 16; k += kThreads) d_op[k] = __ldcs(g_op + k);
+    } else {
+        for (u32 k = tid; k < nt; k += kThreads) {
+            s.addr[k] = A.address[start + k];
+            s.arr[k] = A.arrival[start + k];
+            s.bytes[k] = A.bytes[start + k];
+            s.op[k] = A.op[start + k];
+        }
+    }
+    for (u32 k = tid; k < kWarps * (C + 1); k += kThreads) s.wcnt[k] = 0;
+    __syncthreads();
+
+    const u32 chunk = T / kWarps;
+    bool unsorted = false;
+    for (u32 j = 0; j < chunk; j += 32) {
+        const u32 e = warp * chunk + j + lane;
+        u32 key = C;
+        if (e < nt) {
+            const u64 a = s.addr[e];
+            const u32 b = s.bytes[e];
+            const u32 o = s.op[e];
+            const u64 arr = s.arr[e];
+            if (PASS == 1) {
+                const u64 prev = e > 0 ? s.arr[e - 1]
+                                       : (start > 0 ? A.arrival[start - 1] : *A.last_arrival);
+                if (arr < prev) unsorted = true;
+                if (arr >= kArrivalLimit) atomicOr(A.error, kErrNeedSeq);
+            }
+            const Decoded d = classify_decode(A.dp, a, b, o, MODEL == kModelDie);
+            u32 info = (o & 1u) << 28;
+            if (d.status == kModeled) {
+                key = MODEL == kModelDie ? d.local : 0u;
+                if (MODEL == kModelDie) {
+                    const u64 x = transfer_ticks(b, s.chan[key], A.tp.time_scale);
+                    if (x > 0xffffffull) atomicOr(A.error, kErrNeedSeq);
+                    info |= static_cast<u32>(x & 0xffffffull) | (d.die << 24);
+                    if (activity) {
+                        if (o) atomicAdd(&s.act[2 * (key * D + d.die) + 1], 1ull);
+                        else atomicAdd(&s.act[2 * (key * D + d.die)],
+                                       static_cast<unsigned long long>(b));
+                    }
+                }
+                if (PASS == 2) ++st.modeled;
+            } else if (PASS == 2) {
+                s.addr[e] = arr;  // done = arrival
+                s.arr[e] = 0;     // latency 0
+                if (d.status == kBypass) ++st.bypass;
+                else if (d.status == kForeign) ++st.foreign;
+                else ++st.unsup;
+            }
+            s.bytes[e] = info;
+            s.op[e] = static_cast<u8>(d.status);
+        }
+        const u32 peers = __match_any_sync(0xffffffffu, key);
+        const u32 before = __popc(peers & ((1u << lane) - 1u));
+        const u32 base = s.wcnt[warp * (C + 1) + key];
+        __syncwarp();
+        if (before == 0) s.wcnt[warp * (C + 1) + key] = base + __popc(peers);
+        if (e < nt) {
+            s.key[e] = static_cast<u16>(key);
+            s.rank[e] = static_cast<u16>(base + before);
+        }
+        __syncwarp();
+    }
+    if (PASS == 1 && unsorted) atomicOr(A.error, kErrUnsorted);
+    __syncthreads();
+
+    // segment offsets: key-major, warp-minor
+    for (u32 c = tid; c < C; c += kThreads) {
+        u32 total = 0;
+        for (u32 w = 0; w < kWarps; ++w) total += s.wcnt[w * (C + 1) + c];
+        s.seg[c] = total;
+    }
+    __syncthreads();
+    warp0_exclusive_scan(s.seg, C, &s.seg[C]);
+    __syncthreads();
+    for (u32 c = tid; c < C; c += kThreads) {
+        u32 running = s.seg[c];
+        for (u32 w = 0; w < kWarps; ++w) {
+            const u32 cnt = s.wcnt[w * (C + 1) + c];
+            s.wcnt[w * (C + 1) + c] = running;
+            running += cnt;
+        }
+    }
+    __syncthreads();
+    for (u32 j = 0; j < chunk; j += 32) {
+        const u32 e = warp * chunk + j + lane;
+        if (e < nt) {
+            const u32 key = s.key[e];
+            if (key < C) s.ord[s.wcnt[warp * (C + 1) + key] + s.rank[e]] = static_cast<u16>(e);
+        }
+    }
+    __syncthreads();
+}
+
+__device__ __forceinline__ void store_tile(const PassArgs& A, const TileSmem& s, u64 start,
+                                           u32 nt)
+{
+    const u32 tid = threadIdx.x, T = A.T;
+    if (nt == T && A.vec) {
+        uint4* g_done = reinterpret_cast<uint4*>(A.done + start);
+        uint4* g_lat = reinterpret_cast<uint4*>(A.latency + start);
+        uint4* g_st = reinterpret_cast<uint4*>(A.status + start);
+        const uint4* d_done = reinterpret_cast<const uint4*>(s.addr);
+        const uint4* d_lat = reinterpret_cast<const uint4*>(s.arr);
+        const uint4* d_st = reinterpret_cast<const uint4*>(s.op);
+        for (u32 k = tid; k < T / 2; k += kThreads) {
+            __stcs(g_done + k, d_done[k]);
+            __stcs(g_lat + k, d_lat[k]);
+        }
+        for (u32 k = tid; k < T / 16; k += kThreads) __stcs(g_st + k, d_st[k]);
+    } else {
+        for (u32 k = tid; k < nt; k += kThreads) {
+            A.done[start + k] = s.addr[k];
+            A.latency[start + k] = s.arr[k];
+            A.status[start + k] = s.op[k];
+        }
+    }
+}
+
+// Block-reduce the pass-2 statistics and the die activity; one atomic each
+// per CTA.
+__device__ __forceinline__ void flush_stats(const PassArgs& A, const TileSmem& s,
+                                            const Stats7& st, bool activity)
+{
+    const u32 tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
+    const u32 C = A.C, D = A.tp.dies;
+    if (activity) {
+        for (u32 k = tid; k < C * D; k += kThreads) {
+            if (s.act[2 * k]) atomicAdd(&A.tp.die_read_bytes[k], s.act[2 * k]);
+            if (s.act[2 * k + 1]) atomicAdd(&A.tp.die_writes[k], s.act[2 * k + 1]);
+        }
+    }
+    unsigned long long vals[7] = {st.modeled, st.bypass, st.unsup, st.foreign,
+                                  st.lat, st.max, st.fast};
+#pragma unroll
+    for (int k = 0; k < 7; ++k) {
+        unsigned long long v = vals[k];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long y = __shfl_down_sync(0xffffffffu, v, o);
+            v = k == 5 ? (y > v ? y : v) : v + y;
+        }
+        if (lane == 0) s.red[k * kWarps + warp] = v;
+    }
+    __syncthreads();
+    if (tid < 7) {
+        unsigned long long v = 0;
+        for (u32 w = 0; w < kWarps; ++w) {
+            const unsigned long long y = s.red[tid * kWarps + w];
+            v = tid == 5 ? (y > v ? y : v) : v + y;
+        }
+        unsigned long long* dst = &A.counters->modeled;
+        if (tid == 5) atomicMax(&A.counters->max_done, v);
+        else if (v) atomicAdd(tid == 6 ? &A.counters->fast_modeled_ns : dst + tid, v);
+    }
+}
+
+__device__ __forceinline__ void prologue(const PassArgs& A, const TileSmem& s, bool die,
+                                         bool activity)
+{
+    const u32 tid = threadIdx.x, C = A.C, D = A.tp.dies;
+    for (u32 c = tid; c < C; c += kThreads) s.chan[c] = stage_channel(A.tp, c, die);
+    if (activity)
+        for (u32 k = tid; k < 2 * C * D; k += kThreads) s.act[k] = 0;
+    if (blockIdx.x == 0 && A.state_in) {
+        // the parallel path needs every carried tick below 2^59
+        for (u32 k = tid; k < C * A.K; k += kThreads)
+            if (A.state_in[k] >= kArrivalLimit) atomicOr(A.error, kErrNeedSeq);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Piece kernel: generic K; channel segments are cut into pieces of <= L
+// accesses whose max-plus matrices are built by replaying each column.
 template <int MODEL, int PASS>
 __global__ void __launch_bounds__(kThreads, 2)
 timing_pass_kernel(const PassArgs args)
@@ -274,193 +570,46 @@ timing_pass_kernel(const PassArgs args)
     extern __shared__ __align__(16) unsigned char smem[];
     const PassArgs& A = args;
     const u32 tid = threadIdx.x;
-    const u32 warp = tid >> 5;
-    const u32 lane = tid & 31u;
     const u32 T = A.T, L = A.L, C = A.C, K = A.K;
-
-    u64* s_addr = reinterpret_cast<u64*>(smem + A.off_addr);   // -> done
-    u64* s_arr = reinterpret_cast<u64*>(smem + A.off_arr);     // -> latency
-    u32* s_bytes = reinterpret_cast<u32*>(smem + A.off_bytes); // -> xinfo
-    u8* s_op = smem + A.off_op;                                // -> status
-    u16* s_ord = reinterpret_cast<u16*>(smem + A.off_ord);
-    u16* s_key = reinterpret_cast<u16*>(smem + A.off_key);
-    u16* s_rank = reinterpret_cast<u16*>(smem + A.off_rank);
-    u32* s_wcnt = reinterpret_cast<u32*>(smem + A.off_wcnt);   // [W][C+1]
-    u32* s_seg = reinterpret_cast<u32*>(smem + A.off_seg);     // [C+2]
+    const TileSmem s = tile_views(smem, A);
     u32* s_pbase = reinterpret_cast<u32*>(smem + A.off_pbase); // [C+2]
     u16* s_pchan = reinterpret_cast<u16*>(smem + A.off_pchan);
     i64* s_pm = reinterpret_cast<i64*>(smem + A.off_pm);       // [P][K][K+1]
     i64* s_pin = reinterpret_cast<i64*>(smem + A.off_pin);     // [P][K]
-    i64* s_die = reinterpret_cast<i64*>(smem + A.off_die);     // [16][threads]
-    ChanInfo* s_chan = reinterpret_cast<ChanInfo*>(smem + A.off_chan);
-    unsigned long long* s_act =
-        reinterpret_cast<unsigned long long*>(smem + A.off_act); // [C*D][2]
-    unsigned long long* s_red =
-        reinterpret_cast<unsigned long long*>(smem + A.off_red);
+    i64* s_die = reinterpret_cast<i64*>(smem + A.off_die);     // [D][threads]
 
-    if (PASS == 2 && *A.error != 0) return;  // pass 1 refused the batch
-
+    if (PASS == 2 && *A.error != 0) return;  // pass 1 refused or rerouted the batch
     const u32 KK = K + 1;
-    const u32 D = A.tp.dies;
-    for (u32 c = tid; c < C; c += kThreads) {
-        ChanInfo ci{};
-        if (MODEL == kModelDie) {
-            ci.t_read = A.tp.chan_t_read[c];
-            ci.t_prog = A.tp.chan_t_prog[c];
-            ci.admit = A.tp.chan_admit[c];
-            ci.bw = A.tp.chan_bw[c];
-        }
-        s_chan[c] = ci;
-    }
-    const bool activity = PASS == 2 && MODEL == kModelDie &&
-                          A.tp.die_read_bytes != nullptr;
-    if (activity)
-        for (u32 k = tid; k < 2 * C * D; k += kThreads) s_act[k] = 0;
+    const bool activity = PASS == 2 && MODEL == kModelDie && A.tp.die_read_bytes != nullptr;
+    if (PASS == 1) prologue(A, s, MODEL == kModelDie, false);
+    else prologue(A, s, MODEL == kModelDie, activity);
 
     i64* agg = A.agg + static_cast<u64>(blockIdx.x) * C * K * KK;
     i64* carry = A.incoming + static_cast<u64>(blockIdx.x) * C * K;
-    if (PASS == 1 && blockIdx.x == 0) {
-        // the parallel path needs every carried tick below 2^59
-        for (u32 k = tid; k < C * K; k += kThreads)
-            if (A.state_in[k] >= kArrivalLimit) atomicOr(A.error, kErrNeedSeq);
-    }
     if (PASS == 1) {
-        // R_b starts as the identity map: out_i = in_i
-        for (u32 k = tid; k < C * K * KK; k += kThreads) {
+        for (u32 k = tid; k < C * K * KK; k += kThreads) {  // identity map
             const u32 col = k % KK, row = (k / KK) % K;
             agg[k] = col == row ? 0 : kNeg;
         }
     }
     __syncthreads();
-
-    // per-thread statistics (pass 2)
-    unsigned long long st_modeled = 0, st_bypass = 0, st_unsup = 0,
-                       st_foreign = 0, st_lat = 0, st_max = 0, st_fast = 0;
+    Stats7 st;
 
     const u64 tile_first = static_cast<u64>(blockIdx.x) * A.tiles_per_cta;
     for (u32 tt = 0; tt < A.tiles_per_cta; ++tt) {
         const u64 start = (tile_first + tt) * T;
         if (start >= A.n) break;
         const u32 nt = static_cast<u32>(A.n - start < T ? A.n - start : T);
+        load_decode_partition<MODEL, PASS>(A, s, start, nt, activity, st);
 
-        // ---- stage inputs (16-byte vector loads for full tiles)
-        if (nt == T && A.vec) {
-            const uint4* g_addr = reinterpret_cast<const uint4*>(A.address + start);
-            const uint4* g_arr = reinterpret_cast<const uint4*>(A.arrival + start);
-            const uint4* g_bytes = reinterpret_cast<const uint4*>(A.bytes + start);
-            const uint4* g_op = reinterpret_cast<const uint4*>(A.op + start);
-            uint4* d_addr = reinterpret_cast<uint4*>(s_addr);
-            uint4* d_arr = reinterpret_cast<uint4*>(s_arr);
-            uint4* d_bytes = reinterpret_cast<uint4*>(s_bytes);
-            uint4* d_op = reinterpret_cast<uint4*>(s_op);
-            for (u32 k = tid; k < T / 2; k += kThreads) {
-                d_addr[k] = __ldcs(g_addr + k);
-                d_arr[k] = __ldcs(g_arr + k);
-            }
-            for (u32 k = tid; k < T / 4; k += kThreads) d_bytes[k] = __ldcs(g_bytes + k);
-            for (u32 k = tid; k < T / 16; k += kThreads) d_op[k] = __ldcs(g_op + k);
-        } else {
-            for (u32 k = tid; k < nt; k += kThreads) {
-                s_addr[k] = A.address[start + k];
-                s_arr[k] = A.arrival[start + k];
-                s_bytes[k] = A.bytes[start + k];
-                s_op[k] = A.op[start + k];
-            }
-        }
-        for (u32 k = tid; k < kWarps * (C + 1); k += kThreads) s_wcnt[k] = 0;
+        for (u32 c = tid; c < C; c += kThreads) s_pbase[c] = (s.seg[c + 1] - s.seg[c] + L - 1) / L;
         __syncthreads();
-
-        // ---- decode + stable ranking by local channel (warp-contiguous)
-        const u32 chunk = T / kWarps;
-        bool unsorted = false;
-        for (u32 j = 0; j < chunk; j += 32) {
-            const u32 e = warp * chunk + j + lane;
-            u32 key = C;
-            if (e < nt) {
-                const u64 a = s_addr[e];
-                const u32 b = s_bytes[e];
-                const u32 o = s_op[e];
-                const u64 arr = s_arr[e];
-                if (PASS == 1) {
-                    const u64 prev = e > 0 ? s_arr[e - 1]
-                                 : (start > 0 ? A.arrival[start - 1] : *A.last_arrival);
-                    if (arr < prev) unsorted = true;
-                    if (arr >= kArrivalLimit) atomicOr(A.error, kErrNeedSeq);
-                }
-                const Decoded d = classify_decode(A.dp, a, b, o, MODEL == kModelDie);
-                u32 info = (o & 1u) << 28;
-                if (d.status == kModeled) {
-                    key = MODEL == kModelDie ? d.local : 0u;
-                    if (MODEL == kModelDie) {
-                        const u64 x = sat_mul_u64(
-                            ceil_div_u64(static_cast<u64>(b) * 1000000000ull,
-                                         s_chan[key].bw),
-                            A.tp.time_scale);
-                        if (x > 0xffffffull) atomicOr(A.error, kErrNeedSeq);
-                        info |= static_cast<u32>(x & 0xffffffull) | (d.die << 24);
-                        if (activity) {
-                            if (o) atomicAdd(&s_act[2 * (key * D + d.die) + 1], 1ull);
-                            else atomicAdd(&s_act[2 * (key * D + d.die)],
-                                           static_cast<unsigned long long>(b));
-                        }
-                    }
-                    if (PASS == 2) ++st_modeled;
-                } else if (PASS == 2) {
-                    s_addr[e] = arr;  // done = arrival
-                    s_arr[e] = 0;     // latency 0
-                    if (d.status == kBypass) ++st_bypass;
-                    else if (d.status == kForeign) ++st_foreign;
-                    else ++st_unsup;
-                }
-                s_bytes[e] = info;
-                s_op[e] = static_cast<u8>(d.status);
-            }
-            const u32 peers = __match_any_sync(0xffffffffu, key);
-            const u32 before = __popc(peers & ((1u << lane) - 1u));
-            const u32 base = s_wcnt[warp * (C + 1) + key];
-            __syncwarp();
-            if (before == 0) s_wcnt[warp * (C + 1) + key] = base + __popc(peers);
-            if (e < nt) {
-                s_key[e] = static_cast<u16>(key);
-                s_rank[e] = static_cast<u16>(base + before);
-            }
-            __syncwarp();
-        }
-        if (PASS == 1 && unsorted) atomicOr(A.error, kErrUnsorted);
-        __syncthreads();
-
-        // ---- segment offsets: key-major, warp-minor
-        for (u32 c = tid; c < C; c += kThreads) {
-            u32 total = 0;
-            for (u32 w = 0; w < kWarps; ++w) total += s_wcnt[w * (C + 1) + c];
-            s_seg[c] = total;
-            s_pbase[c] = (total + L - 1) / L;
-        }
-        __syncthreads();
-        warp0_exclusive_scan(s_seg, C, &s_seg[C]);
         warp0_exclusive_scan(s_pbase, C, &s_pbase[C]);
         __syncthreads();
-        for (u32 c = tid; c < C; c += kThreads) {
-            u32 running = s_seg[c];
-            for (u32 w = 0; w < kWarps; ++w) {
-                const u32 cnt = s_wcnt[w * (C + 1) + c];
-                s_wcnt[w * (C + 1) + c] = running;
-                running += cnt;
-            }
-            for (u32 p = s_pbase[c]; p < s_pbase[c + 1]; ++p)
-                s_pchan[p] = static_cast<u16>(c);
-        }
-        __syncthreads();
-        for (u32 j = 0; j < chunk; j += 32) {
-            const u32 e = warp * chunk + j + lane;
-            if (e < nt) {
-                const u32 key = s_key[e];
-                if (key < C) s_ord[s_wcnt[warp * (C + 1) + key] + s_rank[e]] = static_cast<u16>(e);
-            }
-        }
+        for (u32 c = tid; c < C; c += kThreads)
+            for (u32 p = s_pbase[c]; p < s_pbase[c + 1]; ++p) s_pchan[p] = static_cast<u16>(c);
         __syncthreads();
 
-        // ---- channel groups: piece matrices, fold / propagate, replay
         for (u32 cg0 = 0; cg0 < C; cg0 += A.group_channels) {
             const u32 cg1 = cg0 + A.group_channels < C ? cg0 + A.group_channels : C;
             const u32 p0 = s_pbase[cg0];
@@ -472,18 +621,18 @@ timing_pass_kernel(const PassArgs args)
                 const u32 pl = q % np, r = q / np;
                 const u32 pg = p0 + pl;
                 const u32 c = s_pchan[pg];
-                const u32 first = s_seg[c] + (pg - s_pbase[c]) * L;
-                const u32 seg_end = s_seg[c + 1];
+                const u32 first = s.seg[c] + (pg - s_pbase[c]) * L;
+                const u32 seg_end = s.seg[c + 1];
                 const u32 last = first + L < seg_end ? first + L : seg_end;
-                const ChanInfo ci = s_chan[c];
+                const ChanInfo ci = s.chan[c];
                 i64 chan = r == 0 ? 0 : kNeg;
                 i64* die = s_die + tid;
                 for (u32 j = 1; j < K; ++j) die[(j - 1) * kThreads] = r == j ? 0 : kNeg;
                 const bool real = r == K;
                 for (u32 k = first; k < last; ++k) {
-                    const u32 e = s_ord[k];
-                    const i64 a = real ? imax(static_cast<i64>(s_arr[e]), ci.admit) : kNeg;
-                    StepModel<MODEL>::step(chan, die, kThreads, a, s_bytes[e], ci, A.tp);
+                    const u32 e = s.ord[k];
+                    const i64 a = real ? imax(static_cast<i64>(s.arr[e]), ci.admit) : kNeg;
+                    StepModel<MODEL>::step(chan, die, kThreads, a, s.bytes[e], ci, A.tp);
                 }
                 i64* col = s_pm + static_cast<u64>(pl) * K * KK + r;
                 col[0] = chan;
@@ -539,92 +688,137 @@ timing_pass_kernel(const PassArgs args)
                 for (u32 pl = tid; pl < np; pl += kThreads) {
                     const u32 pg = p0 + pl;
                     const u32 c = s_pchan[pg];
-                    const u32 first = s_seg[c] + (pg - s_pbase[c]) * L;
-                    const u32 seg_end = s_seg[c + 1];
+                    const u32 first = s.seg[c] + (pg - s_pbase[c]) * L;
+                    const u32 seg_end = s.seg[c + 1];
                     const u32 last = first + L < seg_end ? first + L : seg_end;
-                    const ChanInfo ci = s_chan[c];
+                    const ChanInfo ci = s.chan[c];
                     const i64* pin = s_pin + static_cast<u64>(pl) * K;
                     i64 chan = pin[0];
                     i64* die = s_die + tid;
                     for (u32 j = 1; j < K; ++j) die[(j - 1) * kThreads] = pin[j];
                     for (u32 k = first; k < last; ++k) {
-                        const u32 e = s_ord[k];
-                        const u32 info = s_bytes[e];
-                        const u64 arr = s_arr[e];
+                        const u32 e = s.ord[k];
+                        const u32 info = s.bytes[e];
+                        const u64 arr = s.arr[e];
                         const i64 a = imax(static_cast<i64>(arr), ci.admit);
                         const i64 done = StepModel<MODEL>::step(chan, die, kThreads, a,
                                                                 info, ci, A.tp);
                         const u64 ud = static_cast<u64>(done);
-                        s_addr[e] = ud;
-                        s_arr[e] = ud - arr;
-                        st_lat += ud - arr;
-                        st_max = ud > st_max ? ud : st_max;
+                        s.addr[e] = ud;
+                        s.arr[e] = ud - arr;
+                        st.lat += ud - arr;
+                        st.max = ud > st.max ? ud : st.max;
                         if (MODEL == kModelFast)
-                            st_fast += (info >> 28) & 1u ? A.tp.fast_service_prog
+                            st.fast += (info >> 28) & 1u ? A.tp.fast_service_prog
                                                          : A.tp.fast_service_read;
                     }
                 }
                 __syncthreads();
             }
         }
+        if (PASS == 2) store_tile(A, s, start, nt);
+        __syncthreads();
+    }
+    if (PASS == 2) flush_stats(A, s, st, activity);
+}
 
-        if (PASS == 2) {
-            // ---- write the tile's results
-            if (nt == T && A.vec) {
-                uint4* g_done = reinterpret_cast<uint4*>(A.done + start);
-                uint4* g_lat = reinterpret_cast<uint4*>(A.latency + start);
-                uint4* g_st = reinterpret_cast<uint4*>(A.status + start);
-                const uint4* d_done = reinterpret_cast<const uint4*>(s_addr);
-                const uint4* d_lat = reinterpret_cast<const uint4*>(s_arr);
-                const uint4* d_st = reinterpret_cast<const uint4*>(s_op);
-                for (u32 k = tid; k < T / 2; k += kThreads) {
-                    __stcs(g_done + k, d_done[k]);
-                    __stcs(g_lat + k, d_lat[k]);
+// ---------------------------------------------------------------------------
+// Direct kernel (die model, D dies known at compile time, enough channels
+// for parallelism): no pieces.  Pass 1: thread item (c, r) carries column r
+// of channel c's range aggregate in registers through every tile of the
+// CTA's range.  Pass 2: thread c carries channel c's exact state.
+template <int PASS, int D>
+__global__ void __launch_bounds__(kThreads, 3)
+direct_pass_kernel(const PassArgs args)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    const PassArgs& A = args;
+    const u32 tid = threadIdx.x;
+    constexpr u32 K = D + 1, KK = D + 2;
+    const u32 T = A.T, C = A.C;
+    const TileSmem s = tile_views(smem, A);
+    if (PASS == 2 && *A.error != 0) return;
+    const bool activity = PASS == 2 && A.tp.die_read_bytes != nullptr;
+    prologue(A, s, true, activity);
+
+    // register state: pass 1 holds up to two (c, r) columns, pass 2 one channel
+    constexpr int kItems = PASS == 1 ? 2 : 1;
+    DieRegs<D> reg[kItems];
+    u32 item_c[kItems], item_r[kItems];
+    bool item_on[kItems];
+    i64* agg = A.agg + static_cast<u64>(blockIdx.x) * C * K * KK;
+    i64* carry = A.incoming + static_cast<u64>(blockIdx.x) * C * K;
+#pragma unroll
+    for (int it = 0; it < kItems; ++it) {
+        const u32 q = tid + it * kThreads;
+        item_on[it] = PASS == 1 ? q < C * KK : q < C;
+        item_c[it] = PASS == 1 ? q / KK : q;
+        item_r[it] = PASS == 1 ? q % KK : 0;
+        if (!item_on[it]) continue;
+        if (PASS == 1) {  // identity column e_r (r == K: no constant yet)
+            reg[it].chan = item_r[it] == 0 ? 0 : kNeg;
+#pragma unroll
+            for (int j = 0; j < D; ++j) reg[it].die[j] = item_r[it] == static_cast<u32>(j + 1) ? 0 : kNeg;
+        } else {
+            const i64* cv = carry + static_cast<u64>(item_c[it]) * K;
+            reg[it].chan = cv[0];
+#pragma unroll
+            for (int j = 0; j < D; ++j) reg[it].die[j] = cv[1 + j];
+        }
+    }
+    __syncthreads();
+    Stats7 st;
+
+    const u64 tile_first = static_cast<u64>(blockIdx.x) * A.tiles_per_cta;
+    for (u32 tt = 0; tt < A.tiles_per_cta; ++tt) {
+        const u64 start = (tile_first + tt) * T;
+        if (start >= A.n) break;
+        const u32 nt = static_cast<u32>(A.n - start < T ? A.n - start : T);
+        load_decode_partition<kModelDie, PASS>(A, s, start, nt, activity, st);
+#pragma unroll
+        for (int it = 0; it < kItems; ++it) {
+            if (!item_on[it]) continue;
+            const u32 c = item_c[it];
+            const u32 first = s.seg[c], last = s.seg[c + 1];
+            const ChanInfo ci = s.chan[c];
+            if (PASS == 1) {
+                const bool real = item_r[it] == K;
+#pragma unroll 4
+                for (u32 k = first; k < last; ++k) {
+                    const u32 e = s.ord[k];
+                    const i64 a = real ? imax(static_cast<i64>(s.arr[e]), ci.admit) : kNeg;
+                    reg[it].step(a, s.bytes[e], ci);
                 }
-                for (u32 k = tid; k < T / 16; k += kThreads) __stcs(g_st + k, d_st[k]);
             } else {
-                for (u32 k = tid; k < nt; k += kThreads) {
-                    A.done[start + k] = s_addr[k];
-                    A.latency[start + k] = s_arr[k];
-                    A.status[start + k] = s_op[k];
+#pragma unroll 4
+                for (u32 k = first; k < last; ++k) {
+                    const u32 e = s.ord[k];
+                    const u64 arr = s.arr[e];
+                    const i64 done = reg[it].step(imax(static_cast<i64>(arr), ci.admit),
+                                                  s.bytes[e], ci);
+                    const u64 ud = static_cast<u64>(done);
+                    s.addr[e] = ud;
+                    s.arr[e] = ud - arr;
+                    st.lat += ud - arr;
+                    st.max = ud > st.max ? ud : st.max;
                 }
             }
         }
         __syncthreads();
-    }
-
-    if (PASS == 2) {
-        if (activity) {
-            for (u32 k = tid; k < C * D; k += kThreads) {
-                if (s_act[2 * k]) atomicAdd(&A.tp.die_read_bytes[k], s_act[2 * k]);
-                if (s_act[2 * k + 1]) atomicAdd(&A.tp.die_writes[k], s_act[2 * k + 1]);
-            }
-        }
-        // block-reduce the statistics, one atomic each per CTA
-        unsigned long long vals[7] = {st_modeled, st_bypass, st_unsup, st_foreign,
-                                      st_lat, st_max, st_fast};
-#pragma unroll
-        for (int k = 0; k < 7; ++k) {
-            unsigned long long v = vals[k];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const unsigned long long y = __shfl_down_sync(0xffffffffu, v, o);
-                v = k == 5 ? (y > v ? y : v) : v + y;
-            }
-            if (lane == 0) s_red[k * kWarps + warp] = v;
-        }
+        if (PASS == 2) store_tile(A, s, start, nt);
         __syncthreads();
-        if (tid < 7) {
-            unsigned long long v = 0;
-            for (u32 w = 0; w < kWarps; ++w) {
-                const unsigned long long y = s_red[tid * kWarps + w];
-                v = tid == 5 ? (y > v ? y : v) : v + y;
-            }
-            unsigned long long* dst = &A.counters->modeled;
-            if (tid == 5) atomicMax(&A.counters->max_done, v);
-            else if (v) atomicAdd(tid == 6 ? &A.counters->fast_modeled_ns : dst + tid, v);
+    }
+#pragma unroll
+    for (int it = 0; it < kItems; ++it) {
+        if (!item_on[it]) continue;
+        if (PASS == 1) {
+            i64* col = agg + static_cast<u64>(item_c[it]) * K * KK + item_r[it];
+            col[0] = reg[it].chan;
+#pragma unroll
+            for (int j = 0; j < D; ++j) col[(j + 1) * KK] = reg[it].die[j];
         }
     }
+    if (PASS == 2) flush_stats(A, s, st, activity);
 }
 
 // Sequential scan of the CTA range aggregates: incoming_b = R_{b-1} ...
@@ -821,8 +1015,9 @@ struct Launch {
 static u32 align_up(u32 v, u32 a) { return (v + a - 1) / a * a; }
 
 // Shared-memory layout for a tile of T accesses with C channels, K words.
+// The piece arrays exist only in piece mode.
 static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
-                  u32 group_channels)
+                  u32 group_channels, bool direct)
 {
     u32 off = 0;
     auto take = [&](u32 bytes) {
@@ -831,7 +1026,7 @@ static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
         off += bytes;
         return at;
     };
-    const u32 pm_capacity = T / L + group_channels;
+    const u32 pm_capacity = direct ? 0 : T / L + group_channels;
     a.T = T;
     a.L = L;
     a.C = C;
@@ -847,14 +1042,16 @@ static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
     a.off_rank = take(2 * T);
     a.off_wcnt = take(4 * kWarps * (C + 1));
     a.off_seg = take(4 * (C + 2));
-    a.off_pbase = take(4 * (C + 2));
-    a.off_pchan = take(2 * (T / L + C + 1));
-    a.off_pm = take(8 * pm_capacity * K * (K + 1));
-    a.off_pin = take(8 * pm_capacity * K);
-    a.off_die = take(8 * 16 * kThreads);
     a.off_chan = take(static_cast<u32>(sizeof(ChanInfo)) * C);
     a.off_act = take(16 * C * (dies ? dies : 1));
     a.off_red = take(8 * 8 * kWarps);
+    if (!direct) {
+        a.off_pbase = take(4 * (C + 2));
+        a.off_pchan = take(2 * (T / L + C + 1));
+        a.off_pm = take(8 * pm_capacity * K * (K + 1));
+        a.off_pin = take(8 * pm_capacity * K);
+        a.off_die = take(8 * (dies ? dies : 1) * kThreads);
+    }
     return align_up(off, 16);
 }
 
@@ -864,22 +1061,37 @@ static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
 // (called by context.cu; not part of the C ABI)
 namespace hbfb {
 
+static bool direct_supported(u32 C, u32 K, u32 dies)
+{
+    const bool d_ok = dies == 1 || dies == 2 || dies == 4 || dies == 8;
+    return dies > 0 && d_ok && K == dies + 1 && C * (K + 1) <= 2 * kThreads && C <= kThreads;
+}
+
 int plan_batch(u64 n, u32 C, u32 K, u32 dies, int sm_count, BatchPlan* plan)
 {
-    const u32 L = 32;
-    const u32 smem_limit = 110 * 1024;  // two CTAs per SM
-    u32 T = 2048;
-    u32 group = C;
     PassArgs probe{};
-    for (;;) {
-        const u32 bytes = layout(probe, T, L, C, K, dies, group);
-        if (bytes <= smem_limit) break;
-        if (group > 8) group = (group + 1) / 2;
-        else if (T > 512) T /= 2;
-        else return -1;
+    const bool direct = direct_supported(C, K, dies);
+    u32 T = 2048, L = 32, group = C;
+    const u32 per_sm = direct ? 3 : 2;
+    const u32 smem_limit = (direct ? 72 : 110) * 1024;
+    if (direct) {
+        L = T;
+        while (layout(probe, T, L, C, K, dies, group, true) > smem_limit) {
+            if (T <= 512) return -1;
+            T /= 2;
+            L = T;
+        }
+    } else {
+        for (;;) {
+            const u32 bytes = layout(probe, T, L, C, K, dies, group, false);
+            if (bytes <= smem_limit) break;
+            if (group > 8) group = (group + 1) / 2;
+            else if (T > 512) T /= 2;
+            else return -1;
+        }
     }
     const u64 tiles = (n + T - 1) / T;
-    const u64 max_ctas = static_cast<u64>(sm_count) * 2;
+    const u64 max_ctas = static_cast<u64>(sm_count) * per_sm;
     u64 ctas = tiles < max_ctas ? tiles : max_ctas;
     if (ctas == 0) ctas = 1;
     const u64 per = (tiles + ctas - 1) / ctas;
@@ -892,7 +1104,9 @@ int plan_batch(u64 n, u32 C, u32 K, u32 dies, int sm_count, BatchPlan* plan)
     plan->group_channels = group;
     plan->ctas = static_cast<u32>(ctas);
     plan->tiles_per_cta = static_cast<u32>(per ? per : 1);
-    plan->smem_bytes = layout(probe, T, L, C, K, dies, group);
+    plan->smem_bytes = layout(probe, T, L, C, K, dies, group, direct);
+    plan->direct = direct ? 1u : 0u;
+    plan->dies = dies;
     return 0;
 }
 
@@ -916,7 +1130,8 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
     }
     if (!force_sequential) {
         PassArgs a{};
-        layout(a, plan.T, plan.L, plan.C, plan.K, tp.dies, plan.group_channels);
+        layout(a, plan.T, plan.L, plan.C, plan.K, tp.dies, plan.group_channels,
+               plan.direct != 0);
         a.dp = dp;
         a.tp = tp;
         a.address = io.address;
@@ -936,8 +1151,17 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
         a.state_in = s.state_in;
         a.counters = s.counters;
         const bool fast = tp.model == kModelFast;
-        auto p1 = fast ? timing_pass_kernel<kModelFast, 1> : timing_pass_kernel<kModelDie, 1>;
-        auto p2 = fast ? timing_pass_kernel<kModelFast, 2> : timing_pass_kernel<kModelDie, 2>;
+        using Kernel = void (*)(const PassArgs);
+        Kernel p1 = fast ? timing_pass_kernel<kModelFast, 1> : timing_pass_kernel<kModelDie, 1>;
+        Kernel p2 = fast ? timing_pass_kernel<kModelFast, 2> : timing_pass_kernel<kModelDie, 2>;
+        if (plan.direct) {
+            switch (plan.dies) {
+            case 1: p1 = direct_pass_kernel<1, 1>; p2 = direct_pass_kernel<2, 1>; break;
+            case 2: p1 = direct_pass_kernel<1, 2>; p2 = direct_pass_kernel<2, 2>; break;
+            case 4: p1 = direct_pass_kernel<1, 4>; p2 = direct_pass_kernel<2, 4>; break;
+            default: p1 = direct_pass_kernel<1, 8>; p2 = direct_pass_kernel<2, 8>; break;
+            }
+        }
         for (auto k : {p1, p2}) {
             err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(plan.smem_bytes));

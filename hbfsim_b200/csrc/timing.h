@@ -9,6 +9,8 @@ namespace hbfb {
 
 struct BatchPlan {
     u32 T, L, C, K, group_channels, ctas, tiles_per_cta, smem_bytes;
+    u32 direct;  // 1: one register chain per channel; 0: pieces of L accesses
+    u32 dies;
 };
 
 struct BatchIO {

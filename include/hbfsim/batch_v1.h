@@ -237,6 +237,29 @@ int hbfsim_thermal_configure_v1(hbfsim_context* context,
 int hbfsim_advance_epoch_v1(hbfsim_context* context, double epoch_s,
                             void* stream);
 
+/* Sharded contexts (shard_count > 1): the same epoch step driven by the
+ * all-gathered activity of every global die (device pointers, index
+ * g*D+d, e.g. an NCCL all-gather of each rank's
+ * hbfsim_copy_die_activity_v1 output).  The grid step is replicated on every
+ * rank (deterministic fp64, same launches); each rank then derives the
+ * factors of its own channels. */
+int hbfsim_advance_epoch_global_v1(hbfsim_context* context, double epoch_s,
+                                   const uint64_t* read_bytes,
+                                   const uint64_t* writes, void* stream);
+
+/* Copies this context's per-die activity since the last epoch (local die
+ * index c*D+d) into caller device buffers, asynchronously on `stream`. */
+int hbfsim_copy_die_activity_v1(hbfsim_context* context, uint64_t* read_bytes,
+                                uint64_t* writes, void* stream);
+
+/* Factors the epoch controller derived (host copies; NULL to skip):
+ * refresh per local channel, throttle permille / admit-after tick / level
+ * (0 Normal, 1 Light, 2 Severe, 3 Shutdown) per stack. */
+int hbfsim_get_thermal_factors_v1(hbfsim_context* context,
+                                  uint32_t* refresh_permille,
+                                  uint32_t* throttle_permille,
+                                  uint64_t* admit_after_ns, uint32_t* levels);
+
 /* Host copies of the grid temperatures (nx*ny*layers, K, cell index
  * z*nx*ny + y*nx + x) and of per-die mean temperatures. */
 int hbfsim_get_temperatures_v1(hbfsim_context* context, double* out,
