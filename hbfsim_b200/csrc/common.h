@@ -88,6 +88,8 @@ struct DecodeParams {
     FastDiv radix[4];        // per letter
     FastDiv shard_div;
     FastDiv stack_div;
+    FastDiv chan_stride;     // product of the radices faster than C
+    FastDiv die_stride;      // product of the radices faster than D
 };
 
 struct TimingParams {

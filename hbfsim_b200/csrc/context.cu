@@ -195,7 +195,7 @@ int configure_geometry(hbfsim_context* c, std::uint32_t stacks,
     if (is_fast(c) && shards != 1) return HBFSIM_UNSUPPORTED;  // one global tail
     if (!is_fast(c) && p.dies_per_channel > 15) return HBFSIM_UNSUPPORTED;
     // stripe units of the whole media space must fit 32 bits
-    if (p.capacity_bytes / stripe > 0xffffffffull) return HBFSIM_UNSUPPORTED;
+    if (p.capacity_bytes / stripe >= 0xffffffffull) return HBFSIM_UNSUPPORTED;
     if (cudaDeviceSynchronize() != cudaSuccess) return HBFSIM_CUDA_ERROR;
     free_geometry(c);
     c->stacks = stacks;
@@ -251,6 +251,19 @@ DecodeParams decode_params(const hbfsim_context* c)
     d.radix[3] = make_fastdiv(p.planes_per_die);
     d.shard_div = make_fastdiv(c->shard_count);
     d.stack_div = make_fastdiv(c->stacks);
+    const std::uint32_t radix[4] = {c->channels_total, 1, p.dies_per_channel,
+                                    p.planes_per_die};
+    std::uint64_t stride = 1, chan_stride = 1, die_stride = 1;
+    for (int k = 0; k < 4; ++k) {
+        if (c->order[k] == 0) chan_stride = stride;
+        if (c->order[k] == 2) die_stride = stride;
+        stride *= radix[c->order[k]];
+    }
+    // strides beyond 32 bits mean the digit is always 0 for 32-bit units
+    d.chan_stride = make_fastdiv(chan_stride > 0xffffffffull ? 0xffffffffu
+                                                             : static_cast<std::uint32_t>(chan_stride));
+    d.die_stride = make_fastdiv(die_stride > 0xffffffffull ? 0xffffffffu
+                                                           : static_cast<std::uint32_t>(die_stride));
     return d;
 }
 
@@ -272,8 +285,10 @@ TimingParams timing_params(const hbfsim_context* c)
     t.chan_t_read = c->d_t_read;
     t.chan_t_prog = c->d_t_prog;
     t.chan_admit = c->d_admit;
-    t.die_read_bytes = c->mode == HBFSIM_MODEL_DIE_V1 ? c->d_die_read_bytes : nullptr;
-    t.die_writes = c->mode == HBFSIM_MODEL_DIE_V1 ? c->d_die_writes : nullptr;
+    // per-die activity feeds the thermal epoch controller only
+    const bool track = c->mode == HBFSIM_MODEL_DIE_V1 && (c->thermal || c->track_activity);
+    t.die_read_bytes = track ? c->d_die_read_bytes : nullptr;
+    t.die_writes = track ? c->d_die_writes : nullptr;
     return t;
 }
 

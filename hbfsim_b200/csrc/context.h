@@ -78,6 +78,7 @@ struct hbfsim_context {
     std::uint64_t stage_capacity = 0;  // accesses per stage
 
     hbfb::ThermalState* thermal = nullptr;
+    bool track_activity = false;  // accumulate per-die activity without thermal
 
     // launch profiling (event pairs per kernel slot)
     bool profiling = false;

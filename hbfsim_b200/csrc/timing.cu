@@ -55,13 +55,14 @@ __device__ __forceinline__ u64 ceil_div_u64(u64 n, u64 d)
 }
 
 // hbf_device.cuh:826-841 -- upper-bound binary search on the sorted bases.
+// `r` may point to global or shared memory.
 __device__ __forceinline__ u32 find_range_index(const DevRange* r, u32 count,
                                                 u64 address)
 {
     u32 first = 0, last = count;
     while (first < last) {
         const u32 middle = first + (last - first) / 2;
-        if (__ldg(&r[middle].base) <= address) first = middle + 1;
+        if (r[middle].base <= address) first = middle + 1;
         else last = middle;
     }
     return first == 0 ? count : first - 1;
@@ -102,7 +103,7 @@ __device__ __forceinline__ Decoded classify_decode(const DecodeParams& p,
     d.range_index = p.range_count;
     if (bytes == 0) { d.status = kUnsupported; return d; }
     const u32 index = find_range_index(p.ranges, p.range_count, a);
-    DevRange r;
+    DevRange r{};
     if (index != p.range_count) r = p.ranges[index];
     if (index == p.range_count || a < r.base || a - r.base >= r.length) {
         const u32 successor = index == p.range_count ? 0u : index + 1u;
@@ -135,10 +136,10 @@ __device__ __forceinline__ Decoded classify_decode(const DecodeParams& p,
     d.media = r.file_offset + page_offset;
     d.range_index = index;
     d.status = kModeled;
-    if (!want_geometry) return d;
-    // stripe decode: mixed radix in allocation order, fastest letter first
     const u64 m = r.file_offset + offset;
     u32 u = static_cast<u32>(m >> p.stripe_shift);  // host: m>>shift < 2^32
+    if (!want_geometry) return d;
+    // stripe decode: mixed radix in allocation order, fastest letter first
     u32 digit[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -159,6 +160,28 @@ __device__ __forceinline__ Decoded classify_decode(const DecodeParams& p,
     d.local = lq;
     if (p.shard_count > 1 && d.channel - lq * p.shard_div.d != p.shard_rank)
         d.status = kForeign;
+    return d;
+}
+
+// Timing decode: status, local channel and die only.  The channel and die
+// digits come straight from their strides in the allocation order
+// (digit = (u / stride) % radix), two invariant divisions each.
+__device__ __forceinline__ Decoded classify_timing(const DecodeParams& p, u64 a, u32 bytes,
+                                                   u32 op)
+{
+    Decoded d = classify_decode(p, a, bytes, op, false);
+    if (d.status != kModeled) return d;
+    const DevRange r = p.ranges[d.range_index];
+    const u64 m = r.file_offset + (a - r.base);
+    const u32 u = static_cast<u32>(m >> p.stripe_shift);
+    const u32 uc = fastdiv_q(u, p.chan_stride);
+    const u32 g = uc - fastdiv_q(uc, p.radix[0]) * p.radix[0].d;
+    const u32 ud = fastdiv_q(u, p.die_stride);
+    d.die = ud - fastdiv_q(ud, p.radix[2]) * p.radix[2].d;
+    d.channel = g;
+    const u32 lq = fastdiv_q(g, p.shard_div);
+    d.local = lq;
+    if (p.shard_count > 1 && g - lq * p.shard_div.d != p.shard_rank) d.status = kForeign;
     return d;
 }
 
@@ -185,7 +208,7 @@ struct PassArgs {
     // shared memory offsets (bytes)
     u32 off_addr, off_arr, off_bytes, off_op, off_ord, off_key, off_rank;
     u32 off_wcnt, off_seg, off_pbase, off_pchan, off_pm, off_pin, off_die;
-    u32 off_chan, off_act, off_red;
+    u32 off_chan, off_act, off_red, off_ranges;
     // global scratch
     i64* agg;        // [ctas][C][K][K+1]  (pass 1 out)
     i64* incoming;   // [ctas][C][K]       (pass 2 in, carried in place)
@@ -207,7 +230,10 @@ struct ChanInfo {  // per local channel, staged in shared memory
     u32 x_exact;   // 1e9 / bw reduces to 1 / 2^x_shift
 };
 
-// ceil(bytes * 1e9 / bw) * time_scale for one access of a channel.
+// ceil(bytes * 1e9 / bw) * time_scale for one access of a channel.  An
+// access never exceeds its page (access_supported), and the host admits the
+// parallel path only when a page's transfer times the scale stays below
+// 2^24, so the plain product is exact here.
 __device__ __forceinline__ u64 transfer_ticks(u32 bytes, const ChanInfo& ci, u32 scale)
 {
     u64 x;
@@ -215,7 +241,7 @@ __device__ __forceinline__ u64 transfer_ticks(u32 bytes, const ChanInfo& ci, u32
         x = (static_cast<u64>(bytes) + (u64{1} << ci.x_shift) - 1) >> ci.x_shift;
     else
         x = ceil_div_u64(static_cast<u64>(bytes) * 1000000000ull, ci.bw);
-    return sat_mul_u64(x, scale);
+    return x * scale;
 }
 
 __device__ ChanInfo stage_channel(const TimingParams& tp, u32 c, bool die)
@@ -338,7 +364,10 @@ struct TileSmem {
     ChanInfo* chan;
     unsigned long long* act;  // [C*D][2]
     unsigned long long* red;
+    DevRange* ranges;         // staged range table (kSmemRanges entries)
 };
+
+constexpr u32 kSmemRanges = 32;
 
 __device__ __forceinline__ TileSmem tile_views(unsigned char* smem, const PassArgs& A)
 {
@@ -355,6 +384,7 @@ __device__ __forceinline__ TileSmem tile_views(unsigned char* smem, const PassAr
     s.chan = reinterpret_cast<ChanInfo*>(smem + A.off_chan);
     s.act = reinterpret_cast<unsigned long long*>(smem + A.off_act);
     s.red = reinterpret_cast<unsigned long long*>(smem + A.off_red);
+    s.ranges = reinterpret_cast<DevRange*>(smem + A.off_ranges);
     return s;
 }
 
@@ -400,6 +430,8 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
     for (u32 k = tid; k < kWarps * (C + 1); k += kThreads) s.wcnt[k] = 0;
     __syncthreads();
 
+    DecodeParams dp = A.dp;
+    if (dp.range_count <= kSmemRanges) dp.ranges = s.ranges;
     const u32 chunk = T / kWarps;
     bool unsorted = false;
     for (u32 j = 0; j < chunk; j += 32) {
@@ -416,7 +448,8 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
                 if (arr < prev) unsorted = true;
                 if (arr >= kArrivalLimit) atomicOr(A.error, kErrNeedSeq);
             }
-            const Decoded d = classify_decode(A.dp, a, b, o, MODEL == kModelDie);
+            const Decoded d = MODEL == kModelDie ? classify_timing(dp, a, b, o)
+                                                 : classify_decode(dp, a, b, o, false);
             u32 info = (o & 1u) << 28;
             if (d.status == kModeled) {
                 key = MODEL == kModelDie ? d.local : 0u;
@@ -551,6 +584,8 @@ __device__ __forceinline__ void prologue(const PassArgs& A, const TileSmem& s, b
 {
     const u32 tid = threadIdx.x, C = A.C, D = A.tp.dies;
     for (u32 c = tid; c < C; c += kThreads) s.chan[c] = stage_channel(A.tp, c, die);
+    if (A.dp.range_count <= kSmemRanges)
+        for (u32 k = tid; k < A.dp.range_count; k += kThreads) s.ranges[k] = A.dp.ranges[k];
     if (activity)
         for (u32 k = tid; k < 2 * C * D; k += kThreads) s.act[k] = 0;
     if (blockIdx.x == 0 && A.state_in) {
@@ -724,9 +759,45 @@ timing_pass_kernel(const PassArgs args)
 
 // ---------------------------------------------------------------------------
 // Direct kernel (die model, D dies known at compile time, enough channels
-// for parallelism): no pieces.  Pass 1: thread item (c, r) carries column r
-// of channel c's range aggregate in registers through every tile of the
-// CTA's range.  Pass 2: thread c carries channel c's exact state.
+// for parallelism): no pieces.
+//
+// Pass 2: thread c carries channel c's exact state through every tile of the
+// CTA's range, one step per access.
+//
+// Pass 1: item (r, c) carries column r of channel c's range aggregate.  Items
+// are laid out r-major so that a warp holds one kind of column.  Column 0
+// (channel unit) and column K (real arrivals) are replayed over the whole
+// range.  A die column r = 1..D is replayed only until it couples to column
+// 0: equal to it plus one scalar delta in every finite component and -inf
+// exactly where column 0 is.  From then on it stays so -- the homogeneous
+// max-plus maps of later accesses commute with adding a scalar -- and only
+// delta is kept; the warps whose columns have all coupled skip their loops.
+__device__ __forceinline__ bool is_neg_inf(i64 v) { return v < kNeg / 2; }
+
+template <int D>
+__device__ __forceinline__ bool try_couple(const i64* col0, const DieRegs<D>& v, i64& delta)
+{
+    bool have = false;
+    i64 dl = 0;
+#pragma unroll
+    for (int i = 0; i <= D; ++i) {
+        const i64 a = col0[i];
+        const i64 b = i == 0 ? v.chan : v.die[i - 1];
+        const bool ia = is_neg_inf(a), ib = is_neg_inf(b);
+        if (ia != ib) return false;
+        if (ia) continue;
+        if (!have) {
+            dl = b - a;
+            have = true;
+        } else if (b - a != dl) {
+            return false;
+        }
+    }
+    if (!have) return false;
+    delta = dl;
+    return true;
+}
+
 template <int PASS, int D>
 __global__ void __launch_bounds__(kThreads, 3)
 direct_pass_kernel(const PassArgs args)
@@ -737,28 +808,32 @@ direct_pass_kernel(const PassArgs args)
     constexpr u32 K = D + 1, KK = D + 2;
     const u32 T = A.T, C = A.C;
     const TileSmem s = tile_views(smem, A);
+    i64* s_col0 = reinterpret_cast<i64*>(smem + A.off_pm);  // [C][K], pass 1
     if (PASS == 2 && *A.error != 0) return;
     const bool activity = PASS == 2 && A.tp.die_read_bytes != nullptr;
     prologue(A, s, true, activity);
 
-    // register state: pass 1 holds up to two (c, r) columns, pass 2 one channel
     constexpr int kItems = PASS == 1 ? 2 : 1;
     DieRegs<D> reg[kItems];
     u32 item_c[kItems], item_r[kItems];
-    bool item_on[kItems];
+    bool item_on[kItems], coupled[kItems];
+    i64 delta[kItems];
     i64* agg = A.agg + static_cast<u64>(blockIdx.x) * C * K * KK;
     i64* carry = A.incoming + static_cast<u64>(blockIdx.x) * C * K;
 #pragma unroll
     for (int it = 0; it < kItems; ++it) {
         const u32 q = tid + it * kThreads;
         item_on[it] = PASS == 1 ? q < C * KK : q < C;
-        item_c[it] = PASS == 1 ? q / KK : q;
-        item_r[it] = PASS == 1 ? q % KK : 0;
+        item_r[it] = PASS == 1 ? q / C : 0;
+        item_c[it] = PASS == 1 ? q % C : q;
+        coupled[it] = false;
+        delta[it] = 0;
         if (!item_on[it]) continue;
         if (PASS == 1) {  // identity column e_r (r == K: no constant yet)
             reg[it].chan = item_r[it] == 0 ? 0 : kNeg;
 #pragma unroll
-            for (int j = 0; j < D; ++j) reg[it].die[j] = item_r[it] == static_cast<u32>(j + 1) ? 0 : kNeg;
+            for (int j = 0; j < D; ++j)
+                reg[it].die[j] = item_r[it] == static_cast<u32>(j + 1) ? 0 : kNeg;
         } else {
             const i64* cv = carry + static_cast<u64>(item_c[it]) * K;
             reg[it].chan = cv[0];
@@ -777,7 +852,7 @@ direct_pass_kernel(const PassArgs args)
         load_decode_partition<kModelDie, PASS>(A, s, start, nt, activity, st);
 #pragma unroll
         for (int it = 0; it < kItems; ++it) {
-            if (!item_on[it]) continue;
+            if (!item_on[it] || coupled[it]) continue;
             const u32 c = item_c[it];
             const u32 first = s.seg[c], last = s.seg[c + 1];
             const ChanInfo ci = s.chan[c];
@@ -805,20 +880,49 @@ direct_pass_kernel(const PassArgs args)
             }
         }
         __syncthreads();
-        if (PASS == 2) store_tile(A, s, start, nt);
+        if (PASS == 1) {
+            // snapshot column 0, then let die columns try to couple to it
+#pragma unroll
+            for (int it = 0; it < kItems; ++it) {
+                if (!item_on[it] || item_r[it] != 0) continue;
+                i64* v0 = s_col0 + static_cast<u64>(item_c[it]) * K;
+                v0[0] = reg[it].chan;
+#pragma unroll
+                for (int j = 0; j < D; ++j) v0[1 + j] = reg[it].die[j];
+            }
+            __syncthreads();
+#pragma unroll
+            for (int it = 0; it < kItems; ++it) {
+                if (!item_on[it] || coupled[it] || item_r[it] == 0 || item_r[it] == K) continue;
+                coupled[it] = try_couple<D>(s_col0 + static_cast<u64>(item_c[it]) * K,
+                                            reg[it], delta[it]);
+            }
+        } else {
+            store_tile(A, s, start, nt);
+        }
         __syncthreads();
     }
+    if (PASS == 1) {
+        // s_col0 holds column 0 after the last tile of the range
 #pragma unroll
-    for (int it = 0; it < kItems; ++it) {
-        if (!item_on[it]) continue;
-        if (PASS == 1) {
-            i64* col = agg + static_cast<u64>(item_c[it]) * K * KK + item_r[it];
-            col[0] = reg[it].chan;
+        for (int it = 0; it < kItems; ++it) {
+            if (!item_on[it]) continue;
+            const u32 c = item_c[it], r = item_r[it];
+            i64* col = agg + static_cast<u64>(c) * K * KK + r;
+            if (coupled[it]) {
+                const i64* v0 = s_col0 + static_cast<u64>(c) * K;
 #pragma unroll
-            for (int j = 0; j < D; ++j) col[(j + 1) * KK] = reg[it].die[j];
+                for (int i = 0; i <= D; ++i)
+                    col[i * KK] = is_neg_inf(v0[i]) ? kNeg : v0[i] + delta[it];
+            } else {
+                col[0] = reg[it].chan;
+#pragma unroll
+                for (int j = 0; j < D; ++j) col[(j + 1) * KK] = reg[it].die[j];
+            }
         }
+    } else {
+        flush_stats(A, s, st, activity);
     }
-    if (PASS == 2) flush_stats(A, s, st, activity);
 }
 
 // Sequential scan of the CTA range aggregates: incoming_b = R_{b-1} ...
@@ -1045,7 +1149,10 @@ static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
     a.off_chan = take(static_cast<u32>(sizeof(ChanInfo)) * C);
     a.off_act = take(16 * C * (dies ? dies : 1));
     a.off_red = take(8 * 8 * kWarps);
-    if (!direct) {
+    a.off_ranges = take(static_cast<u32>(sizeof(DevRange)) * kSmemRanges);
+    if (direct) {
+        a.off_pm = take(8 * C * K);  // column-0 snapshot of pass 1
+    } else {
         a.off_pbase = take(4 * (C + 2));
         a.off_pchan = take(2 * (T / L + C + 1));
         a.off_pm = take(8 * pm_capacity * K * (K + 1));
