@@ -123,6 +123,7 @@ SIGNATURES = {
     "hbfsim_set_geometry_v1": (i32, [vp, ctypes.POINTER(GeometryV1)]),
     "hbfsim_submit_access_batch_v1": (i32, [vp, ctypes.POINTER(AccessBatchV1), vp]),
     "hbfsim_submit_access_batch_host_v1": (i32, [vp, ctypes.POINTER(AccessBatchV1)]),
+    "hbfsim_submit_access_batch_static_v1": (i32, [vp, ctypes.POINTER(AccessBatchV1), vp]),
     "hbfsim_get_simulated_time_v1": (i32, [vp, ctypes.POINTER(u64)]),
     "hbfsim_reset_state_v1": (i32, [vp, vp]),
     "hbfsim_set_profiling_v1": (i32, [vp, i32]),

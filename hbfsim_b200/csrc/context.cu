@@ -831,3 +831,118 @@ int hbfsim_get_die_activity_v1(hbfsim_context* c, uint64_t* read_bytes, uint64_t
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Batch entry point that allocates nothing.
+//
+// Some callers cannot call cudaMalloc while they run: an inference server that
+// has reserved almost all device memory for its own pool up front (vLLM sizes
+// its KV cache that way) would see the allocation fail, and in any process a
+// first-time cudaMalloc can synchronize the device and stall every other
+// stream.  hbfsim_submit_access_batch_static_v1 therefore takes its scratch --
+// the per-CTA range aggregates, the carried states and the batch error word --
+// from the fixed array below instead of from memory the context allocates.
+//
+// The array is 8 MiB.  Every GPU that loads this library holds it until the
+// process exits.  All calls, from every context, share it, and it keeps the
+// previous call's contents: the error word is cleared by each call and every
+// other byte a call reads is written by that call first.  Calls whose work
+// overlaps on the GPU (different streams, or different contexts on one
+// device, without ordering between them) race on the array; serialize them.
+// In host code the array's name is only a stand-in for the device variable:
+// its device address is looked up with cudaGetSymbolAddress once per device,
+// on that device's first call, so that first call should come before any
+// stream capture begins.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr std::size_t kStaticScratchBytes = std::size_t{8} << 20;
+constexpr std::size_t kStaticErrorBytes = 256;  // error word, padded
+constexpr int kMaxDevices = 64;
+
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+namespace {
+
+std::mutex g_static_mu;
+void* g_static_address[kMaxDevices] = {};
+
+// Device address of g_static_scratch on `device` (which must be current).
+int static_scratch_address(int device, void** out)
+{
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (device < 0 || device >= kMaxDevices) return HBFSIM_UNSUPPORTED;
+    if (!g_static_address[device]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || !p)
+            return HBFSIM_CUDA_ERROR;
+        g_static_address[device] = p;
+    }
+    *out = g_static_address[device];
+    return HBFSIM_OK;
+}
+
+}  // namespace
+
+extern "C" int hbfsim_submit_access_batch_static_v1(hbfsim_context* c,
+                                                    const hbfsim_access_batch_v1* b,
+                                                    void* stream)
+{
+    if (!c || !b || b->struct_size != sizeof(hbfsim_access_batch_v1) ||
+        b->version != HBFSIM_ACCESS_BATCH_V1_VERSION)
+        return HBFSIM_INVALID_ARGUMENT;
+    if (b->count && (!b->address || !b->bytes || !b->operation || !b->arrival_ns ||
+                     !b->done_ns || !b->latency_ns || !b->status))
+        return HBFSIM_INVALID_ARGUMENT;
+    Guard g(c);
+    const int ok = model_supported(c);
+    if (ok != HBFSIM_OK) return ok;
+    if (b->count == 0) return HBFSIM_OK;
+    void* base = nullptr;
+    const int rc = static_scratch_address(c->device, &base);
+    if (rc != HBFSIM_OK) return rc;
+    BatchIO io{b->address, b->bytes, b->operation, b->arrival_ns, b->done_ns,
+               b->latency_ns, b->status, b->count, false};
+    io.aligned = aligned16(io.address) && aligned16(io.bytes) && aligned16(io.op) &&
+                 aligned16(io.arrival) && aligned16(io.done) && aligned16(io.latency) &&
+                 aligned16(io.status);
+    // the same bound proof as the allocating entry point
+    const std::uint64_t growth = sat_mul(sat_add(c->x_max, c->t_max), io.n);
+    const bool sequential = growth >= static_cast<std::uint64_t>(kArrivalLimit) ||
+                            c->admit_max >= static_cast<std::uint64_t>(kArrivalLimit) ||
+                            c->x_max > 0xffffffull || c->t_max >= (1ull << 40);
+    BatchPlan plan{};
+    if (plan_batch(io.n, c->C, c->K, c->D, c->sm_count, &plan) != 0) return HBFSIM_UNSUPPORTED;
+    // Fit the CTA grid to the array: each CTA needs its range aggregate and
+    // its incoming state.  Fewer CTAs cover longer ranges; results do not
+    // depend on how the batch is split.  A shape whose single CTA does not
+    // fit is refused.
+    const std::uint64_t words_per_cta =
+        static_cast<std::uint64_t>(c->C) * c->K * (c->K + 1) + static_cast<std::uint64_t>(c->C) * c->K;
+    const std::uint64_t max_ctas =
+        (kStaticScratchBytes - kStaticErrorBytes) / (8 * words_per_cta);
+    if (max_ctas == 0) return HBFSIM_UNSUPPORTED;
+    if (plan.ctas > max_ctas) {
+        const std::uint64_t tiles = (io.n + plan.T - 1) / plan.T;
+        const std::uint64_t per = (tiles + max_ctas - 1) / max_ctas;
+        plan.tiles_per_cta = static_cast<std::uint32_t>(per);
+        plan.ctas = static_cast<std::uint32_t>((tiles + per - 1) / per);
+    }
+    auto* bytes = static_cast<unsigned char*>(base);
+    BatchScratch s{};
+    s.error = reinterpret_cast<std::uint32_t*>(bytes);
+    s.agg = reinterpret_cast<i64*>(bytes + kStaticErrorBytes);
+    s.incoming = s.agg + static_cast<std::uint64_t>(plan.ctas) * c->C * c->K * (c->K + 1);
+    s.last_arrival = c->d_last_arrival;
+    s.counters = c->d_counters;
+    s.state_in = c->d_state[c->cur];
+    s.state_out = c->d_state[1 - c->cur];
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    if (launch_batch(decode_params(c), timing_params(c), io, plan, s, sequential, st,
+                     LaunchHooks{}) != cudaSuccess)
+        return HBFSIM_CUDA_ERROR;
+    c->cur = 1 - c->cur;
+    return HBFSIM_OK;
+}

@@ -92,6 +92,24 @@ int hbfsim_submit_access_batch_v1(hbfsim_context* context,
                                   const hbfsim_access_batch_v1* batch,
                                   void* stream);
 
+/* The same batch call without any device allocation.  No counterpart in
+ * the reference.  For callers that must not call cudaMalloc while running
+ * -- a server that pre-reserved nearly all device memory for its own pool,
+ * or code that cannot afford the device-wide synchronization a first
+ * cudaMalloc may cause.  Its scratch (per-CTA range aggregates, carried
+ * states, the batch error word) lives in one 8 MiB device array that the
+ * library defines statically; every GPU that loads the library holds those
+ * 8 MiB until the process exits.  All calls share the array: calls whose
+ * work overlaps on the GPU race and must be serialized by the caller.  The
+ * first call on a device looks up the array's device address; make that
+ * first call before any stream capture begins.  Returns HBFSIM_UNSUPPORTED
+ * when one CTA's scratch (local channels * (D+1) * (D+3) * 8 bytes) exceeds
+ * the array; otherwise it times the batch exactly as
+ * hbfsim_submit_access_batch_v1 does. */
+int hbfsim_submit_access_batch_static_v1(hbfsim_context* context,
+                                         const hbfsim_access_batch_v1* batch,
+                                         void* stream);
+
 /* The same call with HOST pointers: copies in, times, copies out, pipelined
  * over chunks on the context's streams.  Synchronous. */
 int hbfsim_submit_access_batch_host_v1(hbfsim_context* context,

@@ -1,0 +1,69 @@
+"""The batch entry point that allocates nothing (hbfsim_submit_access_batch_static_v1).
+
+It exists for callers that cannot call cudaMalloc while they run -- a server
+that reserved nearly all device memory for its own pool up front, or code that
+cannot afford the device-wide synchronization a first cudaMalloc may cause.
+Its scratch lives in one fixed device array that the library defines, so this
+test checks, through the C ABI, that two calls in a row give exactly what the
+allocating entry point gives (integer ticks: bit-exact), including a shape
+whose CTA grid must shrink to fit the array.
+
+Kept in a file of its own so that pytest collects it last.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+from helpers import Setup, make_context, to_device
+from hbfsim_b200 import _lib
+from hbfsim_b200 import workloads as wl
+
+pytestmark = pytest.mark.gpu
+
+
+def _submit(lib, ctx, fn_name, dev):
+    import torch
+    address, nbytes, op, arrival = dev
+    n = address.numel()
+    out = [torch.empty(n, dtype=torch.int64, device="cuda"),
+           torch.empty(n, dtype=torch.int64, device="cuda"),
+           torch.empty(n, dtype=torch.uint8, device="cuda")]
+    batch = _lib.AccessBatchV1(ctypes.sizeof(_lib.AccessBatchV1), 1, n,
+                               address.data_ptr(), nbytes.data_ptr(), op.data_ptr(),
+                               arrival.data_ptr(), out[0].data_ptr(), out[1].data_ptr(),
+                               out[2].data_ptr())
+    stream = torch.cuda.current_stream().cuda_stream or 1  # 1 = cudaStreamLegacy
+    rc = getattr(lib, fn_name)(ctx.handle, ctypes.byref(batch), ctypes.c_void_p(stream))
+    assert rc == 0, f"{fn_name} returned {rc}"
+    torch.cuda.synchronize()
+    return [t.cpu().numpy() for t in out]
+
+
+@pytest.mark.parametrize("model,dies,stacks,n", [(3, 4, 1, 70001), (1, 4, 1, 50000),
+                                                 (3, 8, 4, 600000)])
+def test_static_entry_matches_allocating_entry(tmp_path, model, dies, stacks, n):
+    lib = _lib.load()
+    p = wl.c0_profile()
+    p["dies_per_channel"] = dies
+    p["capacity_bytes"] = p["page_bytes"] * 16 * dies * 4 * 256 * 64
+    setup = Setup(profile=p, model=model, stacks=stacks, stripe=4096)
+    setup.ranges = [(wl.RANGE_BASE, p["capacity_bytes"] - (1 << 20), 1, 3)]
+    arrays = wl.c0_trace(n, seed=77 + n, range_length=p["capacity_bytes"] - (1 << 20))
+    split = n * 3 // 5
+    calls = [tuple(a[:split] for a in arrays), tuple(a[split:] for a in arrays)]
+
+    reference = make_context(setup, str(tmp_path / "alloc"))
+    static = make_context(setup, str(tmp_path / "static"))
+    for k, part in enumerate(calls):
+        dev = to_device(part)
+        want = _submit(lib, reference, "hbfsim_submit_access_batch_v1", dev)
+        got = _submit(lib, static, "hbfsim_submit_access_batch_static_v1", dev)
+        for w, g, name in zip(want, got, ("done", "latency", "status")):
+            assert np.array_equal(w, g), f"call {k}: {name} differs"
+        assert np.array_equal(reference.get_state(), static.get_state()), f"call {k}: state"
+    reference.flush()
+    static.flush()
+    assert reference.batch_stats()["modeled"] == static.batch_stats()["modeled"]
+    reference.close()
+    static.close()
