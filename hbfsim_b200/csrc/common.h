@@ -43,9 +43,12 @@ struct DevRange {
     u32 range_id;
     u32 mode;
     u32 permissions;
-    u32 reserved;
+    u32 reserved;      // log2(page_bytes)
+    u64 end;           // base + length (meaningful when `ok`)
+    u32 ok;            // mode 1 or 2, 0 < page_bytes <= 2^32, no end overflow
+    u32 timing;        // ok and mode 1 (timing range)
 };
-static_assert(sizeof(DevRange) == 48, "range record layout");
+static_assert(sizeof(DevRange) == 64, "range record layout");
 
 // Divide a 32-bit value by an invariant 32-bit divisor with one 64-bit
 // multiply-high (Lemire, Kaser & Kurz, "Faster remainder by direct
@@ -90,6 +93,8 @@ struct DecodeParams {
     FastDiv stack_div;
     FastDiv chan_stride;     // product of the radices faster than C
     FastDiv die_stride;      // product of the radices faster than D
+    u32 pow2;                // every stride, radix and the shard count are 2^k
+    u32 chan_shift, chan_mask, die_shift, die_mask, shard_shift, shard_mask;
 };
 
 struct TimingParams {

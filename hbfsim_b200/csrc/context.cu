@@ -264,6 +264,18 @@ DecodeParams decode_params(const hbfsim_context* c)
                                                              : static_cast<std::uint32_t>(chan_stride));
     d.die_stride = make_fastdiv(die_stride > 0xffffffffull ? 0xffffffffu
                                                            : static_cast<std::uint32_t>(die_stride));
+    auto is_pow2 = [](std::uint64_t v) { return v != 0 && (v & (v - 1)) == 0; };
+    d.pow2 = is_pow2(chan_stride) && chan_stride <= 0x80000000ull && is_pow2(die_stride) &&
+             die_stride <= 0x80000000ull && is_pow2(c->channels_total) &&
+             is_pow2(p.dies_per_channel) && is_pow2(c->shard_count);
+    if (d.pow2) {
+        d.chan_shift = log2u(chan_stride);
+        d.chan_mask = c->channels_total - 1;
+        d.die_shift = log2u(die_stride);
+        d.die_mask = p.dies_per_channel - 1;
+        d.shard_shift = log2u(c->shard_count);
+        d.shard_mask = c->shard_count - 1;
+    }
     return d;
 }
 
@@ -457,6 +469,9 @@ int hbfsim_register_device(hbfsim_context* c, void* device_ptr, size_t length,
     r.mode = o->mode;
     r.permissions = o->permissions;
     r.reserved = log2u(page);
+    r.end = base + length;
+    r.ok = (r.mode == 1 || r.mode == 2) && page != 0 && page <= 0xffffffffull ? 1u : 0u;
+    r.timing = r.ok && r.mode == HBFSIM_RANGE_MODE_TIMING ? 1u : 0u;
     c->ranges.insert(at, r);
     const int rc = upload_ranges(c);
     if (rc != HBFSIM_OK) {

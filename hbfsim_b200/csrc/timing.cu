@@ -163,25 +163,56 @@ __device__ __forceinline__ Decoded classify_decode(const DecodeParams& p,
     return d;
 }
 
-// Timing decode: status, local channel and die only.  The channel and die
-// digits come straight from their strides in the allocation order
-// (digit = (u / stride) % radix), two invariant divisions each.
-__device__ __forceinline__ Decoded classify_timing(const DecodeParams& p, u64 a, u32 bytes,
-                                                   u32 op)
+// Timing decode: status, local channel and die only -- the classification
+// of classify_decode on the precomputed range record, then the channel and
+// die digits straight from their strides in the allocation order
+// (digit = (u / stride) % radix): shifts and masks when every factor is a
+// power of two, invariant divisions otherwise.
+struct TimingDecoded {
+    u32 status;
+    u32 local;
+    u32 die;
+};
+
+__device__ __forceinline__ TimingDecoded classify_timing(const DecodeParams& p, u64 a,
+                                                         u32 bytes, u32 op)
 {
-    Decoded d = classify_decode(p, a, bytes, op, false);
-    if (d.status != kModeled) return d;
-    const DevRange r = p.ranges[d.range_index];
-    const u64 m = r.file_offset + (a - r.base);
-    const u32 u = static_cast<u32>(m >> p.stripe_shift);
-    const u32 uc = fastdiv_q(u, p.chan_stride);
-    const u32 g = uc - fastdiv_q(uc, p.radix[0]) * p.radix[0].d;
-    const u32 ud = fastdiv_q(u, p.die_stride);
-    d.die = ud - fastdiv_q(ud, p.radix[2]) * p.radix[2].d;
-    d.channel = g;
-    const u32 lq = fastdiv_q(g, p.shard_div);
-    d.local = lq;
-    if (p.shard_count > 1 && g - lq * p.shard_div.d != p.shard_rank) d.status = kForeign;
+    TimingDecoded d{kUnsupported, 0, 0};
+    if (bytes == 0) return d;                                  // hbf_device.cu:997-1003
+    const u32 index = find_range_index(p.ranges, p.range_count, a);
+    if (index == p.range_count || a - p.ranges[index].base >= p.ranges[index].length) {
+        const u32 successor = index == p.range_count ? 0u : index + 1u;  // 1083-1127
+        d.status = successor < p.range_count && range_overlaps(p.ranges[successor], a, bytes)
+                       ? kUnsupported : kBypass;
+        return d;
+    }
+    const DevRange& r = p.ranges[index];
+    // access_supported (hbf_device.cuh:843-862) with the static range checks
+    // folded into r.ok; a >= base and a - base < length hold here
+    if (op > 1 || !r.ok || bytes > ~u64{0} - a || a + bytes > r.end ||
+        (r.permissions & (1u << op)) == 0)
+        return d;
+    const u64 offset = a - r.base;
+    if ((offset >> r.reserved) != ((offset + bytes - 1) >> r.reserved)) return d;
+    if (((offset >> r.reserved) << r.reserved) > ~u64{0} - r.file_offset || !r.timing)
+        return d;                                               // media_descriptor
+    const u32 u = static_cast<u32>((r.file_offset + offset) >> p.stripe_shift);
+    u32 g;
+    if (p.pow2) {
+        g = (u >> p.chan_shift) & p.chan_mask;
+        d.die = (u >> p.die_shift) & p.die_mask;
+        d.local = g >> p.shard_shift;
+        d.status = (g & p.shard_mask) == p.shard_rank ? kModeled : kForeign;
+    } else {
+        const u32 uc = fastdiv_q(u, p.chan_stride);
+        g = uc - fastdiv_q(uc, p.radix[0]) * p.radix[0].d;
+        const u32 ud = fastdiv_q(u, p.die_stride);
+        d.die = ud - fastdiv_q(ud, p.radix[2]) * p.radix[2].d;
+        const u32 lq = fastdiv_q(g, p.shard_div);
+        d.local = lq;
+        d.status = p.shard_count > 1 && g - lq * p.shard_div.d != p.shard_rank ? kForeign
+                                                                                 : kModeled;
+    }
     return d;
 }
 
@@ -448,8 +479,13 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
                 if (arr < prev) unsorted = true;
                 if (arr >= kArrivalLimit) atomicOr(A.error, kErrNeedSeq);
             }
-            const Decoded d = MODEL == kModelDie ? classify_timing(dp, a, b, o)
-                                                 : classify_decode(dp, a, b, o, false);
+            TimingDecoded d;
+            if (MODEL == kModelDie) {
+                d = classify_timing(dp, a, b, o);
+            } else {
+                const Decoded f = classify_decode(dp, a, b, o, false);
+                d = TimingDecoded{f.status, 0u, 0u};
+            }
             u32 info = (o & 1u) << 28;
             if (d.status == kModeled) {
                 key = MODEL == kModelDie ? d.local : 0u;
@@ -1144,8 +1180,8 @@ static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
     a.off_ord = take(2 * T);
     a.off_key = take(2 * T);
     a.off_rank = take(2 * T);
-    a.off_wcnt = take(4 * kWarps * (C + 1));
     a.off_seg = take(4 * (C + 2));
+    a.off_wcnt = take(4 * kWarps * (C + 1));
     a.off_chan = take(static_cast<u32>(sizeof(ChanInfo)) * C);
     a.off_act = take(16 * C * (dies ? dies : 1));
     a.off_red = take(8 * 8 * kWarps);
@@ -1168,6 +1204,7 @@ static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
 // (called by context.cu; not part of the C ABI)
 namespace hbfb {
 
+// Direct mode: pass 1 holds two column items per thread, pass 2 one channel.
 static bool direct_supported(u32 C, u32 K, u32 dies)
 {
     const bool d_ok = dies == 1 || dies == 2 || dies == 4 || dies == 8;
