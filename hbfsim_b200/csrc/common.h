@@ -116,6 +116,9 @@ struct TimingParams {
     // per-die activity accumulation (NULL = off); index c*D+d
     unsigned long long* die_read_bytes;
     unsigned long long* die_writes;
+    // activity counted by pass 1, [C*D][2] (read bytes, writes); the range
+    // scan adds it to the die counters once the batch is accepted
+    unsigned long long* act_stage;
 };
 
 // Device-side counters (one block of u64 per context).

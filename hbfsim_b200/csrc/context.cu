@@ -175,6 +175,7 @@ void free_geometry(hbfsim_context* c)
     dfree(c->d_admit);
     dfree(c->d_die_read_bytes);
     dfree(c->d_die_writes);
+    dfree(c->d_act_stage);
     dfree(c->d_agg);
     dfree(c->d_incoming);
     c->scratch_ctas = 0;
@@ -214,7 +215,8 @@ int configure_geometry(hbfsim_context* c, std::uint32_t stacks,
         dalloc(&c->d_chan_bw, c->C) || dalloc(&c->d_t_read, c->C) ||
         dalloc(&c->d_t_prog, c->C) || dalloc(&c->d_admit, c->C) ||
         dalloc(&c->d_die_read_bytes, std::uint64_t{c->C} * std::max(1u, c->D)) ||
-        dalloc(&c->d_die_writes, std::uint64_t{c->C} * std::max(1u, c->D)))
+        dalloc(&c->d_die_writes, std::uint64_t{c->C} * std::max(1u, c->D)) ||
+        dalloc(&c->d_act_stage, 2ull * c->C * std::max(1u, c->D)))
         return HBFSIM_CUDA_ERROR;
     cudaMemset(c->d_state[0], 0, sizeof(std::uint64_t) * words);
     cudaMemset(c->d_state[1], 0, sizeof(std::uint64_t) * words);
@@ -301,6 +303,7 @@ TimingParams timing_params(const hbfsim_context* c)
     const bool track = c->mode == HBFSIM_MODEL_DIE_V1 && (c->thermal || c->track_activity);
     t.die_read_bytes = track ? c->d_die_read_bytes : nullptr;
     t.die_writes = track ? c->d_die_writes : nullptr;
+    t.act_stage = track ? c->d_act_stage : nullptr;
     return t;
 }
 

@@ -70,6 +70,7 @@ struct hbfsim_context {
     // per-die activity since the last epoch (die model), index c*D+d
     unsigned long long* d_die_read_bytes = nullptr;
     unsigned long long* d_die_writes = nullptr;
+    unsigned long long* d_act_stage = nullptr;  // [C*D][2], one batch's pass-1 count
 
     // host-buffer pipeline
     cudaStream_t copy_in = nullptr;

@@ -9,12 +9,18 @@
 //           matrix of every piece (<= L consecutive accesses of one channel).
 //           The pieces are folded into the CTA's range aggregate R_b
 //           (per channel a K x (K+1) max-plus affine map, K = state words).
-//   scan    (range_scan_kernel)  one CTA applies R_0, R_1, ... to the
-//           context's die/channel state and writes each CTA's incoming state.
+//   scan    (range_scan_kernel)  one CTA per channel applies R_0, R_1, ...
+//           to the channel's carried state and writes each CTA's incoming
+//           state.
 //   pass 2  (timing_pass_kernel<..., 2>)  every CTA re-stages its tiles,
 //           propagates its incoming state through the pieces (one max-plus
 //           matrix-vector product per piece) and replays each piece from its
 //           exact incoming state, writing completion tick, latency and status.
+//
+// The direct kernel (direct_pass_kernel, die model with few dies) keeps the
+// state in registers instead of pieces, and its pass 1 leaves one compact
+// record per access in the latency buffer, so that its pass 2 re-reads only
+// arrivals and records: no second decode or partition.
 //
 // Why max-plus: both timing models are max-plus affine in the per-channel
 // state (see the step functions below), so a chunk of accesses is summarized
@@ -577,6 +583,70 @@ __device__ __forceinline__ void store_tile(const PassArgs& A, const TileSmem& s,
     }
 }
 
+// Compact per-access records that pass 1 of the direct kernel leaves for
+// pass 2 in the caller's latency buffer (overwritten by pass 2 with the
+// latency):  bits 0-31  packed step info of access j (transfer | die | op),
+//            bits 32-47 s.ord[j] (the access at channel-sorted position j),
+//            bits 48-55 status of access j,
+//            bits 56-63 local channel of access j (C < 256 in direct mode).
+// Pass 2 rebuilds the tile's partition from them without decoding again.
+__device__ __forceinline__ void write_records(const PassArgs& A, const TileSmem& s, u64 start,
+                                              u32 nt)
+{
+    const u32 tid = threadIdx.x;
+    u64* rec = A.latency + start;
+    for (u32 j = tid; j < nt; j += kThreads)
+        rec[j] = static_cast<u64>(s.bytes[j]) | (static_cast<u64>(s.ord[j]) << 32) |
+                 (static_cast<u64>(s.op[j]) << 48) | (static_cast<u64>(s.key[j] & 0xffu) << 56);
+}
+
+// Pass 2: stage the arrivals and the records of one tile, restore info,
+// sorted order and status, count the channel segments, and fill in the
+// outputs of the accesses that are not timed (done = arrival, latency 0).
+__device__ __forceinline__ void load_records(const PassArgs& A, const TileSmem& s, u64 start,
+                                             u32 nt, Stats7& st)
+{
+    const u32 tid = threadIdx.x, T = A.T, C = A.C;
+    const u64* rec = A.latency + start;
+    if (nt == T && A.vec) {
+        const uint4* g_arr = reinterpret_cast<const uint4*>(A.arrival + start);
+        const uint4* g_rec = reinterpret_cast<const uint4*>(rec);
+        uint4* d_arr = reinterpret_cast<uint4*>(s.arr);
+        uint4* d_rec = reinterpret_cast<uint4*>(s.addr);
+        for (u32 k = tid; k < T / 2; k += kThreads) {
+            d_arr[k] = __ldcs(g_arr + k);
+            d_rec[k] = __ldcs(g_rec + k);
+        }
+    } else {
+        for (u32 k = tid; k < nt; k += kThreads) {
+            s.arr[k] = A.arrival[start + k];
+            s.addr[k] = rec[k];
+        }
+    }
+    for (u32 c = tid; c <= C; c += kThreads) s.seg[c] = 0;
+    __syncthreads();
+    for (u32 j = tid; j < nt; j += kThreads) {
+        const u64 r = s.addr[j];
+        const u32 status = static_cast<u32>(r >> 48) & 0xffu;
+        s.bytes[j] = static_cast<u32>(r);
+        s.ord[j] = static_cast<u16>(r >> 32);
+        s.op[j] = static_cast<u8>(status);
+        if (status == kModeled) {
+            atomicAdd(&s.seg[r >> 56], 1u);
+            ++st.modeled;
+        } else {
+            s.addr[j] = s.arr[j];  // done = arrival
+            s.arr[j] = 0;          // latency 0
+            if (status == kBypass) ++st.bypass;
+            else if (status == kForeign) ++st.foreign;
+            else ++st.unsup;
+        }
+    }
+    __syncthreads();
+    warp0_exclusive_scan(s.seg, C, &s.seg[C]);
+    __syncthreads();
+}
+
 // Block-reduce the pass-2 statistics and the die activity; one atomic each
 // per CTA.
 __device__ __forceinline__ void flush_stats(const PassArgs& A, const TileSmem& s,
@@ -798,7 +868,8 @@ timing_pass_kernel(const PassArgs args)
 // for parallelism): no pieces.
 //
 // Pass 2: thread c carries channel c's exact state through every tile of the
-// CTA's range, one step per access.
+// CTA's range, one step per access, on the partition rebuilt from pass 1's
+// records (load_records).
 //
 // Pass 1: item (r, c) carries column r of channel c's range aggregate.  Items
 // are laid out r-major so that a warp holds one kind of column.  Column 0
@@ -846,7 +917,9 @@ direct_pass_kernel(const PassArgs args)
     const TileSmem s = tile_views(smem, A);
     i64* s_col0 = reinterpret_cast<i64*>(smem + A.off_pm);  // [C][K], pass 1
     if (PASS == 2 && *A.error != 0) return;
-    const bool activity = PASS == 2 && A.tp.die_read_bytes != nullptr;
+    // activity is counted where the access sizes are decoded (pass 1) and
+    // staged until the range scan accepts the batch
+    const bool activity = PASS == 1 && A.tp.act_stage != nullptr;
     prologue(A, s, true, activity);
 
     constexpr int kItems = PASS == 1 ? 2 : 1;
@@ -885,7 +958,12 @@ direct_pass_kernel(const PassArgs args)
         const u64 start = (tile_first + tt) * T;
         if (start >= A.n) break;
         const u32 nt = static_cast<u32>(A.n - start < T ? A.n - start : T);
-        load_decode_partition<kModelDie, PASS>(A, s, start, nt, activity, st);
+        if (PASS == 1) {
+            load_decode_partition<kModelDie, 1>(A, s, start, nt, activity, st);
+            write_records(A, s, start, nt);
+        } else {
+            load_records(A, s, start, nt, st);
+        }
 #pragma unroll
         for (int it = 0; it < kItems; ++it) {
             if (!item_on[it] || coupled[it]) continue;
@@ -956,13 +1034,20 @@ direct_pass_kernel(const PassArgs args)
                 for (int j = 0; j < D; ++j) col[(j + 1) * KK] = reg[it].die[j];
             }
         }
+        if (activity)
+            for (u32 k = tid; k < 2 * C * D; k += kThreads)
+                if (s.act[k]) atomicAdd(&A.tp.act_stage[k], s.act[k]);
     } else {
-        flush_stats(A, s, st, activity);
+        flush_stats(A, s, st, false);
     }
 }
 
-// Sequential scan of the CTA range aggregates: incoming_b = R_{b-1} ...
-// R_0 (state).  One CTA; thread (c, i) owns state word i of channel c.
+// Range scan: incoming_b = R_{b-1} ... R_0 (state), one CTA per local
+// channel (channels are independent).  The CTA stages a chunk of its
+// channel's range aggregates in shared memory with coalesced loads; warp 0
+// then walks them, lane i holding state word i: one step is K shuffles and
+// K+1 max-plus terms per lane.  When the batch is accepted the CTA also adds
+// the activity pass 1 staged for its channel to the die counters.
 struct ScanArgs {
     const i64* agg;     // [ctas][C][K][K+1]
     i64* incoming;      // [ctas][C][K]
@@ -973,46 +1058,61 @@ struct ScanArgs {
     const u64* arrival;
     u64 n;
     u32 ctas, C, K;
+    u32 chunk;          // aggregates staged per round
+    u32 dies;
     DevCounters* counters;
+    const unsigned long long* act_stage;  // [C*D][2] or null
+    unsigned long long* die_read_bytes;
+    unsigned long long* die_writes;
 };
 
-__global__ void __launch_bounds__(1024) range_scan_kernel(const ScanArgs a)
+__global__ void __launch_bounds__(256) range_scan_kernel(const ScanArgs a)
 {
     extern __shared__ __align__(16) unsigned char smem[];
-    i64* v = reinterpret_cast<i64*>(smem);           // [C][K]
-    i64* w = v + static_cast<u64>(a.C) * a.K;         // [C][K]
-    const u32 words = a.C * a.K;
-    const u32 KK = a.K + 1;
+    i64* s_r = reinterpret_cast<i64*>(smem);  // [chunk][K][K+1]
+    const u32 tid = threadIdx.x, lane = tid & 31u;
+    const u32 c = blockIdx.x, K = a.K, KK = K + 1, per = K * KK;
     const u32 err = *a.error;
     if (!(err & kErrUnsorted) && (err & kErrNeedSeq)) return;  // sequential path
-    for (u32 k = threadIdx.x; k < words; k += blockDim.x)
-        v[k] = static_cast<i64>(a.state_in[k]);
-    __syncthreads();
-    if (err & kErrUnsorted) {
-        for (u32 k = threadIdx.x; k < words; k += blockDim.x) a.state_out[k] = a.state_in[k];
-        if (threadIdx.x == 0) atomicAdd(&a.counters->errors, 1ull);
-        if (threadIdx.x == 0) atomicOr(&a.counters->error_code, static_cast<unsigned long long>(*a.error));
+    const u64 row0 = static_cast<u64>(c) * K;
+    if (err & kErrUnsorted) {  // refused: keep the state
+        for (u32 k = tid; k < K; k += blockDim.x) a.state_out[row0 + k] = a.state_in[row0 + k];
+        if (c == 0 && tid == 0) {
+            atomicAdd(&a.counters->errors, 1ull);
+            atomicOr(&a.counters->error_code, static_cast<unsigned long long>(err));
+        }
         return;
     }
-    for (u32 b = 0; b < a.ctas; ++b) {
-        const i64* R = a.agg + static_cast<u64>(b) * a.C * a.K * KK;
-        i64* in = a.incoming + static_cast<u64>(b) * words;
-        for (u32 k = threadIdx.x; k < words; k += blockDim.x) {
-            in[k] = v[k];
-            const u32 c = k / a.K, i = k % a.K;
-            const i64* row = R + (static_cast<u64>(c) * a.K + i) * KK;
-            const i64* vc = v + static_cast<u64>(c) * a.K;
-            i64 best = row[a.K];
-            for (u32 j = 0; j < a.K; ++j) best = imax(best, row[j] + vc[j]);
-            w[k] = best;
+    i64 v = lane < K ? static_cast<i64>(a.state_in[row0 + lane]) : 0;
+    const u32 my_row = lane < K ? lane : 0u;
+    for (u32 b0 = 0; b0 < a.ctas; b0 += a.chunk) {
+        const u32 nb = a.ctas - b0 < a.chunk ? a.ctas - b0 : a.chunk;
+        __syncthreads();  // the previous chunk is consumed
+        for (u32 k = tid; k < nb * per; k += blockDim.x) {
+            const u32 b = k / per, w = k - b * per;
+            s_r[k] = a.agg[(static_cast<u64>(b0 + b) * a.C + c) * per + w];
         }
         __syncthreads();
-        for (u32 k = threadIdx.x; k < words; k += blockDim.x) v[k] = w[k];
-        __syncthreads();
+        if (tid < 32) {
+            for (u32 b = 0; b < nb; ++b) {
+                if (lane < K) a.incoming[(static_cast<u64>(b0 + b) * a.C + c) * K + lane] = v;
+                const i64* row = s_r + b * per + my_row * KK;
+                i64 best = row[K];
+                for (u32 j = 0; j < K; ++j) best = imax(best, row[j] + __shfl_sync(0xffffffffu, v, j));
+                if (lane < K) v = best;
+            }
+        }
     }
-    for (u32 k = threadIdx.x; k < words; k += blockDim.x)
-        a.state_out[k] = static_cast<u64>(v[k]);
-    if (threadIdx.x == 0) {
+    if (tid < K) a.state_out[row0 + tid] = static_cast<u64>(v);
+    if (a.act_stage) {
+        const u32 D = a.dies;
+        for (u32 d = tid; d < D; d += blockDim.x) {
+            const u64 k = static_cast<u64>(c) * D + d;
+            a.die_read_bytes[k] += a.act_stage[2 * k];
+            a.die_writes[k] += a.act_stage[2 * k + 1];
+        }
+    }
+    if (c == 0 && tid == 0) {
         if (a.n) *a.last_arrival = a.arrival[a.n - 1];
         atomicAdd(&a.counters->batches, 1ull);
     }
@@ -1089,6 +1189,11 @@ __global__ void sequential_kernel(const SeqArgs a)
             st[0] = sat_add_u64(s, x);
             st[1 + d.die] = sat_add_u64(st[0], top);
             done = st[1 + d.die];
+            if (a.tp.die_read_bytes) {  // this thread owns channel c's dies
+                const u64 k = static_cast<u64>(c) * a.tp.dies + d.die;
+                if (a.op[i]) a.tp.die_writes[k] += 1;
+                else a.tp.die_read_bytes[k] += a.bytes[i];
+            }
         }
         a.done[i] = done;
         a.latency[i] = done - arr;
@@ -1267,6 +1372,10 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
     const u32 initial = force_sequential ? kErrNeedSeq : 0u;
     cudaError_t err = cudaMemsetAsync(s.error, 0, sizeof(u32), stream);
     if (err != cudaSuccess) return err;
+    if (tp.act_stage && !force_sequential) {
+        err = cudaMemsetAsync(tp.act_stage, 0, 16ull * plan.C * (tp.dies ? tp.dies : 1), stream);
+        if (err != cudaSuccess) return err;
+    }
     if (initial) {
         err = cudaMemcpyAsync(s.error, &kSeqFlagHost, sizeof(u32),
                               cudaMemcpyHostToDevice, stream);
@@ -1327,13 +1436,19 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
         sa.C = plan.C;
         sa.K = plan.K;
         sa.counters = s.counters;
-        const u32 scan_smem = 2 * 8 * plan.C * plan.K;
+        sa.dies = tp.dies;
+        sa.act_stage = tp.act_stage;
+        sa.die_read_bytes = tp.die_read_bytes;
+        sa.die_writes = tp.die_writes;
+        const u32 per = 8 * plan.K * (plan.K + 1);
+        sa.chunk = (96u * 1024u) / per < plan.ctas ? (96u * 1024u) / per : plan.ctas;
+        const u32 scan_smem = sa.chunk * per;
         err = cudaFuncSetAttribute(range_scan_kernel,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(scan_smem));
         if (err != cudaSuccess) return err;
         hooks(kSlotScan, 0, stream);
-        range_scan_kernel<<<1, 1024, scan_smem, stream>>>(sa);
+        range_scan_kernel<<<plan.C, 256, scan_smem, stream>>>(sa);
         hooks(kSlotScan, 1, stream);
         hooks(kSlotPass2, 0, stream);
         p2<<<plan.ctas, kThreads, plan.smem_bytes, stream>>>(a);

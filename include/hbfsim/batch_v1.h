@@ -87,7 +87,8 @@ typedef struct hbfsim_access_batch_v1 {
  * end of the call.  Arrivals must be non-decreasing within a batch and must
  * not go below the previous batch's; a violation is recorded on the device,
  * leaves the context state unchanged, and is returned by the next
- * hbfsim_flush. */
+ * hbfsim_flush.  The outputs of such a refused batch are unspecified (the
+ * latency buffer doubles as working space between the two timing passes). */
 int hbfsim_submit_access_batch_v1(hbfsim_context* context,
                                   const hbfsim_access_batch_v1* batch,
                                   void* stream);
