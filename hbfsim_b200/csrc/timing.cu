@@ -246,6 +246,7 @@ struct PassArgs {
     u32 off_addr, off_arr, off_bytes, off_op, off_ord, off_key, off_rank;
     u32 off_wcnt, off_seg, off_pbase, off_pchan, off_pm, off_pin, off_die;
     u32 off_chan, off_act, off_red, off_ranges;
+    u32 off_sarr[2], off_sinfo[2];  // direct kernel: channel-sorted arrays per pass
     // global scratch
     i64* agg;        // [ctas][C][K][K+1]  (pass 1 out)
     i64* incoming;   // [ctas][C][K]       (pass 2 in, carried in place)
@@ -402,13 +403,21 @@ struct TileSmem {
     unsigned long long* act;  // [C*D][2]
     unsigned long long* red;
     DevRange* ranges;         // staged range table (kSmemRanges entries)
+    // Direct kernel: the tile's timed accesses in channel-sorted order, with
+    // channel c's segment shifted by c slots (starts at seg[c] + c) so that
+    // the lanes of a chain warp, one channel each, spread over the banks.
+    i64* sarr;    // max(arrival, admit); pass 2 overwrites it with done
+    u32* sinfo;   // packed step info
 };
 
 constexpr u32 kSmemRanges = 32;
 
-__device__ __forceinline__ TileSmem tile_views(unsigned char* smem, const PassArgs& A)
+__device__ __forceinline__ TileSmem tile_views(unsigned char* smem, const PassArgs& A,
+                                               int pass = 1)
 {
     TileSmem s;
+    s.sarr = reinterpret_cast<i64*>(smem + A.off_sarr[pass - 1]);
+    s.sinfo = reinterpret_cast<u32*>(smem + A.off_sinfo[pass - 1]);
     s.addr = reinterpret_cast<u64*>(smem + A.off_addr);
     s.arr = reinterpret_cast<u64*>(smem + A.off_arr);
     s.bytes = reinterpret_cast<u32*>(smem + A.off_bytes);
@@ -434,7 +443,7 @@ struct Stats7 {
 // Stage one tile, decode it, and build the channel-sorted order in s.ord
 // with segment starts in s.seg (stable: warps own contiguous chunks, lanes
 // are ranked in index order with __match_any_sync).
-template <int MODEL, int PASS>
+template <int MODEL, int PASS, bool SORTED = false>
 __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const TileSmem& s,
                                                       u64 start, u32 nt, bool activity,
                                                       Stats7& st)
@@ -552,7 +561,18 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
         const u32 e = warp * chunk + j + lane;
         if (e < nt) {
             const u32 key = s.key[e];
-            if (key < C) s.ord[s.wcnt[warp * (C + 1) + key] + s.rank[e]] = static_cast<u16>(e);
+            if (SORTED) {
+                // sorted position into s.rank (for the records), and the
+                // shifted channel-sorted copy that the chains read
+                const u32 pos = key < C ? s.wcnt[warp * (C + 1) + key] + s.rank[e] : 0u;
+                s.rank[e] = static_cast<u16>(pos);
+                if (key < C) {
+                    s.sinfo[pos + key] = s.bytes[e];
+                    s.sarr[pos + key] = imax(static_cast<i64>(s.arr[e]), s.chan[key].admit);
+                }
+            } else if (key < C) {
+                s.ord[s.wcnt[warp * (C + 1) + key] + s.rank[e]] = static_cast<u16>(e);
+            }
         }
     }
     __syncthreads();
@@ -586,7 +606,7 @@ __device__ __forceinline__ void store_tile(const PassArgs& A, const TileSmem& s,
 // Compact per-access records that pass 1 of the direct kernel leaves for
 // pass 2 in the caller's latency buffer (overwritten by pass 2 with the
 // latency):  bits 0-31  packed step info of access j (transfer | die | op),
-//            bits 32-47 s.ord[j] (the access at channel-sorted position j),
+//            bits 32-47 channel-sorted position of access j,
 //            bits 48-55 status of access j,
 //            bits 56-63 local channel of access j (C < 256 in direct mode).
 // Pass 2 rebuilds the tile's partition from them without decoding again.
@@ -596,12 +616,17 @@ __device__ __forceinline__ void write_records(const PassArgs& A, const TileSmem&
     const u32 tid = threadIdx.x;
     u64* rec = A.latency + start;
     for (u32 j = tid; j < nt; j += kThreads)
-        rec[j] = static_cast<u64>(s.bytes[j]) | (static_cast<u64>(s.ord[j]) << 32) |
+        rec[j] = static_cast<u64>(s.bytes[j]) | (static_cast<u64>(s.rank[j]) << 32) |
                  (static_cast<u64>(s.op[j]) << 48) | (static_cast<u64>(s.key[j] & 0xffu) << 56);
 }
 
-// Pass 2: stage the arrivals and the records of one tile, restore info,
-// sorted order and status, count the channel segments, and fill in the
+__device__ __forceinline__ u32 record_slot(u64 r)
+{
+    return static_cast<u32>((r >> 32) & 0xffffu) + static_cast<u32>(r >> 56);
+}
+
+// Pass 2: stage the arrivals and the records of one tile, rebuild the
+// shifted channel-sorted arrays, count the channel segments, and fill in the
 // outputs of the accesses that are not timed (done = arrival, latency 0).
 __device__ __forceinline__ void load_records(const PassArgs& A, const TileSmem& s, u64 start,
                                              u32 nt, Stats7& st)
@@ -628,11 +653,13 @@ __device__ __forceinline__ void load_records(const PassArgs& A, const TileSmem& 
     for (u32 j = tid; j < nt; j += kThreads) {
         const u64 r = s.addr[j];
         const u32 status = static_cast<u32>(r >> 48) & 0xffu;
-        s.bytes[j] = static_cast<u32>(r);
-        s.ord[j] = static_cast<u16>(r >> 32);
         s.op[j] = static_cast<u8>(status);
         if (status == kModeled) {
-            atomicAdd(&s.seg[r >> 56], 1u);
+            const u32 c = static_cast<u32>(r >> 56);
+            const u32 k = record_slot(r);
+            s.sinfo[k] = static_cast<u32>(r);
+            s.sarr[k] = imax(static_cast<i64>(s.arr[j]), s.chan[c].admit);
+            atomicAdd(&s.seg[c], 1u);
             ++st.modeled;
         } else {
             s.addr[j] = s.arr[j];  // done = arrival
@@ -645,6 +672,21 @@ __device__ __forceinline__ void load_records(const PassArgs& A, const TileSmem& 
     __syncthreads();
     warp0_exclusive_scan(s.seg, C, &s.seg[C]);
     __syncthreads();
+}
+
+// Pass 2 after the chains: completion ticks back to access order
+// (s.addr = done, s.arr = latency) and the latency statistics.
+__device__ __forceinline__ void scatter_results(const TileSmem& s, u32 nt, Stats7& st)
+{
+    for (u32 j = threadIdx.x; j < nt; j += kThreads) {
+        if (s.op[j] != kModeled) continue;
+        const u64 done = static_cast<u64>(s.sarr[record_slot(s.addr[j])]);
+        const u64 lat = done - s.arr[j];
+        s.addr[j] = done;
+        s.arr[j] = lat;
+        st.lat += lat;
+        st.max = done > st.max ? done : st.max;
+    }
 }
 
 // Block-reduce the pass-2 statistics and the die activity; one atomic each
@@ -686,11 +728,11 @@ __device__ __forceinline__ void flush_stats(const PassArgs& A, const TileSmem& s
 }
 
 __device__ __forceinline__ void prologue(const PassArgs& A, const TileSmem& s, bool die,
-                                         bool activity)
+                                         bool activity, bool stage_ranges = true)
 {
     const u32 tid = threadIdx.x, C = A.C, D = A.tp.dies;
     for (u32 c = tid; c < C; c += kThreads) s.chan[c] = stage_channel(A.tp, c, die);
-    if (A.dp.range_count <= kSmemRanges)
+    if (stage_ranges && A.dp.range_count <= kSmemRanges)
         for (u32 k = tid; k < A.dp.range_count; k += kThreads) s.ranges[k] = A.dp.ranges[k];
     if (activity)
         for (u32 k = tid; k < 2 * C * D; k += kThreads) s.act[k] = 0;
@@ -914,13 +956,13 @@ direct_pass_kernel(const PassArgs args)
     const u32 tid = threadIdx.x;
     constexpr u32 K = D + 1, KK = D + 2;
     const u32 T = A.T, C = A.C;
-    const TileSmem s = tile_views(smem, A);
+    const TileSmem s = tile_views(smem, A, PASS);
     i64* s_col0 = reinterpret_cast<i64*>(smem + A.off_pm);  // [C][K], pass 1
     if (PASS == 2 && *A.error != 0) return;
     // activity is counted where the access sizes are decoded (pass 1) and
     // staged until the range scan accepts the batch
     const bool activity = PASS == 1 && A.tp.act_stage != nullptr;
-    prologue(A, s, true, activity);
+    prologue(A, s, true, activity, PASS == 1);
 
     constexpr int kItems = PASS == 1 ? 2 : 1;
     DieRegs<D> reg[kItems];
@@ -959,7 +1001,7 @@ direct_pass_kernel(const PassArgs args)
         if (start >= A.n) break;
         const u32 nt = static_cast<u32>(A.n - start < T ? A.n - start : T);
         if (PASS == 1) {
-            load_decode_partition<kModelDie, 1>(A, s, start, nt, activity, st);
+            load_decode_partition<kModelDie, 1, true>(A, s, start, nt, activity, st);
             write_records(A, s, start, nt);
         } else {
             load_records(A, s, start, nt, st);
@@ -968,32 +1010,26 @@ direct_pass_kernel(const PassArgs args)
         for (int it = 0; it < kItems; ++it) {
             if (!item_on[it] || coupled[it]) continue;
             const u32 c = item_c[it];
-            const u32 first = s.seg[c], last = s.seg[c + 1];
+            const u32 first = s.seg[c] + c, last = s.seg[c + 1] + c;  // shifted segment
             const ChanInfo ci = s.chan[c];
             if (PASS == 1) {
-                const bool real = item_r[it] == K;
+                if (item_r[it] == K) {
 #pragma unroll 4
-                for (u32 k = first; k < last; ++k) {
-                    const u32 e = s.ord[k];
-                    const i64 a = real ? imax(static_cast<i64>(s.arr[e]), ci.admit) : kNeg;
-                    reg[it].step(a, s.bytes[e], ci);
+                    for (u32 k = first; k < last; ++k) reg[it].step(s.sarr[k], s.sinfo[k], ci);
+                } else {
+#pragma unroll 4
+                    for (u32 k = first; k < last; ++k) reg[it].step(kNeg, s.sinfo[k], ci);
                 }
             } else {
 #pragma unroll 4
-                for (u32 k = first; k < last; ++k) {
-                    const u32 e = s.ord[k];
-                    const u64 arr = s.arr[e];
-                    const i64 done = reg[it].step(imax(static_cast<i64>(arr), ci.admit),
-                                                  s.bytes[e], ci);
-                    const u64 ud = static_cast<u64>(done);
-                    s.addr[e] = ud;
-                    s.arr[e] = ud - arr;
-                    st.lat += ud - arr;
-                    st.max = ud > st.max ? ud : st.max;
-                }
+                for (u32 k = first; k < last; ++k) s.sarr[k] = reg[it].step(s.sarr[k], s.sinfo[k], ci);
             }
         }
         __syncthreads();
+        if (PASS == 2) {
+            scatter_results(s, nt, st);
+            __syncthreads();
+        }
         if (PASS == 1) {
             // snapshot column 0, then let die columns try to couple to it
 #pragma unroll
@@ -1260,7 +1296,11 @@ struct Launch {
 static u32 align_up(u32 v, u32 a) { return (v + a - 1) / a * a; }
 
 // Shared-memory layout for a tile of T accesses with C channels, K words.
-// The piece arrays exist only in piece mode.
+// Piece mode: one layout for both passes.  Direct mode: a common part
+// (staged inputs / outputs, status, segments, channel table, reduction
+// slots) and a tail that pass 1 fills with its partition and column arrays
+// and pass 2 with its channel-sorted copy.  In pass 1 the sorted arrivals
+// overlay the staged addresses, which are dead once the tile is decoded.
 static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
                   u32 group_channels, bool direct)
 {
@@ -1278,6 +1318,34 @@ static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
     a.K = K;
     a.group_channels = group_channels;
     a.pm_capacity = pm_capacity;
+    const u32 D = dies ? dies : 1;
+    if (direct) {
+        a.off_addr = take(8 * (T + C));
+        a.off_arr = take(8 * T);
+        a.off_op = take(T);
+        a.off_seg = take(4 * (C + 2));
+        a.off_chan = take(static_cast<u32>(sizeof(ChanInfo)) * C);
+        a.off_red = take(8 * 8 * kWarps);
+        const u32 tail = align_up(off, 16);
+        // pass 1
+        a.off_bytes = take(4 * T);
+        a.off_key = take(2 * T);
+        a.off_rank = take(2 * T);
+        a.off_wcnt = take(4 * kWarps * (C + 1));
+        a.off_act = take(16 * C * D);
+        a.off_ranges = take(static_cast<u32>(sizeof(DevRange)) * kSmemRanges);
+        a.off_pm = take(8 * C * K);  // column-0 snapshot
+        a.off_sinfo[0] = take(4 * (T + C));
+        a.off_sarr[0] = a.off_addr;
+        a.off_ord = 0;
+        const u32 end1 = align_up(off, 16);
+        // pass 2
+        off = tail;
+        a.off_sarr[1] = take(8 * (T + C));
+        a.off_sinfo[1] = take(4 * (T + C));
+        const u32 end2 = align_up(off, 16);
+        return end1 > end2 ? end1 : end2;
+    }
     a.off_addr = take(8 * T);
     a.off_arr = take(8 * T);
     a.off_bytes = take(4 * T);
@@ -1288,18 +1356,16 @@ static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
     a.off_seg = take(4 * (C + 2));
     a.off_wcnt = take(4 * kWarps * (C + 1));
     a.off_chan = take(static_cast<u32>(sizeof(ChanInfo)) * C);
-    a.off_act = take(16 * C * (dies ? dies : 1));
+    a.off_act = take(16 * C * D);
     a.off_red = take(8 * 8 * kWarps);
     a.off_ranges = take(static_cast<u32>(sizeof(DevRange)) * kSmemRanges);
-    if (direct) {
-        a.off_pm = take(8 * C * K);  // column-0 snapshot of pass 1
-    } else {
-        a.off_pbase = take(4 * (C + 2));
-        a.off_pchan = take(2 * (T / L + C + 1));
-        a.off_pm = take(8 * pm_capacity * K * (K + 1));
-        a.off_pin = take(8 * pm_capacity * K);
-        a.off_die = take(8 * (dies ? dies : 1) * kThreads);
-    }
+    a.off_pbase = take(4 * (C + 2));
+    a.off_pchan = take(2 * (T / L + C + 1));
+    a.off_pm = take(8 * pm_capacity * K * (K + 1));
+    a.off_pin = take(8 * pm_capacity * K);
+    a.off_die = take(8 * D * kThreads);
+    a.off_sarr[0] = a.off_sarr[1] = 0;
+    a.off_sinfo[0] = a.off_sinfo[1] = 0;
     return align_up(off, 16);
 }
 
@@ -1322,7 +1388,7 @@ int plan_batch(u64 n, u32 C, u32 K, u32 dies, int sm_count, BatchPlan* plan)
     const bool direct = direct_supported(C, K, dies);
     u32 T = 2048, L = 32, group = C;
     const u32 per_sm = direct ? 3 : 2;
-    const u32 smem_limit = (direct ? 72 : 110) * 1024;
+    const u32 smem_limit = (direct ? 74 : 110) * 1024;  // 3 or 2 CTAs per SM
     if (direct) {
         L = T;
         while (layout(probe, T, L, C, K, dies, group, true) > smem_limit) {
