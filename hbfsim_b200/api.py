@@ -233,3 +233,89 @@ class Context:
         check(self._lib.hbfsim_get_die_activity_v1(self.handle, _ptr(rb), _ptr(wr), dies_total),
               "hbfsim_get_die_activity_v1")
         return rb, wr
+
+    # ---- eq3 thermal grid and epoch controller ----
+    def thermal_configure(self, stack: dict, floorplan: dict, power: dict,
+                          refresh: dict, throttle: dict) -> None:
+        """Configures the layered thermal grid and the epoch controller.
+
+        stack: {"nx", "ny", "cell_m", "layers": [{"thickness_m", "cv_j_m3_k",
+        "k_xyz_w_m_k"}], "bottom": {"h_w_m2_k", "ambient_k"}, "top": {...},
+        "initial_k"} (the layered-export description).
+        floorplan: arrays z0, z_count, x0, x1, y0, y1 indexed g*D+d.
+        power: {"idle_w", "read_j_per_byte", "write_j_per_access"}.
+        refresh: {"onset_k", "step_k", "base_permille", "cap_permille"}.
+        throttle: {"light_k", "severe_k", "shutdown_k", "hysteresis_k",
+        "light_permille", "severe_permille"}."""
+        c = _lib.ThermalConfigV1()
+        c.struct_size = ctypes.sizeof(_lib.ThermalConfigV1)
+        c.version = 1
+        c.nx, c.ny = stack["nx"], stack["ny"]
+        c.layer_count = len(stack["layers"])
+        c.cell_m = stack["cell_m"]
+        for i, layer in enumerate(stack["layers"]):
+            c.layers[i].thickness_m = layer["thickness_m"]
+            c.layers[i].cv_j_m3_k = layer["cv_j_m3_k"]
+            for a in range(3):
+                c.layers[i].k_xyz_w_m_k[a] = layer["k_xyz_w_m_k"][a]
+        c.bottom_h_w_m2_k = stack["bottom"]["h_w_m2_k"]
+        c.bottom_ambient_k = stack["bottom"]["ambient_k"]
+        c.top_h_w_m2_k = stack["top"]["h_w_m2_k"]
+        c.top_ambient_k = stack["top"]["ambient_k"]
+        c.initial_k = stack["initial_k"]
+        c.die_idle_w = power["idle_w"]
+        c.read_j_per_byte = power["read_j_per_byte"]
+        c.write_j_per_access = power["write_j_per_access"]
+        c.refresh_onset_k = refresh["onset_k"]
+        c.refresh_step_k = refresh["step_k"]
+        c.refresh_base_permille = refresh["base_permille"]
+        c.refresh_cap_permille = refresh["cap_permille"]
+        for key in ("light_k", "severe_k", "shutdown_k", "hysteresis_k",
+                    "light_permille", "severe_permille"):
+            setattr(c, key, throttle[key])
+        keep = {}
+        for key in ("z0", "z_count", "x0", "x1", "y0", "y1"):
+            keep[key] = np.ascontiguousarray(floorplan[key], np.uint32)
+            setattr(c, "die_" + key, keep[key].ctypes.data)
+        check(self._lib.hbfsim_thermal_configure_v1(self.handle, ctypes.byref(c)),
+              "hbfsim_thermal_configure_v1")
+
+    def advance_epoch(self, epoch_s: float, stream=None) -> None:
+        check(self._lib.hbfsim_advance_epoch_v1(self.handle, ctypes.c_double(epoch_s),
+                                                ctypes.c_void_p(_stream_handle(stream))),
+              "hbfsim_advance_epoch_v1")
+
+    def advance_epoch_global(self, epoch_s: float, read_bytes, writes, stream=None) -> None:
+        """Epoch step driven by the activity of every global die (device
+        tensors of uint64 viewed as int64, index g*D+d)."""
+        check(self._lib.hbfsim_advance_epoch_global_v1(
+            self.handle, ctypes.c_double(epoch_s), _ptr(read_bytes), _ptr(writes),
+            ctypes.c_void_p(_stream_handle(stream))), "hbfsim_advance_epoch_global_v1")
+
+    def copy_die_activity(self, read_bytes, writes, stream=None) -> None:
+        check(self._lib.hbfsim_copy_die_activity_v1(self.handle, _ptr(read_bytes), _ptr(writes),
+                                                    ctypes.c_void_p(_stream_handle(stream))),
+              "hbfsim_copy_die_activity_v1")
+
+    def temperatures(self, cells: int) -> np.ndarray:
+        out = np.zeros(cells, np.float64)
+        check(self._lib.hbfsim_get_temperatures_v1(self.handle, _ptr(out), cells),
+              "hbfsim_get_temperatures_v1")
+        return out
+
+    def die_temperatures(self, dies_total: int) -> np.ndarray:
+        out = np.zeros(dies_total, np.float64)
+        check(self._lib.hbfsim_get_die_temperatures_v1(self.handle, _ptr(out), dies_total),
+              "hbfsim_get_die_temperatures_v1")
+        return out
+
+    def thermal_factors(self, channels: int, stacks: int):
+        """(refresh per local channel, throttle, admit-after, level per stack)."""
+        r = np.zeros(channels, np.uint32)
+        t = np.zeros(stacks, np.uint32)
+        a = np.zeros(stacks, np.uint64)
+        lv = np.zeros(stacks, np.uint32)
+        check(self._lib.hbfsim_get_thermal_factors_v1(self.handle, _ptr(r), _ptr(t), _ptr(a),
+                                                      _ptr(lv)),
+              "hbfsim_get_thermal_factors_v1")
+        return r, t, a, lv

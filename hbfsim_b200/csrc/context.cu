@@ -115,6 +115,20 @@ int upload_ranges(hbfsim_context* c)
 }
 
 // Recompute the per-channel device tables from the factor inputs.
+// With a thermal grid configured, the epoch controller writes the factors
+// on the device; bring them back into the host copies.
+int pull_thermal_factors(hbfsim_context* c)
+{
+    std::uint32_t *r, *t;
+    std::uint64_t* a;
+    thermal_factor_arrays(c->thermal, &r, &t, &a);
+    if (cudaMemcpy(c->refresh_permille.data(), r, 4ull * c->C, cudaMemcpyDeviceToHost) ||
+        cudaMemcpy(c->throttle_permille.data(), t, 4ull * c->stacks, cudaMemcpyDeviceToHost) ||
+        cudaMemcpy(c->admit_after.data(), a, 8ull * c->stacks, cudaMemcpyDeviceToHost))
+        return HBFSIM_CUDA_ERROR;
+    return HBFSIM_OK;
+}
+
 int update_tables(hbfsim_context* c)
 {
     const Profile& p = c->profile;
@@ -154,6 +168,13 @@ int update_tables(hbfsim_context* c)
                            p.time_scale);
         c->t_max = sat_mul(std::max(p.read_latency_ns, p.program_latency_ns), p.time_scale);
         c->admit_max = 0;
+    }
+    if (c->thermal) {  // the epoch controller may raise the factors later
+        std::uint64_t xb, ob, ab;
+        thermal_tick_bounds(c->thermal, &xb, &ob, &ab);
+        c->x_max = std::max(c->x_max, xb);
+        c->t_max = std::max(c->t_max, ob);
+        c->admit_max = std::max(c->admit_max, ab);
     }
     const std::size_t bytes = sizeof(std::uint64_t) * c->C;
     if (cudaMemcpyAsync(c->d_chan_bw, h_bw.data(), bytes, cudaMemcpyHostToDevice, c->stream) ||
@@ -789,10 +810,24 @@ int hbfsim_set_channel_factors_v1(hbfsim_context* c, const uint32_t* refresh,
         for (std::uint32_t k = 0; k < c->stacks; ++k)
             if (throttle[k] == 0) return HBFSIM_INVALID_ARGUMENT;
     if (cudaDeviceSynchronize() != cudaSuccess) return HBFSIM_CUDA_ERROR;
+    if (c->thermal) {  // the controller's values are the ones in force
+        const int rc = pull_thermal_factors(c);
+        if (rc != HBFSIM_OK) return rc;
+    }
     if (refresh) c->refresh_permille.assign(refresh, refresh + c->C);
     if (throttle) c->throttle_permille.assign(throttle, throttle + c->stacks);
     if (admit) c->admit_after.assign(admit, admit + c->stacks);
-    return update_tables(c);
+    const int rc = update_tables(c);
+    if (rc != HBFSIM_OK || !c->thermal) return rc;
+    // keep the controller's copy in step: the next epoch starts from these
+    std::uint32_t *r, *t;
+    std::uint64_t* a;
+    thermal_factor_arrays(c->thermal, &r, &t, &a);
+    if (cudaMemcpy(r, c->refresh_permille.data(), 4ull * c->C, cudaMemcpyHostToDevice) ||
+        cudaMemcpy(t, c->throttle_permille.data(), 4ull * c->stacks, cudaMemcpyHostToDevice) ||
+        cudaMemcpy(a, c->admit_after.data(), 8ull * c->stacks, cudaMemcpyHostToDevice))
+        return HBFSIM_CUDA_ERROR;
+    return HBFSIM_OK;
 }
 
 int hbfsim_get_channel_factors_v1(hbfsim_context* c, uint32_t* refresh, uint32_t* throttle,
@@ -800,6 +835,11 @@ int hbfsim_get_channel_factors_v1(hbfsim_context* c, uint32_t* refresh, uint32_t
 {
     if (!c) return HBFSIM_INVALID_ARGUMENT;
     Guard g(c);
+    if (c->thermal) {
+        if (cudaDeviceSynchronize() != cudaSuccess) return HBFSIM_CUDA_ERROR;
+        const int rc = pull_thermal_factors(c);
+        if (rc != HBFSIM_OK) return rc;
+    }
     if (refresh) std::copy(c->refresh_permille.begin(), c->refresh_permille.end(), refresh);
     if (throttle) std::copy(c->throttle_permille.begin(), c->throttle_permille.end(), throttle);
     if (admit) std::copy(c->admit_after.begin(), c->admit_after.end(), admit);

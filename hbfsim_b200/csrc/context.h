@@ -96,4 +96,12 @@ struct hbfsim_context {
 namespace hbfb {
 // thermal.cu
 void thermal_destroy(ThermalState* t);
+// Device arrays of the factors the epoch controller derived (refresh per
+// local channel, throttle permille and admit-after tick per stack).
+void thermal_factor_arrays(ThermalState* t, std::uint32_t** refresh, std::uint32_t** throttle,
+                           std::uint64_t** admit);
+// Largest transfer tick, die-op tick and admit tick the controller can put
+// into the channel tables (bounds for the parallel path's tick proof).
+void thermal_tick_bounds(const ThermalState* t, std::uint64_t* x, std::uint64_t* op,
+                         std::uint64_t* admit);
 }

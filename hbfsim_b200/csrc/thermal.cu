@@ -56,7 +56,25 @@ struct ThermalState {
     std::uint64_t* d_admit = nullptr;    // per stack
     std::uint64_t epoch_end_ns = 0;
     std::uint64_t epochs = 0;
+    // bounds of what the controller can write into the channel tables
+    std::uint64_t x_bound = 0, op_bound = 0, admit_bound = 0;
 };
+
+void thermal_factor_arrays(ThermalState* t, std::uint32_t** refresh, std::uint32_t** throttle,
+                           std::uint64_t** admit)
+{
+    *refresh = t->d_refresh;
+    *throttle = t->d_throttle;
+    *admit = t->d_admit;
+}
+
+void thermal_tick_bounds(const ThermalState* t, std::uint64_t* x, std::uint64_t* op,
+                         std::uint64_t* admit)
+{
+    *x = t->x_bound;
+    *op = t->op_bound;
+    *admit = t->admit_bound;
+}
 
 void thermal_destroy(ThermalState* t)
 {
@@ -370,7 +388,8 @@ int advance(hbfsim_context* c, double epoch_s, const unsigned long long* rb,
     controller_kernel<<<1, 1024, 0, s>>>(a);
     hooks(kSlotController, 1, s);
     // the admission tick bound used by the host's path choice
-    c->admit_max = std::max<std::uint64_t>(c->admit_max, a.next_epoch_end);
+    t->admit_bound = std::max<std::uint64_t>(t->admit_bound, a.next_epoch_end);
+    c->admit_max = std::max<std::uint64_t>(c->admit_max, t->admit_bound);
     const std::uint64_t dies_local = static_cast<std::uint64_t>(c->C) * std::max(1u, c->D);
     if (cudaMemsetAsync(c->d_die_read_bytes, 0, 8 * dies_local, s) ||
         cudaMemsetAsync(c->d_die_writes, 0, 8 * dies_local, s))
@@ -517,11 +536,11 @@ int hbfsim_thermal_configure_v1(hbfsim_context* c, const hbfsim_thermal_config_v
         up(t->d_cell_die, owner.data(), sizeof(int) * cells);
         up(t->d_die_cells, die_cells.data(), 8 * dies);
         ok = ok && cudaMemset(t->d_level, 0, 4 * c->stacks) == cudaSuccess &&
-             cudaMemset(t->d_refresh, 0, 4 * c->C) == cudaSuccess &&
-             cudaMemset(t->d_admit, 0, 8 * c->stacks) == cudaSuccess &&
              cudaMemset(t->d_die_temp, 0, 8 * dies) == cudaSuccess;
-        std::vector<std::uint32_t> one(c->stacks, 1000);
-        up(t->d_throttle, one.data(), 4 * c->stacks);
+        // the factors in force until the first epoch closes
+        up(t->d_refresh, c->refresh_permille.data(), 4ull * c->C);
+        up(t->d_throttle, c->throttle_permille.data(), 4ull * c->stacks);
+        up(t->d_admit, c->admit_after.data(), 8ull * c->stacks);
     }
     if (!ok) {
         thermal_destroy(t);
@@ -542,6 +561,8 @@ int hbfsim_thermal_configure_v1(hbfsim_context* c, const hbfsim_thermal_config_v
         (static_cast<unsigned __int128>(std::max(c->profile.read_latency_ns,
                                                  c->profile.program_latency_ns)) * thr + 999) /
         1000 * c->profile.time_scale;
+    t->x_bound = xw;
+    t->op_bound = tw;
     c->x_max = std::max(c->x_max, xw);
     c->t_max = std::max(c->t_max, tw);
     return HBFSIM_OK;

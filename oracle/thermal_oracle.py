@@ -106,3 +106,91 @@ class ThermalGrid:
             step_dt = dt * (s + 1) - dt * s
             out.append(self.step(np.asarray(p, dtype=np.float64), step_dt).copy())
         return out
+
+
+# ---------------------------------------------------------------------------
+# Epoch coupling: die activity -> cell power, and the refresh / throttle
+# controller.  The refresh-doubling law and the per-die power law come from
+# the benchmark's thermal-coupled configuration (the reference marks both
+# NOT_IMPLEMENTED), so their parity is unpinned; the throttle levels follow CpuService's control
+# sample (src/eq3_thermal/cpu_service.cpp:221-247) with the decision applied
+# at once at each epoch boundary (no action delay or dwell).
+
+def die_floorplan(owner_shape, z0, z_count, x0, x1, y0, y1):
+    """Cell -> owning die (-1 = none), cell index z*nx*ny + y*nx + x."""
+    nz, ny, nx = owner_shape
+    owner = np.full(nz * ny * nx, -1, np.int64)
+    for d in range(len(z0)):
+        for z in range(z0[d], z0[d] + z_count[d]):
+            for y in range(y0[d], y1[d]):
+                for x in range(x0[d], x1[d]):
+                    i = z * nx * ny + y * nx + x
+                    assert owner[i] < 0, "overlapping dies"
+                    owner[i] = d
+    return owner
+
+
+def cell_power(owner, dies, read_bytes, writes, idle_w, j_per_byte, j_per_write, dt):
+    """Die power = idle + (read bytes * J/B + writes * J/write) / dt, spread
+    evenly over the die's cells."""
+    die_w = idle_w + (np.asarray(read_bytes, np.float64) * j_per_byte +
+                      np.asarray(writes, np.float64) * j_per_write) / dt
+    cells = np.bincount(owner[owner >= 0], minlength=dies).astype(np.float64)
+    p = np.zeros(owner.size)
+    m = owner >= 0
+    p[m] = die_w[owner[m]] / cells[owner[m]]
+    return p
+
+
+def die_mean(owner, dies, temperature):
+    m = owner >= 0
+    s = np.bincount(owner[m], weights=temperature[m], minlength=dies)
+    c = np.bincount(owner[m], minlength=dies)
+    return np.where(c > 0, s / np.maximum(c, 1), 0.0)
+
+
+class Controller:
+    """Refresh permille per local channel, throttle level / permille /
+    admit-after tick per stack, from per-die temperatures (global die index
+    g*D+d; stack of channel g = g mod stacks)."""
+
+    def __init__(self, stacks, channels_total, dies, refresh, throttle,
+                 shard_rank=0, shard_count=1):
+        self.stacks, self.channels_total, self.dies = stacks, channels_total, dies
+        self.refresh, self.throttle = refresh, throttle
+        self.rank, self.shards = shard_rank, shard_count
+        self.level = np.zeros(stacks, np.int64)
+
+    def step(self, die_temp, next_epoch_end):
+        th = self.throttle
+        thresholds = (th["light_k"], th["severe_k"], th["shutdown_k"])
+        permille = np.zeros(self.stacks, np.uint32)
+        admit = np.zeros(self.stacks, np.uint64)
+        for s in range(self.stacks):
+            hot = 0.0
+            for g in range(s, self.channels_total, self.stacks):
+                hot = max(hot, float(np.max(die_temp[g * self.dies:(g + 1) * self.dies])))
+            applied = int(self.level[s])
+            desired = sum(1 for t in thresholds if hot >= t)
+            if desired < applied and hot >= thresholds[applied - 1] - th["hysteresis_k"]:
+                desired = applied
+            self.level[s] = desired
+            permille[s] = (th["light_permille"] if desired == 1 else
+                           th["severe_permille"] if desired >= 2 else 1000)
+            admit[s] = next_epoch_end if desired == 3 else 0
+        local = -(-self.channels_total // self.shards)
+        refresh = np.zeros(local, np.uint32)
+        rf = self.refresh
+        for c in range(local):
+            g = c * self.shards + self.rank
+            total = 0
+            if g < self.channels_total:
+                for d in range(self.dies):
+                    t = float(die_temp[g * self.dies + d])
+                    share = rf["base_permille"]
+                    if t >= rf["onset_k"]:
+                        share <<= min(20, int(np.floor((t - rf["onset_k"]) / rf["step_k"])))
+                    total += share
+                total //= self.dies
+            refresh[c] = min(total, rf["cap_permille"])
+        return refresh, permille, admit, self.level.copy()
