@@ -130,6 +130,7 @@ SIGNATURES = {
     "hbfsim_get_kernel_times_v1": (i32, [vp, ctypes.POINTER(KernelTimesV1)]),
     "hbfsim_get_batch_stats_v1": (i32, [vp, ctypes.POINTER(BatchStatsV1)]),
     "hbfsim_decode_batch_v1": (i32, [vp, vp, vp, vp, u64, vp, vp]),
+    "hbfsim_sample_batch_v1": (i32, [vp, vp, vp, vp, u64, vp, vp]),
     "hbfsim_set_channel_factors_v1": (i32, [vp, vp, vp, vp]),
     "hbfsim_get_channel_factors_v1": (i32, [vp, vp, vp, vp]),
     "hbfsim_get_state_v1": (i32, [vp, vp, u64]),

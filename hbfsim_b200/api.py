@@ -199,6 +199,17 @@ class Context:
               "hbfsim_decode_batch_v1")
         return out
 
+    def sample(self, address, nbytes, op, stream=None):
+        """Hybrid sampler bits of device tensors (uint8 device tensor; 1 =
+        the hybrid model would send the access to the reference model)."""
+        import torch
+        out = torch.empty(address.numel(), dtype=torch.uint8, device=address.device)
+        check(self._lib.hbfsim_sample_batch_v1(self.handle, _ptr(address), _ptr(nbytes), _ptr(op),
+                                               address.numel(), _ptr(out),
+                                               ctypes.c_void_p(_stream_handle(stream))),
+              "hbfsim_sample_batch_v1")
+        return out
+
     def set_channel_factors(self, refresh_permille=None, throttle_permille=None,
                             admit_after_ns=None) -> None:
         r = None if refresh_permille is None else np.ascontiguousarray(refresh_permille, np.uint32)

@@ -114,7 +114,6 @@ int upload_ranges(hbfsim_context* c)
     return HBFSIM_OK;
 }
 
-// Recompute the per-channel device tables from the factor inputs.
 // With a thermal grid configured, the epoch controller writes the factors
 // on the device; bring them back into the host copies.
 int pull_thermal_factors(hbfsim_context* c)
@@ -129,6 +128,7 @@ int pull_thermal_factors(hbfsim_context* c)
     return HBFSIM_OK;
 }
 
+// Recompute the per-channel device tables from the factor inputs.
 int update_tables(hbfsim_context* c)
 {
     const Profile& p = c->profile;
@@ -441,13 +441,16 @@ int hbfsim_context_create(const hbfsim_options* options, hbfsim_context** out)
         cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, c->device) !=
             cudaSuccess ||
         cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
-        dalloc(&c->d_error, 1) || dalloc(&c->d_last_arrival, 1) || dalloc(&c->d_counters, 1)) {
+        dalloc(&c->d_error, 1) || dalloc(&c->d_last_arrival, 1) || dalloc(&c->d_counters, 1) ||
+        dalloc(&c->d_sample_seq, 1) ||
+        dalloc(&c->d_sample_counts, hbfsim_context::kSampleCtas)) {
         hbfsim_context_destroy(c);
         return HBFSIM_CUDA_ERROR;
     }
     cudaMemset(c->d_error, 0, sizeof(std::uint32_t));
     cudaMemset(c->d_last_arrival, 0, sizeof(std::uint64_t));
     cudaMemset(c->d_counters, 0, sizeof(DevCounters));
+    cudaMemset(c->d_sample_seq, 0, sizeof(std::uint64_t));
     const int rc = configure_geometry(c, 1, 0, 0, 1);
     if (rc != HBFSIM_OK) {
         hbfsim_context_destroy(c);
@@ -587,6 +590,8 @@ void hbfsim_context_destroy(hbfsim_context* c)
     dfree(c->d_error);
     dfree(c->d_last_arrival);
     dfree(c->d_counters);
+    dfree(c->d_sample_seq);
+    dfree(c->d_sample_counts);
     for (auto& p : c->d_stage) {
         if (p) cudaFree(p);
         p = nullptr;
@@ -793,6 +798,29 @@ int hbfsim_decode_batch_v1(hbfsim_context* c, const uint64_t* address, const uin
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
     return launch_decode(decode_params(c), address, bytes, operation, count, out, s,
                          c->hooks()) ==
+                   cudaSuccess
+               ? HBFSIM_OK
+               : HBFSIM_CUDA_ERROR;
+}
+
+int hbfsim_sample_batch_v1(hbfsim_context* c, const uint64_t* address, const uint32_t* bytes,
+                           const uint8_t* operation, uint64_t count, uint8_t* sample,
+                           void* stream)
+{
+    if (!c || (count && (!address || !bytes || !operation || !sample)))
+        return HBFSIM_INVALID_ARGUMENT;
+    Guard g(c);
+    const Profile& p = c->profile;
+    // reference context.cpp:975-981: rate * (long double) UINT64_MAX
+    const std::uint64_t threshold =
+        p.reference_sample_rate >= 1.0
+            ? ~std::uint64_t{0}
+            : static_cast<std::uint64_t>(p.reference_sample_rate *
+                                         static_cast<long double>(~std::uint64_t{0}));
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    return launch_sample(decode_params(c), address, bytes, operation, count, sample,
+                         p.reference_warmup_requests, threshold, c->d_sample_seq,
+                         c->d_sample_counts, hbfsim_context::kSampleCtas, s, c->hooks()) ==
                    cudaSuccess
                ? HBFSIM_OK
                : HBFSIM_CUDA_ERROR;

@@ -53,6 +53,10 @@ struct hbfsim_context {
     std::uint32_t* d_error = nullptr;
     std::uint64_t* d_last_arrival = nullptr;
     hbfb::DevCounters* d_counters = nullptr;
+    // hybrid sampler: running count of timed accesses, per-CTA scratch
+    std::uint64_t* d_sample_seq = nullptr;
+    std::uint64_t* d_sample_counts = nullptr;
+    static constexpr std::uint32_t kSampleCtas = 1024;
     std::uint64_t errors_reported = 0;
 
     // channel factor tables (device, per local channel) + host inputs

@@ -1564,3 +1564,148 @@ cudaError_t launch_decode(const DecodeParams& dp, const u64* address,
 }
 
 }  // namespace hbfb
+
+// ---------------------------------------------------------------------------
+// Hybrid sampler bit (A7).  The reference numbers every access that reaches
+// resolve_fast_or_hybrid (hbf_device.cu:779-788) with a device-wide counter
+// and sends it to the reference model when hybrid_reference_sample
+// (hbf_device.cuh:738-744) says so, keyed by
+// media address ^ range_id << 32 ^ op.  Here the counter is the context's
+// running count of timed accesses in batch order: each CTA counts its
+// contiguous share, a one-block scan turns the counts into starting numbers,
+// and the write pass numbers the accesses in order.
+namespace hbfb {
+namespace {
+
+constexpr u32 kSampleThreads = 256;
+constexpr u32 kSampleItems = 8;  // contiguous accesses per thread per round
+
+// splitmix64 finalizer (Steele, Lea & Flood, "Fast splittable pseudorandom
+// number generators", 2014), the mix the reference sampler uses
+__device__ __forceinline__ u64 sample_mix(u64 v)
+{
+    v += 0x9e3779b97f4a7c15ull;
+    v = (v ^ (v >> 30)) * 0xbf58476d1ce4e5b9ull;
+    v = (v ^ (v >> 27)) * 0x94d049bb133111ebull;
+    return v ^ (v >> 31);
+}
+
+__device__ __forceinline__ u64 sample_key(const DecodeParams& p, const Decoded& d, u32 op)
+{
+    return d.media ^ (static_cast<u64>(p.ranges[d.range_index].range_id) << 32) ^ op;
+}
+
+__global__ void __launch_bounds__(kSampleThreads)
+sample_count_kernel(const DecodeParams p, const u64* address, const u32* bytes, const u8* op,
+                    u64 n, u64 per, u64* counts)
+{
+    const u64 lo = blockIdx.x * per, hi = lo + per < n ? lo + per : n;
+    u32 mine = 0;
+    for (u64 i = lo + threadIdx.x; i < hi; i += kSampleThreads)
+        mine += classify_decode(p, address[i], bytes[i], op[i], false).status == kModeled;
+    __shared__ u32 red[kSampleThreads / 32];
+    for (int o = 16; o > 0; o >>= 1) mine += __shfl_down_sync(0xffffffffu, mine, o);
+    if ((threadIdx.x & 31u) == 0) red[threadIdx.x >> 5] = mine;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        u64 total = 0;
+        for (u32 w = 0; w < kSampleThreads / 32; ++w) total += red[w];
+        counts[blockIdx.x] = total;
+    }
+}
+
+// counts -> starting sequence numbers; the context counter moves past them
+__global__ void sample_scan_kernel(u64* counts, u32 ctas, u64* seq)
+{
+    if (threadIdx.x != 0) return;
+    u64 run = *seq;
+    for (u32 b = 0; b < ctas; ++b) {
+        const u64 c = counts[b];
+        counts[b] = run;
+        run += c;
+    }
+    *seq = run;
+}
+
+__global__ void __launch_bounds__(kSampleThreads)
+sample_write_kernel(const DecodeParams p, const u64* address, const u32* bytes, const u8* op,
+                    u64 n, u64 per, const u64* starts, u32 warmup, u64 threshold, u8* sample)
+{
+    const u64 lo = blockIdx.x * per, hi = lo + per < n ? lo + per : n;
+    __shared__ u32 warp_sum[kSampleThreads / 32];
+    __shared__ u32 round_total;
+    const u32 lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    u64 next = starts[blockIdx.x];
+    for (u64 base = lo; base < hi; base += static_cast<u64>(kSampleThreads) * kSampleItems) {
+        const u64 first = base + static_cast<u64>(threadIdx.x) * kSampleItems;
+        Decoded d[kSampleItems];
+        u32 count = 0;
+#pragma unroll
+        for (u32 k = 0; k < kSampleItems; ++k) {
+            const u64 i = first + k;
+            d[k].status = 0;
+            if (i < hi) {
+                d[k] = classify_decode(p, address[i], bytes[i], op[i], false);
+                count += d[k].status == kModeled;
+            }
+        }
+        // block exclusive scan of the per-thread counts (index order)
+        u32 incl = count;
+        for (int o = 1; o < 32; o <<= 1) {
+            const u32 y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= static_cast<u32>(o)) incl += y;
+        }
+        if (lane == 31) warp_sum[warp] = incl;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            u32 run = 0;
+            for (u32 w = 0; w < kSampleThreads / 32; ++w) {
+                const u32 s = warp_sum[w];
+                warp_sum[w] = run;
+                run += s;
+            }
+            round_total = run;
+        }
+        __syncthreads();
+        u64 seq = next + warp_sum[warp] + incl - count;
+#pragma unroll
+        for (u32 k = 0; k < kSampleItems; ++k) {
+            const u64 i = first + k;
+            if (i >= hi) break;
+            u8 bit = 0;
+            if (d[k].status == kModeled) {
+                bit = seq < warmup ||
+                      (threshold != 0 && sample_mix(seq ^ sample_key(p, d[k], op[i])) <= threshold);
+                ++seq;
+            }
+            sample[i] = bit;
+        }
+        next += round_total;
+        __syncthreads();
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_sample(const DecodeParams& dp, const u64* address, const u32* bytes,
+                          const u8* op, u64 n, u8* sample, u32 warmup, u64 threshold,
+                          u64* seq, u64* counts, u32 max_ctas, cudaStream_t stream,
+                          const LaunchHooks& hooks)
+{
+    if (n == 0) return cudaSuccess;
+    const u64 min_per = static_cast<u64>(kSampleThreads) * kSampleItems;
+    u64 ctas = (n + min_per - 1) / min_per;
+    if (ctas > max_ctas) ctas = max_ctas;
+    const u64 per = (n + ctas - 1) / ctas;
+    ctas = (n + per - 1) / per;
+    hooks(kSlotOther, 0, stream);
+    sample_count_kernel<<<static_cast<unsigned>(ctas), kSampleThreads, 0, stream>>>(
+        dp, address, bytes, op, n, per, counts);
+    sample_scan_kernel<<<1, 32, 0, stream>>>(counts, static_cast<u32>(ctas), seq);
+    sample_write_kernel<<<static_cast<unsigned>(ctas), kSampleThreads, 0, stream>>>(
+        dp, address, bytes, op, n, per, counts, warmup, threshold, sample);
+    hooks(kSlotOther, 1, stream);
+    return cudaGetLastError();
+}
+
+}  // namespace hbfb

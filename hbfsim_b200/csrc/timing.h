@@ -63,4 +63,12 @@ cudaError_t launch_decode(const DecodeParams& dp, const u64* address,
                           const u32* bytes, const u8* op, u64 n, void* out,
                           cudaStream_t stream, const LaunchHooks& hooks = {});
 
+// Hybrid sampler bits of n accesses (1 = the hybrid model would send the
+// access to the reference media model); `seq` is the device-side running
+// count of timed accesses, `counts` scratch of max_ctas words.
+cudaError_t launch_sample(const DecodeParams& dp, const u64* address, const u32* bytes,
+                          const u8* op, u64 n, u8* sample, u32 warmup, u64 threshold,
+                          u64* seq, u64* counts, u32 max_ctas, cudaStream_t stream,
+                          const LaunchHooks& hooks = {});
+
 }  // namespace hbfb

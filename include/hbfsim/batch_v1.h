@@ -174,6 +174,20 @@ typedef struct hbfsim_decoded_v1 {
     uint32_t plane;
 } hbfsim_decoded_v1;
 
+/* Hybrid sampler bits (reference hybrid_reference_sample,
+ * src/cuda_runtime/device/hbf_device.cuh:738-744, as resolve_fast_or_hybrid
+ * applies it, hbf_device.cu:779-788): for each access the timing model would
+ * serve (status 1), sample[i] = 1 when the hybrid model would send it to the
+ * reference media model -- its sequence number is below the profile's
+ * reference_warmup_requests, or the splitmix64 mix of
+ * (sequence ^ media_address ^ range_id << 32 ^ operation) is at most
+ * reference_sample_rate * UINT64_MAX; 0 for every other access.  Sequence
+ * numbers are the context's running count of such accesses in batch order,
+ * from 0 at context creation.  Device pointers; asynchronous on `stream`. */
+int hbfsim_sample_batch_v1(hbfsim_context* context, const uint64_t* address,
+                           const uint32_t* bytes, const uint8_t* operation,
+                           uint64_t count, uint8_t* sample, void* stream);
+
 int hbfsim_decode_batch_v1(hbfsim_context* context, const uint64_t* address,
                            const uint32_t* bytes, const uint8_t* operation,
                            uint64_t count, hbfsim_decoded_v1* out,

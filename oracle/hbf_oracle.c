@@ -102,6 +102,12 @@ static uint64_t or_fast_hash(uint64_t value)
     return value ^ (value >> 31);
 }
 
+uint64_t or_sample_threshold(double rate)
+{
+    if (rate >= 1.0) return UINT64_MAX;
+    return (uint64_t)(rate * (long double)UINT64_MAX);
+}
+
 int or_hybrid_reference_sample(uint64_t sequence, uint32_t warmup,
                                uint64_t threshold, uint64_t key)
 {

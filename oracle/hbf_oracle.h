@@ -106,6 +106,11 @@ int or_range_overlaps(const or_range* r, uint64_t address, uint32_t bytes);
 int or_media_descriptor(const or_range* r, uint64_t address, uint32_t bytes,
                         uint32_t op, uint64_t* logical_address,
                         uint32_t* media_bytes);
+/* Sampling threshold from a profile's reference_sample_rate
+ * (src/cuda_runtime/context.cpp:975-981): UINT64_MAX for rate >= 1, else
+ * rate * (long double) UINT64_MAX truncated. */
+uint64_t or_sample_threshold(double rate);
+
 int or_hybrid_reference_sample(uint64_t sequence, uint32_t warmup,
                                uint64_t threshold, uint64_t key);
 

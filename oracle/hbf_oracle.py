@@ -84,6 +84,8 @@ def _load() -> ctypes.CDLL:
     lib.or_range_overlaps.argtypes = [p, u64, u32]
     lib.or_media_descriptor.restype = ctypes.c_int
     lib.or_media_descriptor.argtypes = [p, u64, u32, u32, p, p]
+    lib.or_sample_threshold.restype = u64
+    lib.or_sample_threshold.argtypes = [ctypes.c_double]
     lib.or_hybrid_reference_sample.restype = ctypes.c_int
     lib.or_hybrid_reference_sample.argtypes = [u64, u32, u64, u64]
     lib.or_decode_batch.restype = None

@@ -272,3 +272,34 @@ def test_kernel_variants(tmp, dies, stacks):
     ora = OracleRun(s)
     assert_same(gpu_run(ctx, arrays), ora.run(*arrays, threads=4), f"D={dies} S={stacks}")
     assert np.array_equal(ctx.get_state(), ora.state)
+
+
+def test_hybrid_sampler_bits(tmp):
+    """A7: the sampler bit of every timed access, numbered across batches,
+    against the reference predicate (hbf_device.cuh:738-744) restated in the
+    oracle and applied in batch order."""
+    import torch
+    p = wl.c0_profile()
+    p["reference_sample_rate"] = 0.3
+    p["reference_warmup_requests"] = 700
+    s = Setup(profile=p, model=3, stacks=2, stripe=4096)
+    s.ranges = [(wl.RANGE_BASE, 8 << 30, 1, 3), (wl.RANGE_BASE + (16 << 30), 4 << 30, 1, 1)]
+    ctx = make_context(s, tmp)
+    oracle = OracleRun(s)
+    thr = ho.LIB.or_sample_threshold(0.3)
+    seq = 0
+    for k, n in enumerate((5000, 12345)):
+        arrays = wl.c0_trace(n, seed=40 + k, range_length=24 << 30)
+        dev = to_device(arrays)
+        got = ctx.sample(dev[0], dev[1], dev[2]).cpu().numpy()
+        torch.cuda.synchronize()
+        dec = ho.decode(oracle.ranges, oracle.count, oracle.geometry, *arrays[:3])
+        want = np.zeros(n, np.uint8)
+        for i in np.flatnonzero(dec["status"] == 1):
+            rid = oracle.ranges[int(dec["range_index"][i])].range_id
+            key = int(dec["media_address"][i]) ^ (rid << 32) ^ int(arrays[2][i])
+            want[i] = ho.LIB.or_hybrid_reference_sample(seq, 700, thr, key)
+            seq += 1
+        assert np.array_equal(got, want), f"batch {k}"
+        assert 0 < want.sum() < (dec["status"] == 1).sum()
+    ctx.close()
