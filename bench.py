@@ -114,18 +114,8 @@ class ClockSampler:
 def remap_to_shard(address, rank: int, world: int, range_base: int):
     """Place a 64-channel trace on the channels g % world == rank of a
     64*world-channel geometry, preserving (local channel, die, plane)."""
-    import torch
-    if world == 1:
-        return address
-    channels = 16 * STACKS_PER_RANK
-    inside = (address >= range_base) & (address < range_base + (60 << 30))
-    off = address - range_base
-    u = off // STRIPE
-    w = off % STRIPE
-    g0 = u % channels
-    rest = u // channels
-    u2 = rest * (channels * world) + g0 * world + rank
-    return torch.where(inside, range_base + u2 * STRIPE + w, address)
+    from hbfsim_b200.sharding import remap_to_shard as remap
+    return remap(address, rank, world, range_base, 60 << 30, 16 * STACKS_PER_RANK, STRIPE)
 
 
 def make_trace(device, rank: int, world: int, seed: int = 0, decode_steps: int = 8):
