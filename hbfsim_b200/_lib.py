@@ -88,6 +88,12 @@ class DecodedV1(ctypes.Structure):
                 ("die", u32), ("plane", u32)]
 
 
+class CapacityBatchV1(ctypes.Structure):
+    _fields_ = [("struct_size", u32), ("version", u32), ("count", u64),
+                ("address", vp), ("bytes", vp), ("operation", vp), ("arrival_ns", vp),
+                ("hit", vp), ("victim_page", vp), ("victim_dirty", vp), ("status", vp)]
+
+
 class ThermalLayerV1(ctypes.Structure):
     _fields_ = [("thickness_m", dbl), ("cv_j_m3_k", dbl), ("k_xyz_w_m_k", dbl * 3)]
 
@@ -131,6 +137,9 @@ SIGNATURES = {
     "hbfsim_get_batch_stats_v1": (i32, [vp, ctypes.POINTER(BatchStatsV1)]),
     "hbfsim_decode_batch_v1": (i32, [vp, vp, vp, vp, u64, vp, vp]),
     "hbfsim_sample_batch_v1": (i32, [vp, vp, vp, vp, u64, vp, vp]),
+    "hbfsim_capacity_configure_v1": (i32, [vp, u64, u32]),
+    "hbfsim_submit_capacity_batch_v1": (i32, [vp, ctypes.POINTER(CapacityBatchV1), vp]),
+    "hbfsim_get_capacity_state_v1": (i32, [vp, vp, vp, u64, ctypes.POINTER(u64)]),
     "hbfsim_set_channel_factors_v1": (i32, [vp, vp, vp, vp]),
     "hbfsim_get_channel_factors_v1": (i32, [vp, vp, vp, vp]),
     "hbfsim_get_state_v1": (i32, [vp, vp, u64]),

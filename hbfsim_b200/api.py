@@ -199,6 +199,42 @@ class Context:
               "hbfsim_decode_batch_v1")
         return out
 
+    # ---- Capacity mode ----
+    def capacity_configure(self, frames: int, page_bytes: int = 4096) -> None:
+        check(self._lib.hbfsim_capacity_configure_v1(self.handle, frames, page_bytes),
+              "hbfsim_capacity_configure_v1")
+
+    def submit_capacity(self, address, nbytes, op, arrival=None, stream=None):
+        """Exact-LRU decisions for device tensors: (hit u8, victim page
+        int64 (-1 = none), victim dirty u8, status u8) device tensors."""
+        import torch
+        n = address.numel()
+        dev = address.device
+        hit = torch.empty(n, dtype=torch.uint8, device=dev)
+        victim = torch.empty(n, dtype=torch.int64, device=dev)
+        dirty = torch.empty(n, dtype=torch.uint8, device=dev)
+        status = torch.empty(n, dtype=torch.uint8, device=dev)
+        b = _lib.CapacityBatchV1(ctypes.sizeof(_lib.CapacityBatchV1), 1, n, _ptr(address),
+                                 _ptr(nbytes), _ptr(op), _ptr(arrival), _ptr(hit),
+                                 _ptr(victim), _ptr(dirty), _ptr(status))
+        check(self._lib.hbfsim_submit_capacity_batch_v1(
+            self.handle, ctypes.byref(b), ctypes.c_void_p(_stream_handle(stream))),
+            "hbfsim_submit_capacity_batch_v1")
+        return hit, victim, dirty, status
+
+    def capacity_state(self):
+        """(resident pages oldest first, their dirty bits) as numpy arrays."""
+        count = ctypes.c_uint64()
+        check(self._lib.hbfsim_get_capacity_state_v1(self.handle, None, None, 0,
+                                                     ctypes.byref(count)),
+              "hbfsim_get_capacity_state_v1")
+        pages = np.zeros(count.value, np.uint64)
+        dirty = np.zeros(count.value, np.uint8)
+        check(self._lib.hbfsim_get_capacity_state_v1(self.handle, _ptr(pages), _ptr(dirty),
+                                                     count.value, ctypes.byref(count)),
+              "hbfsim_get_capacity_state_v1")
+        return pages, dirty
+
     def sample(self, address, nbytes, op, stream=None):
         """Hybrid sampler bits of device tensors (uint8 device tensor; 1 =
         the hybrid model would send the access to the reference model)."""

@@ -1,0 +1,821 @@
+// capacity.cu -- Capacity mode: exact LRU over HBM frames, batch-parallel.
+//
+// Reference: CapacityPageService::resolve
+// (src/host_service/capacity_page_service.cpp:97-210) keeps pages of
+// CAPACITY ranges in HBM frames and, on a miss, reads the page from HBF after
+// programming a dirty victim (request_dispatcher.cpp:107-126); the exact-LRU
+// policy is the reference's offline LruCache
+// (adapters/vllm_capacity/placement_policy.py:68-93).  The reference runtime
+// decides one request at a time under a mutex.
+//
+// B200 design.  LRU decisions follow from reuse distances, so a whole batch
+// is decided at once.  The batch is prefixed with the resident list (oldest
+// first, as if those pages had just been accessed in that order), giving a
+// sequence S of m accesses.  Then, for access i with previous access p of
+// the same page (prev(i), found by a stable radix sort on the page):
+//
+//   hit(i)  <=>  p exists and  distinct pages in (p, i)  <  F   (F = frames)
+//   distinct pages in (p, i) = (i - p - 1) - #{u < i : prev(u) > p}
+//
+// and the count is one query on a wavelet matrix over prev(.) (each level a
+// stable one-bit partition: ballots and prefix counts).  A miss evicts when
+// F distinct pages are already resident.  Entry j leaves the cache exactly
+// when its page's next access is a miss (or never comes), and entries leave
+// in order of j: so the k-th evicting miss evicts the page of the k-th such
+// entry.  A victim is dirty when a write hit its page since the miss that
+// brought it in (segmented OR over the page-sorted order).  The new resident
+// list is the newest F last-occurrences of pages, oldest first.
+#include "context.h"
+
+#include <algorithm>
+#include <vector>
+
+namespace hbfb {
+
+constexpr u32 kNone = 0xffffffffu;
+
+struct CapacityState {
+    std::uint64_t frames = 0;        // F
+    std::uint32_t page_shift = 12;   // LRU page = 2^page_shift bytes
+    std::uint64_t resident = 0;      // entries in the resident list
+    std::uint64_t capacity_m = 0;    // scratch size (sequence entries)
+    // resident list, oldest first (device)
+    u32* res_page = nullptr;
+    u8* res_dirty = nullptr;
+    // sequence and scratch
+    u32 *key = nullptr, *w = nullptr, *bidx = nullptr;
+    u32 *sk = nullptr, *si = nullptr, *tk = nullptr, *ti = nullptr;
+    u32 *prev = nullptr, *next = nullptr, *cur = nullptr, *nxt = nullptr;
+    uint2* levels = nullptr;         // wavelet levels [32][m/32 + 1]
+    u32 *hit = nullptr, *a = nullptr, *b = nullptr, *c = nullptr, *d = nullptr;
+    u32* tile_sums = nullptr;
+    std::uint64_t tile_sums_words = 0;
+    u32* valid = nullptr;            // per batch access: 1 = capacity access
+    u32* status = nullptr;
+    u32* counts = nullptr;           // small device results
+    // counters (host)
+    std::uint64_t calls = 0, accesses = 0, hits = 0, misses = 0, evictions = 0,
+                  dirty_evictions = 0;
+};
+
+namespace {
+
+constexpr u32 kT = 256;          // threads per CTA
+constexpr u32 kItems = 8;        // elements per thread in scans
+constexpr u32 kTile = kT * kItems;
+
+template <typename T>
+cudaError_t grow(T** p, std::uint64_t n)
+{
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    return cudaMalloc(reinterpret_cast<void**>(p), sizeof(T) * (n ? n : 1));
+}
+
+__device__ __forceinline__ u32 lane() { return threadIdx.x & 31u; }
+
+// ---------------------------------------------------------------- scans
+struct AddOp {
+    static __device__ __forceinline__ u32 f(u32 a, u32 b) { return a + b; }
+    static constexpr u32 id = 0;
+};
+struct MaxOp {
+    static __device__ __forceinline__ u32 f(u32 a, u32 b) { return a > b ? a : b; }
+    static constexpr u32 id = 0;
+};
+
+// Block-wide exclusive scan of one value per thread; returns the exclusive
+// prefix and writes the block total to *total (all threads).
+template <class Op>
+__device__ __forceinline__ u32 block_scan(u32 v, u32* total)
+{
+    __shared__ u32 warp_tot[kT / 32];
+    u32 incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const u32 y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane() >= static_cast<u32>(o)) incl = Op::f(incl, y);
+    }
+    const u32 w = threadIdx.x >> 5;
+    if (lane() == 31) warp_tot[w] = incl;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        u32 x = threadIdx.x < kT / 32 ? warp_tot[threadIdx.x] : Op::id;
+        u32 xi = x;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const u32 y = __shfl_up_sync(0xffffffffu, xi, o);
+            if (lane() >= static_cast<u32>(o)) xi = Op::f(xi, y);
+        }
+        if (threadIdx.x < kT / 32) warp_tot[threadIdx.x] = xi;  // inclusive
+    }
+    __syncthreads();
+    const u32 before = w ? warp_tot[w - 1] : Op::id;
+    const u32 excl_in_warp = __shfl_up_sync(0xffffffffu, incl, 1);
+    const u32 excl = lane() ? Op::f(before, excl_in_warp) : before;
+    *total = warp_tot[kT / 32 - 1];
+    __syncthreads();
+    return excl;
+}
+
+// Scan of one tile of kTile elements per CTA; tile totals to `sums`.
+template <class Op>
+__global__ void __launch_bounds__(kT) scan_tile_kernel(const u32* in, u32* out, u64 n, u32* sums,
+                                                       int inclusive)
+{
+    const u64 base = static_cast<u64>(blockIdx.x) * kTile + threadIdx.x * kItems;
+    u32 v[kItems];
+    u32 run = Op::id;
+#pragma unroll
+    for (u32 k = 0; k < kItems; ++k) {
+        v[k] = base + k < n ? in[base + k] : Op::id;
+        run = Op::f(run, v[k]);
+    }
+    u32 total;
+    u32 pre = block_scan<Op>(run, &total);
+#pragma unroll
+    for (u32 k = 0; k < kItems; ++k) {
+        const u32 x = v[k];
+        if (base + k < n) out[base + k] = inclusive ? Op::f(pre, x) : pre;
+        pre = Op::f(pre, x);
+    }
+    if (threadIdx.x == 0) sums[blockIdx.x] = total;
+}
+
+template <class Op>
+__global__ void __launch_bounds__(kT) scan_fix_kernel(u32* out, u64 n, const u32* offsets)
+{
+    const u64 base = static_cast<u64>(blockIdx.x) * kTile;
+    const u32 off = offsets[blockIdx.x];
+    for (u32 k = threadIdx.x; k < kTile; k += kT)
+        if (base + k < n) out[base + k] = Op::f(off, out[base + k]);
+}
+
+// Device-wide scan (exclusive or inclusive; in place allowed), recursive
+// over the tile sums.  `scratch` holds 2 words per tile per level.
+template <class Op>
+cudaError_t scan(const u32* in, u32* out, u64 n, bool inclusive, u32* scratch, cudaStream_t s)
+{
+    if (n == 0) return cudaSuccess;
+    const u64 tiles = (n + kTile - 1) / kTile;
+    u32* sums = scratch;
+    scan_tile_kernel<Op><<<static_cast<unsigned>(tiles), kT, 0, s>>>(in, out, n, sums,
+                                                                      inclusive ? 1 : 0);
+    if (tiles == 1) return cudaGetLastError();
+    // exclusive scan of the tile sums, then add them back
+    u32* sums_scanned = scratch + tiles;
+    const cudaError_t e = scan<Op>(sums, sums_scanned, tiles, false, scratch + 2 * tiles, s);
+    if (e != cudaSuccess) return e;
+    scan_fix_kernel<Op><<<static_cast<unsigned>(tiles), kT, 0, s>>>(out, n, sums_scanned);
+    return cudaGetLastError();
+}
+
+__global__ void total_kernel(const u32* excl_scan, const u32* in, u64 n, u32* total)
+{
+    if (threadIdx.x == 0 && blockIdx.x == 0) *total = n ? excl_scan[n - 1] + in[n - 1] : 0u;
+}
+
+// ---------------------------------------------------------------- classify
+__device__ __forceinline__ u32 find_range(const DevRange* r, u32 count, u64 a)
+{
+    u32 first = 0, last = count;
+    while (first < last) {
+        const u32 mid = first + (last - first) / 2;
+        if (r[mid].base <= a) first = mid + 1;
+        else last = mid;
+    }
+    return first == 0 ? count : first - 1;
+}
+
+// One access of a capacity batch: status, and the LRU page of a capacity
+// access (range lookup and checks as access_supported, hbf_device.cuh:843-862,
+// on CAPACITY ranges; the access must stay inside one LRU page).
+__global__ void cap_classify_kernel(const DevRange* ranges, u32 count, const u64* address,
+                                    const u32* bytes, const u8* op, u64 n, u32 shift, u32* page,
+                                    u32* valid, u32* status)
+{
+    const u64 i = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const u64 a = address[i];
+    const u32 b = bytes[i], o = op[i];
+    u32 st = kUnsupported, pg = 0;
+    if (b != 0) {
+        const u32 idx = find_range(ranges, count, a);
+        if (idx == count || a - ranges[idx].base >= ranges[idx].length) {
+            const u32 succ = idx == count ? 0u : idx + 1u;
+            bool overlap = false;
+            if (succ < count) {
+                const DevRange& r = ranges[succ];
+                overlap = r.length != 0 && r.base <= ~u64{0} - r.length &&
+                          a <= ~u64{0} - b && a < r.base + r.length && r.base < a + b;
+            }
+            st = overlap ? kUnsupported : kBypass;
+        } else {
+            const DevRange& r = ranges[idx];
+            const u64 off = a - r.base;
+            if (r.mode == 2 && r.ok && o <= 1 && b <= ~u64{0} - a && a + b <= r.end &&
+                (r.permissions & (1u << o)) && (off >> shift) == ((off + b - 1) >> shift)) {
+                st = kModeled;
+                pg = static_cast<u32>((r.file_offset + off) >> shift);
+            }
+        }
+    }
+    page[i] = pg;
+    valid[i] = st == kModeled ? 1u : 0u;
+    status[i] = st;
+}
+
+// Sequence S: the resident list, then the batch's capacity accesses.
+__global__ void cap_build_kernel(const u32* res_page, const u8* res_dirty, u64 resident,
+                                 const u32* page, const u8* op, const u32* valid,
+                                 const u32* pos, u64 n, u32* key, u32* w, u32* bidx)
+{
+    const u64 i = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < resident) {
+        key[i] = res_page[i];
+        w[i] = res_dirty[i];
+        bidx[i] = kNone;
+    }
+    if (i < n && valid[i]) {
+        const u64 j = resident + pos[i];
+        key[j] = page[i];
+        w[j] = op[i] == 1 ? 1u : 0u;
+        bidx[j] = static_cast<u32>(i);
+    }
+}
+
+// ---------------------------------------------------------------- radix sort
+// Stable LSD radix sort of (key, index) by 8-bit digits; one CTA per tile of
+// kTile elements.  Histogram layout: digit-major, tile-minor.
+__global__ void __launch_bounds__(kT) radix_hist_kernel(const u32* key, u64 m, u32 shift,
+                                                        u32* hist, u32 tiles)
+{
+    __shared__ u32 h[256];
+    h[threadIdx.x] = 0;
+    __syncthreads();
+    const u64 base = static_cast<u64>(blockIdx.x) * kTile;
+    for (u32 k = threadIdx.x; k < kTile; k += kT)
+        if (base + k < m) atomicAdd(&h[(key[base + k] >> shift) & 255u], 1u);
+    __syncthreads();
+    hist[static_cast<u64>(threadIdx.x) * tiles + blockIdx.x] = h[threadIdx.x];
+}
+
+__global__ void __launch_bounds__(kT) radix_scatter_kernel(const u32* key, const u32* val,
+                                                           u64 m, u32 shift, const u32* offsets,
+                                                           u32 tiles, u32* key_out,
+                                                           u32* val_out)
+{
+    __shared__ u32 running[256];
+    __shared__ u32 warp_count[kT / 32][256];
+    running[threadIdx.x] = offsets[static_cast<u64>(threadIdx.x) * tiles + blockIdx.x];
+    const u32 wid = threadIdx.x >> 5;
+    const u64 base = static_cast<u64>(blockIdx.x) * kTile;
+    for (u32 round = 0; round < kItems; ++round) {
+        for (u32 k = threadIdx.x; k < (kT / 32) * 256; k += kT) (&warp_count[0][0])[k] = 0;
+        __syncthreads();
+        const u64 i = base + static_cast<u64>(round) * kT + threadIdx.x;
+        const bool on = i < m;
+        const u32 kv = on ? key[i] : 0u;
+        const u32 d = on ? (kv >> shift) & 255u : 256u;
+        const u32 peers = __match_any_sync(0xffffffffu, d);
+        const u32 rank = __popc(peers & ((1u << lane()) - 1u));
+        if (on && rank == 0) warp_count[wid][d] = __popc(peers);
+        __syncthreads();
+        if (on) {
+            u32 pos = running[d] + rank;
+            for (u32 w2 = 0; w2 < wid; ++w2) pos += warp_count[w2][d];
+            key_out[pos] = kv;
+            val_out[pos] = val[i];
+        }
+        __syncthreads();
+        u32 add = 0;
+        for (u32 w2 = 0; w2 < kT / 32; ++w2) add += warp_count[w2][threadIdx.x];
+        running[threadIdx.x] += add;
+        __syncthreads();
+    }
+}
+
+__global__ void iota_kernel(u32* v, u64 m)
+{
+    const u64 i = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < m) v[i] = static_cast<u32>(i);
+}
+
+__global__ void fill_kernel(u32* v, u64 m, u32 x)
+{
+    const u64 i = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < m) v[i] = x;
+}
+
+// prev / next links from the page-sorted order
+__global__ void link_kernel(const u32* sk, const u32* si, u64 m, u32* prev, u32* next)
+{
+    const u64 k = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (k + 1 >= m) return;
+    if (sk[k] == sk[k + 1]) {
+        next[si[k]] = si[k + 1];
+        prev[si[k + 1]] = si[k];
+    }
+}
+
+// ---------------------------------------------------------------- wavelet
+// Values v = prev + 1 (0 = no previous access).  Level l partitions the
+// current order stably by bit l (zeros first) and stores, per 32 positions,
+// the bits and the number of ones before them.
+__global__ void value_kernel(const u32* prev, u64 m, u32* v)
+{
+    const u64 i = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < m) v[i] = prev[i] == kNone ? 0u : prev[i] + 1u;
+}
+
+__global__ void __launch_bounds__(kT) wm_zero_count_kernel(const u32* v, u64 m, u32 bit,
+                                                           u32* zeros)
+{
+    const u64 base = static_cast<u64>(blockIdx.x) * kTile;
+    u32 z = 0;
+    for (u32 k = threadIdx.x; k < kTile; k += kT)
+        if (base + k < m) z += ((v[base + k] >> bit) & 1u) == 0;
+    u32 total;
+    block_scan<AddOp>(z, &total);
+    if (threadIdx.x == 0) zeros[blockIdx.x] = total;
+}
+
+__global__ void __launch_bounds__(kT) wm_split_kernel(const u32* v, u64 m, u32 bit,
+                                                      const u32* zeros_before,
+                                                      const u32* total_zeros, u32* out,
+                                                      uint2* level)
+{
+    __shared__ u32 warp_ones[kT / 32];
+    const u64 base = static_cast<u64>(blockIdx.x) * kTile;
+    const u32 Z = *total_zeros;
+    u32 ob = static_cast<u32>(base) - zeros_before[blockIdx.x];  // ones before i
+    const u32 wid = threadIdx.x >> 5;
+    for (u32 round = 0; round < kItems; ++round) {
+        const u64 i = base + static_cast<u64>(round) * kT + threadIdx.x;
+        const bool on = i < m;
+        const u32 x = on ? v[i] : 0u;
+        const u32 b = (x >> bit) & 1u;
+        const u32 ones = __ballot_sync(0xffffffffu, on && b);
+        if (lane() == 0) warp_ones[wid] = __popc(ones);
+        __syncthreads();
+        u32 before_warp = 0, round_ones = 0;
+        for (u32 w2 = 0; w2 < kT / 32; ++w2) {
+            before_warp += w2 < wid ? warp_ones[w2] : 0u;
+            round_ones += warp_ones[w2];
+        }
+        const u32 word_rank = ob + before_warp;  // ones before this warp's 32 positions
+        const u32 o_rank = word_rank + __popc(ones & ((1u << lane()) - 1u));
+        if (on) {
+            if (b) out[Z + o_rank] = x;
+            else out[static_cast<u32>(i) - o_rank] = x;
+            if (lane() == 0) level[i >> 5] = make_uint2(ones, word_rank);
+        }
+        ob += round_ones;
+        __syncthreads();
+    }
+}
+
+// rank sentinel at position m when m is a multiple of 32
+__global__ void wm_sentinel_kernel(u64 m, const u32* total_zeros, uint2* level)
+{
+    if ((m & 31u) == 0) level[m >> 5] = make_uint2(0u, static_cast<u32>(m) - *total_zeros);
+}
+
+__device__ __forceinline__ u32 rank1(const uint2* level, u32 x)
+{
+    const uint2 wv = level[x >> 5];
+    return wv.y + __popc(wv.x & ((1u << (x & 31u)) - 1u));
+}
+
+// #{u < hi : value(u) > v} on the wavelet matrix (levels bits-1 .. 0)
+__device__ __forceinline__ u32 count_greater(const uint2* levels, u64 words, u32 bits,
+                                             const u32* zeros, u32 v, u32 hi)
+{
+    u32 lo = 0, cnt = 0;
+    for (int l = static_cast<int>(bits) - 1; l >= 0; --l) {
+        const uint2* L = levels + static_cast<u64>(l) * words;
+        const u32 r_lo = rank1(L, lo), r_hi = rank1(L, hi);
+        if (((v >> l) & 1u) == 0) {
+            cnt += r_hi - r_lo;
+            lo -= r_lo;
+            hi -= r_hi;
+        } else {
+            lo = zeros[l] + r_lo;
+            hi = zeros[l] + r_hi;
+        }
+    }
+    return cnt;
+}
+
+// hit(i) and first-occurrence flags
+__global__ void hit_kernel(const u32* prev, u64 m, u64 resident, u64 frames,
+                           const uint2* levels, u64 words, u32 bits, const u32* zeros,
+                           u32* hit, u32* first)
+{
+    const u64 i = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= m) return;
+    const u32 p = prev[i];
+    first[i] = p == kNone ? 1u : 0u;
+    u32 h = 0;
+    if (i >= resident && p != kNone) {
+        const u64 w = i - p - 1;  // accesses strictly between
+        if (w < frames) {
+            h = 1;
+        } else {
+            const u32 r = count_greater(levels, words, bits, zeros, p + 1, static_cast<u32>(i));
+            h = w - r < frames ? 1u : 0u;  // distinct pages in between
+        }
+    }
+    hit[i] = h;
+}
+
+__global__ void evict_kernel(const u32* hit, const u32* distinct_before, u64 m, u64 resident,
+                             u64 frames, u32* evict)
+{
+    const u64 i = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= m) return;
+    evict[i] = i >= resident && frames > 0 && !hit[i] && distinct_before[i] >= frames ? 1u : 0u;
+}
+
+// entry j leaves the cache (in order of j) when its page's next access misses
+__global__ void leave_kernel(const u32* next, const u32* hit, u64 m, u32* leave)
+{
+    const u64 j = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (j >= m) return;
+    const u32 nx = next[j];
+    leave[j] = nx == kNone || !hit[nx] ? 1u : 0u;
+}
+
+__global__ void compact_kernel(const u32* flag, const u32* pos, u64 m, u32* out)
+{
+    const u64 j = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (j < m && flag[j]) out[pos[j]] = static_cast<u32>(j);
+}
+
+// residency starts (misses) and writes, as position+1 in page-sorted order
+__global__ void dirty_marks_kernel(const u32* sk, const u32* si, const u32* hit, const u32* w,
+                                   u64 m, u32* start_mark, u32* write_mark)
+{
+    const u64 k = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (k >= m) return;
+    const u32 j = si[k];
+    const bool start = k == 0 || sk[k - 1] != sk[k] || !hit[j];
+    start_mark[k] = start ? static_cast<u32>(k) + 1u : 0u;
+    write_mark[k] = w[j] ? static_cast<u32>(k) + 1u : 0u;
+}
+
+__global__ void dirty_kernel(const u32* si, const u32* last_start, const u32* last_write, u64 m,
+                             u32* dirty)
+{
+    const u64 k = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (k < m) dirty[si[k]] = last_write[k] >= last_start[k] ? 1u : 0u;
+}
+
+struct OutArgs {
+    const u32* key;
+    const u32* bidx;
+    const u32* hit;
+    const u32* evict;
+    const u32* evict_rank;
+    const u32* leave_list;
+    const u32* dirty;
+    const u32* leave_total;
+    u64 m;
+    u8* out_hit;
+    u64* out_victim;
+    u8* out_dirty;
+    u32* counters;  // [0] hits, [1] dirty evictions
+};
+
+__global__ void output_kernel(OutArgs a)
+{
+    const u64 i = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= a.m) return;
+    const u32 b = a.bidx[i];
+    if (b == kNone) return;
+    u64 victim = ~u64{0};
+    u32 vd = 0;
+    if (a.evict[i] && a.evict_rank[i] < *a.leave_total) {
+        const u32 j = a.leave_list[a.evict_rank[i]];
+        victim = a.key[j];
+        vd = a.dirty[j];
+        if (vd) atomicAdd(&a.counters[1], 1u);
+    }
+    if (a.hit[i]) atomicAdd(&a.counters[0], 1u);
+    if (a.out_hit) a.out_hit[b] = static_cast<u8>(a.hit[i]);
+    if (a.out_victim) a.out_victim[b] = victim;
+    if (a.out_dirty) a.out_dirty[b] = static_cast<u8>(vd);
+}
+
+__global__ void status_kernel(const u32* st, u64 n, u8* out)
+{
+    const u64 i = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = static_cast<u8>(st[i]);
+}
+
+// the last `keep` of the L last occurrences, oldest first
+__global__ void resident_kernel(const u32* next, const u32* live_pos, const u32* key,
+                                const u32* dirty, u64 m, u32 live_total, u32 keep,
+                                u32* res_page, u8* res_dirty)
+{
+    const u64 j = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (j >= m || next[j] != kNone) return;
+    const u32 r = live_pos[j];
+    if (r + keep >= live_total) {
+        const u32 slot = r - (live_total - keep);
+        res_page[slot] = key[j];
+        res_dirty[slot] = static_cast<u8>(dirty[j]);
+    }
+}
+
+__global__ void live_kernel(const u32* next, u64 m, u32* live)
+{
+    const u64 j = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (j < m) live[j] = next[j] == kNone ? 1u : 0u;
+}
+
+inline unsigned blocks(u64 n) { return static_cast<unsigned>((n + kT - 1) / kT); }
+
+}  // namespace
+
+void capacity_destroy(CapacityState* c)
+{
+    if (!c) return;
+    void* ptrs[] = {c->res_page, c->res_dirty, c->key, c->w, c->bidx, c->sk, c->si, c->tk,
+                    c->ti, c->prev, c->next, c->cur, c->nxt, c->levels, c->hit, c->a,
+                    c->b, c->c, c->d, c->tile_sums, c->valid, c->status, c->counts};
+    for (void* p : ptrs)
+        if (p) cudaFree(p);
+    delete c;
+}
+
+}  // namespace hbfb
+
+using namespace hbfb;
+
+namespace {
+
+constexpr std::uint32_t kCapCounts = 64;  // device result words
+
+struct CGuard {
+    explicit CGuard(hbfsim_context* c) : lock(c->mu) { cudaSetDevice(c->device); }
+    std::lock_guard<std::mutex> lock;
+};
+
+std::uint32_t bits_for(std::uint64_t v)
+{
+    std::uint32_t b = 1;
+    while (b < 32 && (std::uint64_t{1} << b) <= v) ++b;
+    return b;
+}
+
+int ensure_scratch(CapacityState* s, std::uint64_t need)
+{
+    if (need <= s->capacity_m) return HBFSIM_OK;
+    const std::uint64_t m = std::max<std::uint64_t>(need, 1 << 16);
+    const std::uint64_t words = m / 32 + 2;
+    const std::uint64_t tiles = (m + kTile - 1) / kTile;
+    std::uint64_t sums = 0, t = tiles;
+    while (t > 1) {
+        sums += 2 * t + 2;
+        t = (t + kTile - 1) / kTile;
+    }
+    sums += 8 + 256 * tiles;  // radix histograms
+    if (grow(&s->key, m) || grow(&s->w, m) || grow(&s->bidx, m) || grow(&s->sk, m) ||
+        grow(&s->si, m) || grow(&s->tk, m) || grow(&s->ti, m) || grow(&s->prev, m) ||
+        grow(&s->next, m) || grow(&s->cur, m) || grow(&s->nxt, m) ||
+        grow(&s->levels, 32 * words) || grow(&s->hit, m) || grow(&s->a, m) ||
+        grow(&s->b, m) || grow(&s->c, m) || grow(&s->d, m) || grow(&s->valid, m) ||
+        grow(&s->status, m) || grow(&s->tile_sums, 2 * (256 * tiles + sums)))
+        return HBFSIM_CUDA_ERROR;
+    s->tile_sums_words = 2 * (256 * tiles + sums);
+    s->capacity_m = m;
+    return HBFSIM_OK;
+}
+
+// exclusive (or inclusive) add-scan with the total written to *total_dev
+cudaError_t scan_add(CapacityState* s, const u32* in, u32* out, u64 n, bool inclusive,
+                     u32* total_dev, cudaStream_t st)
+{
+    cudaError_t e = scan<AddOp>(in, out, n, inclusive, s->tile_sums, st);
+    if (e != cudaSuccess || !total_dev) return e;
+    if (inclusive) {
+        if (n) cudaMemcpyAsync(total_dev, out + n - 1, 4, cudaMemcpyDeviceToDevice, st);
+        return cudaGetLastError();
+    }
+    total_kernel<<<1, 32, 0, st>>>(out, in, n, total_dev);
+    return cudaGetLastError();
+}
+
+int run_capacity(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStream_t st)
+{
+    CapacityState* s = ctx->capacity;
+    const std::uint64_t n = b->count;
+    const std::uint64_t resident = s->resident;
+    if (ensure_scratch(s, resident + n) != HBFSIM_OK) return HBFSIM_CUDA_ERROR;
+    u32* cnt = s->counts;  // [0] valid total, [1] hits, [2] dirty ev, [3] Z, [4] distinct,
+                           // [5] evictions, [6] leave total, [7] live total, [8..] zeros/level
+    cudaMemsetAsync(cnt, 0, 4 * kCapCounts, st);
+    // 1. classify the batch; capacity accesses get sequence positions
+    cap_classify_kernel<<<blocks(n), kT, 0, st>>>(ctx->d_ranges,
+                                                   static_cast<u32>(ctx->ranges.size()),
+                                                   b->address, b->bytes, b->operation, n,
+                                                   s->page_shift, s->ti, s->valid, s->status);
+    scan_add(s, s->valid, s->a, n, false, cnt + 0, st);
+    std::uint32_t valid_total = 0;
+    cudaMemcpyAsync(&valid_total, cnt + 0, 4, cudaMemcpyDeviceToHost, st);
+    if (cudaStreamSynchronize(st) != cudaSuccess) return HBFSIM_CUDA_ERROR;
+    const std::uint64_t m = resident + valid_total;
+    if (b->status) status_kernel<<<blocks(n), kT, 0, st>>>(s->status, n, b->status);
+    // 2. the sequence: resident list, then the capacity accesses
+    cap_build_kernel<<<blocks(std::max(n, resident)), kT, 0, st>>>(
+        s->res_page, s->res_dirty, resident, s->ti, b->operation, s->valid, s->a, n, s->key,
+        s->w, s->bidx);
+    if (m == 0) {
+        if (b->hit) cudaMemsetAsync(b->hit, 0, n, st);
+        if (b->victim_page) cudaMemsetAsync(b->victim_page, 0xff, 8 * n, st);
+        if (b->victim_dirty) cudaMemsetAsync(b->victim_dirty, 0, n, st);
+        return cudaStreamSynchronize(st) == cudaSuccess ? HBFSIM_OK : HBFSIM_CUDA_ERROR;
+    }
+    // 3. stable radix sort of (page, position)
+    const std::uint64_t max_page = ctx->profile.capacity_bytes >> s->page_shift;
+    const std::uint32_t key_bits = bits_for(max_page);
+    const u32 tiles = static_cast<u32>((m + kTile - 1) / kTile);
+    cudaMemcpyAsync(s->sk, s->key, 4 * m, cudaMemcpyDeviceToDevice, st);
+    iota_kernel<<<blocks(m), kT, 0, st>>>(s->si, m);
+    u32 *ik = s->sk, *iv = s->si, *ok = s->tk, *ov = s->ti;
+    u32* hist = s->tile_sums + s->tile_sums_words / 2;
+    for (std::uint32_t shift = 0; shift < key_bits; shift += 8) {
+        radix_hist_kernel<<<tiles, kT, 0, st>>>(ik, m, shift, hist, tiles);
+        scan<AddOp>(hist, hist, 256ull * tiles, false, s->tile_sums, st);
+        radix_scatter_kernel<<<tiles, kT, 0, st>>>(ik, iv, m, shift, hist, tiles, ok, ov);
+        std::swap(ik, ok);
+        std::swap(iv, ov);
+    }
+    // 4. previous / next access of the same page
+    fill_kernel<<<blocks(m), kT, 0, st>>>(s->prev, m, kNone);
+    fill_kernel<<<blocks(m), kT, 0, st>>>(s->next, m, kNone);
+    link_kernel<<<blocks(m), kT, 0, st>>>(ik, iv, m, s->prev, s->next);
+    // 5. wavelet matrix over prev + 1
+    const std::uint32_t vbits = bits_for(m);
+    const std::uint64_t words = m / 32 + 2;
+    value_kernel<<<blocks(m), kT, 0, st>>>(s->prev, m, s->cur);
+    u32* zeros_dev = cnt + 16;  // per level
+    u32 *wc = s->cur, *wn = s->nxt;
+    for (int l = static_cast<int>(vbits) - 1; l >= 0; --l) {
+        wm_zero_count_kernel<<<tiles, kT, 0, st>>>(wc, m, static_cast<u32>(l), s->d);
+        scan_add(s, s->d, s->c, tiles, false, zeros_dev + l, st);
+        uint2* level = s->levels + static_cast<std::uint64_t>(l) * words;
+        wm_split_kernel<<<tiles, kT, 0, st>>>(wc, m, static_cast<u32>(l), s->c, zeros_dev + l,
+                                              wn, level);
+        wm_sentinel_kernel<<<1, 1, 0, st>>>(m, zeros_dev + l, level);
+        std::swap(wc, wn);
+    }
+    // 6. hits, distinct pages before each access, evicting misses
+    hit_kernel<<<blocks(m), kT, 0, st>>>(s->prev, m, resident, s->frames, s->levels, words,
+                                         vbits, zeros_dev, s->hit, s->a);
+    scan_add(s, s->a, s->b, m, false, cnt + 4, st);            // distinct before i
+    evict_kernel<<<blocks(m), kT, 0, st>>>(s->hit, s->b, m, resident, s->frames, s->c);
+    scan_add(s, s->c, s->d, m, false, cnt + 5, st);            // eviction rank
+    // 7. entries that leave the cache, in order
+    leave_kernel<<<blocks(m), kT, 0, st>>>(s->next, s->hit, m, s->a);
+    scan_add(s, s->a, s->cur, m, false, cnt + 6, st);
+    compact_kernel<<<blocks(m), kT, 0, st>>>(s->a, s->cur, m, s->nxt);
+    // 8. dirty bits (page-sorted order; ik/iv hold the sorted pairs)
+    u32* start_mark = ok;   // the sort's other buffers are free now
+    u32* write_mark = ov;
+    dirty_marks_kernel<<<blocks(m), kT, 0, st>>>(ik, iv, s->hit, s->w, m, start_mark,
+                                                 write_mark);
+    scan<MaxOp>(start_mark, start_mark, m, true, s->tile_sums, st);
+    scan<MaxOp>(write_mark, write_mark, m, true, s->tile_sums, st);
+    dirty_kernel<<<blocks(m), kT, 0, st>>>(iv, start_mark, write_mark, m, s->b);
+    // 9. per-access outputs
+    OutArgs oa{};
+    oa.key = s->key;
+    oa.bidx = s->bidx;
+    oa.hit = s->hit;
+    oa.evict = s->c;
+    oa.evict_rank = s->d;
+    oa.leave_list = s->nxt;
+    oa.dirty = s->b;
+    oa.leave_total = cnt + 6;
+    oa.m = m;
+    oa.out_hit = b->hit;
+    oa.out_victim = b->victim_page;
+    oa.out_dirty = b->victim_dirty;
+    oa.counters = cnt + 1;
+    if (b->hit) cudaMemsetAsync(b->hit, 0, n, st);
+    if (b->victim_page) cudaMemsetAsync(b->victim_page, 0xff, 8 * n, st);
+    if (b->victim_dirty) cudaMemsetAsync(b->victim_dirty, 0, n, st);
+    output_kernel<<<blocks(m), kT, 0, st>>>(oa);
+    // 10. the new resident list
+    live_kernel<<<blocks(m), kT, 0, st>>>(s->next, m, s->a);
+    scan_add(s, s->a, s->cur, m, false, cnt + 7, st);
+    std::uint32_t host_cnt[kCapCounts];
+    cudaMemcpyAsync(host_cnt, cnt, 4 * kCapCounts, cudaMemcpyDeviceToHost, st);
+    if (cudaStreamSynchronize(st) != cudaSuccess) return HBFSIM_CUDA_ERROR;
+    const std::uint32_t live_total = host_cnt[7];
+    const std::uint32_t keep =
+        static_cast<std::uint32_t>(std::min<std::uint64_t>(live_total, s->frames));
+    resident_kernel<<<blocks(m), kT, 0, st>>>(s->next, s->cur, s->key, s->b, m, live_total,
+                                              keep, s->res_page, s->res_dirty);
+    if (cudaStreamSynchronize(st) != cudaSuccess) return HBFSIM_CUDA_ERROR;
+    s->resident = keep;
+    ++s->calls;
+    s->accesses += valid_total;
+    s->hits += host_cnt[1];
+    s->misses += valid_total - host_cnt[1];
+    s->evictions += host_cnt[5];
+    s->dirty_evictions += host_cnt[2];
+    return cudaGetLastError() == cudaSuccess ? HBFSIM_OK : HBFSIM_CUDA_ERROR;
+}
+
+}  // namespace
+
+extern "C" {
+
+int hbfsim_capacity_configure_v1(hbfsim_context* c, uint64_t frames, uint32_t page_bytes)
+{
+    if (!c) return HBFSIM_INVALID_ARGUMENT;
+    CGuard g(c);
+    if (page_bytes == 0) page_bytes = 4096;
+    if (page_bytes < 512 || (page_bytes & (page_bytes - 1)) != 0 ||
+        page_bytes > c->profile.page_bytes)
+        return HBFSIM_INVALID_ARGUMENT;
+    std::uint32_t shift = 0;
+    while ((1u << shift) < page_bytes) ++shift;
+    if ((c->profile.capacity_bytes >> shift) >= 0xffffffffull ||
+        frames >= 0x7fffffffull)
+        return HBFSIM_UNSUPPORTED;  // page ids and positions are 32-bit
+    if (cudaDeviceSynchronize() != cudaSuccess) return HBFSIM_CUDA_ERROR;
+    if (c->capacity) capacity_destroy(c->capacity);
+    auto* s = new CapacityState();
+    c->capacity = s;
+    s->frames = frames;
+    s->page_shift = shift;
+    if (grow(&s->res_page, frames) || grow(&s->res_dirty, frames) ||
+        grow(&s->counts, kCapCounts)) {
+        capacity_destroy(s);
+        c->capacity = nullptr;
+        return HBFSIM_CUDA_ERROR;
+    }
+    return HBFSIM_OK;
+}
+
+int hbfsim_submit_capacity_batch_v1(hbfsim_context* c, const hbfsim_capacity_batch_v1* b,
+                                    void* stream)
+{
+    if (!c || !b || b->struct_size != sizeof(hbfsim_capacity_batch_v1) ||
+        b->version != HBFSIM_CAPACITY_BATCH_V1_VERSION)
+        return HBFSIM_INVALID_ARGUMENT;
+    if (b->count && (!b->address || !b->bytes || !b->operation)) return HBFSIM_INVALID_ARGUMENT;
+    CGuard g(c);
+    if (!c->capacity) return HBFSIM_INVALID_ARGUMENT;
+    if (c->capacity->resident + b->count >= 0x7fffffffull) return HBFSIM_UNSUPPORTED;
+    if (b->count == 0) return HBFSIM_OK;
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    return run_capacity(c, b, s);
+}
+
+int hbfsim_get_capacity_state_v1(hbfsim_context* c, uint64_t* resident_pages,
+                                 uint8_t* resident_dirty, uint64_t count, uint64_t* resident)
+{
+    if (!c || !resident) return HBFSIM_INVALID_ARGUMENT;
+    CGuard g(c);
+    CapacityState* s = c->capacity;
+    if (!s) return HBFSIM_INVALID_ARGUMENT;
+    *resident = s->resident;
+    if (!resident_pages && !resident_dirty) return HBFSIM_OK;
+    if (count < s->resident) return HBFSIM_INVALID_ARGUMENT;
+    std::vector<std::uint32_t> pages(s->resident);
+    if (cudaDeviceSynchronize() != cudaSuccess ||
+        (s->resident && cudaMemcpy(pages.data(), s->res_page, 4 * s->resident,
+                                   cudaMemcpyDeviceToHost) != cudaSuccess) ||
+        (resident_dirty && s->resident &&
+         cudaMemcpy(resident_dirty, s->res_dirty, s->resident, cudaMemcpyDeviceToHost) !=
+             cudaSuccess))
+        return HBFSIM_CUDA_ERROR;
+    if (resident_pages)
+        for (std::uint64_t k = 0; k < s->resident; ++k) resident_pages[k] = pages[k];
+    return HBFSIM_OK;
+}
+
+}  // extern "C"
+
+namespace hbfb {
+void capacity_stats(const CapacityState* s, hbfsim_capacity_stats_v1* out)
+{
+    out->enabled = 1;
+    out->page_bytes = std::uint64_t{1} << s->page_shift;
+    out->logical_frame_count = s->frames;
+    out->service_resolve_calls = s->accesses;
+    out->service_resident_hits = s->hits;
+    out->service_misses = s->misses;
+    out->successful_backing_read_pages = s->misses;
+    out->successful_backing_read_bytes = s->misses << s->page_shift;
+    out->successful_resolve_evictions = s->evictions;
+    out->successful_d2h_readback_pages = s->dirty_evictions;
+    out->successful_d2h_readback_bytes = s->dirty_evictions << s->page_shift;
+    out->service_ready_results = s->accesses;
+}
+}  // namespace hbfb

@@ -559,7 +559,14 @@ int hbfsim_get_capacity_stats_v1(hbfsim_context* c, hbfsim_capacity_stats_v1* ou
     if (!c || !out || out->struct_size != sizeof(hbfsim_capacity_stats_v1) ||
         out->version != HBFSIM_CAPACITY_STATS_V1_VERSION)
         return HBFSIM_INVALID_ARGUMENT;
-    return HBFSIM_INVALID_ARGUMENT;  // context.cpp:2019-2022: no capacity service
+    Guard g(c);
+    if (!c->capacity) return HBFSIM_INVALID_ARGUMENT;  // context.cpp:2019-2022: no service
+    const std::uint32_t size = out->struct_size, version = out->version;
+    std::memset(out, 0, sizeof *out);
+    out->struct_size = size;
+    out->version = version;
+    capacity_stats(c->capacity, out);
+    return HBFSIM_OK;
 }
 
 int hbfsim_unregister(hbfsim_context* c, void* range_base)
@@ -585,6 +592,7 @@ void hbfsim_context_destroy(hbfsim_context* c)
     cudaSetDevice(c->device);
     cudaDeviceSynchronize();
     if (c->thermal) thermal_destroy(c->thermal);
+    if (c->capacity) capacity_destroy(c->capacity);
     free_geometry(c);
     dfree(c->d_ranges);
     dfree(c->d_error);

@@ -10,7 +10,8 @@
 #include <vector>
 
 namespace hbfb {
-struct ThermalState;  // thermal.cu
+struct ThermalState;   // thermal.cu
+struct CapacityState;  // capacity.cu
 }
 
 struct hbfsim_context {
@@ -83,6 +84,7 @@ struct hbfsim_context {
     std::uint64_t stage_capacity = 0;  // accesses per stage
 
     hbfb::ThermalState* thermal = nullptr;
+    hbfb::CapacityState* capacity = nullptr;  // Capacity-mode LRU (capacity.cu)
     bool track_activity = false;  // accumulate per-die activity without thermal
 
     // launch profiling (event pairs per kernel slot)
@@ -100,6 +102,8 @@ struct hbfsim_context {
 namespace hbfb {
 // thermal.cu
 void thermal_destroy(ThermalState* t);
+void capacity_destroy(CapacityState* c);
+void capacity_stats(const CapacityState* c, hbfsim_capacity_stats_v1* out);
 // Device arrays of the factors the epoch controller derived (refresh per
 // local channel, throttle permille and admit-after tick per stack).
 void thermal_factor_arrays(ThermalState* t, std::uint32_t** refresh, std::uint32_t** throttle,

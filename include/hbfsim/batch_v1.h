@@ -213,6 +213,46 @@ int hbfsim_set_state_v1(hbfsim_context* context, const uint64_t* host_words,
                         uint64_t words);
 uint64_t hbfsim_state_words_v1(hbfsim_context* context);
 
+/* ---- Capacity mode: exact LRU over HBM frames ----
+ * Replaces CapacityPageService::resolve
+ * (src/host_service/capacity_page_service.cpp:97-210) with the exact-LRU
+ * policy of adapters/vllm_capacity/placement_policy.py:68-93, decided for a
+ * whole batch at once.  Pages are LRU pages of page_bytes (default 4096,
+ * a power of two no larger than the profile page) in media order:
+ * page = (range file offset + offset in range) / page_bytes. */
+int hbfsim_capacity_configure_v1(hbfsim_context* context, uint64_t frames,
+                                 uint32_t page_bytes);
+
+#define HBFSIM_CAPACITY_BATCH_V1_VERSION 1u
+typedef struct hbfsim_capacity_batch_v1 {
+    uint32_t struct_size;
+    uint32_t version;
+    uint64_t count;
+    const uint64_t* address;     /* in CAPACITY ranges; one LRU page each   */
+    const uint32_t* bytes;
+    const uint8_t* operation;    /* 0 read, 1 write (dirties the page)      */
+    const uint64_t* arrival_ns;  /* reserved for the media-action timing    */
+    uint8_t* hit;                /* out: 1 = resident in HBM                 */
+    uint64_t* victim_page;       /* out: page evicted by this access,
+                                  *      UINT64_MAX if none                  */
+    uint8_t* victim_dirty;       /* out: 1 = the victim must be programmed   */
+    uint8_t* status;             /* out: 1 capacity access, 6 unsupported,
+                                  *      8 outside every range               */
+} hbfsim_capacity_batch_v1;
+
+/* Decides hit / victim / dirty for every access, in batch order, continuing
+ * from the resident list the previous batch left.  Device pointers (NULL
+ * outputs are skipped).  Synchronous: returns when the results are written. */
+int hbfsim_submit_capacity_batch_v1(hbfsim_context* context,
+                                    const hbfsim_capacity_batch_v1* batch,
+                                    void* stream);
+
+/* The resident list, oldest first (host copies; NULL arrays return only
+ * *resident). */
+int hbfsim_get_capacity_state_v1(hbfsim_context* context, uint64_t* resident_pages,
+                                 uint8_t* resident_dirty, uint64_t count,
+                                 uint64_t* resident);
+
 /* ---- eq3 thermal grid and epoch controller ---- */
 #define HBFSIM_THERMAL_MAX_LAYERS 32
 #define HBFSIM_THERMAL_CONFIG_V1_VERSION 1u

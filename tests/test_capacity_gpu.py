@@ -1,0 +1,150 @@
+"""GPU parity of Capacity mode (A4): exact-LRU hit / victim / victim-dirty
+decisions of the batch-parallel kernels against the oracle's sequential LRU
+(oracle/hbf_oracle.c or_lru_run, itself pinned to the reference LruCache by
+tests/golden/lru_goldens.json), bit for bit, across batches that carry the
+resident list."""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import hbf_oracle as ho
+from helpers import Setup, make_context
+from hbfsim_b200 import workloads as wl
+
+pytestmark = pytest.mark.gpu
+
+PAGE = 4096
+GOLDEN = Path(__file__).resolve().parent / "golden" / "lru_goldens.json"
+NONE = (1 << 64) - 1
+
+
+def capacity_context(tmp, frames, capacity_gib=64):
+    p = wl.c0_profile()
+    p["capacity_bytes"] = capacity_gib << 30
+    s = Setup(profile=p, model=3, stacks=1, stripe=4096)
+    s.ranges = [(wl.RANGE_BASE, (capacity_gib - 1) << 30, 2, 3)]
+    ctx = make_context(s, tmp)
+    ctx.capacity_configure(frames, PAGE)
+    return ctx
+
+
+def to_accesses(pages, writes, rng):
+    off = rng.integers(0, PAGE // 128, pages.size) * 128
+    address = (wl.RANGE_BASE + pages.astype(np.uint64) * PAGE + off.astype(np.uint64))
+    nbytes = np.minimum(rng.choice([128, 512, 4096], pages.size), PAGE - off).astype(np.uint32)
+    return address.astype(np.uint64), nbytes, writes.astype(np.uint8)
+
+
+def run_gpu(ctx, address, nbytes, op):
+    import torch
+    dev = [torch.from_numpy(address.view(np.int64)).cuda(),
+           torch.from_numpy(nbytes.view(np.int32)).cuda(), torch.from_numpy(op).cuda()]
+    hit, victim, dirty, status = ctx.submit_capacity(*dev)
+    return (hit.cpu().numpy(), victim.cpu().numpy().view(np.uint64), dirty.cpu().numpy(),
+            status.cpu().numpy())
+
+
+def check(got, want, what):
+    hit, victim, dirty, status = got
+    assert np.all(status == 1), what
+    bad = np.flatnonzero(hit != want[0])
+    assert bad.size == 0, f"{what}: hit differs at {bad[:5]}"
+    bad = np.flatnonzero(victim != want[1])
+    assert bad.size == 0, f"{what}: victim differs at {bad[:5]}: {victim[bad[:5]]} vs {want[1][bad[:5]]}"
+    bad = np.flatnonzero(dirty != want[2])
+    assert bad.size == 0, f"{what}: dirty differs at {bad[:5]}"
+
+
+def test_reference_lru_goldens(tmp_path):
+    rng = np.random.default_rng(0)
+    for k, case in enumerate(json.loads(GOLDEN.read_text())):
+        ctx = capacity_context(str(tmp_path / f"c{k}"), case["frames"])
+        pages = np.array(case["keys"], np.uint64)
+        got = run_gpu(ctx, *to_accesses(pages, np.zeros(pages.size, np.uint8), rng))
+        assert got[0].tolist() == case["hits"], f"case {k}"
+        victims = [NONE if v < 0 else v for v in case["victims"]]
+        assert [int(v) for v in got[1]] == victims, f"case {k}"
+        ctx.close()
+
+
+def trace(rng, n, universe, locality):
+    pages = np.empty(n, np.uint64)
+    hot = rng.integers(0, universe, 64)
+    for i in range(n):
+        r = rng.random()
+        if r < locality and i:
+            pages[i] = pages[i - 1 - rng.integers(0, min(i, 48))]
+        elif r < locality + 0.2:
+            pages[i] = hot[rng.integers(0, hot.size)]
+        else:
+            pages[i] = rng.integers(0, universe)
+    return pages
+
+
+@pytest.mark.parametrize("frames,universe,n,batches", [(1, 5, 3000, 3), (7, 40, 20000, 4),
+                                                      (300, 2000, 60000, 5),
+                                                      (5000, 4000, 40000, 2),
+                                                      (2048, 1 << 20, 200000, 3)])
+def test_lru_matches_oracle_across_batches(tmp_path, frames, universe, n, batches):
+    rng = np.random.default_rng(frames + n)
+    pages = trace(rng, n, universe, 0.4) if n <= 60000 else \
+        np.where(rng.random(n) < 0.5, rng.integers(0, 4096, n), rng.integers(0, universe, n)).astype(np.uint64)
+    writes = (rng.random(n) < 0.2).astype(np.uint8)
+    want = ho.lru(pages, writes, frames)
+    ctx = capacity_context(str(tmp_path), frames)
+    cuts = np.sort(rng.choice(np.arange(1, n), batches - 1, replace=False))
+    for k, (lo, hi) in enumerate(zip(np.r_[0, cuts], np.r_[cuts, n])):
+        got = run_gpu(ctx, *to_accesses(pages[lo:hi], writes[lo:hi], rng))
+        check(got, tuple(w[lo:hi] for w in want), f"batch {k}")
+    resident, _ = ctx.capacity_state()
+    assert resident.size == min(frames, np.unique(pages).size)
+    ctx.close()
+
+
+def test_cyclic_scan_larger_than_the_cache(tmp_path):
+    """Config-2 shape, reduced: every step reads all KV pages in the same
+    order (a scan larger than HBM: exact LRU misses every time) and appends."""
+    rng = np.random.default_rng(4)
+    blocks = rng.integers(64, 512, 16)
+    steps, frames = 4, int(blocks.sum() * 0.2)
+    pages, writes = [], []
+    base = np.cumsum(np.r_[0, blocks[:-1] + steps])
+    for t in range(steps):
+        for s_, (b0, nb) in enumerate(zip(base, blocks)):
+            pages.append(np.arange(b0, b0 + nb + t, dtype=np.uint64))
+            w = np.zeros(nb + t, np.uint8)
+            w[-1] = 1  # the appended token's page is written
+            writes.append(w)
+    pages = np.concatenate(pages)
+    writes = np.concatenate(writes)
+    want = ho.lru(pages, writes, frames)
+    ctx = capacity_context(str(tmp_path), frames)
+    got = run_gpu(ctx, *to_accesses(pages, writes, rng))
+    check(got, want, "scan")
+    assert want[0].sum() < pages.size * 0.05
+    ctx.close()
+
+
+def test_statuses_and_page_numbering(tmp_path):
+    """Accesses outside capacity ranges are not cached; LRU pages count from
+    each range's file offset; an access crossing an LRU page is refused."""
+    p = wl.c0_profile()
+    s = Setup(profile=p, model=3, stacks=1, stripe=4096)
+    s.ranges = [(wl.RANGE_BASE, 1 << 30, 1, 3), (wl.RANGE_BASE + (4 << 30), 1 << 30, 2, 3)]
+    ctx = make_context(s, str(tmp_path))
+    ctx.capacity_configure(4, PAGE)
+    cap = wl.RANGE_BASE + (4 << 30)
+    address = np.array([wl.RANGE_BASE + 100, cap + 5 * PAGE, cap + 5 * PAGE + 8, cap + PAGE - 64,
+                        wl.HBM_BASE, cap + 7 * PAGE], np.uint64)
+    nbytes = np.array([128, 128, 128, 128, 128, 256], np.uint32)
+    op = np.array([0, 1, 0, 0, 0, 0], np.uint8)
+    hit, victim, dirty, status = run_gpu(ctx, address, nbytes, op)
+    assert status.tolist() == [6, 1, 1, 6, 8, 1]
+    assert hit.tolist() == [0, 0, 1, 0, 0, 0]
+    first_page = (1 << 30) // PAGE  # the capacity range's file offset in pages
+    pages, dirty_bits = ctx.capacity_state()
+    assert pages.tolist() == [first_page + 5, first_page + 7]
+    assert dirty_bits.tolist() == [1, 0]
+    ctx.close()
