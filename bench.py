@@ -219,6 +219,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the secondary measurements (config-2 LRU, config-3 grid step)")
     ap.add_argument("--decode-steps", type=int, default=8,
                     help="config-1 decode steps in the trace (8 = the full config; "
                          "fewer only for small profiling captures)")
@@ -335,9 +337,16 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, cores, sample = cpu_sample_rate(segments)
         cpu = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+    extras = None
+    if rank == 0 and world == 1 and not args.no_extras:
+        try:
+            extras = run_extras(args, device, tmp)
+        except Exception as e:  # a secondary measurement must not hide the headline line
+            log(f"extras failed: {e!r}")
+            extras = {"error": repr(e)}
     if rank == 0:
         emit(args, world, n, ms_max, e2e_rate, same, kernels, launches, dominant, achieved,
-             peak, peak_kind, traffic, alg, path_gbs, cpu, clocks, tot)
+             peak, peak_kind, traffic, alg, path_gbs, cpu, clocks, tot, extras)
     ctx.close()
     if world > 1:
         dist.barrier()
@@ -373,8 +382,132 @@ def run_e2e(ctx, address, nbytes, op, arrival, out, stream, args, world, device,
     return n * world / float(e2e_t.item()), bool(same)
 
 
+def run_extras(args, device, tmp):
+    """Secondary measurements beside the headline: one config-2 decode step
+    through the Capacity-mode LRU (exact), and the config-3 thermal grid
+    step; each with its CPU counterpart timed on a bounded sample."""
+    import torch
+    from hbfsim_b200 import Context, workloads as wl
+    out = {}
+    # ---- config 2: exact LRU over 20 % of the KV pages
+    lengths = wl.c2_lengths(0)
+    frames = wl.c2_frames(lengths)
+    p = wl.c0_profile()
+    p["name"] = "bench-c2"
+    p["capacity_bytes"] = 160 << 30
+    w = wl.Workload("c2", p, 1, STRIPE, wl.RANGE_BASE, 150 << 30)
+    ctx = Context(w.write_profile(tmp), report_dir=f"{tmp}/report-c2", mode=3)
+    ctx.register_device(wl.RANGE_BASE, 150 << 30, 2, 3)
+    ctx.capacity_configure(frames, wl.C2_PAGE)
+    times, sizes, hits = [], [], []
+    for step in range(3):
+        address, nbytes, op = wl.c2_step(lengths, step, 256, device=device)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        hit, victim, dirty, status = ctx.submit_capacity(address, nbytes, op)
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+        sizes.append(address.numel())
+        hits.append(int(hit.sum().item()))
+        del address, nbytes, op, hit, victim, dirty, status
+    ctx.close()
+    # steps 1 and 2 start with a full cache
+    rate = (sizes[1] + sizes[2]) / ((times[1] + times[2]) * 1e-3)
+    cap = {"workload": "config-2 decode steps 1-2 (Llama-3-8B-shaped paged KV, 64 sequences, "
+                       f"4 KiB pages, HBM = 20 percent of KV = {frames} frames)",
+           "page_refs_per_step": sizes[1], "ms_per_step": times[1],
+           "value": rate, "unit": "page refs/s", "hits_per_step": hits[1]}
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, str(REPO / "oracle"))
+        import hbf_oracle as ho
+        a, _, o = wl.c2_step(lengths[:4], 0, 256)
+        pages = ((a - np.uint64(wl.RANGE_BASE)) // np.uint64(wl.C2_PAGE)).astype(np.uint64)
+        f = wl.c2_frames(lengths[:4])
+        t0 = time.perf_counter()
+        ho.lru(pages, o, f)
+        dt = time.perf_counter() - t0
+        cap["cpu_baseline"] = {"value": pages.size / dt, "unit": "page refs/s", "cores": 1,
+                               "kind": "port",
+                               "sample": f"one decode step of 4 sequences ({pages.size} refs, "
+                                         f"{f} frames), exact LRU, single thread"}
+    out["capacity_lru"] = cap
+    # ---- config 3: eq3 grid 8 NAND + 1 logic layer x 128 x 128, 1 ms steps
+    p = wl.c0_profile()
+    p["name"] = "bench-c3"
+    w = wl.Workload("c3", p, 1, STRIPE, wl.RANGE_BASE, 60 << 30)
+    ctx = Context(w.write_profile(tmp), report_dir=f"{tmp}/report-c3", mode=3)
+    ctx.set_geometry(1, STRIPE, 0, 1)
+    stack, fp = c3_grid()
+    ctx.thermal_configure(stack, fp, {"idle_w": 0.5, "read_j_per_byte": 2e-9 / 128,
+                                      "write_j_per_access": 50e-9},
+                          {"onset_k": 343.15, "step_k": 10.0, "base_permille": 10,
+                           "cap_permille": 500},
+                          {"light_k": 358.15, "severe_k": 368.15, "shutdown_k": 378.15,
+                           "hysteresis_k": 2.0, "light_permille": 1500,
+                           "severe_permille": 3000})
+    for _ in range(3):
+        ctx.advance_epoch(1e-3)
+    torch.cuda.synchronize()
+    ctx.kernel_times()
+    ctx.set_profiling(True)
+    steps = 100
+    for _ in range(steps):
+        ctx.advance_epoch(1e-3)
+    torch.cuda.synchronize()
+    kt = ctx.kernel_times()
+    ctx.set_profiling(False)
+    ctx.close()
+    cells = 128 * 128 * 9
+    step_ms = kt["thermal"][1] / max(1, kt["thermal"][0])
+    ctrl_ms = kt["controller"][1] / max(1, kt["controller"][0])
+    th = {"workload": "config-3 grid: 1 logic + 8 NAND layers x 128 x 128 cells, fp64, "
+                      "1 ms backward-Euler steps, 64 dies",
+          "cells": cells, "steps": steps, "ms_per_step": step_ms,
+          "controller_ms_per_epoch": ctrl_ms,
+          "cell_bytes_per_step": 16 * cells,
+          "achieved_gbs_16B_per_cell": 16 * cells / (step_ms * 1e-3) / 1e9}
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, str(REPO / "oracle"))
+        import thermal_oracle as to
+        grid = to.ThermalGrid(stack)
+        power = np.zeros(cells)
+        t0 = time.perf_counter()
+        grid.step(power, 1e-3)          # includes the sparse LU factorization
+        t1 = time.perf_counter()
+        for _ in range(3):
+            grid.step(power, 1e-3)
+        t2 = time.perf_counter()
+        th["cpu_baseline"] = {"ms_per_step": (t2 - t1) / 3 * 1e3,
+                              "factor_ms": (t1 - t0) * 1e3, "cores": 1, "kind": "port",
+                              "sample": "scipy splu factor once, then 3 solves"}
+    out["thermal_step"] = th
+    return out
+
+
+def c3_grid():
+    """Config-3 grid and floorplan: 16 channels as a 4 x 4 array of 32 x 32
+    cell tiles; die d of a channel heats NAND layers 1 + 2d and 2 + 2d."""
+    silicon = {"cv_j_m3_k": 1.66e6, "k_xyz_w_m_k": [148.0, 148.0, 148.0]}
+    nand = {"cv_j_m3_k": 1.75e6, "k_xyz_w_m_k": [110.0, 110.0, 35.0]}
+    stack = {"nx": 128, "ny": 128, "cell_m": 100e-6,
+             "layers": [dict(silicon, thickness_m=100e-6)] +
+                       [dict(nand, thickness_m=50e-6) for _ in range(8)],
+             "bottom": {"h_w_m2_k": 0.0, "ambient_k": 318.15},
+             "top": {"h_w_m2_k": 2.0e4, "ambient_k": 318.15}, "initial_k": 318.15}
+    fp = {k: np.zeros(64, np.uint32) for k in ("z0", "z_count", "x0", "x1", "y0", "y1")}
+    for g in range(16):
+        for d in range(4):
+            i = g * 4 + d
+            fp["z0"][i], fp["z_count"][i] = 1 + 2 * d, 2
+            fp["x0"][i], fp["x1"][i] = (g % 4) * 32, (g % 4) * 32 + 32
+            fp["y0"][i], fp["y1"][i] = (g // 4) * 32, (g // 4) * 32 + 32
+    return stack, fp
+
+
 def emit(args, world, n, ms_max, e2e_rate, same, kernels, launches, dominant, achieved,
-         peak, peak_kind, traffic, alg, path_gbs, cpu, clocks, tot):
+         peak, peak_kind, traffic, alg, path_gbs, cpu, clocks, tot, extras=None):
     value = n * world / (ms_max * 1e-3)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
@@ -405,6 +538,7 @@ def emit(args, world, n, ms_max, e2e_rate, same, kernels, launches, dominant, ac
         "gpu_launches": launches,
         "cpu_baseline": cpu,
         "clocks": clocks,
+        "extras": extras,
         "per_step_totals": {"modeled": int(tot[0]), "bypass": int(tot[1]),
                             "unsupported": int(tot[2]), "foreign": int(tot[3])},
     }

@@ -176,3 +176,64 @@ def expand_segments(bases, counts, device=None):
     nbytes = torch.full((n,), READ_BYTES, dtype=torch.int32, device=device)
     op = torch.zeros(n, dtype=torch.uint8, device=device)
     return address, nbytes, op, idx
+
+
+# ---------------------------------------------------------------------------
+# c2: Capacity-mode paged KV shaped like Llama-3-8B.  32 layers x 8 KV heads
+# x head_dim 128 x bf16 x (K, V) = 4096 B per token-layer: one 4 KiB LRU page
+# per token and layer.  64 sequences with lengths uniform on [1024, 32768];
+# each decode step, layer by layer and sequence by sequence, writes the new
+# token's page (the append) and then reads every page of the sequence
+# including it.  HBM holds 20 % of the KV pages.  KV of (layer, sequence)
+# is contiguous, with room for the tokens the run appends.
+C2_LAYERS, C2_SEQS, C2_PAGE = 32, 64, 4096
+
+
+def c2_lengths(seed: int = 0, seqs: int = C2_SEQS, lmin: int = 1024, lmax: int = 32768):
+    return np.random.default_rng(seed).integers(lmin, lmax + 1, seqs)
+
+
+def c2_step(lengths, step: int, steps_total: int, layers: int = C2_LAYERS,
+            base: int = RANGE_BASE, device=None):
+    """(address u64, bytes u32, op u8) of one decode step, in issue order.
+    With `device` set, torch tensors built on that device (int64 carrying
+    the u64 addresses)."""
+    if device is not None:
+        return _c2_step_torch(lengths, step, steps_total, layers, base, device)
+    lengths = np.asarray(lengths, np.int64)
+    room = lengths + steps_total
+    region = np.concatenate([[0], np.cumsum(np.tile(room, layers))[:-1]])  # per (layer, seq)
+    cur = lengths + step                       # tokens before this step's append
+    per = np.tile(cur + 2, layers)             # 1 write + (cur + 1) reads
+    n = int(per.sum())
+    starts = np.concatenate([[0], np.cumsum(per)[:-1]])
+    k = np.arange(n, dtype=np.int64) - np.repeat(starts, per)   # position in group
+    grp_region = np.repeat(region, per)
+    grp_cur = np.repeat(np.tile(cur, layers), per)
+    token = np.where(k == 0, grp_cur, k - 1)                   # write new, then read 0..cur
+    page = grp_region + token
+    op = (k == 0).astype(np.uint8)
+    address = (base + page * C2_PAGE).astype(np.uint64)
+    return address, np.full(n, C2_PAGE, np.uint32), op
+
+
+def c2_frames(lengths, layers: int = C2_LAYERS, fraction: float = 0.2) -> int:
+    return int(int(np.asarray(lengths).sum()) * layers * fraction)
+
+
+def _c2_step_torch(lengths, step, steps_total, layers, base, device):
+    import torch
+    lengths = torch.as_tensor(np.asarray(lengths, np.int64), device=device)
+    room = lengths + steps_total
+    tiled_room = room.repeat(layers)
+    region = torch.cumsum(tiled_room, 0) - tiled_room
+    cur = (lengths + step).repeat(layers)
+    per = cur + 2
+    n = int(per.sum().item())
+    starts = torch.cumsum(per, 0) - per
+    k = torch.arange(n, dtype=torch.int64, device=device) - torch.repeat_interleave(starts, per)
+    token = torch.where(k == 0, torch.repeat_interleave(cur, per), k - 1)
+    page = torch.repeat_interleave(region, per) + token
+    address = base + page * C2_PAGE
+    op = (k == 0).to(torch.uint8)
+    return address, torch.full((n,), C2_PAGE, dtype=torch.int32, device=device), op
