@@ -572,7 +572,9 @@ std::uint32_t bits_for(std::uint64_t v)
 int ensure_scratch(CapacityState* s, std::uint64_t need)
 {
     if (need <= s->capacity_m) return HBFSIM_OK;
-    const std::uint64_t m = std::max<std::uint64_t>(need, 1 << 16);
+    // headroom: batches of a run grow slowly (appends), and regrowing costs
+    // a free and an allocation of every array
+    const std::uint64_t m = std::max<std::uint64_t>(need + need / 4, 1 << 16);
     const std::uint64_t words = m / 32 + 2;
     const std::uint64_t tiles = (m + kTile - 1) / kTile;
     std::uint64_t sums = 0, t = tiles;

@@ -48,6 +48,8 @@ struct ThermalState {
     double* d_w1 = nullptr;
     int* d_cell_die = nullptr;  // owning global die or -1
     double* d_die_cells = nullptr;
+    int* d_die_start = nullptr;  // cells of die d: d_die_list[start[d] .. start[d+1])
+    int* d_die_list = nullptr;
     double* d_die_power = nullptr;
     double* d_die_temp = nullptr;
     std::uint32_t* d_level = nullptr;    // throttle level per stack
@@ -87,6 +89,7 @@ void thermal_destroy(ThermalState* t)
                     static_cast<void*>(t->d_t), static_cast<void*>(t->d_w0),
                     static_cast<void*>(t->d_w1), static_cast<void*>(t->d_cell_die),
                     static_cast<void*>(t->d_die_cells), static_cast<void*>(t->d_die_power),
+                    static_cast<void*>(t->d_die_start), static_cast<void*>(t->d_die_list),
                     static_cast<void*>(t->d_die_temp), static_cast<void*>(t->d_level),
                     static_cast<void*>(t->d_refresh), static_cast<void*>(t->d_throttle),
                     static_cast<void*>(t->d_admit)})
@@ -197,17 +200,16 @@ __global__ void tridiag_kernel(const double* rhs, int nx, int ny, int nz, const 
     }
 }
 
-// Mean temperature of each global die over its cells.
-__global__ void die_temp_kernel(const double* t, const int* cell_die, long long cells,
-                                int dies, const double* die_cells, double* sum_out)
+// Mean temperature of each global die over its cells (one block per die,
+// over the die's own cell list; fixed summation order).
+__global__ void die_temp_kernel(const double* t, const int* die_start, const int* die_list,
+                                int dies, const double* die_cells, double* mean_out)
 {
-    // one block per die; cells owned by the die are found by scanning, which
-    // is cheap at grid sizes of ~1e5 cells and keeps the result order-stable
     const int d = blockIdx.x;
     if (d >= dies) return;
     double s = 0.0;
-    for (long long i = threadIdx.x; i < cells; i += blockDim.x)
-        if (cell_die[i] == d) s += t[i];
+    for (int k = die_start[d] + threadIdx.x; k < die_start[d + 1]; k += blockDim.x)
+        s += t[die_list[k]];
     __shared__ double red[256];
     red[threadIdx.x] = s;
     __syncthreads();
@@ -215,7 +217,7 @@ __global__ void die_temp_kernel(const double* t, const int* cell_die, long long 
         if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
         __syncthreads();
     }
-    if (threadIdx.x == 0) sum_out[d] = die_cells[d] > 0 ? red[0] / die_cells[d] : 0.0;
+    if (threadIdx.x == 0) mean_out[d] = die_cells[d] > 0 ? red[0] / die_cells[d] : 0.0;
 }
 
 struct ControllerArgs {
@@ -346,8 +348,7 @@ int advance(hbfsim_context* c, double epoch_s, const unsigned long long* rb,
     // inverse: W0_z = Qy W1_z, then T = W0 Qx^T
     dgemm(t->ny, t->nx, t->ny, t->d_qy, 0, 0, t->d_w1, plane, 0, t->d_w0, plane, t->nz, s);
     dgemm(t->nz * t->ny, t->nx, t->nx, t->d_w0, 0, 0, t->d_qx, 0, 1, t->d_t, 0, 1, s);
-    die_temp_kernel<<<t->dies_total, 256, 0, s>>>(t->d_t, t->d_cell_die,
-                                                   static_cast<long long>(t->cells),
+    die_temp_kernel<<<t->dies_total, 256, 0, s>>>(t->d_t, t->d_die_start, t->d_die_list,
                                                    static_cast<int>(t->dies_total),
                                                    t->d_die_cells, t->d_die_temp);
     hooks(kSlotThermal, 1, s);
@@ -515,6 +516,7 @@ int hbfsim_thermal_configure_v1(hbfsim_context* c, const hbfsim_thermal_config_v
               !alloc(&t->d_qy, static_cast<std::uint64_t>(ny) * ny) && !alloc(&t->d_t, cells) &&
               !alloc(&t->d_w0, cells) && !alloc(&t->d_w1, cells) &&
               !alloc(&t->d_cell_die, cells) && !alloc(&t->d_die_cells, dies) &&
+              !alloc(&t->d_die_start, dies + 1ull) && !alloc(&t->d_die_list, cells) &&
               !alloc(&t->d_die_power, dies) && !alloc(&t->d_die_temp, dies) &&
               !alloc(&t->d_level, c->stacks) && !alloc(&t->d_refresh, c->C) &&
               !alloc(&t->d_throttle, c->stacks) && !alloc(&t->d_admit, c->stacks);
@@ -534,6 +536,18 @@ int hbfsim_thermal_configure_v1(hbfsim_context* c, const hbfsim_thermal_config_v
         up(t->d_qy, qy.data(), 8 * qy.size());
         up(t->d_t, t0.data(), 8 * cells);
         up(t->d_cell_die, owner.data(), sizeof(int) * cells);
+        // per-die cell lists, ascending cell index
+        std::vector<int> start(dies + 1, 0), list;
+        list.reserve(cells);
+        for (std::uint64_t i = 0; i < cells; ++i)
+            if (owner[i] >= 0) ++start[owner[i] + 1];
+        for (std::uint32_t d = 0; d < dies; ++d) start[d + 1] += start[d];
+        list.assign(static_cast<std::size_t>(start[dies]), 0);
+        std::vector<int> fill(start.begin(), start.end() - 1);
+        for (std::uint64_t i = 0; i < cells; ++i)
+            if (owner[i] >= 0) list[fill[owner[i]]++] = static_cast<int>(i);
+        up(t->d_die_start, start.data(), sizeof(int) * (dies + 1));
+        if (!list.empty()) up(t->d_die_list, list.data(), sizeof(int) * list.size());
         up(t->d_die_cells, die_cells.data(), 8 * dies);
         ok = ok && cudaMemset(t->d_level, 0, 4 * c->stacks) == cudaSuccess &&
              cudaMemset(t->d_die_temp, 0, 8 * dies) == cudaSuccess;
