@@ -91,7 +91,8 @@ class DecodedV1(ctypes.Structure):
 class CapacityBatchV1(ctypes.Structure):
     _fields_ = [("struct_size", u32), ("version", u32), ("count", u64),
                 ("address", vp), ("bytes", vp), ("operation", vp), ("arrival_ns", vp),
-                ("hit", vp), ("victim_page", vp), ("victim_dirty", vp), ("status", vp)]
+                ("hit", vp), ("victim_page", vp), ("victim_dirty", vp), ("status", vp),
+                ("done_ns", vp), ("latency_ns", vp)]
 
 
 class ThermalLayerV1(ctypes.Structure):

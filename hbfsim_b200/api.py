@@ -204,9 +204,10 @@ class Context:
         check(self._lib.hbfsim_capacity_configure_v1(self.handle, frames, page_bytes),
               "hbfsim_capacity_configure_v1")
 
-    def submit_capacity(self, address, nbytes, op, arrival=None, stream=None):
+    def submit_capacity(self, address, nbytes, op, arrival=None, stream=None, timed=False):
         """Exact-LRU decisions for device tensors: (hit u8, victim page
-        int64 (-1 = none), victim dirty u8, status u8) device tensors."""
+        int64 (-1 = none), victim dirty u8, status u8) device tensors; with
+        timed=True also (done, latency) int64 tensors of the media actions."""
         import torch
         n = address.numel()
         dev = address.device
@@ -214,12 +215,17 @@ class Context:
         victim = torch.empty(n, dtype=torch.int64, device=dev)
         dirty = torch.empty(n, dtype=torch.uint8, device=dev)
         status = torch.empty(n, dtype=torch.uint8, device=dev)
+        done = torch.empty(n, dtype=torch.int64, device=dev) if timed else None
+        latency = torch.empty(n, dtype=torch.int64, device=dev) if timed else None
         b = _lib.CapacityBatchV1(ctypes.sizeof(_lib.CapacityBatchV1), 1, n, _ptr(address),
                                  _ptr(nbytes), _ptr(op), _ptr(arrival), _ptr(hit),
-                                 _ptr(victim), _ptr(dirty), _ptr(status))
+                                 _ptr(victim), _ptr(dirty), _ptr(status), _ptr(done),
+                                 _ptr(latency))
         check(self._lib.hbfsim_submit_capacity_batch_v1(
             self.handle, ctypes.byref(b), ctypes.c_void_p(_stream_handle(stream))),
             "hbfsim_submit_capacity_batch_v1")
+        if timed:
+            return hit, victim, dirty, status, done, latency
         return hit, victim, dirty, status
 
     def capacity_state(self):

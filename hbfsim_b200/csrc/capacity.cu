@@ -52,6 +52,23 @@ struct CapacityState {
     std::uint64_t tile_sums_words = 0;
     u32* valid = nullptr;            // per batch access: 1 = capacity access
     u32* status = nullptr;
+    // per batch access (batch order): LRU page and decisions, action slot
+    u32 *apage = nullptr, *ahit = nullptr, *avictim = nullptr, *adirty = nullptr;
+    u32 *anact = nullptr, *apos = nullptr;
+    // media actions (program of a dirty victim, read of a missed page)
+    std::uint64_t act_capacity = 0;
+    u64* act_addr = nullptr;
+    u32* act_bytes = nullptr;
+    u8* act_op = nullptr;
+    u64* act_arr = nullptr;
+    u32* act_chain = nullptr;        // program feeding a chained read, or kNone
+    u64* act_done = nullptr;
+    u64* act_lat = nullptr;
+    u8* act_status = nullptr;
+    u32* chained = nullptr;          // indices of the chained reads
+    u32* chained_flag = nullptr;
+    u32* chained_pos = nullptr;
+    DevRange* media_range = nullptr; // identity range: media address -> itself
     u32* counts = nullptr;           // small device results
     // counters (host)
     std::uint64_t calls = 0, accesses = 0, hits = 0, misses = 0, evictions = 0,
@@ -484,6 +501,9 @@ struct OutArgs {
     u8* out_hit;
     u64* out_victim;
     u8* out_dirty;
+    u32* in_hit;     // the same decisions for the media-action pass
+    u32* in_victim;
+    u32* in_dirty;
     u32* counters;  // [0] hits, [1] dirty evictions
 };
 
@@ -505,6 +525,9 @@ __global__ void output_kernel(OutArgs a)
     if (a.out_hit) a.out_hit[b] = static_cast<u8>(a.hit[i]);
     if (a.out_victim) a.out_victim[b] = victim;
     if (a.out_dirty) a.out_dirty[b] = static_cast<u8>(vd);
+    a.in_hit[b] = a.hit[i];
+    a.in_victim[b] = victim == ~u64{0} ? kNone : static_cast<u32>(victim);
+    a.in_dirty[b] = vd;
 }
 
 __global__ void status_kernel(const u32* st, u64 n, u8* out)
@@ -534,6 +557,64 @@ __global__ void live_kernel(const u32* next, u64 m, u32* live)
     if (j < m) live[j] = next[j] == kNone ? 1u : 0u;
 }
 
+// ---------------------------------------------------------------- actions
+// Media actions of the misses (request_dispatcher.cpp:107-126): the program
+// of a dirty victim's page, then the read of the missed page, each one LRU
+// page at its media address; the read after a program is chained to it.
+__global__ void act_count_kernel(const u32* status, const u32* hit, const u32* dirty, u64 n,
+                                 u32* nact)
+{
+    const u64 i = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) nact[i] = status[i] == kModeled && !hit[i] ? 1u + (dirty[i] ? 1u : 0u) : 0u;
+}
+
+__global__ void act_build_kernel(const u32* status, const u32* hit, const u32* victim,
+                                 const u32* dirty, const u32* page, const u32* pos,
+                                 const u64* arrival, u64 n, u32 shift, u32 page_bytes,
+                                 u64* addr, u32* bytes, u8* op, u64* arr, u32* chain)
+{
+    const u64 i = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n || status[i] != kModeled || hit[i]) return;
+    u64 k = pos[i];
+    const u64 a = arrival[i];
+    u32 feed = kNone;
+    if (dirty[i]) {
+        addr[k] = static_cast<u64>(victim[i]) << shift;
+        bytes[k] = page_bytes;
+        op[k] = 1;
+        arr[k] = a;
+        chain[k] = kNone;
+        feed = static_cast<u32>(k);
+        ++k;
+    }
+    addr[k] = static_cast<u64>(page[i]) << shift;
+    bytes[k] = page_bytes;
+    op[k] = 0;
+    arr[k] = a;
+    chain[k] = feed;
+}
+
+__global__ void chained_flag_kernel(const u32* chain, u64 count, u32* flag)
+{
+    const u64 k = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (k < count) flag[k] = chain[k] != kNone ? 1u : 0u;
+}
+
+// completion of each access: its read, or its arrival when served from HBM
+// (hit) or not a capacity access
+__global__ void act_result_kernel(const u32* status, const u32* hit, const u32* dirty,
+                                  const u32* pos, const u64* arrival, const u64* act_done,
+                                  u64 n, u64* done, u64* latency)
+{
+    const u64 i = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const u64 a = arrival[i];
+    u64 d = a;
+    if (status[i] == kModeled && !hit[i]) d = act_done[pos[i] + (dirty[i] ? 1u : 0u)];
+    if (done) done[i] = d;
+    if (latency) latency[i] = d - a;
+}
+
 inline unsigned blocks(u64 n) { return static_cast<unsigned>((n + kT - 1) / kT); }
 
 }  // namespace
@@ -543,7 +624,11 @@ void capacity_destroy(CapacityState* c)
     if (!c) return;
     void* ptrs[] = {c->res_page, c->res_dirty, c->key, c->w, c->bidx, c->sk, c->si, c->tk,
                     c->ti, c->prev, c->next, c->cur, c->nxt, c->levels, c->hit, c->a,
-                    c->b, c->c, c->d, c->tile_sums, c->valid, c->status, c->counts};
+                    c->b, c->c, c->d, c->tile_sums, c->valid, c->status, c->counts,
+                    c->apage, c->ahit, c->avictim, c->adirty, c->anact, c->apos,
+                    c->act_addr, c->act_bytes, c->act_op, c->act_arr, c->act_chain,
+                    c->act_done, c->act_lat, c->act_status, c->chained, c->chained_flag,
+                    c->chained_pos, c->media_range};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     delete c;
@@ -588,7 +673,9 @@ int ensure_scratch(CapacityState* s, std::uint64_t need)
         grow(&s->next, m) || grow(&s->cur, m) || grow(&s->nxt, m) ||
         grow(&s->levels, 32 * words) || grow(&s->hit, m) || grow(&s->a, m) ||
         grow(&s->b, m) || grow(&s->c, m) || grow(&s->d, m) || grow(&s->valid, m) ||
-        grow(&s->status, m) || grow(&s->tile_sums, 2 * (256 * tiles + sums)))
+        grow(&s->status, m) || grow(&s->tile_sums, 2 * (256 * tiles + sums)) ||
+        grow(&s->apage, m) || grow(&s->ahit, m) || grow(&s->avictim, m) ||
+        grow(&s->adirty, m) || grow(&s->anact, m) || grow(&s->apos, m))
         return HBFSIM_CUDA_ERROR;
     s->tile_sums_words = 2 * (256 * tiles + sums);
     s->capacity_m = m;
@@ -609,6 +696,99 @@ cudaError_t scan_add(CapacityState* s, const u32* in, u32* out, u64 n, bool incl
     return cudaGetLastError();
 }
 
+bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
+
+constexpr std::uint64_t kMaxChainPieces = 4096;
+
+// Times the media actions of the batch's misses with the context's die
+// model, in batch order, and writes each access's completion.  Every chained
+// read starts a piece; pieces run back to back on the stream, and before
+// each one its chained read's arrival is raised to its program's
+// completion.  Beyond kMaxChainPieces chained reads, one thread walks all
+// actions instead (exact, slow).
+int time_actions(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStream_t st)
+{
+    CapacityState* s = ctx->capacity;
+    const std::uint64_t n = b->count;
+    u32* cnt = s->counts;
+    act_count_kernel<<<blocks(n), kT, 0, st>>>(s->status, s->ahit, s->adirty, n, s->anact);
+    scan_add(s, s->anact, s->apos, n, false, cnt + 8, st);
+    std::uint32_t actions = 0;
+    cudaMemcpyAsync(&actions, cnt + 8, 4, cudaMemcpyDeviceToHost, st);
+    if (cudaStreamSynchronize(st) != cudaSuccess) return HBFSIM_CUDA_ERROR;
+    if (actions > s->act_capacity) {
+        const std::uint64_t cap = actions + actions / 4 + 1024;
+        if (grow(&s->act_addr, cap) || grow(&s->act_bytes, cap) || grow(&s->act_op, cap) ||
+            grow(&s->act_arr, cap) || grow(&s->act_chain, cap) || grow(&s->act_done, cap) ||
+            grow(&s->act_lat, cap) || grow(&s->act_status, cap) || grow(&s->chained, cap) ||
+            grow(&s->chained_flag, cap) || grow(&s->chained_pos, cap)) {
+            s->act_capacity = 0;
+            return HBFSIM_CUDA_ERROR;
+        }
+        s->act_capacity = cap;
+    }
+    if (actions) {
+        act_build_kernel<<<blocks(n), kT, 0, st>>>(s->status, s->ahit, s->avictim, s->adirty,
+                                                    s->apage, s->apos, b->arrival_ns, n,
+                                                    s->page_shift, 1u << s->page_shift,
+                                                    s->act_addr, s->act_bytes, s->act_op,
+                                                    s->act_arr, s->act_chain);
+        chained_flag_kernel<<<blocks(actions), kT, 0, st>>>(s->act_chain, actions,
+                                                             s->chained_flag);
+        scan_add(s, s->chained_flag, s->chained_pos, actions, false, cnt + 9, st);
+        compact_kernel<<<blocks(actions), kT, 0, st>>>(s->chained_flag, s->chained_pos, actions,
+                                                       s->chained);
+        std::uint32_t q = 0;
+        cudaMemcpyAsync(&q, cnt + 9, 4, cudaMemcpyDeviceToHost, st);
+        if (cudaStreamSynchronize(st) != cudaSuccess) return HBFSIM_CUDA_ERROR;
+        if (q <= kMaxChainPieces) {
+            std::vector<std::uint32_t> starts(q);
+            if (q && cudaMemcpy(starts.data(), s->chained, 4ull * q, cudaMemcpyDeviceToHost) !=
+                         cudaSuccess)
+                return HBFSIM_CUDA_ERROR;
+            std::vector<std::uint64_t> cuts{0};
+            for (std::uint32_t v : starts)
+                if (v != 0) cuts.push_back(v);
+            cuts.push_back(actions);
+            for (std::size_t p = 0; p + 1 < cuts.size(); ++p) {
+                const std::uint64_t lo = cuts[p], hi = cuts[p + 1];
+                if (hi <= lo) continue;
+                if (launch_chain_fixup(s->act_arr, s->act_done, s->act_chain, lo, st) !=
+                    cudaSuccess)
+                    return HBFSIM_CUDA_ERROR;
+                BatchIO io{};
+                io.address = s->act_addr + lo;
+                io.bytes = s->act_bytes + lo;
+                io.op = s->act_op + lo;
+                io.arrival = s->act_arr + lo;
+                io.done = s->act_done + lo;
+                io.latency = s->act_lat + lo;
+                io.status = s->act_status + lo;
+                io.n = hi - lo;
+                io.aligned = aligned16(io.address) && aligned16(io.bytes) && aligned16(io.op) &&
+                             aligned16(io.arrival) && aligned16(io.done) &&
+                             aligned16(io.latency) && aligned16(io.status);
+                const int rc = run_media_batch(ctx, io, s->media_range, 1, st);
+                if (rc != HBFSIM_OK) return rc;
+            }
+        } else {
+            const DecodeParams dp = media_decode_params(ctx, s->media_range, 1);
+            const std::uint64_t words = static_cast<std::uint64_t>(ctx->C) * ctx->K;
+            if (launch_chain_sequential(dp, context_timing_params(ctx), s->act_addr,
+                                        s->act_bytes, s->act_op, s->act_arr, s->act_chain,
+                                        actions, ctx->K, ctx->d_state[ctx->cur],
+                                        ctx->d_state[1 - ctx->cur], words, s->act_done,
+                                        s->act_lat, s->act_status, st) != cudaSuccess)
+                return HBFSIM_CUDA_ERROR;
+            ctx->cur = 1 - ctx->cur;
+        }
+    }
+    act_result_kernel<<<blocks(n), kT, 0, st>>>(s->status, s->ahit, s->adirty, s->apos,
+                                                 b->arrival_ns, s->act_done, n, b->done_ns,
+                                                 b->latency_ns);
+    return cudaStreamSynchronize(st) == cudaSuccess ? HBFSIM_OK : HBFSIM_CUDA_ERROR;
+}
+
 int run_capacity(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStream_t st)
 {
     CapacityState* s = ctx->capacity;
@@ -622,7 +802,7 @@ int run_capacity(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStr
     cap_classify_kernel<<<blocks(n), kT, 0, st>>>(ctx->d_ranges,
                                                    static_cast<u32>(ctx->ranges.size()),
                                                    b->address, b->bytes, b->operation, n,
-                                                   s->page_shift, s->ti, s->valid, s->status);
+                                                   s->page_shift, s->apage, s->valid, s->status);
     scan_add(s, s->valid, s->a, n, false, cnt + 0, st);
     std::uint32_t valid_total = 0;
     cudaMemcpyAsync(&valid_total, cnt + 0, 4, cudaMemcpyDeviceToHost, st);
@@ -631,12 +811,16 @@ int run_capacity(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStr
     if (b->status) status_kernel<<<blocks(n), kT, 0, st>>>(s->status, n, b->status);
     // 2. the sequence: resident list, then the capacity accesses
     cap_build_kernel<<<blocks(std::max(n, resident)), kT, 0, st>>>(
-        s->res_page, s->res_dirty, resident, s->ti, b->operation, s->valid, s->a, n, s->key,
+        s->res_page, s->res_dirty, resident, s->apage, b->operation, s->valid, s->a, n, s->key,
         s->w, s->bidx);
     if (m == 0) {
         if (b->hit) cudaMemsetAsync(b->hit, 0, n, st);
         if (b->victim_page) cudaMemsetAsync(b->victim_page, 0xff, 8 * n, st);
         if (b->victim_dirty) cudaMemsetAsync(b->victim_dirty, 0, n, st);
+        if (b->done_ns || b->latency_ns)  // nothing cached: every access keeps its arrival
+            act_result_kernel<<<blocks(n), kT, 0, st>>>(s->status, s->ahit, s->adirty,
+                                                         s->apos, b->arrival_ns, nullptr, n,
+                                                         b->done_ns, b->latency_ns);
         return cudaStreamSynchronize(st) == cudaSuccess ? HBFSIM_OK : HBFSIM_CUDA_ERROR;
     }
     // 3. stable radix sort of (page, position)
@@ -705,6 +889,9 @@ int run_capacity(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStr
     oa.out_hit = b->hit;
     oa.out_victim = b->victim_page;
     oa.out_dirty = b->victim_dirty;
+    oa.in_hit = s->ahit;
+    oa.in_victim = s->avictim;
+    oa.in_dirty = s->adirty;
     oa.counters = cnt + 1;
     if (b->hit) cudaMemsetAsync(b->hit, 0, n, st);
     if (b->victim_page) cudaMemsetAsync(b->victim_page, 0xff, 8 * n, st);
@@ -723,6 +910,10 @@ int run_capacity(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStr
                                               keep, s->res_page, s->res_dirty);
     if (cudaStreamSynchronize(st) != cudaSuccess) return HBFSIM_CUDA_ERROR;
     s->resident = keep;
+    if (b->done_ns || b->latency_ns) {
+        const int rc = time_actions(ctx, b, st);
+        if (rc != HBFSIM_OK) return rc;
+    }
     ++s->calls;
     s->accesses += valid_total;
     s->hits += host_cnt[1];
@@ -755,8 +946,22 @@ int hbfsim_capacity_configure_v1(hbfsim_context* c, uint64_t frames, uint32_t pa
     c->capacity = s;
     s->frames = frames;
     s->page_shift = shift;
+    DevRange media{};
+    media.base = 0;
+    media.length = c->profile.capacity_bytes;
+    media.file_offset = 0;
+    media.page_bytes = c->profile.page_bytes;
+    media.mode = HBFSIM_RANGE_MODE_TIMING;
+    media.permissions = 3;
+    std::uint32_t page_log = 0;
+    while ((std::uint64_t{1} << page_log) < c->profile.page_bytes) ++page_log;
+    media.reserved = page_log;
+    media.end = media.base + media.length;
+    media.ok = 1;
+    media.timing = 1;
     if (grow(&s->res_page, frames) || grow(&s->res_dirty, frames) ||
-        grow(&s->counts, kCapCounts)) {
+        grow(&s->counts, kCapCounts) || grow(&s->media_range, 1) ||
+        cudaMemcpy(s->media_range, &media, sizeof media, cudaMemcpyHostToDevice) != cudaSuccess) {
         capacity_destroy(s);
         c->capacity = nullptr;
         return HBFSIM_CUDA_ERROR;
@@ -774,6 +979,11 @@ int hbfsim_submit_capacity_batch_v1(hbfsim_context* c, const hbfsim_capacity_bat
     CGuard g(c);
     if (!c->capacity) return HBFSIM_INVALID_ARGUMENT;
     if (c->capacity->resident + b->count >= 0x7fffffffull) return HBFSIM_UNSUPPORTED;
+    if (b->done_ns || b->latency_ns) {
+        // the media actions are timed with the per-die model of one shard
+        if (!b->arrival_ns) return HBFSIM_INVALID_ARGUMENT;
+        if (c->mode != HBFSIM_MODEL_DIE_V1 || c->shard_count != 1) return HBFSIM_UNSUPPORTED;
+    }
     if (b->count == 0) return HBFSIM_OK;
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
     return run_capacity(c, b, s);

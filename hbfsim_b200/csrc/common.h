@@ -119,6 +119,9 @@ struct TimingParams {
     // activity counted by pass 1, [C*D][2] (read bytes, writes); the range
     // scan adds it to the die counters once the batch is accepted
     unsigned long long* act_stage;
+    // 1: the batch order need not follow the arrival order (media actions
+    // whose arrival waits for an earlier action's completion)
+    u32 any_order;
 };
 
 // Device-side counters (one block of u64 per context).

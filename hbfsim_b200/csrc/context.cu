@@ -361,8 +361,12 @@ int model_supported(const hbfsim_context* c)
     return HBFSIM_OK;
 }
 
-// Times n accesses already on the device.  Caller holds the lock.
-int run_device_batch(hbfsim_context* c, const BatchIO& io, cudaStream_t stream)
+// Times n accesses already on the device.  Caller holds the lock.  With
+// `ranges` set, the accesses are decoded against that table instead of the
+// registered ranges (media addresses of Capacity-mode actions), and their
+// arrivals need not be ordered.
+int run_device_batch(hbfsim_context* c, const BatchIO& io, cudaStream_t stream,
+                     const DevRange* ranges = nullptr, std::uint32_t range_count = 0)
 {
     if (io.n == 0) return HBFSIM_OK;
     // Bound proof for the parallel path.  Pass 1 checks on the device that
@@ -396,14 +400,39 @@ int run_device_batch(hbfsim_context* c, const BatchIO& io, cudaStream_t stream)
     s.counters = c->d_counters;
     s.state_in = c->d_state[c->cur];
     s.state_out = c->d_state[1 - c->cur];
-    const cudaError_t err = launch_batch(decode_params(c), timing_params(c), io, plan, s,
-                                         sequential, stream, c->hooks());
+    DecodeParams dp = decode_params(c);
+    TimingParams tp = timing_params(c);
+    if (ranges) {
+        dp.ranges = ranges;
+        dp.range_count = range_count;
+        tp.any_order = 1;
+    }
+    const cudaError_t err = launch_batch(dp, tp, io, plan, s, sequential, stream, c->hooks());
     if (err != cudaSuccess) return HBFSIM_CUDA_ERROR;
     c->cur = 1 - c->cur;
     return HBFSIM_OK;
 }
 
 }  // namespace
+
+namespace hbfb {
+int run_media_batch(hbfsim_context* c, const BatchIO& io, const DevRange* ranges,
+                    std::uint32_t range_count, cudaStream_t stream)
+{
+    return run_device_batch(c, io, stream, ranges, range_count);
+}
+
+DecodeParams media_decode_params(const hbfsim_context* c, const DevRange* ranges,
+                                 std::uint32_t range_count)
+{
+    DecodeParams dp = decode_params(c);
+    dp.ranges = ranges;
+    dp.range_count = range_count;
+    return dp;
+}
+
+TimingParams context_timing_params(const hbfsim_context* c) { return timing_params(c); }
+}  // namespace hbfb
 
 hbfb::LaunchHooks hbfsim_context::hooks()
 {

@@ -103,6 +103,13 @@ namespace hbfb {
 // thermal.cu
 void thermal_destroy(ThermalState* t);
 void capacity_destroy(CapacityState* c);
+// Times media actions (device arrays) decoded against `ranges`, in batch
+// order whatever their arrivals; carries the context's timing state.
+int run_media_batch(hbfsim_context* c, const BatchIO& io, const DevRange* ranges,
+                    std::uint32_t range_count, cudaStream_t stream);
+DecodeParams media_decode_params(const hbfsim_context* c, const DevRange* ranges,
+                                 std::uint32_t range_count);
+TimingParams context_timing_params(const hbfsim_context* c);
 void capacity_stats(const CapacityState* c, hbfsim_capacity_stats_v1* out);
 // Device arrays of the factors the epoch controller derived (refresh per
 // local channel, throttle permille and admit-after tick per stack).

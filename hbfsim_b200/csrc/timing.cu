@@ -491,7 +491,7 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
             if (PASS == 1) {
                 const u64 prev = e > 0 ? s.arr[e - 1]
                                        : (start > 0 ? A.arrival[start - 1] : *A.last_arrival);
-                if (arr < prev) unsorted = true;
+                if (arr < prev && !A.tp.any_order) unsorted = true;
                 if (arr >= kArrivalLimit) atomicOr(A.error, kErrNeedSeq);
             }
             TimingDecoded d;
@@ -1705,6 +1705,90 @@ cudaError_t launch_sample(const DecodeParams& dp, const u64* address, const u32*
     sample_write_kernel<<<static_cast<unsigned>(ctas), kSampleThreads, 0, stream>>>(
         dp, address, bytes, op, n, per, counts, warmup, threshold, sample);
     hooks(kSlotOther, 1, stream);
+    return cudaGetLastError();
+}
+
+}  // namespace hbfb
+
+// ---------------------------------------------------------------------------
+// Chained media actions (Capacity mode).  A read that refills a page after a
+// dirty victim's program arrives at max(arrival, program completion)
+// (request_dispatcher.cpp:294-298).  The batch is timed in pieces that each
+// start at such a read; before a piece runs, its first read's arrival is
+// raised to the completion of its program, which an earlier piece produced.
+namespace hbfb {
+namespace {
+
+__global__ void chain_fixup_kernel(u64* arrival, const u64* done, const u32* chain, u64 index)
+{
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        const u32 src = chain[index];
+        if (src != 0xffffffffu && done[src] > arrival[index]) arrival[index] = done[src];
+    }
+}
+
+// Exact fallback for batches with very many chained reads: one thread walks
+// every action in batch order with the saturating die model.
+__global__ void chain_sequential_kernel(const DecodeParams dp, const TimingParams tp,
+                                        const u64* address, const u32* bytes, const u8* op,
+                                        u64* arrival, const u32* chain, u64 n, u32 K,
+                                        const u64* state_in, u64* state_out, u64* done,
+                                        u64* latency, u8* status, u64 words)
+{
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    for (u64 k = 0; k < words; ++k) state_out[k] = state_in[k];
+    for (u64 i = 0; i < n; ++i) {
+        u64 a = arrival[i];
+        if (chain[i] != 0xffffffffu && done[chain[i]] > a) a = done[chain[i]];
+        arrival[i] = a;
+        const Decoded d = classify_decode(dp, address[i], bytes[i], op[i], true);
+        status[i] = static_cast<u8>(d.status);
+        if (d.status != kModeled) {
+            done[i] = a;
+            latency[i] = 0;
+            continue;
+        }
+        const u32 c = d.local;
+        u64* st = state_out + static_cast<u64>(c) * K;
+        const u64 bw = tp.chan_bw[c];
+        const u64 num = static_cast<u64>(bytes[i]) * 1000000000ull;
+        const u64 x = sat_mul_u64(num / bw + (num % bw != 0), tp.time_scale);
+        const u64 top = static_cast<u64>(op[i] ? tp.chan_t_prog[c] : tp.chan_t_read[c]);
+        u64 s = a;
+        const u64 admit = static_cast<u64>(tp.chan_admit[c]);
+        if (admit > s) s = admit;
+        if (st[0] > s) s = st[0];
+        if (st[1 + d.die] > s) s = st[1 + d.die];
+        st[0] = sat_add_u64(s, x);
+        st[1 + d.die] = sat_add_u64(st[0], top);
+        done[i] = st[1 + d.die];
+        latency[i] = done[i] - a;
+        if (tp.die_read_bytes) {
+            const u64 k = static_cast<u64>(c) * tp.dies + d.die;
+            if (op[i]) tp.die_writes[k] += 1;
+            else tp.die_read_bytes[k] += bytes[i];
+        }
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_chain_fixup(u64* arrival, const u64* done, const u32* chain, u64 index,
+                               cudaStream_t stream)
+{
+    chain_fixup_kernel<<<1, 32, 0, stream>>>(arrival, done, chain, index);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_chain_sequential(const DecodeParams& dp, const TimingParams& tp,
+                                    const u64* address, const u32* bytes, const u8* op,
+                                    u64* arrival, const u32* chain, u64 n, u32 K,
+                                    const u64* state_in, u64* state_out, u64 words, u64* done,
+                                    u64* latency, u8* status, cudaStream_t stream)
+{
+    chain_sequential_kernel<<<1, 32, 0, stream>>>(dp, tp, address, bytes, op, arrival, chain, n,
+                                                  K, state_in, state_out, done, latency, status,
+                                                  words);
     return cudaGetLastError();
 }
 

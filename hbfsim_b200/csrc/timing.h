@@ -71,4 +71,14 @@ cudaError_t launch_sample(const DecodeParams& dp, const u64* address, const u32*
                           u64* seq, u64* counts, u32 max_ctas, cudaStream_t stream,
                           const LaunchHooks& hooks = {});
 
+// Chained media actions: raise arrival[index] to done[chain[index]].
+cudaError_t launch_chain_fixup(u64* arrival, const u64* done, const u32* chain, u64 index,
+                               cudaStream_t stream);
+// Exact single-thread walk of n chained actions (state_in -> state_out).
+cudaError_t launch_chain_sequential(const DecodeParams& dp, const TimingParams& tp,
+                                    const u64* address, const u32* bytes, const u8* op,
+                                    u64* arrival, const u32* chain, u64 n, u32 K,
+                                    const u64* state_in, u64* state_out, u64 words, u64* done,
+                                    u64* latency, u8* status, cudaStream_t stream);
+
 }  // namespace hbfb

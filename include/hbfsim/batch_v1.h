@@ -231,18 +231,29 @@ typedef struct hbfsim_capacity_batch_v1 {
     const uint64_t* address;     /* in CAPACITY ranges; one LRU page each   */
     const uint32_t* bytes;
     const uint8_t* operation;    /* 0 read, 1 write (dirties the page)      */
-    const uint64_t* arrival_ns;  /* reserved for the media-action timing    */
+    const uint64_t* arrival_ns;  /* needed when done_ns / latency_ns are set */
     uint8_t* hit;                /* out: 1 = resident in HBM                 */
     uint64_t* victim_page;       /* out: page evicted by this access,
                                   *      UINT64_MAX if none                  */
     uint8_t* victim_dirty;       /* out: 1 = the victim must be programmed   */
     uint8_t* status;             /* out: 1 capacity access, 6 unsupported,
                                   *      8 outside every range               */
+    uint64_t* done_ns;           /* out (optional): completion tick          */
+    uint64_t* latency_ns;        /* out (optional): done - arrival           */
 } hbfsim_capacity_batch_v1;
 
 /* Decides hit / victim / dirty for every access, in batch order, continuing
  * from the resident list the previous batch left.  Device pointers (NULL
- * outputs are skipped).  Synchronous: returns when the results are written. */
+ * outputs are skipped).  Synchronous: returns when the results are written.
+ *
+ * With done_ns or latency_ns set, the misses' media actions are timed with
+ * the context's per-die model (mode 3, one shard), continuing its die and
+ * channel state: for each miss in batch order, the program of a dirty
+ * victim's page at the access's arrival, then the read of the missed page
+ * at max(arrival, program completion) (request_dispatcher.cpp:107-126,
+ * 294-298); one LRU page each, at its media address.  A miss completes with
+ * its read; hits (served from HBM) and non-capacity accesses complete at
+ * their arrival. */
 int hbfsim_submit_capacity_batch_v1(hbfsim_context* context,
                                     const hbfsim_capacity_batch_v1* batch,
                                     void* stream);

@@ -540,3 +540,53 @@ void or_lru_run(const uint64_t* pages, const uint8_t* writes, uint64_t n,
 #undef OR_PUSH_FRONT
     free(table); free(key); free(prev); free(next); free(dirty);
 }
+
+/* One media action of the capacity path through the die model. */
+static uint64_t or_media_step(const or_geometry* g, const or_timing* t,
+                              const uint64_t* chan_bw, const uint64_t* t_read,
+                              const uint64_t* t_prog, const uint64_t* admit,
+                              uint64_t media, uint32_t bytes, int op, uint64_t arrival,
+                              uint64_t* state)
+{
+    or_decoded d;
+    memset(&d, 0, sizeof d);
+    or_decode_one(g, media, &d);
+    const uint32_t shards = g->shard_count ? g->shard_count : 1;
+    const uint32_t c = d.channel / shards;
+    uint64_t* st = &state[(uint64_t)c * (g->dies_per_channel + 1)];
+    const uint64_t x = or_saturating_multiply(or_channel_transfer_ns(bytes, chan_bw[c]),
+                                              t->time_scale);
+    const uint64_t top = op ? t_prog[d.stack] : t_read[d.stack];
+    const uint64_t tt = or_saturating_multiply(top, t->time_scale);
+    const uint64_t adm = admit ? admit[d.stack] : 0;
+    return or_die_step(&st[0], &st[1 + d.die], arrival, adm, x, tt);
+}
+
+void or_capacity_timing(const or_geometry* g, const or_timing* t,
+                        const uint64_t* chan_bw, const uint64_t* t_read,
+                        const uint64_t* t_prog, const uint64_t* admit,
+                        const uint8_t* status, const uint8_t* hit, const uint64_t* page,
+                        const uint64_t* victim, const uint8_t* victim_dirty,
+                        const uint64_t* arrival, uint64_t n, uint32_t page_shift,
+                        uint64_t* state, uint64_t* done, uint64_t* latency)
+{
+    const uint32_t bytes = 1u << page_shift;
+    for (uint64_t i = 0; i < n; ++i) {
+        const uint64_t a = arrival[i];
+        if (status[i] != OR_STATUS_MODELED || hit[i]) {
+            done[i] = a;
+            latency[i] = 0;
+            continue;
+        }
+        uint64_t read_arrival = a;
+        if (victim_dirty[i]) {
+            const uint64_t p = or_media_step(g, t, chan_bw, t_read, t_prog, admit,
+                                             victim[i] << page_shift, bytes, 1, a, state);
+            if (p > read_arrival) read_arrival = p;
+        }
+        const uint64_t r = or_media_step(g, t, chan_bw, t_read, t_prog, admit,
+                                         page[i] << page_shift, bytes, 0, read_arrival, state);
+        done[i] = r;
+        latency[i] = r - a;
+    }
+}

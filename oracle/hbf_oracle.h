@@ -157,6 +157,20 @@ void or_lru_run(const uint64_t* pages, const uint8_t* writes, uint64_t n,
                 uint64_t frames, uint8_t* hit, uint64_t* victim,
                 uint8_t* victim_dirty);
 
+/* ---- capacity mode: media actions of the misses, timed with the die model
+ * in batch order (request_dispatcher.cpp:107-126, 294-298): for a miss, the
+ * program of a dirty victim's page at the access's arrival, then the read of
+ * the missed page at max(arrival, program completion); one LRU page
+ * (2^page_shift bytes) each, at its media address (page << page_shift).
+ * Hits and non-capacity accesses (status != 1) complete at their arrival. */
+void or_capacity_timing(const or_geometry* g, const or_timing* t,
+                        const uint64_t* chan_bw, const uint64_t* t_read,
+                        const uint64_t* t_prog, const uint64_t* admit,
+                        const uint8_t* status, const uint8_t* hit, const uint64_t* page,
+                        const uint64_t* victim, const uint8_t* victim_dirty,
+                        const uint64_t* arrival, uint64_t n, uint32_t page_shift,
+                        uint64_t* state, uint64_t* done, uint64_t* latency);
+
 #ifdef __cplusplus
 }
 #endif

@@ -93,6 +93,8 @@ def _load() -> ctypes.CDLL:
     lib.or_run_batch_threads.restype = ctypes.c_int
     lib.or_run_batch_threads.argtypes = [p, u32, p, p, p, p, p, p, p, p, p, p,
                                          u64, p, p, p, p, p, ctypes.c_int]
+    lib.or_capacity_timing.restype = None
+    lib.or_capacity_timing.argtypes = [p, p, p, p, p, p, p, p, p, p, p, p, u64, u32, p, p, p]
     lib.or_lru_run.restype = None
     lib.or_lru_run.argtypes = [p, p, u64, u64, p, p, p]
     return lib
@@ -165,6 +167,21 @@ def lru(pages: np.ndarray, writes: np.ndarray, frames: int):
     LIB.or_lru_run(_ptr(pages), _ptr(writes), n, frames, _ptr(hit), _ptr(victim),
                    _ptr(vdirty))
     return hit, victim, vdirty
+
+
+def capacity_timing(geometry, timing, chan_bw, t_read, t_prog, admit, status, hit, page,
+                    victim, victim_dirty, arrival, page_shift, state):
+    """Completion and latency of every access of a capacity batch; updates
+    `state` (die model words) in place."""
+    n = arrival.size
+    done = np.zeros(n, np.uint64)
+    latency = np.zeros(n, np.uint64)
+    LIB.or_capacity_timing(ctypes.byref(geometry), ctypes.byref(timing), _ptr(chan_bw),
+                           _ptr(t_read), _ptr(t_prog), None if admit is None else _ptr(admit),
+                           _ptr(status), _ptr(hit), _ptr(page), _ptr(victim),
+                           _ptr(victim_dirty), _ptr(arrival), n, page_shift, _ptr(state),
+                           _ptr(done), _ptr(latency))
+    return done, latency
 
 
 def cores() -> int:

@@ -148,3 +148,46 @@ def test_statuses_and_page_numbering(tmp_path):
     assert pages.tolist() == [first_page + 5, first_page + 7]
     assert dirty_bits.tolist() == [1, 0]
     ctx.close()
+
+
+@pytest.mark.parametrize("frames,write_p,n", [(256, 0.02, 60000), (64, 0.5, 30000)])
+def test_media_action_timing_matches_oracle(tmp_path, frames, write_p, n):
+    """Misses become media actions timed with the die model: the program of
+    a dirty victim, then the chained read.  Few chained reads run as pieces
+    of the parallel path; many take the exact one-thread walk."""
+    import torch
+    from helpers import OracleRun
+    rng = np.random.default_rng(frames)
+    pages = np.where(rng.random(n) < 0.6, rng.integers(0, 2 * frames, n),
+                     rng.integers(0, 1 << 18, n)).astype(np.uint64)
+    writes = (rng.random(n) < write_p).astype(np.uint8)
+    address, nbytes, op = to_accesses(pages, writes, rng)
+    arrival = np.cumsum(rng.exponential(20.0, n).astype(np.uint64) + 1).astype(np.uint64)
+    hit_w, victim_w, dirty_w = ho.lru(pages, writes, frames)
+    p = wl.c0_profile()
+    p["capacity_bytes"] = 64 << 30
+    s = Setup(profile=p, model=3, stacks=1, stripe=4096)
+    s.ranges = [(wl.RANGE_BASE, 63 << 30, 2, 3)]
+    oracle = OracleRun(s)
+    ctx = capacity_context(str(tmp_path), frames)
+    cut = n // 3
+    for k, (lo, hi) in enumerate(((0, cut), (cut, n))):
+        dev = [torch.from_numpy(address[lo:hi].view(np.int64)).cuda(),
+               torch.from_numpy(nbytes[lo:hi].view(np.int32)).cuda(),
+               torch.from_numpy(op[lo:hi]).cuda(),
+               torch.from_numpy(arrival[lo:hi].view(np.int64)).cuda()]
+        hit, victim, dirty, status, done, latency = ctx.submit_capacity(*dev, timed=True)
+        done = done.cpu().numpy().view(np.uint64)
+        latency = latency.cpu().numpy().view(np.uint64)
+        assert np.array_equal(hit.cpu().numpy(), hit_w[lo:hi])
+        want_done, want_lat = ho.capacity_timing(
+            oracle.geometry, oracle.timing, oracle.chan_bw, oracle.t_read, oracle.t_prog,
+            oracle.admit, np.ones(hi - lo, np.uint8), hit_w[lo:hi], pages[lo:hi],
+            victim_w[lo:hi], dirty_w[lo:hi], arrival[lo:hi], 12, oracle.state)
+        bad = np.flatnonzero(done != want_done)
+        assert bad.size == 0, f"batch {k}: done differs at {bad[:5]}: {done[bad[:5]]} vs {want_done[bad[:5]]}"
+        assert np.array_equal(latency, want_lat)
+        chained = int((dirty_w[lo:hi] == 1).sum())
+        assert chained > 0
+    assert np.array_equal(ctx.get_state(), oracle.state)
+    ctx.close()
