@@ -958,7 +958,7 @@ int hbfsim_capacity_configure_v1(hbfsim_context* c, uint64_t frames, uint32_t pa
     media.reserved = page_log;
     media.end = media.base + media.length;
     media.ok = 1;
-    media.timing = 1;
+    media.timing = 3;  // reads and writes
     if (grow(&s->res_page, frames) || grow(&s->res_dirty, frames) ||
         grow(&s->counts, kCapCounts) || grow(&s->media_range, 1) ||
         cudaMemcpy(s->media_range, &media, sizeof media, cudaMemcpyHostToDevice) != cudaSuccess) {

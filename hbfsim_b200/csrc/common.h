@@ -44,9 +44,10 @@ struct DevRange {
     u32 mode;
     u32 permissions;
     u32 reserved;      // log2(page_bytes)
-    u64 end;           // base + length (meaningful when `ok`)
-    u32 ok;            // mode 1 or 2, 0 < page_bytes <= 2^32, no end overflow
-    u32 timing;        // ok and mode 1 (timing range)
+    u64 end;           // base + length (registration rejects an overflow)
+    u32 ok;            // mode 1 or 2, 0 < page_bytes <= 2^32
+    u32 timing;        // timing path: bit op set = operation op allowed
+                       // (ok, mode 1, permission bit); 0 for other ranges
 };
 static_assert(sizeof(DevRange) == 64, "range record layout");
 

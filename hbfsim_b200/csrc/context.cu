@@ -527,7 +527,7 @@ int hbfsim_register_device(hbfsim_context* c, void* device_ptr, size_t length,
     r.reserved = log2u(page);
     r.end = base + length;
     r.ok = (r.mode == 1 || r.mode == 2) && page != 0 && page <= 0xffffffffull ? 1u : 0u;
-    r.timing = r.ok && r.mode == HBFSIM_RANGE_MODE_TIMING ? 1u : 0u;
+    r.timing = r.ok && r.mode == HBFSIM_RANGE_MODE_TIMING ? (r.permissions & 3u) : 0u;
     c->ranges.insert(at, r);
     const int rc = upload_ranges(c);
     if (rc != HBFSIM_OK) {

@@ -185,23 +185,73 @@ __device__ __forceinline__ TimingDecoded classify_timing(const DecodeParams& p, 
 {
     TimingDecoded d{kUnsupported, 0, 0};
     if (bytes == 0) return d;                                  // hbf_device.cu:997-1003
-    const u32 index = find_range_index(p.ranges, p.range_count, a);
-    if (index == p.range_count || a - p.ranges[index].base >= p.ranges[index].length) {
+    const u32 index = p.range_count == 1 ? (p.ranges[0].base <= a ? 0u : 1u)
+                                         : find_range_index(p.ranges, p.range_count, a);
+    const u64 offset = index < p.range_count ? a - p.ranges[index].base : 0;
+    if (index == p.range_count || offset >= p.ranges[index].length) {
         const u32 successor = index == p.range_count ? 0u : index + 1u;  // 1083-1127
         d.status = successor < p.range_count && range_overlaps(p.ranges[successor], a, bytes)
                        ? kUnsupported : kBypass;
         return d;
     }
     const DevRange& r = p.ranges[index];
-    // access_supported (hbf_device.cuh:843-862) with the static range checks
-    // folded into r.ok; a >= base and a - base < length hold here
-    if (op > 1 || !r.ok || bytes > ~u64{0} - a || a + bytes > r.end ||
-        (r.permissions & (1u << op)) == 0)
+    // access_supported (hbf_device.cuh:843-862) and media_descriptor
+    // (929-944).  Registration guarantees base + length and file_offset +
+    // length do not overflow, so with offset < length the reference's
+    // overflow checks reduce to bytes <= length - offset, and r.timing holds
+    // the operations a timing range allows.
+    if (op > 1 || ((r.timing >> op) & 1u) == 0 || bytes > r.length - offset) return d;
+    const u64 page_mask = (u64{1} << r.reserved) - 1;
+    if ((offset & page_mask) + bytes > page_mask + 1) return d;   // one page only
+    const u32 u = static_cast<u32>((r.file_offset + offset) >> p.stripe_shift);
+    u32 g;
+    if (p.pow2) {
+        g = (u >> p.chan_shift) & p.chan_mask;
+        d.die = (u >> p.die_shift) & p.die_mask;
+        d.local = g >> p.shard_shift;
+        d.status = (g & p.shard_mask) == p.shard_rank ? kModeled : kForeign;
+    } else {
+        const u32 uc = fastdiv_q(u, p.chan_stride);
+        g = uc - fastdiv_q(uc, p.radix[0]) * p.radix[0].d;
+        const u32 ud = fastdiv_q(u, p.die_stride);
+        d.die = ud - fastdiv_q(ud, p.radix[2]) * p.radix[2].d;
+        const u32 lq = fastdiv_q(g, p.shard_div);
+        d.local = lq;
+        d.status = p.shard_count > 1 && g - lq * p.shard_div.d != p.shard_rank ? kForeign
+                                                                                 : kModeled;
+    }
+    return d;
+}
+
+// The same classification for a context with one registered range, its
+// record held in registers (hoisted out of the tile loop).
+struct RangeRegs {
+    u64 base, length, file_offset, page_mask;
+    u32 allowed;  // DevRange::timing
+};
+
+__device__ __forceinline__ RangeRegs range_regs(const DevRange& r)
+{
+    return RangeRegs{r.base, r.length, r.file_offset, (u64{1} << r.reserved) - 1, r.timing};
+}
+
+__device__ __forceinline__ TimingDecoded classify_single(const RangeRegs& r,
+                                                         const DecodeParams& p, u64 a,
+                                                         u32 bytes, u32 op)
+{
+    TimingDecoded d{kUnsupported, 0, 0};
+    if (bytes == 0) return d;                                  // hbf_device.cu:997-1003
+    if (a < r.base) {  // not in the range: straddles into it, or bypass
+        d.status = a <= ~u64{0} - bytes && r.base < a + bytes ? kUnsupported : kBypass;
         return d;
+    }
     const u64 offset = a - r.base;
-    if ((offset >> r.reserved) != ((offset + bytes - 1) >> r.reserved)) return d;
-    if (((offset >> r.reserved) << r.reserved) > ~u64{0} - r.file_offset || !r.timing)
-        return d;                                               // media_descriptor
+    if (offset >= r.length) {
+        d.status = kBypass;
+        return d;
+    }
+    if (op > 1 || ((r.allowed >> op) & 1u) == 0 || bytes > r.length - offset) return d;
+    if ((offset & r.page_mask) + bytes > r.page_mask + 1) return d;
     const u32 u = static_cast<u32>((r.file_offset + offset) >> p.stripe_shift);
     u32 g;
     if (p.pow2) {
@@ -272,13 +322,17 @@ struct ChanInfo {  // per local channel, staged in shared memory
 // access never exceeds its page (access_supported), and the host admits the
 // parallel path only when a page's transfer times the scale stays below
 // 2^24, so the plain product is exact here.
+__device__ __noinline__ u64 transfer_ticks_div(u32 bytes, u64 bw)
+{
+    return ceil_div_u64(static_cast<u64>(bytes) * 1000000000ull, bw);
+}
+
 __device__ __forceinline__ u64 transfer_ticks(u32 bytes, const ChanInfo& ci, u32 scale)
 {
-    u64 x;
-    if (ci.x_exact)
-        x = (static_cast<u64>(bytes) + (u64{1} << ci.x_shift) - 1) >> ci.x_shift;
-    else
-        x = ceil_div_u64(static_cast<u64>(bytes) * 1000000000ull, ci.bw);
+    // the division stays out of line: per-channel rates are almost always
+    // 1e9 / 2^k bytes per second
+    const u64 x = ci.x_exact ? (static_cast<u64>(bytes) + ((u64{1} << ci.x_shift) - 1)) >> ci.x_shift
+                             : transfer_ticks_div(bytes, ci.bw);
     return x * scale;
 }
 
@@ -478,6 +532,8 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
 
     DecodeParams dp = A.dp;
     if (dp.range_count <= kSmemRanges) dp.ranges = s.ranges;
+    const bool single = dp.range_count == 1;
+    const RangeRegs rr = single ? range_regs(dp.ranges[0]) : RangeRegs{};
     const u32 chunk = T / kWarps;
     bool unsorted = false;
     for (u32 j = 0; j < chunk; j += 32) {
@@ -496,7 +552,7 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
             }
             TimingDecoded d;
             if (MODEL == kModelDie) {
-                d = classify_timing(dp, a, b, o);
+                d = single ? classify_single(rr, dp, a, b, o) : classify_timing(dp, a, b, o);
             } else {
                 const Decoded f = classify_decode(dp, a, b, o, false);
                 d = TimingDecoded{f.status, 0u, 0u};
