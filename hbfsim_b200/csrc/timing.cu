@@ -718,8 +718,6 @@ __device__ __forceinline__ void load_records(const PassArgs& A, const TileSmem& 
             atomicAdd(&s.seg[c], 1u);
             ++st.modeled;
         } else {
-            s.addr[j] = s.arr[j];  // done = arrival
-            s.arr[j] = 0;          // latency 0
             if (status == kBypass) ++st.bypass;
             else if (status == kForeign) ++st.foreign;
             else ++st.unsup;
@@ -730,18 +728,29 @@ __device__ __forceinline__ void load_records(const PassArgs& A, const TileSmem& 
     __syncthreads();
 }
 
-// Pass 2 after the chains: completion ticks back to access order
-// (s.addr = done, s.arr = latency) and the latency statistics.
-__device__ __forceinline__ void scatter_results(const TileSmem& s, u32 nt, Stats7& st)
+// Pass 2 after the chains: each thread takes accesses in access order,
+// gathers the completion tick of a timed access from the sorted copy, and
+// stores done / latency / status straight to the outputs (coalesced);
+// accesses that are not timed complete at their arrival.
+__device__ __forceinline__ void write_results(const PassArgs& A, const TileSmem& s, u64 start,
+                                              u32 nt, Stats7& st)
 {
+    u64* done_out = A.done + start;
+    u64* lat_out = A.latency + start;
+    u8* status_out = A.status + start;
     for (u32 j = threadIdx.x; j < nt; j += kThreads) {
-        if (s.op[j] != kModeled) continue;
-        const u64 done = static_cast<u64>(s.sarr[record_slot(s.addr[j])]);
-        const u64 lat = done - s.arr[j];
-        s.addr[j] = done;
-        s.arr[j] = lat;
-        st.lat += lat;
-        st.max = done > st.max ? done : st.max;
+        const u8 status = s.op[j];
+        const u64 arr = s.arr[j];
+        u64 done = arr, lat = 0;
+        if (status == kModeled) {
+            done = static_cast<u64>(s.sarr[record_slot(s.addr[j])]);
+            lat = done - arr;
+            st.lat += lat;
+            st.max = done > st.max ? done : st.max;
+        }
+        __stcs(reinterpret_cast<unsigned long long*>(done_out + j), done);
+        __stcs(reinterpret_cast<unsigned long long*>(lat_out + j), lat);
+        status_out[j] = status;
     }
 }
 
@@ -1082,10 +1091,7 @@ direct_pass_kernel(const PassArgs args)
             }
         }
         __syncthreads();
-        if (PASS == 2) {
-            scatter_results(s, nt, st);
-            __syncthreads();
-        }
+        if (PASS == 2) write_results(A, s, start, nt, st);
         if (PASS == 1) {
             // snapshot column 0, then let die columns try to couple to it
 #pragma unroll
@@ -1103,8 +1109,6 @@ direct_pass_kernel(const PassArgs args)
                 coupled[it] = try_couple<D>(s_col0 + static_cast<u64>(item_c[it]) * K,
                                             reg[it], delta[it]);
             }
-        } else {
-            store_tile(A, s, start, nt);
         }
         __syncthreads();
     }
