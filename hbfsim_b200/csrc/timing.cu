@@ -618,14 +618,18 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
         if (e < nt) {
             const u32 key = s.key[e];
             if (SORTED) {
-                // sorted position into s.rank (for the records), and the
-                // shifted channel-sorted copy that the chains read
+                // the shifted channel-sorted copy that the chains read, and
+                // the access's record for pass 2 (format at record_slot)
                 const u32 pos = key < C ? s.wcnt[warp * (C + 1) + key] + s.rank[e] : 0u;
-                s.rank[e] = static_cast<u16>(pos);
+                const u32 info = s.bytes[e];
                 if (key < C) {
-                    s.sinfo[pos + key] = s.bytes[e];
+                    s.sinfo[pos + key] = info;
                     s.sarr[pos + key] = imax(static_cast<i64>(s.arr[e]), s.chan[key].admit);
                 }
+                __stcs(reinterpret_cast<unsigned long long*>(A.latency + start + e),
+                       static_cast<u64>(info) | (static_cast<u64>(pos) << 32) |
+                           (static_cast<u64>(s.op[e]) << 48) |
+                           (static_cast<u64>(key & 0xffu) << 56));
             } else if (key < C) {
                 s.ord[s.wcnt[warp * (C + 1) + key] + s.rank[e]] = static_cast<u16>(e);
             }
@@ -660,22 +664,13 @@ __device__ __forceinline__ void store_tile(const PassArgs& A, const TileSmem& s,
 }
 
 // Compact per-access records that pass 1 of the direct kernel leaves for
-// pass 2 in the caller's latency buffer (overwritten by pass 2 with the
-// latency):  bits 0-31  packed step info of access j (transfer | die | op),
+// pass 2 in the caller's latency buffer (written by the sorted partition in
+// load_decode_partition; overwritten by pass 2 with the latency):
+//            bits 0-31  packed step info of access j (transfer | die | op),
 //            bits 32-47 channel-sorted position of access j,
 //            bits 48-55 status of access j,
 //            bits 56-63 local channel of access j (C < 256 in direct mode).
 // Pass 2 rebuilds the tile's partition from them without decoding again.
-__device__ __forceinline__ void write_records(const PassArgs& A, const TileSmem& s, u64 start,
-                                              u32 nt)
-{
-    const u32 tid = threadIdx.x;
-    u64* rec = A.latency + start;
-    for (u32 j = tid; j < nt; j += kThreads)
-        rec[j] = static_cast<u64>(s.bytes[j]) | (static_cast<u64>(s.rank[j]) << 32) |
-                 (static_cast<u64>(s.op[j]) << 48) | (static_cast<u64>(s.key[j] & 0xffu) << 56);
-}
-
 __device__ __forceinline__ u32 record_slot(u64 r)
 {
     return static_cast<u32>((r >> 32) & 0xffffu) + static_cast<u32>(r >> 56);
@@ -1067,7 +1062,6 @@ direct_pass_kernel(const PassArgs args)
         const u32 nt = static_cast<u32>(A.n - start < T ? A.n - start : T);
         if (PASS == 1) {
             load_decode_partition<kModelDie, 1, true>(A, s, start, nt, activity, st);
-            write_records(A, s, start, nt);
         } else {
             load_records(A, s, start, nt, st);
         }
