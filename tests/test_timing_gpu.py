@@ -303,3 +303,36 @@ def test_hybrid_sampler_bits(tmp):
         assert np.array_equal(got, want), f"batch {k}"
         assert 0 < want.sum() < (dec["status"] == 1).sum()
     ctx.close()
+
+
+@pytest.mark.parametrize("rank,shards", [(0, 8), (5, 8), (1, 2)])
+def test_config4_shard(tmp, rank, shards):
+    """Config-4 geometry (16 stacks x 16 channels x 8 dies x 4 planes) as one
+    rank of an N-GPU run: a mixed trace of the config-1 (expert streaming)
+    and config-2 (paged KV) patterns interleaved by arrival; the rank times
+    its channels bit-exactly and marks the others' accesses foreign."""
+    p = wl.c4_profile()
+    s = Setup(profile=p, model=3, stacks=16, stripe=4096, shard_rank=rank, shard_count=shards)
+    s.ranges = [(wl.RANGE_BASE, 120 << 30, 1, 3)]
+    rng = np.random.default_rng(rank + 10 * shards)
+    bases, counts = wl.c1_segments(seed=rank, steps=1, layers=2)
+    moe = wl.expand_segments(bases, counts)
+    lengths = wl.c2_lengths(seed=rank, seqs=32, lmin=512, lmax=2048)
+    kv_addr, kv_bytes, kv_op = wl.c2_step(lengths, 0, 4, layers=2, base=wl.RANGE_BASE + (64 << 30))
+    n1, n2 = moe[0].size, kv_addr.size
+    # interleave by arrival: 60 % expert reads, 40 % KV page accesses
+    take = min(n1, int(n2 * 1.5))
+    order = np.argsort(np.r_[np.arange(take) / 0.6, np.arange(int(take / 1.5)) / 0.4],
+                       kind="stable")
+    address = np.r_[moe[0][:take], kv_addr[:int(take / 1.5)]][order]
+    nbytes = np.r_[moe[1][:take], kv_bytes[:int(take / 1.5)]][order]
+    op = np.r_[moe[2][:take], kv_op[:int(take / 1.5)]][order]
+    arrival = np.arange(address.size, dtype=np.uint64)
+    arrays = (address.astype(np.uint64), nbytes.astype(np.uint32), op.astype(np.uint8), arrival)
+    ctx = make_context(s, tmp)
+    ora = OracleRun(s)
+    got = gpu_run(ctx, arrays)
+    want = ora.run(*arrays, threads=8)
+    assert_same(got, want, f"c4 rank {rank}/{shards}")
+    assert (want[2] == 9).sum() > 0 and (want[2] == 1).sum() > 0
+    assert np.array_equal(ctx.get_state(), ora.state)
