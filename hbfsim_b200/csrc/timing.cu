@@ -297,6 +297,7 @@ struct PassArgs {
     u32 off_wcnt, off_seg, off_pbase, off_pchan, off_pm, off_pin, off_die;
     u32 off_chan, off_act, off_red, off_ranges;
     u32 off_sarr[2], off_sinfo[2];  // direct kernel: channel-sorted arrays per pass
+    u32 off_slot;                   // direct replay: sorted slot of each access
     // global scratch
     i64* agg;        // [ctas][C][K][K+1]  (pass 1 out)
     i64* incoming;   // [ctas][C][K]       (pass 2 in, carried in place)
@@ -1132,6 +1133,139 @@ direct_pass_kernel(const PassArgs args)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Direct replay (pass 2 of the direct kernel), streamed.  Thread c < C
+// carries channel c's exact state through the CTA's tiles.  Per tile: the
+// staged records and arrivals are unpacked into the shifted channel-sorted
+// copy (and each access's slot in it); statuses and the outputs of untimed
+// accesses go straight out.  Then -- while the chains run and the outputs are
+// written -- the next tile's records and arrivals stream into the staging
+// buffers with cp.async.  The outputs of timed accesses are written in access
+// order (coalesced), their arrival re-read from global memory (in L2).
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
+{
+    const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(gmem_src));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+__device__ __forceinline__ void cp_async_wait_all()
+{
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+}
+
+// Stage tile [start, start + nt) (records from the latency buffer, arrivals):
+// asynchronously when the tile is full and the buffers are 16-byte aligned.
+__device__ __forceinline__ void stage_records(const PassArgs& A, const TileSmem& s, u64 start,
+                                              u32 nt)
+{
+    const u32 tid = threadIdx.x, T = A.T;
+    const u64* rec = A.latency + start;
+    if (nt == T && A.vec) {
+        const uint4* g_arr = reinterpret_cast<const uint4*>(A.arrival + start);
+        const uint4* g_rec = reinterpret_cast<const uint4*>(rec);
+        uint4* d_arr = reinterpret_cast<uint4*>(s.arr);
+        uint4* d_rec = reinterpret_cast<uint4*>(s.addr);
+        for (u32 k = tid; k < T / 2; k += kThreads) {
+            cp_async16(d_arr + k, g_arr + k);
+            cp_async16(d_rec + k, g_rec + k);
+        }
+        cp_async_commit();
+    } else {
+        for (u32 k = tid; k < nt; k += kThreads) {
+            s.arr[k] = A.arrival[start + k];
+            s.addr[k] = rec[k];
+        }
+    }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 3)
+direct_replay_kernel(const PassArgs args)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    const PassArgs& A = args;
+    const u32 tid = threadIdx.x;
+    constexpr u32 K = D + 1;
+    const u32 T = A.T, C = A.C;
+    const TileSmem s = tile_views(smem, A, 2);
+    u16* slot_of = reinterpret_cast<u16*>(smem + A.off_slot);  // access -> sorted slot
+    if (*A.error != 0) return;  // pass 1 refused or rerouted the batch
+    prologue(A, s, true, false, false);
+
+    DieRegs<D> reg;
+    const bool chain = tid < C;
+    if (chain) {
+        const i64* cv = A.incoming + (static_cast<u64>(blockIdx.x) * C + tid) * K;
+        reg.chan = cv[0];
+#pragma unroll
+        for (int j = 0; j < D; ++j) reg.die[j] = cv[1 + j];
+    }
+    Stats7 st;
+    const u64 tile_first = static_cast<u64>(blockIdx.x) * A.tiles_per_cta;
+    auto tile_size = [&](u64 start) -> u32 {
+        return static_cast<u32>(A.n - start < T ? A.n - start : T);
+    };
+    if (tile_first * T < A.n) stage_records(A, s, tile_first * T, tile_size(tile_first * T));
+    for (u32 tt = 0; tt < A.tiles_per_cta; ++tt) {
+        const u64 start = (tile_first + tt) * T;
+        if (start >= A.n) break;
+        const u32 nt = tile_size(start);
+        cp_async_wait_all();
+        for (u32 c = tid; c <= C; c += kThreads) s.seg[c] = 0;
+        __syncthreads();
+        // unpack: sorted copy, access -> slot, statuses, untimed outputs
+        for (u32 j = tid; j < nt; j += kThreads) {
+            const u64 r = s.addr[j];
+            const u64 arr = s.arr[j];
+            const u32 status = static_cast<u32>(r >> 48) & 0xffu;
+            A.status[start + j] = static_cast<u8>(status);
+            if (status == kModeled) {
+                const u32 k = record_slot(r);
+                s.sinfo[k] = static_cast<u32>(r);
+                s.sarr[k] = imax(static_cast<i64>(arr), s.chan[r >> 56].admit);
+                slot_of[j] = static_cast<u16>(k);
+                atomicAdd(&s.seg[r >> 56], 1u);
+                ++st.modeled;
+            } else {
+                slot_of[j] = 0xffffu;
+                __stcs(reinterpret_cast<unsigned long long*>(A.done + start + j), arr);
+                __stcs(reinterpret_cast<unsigned long long*>(A.latency + start + j), 0ull);
+                if (status == kBypass) ++st.bypass;
+                else if (status == kForeign) ++st.foreign;
+                else ++st.unsup;
+            }
+        }
+        __syncthreads();
+        warp0_exclusive_scan(s.seg, C, &s.seg[C]);
+        __syncthreads();
+        // the staging buffers are free: stream the next tile in
+        const u64 next = start + T;
+        if (tt + 1 < A.tiles_per_cta && next < A.n) stage_records(A, s, next, tile_size(next));
+        if (chain) {
+            const u32 c = tid;
+            const u32 first = s.seg[c] + c, last = s.seg[c + 1] + c;  // shifted segment
+            const ChanInfo ci = s.chan[c];
+#pragma unroll 4
+            for (u32 k = first; k < last; ++k) s.sarr[k] = reg.step(s.sarr[k], s.sinfo[k], ci);
+        }
+        __syncthreads();
+        // outputs of the timed accesses, in access order
+        for (u32 j = tid; j < nt; j += kThreads) {
+            const u32 k = slot_of[j];
+            if (k == 0xffffu) continue;
+            const u64 done = static_cast<u64>(s.sarr[k]);
+            const u64 lat = done - __ldcg(reinterpret_cast<const unsigned long long*>(A.arrival) +
+                                          start + j);
+            __stcs(reinterpret_cast<unsigned long long*>(A.done + start + j), done);
+            __stcs(reinterpret_cast<unsigned long long*>(A.latency + start + j), lat);
+            st.lat += lat;
+            st.max = done > st.max ? done : st.max;
+        }
+        // the next iteration's barrier keeps the sorted copy until this is done
+    }
+    flush_stats(A, s, st, false);
+}
+
 // Range scan: incoming_b = R_{b-1} ... R_0 (state), one CTA per local
 // channel (channels are independent).  The CTA stages a chunk of its
 // channel's range aggregates in shared memory with coalesced loads; warp 0
@@ -1397,6 +1531,7 @@ static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
         off = tail;
         a.off_sarr[1] = take(8 * (T + C));
         a.off_sinfo[1] = take(4 * (T + C));
+        a.off_slot = take(2 * T);
         const u32 end2 = align_up(off, 16);
         return end1 > end2 ? end1 : end2;
     }
@@ -1529,10 +1664,10 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
         Kernel p2 = fast ? timing_pass_kernel<kModelFast, 2> : timing_pass_kernel<kModelDie, 2>;
         if (plan.direct) {
             switch (plan.dies) {
-            case 1: p1 = direct_pass_kernel<1, 1>; p2 = direct_pass_kernel<2, 1>; break;
-            case 2: p1 = direct_pass_kernel<1, 2>; p2 = direct_pass_kernel<2, 2>; break;
-            case 4: p1 = direct_pass_kernel<1, 4>; p2 = direct_pass_kernel<2, 4>; break;
-            default: p1 = direct_pass_kernel<1, 8>; p2 = direct_pass_kernel<2, 8>; break;
+            case 1: p1 = direct_pass_kernel<1, 1>; p2 = direct_replay_kernel<1>; break;
+            case 2: p1 = direct_pass_kernel<1, 2>; p2 = direct_replay_kernel<2>; break;
+            case 4: p1 = direct_pass_kernel<1, 4>; p2 = direct_replay_kernel<4>; break;
+            default: p1 = direct_pass_kernel<1, 8>; p2 = direct_replay_kernel<8>; break;
             }
         }
         for (auto k : {p1, p2}) {
