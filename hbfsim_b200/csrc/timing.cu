@@ -677,79 +677,6 @@ __device__ __forceinline__ u32 record_slot(u64 r)
     return static_cast<u32>((r >> 32) & 0xffffu) + static_cast<u32>(r >> 56);
 }
 
-// Pass 2: stage the arrivals and the records of one tile, rebuild the
-// shifted channel-sorted arrays, count the channel segments, and fill in the
-// outputs of the accesses that are not timed (done = arrival, latency 0).
-__device__ __forceinline__ void load_records(const PassArgs& A, const TileSmem& s, u64 start,
-                                             u32 nt, Stats7& st)
-{
-    const u32 tid = threadIdx.x, T = A.T, C = A.C;
-    const u64* rec = A.latency + start;
-    if (nt == T && A.vec) {
-        const uint4* g_arr = reinterpret_cast<const uint4*>(A.arrival + start);
-        const uint4* g_rec = reinterpret_cast<const uint4*>(rec);
-        uint4* d_arr = reinterpret_cast<uint4*>(s.arr);
-        uint4* d_rec = reinterpret_cast<uint4*>(s.addr);
-        for (u32 k = tid; k < T / 2; k += kThreads) {
-            d_arr[k] = __ldcs(g_arr + k);
-            d_rec[k] = __ldcs(g_rec + k);
-        }
-    } else {
-        for (u32 k = tid; k < nt; k += kThreads) {
-            s.arr[k] = A.arrival[start + k];
-            s.addr[k] = rec[k];
-        }
-    }
-    for (u32 c = tid; c <= C; c += kThreads) s.seg[c] = 0;
-    __syncthreads();
-    for (u32 j = tid; j < nt; j += kThreads) {
-        const u64 r = s.addr[j];
-        const u32 status = static_cast<u32>(r >> 48) & 0xffu;
-        s.op[j] = static_cast<u8>(status);
-        if (status == kModeled) {
-            const u32 c = static_cast<u32>(r >> 56);
-            const u32 k = record_slot(r);
-            s.sinfo[k] = static_cast<u32>(r);
-            s.sarr[k] = imax(static_cast<i64>(s.arr[j]), s.chan[c].admit);
-            atomicAdd(&s.seg[c], 1u);
-            ++st.modeled;
-        } else {
-            if (status == kBypass) ++st.bypass;
-            else if (status == kForeign) ++st.foreign;
-            else ++st.unsup;
-        }
-    }
-    __syncthreads();
-    warp0_exclusive_scan(s.seg, C, &s.seg[C]);
-    __syncthreads();
-}
-
-// Pass 2 after the chains: each thread takes accesses in access order,
-// gathers the completion tick of a timed access from the sorted copy, and
-// stores done / latency / status straight to the outputs (coalesced);
-// accesses that are not timed complete at their arrival.
-__device__ __forceinline__ void write_results(const PassArgs& A, const TileSmem& s, u64 start,
-                                              u32 nt, Stats7& st)
-{
-    u64* done_out = A.done + start;
-    u64* lat_out = A.latency + start;
-    u8* status_out = A.status + start;
-    for (u32 j = threadIdx.x; j < nt; j += kThreads) {
-        const u8 status = s.op[j];
-        const u64 arr = s.arr[j];
-        u64 done = arr, lat = 0;
-        if (status == kModeled) {
-            done = static_cast<u64>(s.sarr[record_slot(s.addr[j])]);
-            lat = done - arr;
-            st.lat += lat;
-            st.max = done > st.max ? done : st.max;
-        }
-        __stcs(reinterpret_cast<unsigned long long*>(done_out + j), done);
-        __stcs(reinterpret_cast<unsigned long long*>(lat_out + j), lat);
-        status_out[j] = status;
-    }
-}
-
 // Block-reduce the pass-2 statistics and the die activity; one atomic each
 // per CTA.
 __device__ __forceinline__ void flush_stats(const PassArgs& A, const TileSmem& s,
@@ -967,12 +894,9 @@ timing_pass_kernel(const PassArgs args)
 }
 
 // ---------------------------------------------------------------------------
-// Direct kernel (die model, D dies known at compile time, enough channels
-// for parallelism): no pieces.
-//
-// Pass 2: thread c carries channel c's exact state through every tile of the
-// CTA's range, one step per access, on the partition rebuilt from pass 1's
-// records (load_records).
+// Direct kernels (die model, D dies known at compile time, enough channels
+// for parallelism): no pieces.  Pass 1 is direct_pass_kernel<1, D>, pass 2
+// direct_replay_kernel<D> below.
 //
 // Pass 1: item (r, c) carries column r of channel c's range aggregate.  Items
 // are laid out r-major so that a warp holds one kind of column.  Column 0
@@ -1012,46 +936,39 @@ template <int PASS, int D>
 __global__ void __launch_bounds__(kThreads, 3)
 direct_pass_kernel(const PassArgs args)
 {
+    static_assert(PASS == 1, "pass 2 of the direct path is direct_replay_kernel");
     extern __shared__ __align__(16) unsigned char smem[];
     const PassArgs& A = args;
     const u32 tid = threadIdx.x;
     constexpr u32 K = D + 1, KK = D + 2;
     const u32 T = A.T, C = A.C;
-    const TileSmem s = tile_views(smem, A, PASS);
-    i64* s_col0 = reinterpret_cast<i64*>(smem + A.off_pm);  // [C][K], pass 1
-    if (PASS == 2 && *A.error != 0) return;
+    const TileSmem s = tile_views(smem, A, 1);
+    i64* s_col0 = reinterpret_cast<i64*>(smem + A.off_pm);  // [C][K]
     // activity is counted where the access sizes are decoded (pass 1) and
     // staged until the range scan accepts the batch
-    const bool activity = PASS == 1 && A.tp.act_stage != nullptr;
-    prologue(A, s, true, activity, PASS == 1);
+    const bool activity = A.tp.act_stage != nullptr;
+    prologue(A, s, true, activity, true);
 
-    constexpr int kItems = PASS == 1 ? 2 : 1;
+    constexpr int kItems = 2;
     DieRegs<D> reg[kItems];
     u32 item_c[kItems], item_r[kItems];
     bool item_on[kItems], coupled[kItems];
     i64 delta[kItems];
     i64* agg = A.agg + static_cast<u64>(blockIdx.x) * C * K * KK;
-    i64* carry = A.incoming + static_cast<u64>(blockIdx.x) * C * K;
 #pragma unroll
     for (int it = 0; it < kItems; ++it) {
         const u32 q = tid + it * kThreads;
-        item_on[it] = PASS == 1 ? q < C * KK : q < C;
-        item_r[it] = PASS == 1 ? q / C : 0;
-        item_c[it] = PASS == 1 ? q % C : q;
+        item_on[it] = q < C * KK;
+        item_r[it] = q / C;
+        item_c[it] = q % C;
         coupled[it] = false;
         delta[it] = 0;
         if (!item_on[it]) continue;
-        if (PASS == 1) {  // identity column e_r (r == K: no constant yet)
-            reg[it].chan = item_r[it] == 0 ? 0 : kNeg;
+        // identity column e_r (r == K: no constant yet)
+        reg[it].chan = item_r[it] == 0 ? 0 : kNeg;
 #pragma unroll
-            for (int j = 0; j < D; ++j)
-                reg[it].die[j] = item_r[it] == static_cast<u32>(j + 1) ? 0 : kNeg;
-        } else {
-            const i64* cv = carry + static_cast<u64>(item_c[it]) * K;
-            reg[it].chan = cv[0];
-#pragma unroll
-            for (int j = 0; j < D; ++j) reg[it].die[j] = cv[1 + j];
-        }
+        for (int j = 0; j < D; ++j)
+            reg[it].die[j] = item_r[it] == static_cast<u32>(j + 1) ? 0 : kNeg;
     }
     __syncthreads();
     Stats7 st;
@@ -1061,76 +978,59 @@ direct_pass_kernel(const PassArgs args)
         const u64 start = (tile_first + tt) * T;
         if (start >= A.n) break;
         const u32 nt = static_cast<u32>(A.n - start < T ? A.n - start : T);
-        if (PASS == 1) {
-            load_decode_partition<kModelDie, 1, true>(A, s, start, nt, activity, st);
-        } else {
-            load_records(A, s, start, nt, st);
-        }
+        load_decode_partition<kModelDie, 1, true>(A, s, start, nt, activity, st);
 #pragma unroll
         for (int it = 0; it < kItems; ++it) {
             if (!item_on[it] || coupled[it]) continue;
             const u32 c = item_c[it];
             const u32 first = s.seg[c] + c, last = s.seg[c + 1] + c;  // shifted segment
             const ChanInfo ci = s.chan[c];
-            if (PASS == 1) {
-                if (item_r[it] == K) {
+            if (item_r[it] == K) {
 #pragma unroll 4
-                    for (u32 k = first; k < last; ++k) reg[it].step(s.sarr[k], s.sinfo[k], ci);
-                } else {
-#pragma unroll 4
-                    for (u32 k = first; k < last; ++k) reg[it].step(kNeg, s.sinfo[k], ci);
-                }
+                for (u32 k = first; k < last; ++k) reg[it].step(s.sarr[k], s.sinfo[k], ci);
             } else {
 #pragma unroll 4
-                for (u32 k = first; k < last; ++k) s.sarr[k] = reg[it].step(s.sarr[k], s.sinfo[k], ci);
+                for (u32 k = first; k < last; ++k) reg[it].step(kNeg, s.sinfo[k], ci);
             }
         }
         __syncthreads();
-        if (PASS == 2) write_results(A, s, start, nt, st);
-        if (PASS == 1) {
-            // snapshot column 0, then let die columns try to couple to it
-#pragma unroll
-            for (int it = 0; it < kItems; ++it) {
-                if (!item_on[it] || item_r[it] != 0) continue;
-                i64* v0 = s_col0 + static_cast<u64>(item_c[it]) * K;
-                v0[0] = reg[it].chan;
-#pragma unroll
-                for (int j = 0; j < D; ++j) v0[1 + j] = reg[it].die[j];
-            }
-            __syncthreads();
-#pragma unroll
-            for (int it = 0; it < kItems; ++it) {
-                if (!item_on[it] || coupled[it] || item_r[it] == 0 || item_r[it] == K) continue;
-                coupled[it] = try_couple<D>(s_col0 + static_cast<u64>(item_c[it]) * K,
-                                            reg[it], delta[it]);
-            }
-        }
-        __syncthreads();
-    }
-    if (PASS == 1) {
-        // s_col0 holds column 0 after the last tile of the range
+        // snapshot column 0, then let die columns try to couple to it
 #pragma unroll
         for (int it = 0; it < kItems; ++it) {
-            if (!item_on[it]) continue;
-            const u32 c = item_c[it], r = item_r[it];
-            i64* col = agg + static_cast<u64>(c) * K * KK + r;
-            if (coupled[it]) {
-                const i64* v0 = s_col0 + static_cast<u64>(c) * K;
+            if (!item_on[it] || item_r[it] != 0) continue;
+            i64* v0 = s_col0 + static_cast<u64>(item_c[it]) * K;
+            v0[0] = reg[it].chan;
 #pragma unroll
-                for (int i = 0; i <= D; ++i)
-                    col[i * KK] = is_neg_inf(v0[i]) ? kNeg : v0[i] + delta[it];
-            } else {
-                col[0] = reg[it].chan;
-#pragma unroll
-                for (int j = 0; j < D; ++j) col[(j + 1) * KK] = reg[it].die[j];
-            }
+            for (int j = 0; j < D; ++j) v0[1 + j] = reg[it].die[j];
         }
-        if (activity)
-            for (u32 k = tid; k < 2 * C * D; k += kThreads)
-                if (s.act[k]) atomicAdd(&A.tp.act_stage[k], s.act[k]);
-    } else {
-        flush_stats(A, s, st, false);
+        __syncthreads();
+#pragma unroll
+        for (int it = 0; it < kItems; ++it) {
+            if (!item_on[it] || coupled[it] || item_r[it] == 0 || item_r[it] == K) continue;
+            coupled[it] = try_couple<D>(s_col0 + static_cast<u64>(item_c[it]) * K, reg[it],
+                                        delta[it]);
+        }
+        __syncthreads();
     }
+    // s_col0 holds column 0 after the last tile of the range
+#pragma unroll
+    for (int it = 0; it < kItems; ++it) {
+        if (!item_on[it]) continue;
+        const u32 c = item_c[it], r = item_r[it];
+        i64* col = agg + static_cast<u64>(c) * K * KK + r;
+        if (coupled[it]) {
+            const i64* v0 = s_col0 + static_cast<u64>(c) * K;
+#pragma unroll
+            for (int i = 0; i <= D; ++i) col[i * KK] = is_neg_inf(v0[i]) ? kNeg : v0[i] + delta[it];
+        } else {
+            col[0] = reg[it].chan;
+#pragma unroll
+            for (int j = 0; j < D; ++j) col[(j + 1) * KK] = reg[it].die[j];
+        }
+    }
+    if (activity)
+        for (u32 k = tid; k < 2 * C * D; k += kThreads)
+            if (s.act[k]) atomicAdd(&A.tp.act_stage[k], s.act[k]);
 }
 
 // ---------------------------------------------------------------------------
