@@ -18,7 +18,8 @@
 //         -> one nz-point tridiagonal solve per (p, q) mode (Thomas)
 //         -> inverse DCT (two more GEMMs).
 // Accuracy is that of the transforms (~1e-14 relative), well inside the
-// 1e-9 tolerance against the sparse direct solve of the oracle.
+// 1e-9 tolerance against the sparse direct solve of the oracle.  The GEMMs
+// run on the double-precision tensor cores.
 #include "context.h"
 
 #include <algorithm>
@@ -99,46 +100,93 @@ void thermal_destroy(ThermalState* t)
 
 namespace {
 
-constexpr int kTile = 32;
-
-// C[b] = op(A[b]) * op(B[b]), fp64, 32x32 tiles in shared memory.
+// C[b] = op(A[b]) * op(B[b]) in fp64 on the double-precision tensor cores
+// (mma.sync m8n8k4 .f64; the tcgen05 instructions have no fp64 kind).
 // op(X) = X or X^T; row-major storage with leading dimension = columns.
-__global__ void dgemm_kernel(int M, int N, int K, const double* A, long long sa, int ta,
-                             const double* B, long long sb, int tb, double* C,
-                             long long sc)
+// CTA tile 32 x 32 (enough CTAs for the small transforms of the grid), K
+// step 32, four warps of 16 x 16 (2 x 2 MMA tiles).  Fragment layout of
+// m8n8k4 .f64 (PTX ISA): lane = 4 g + t holds A(g, t), B(t, g) and C(g, 2t),
+// C(g, 2t + 1).
+constexpr int kBM = 32, kBN = 32, kBK = 32;
+
+__device__ __forceinline__ void dmma_8x8x4(double& c0, double& c1, double a, double b)
 {
-    __shared__ double as[kTile][kTile + 1];
-    __shared__ double bs[kTile][kTile + 1];
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};\n"
+                 : "+d"(c0), "+d"(c1)
+                 : "d"(a), "d"(b));
+}
+
+__global__ void __launch_bounds__(128) dgemm_kernel(int M, int N, int K, const double* A,
+                                                    long long sa, int ta, const double* B,
+                                                    long long sb, int tb, double* C, long long sc)
+{
+    __shared__ double as[kBK][kBM + 1];  // as[k][m] = op(A)(m, k)
+    __shared__ double bs[kBK][kBN + 1];  // bs[k][n] = op(B)(k, n)
     const double* a = A + sa * blockIdx.z;
     const double* b = B + sb * blockIdx.z;
     double* c = C + sc * blockIdx.z;
-    const int row = blockIdx.y * kTile + threadIdx.y;
-    const int col = blockIdx.x * kTile + threadIdx.x;
-    double acc = 0.0;
-    for (int k0 = 0; k0 < K; k0 += kTile) {
-        const int ka = k0 + threadIdx.x;  // A(row, ka)
-        const int kb = k0 + threadIdx.y;  // B(kb, col)
-        double va = 0.0, vb = 0.0;
-        if (row < M && ka < K) va = ta ? a[static_cast<long long>(ka) * M + row]
-                                       : a[static_cast<long long>(row) * K + ka];
-        if (kb < K && col < N) vb = tb ? b[static_cast<long long>(col) * K + kb]
-                                       : b[static_cast<long long>(kb) * N + col];
-        as[threadIdx.y][threadIdx.x] = va;
-        bs[threadIdx.y][threadIdx.x] = vb;
+    const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int wm = (warp >> 1) * 16, wn = (warp & 1) * 16;
+    double acc[2][2][2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) acc[i][j][0] = acc[i][j][1] = 0.0;
+    for (int k0 = 0; k0 < K; k0 += kBK) {
+        // global loads run along the contiguous dimension of each operand
+#pragma unroll 4
+        for (int idx = tid; idx < kBK * kBM; idx += 128) {
+            int m, k;
+            if (ta) { k = idx / kBM; m = idx % kBM; } else { m = idx / kBK; k = idx % kBK; }
+            const int gm = m0 + m, gk = k0 + k;
+            as[k][m] = gm < M && gk < K ? (ta ? a[static_cast<long long>(gk) * M + gm]
+                                             : a[static_cast<long long>(gm) * K + gk])
+                                        : 0.0;
+        }
+#pragma unroll 4
+        for (int idx = tid; idx < kBK * kBN; idx += 128) {
+            int n, k;
+            if (tb) { n = idx / kBK; k = idx % kBK; } else { k = idx / kBN; n = idx % kBN; }
+            const int gn = n0 + n, gk = k0 + k;
+            bs[k][n] = gk < K && gn < N ? (tb ? b[static_cast<long long>(gn) * K + gk]
+                                             : b[static_cast<long long>(gk) * N + gn])
+                                        : 0.0;
+        }
         __syncthreads();
-#pragma unroll 8
-        for (int k = 0; k < kTile; ++k) acc = fma(as[threadIdx.y][k], bs[k][threadIdx.x], acc);
+#pragma unroll
+        for (int kk = 0; kk < kBK; kk += 4) {
+            double fa[2], fb[2];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) fa[i] = as[kk + t][wm + i * 8 + g];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) fb[j] = bs[kk + t][wn + j * 8 + g];
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int j = 0; j < 2; ++j) dmma_8x8x4(acc[i][j][0], acc[i][j][1], fa[i], fb[j]);
+        }
         __syncthreads();
     }
-    if (row < M && col < N) c[static_cast<long long>(row) * N + col] = acc;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int row = m0 + wm + i * 8 + g;
+        if (row >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int col = n0 + wn + j * 8 + 2 * t;
+            if (col < N) c[static_cast<long long>(row) * N + col] = acc[i][j][0];
+            if (col + 1 < N) c[static_cast<long long>(row) * N + col + 1] = acc[i][j][1];
+        }
+    }
 }
 
 void dgemm(int M, int N, int K, const double* A, long long sa, int ta, const double* B,
            long long sb, int tb, double* C, long long sc, int batch, cudaStream_t s)
 {
-    dim3 grid((N + kTile - 1) / kTile, (M + kTile - 1) / kTile, batch);
-    dim3 block(kTile, kTile);
-    dgemm_kernel<<<grid, block, 0, s>>>(M, N, K, A, sa, ta, B, sb, tb, C, sc);
+    dim3 grid((N + kBN - 1) / kBN, (M + kBM - 1) / kBM, batch);
+    dgemm_kernel<<<grid, 128, 0, s>>>(M, N, K, A, sa, ta, B, sb, tb, C, sc);
 }
 
 // die power: idle + (read bytes * J/B + writes * J/write) / dt
