@@ -51,7 +51,6 @@ struct ThermalState {
     double* d_die_cells = nullptr;
     int* d_die_start = nullptr;  // cells of die d: d_die_list[start[d] .. start[d+1])
     int* d_die_list = nullptr;
-    double* d_die_power = nullptr;
     double* d_die_temp = nullptr;
     std::uint32_t* d_level = nullptr;    // throttle level per stack
     std::uint32_t* d_refresh = nullptr;  // per local channel (permille)
@@ -89,7 +88,7 @@ void thermal_destroy(ThermalState* t)
                     static_cast<void*>(t->d_qx), static_cast<void*>(t->d_qy),
                     static_cast<void*>(t->d_t), static_cast<void*>(t->d_w0),
                     static_cast<void*>(t->d_w1), static_cast<void*>(t->d_cell_die),
-                    static_cast<void*>(t->d_die_cells), static_cast<void*>(t->d_die_power),
+                    static_cast<void*>(t->d_die_cells),
                     static_cast<void*>(t->d_die_start), static_cast<void*>(t->d_die_list),
                     static_cast<void*>(t->d_die_temp), static_cast<void*>(t->d_level),
                     static_cast<void*>(t->d_refresh), static_cast<void*>(t->d_throttle),
@@ -189,28 +188,23 @@ void dgemm(int M, int N, int K, const double* A, long long sa, int ta, const dou
     dgemm_kernel<<<grid, 128, 0, s>>>(M, N, K, A, sa, ta, B, sb, tb, C, sc);
 }
 
-// die power: idle + (read bytes * J/B + writes * J/write) / dt
-__global__ void die_power_kernel(const unsigned long long* rb, const unsigned long long* wr,
-                                 int dies, double idle, double jpb, double jpw, double dt,
-                                 double* power)
-{
-    const int d = blockIdx.x * blockDim.x + threadIdx.x;
-    if (d >= dies) return;
-    const double e = static_cast<double>(rb[d]) * jpb + static_cast<double>(wr[d]) * jpw;
-    power[d] = idle + e / dt;
-}
-
 // rhs = C/dt T + P + G_b T_amb
-__global__ void rhs_kernel(const double* t, const int* cell_die, const double* die_power,
-                           const double* die_cells, const double* cap, const double* gb,
-                           const double* tb, int plane, long long cells, double dt,
-                           double* rhs)
+// with the owning die's power (die_power_kernel's formula) folded in
+__global__ void rhs_kernel(const double* t, const int* cell_die,
+                           const unsigned long long* rb, const unsigned long long* wr,
+                           double idle, double jpb, double jpw, const double* die_cells,
+                           const double* cap, const double* gb, const double* tb, int plane,
+                           long long cells, double dt, double* rhs)
 {
     const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= cells) return;
     const int z = static_cast<int>(i / plane);
     const int d = cell_die[i];
-    const double p = d >= 0 ? die_power[d] / die_cells[d] : 0.0;
+    double p = 0.0;
+    if (d >= 0) {
+        const double e = static_cast<double>(rb[d]) * jpb + static_cast<double>(wr[d]) * jpw;
+        p = (idle + e / dt) / die_cells[d];
+    }
     rhs[i] = cap[z] / dt * t[i] + p + gb[z] * tb[z];
 }
 
@@ -292,6 +286,10 @@ struct ControllerArgs {
     i64* t_admit;
     std::uint64_t read_latency, program_latency;
     unsigned time_scale;
+    // this context's die activity, cleared for the next epoch
+    unsigned long long* act_read;
+    unsigned long long* act_write;
+    int act_words;
 };
 
 __device__ std::uint64_t sat_mul_dev(std::uint64_t a, std::uint64_t b)
@@ -353,6 +351,10 @@ __global__ void controller_kernel(ControllerArgs a)
         a.t_prog[c] = static_cast<i64>(sat_mul_dev(tp, a.time_scale));
         a.t_admit[c] = static_cast<i64>(a.admit[stack]);
     }
+    for (int k = tid; k < a.act_words; k += blockDim.x * gridDim.x) {
+        a.act_read[k] = 0;
+        a.act_write[k] = 0;
+    }
 }
 
 template <typename T>
@@ -381,12 +383,10 @@ int advance(hbfsim_context* c, double epoch_s, const unsigned long long* rb,
     const auto& cfg = t->cfg;
     auto hooks = c->hooks();
     hooks(kSlotThermal, 0, s);
-    die_power_kernel<<<(t->dies_total + 255) / 256, 256, 0, s>>>(
-        rb, wr, static_cast<int>(t->dies_total), cfg.die_idle_w, cfg.read_j_per_byte,
-        cfg.write_j_per_access, dt, t->d_die_power);
     rhs_kernel<<<static_cast<unsigned>((t->cells + 255) / 256), 256, 0, s>>>(
-        t->d_t, t->d_cell_die, t->d_die_power, t->d_die_cells, t->d_cap, t->d_gb, t->d_tb,
-        plane, static_cast<long long>(t->cells), dt, t->d_w0);
+        t->d_t, t->d_cell_die, rb, wr, cfg.die_idle_w, cfg.read_j_per_byte,
+        cfg.write_j_per_access, t->d_die_cells, t->d_cap, t->d_gb, t->d_tb, plane,
+        static_cast<long long>(t->cells), dt, t->d_w0);
     // forward: W1 = W0 Qx (rows = nz*ny), then W0_z = Qy^T W1_z
     dgemm(t->nz * t->ny, t->nx, t->nx, t->d_w0, 0, 0, t->d_qx, 0, 0, t->d_w1, 0, 1, s);
     dgemm(t->ny, t->nx, t->ny, t->d_qy, 0, 1, t->d_w1, plane, 0, t->d_w0, plane, t->nz, s);
@@ -433,16 +433,15 @@ int advance(hbfsim_context* c, double epoch_s, const unsigned long long* rb,
     a.read_latency = c->profile.read_latency_ns;
     a.program_latency = c->profile.program_latency_ns;
     a.time_scale = c->profile.time_scale;
+    a.act_read = c->d_die_read_bytes;
+    a.act_write = c->d_die_writes;
+    a.act_words = static_cast<int>(static_cast<std::uint64_t>(c->C) * std::max(1u, c->D));
     hooks(kSlotController, 0, s);
     controller_kernel<<<1, 1024, 0, s>>>(a);
     hooks(kSlotController, 1, s);
     // the admission tick bound used by the host's path choice
     t->admit_bound = std::max<std::uint64_t>(t->admit_bound, a.next_epoch_end);
     c->admit_max = std::max<std::uint64_t>(c->admit_max, t->admit_bound);
-    const std::uint64_t dies_local = static_cast<std::uint64_t>(c->C) * std::max(1u, c->D);
-    if (cudaMemsetAsync(c->d_die_read_bytes, 0, 8 * dies_local, s) ||
-        cudaMemsetAsync(c->d_die_writes, 0, 8 * dies_local, s))
-        return HBFSIM_CUDA_ERROR;
     return cudaGetLastError() == cudaSuccess ? HBFSIM_OK : HBFSIM_CUDA_ERROR;
 }
 
@@ -565,7 +564,7 @@ int hbfsim_thermal_configure_v1(hbfsim_context* c, const hbfsim_thermal_config_v
               !alloc(&t->d_w0, cells) && !alloc(&t->d_w1, cells) &&
               !alloc(&t->d_cell_die, cells) && !alloc(&t->d_die_cells, dies) &&
               !alloc(&t->d_die_start, dies + 1ull) && !alloc(&t->d_die_list, cells) &&
-              !alloc(&t->d_die_power, dies) && !alloc(&t->d_die_temp, dies) &&
+              !alloc(&t->d_die_temp, dies) &&
               !alloc(&t->d_level, c->stacks) && !alloc(&t->d_refresh, c->C) &&
               !alloc(&t->d_throttle, c->stacks) && !alloc(&t->d_admit, c->stacks);
     auto up = [&](void* dst, const void* src, std::size_t bytes) {
