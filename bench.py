@@ -532,7 +532,71 @@ def run_extras(args, device, tmp):
                               "factor_ms": (t1 - t0) * 1e3, "cores": 1, "kind": "port",
                               "sample": "scipy splu factor once, then 3 solves"}
     out["thermal_step"] = th
+    out["thermal_coupled"] = run_c3(args, device, tmp)
     return out
+
+
+def run_c3(args, device, tmp):
+    """Config 3 at full size: the config-0 trace tiled to 100 ms of arrivals
+    (about 5e7 accesses), timed epoch by epoch (1 ms) with the factors the
+    previous epoch's temperatures produced; each epoch closes with one step of
+    the 9 x 128 x 128 fp64 grid and the refresh / throttle controller."""
+    import torch
+    from hbfsim_b200 import Context, workloads as wl
+    p = wl.c0_profile()
+    p["name"] = "bench-c3t"
+    w = wl.Workload("c3t", p, 1, STRIPE, wl.RANGE_BASE, 64 << 30)
+    ctx = Context(w.write_profile(tmp), report_dir=f"{tmp}/report-c3t", mode=3)
+    ctx.register_device(wl.RANGE_BASE, 64 << 30, 1, 3)
+    stack, fp = c3_grid()
+    ctx.thermal_configure(stack, fp, {"idle_w": 0.5, "read_j_per_byte": 2e-9 / 128,
+                                      "write_j_per_access": 50e-9},
+                          {"onset_k": 343.15, "step_k": 10.0, "base_permille": 10,
+                           "cap_permille": 500},
+                          {"light_k": 358.15, "severe_k": 368.15, "shutdown_k": 378.15,
+                           "hysteresis_k": 2.0, "light_permille": 1500,
+                           "severe_permille": 3000})
+    a, b, o, t = wl.c0_trace(1 << 20, seed=0)
+    span = int(t[-1]) + 1
+    epoch_ns, epochs = 1_000_000, 100
+    reps = -(-epochs * epoch_ns // span)
+    dev = lambda x, dt: torch.from_numpy(np.ascontiguousarray(x).view(dt)).to(device)
+    address = dev(np.tile(a, reps), np.int64)
+    nbytes = dev(np.tile(b, reps), np.int32)
+    op = dev(np.tile(o, reps), np.uint8)
+    arrival = (dev(t, np.int64).repeat(reps) +
+               torch.arange(reps, device=device, dtype=torch.int64).repeat_interleave(t.size) * span)
+    cuts = torch.searchsorted(arrival, torch.arange(epochs + 1, device=device,
+                                                    dtype=torch.int64) * epoch_ns).cpu().tolist()
+    n = cuts[-1]
+    from hbfsim_b200 import BatchResult
+    out = BatchResult(torch.empty(n, dtype=torch.int64, device=device),
+                      torch.empty(n, dtype=torch.int64, device=device),
+                      torch.empty(n, dtype=torch.uint8, device=device))
+    stream = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(epochs):
+        lo, hi = cuts[k], cuts[k + 1]
+        if hi > lo:
+            part = BatchResult(out.done_ns[lo:hi], out.latency_ns[lo:hi], out.status[lo:hi])
+            ctx.submit(address[lo:hi], nbytes[lo:hi], op[lo:hi], arrival[lo:hi], part, stream)
+        ctx.advance_epoch(epoch_ns * 1e-9, stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    ctx.flush()
+    refresh, throttle, _, levels = ctx.thermal_factors(16, 1)
+    temps = ctx.die_temperatures(64)
+    ctx.close()
+    return {"workload": "config 3: config-0 trace tiled to 100 ms (%d accesses), 100 epochs "
+                        "of 1 ms, 9 x 128 x 128 fp64 grid, 64 dies" % n,
+            "accesses": n, "epochs": epochs, "ms_total": ms, "ms_per_epoch": ms / epochs,
+            "value": n / (ms * 1e-3), "unit": "accesses/s (timing and thermal coupled)",
+            "final_max_die_temp_k": float(temps.max()),
+            "final_refresh_permille_max": int(refresh.max()),
+            "final_throttle_level": int(levels.max())}
 
 
 def c3_grid():
