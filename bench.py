@@ -222,7 +222,7 @@ def reference_arm(args):
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    print_result(line)
     return 0
 
 
@@ -260,7 +260,27 @@ def bench_config(args, world, n):
               % (n * IN_BYTES / 1e9)}
 
 
+# The JSON result line is the only thing on standard output: libraries that
+# write there (NCCL prints its version on some setups) are sent to stderr.
+_RESULT_OUT = None
+
+
+def _claim_stdout():
+    global _RESULT_OUT
+    if _RESULT_OUT is None:
+        sys.stdout.flush()
+        _RESULT_OUT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
+
+
+def print_result(line: dict) -> None:
+    out = _RESULT_OUT if _RESULT_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main():
+    _claim_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=40)
@@ -646,7 +666,7 @@ def emit(args, world, n, ms_max, e2e_rate, same, kernels, launches, dominant, ac
         "per_step_totals": {"modeled": int(tot[0]), "bypass": int(tot[1]),
                             "unsupported": int(tot[2]), "foreign": int(tot[3])},
     }
-    print(json.dumps(line), flush=True)
+    print_result(line)
 
 
 if __name__ == "__main__":
