@@ -1,7 +1,8 @@
 """Regenerate the golden fixtures in this directory from the HBFSim reference.
 
-Run in a container that holds the HBFSim source tree (default
-/root/reference, override with HBFSIM_REFERENCE):
+Run where the HBFSim source tree is available (its location comes from the
+HBFSIM_REFERENCE environment variable, with the build container's reference
+mount as the default):
 
     make -C oracle            # builds oracle/_ref/ref_goldens from reference sources
     python tests/golden/make_goldens.py
