@@ -241,13 +241,11 @@ __device__ __forceinline__ TimingDecoded classify_single(const RangeRegs& r,
 {
     TimingDecoded d{kUnsupported, 0, 0};
     if (bytes == 0) return d;                                  // hbf_device.cu:997-1003
-    if (a < r.base) {  // not in the range: straddles into it, or bypass
-        d.status = a <= ~u64{0} - bytes && r.base < a + bytes ? kUnsupported : kBypass;
-        return d;
-    }
-    const u64 offset = a - r.base;
+    const u64 offset = a - r.base;  // wraps when a < base
     if (offset >= r.length) {
-        d.status = kBypass;
+        // below the range: unsupported if it straddles into it; else bypass
+        d.status = a < r.base && a <= ~u64{0} - bytes && r.base < a + bytes ? kUnsupported
+                                                                           : kBypass;
         return d;
     }
     if (op > 1 || ((r.allowed >> op) & 1u) == 0 || bytes > r.length - offset) return d;
@@ -315,8 +313,8 @@ struct ChanInfo {  // per local channel, staged in shared memory
     i64 t_prog;
     i64 admit;
     u64 bw;
-    u32 x_shift;   // transfer = ceil(bytes / 2^x_shift) when x_exact
-    u32 x_exact;   // 1e9 / bw reduces to 1 / 2^x_shift
+    u32 x_add;     // transfer = (bytes + x_add) >> x_shift, x_add = 2^x_shift - 1,
+    u32 x_shift;   // when 1e9 / bw reduces to 1 / 2^x_shift; else x_shift = kXDivide
 };
 
 // ceil(bytes * 1e9 / bw) * time_scale for one access of a channel.  An
@@ -328,13 +326,18 @@ __device__ __noinline__ u64 transfer_ticks_div(u32 bytes, u64 bw)
     return ceil_div_u64(static_cast<u64>(bytes) * 1000000000ull, bw);
 }
 
+constexpr u32 kXDivide = 0xffu;
+
 __device__ __forceinline__ u64 transfer_ticks(u32 bytes, const ChanInfo& ci, u32 scale)
 {
     // the division stays out of line: per-channel rates are almost always
-    // 1e9 / 2^k bytes per second
-    const u64 x = ci.x_exact ? (static_cast<u64>(bytes) + ((u64{1} << ci.x_shift) - 1)) >> ci.x_shift
-                             : transfer_ticks_div(bytes, ci.bw);
-    return x * scale;
+    // 1e9 / 2^k bytes per second.  bytes < 2^32, so the quotient fits 32 bits.
+    const uint2 code = *reinterpret_cast<const uint2*>(&ci.x_add);
+    if (code.y != kXDivide) {
+        const u32 x = static_cast<u32>((static_cast<u64>(bytes) + code.x) >> code.y);
+        return static_cast<u64>(x) * scale;
+    }
+    return transfer_ticks_div(bytes, ci.bw) * scale;
 }
 
 __device__ ChanInfo stage_channel(const TimingParams& tp, u32 c, bool die)
@@ -349,9 +352,11 @@ __device__ ChanInfo stage_channel(const TimingParams& tp, u32 c, bool die)
     u64 a = 1000000000ull, b = ci.bw;
     while (b) { const u64 r = a % b; a = b; b = r; }
     const u64 num = 1000000000ull / a, den = ci.bw / a;
-    if (num == 1 && (den & (den - 1)) == 0) {
-        ci.x_exact = 1;
+    ci.x_shift = kXDivide;
+    ci.x_add = 0;
+    if (num == 1 && (den & (den - 1)) == 0 && 63 - __clzll(den) < 32) {
         ci.x_shift = 63 - __clzll(den);
+        ci.x_add = static_cast<u32>((u64{1} << ci.x_shift) - 1);
     }
     return ci;
 }
@@ -537,20 +542,26 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
     const RangeRegs rr = single ? range_regs(dp.ranges[0]) : RangeRegs{};
     const u32 chunk = T / kWarps;
     bool unsorted = false;
+    u64 arr_max = 0;  // arrivals from 2^59 on take the sequential kernel
+    // the arrival before this tile (previous tile, or the previous batch)
+    const u64 tile_prev = PASS == 1 && warp == 0 && lane == 0
+                              ? (start > 0 ? A.arrival[start - 1] : *A.last_arrival)
+                              : 0;
     for (u32 j = 0; j < chunk; j += 32) {
         const u32 e = warp * chunk + j + lane;
         u32 key = C;
+        const u64 arr = e < nt ? s.arr[e] : 0;
+        if (PASS == 1) {
+            // previous arrival: the lane below, else the element before the chunk
+            u64 prev = __shfl_up_sync(0xffffffffu, arr, 1);
+            if (lane == 0) prev = e > 0 ? s.arr[e - 1] : tile_prev;
+            if (e < nt && arr < prev) unsorted = true;
+            arr_max = arr > arr_max ? arr : arr_max;
+        }
         if (e < nt) {
             const u64 a = s.addr[e];
             const u32 b = s.bytes[e];
             const u32 o = s.op[e];
-            const u64 arr = s.arr[e];
-            if (PASS == 1) {
-                const u64 prev = e > 0 ? s.arr[e - 1]
-                                       : (start > 0 ? A.arrival[start - 1] : *A.last_arrival);
-                if (arr < prev && !A.tp.any_order) unsorted = true;
-                if (arr >= kArrivalLimit) atomicOr(A.error, kErrNeedSeq);
-            }
             TimingDecoded d;
             if (MODEL == kModelDie) {
                 d = single ? classify_single(rr, dp, a, b, o) : classify_timing(dp, a, b, o);
@@ -593,7 +604,8 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
         }
         __syncwarp();
     }
-    if (PASS == 1 && unsorted) atomicOr(A.error, kErrUnsorted);
+    if (PASS == 1 && unsorted && !A.tp.any_order) atomicOr(A.error, kErrUnsorted);
+    if (PASS == 1 && arr_max >= kArrivalLimit) atomicOr(A.error, kErrNeedSeq);
     __syncthreads();
 
     // segment offsets: key-major, warp-minor
