@@ -553,7 +553,70 @@ def run_extras(args, device, tmp):
                               "sample": "scipy splu factor once, then 3 solves"}
     out["thermal_step"] = th
     out["thermal_coupled"] = run_c3(args, device, tmp)
+    out["empirical_vmem"] = run_vmem(args, device, tmp)
     return out
+
+
+def run_vmem(args, device, tmp):
+    """The FAST model with an empirical burst-curve profile (cd8p-shaped
+    curve, 4 KiB pages): one batch of 2^25 page accesses in sequential streaks
+    (mean 48 pages), timed from a reset state each step."""
+    import torch
+    from hbfsim_b200 import BatchResult, Context, workloads as wl
+    p = wl.vmem_profile()
+    w = wl.Workload("vmem", p, 1, 4096, wl.RANGE_BASE, 15 << 30)
+    ctx = Context(w.write_profile(tmp), report_dir=f"{tmp}/report-vmem", mode=1)
+    ctx.register_device(wl.RANGE_BASE, 15 << 30, 1, 3)
+    n = 1 << 25
+    host = wl.vmem_trace(n, seed=0)
+    dev = [torch.from_numpy(x.view(dt)).to(device)
+           for x, dt in zip(host, (np.int64, np.int32, np.uint8, np.int64))]
+    out = BatchResult(torch.empty(n, dtype=torch.int64, device=device),
+                      torch.empty(n, dtype=torch.int64, device=device),
+                      torch.empty(n, dtype=torch.uint8, device=device))
+    stream = torch.cuda.current_stream()
+    for _ in range(3):
+        ctx.reset_state(stream)
+        ctx.submit(*dev, out=out, stream=stream)
+    torch.cuda.synchronize()
+    ctx.kernel_times()
+    ctx.set_profiling(True)
+    times = []
+    for _ in range(10):
+        ctx.reset_state(stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        ctx.submit(*dev, out=out, stream=stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    kt = ctx.kernel_times()
+    ctx.set_profiling(False)
+    stats = ctx.batch_stats()
+    ctx.close()
+    ms = statistics.median(times)
+    res = {"workload": "empirical burst curve (cd8p-shaped, FAST model): 2^25 page accesses, "
+                       "sequential streaks of mean 48 pages, 5 percent write streaks",
+           "accesses": n, "ms_per_batch": ms, "value": n / (ms * 1e-3), "unit": "accesses/s",
+           "kernels": {k: {"launches": v[0], "avg_ms": v[1] / max(1, v[0])}
+                       for k, v in kt.items() if v[0]},
+           "achieved_gbs_38B_per_access": 38 * n / (ms * 1e-3) / 1e9,
+           "device_errors": stats["device_errors"]}
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, str(REPO / "oracle"))
+        import hbf_oracle as ho
+        m = 1 << 22
+        curve = p["empirical_vmem"]["read_curve"]
+        e = ho.make_empirical([c["pages"] for c in curve], [c["cumulative_ns"] for c in curve],
+                              p["program_latency_ns"])
+        ranges = ho.make_ranges([(wl.RANGE_BASE, 15 << 30, 0, 1, 1, 3, 4096)])
+        state = np.zeros(2, np.uint64)
+        t0 = time.perf_counter()
+        ho.run_empirical(ranges, 1, e, 1, 10**9, *(x[:m] for x in host), state)
+        dt = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": m / dt, "unit": "accesses/s", "cores": 1,
+                               "kind": "port", "sample": f"first {m} accesses, single thread"}
+    return res
 
 
 def run_c3(args, device, tmp):

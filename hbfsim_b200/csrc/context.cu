@@ -231,7 +231,8 @@ int configure_geometry(hbfsim_context* c, std::uint32_t stacks,
     const std::string& s = p.plane_allocation_scheme;
     for (int k = 0; k < 4; ++k)
         c->order[k] = s[k] == 'C' ? 0 : s[k] == 'W' ? 1 : s[k] == 'D' ? 2 : 3;
-    const std::uint64_t words = static_cast<std::uint64_t>(c->C) * c->K;
+    // FAST with an empirical profile: one more word, the packed burst state
+    const std::uint64_t words = static_cast<std::uint64_t>(c->C) * c->K + (c->empirical ? 1 : 0);
     if (dalloc(&c->d_state[0], words) || dalloc(&c->d_state[1], words) ||
         dalloc(&c->d_chan_bw, c->C) || dalloc(&c->d_t_read, c->C) ||
         dalloc(&c->d_t_prog, c->C) || dalloc(&c->d_admit, c->C) ||
@@ -353,11 +354,63 @@ void mark_launch(void* owner, int slot, int phase, cudaStream_t stream)
 
 bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
 
+// Empirical burst-curve profile: the control-header check and the service
+// of every run length (hbf_device.cuh:978-1128), on the profile's curve.
+// An invalid header makes every timed access Unsupported, as the reference's
+// resolve_fast_or_hybrid does (hbf_device.cu:773-777, 797-801).
+int setup_empirical(hbfsim_context* c)
+{
+    const Profile& p = c->profile;
+    std::uint32_t pages[6];
+    std::uint64_t cum[6];
+    for (int i = 0; i < 6; ++i) {
+        pages[i] = p.empirical[i].pages;
+        cum[i] = p.empirical[i].cumulative_ns;
+    }
+    std::vector<std::uint64_t> table(kRunCap + 1, 0);
+    empirical_service_table(pages, cum, 6, table.data());
+    const bool valid = empirical_control_valid(1, 6, p.program_latency_ns, pages, cum);
+    c->emp.ok = valid && p.time_scale != 0 && c->request_timeout_ns != 0 ? 1u : 0u;
+    c->emp.program_ns = p.program_latency_ns;
+    c->emp.time_scale = p.time_scale;
+    std::uint64_t largest = p.program_latency_ns;
+    for (std::uint32_t r = 1; r <= kRunCap; ++r) largest = std::max(largest, table[r]);
+    c->emp_scaled_max = c->emp.ok ? sat_mul(largest, p.time_scale) : 0;
+    if (dalloc(&c->d_emp_service, kRunCap + 1) || dalloc(&c->d_emp_words, kEmpScratchWords) ||
+        cudaMemcpy(c->d_emp_service, table.data(), 8 * table.size(), cudaMemcpyHostToDevice) !=
+            cudaSuccess)
+        return HBFSIM_CUDA_ERROR;
+    c->emp.service = c->d_emp_service;
+    return HBFSIM_OK;
+}
+
+// One batch of the empirical FAST model (device arrays).  Bound proof: the
+// batch adds at most n times the largest scaled service; below 2^59 (with
+// arrivals and the carried tail checked below 2^59 on the device) no tick
+// reaches 2^60 and the parallel kernels are exact.
+int run_empirical_batch(hbfsim_context* c, const BatchIO& io, cudaStream_t stream,
+                        std::uint32_t* error, const LaunchHooks& hooks)
+{
+    const bool sequential =
+        sat_mul(c->emp_scaled_max, io.n) >= static_cast<std::uint64_t>(kArrivalLimit);
+    EmpiricalScratch s{};
+    s.words = c->d_emp_words;
+    s.error = error;
+    s.last_arrival = c->d_last_arrival;
+    s.counters = c->d_counters;
+    s.state_in = c->d_state[c->cur];
+    s.state_out = c->d_state[1 - c->cur];
+    const cudaError_t err = launch_empirical(decode_params(c), c->emp, io, s, sequential,
+                                             c->sm_count, stream, hooks);
+    if (err != cudaSuccess) return HBFSIM_CUDA_ERROR;
+    c->cur = 1 - c->cur;
+    return HBFSIM_OK;
+}
+
 int model_supported(const hbfsim_context* c)
 {
     if (c->mode != HBFSIM_MODEL_FAST && c->mode != HBFSIM_MODEL_DIE_V1)
         return HBFSIM_UNSUPPORTED;  // REFERENCE/HYBRID need MQSim
-    if (c->profile.has_empirical && is_fast(c)) return HBFSIM_UNSUPPORTED;
     return HBFSIM_OK;
 }
 
@@ -369,6 +422,10 @@ int run_device_batch(hbfsim_context* c, const BatchIO& io, cudaStream_t stream,
                      const DevRange* ranges = nullptr, std::uint32_t range_count = 0)
 {
     if (io.n == 0) return HBFSIM_OK;
+    if (c->empirical) {
+        if (ranges) return HBFSIM_UNSUPPORTED;  // media actions: die model only
+        return run_empirical_batch(c, io, stream, c->d_error, c->hooks());
+    }
     // Bound proof for the parallel path.  Pass 1 checks on the device that
     // every arrival and every carried state word is below 2^59; here the host
     // checks that the admission ticks are too and that the batch can add less
@@ -480,7 +537,9 @@ int hbfsim_context_create(const hbfsim_options* options, hbfsim_context** out)
     cudaMemset(c->d_last_arrival, 0, sizeof(std::uint64_t));
     cudaMemset(c->d_counters, 0, sizeof(DevCounters));
     cudaMemset(c->d_sample_seq, 0, sizeof(std::uint64_t));
-    const int rc = configure_geometry(c, 1, 0, 0, 1);
+    c->empirical = is_fast(c) && profile.has_empirical;
+    int rc = configure_geometry(c, 1, 0, 0, 1);
+    if (rc == HBFSIM_OK && c->empirical) rc = setup_empirical(c);
     if (rc != HBFSIM_OK) {
         hbfsim_context_destroy(c);
         return rc;
@@ -629,6 +688,8 @@ void hbfsim_context_destroy(hbfsim_context* c)
     dfree(c->d_counters);
     dfree(c->d_sample_seq);
     dfree(c->d_sample_counts);
+    dfree(c->d_emp_service);
+    dfree(c->d_emp_words);
     for (auto& p : c->d_stage) {
         if (p) cudaFree(p);
         p = nullptr;
@@ -1031,6 +1092,11 @@ extern "C" int hbfsim_submit_access_batch_static_v1(hbfsim_context* c,
     io.aligned = aligned16(io.address) && aligned16(io.bytes) && aligned16(io.op) &&
                  aligned16(io.arrival) && aligned16(io.done) && aligned16(io.latency) &&
                  aligned16(io.status);
+    if (c->empirical) {  // scratch allocated with the context
+        cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+        return run_empirical_batch(c, io, st, reinterpret_cast<std::uint32_t*>(base),
+                                   LaunchHooks{});
+    }
     // the same bound proof as the allocating entry point
     const std::uint64_t growth = sat_mul(sat_add(c->x_max, c->t_max), io.n);
     const bool sequential = growth >= static_cast<std::uint64_t>(kArrivalLimit) ||

@@ -2,6 +2,7 @@
 #pragma once
 
 #include "../../include/hbfsim/batch_v1.h"
+#include "empirical.h"
 #include "profile.h"
 #include "timing.h"
 
@@ -82,6 +83,15 @@ struct hbfsim_context {
     cudaStream_t copy_out = nullptr;
     void* d_stage[2] = {nullptr, nullptr};
     std::uint64_t stage_capacity = 0;  // accesses per stage
+
+    // FAST model with an empirical burst-curve profile: read service per run
+    // length (device table), per-batch scratch, bound of one scaled service.
+    // The state then holds one more word: the packed burst state.
+    bool empirical = false;
+    hbfb::EmpiricalParams emp{};
+    std::uint64_t* d_emp_service = nullptr;
+    std::uint64_t* d_emp_words = nullptr;
+    std::uint64_t emp_scaled_max = 0;
 
     hbfb::ThermalState* thermal = nullptr;
     hbfb::CapacityState* capacity = nullptr;  // Capacity-mode LRU (capacity.cu)

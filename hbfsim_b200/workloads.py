@@ -59,6 +59,72 @@ def c0_profile() -> dict:
     }
 
 
+def vmem_profile(pages=(1, 4, 16, 64, 256, 512),
+                 cumulative=(11_133, 41_495, 168_606, 2_824_351, 10_767_793, 20_254_374),
+                 program_ns: int = 408_305, time_scale: int = 1) -> dict:
+    """A FAST-model profile with an empirical burst curve (the schema's
+    empirical_vmem block): 4 KiB pages, P50 cumulative read time of a run of
+    k sequential pages at six breakpoints, the shape of the reference's
+    cd8p-vmem-p50 profile.  The source hash is a placeholder."""
+    curve = [{"pages": int(k), "cumulative_ns": int(c), "p95_ns": int(c)}
+             for k, c in zip(pages, cumulative)]
+    return {
+        "name": "vmem-burst",
+        "capacity_bytes": 16 * GIB,
+        "page_bytes": 4096,
+        "read_latency_ns": int(cumulative[0]),
+        "program_latency_ns": int(program_ns),
+        "channels": 32,
+        "dies_per_channel": 8,
+        "planes_per_die": 4,
+        "pages_per_block": 256,
+        "channel_width_bits": 8,
+        "channel_transfer_rate_mtps": 1600,
+        "queue_depth": 1,
+        "aggregate_bandwidth_bytes_per_s": 103_540_697,
+        "hbm_cache_bytes": 0,
+        "reference_sample_rate": 0.0,
+        "reference_warmup_requests": 0,
+        "time_scale": int(time_scale),
+        "timing_tolerance_ns": 27_105,
+        "empirical_vmem": {
+            "source_kind": "synthetic",
+            "source_sha256": "0" * 64,
+            "source_capacity_bytes": 16 * GIB,
+            "quantile": "p50",
+            "sample_count": 1,
+            "read_curve": curve,
+            "program_p50_ns": int(program_ns),
+            "program_p95_ns": int(program_ns),
+        },
+    }
+
+
+def vmem_trace(n: int = 1 << 20, seed: int = 0, range_length: int = 15 * GIB,
+               base: int = RANGE_BASE, mean_run: float = 48.0, write_p: float = 0.05):
+    """Page-granular trace for the empirical burst model: streaks of
+    sequential 4 KiB pages (geometric lengths, mean `mean_run`, one operation
+    per streak) from uniform start pages; arrivals cumulative exponential
+    gaps of mean 2 ns.  Returns (address, bytes, op, arrival) numpy arrays."""
+    rng = np.random.default_rng(seed)
+    pages_total = range_length // 4096
+    streaks = int(n / mean_run * 1.2) + 16
+    length = np.minimum(rng.geometric(1.0 / mean_run, streaks), 4096).astype(np.int64)
+    while int(length.sum()) < n:
+        length = np.concatenate([length, length])
+    start = rng.integers(0, pages_total - 4096, length.size, dtype=np.int64)
+    writes = (rng.random(length.size) < write_p).astype(np.uint8)
+    which = np.repeat(np.arange(length.size), length)[:n]
+    first = np.cumsum(length) - length
+    page = start[which] + (np.arange(n, dtype=np.int64) - first[which])
+    op = writes[which]
+    size = np.where(rng.random(n) < 0.5, 4096, 512).astype(np.uint32)
+    gaps = np.rint(rng.exponential(2.0, n)).astype(np.uint64)
+    arrival = np.cumsum(gaps, dtype=np.uint64)
+    address = (base + page.astype(np.uint64) * 4096).astype(np.uint64)
+    return address, size, op, arrival
+
+
 def c4_profile() -> dict:
     p = c0_profile()
     p.update(name="baseline-c4", dies_per_channel=8, capacity_bytes=128 * GIB)

@@ -590,3 +590,155 @@ void or_capacity_timing(const or_geometry* g, const or_timing* t,
         latency[i] = r - a;
     }
 }
+
+/* ---- empirical burst-curve profile ---- */
+
+#define OR_RUN_CAP 1023u
+#define OR_MAX_EMPIRICAL_PAGE ((UINT64_C(1) << 53) - 2)
+
+/* hbf_device.cuh:959-976: ceil(delta * offset / span) as whole spans times
+ * offset (saturating) plus the rounded-up share of the remainder. */
+static uint64_t or_scaled_ceiling(uint64_t delta, uint32_t offset, uint32_t span)
+{
+    if (delta == 0 || offset == 0) return 0;
+    if (span == 0) return U64MAX;
+    const uint64_t whole = or_saturating_multiply(delta / span, offset);
+    const uint64_t part = ((delta % span) * (uint64_t)offset + span - 1) / span;
+    return or_saturating_add(whole, part);
+}
+
+/* hbf_device.cuh:978-1019: piecewise-linear cumulative time of a run; the
+ * segment ending at the first breakpoint not below the run (the last one
+ * past the curve), interpolated from the breakpoint before it (or 0). */
+uint64_t or_empirical_cumulative_ns(const uint32_t* pages, const uint64_t* cumulative,
+                                    uint32_t count, uint32_t run_pages)
+{
+    if (run_pages == 0) return 0;
+    if (!pages || !cumulative || count == 0) return U64MAX;
+    uint32_t hi = 0;
+    while (hi < count && run_pages > pages[hi]) ++hi;
+    if (hi == count) hi = count - 1;
+    const uint32_t lo_pages = hi ? pages[hi - 1] : 0;
+    const uint64_t lo_ns = hi ? cumulative[hi - 1] : 0;
+    if (pages[hi] <= lo_pages || cumulative[hi] < lo_ns || run_pages < lo_pages)
+        return U64MAX;
+    return or_saturating_add(lo_ns, or_scaled_ceiling(cumulative[hi] - lo_ns,
+                                                      run_pages - lo_pages,
+                                                      pages[hi] - lo_pages));
+}
+
+/* hbf_device.cuh:1021-1032 */
+uint64_t or_empirical_service_ns(const uint32_t* pages, const uint64_t* cumulative,
+                                 uint32_t count, uint32_t run_pages)
+{
+    if (run_pages == 0) return 0;
+    const uint64_t cur = or_empirical_cumulative_ns(pages, cumulative, count, run_pages);
+    const uint64_t prev = or_empirical_cumulative_ns(pages, cumulative, count, run_pages - 1);
+    return cur < prev ? U64MAX : cur - prev;
+}
+
+/* hbf_device.cuh:1036-1081: state = (page + 1) << 11 | op << 10 | run; the
+ * run grows by one (to at most 1023) when the page follows the previous one
+ * with the same operation, else restarts at 1. */
+int or_update_empirical_burst(uint64_t previous, uint64_t page, uint32_t operation,
+                              uint64_t* packed, uint32_t* run_pages)
+{
+    if (page > OR_MAX_EMPIRICAL_PAGE || operation > 1) {
+        *packed = previous;
+        *run_pages = 0;
+        return 0;
+    }
+    const uint32_t prev_run = (uint32_t)(previous & OR_RUN_CAP);
+    const uint32_t prev_op = (uint32_t)((previous >> 10) & 1u);
+    const uint64_t prev_page_plus_one = previous >> 11;
+    uint32_t run = 1;
+    if (previous != 0 && prev_run != 0 && prev_op == operation &&
+        prev_page_plus_one != 0 && prev_page_plus_one == page)
+        run = prev_run == OR_RUN_CAP ? OR_RUN_CAP : prev_run + 1;
+    *packed = ((page + 1) << 11) | ((uint64_t)operation << 10) | run;
+    *run_pages = run;
+    return 1;
+}
+
+/* hbf_device.cuh:1107-1128 */
+int or_empirical_control_valid(const or_empirical* e)
+{
+    if (e->flags != 1 || e->count != 6 || e->program_latency_ns == 0) return 0;
+    for (uint32_t i = 0; i < 6; ++i) {
+        if (e->pages[i] == 0 || e->cumulative_ns[i] == 0) return 0;
+        if (i && (e->pages[i] <= e->pages[i - 1] ||
+                  e->cumulative_ns[i] <= e->cumulative_ns[i - 1]))
+            return 0;
+    }
+    return e->pages[5] <= OR_RUN_CAP;
+}
+
+/* hbf_device.cuh:1110-1140: reads from the curve at the run length, writes
+ * the header's program latency. */
+int or_empirical_request_service(const or_empirical* e, uint64_t previous, uint64_t page,
+                                 uint32_t operation, uint64_t* service_ns,
+                                 uint64_t* packed, uint32_t* run_pages)
+{
+    *service_ns = 0;
+    *packed = 0;
+    *run_pages = 0;
+    if (!or_empirical_control_valid(e)) return 0;
+    uint64_t next;
+    uint32_t run;
+    if (!or_update_empirical_burst(previous, page, operation, &next, &run)) return 0;
+    *service_ns = operation == 0
+                      ? or_empirical_service_ns(e->pages, e->cumulative_ns, e->count, run)
+                      : e->program_latency_ns;
+    *packed = next;
+    *run_pages = run;
+    return 1;
+}
+
+int or_run_empirical_batch(const or_range* ranges, uint32_t count, const or_empirical* e,
+                           uint32_t time_scale, uint64_t request_timeout_ns,
+                           const uint64_t* address, const uint32_t* bytes,
+                           const uint8_t* op, const uint64_t* arrival, uint64_t n,
+                           uint64_t* state, uint64_t* done, uint64_t* latency,
+                           uint8_t* status, or_stats* stats)
+{
+    memset(stats, 0, sizeof *stats);
+    uint64_t* order = or_arrival_order(arrival, n);
+    if (!order) return -1;
+    const int header_ok = or_empirical_control_valid(e);
+    for (uint64_t k = 0; k < n; ++k) {
+        const uint64_t i = order[k];
+        uint32_t index;
+        uint64_t media;
+        uint32_t st = or_classify(ranges, count, address[i], bytes[i], op[i], &index, &media);
+        done[i] = arrival[i];
+        latency[i] = 0;
+        if (st == OR_STATUS_MODELED) {
+            /* hbf_device.cu:773-777 and 797-801 */
+            const uint64_t media_bytes = ranges[index].page_bytes;
+            if (!header_ok || media_bytes != 4096 || media % media_bytes != 0 ||
+                time_scale == 0 || request_timeout_ns == 0)
+                st = OR_STATUS_UNSUPPORTED;
+        }
+        uint64_t service = 0, packed = 0;
+        uint32_t run = 0;
+        if (st == OR_STATUS_MODELED &&
+            !or_empirical_request_service(e, state[1], media / 4096, op[i], &service,
+                                          &packed, &run))
+            st = OR_STATUS_UNSUPPORTED;
+        status[i] = (uint8_t)st;
+        if (st == OR_STATUS_BYPASS) { stats->bypass++; continue; }
+        if (st != OR_STATUS_MODELED) { stats->unsupported++; continue; }
+        state[1] = packed;
+        const uint64_t a = arrival[i];
+        const uint64_t start = state[0] > a ? state[0] : a;
+        state[0] = or_saturating_add(start, or_saturating_multiply(service, time_scale));
+        done[i] = state[0];
+        latency[i] = state[0] - a;
+        stats->modeled++;
+        stats->fast_modeled_ns += service;
+        stats->latency_sum = or_saturating_add(stats->latency_sum, latency[i]);
+        if (state[0] > stats->max_done) stats->max_done = state[0];
+    }
+    free(order);
+    return 0;
+}

@@ -171,6 +171,43 @@ void or_capacity_timing(const or_geometry* g, const or_timing* t,
                         const uint64_t* arrival, uint64_t n, uint32_t page_shift,
                         uint64_t* state, uint64_t* done, uint64_t* latency);
 
+/* ---- empirical burst-curve profile (FAST model with empirical_vmem) ----
+ * hbf_device.cuh:959-1140 and the empirical branch of resolve_fast_or_hybrid
+ * (hbf_device.cu:797-838). */
+typedef struct or_empirical {
+    uint32_t flags;               /* header empirical_flags (1 = on) */
+    uint32_t count;               /* header empirical_point_count */
+    uint64_t program_latency_ns;  /* header program_latency_ns */
+    uint32_t pages[6];
+    uint64_t cumulative_ns[6];
+} or_empirical;
+
+uint64_t or_empirical_cumulative_ns(const uint32_t* pages, const uint64_t* cumulative,
+                                    uint32_t count, uint32_t run_pages);
+uint64_t or_empirical_service_ns(const uint32_t* pages, const uint64_t* cumulative,
+                                 uint32_t count, uint32_t run_pages);
+/* Returns 1 when valid; *packed and *run_pages get the new state (on an
+ * invalid update *packed keeps `previous` and *run_pages is 0). */
+int or_update_empirical_burst(uint64_t previous, uint64_t page, uint32_t operation,
+                              uint64_t* packed, uint32_t* run_pages);
+int or_empirical_control_valid(const or_empirical* e);
+/* Returns 1 when valid; all outputs 0 otherwise. */
+int or_empirical_request_service(const or_empirical* e, uint64_t previous, uint64_t page,
+                                 uint32_t operation, uint64_t* service_ns,
+                                 uint64_t* packed, uint32_t* run_pages);
+/* A batch of the empirical FAST model: classification as or_run_batch, then
+ * per timed access in (arrival, index) order the empirical branch's checks
+ * (a 4 KiB media page on a 4 KiB boundary, time_scale and request timeout
+ * nonzero, the header valid: else Unsupported), the burst update and the
+ * tail step target = max(tail, arrival) + service * time_scale.
+ * state[0] = channel tail, state[1] = packed burst state. */
+int or_run_empirical_batch(const or_range* ranges, uint32_t count, const or_empirical* e,
+                           uint32_t time_scale, uint64_t request_timeout_ns,
+                           const uint64_t* address, const uint32_t* bytes,
+                           const uint8_t* op, const uint64_t* arrival, uint64_t n,
+                           uint64_t* state, uint64_t* done, uint64_t* latency,
+                           uint8_t* status, or_stats* stats);
+
 #ifdef __cplusplus
 }
 #endif

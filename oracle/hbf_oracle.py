@@ -97,6 +97,19 @@ def _load() -> ctypes.CDLL:
     lib.or_capacity_timing.argtypes = [p, p, p, p, p, p, p, p, p, p, p, p, u64, u32, p, p, p]
     lib.or_lru_run.restype = None
     lib.or_lru_run.argtypes = [p, p, u64, u64, p, p, p]
+    lib.or_empirical_cumulative_ns.restype = u64
+    lib.or_empirical_cumulative_ns.argtypes = [p, p, u32, u32]
+    lib.or_empirical_service_ns.restype = u64
+    lib.or_empirical_service_ns.argtypes = [p, p, u32, u32]
+    lib.or_update_empirical_burst.restype = ctypes.c_int
+    lib.or_update_empirical_burst.argtypes = [u64, u64, u32, p, p]
+    lib.or_empirical_control_valid.restype = ctypes.c_int
+    lib.or_empirical_control_valid.argtypes = [p]
+    lib.or_empirical_request_service.restype = ctypes.c_int
+    lib.or_empirical_request_service.argtypes = [p, u64, u64, u32, p, p, p]
+    lib.or_run_empirical_batch.restype = ctypes.c_int
+    lib.or_run_empirical_batch.argtypes = [p, u32, p, u32, u64, p, p, p, p, u64, p, p, p, p,
+                                           p]
     return lib
 
 
@@ -182,6 +195,72 @@ def capacity_timing(geometry, timing, chan_bw, t_read, t_prog, admit, status, hi
                            _ptr(victim_dirty), _ptr(arrival), n, page_shift, _ptr(state),
                            _ptr(done), _ptr(latency))
     return done, latency
+
+
+class Empirical(ctypes.Structure):
+    _fields_ = [("flags", ctypes.c_uint32), ("count", ctypes.c_uint32),
+                ("program_latency_ns", ctypes.c_uint64),
+                ("pages", ctypes.c_uint32 * 6), ("cumulative_ns", ctypes.c_uint64 * 6)]
+
+
+def make_empirical(pages, cumulative, program_latency_ns, flags=1, count=6) -> Empirical:
+    e = Empirical()
+    e.flags, e.count, e.program_latency_ns = flags, count, program_latency_ns
+    for k in range(6):
+        e.pages[k] = int(pages[k]) if k < len(pages) else 0
+        e.cumulative_ns[k] = int(cumulative[k]) if k < len(cumulative) else 0
+    return e
+
+
+def empirical_cumulative(pages, cumulative, count, run) -> int:
+    pa = np.ascontiguousarray(pages, np.uint32)
+    ca = np.ascontiguousarray(cumulative, np.uint64)
+    return int(LIB.or_empirical_cumulative_ns(_ptr(pa), _ptr(ca), count, run))
+
+
+def empirical_service(pages, cumulative, count, run) -> int:
+    pa = np.ascontiguousarray(pages, np.uint32)
+    ca = np.ascontiguousarray(cumulative, np.uint64)
+    return int(LIB.or_empirical_service_ns(_ptr(pa), _ptr(ca), count, run))
+
+
+def update_burst(previous, page, op):
+    """(packed, run_pages, valid) of hbf_device.cuh update_empirical_burst."""
+    packed, run = ctypes.c_uint64(), ctypes.c_uint32()
+    ok = LIB.or_update_empirical_burst(previous, page, op, ctypes.byref(packed),
+                                       ctypes.byref(run))
+    return packed.value, run.value, bool(ok)
+
+
+def empirical_control_valid(e: Empirical) -> bool:
+    return bool(LIB.or_empirical_control_valid(ctypes.byref(e)))
+
+
+def empirical_request(e: Empirical, previous, page, op):
+    """(service_ns, packed, run_pages, valid) of empirical_request_service."""
+    svc, packed, run = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint32()
+    ok = LIB.or_empirical_request_service(ctypes.byref(e), previous, page, op,
+                                          ctypes.byref(svc), ctypes.byref(packed),
+                                          ctypes.byref(run))
+    return svc.value, packed.value, run.value, bool(ok)
+
+
+def run_empirical(ranges, count, e: Empirical, time_scale, request_timeout_ns, address,
+                  nbytes, op, arrival, state):
+    """One batch of the empirical FAST model; state = [tail, packed burst]
+    (uint64[2]) updated in place.  Returns (done, latency, status, stats)."""
+    n = address.size
+    done = np.zeros(n, np.uint64)
+    latency = np.zeros(n, np.uint64)
+    status = np.zeros(n, np.uint8)
+    stats = Stats()
+    rc = LIB.or_run_empirical_batch(
+        ctypes.cast(ranges, ctypes.c_void_p), count, ctypes.byref(e), time_scale,
+        request_timeout_ns, _ptr(address), _ptr(nbytes), _ptr(op), _ptr(arrival), n,
+        _ptr(state), _ptr(done), _ptr(latency), _ptr(status), ctypes.byref(stats))
+    if rc != 0:
+        raise MemoryError("oracle allocation failed")
+    return done, latency, status, {f: getattr(stats, f) for f, _ in Stats._fields_}
 
 
 def cores() -> int:

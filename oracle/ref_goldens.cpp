@@ -79,6 +79,204 @@ void emit_probe(const std::vector<dev::SharedRangeRecord>& r, std::uint64_t a,
                 media_bytes, succ_overlap, touches);
 }
 
+// Empirical burst-curve profile (hbf_device.cuh:959-1140): curve lookups,
+// the packed run-length state, the control-header check and the request
+// service, all by the reference functions; then traces of the empirical fast
+// path (hbf_device.cu:797-838: burst CAS, then the tail CAS with the scaled
+// service) with arrivals in place of the globaltimer.
+void emit_u64s(const char* name, const std::uint64_t* v, std::size_t n, bool last = false)
+{
+    std::printf("\"%s\":[", name);
+    for (std::size_t i = 0; i < n; ++i) std::printf("%s%" PRIu64, i ? "," : "", v[i]);
+    std::printf("]%s", last ? "" : ",");
+}
+
+dev::SharedControlHeader empirical_header(const std::uint32_t* pages, const std::uint64_t* cum,
+                                          std::uint64_t program)
+{
+    dev::SharedControlHeader h{};
+    h.empirical_flags = 1;
+    h.empirical_point_count = 6;
+    h.program_latency_ns = program;
+    for (int i = 0; i < 6; ++i) {
+        h.empirical_breakpoint_pages[i] = pages[i];
+        h.empirical_cumulative_ns[i] = cum[i];
+    }
+    return h;
+}
+
+void random_curve(Rng& rng, std::uint32_t* pages, std::uint64_t* cum, std::uint32_t last_max)
+{
+    std::uint32_t p = 0;
+    std::uint64_t c = 0;
+    for (int i = 0; i < 6; ++i) {
+        const std::uint32_t room = last_max - p - static_cast<std::uint32_t>(5 - i);
+        p += 1 + static_cast<std::uint32_t>(rng.below(std::min<std::uint32_t>(room, 300)));
+        c += 1 + rng.below(i == 0 ? 20'000 : 4'000'000);
+        pages[i] = p;
+        cum[i] = c;
+    }
+}
+
+void empirical_goldens(Rng& rng)
+{
+    // 7a. curve lookups over every run length the state can hold, and beyond
+    struct Curve {
+        std::uint32_t pages[6];
+        std::uint64_t cum[6];
+        std::uint32_t count;
+    };
+    std::vector<Curve> curves;
+    curves.push_back({{1, 4, 16, 64, 256, 512},
+                      {11'133, 41'495, 168'606, 2'824'351, 10'767'793, 20'254'374}, 6});
+    curves.push_back({{1, 2, 0, 0, 0, 0}, {UINT64_MAX - 1, UINT64_MAX, 0, 0, 0, 0}, 2});
+    curves.push_back({{3, 7, 8, 100, 101, 1023}, {5, 9, 10, 1'000'000, 1'000'001, 9'000'000}, 6});
+    for (int k = 0; k < 5; ++k) {
+        Curve c{};
+        c.count = 6;
+        random_curve(rng, c.pages, c.cum, 1023);
+        curves.push_back(c);
+    }
+    for (const auto& c : curves) {
+        std::vector<std::uint64_t> runs, cumulative, service;
+        for (std::uint64_t r = 0; r <= 1100; ++r) runs.push_back(r);
+        for (std::uint64_t r : {100'000ULL, 4'294'967'295ULL}) runs.push_back(r);
+        for (auto r : runs) {
+            const auto run = static_cast<std::uint32_t>(r);
+            cumulative.push_back(dev::empirical_cumulative_ns(c.pages, c.cum, c.count, run));
+            service.push_back(dev::empirical_service_ns(c.pages, c.cum, c.count, run));
+        }
+        std::uint64_t pages64[6];
+        for (int i = 0; i < 6; ++i) pages64[i] = c.pages[i];
+        std::printf("{\"kind\":\"emp_curve\",\"count\":%u,", c.count);
+        emit_u64s("pages", pages64, c.count);
+        emit_u64s("cum", c.cum, c.count);
+        emit_u64s("runs", runs.data(), runs.size());
+        emit_u64s("cumulative", cumulative.data(), cumulative.size());
+        emit_u64s("service", service.data(), service.size(), true);
+        std::printf("}\n");
+    }
+    // 7b. packed run-length state: chains of updates
+    constexpr std::uint64_t kMaxPage = (std::uint64_t{1} << 53) - 2;
+    for (int chain = 0; chain < 4; ++chain) {
+        std::printf("{\"kind\":\"emp_burst\",\"steps\":[");
+        std::uint64_t state = 0;
+        std::uint64_t page = chain == 3 ? kMaxPage - 40 : rng.below(1u << 20);
+        std::uint32_t op = 0;
+        const int steps = chain == 0 ? 1200 : 600;
+        for (int i = 0; i < steps; ++i) {
+            const auto r = rng.below(100);
+            if (chain == 0 || r < 70) page += 1;
+            else if (r < 78) page = rng.below(1ULL << 40);
+            else if (r < 83) op ^= 1u;
+            else if (r < 86) {}  // the same page again
+            else if (r < 90) page = page - 1;
+            else if (r < 93) page = kMaxPage + rng.below(3);
+            else if (r < 95) page = rng.below(64);
+            std::uint32_t use_op = op;
+            if (chain != 0 && rng.below(60) == 0) use_op = 2 + static_cast<std::uint32_t>(rng.below(3));
+            const auto u = dev::update_empirical_burst(state, page, use_op);
+            std::printf("%s[%" PRIu64 ",%" PRIu64 ",%u,%" PRIu64 ",%u,%d]", i ? "," : "", state,
+                        page, use_op, u.packed, u.run_pages, u.valid ? 1 : 0);
+            if (u.valid) state = u.packed;
+            if (page > kMaxPage) page = rng.below(1u << 20);
+        }
+        std::printf("]}\n");
+    }
+    // 7c. control-header validity
+    {
+        const std::uint32_t pages[6] = {1, 4, 16, 64, 256, 512};
+        const std::uint64_t cum[6] = {11'133, 41'495, 168'606, 2'824'351, 10'767'793, 20'254'374};
+        for (int k = 0; k < 40; ++k) {
+            auto h = empirical_header(pages, cum, 408'305);
+            switch (k % 10) {
+            case 0: break;
+            case 1: h.empirical_point_count = static_cast<std::uint32_t>(rng.below(12)); break;
+            case 2: h.empirical_breakpoint_pages[rng.below(6)] = 0; break;
+            case 3: h.empirical_cumulative_ns[rng.below(6)] = 0; break;
+            case 4: {
+                const auto i = 1 + rng.below(5);
+                h.empirical_breakpoint_pages[i] = h.empirical_breakpoint_pages[i - 1];
+                break;
+            }
+            case 5: {
+                const auto i = 1 + rng.below(5);
+                h.empirical_cumulative_ns[i] = h.empirical_cumulative_ns[i - 1] - rng.below(2);
+                break;
+            }
+            case 6: h.empirical_breakpoint_pages[5] = 1023 + static_cast<std::uint32_t>(rng.below(3)); break;
+            case 7: h.empirical_flags = static_cast<std::uint32_t>(rng.below(4)); break;
+            case 8: h.program_latency_ns = rng.below(2); break;
+            default: {
+                std::uint32_t p[6];
+                std::uint64_t c[6];
+                random_curve(rng, p, c, 1023);
+                h = empirical_header(p, c, 1 + rng.below(1'000'000));
+            }
+            }
+            std::uint64_t p64[6];
+            for (int i = 0; i < 6; ++i) p64[i] = h.empirical_breakpoint_pages[i];
+            std::printf("{\"kind\":\"emp_control\",\"flags\":%u,\"count\":%u,\"program\":%" PRIu64 ",",
+                        h.empirical_flags, h.empirical_point_count, h.program_latency_ns);
+            emit_u64s("pages", p64, 6);
+            emit_u64s("cum", h.empirical_cumulative_ns, 6);
+            const auto first = dev::empirical_request_service(h, 0, 5, 0);
+            std::printf("\"valid\":%d,\"service\":%" PRIu64 "}\n",
+                        dev::empirical_control_valid(h) ? 1 : 0, first.valid ? first.service_ns : 0);
+        }
+    }
+    // 7d. traces of the empirical fast path
+    for (int trace = 0; trace < 4; ++trace) {
+        std::uint32_t pages[6] = {1, 4, 16, 64, 256, 512};
+        std::uint64_t cum[6] = {11'133, 41'495, 168'606, 2'824'351, 10'767'793, 20'254'374};
+        std::uint64_t program = 408'305;
+        if (trace == 1 || trace == 3) {
+            random_curve(rng, pages, cum, trace == 3 ? 1023 : 600);
+            program = 1 + rng.below(2'000'000);
+        }
+        const auto h = empirical_header(pages, cum, program);
+        const std::uint32_t scale = trace == 1 ? 7 : 1;
+        std::uint64_t tail = trace == 2 ? UINT64_MAX - 50'000'000ULL : 0;
+        std::uint64_t arrival = trace == 2 ? UINT64_MAX - 60'000'000ULL : 0;
+        std::uint64_t state = 0;
+        std::uint64_t pages64[6];
+        for (int i = 0; i < 6; ++i) pages64[i] = pages[i];
+        std::printf("{\"kind\":\"emp_trace\",\"program\":%" PRIu64 ",\"scale\":%u,\"tail0\":%" PRIu64 ",",
+                    program, scale, tail);
+        emit_u64s("pages", pages64, 6);
+        emit_u64s("cum", cum, 6);
+        std::printf("\"steps\":[");
+        std::uint64_t page = rng.below(1u << 16);
+        std::uint32_t op = 0;
+        std::uint64_t streak = 0;
+        for (int i = 0; i < 3000; ++i) {
+            if (streak == 0) {
+                // a new streak: sequential pages of one operation
+                const auto r = rng.below(10);
+                streak = r < 6 ? 1 + rng.below(8) : r < 9 ? 1 + rng.below(300) : 900 + rng.below(400);
+                page = rng.below(1u << 16);
+                op = rng.below(12) == 0 ? 1u : 0u;
+            }
+            --streak;
+            arrival = dev::saturating_add(arrival, rng.below(4) == 0 ? rng.below(400'000) : rng.below(30));
+            const auto request = dev::empirical_request_service(h, state, page, op);
+            std::uint64_t target = 0;
+            if (request.valid) {
+                state = request.packed_state;
+                const auto scaled = dev::saturating_multiply(request.service_ns, scale);
+                const auto start = tail > arrival ? tail : arrival;
+                target = dev::saturating_add(start, scaled);
+                tail = target;
+            }
+            std::printf("%s[%" PRIu64 ",%" PRIu64 ",%u,%d,%" PRIu64 ",%" PRIu64 ",%u]", i ? "," : "",
+                        arrival, page, op, request.valid ? 1 : 0, target, request.service_ns,
+                        request.run_pages);
+            page += 1;
+        }
+        std::printf("]}\n");
+    }
+}
+
 int device_goldens()
 {
     Rng rng{12345};
@@ -206,6 +404,7 @@ int device_goldens()
         }
         std::printf("]}\n");
     }
+    empirical_goldens(rng);
     return 0;
 }
 

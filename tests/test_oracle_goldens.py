@@ -183,3 +183,92 @@ def test_die_model_threads_agree(threads):
     d1, l1, st1, _ = ho.run_batch(ranges, 1, g, t, bw, tr, tp, addr, nbytes, op, arrival, s1, 1)
     d2, l2, st2, _ = ho.run_batch(ranges, 1, g, t, bw, tr, tp, addr, nbytes, op, arrival, s2, threads)
     assert (d1 == d2).all() and (l1 == l2).all() and (s1 == s2).all()
+
+
+# ---- empirical burst-curve profile (hbf_device.cuh:959-1140) ----
+
+def test_empirical_curve_lookup(golden_dir):
+    curves = [r for r in _device_records(golden_dir) if r["kind"] == "emp_curve"]
+    assert len(curves) >= 8
+    for rec in curves:
+        pages = rec["pages"] + [0] * (6 - len(rec["pages"]))
+        cum = rec["cum"] + [0] * (6 - len(rec["cum"]))
+        for run, want_c, want_s in zip(rec["runs"], rec["cumulative"], rec["service"]):
+            assert ho.empirical_cumulative(pages, cum, rec["count"], run) == want_c, run
+            assert ho.empirical_service(pages, cum, rec["count"], run) == want_s, run
+
+
+def test_empirical_reference_kats():
+    """The reference's own known answers (tests/cpu/device_helper_abi_test.cpp)."""
+    pages = [1, 4, 16, 64, 256, 512]
+    cum = [11133, 41495, 168606, 2824351, 10767793, 20254374]
+    assert ho.empirical_cumulative(pages, cum, 6, 0) == 0
+    assert ho.empirical_cumulative(pages, cum, 6, 1) == 11133
+    assert ho.empirical_cumulative(pages, cum, 6, 3) == 31375
+    assert ho.empirical_cumulative(pages, cum, 6, 4) == 41495
+    assert ho.empirical_cumulative(pages, cum, 6, 512) == 20254374
+    assert ho.empirical_cumulative(pages, cum, 6, 513) == 20291431
+    packed, run, ok = ho.update_burst(0, 100, 0)
+    assert ok and run == 1
+    packed, run, ok = ho.update_burst(packed, 101, 0)
+    assert ok and run == 2
+    assert ho.update_burst(packed, 103, 0)[1] == 1
+    assert ho.update_burst(packed, 101, 0)[1] == 1
+    assert ho.update_burst(packed, 102, 1)[1] == 1
+    e = ho.make_empirical(pages, cum, 408305)
+    total, state = 0, 0
+    for page in range(4):
+        svc, state, _, ok = ho.empirical_request(e, state, page, 0)
+        assert ok
+        total += svc
+    assert total == 41495
+    svc, state, run, ok = ho.empirical_request(e, state, 99, 0)
+    assert ok and run == 1 and svc == 11133
+    svc, state, run, ok = ho.empirical_request(e, state, 100, 1)
+    assert ok and run == 1 and svc == 408305
+
+
+def test_empirical_burst_state(golden_dir):
+    chains = [r for r in _device_records(golden_dir) if r["kind"] == "emp_burst"]
+    assert len(chains) == 4
+    steps = 0
+    for rec in chains:
+        for prev, page, op, packed, run, valid in rec["steps"]:
+            assert ho.update_burst(prev, page, op) == (packed, run, bool(valid))
+            steps += 1
+    assert steps >= 3000
+
+
+def test_empirical_control_header(golden_dir):
+    recs = [r for r in _device_records(golden_dir) if r["kind"] == "emp_control"]
+    assert len(recs) == 40 and {r["valid"] for r in recs} == {0, 1}
+    for rec in recs:
+        e = ho.make_empirical(rec["pages"], rec["cum"], rec["program"], rec["flags"],
+                              rec["count"])
+        assert ho.empirical_control_valid(e) == bool(rec["valid"])
+        svc, _, _, ok = ho.empirical_request(e, 0, 5, 0)
+        assert (svc if ok else 0) == rec["service"]
+
+
+def test_empirical_fast_path_traces(golden_dir):
+    """The empirical branch of resolve_fast_or_hybrid (hbf_device.cu:797-838)
+    as the reference's helpers compute it, against the oracle's batch runner:
+    one timing range of 4 KiB pages, every access one page."""
+    traces = [r for r in _device_records(golden_dir) if r["kind"] == "emp_trace"]
+    assert len(traces) == 4
+    base = 1 << 40
+    for rec in traces:
+        steps = rec["steps"]
+        e = ho.make_empirical(rec["pages"], rec["cum"], rec["program"])
+        ranges = ho.make_ranges([(base, 1 << 34, 0, 1, 1, 3, 4096)])
+        page = np.array([s[1] for s in steps], np.uint64)
+        address = (base + page * 4096).astype(np.uint64)
+        nbytes = np.full(page.size, 64, np.uint32)
+        op = np.array([s[2] for s in steps], np.uint8)
+        arrival = np.array([s[0] for s in steps], np.uint64)
+        state = np.array([rec["tail0"], 0], np.uint64)
+        done, _, status, stats = ho.run_empirical(ranges, 1, e, rec["scale"], 10**9,
+                                                  address, nbytes, op, arrival, state)
+        assert np.all(status == 1)
+        assert done.tolist() == [s[4] for s in steps]
+        assert stats["fast_modeled_ns"] == sum(s[5] for s in steps) % (1 << 64)
