@@ -16,11 +16,14 @@
 //
 // The run length fixes the service, so the burst scan comes first:
 //   1 emp_burst_kernel       every CTA owns a contiguous range of 2048-access
-//                            tiles: classification, burst summary of the range
+//                            tiles: classification (one 8-byte record per
+//                            access left in the latency buffer), burst
+//                            summary of the range
 //   2 emp_burst_scan_kernel  one CTA: incoming burst state of every range and
 //                            the batch's final packed state
-//   3 emp_reduce_kernel      classification again, run lengths, services,
-//                            max-plus summary of the range, arrival checks
+//   3 emp_reduce_kernel      run lengths (from the 8-byte records pass 1
+//                            left in the latency buffer), services, max-plus
+//                            summary of the range, arrival checks
 //   4 emp_tail_scan_kernel   one CTA: incoming tail of every range; commits
 //                            the state when the batch is accepted
 //   5 emp_replay_kernel      per tile a burst block scan and a max-plus block
@@ -32,6 +35,8 @@
 // otherwise the exact single-thread kernel runs instead.
 #include "empirical.h"
 #include "decode.cuh"
+
+#include <algorithm>
 
 namespace hbfb {
 
@@ -123,7 +128,9 @@ struct EArgs {
     u8* status;
     u64 n;
     u64 tiles;
-    u32 ctas;
+    u32 ctas;    // CTAs of passes 3 and 5 (one contiguous tile range each)
+    u32 ctas1;   // CTAs of pass 1: `split` per range
+    u32 split;
     u64* words;
     u32* error;
     u64* last_arrival;
@@ -230,10 +237,10 @@ __device__ __forceinline__ Burst carried(u64 key, u32 run)
 // bypass, media descriptor), then the empirical branch's own checks
 // (hbf_device.cu:797-801): a 4 KiB media page on a 4 KiB boundary, the
 // control header valid.  Returns the access's key, 0 when it is not timed.
-__device__ __forceinline__ u64 access_key(const EArgs& a, u64 i, u32& status)
+__device__ __forceinline__ u64 access_key(const EArgs& a, u64 address, u32 bytes, u32 op,
+                                          u32& status)
 {
-    const u32 op = a.op[i];
-    const Decoded d = classify_decode(a.dp, a.address[i], a.bytes[i], op, false);
+    const Decoded d = classify_decode(a.dp, address, bytes, op, false);
     status = d.status;
     if (d.status != kModeled) return 0;
     if (!a.ep.ok || a.dp.ranges[d.range_index].reserved != 12 || (d.media & 4095u) != 0) {
@@ -243,10 +250,63 @@ __device__ __forceinline__ u64 access_key(const EArgs& a, u64 i, u32& status)
     return ((d.media >> 12) << 1) + op + 1;
 }
 
-__device__ __forceinline__ void cta_tiles(const EArgs& a, u64& t0, u64& t1)
+// The same classification for a context with one registered range, its
+// record in registers: access_supported and media_descriptor reduce to
+// offset checks (registration rules out overflow), and the empirical checks
+// (4 KiB pages, aligned file offset, header valid) are properties of the
+// range, folded into `timed`.
+struct KeyRange {
+    u64 base, length, file_offset, page_mask;
+    u32 allowed;  // DevRange::timing: operations a timing range allows
+    u32 timed;    // the empirical checks pass for this range
+};
+
+__device__ __forceinline__ KeyRange key_range(const DevRange& r, u32 ok)
 {
-    t0 = a.tiles * blockIdx.x / a.ctas;
-    t1 = a.tiles * (blockIdx.x + 1) / a.ctas;
+    const bool timed = ok && r.reserved == 12 && (r.file_offset & 4095u) == 0;
+    return KeyRange{r.base, r.length, r.file_offset, (u64{1} << r.reserved) - 1, r.timing,
+                    timed ? 1u : 0u};
+}
+
+__device__ __forceinline__ u64 key_single(const KeyRange& r, u64 a, u32 bytes, u32 op,
+                                          u32& status)
+{
+    status = kUnsupported;
+    if (bytes == 0) return 0;
+    const u64 offset = a - r.base;  // wraps when a < base
+    if (offset >= r.length) {
+        // below the range: unsupported if it straddles into it; else bypass
+        status = a < r.base && a <= ~u64{0} - bytes && r.base < a + bytes ? kUnsupported
+                                                                          : kBypass;
+        return 0;
+    }
+    if (op > 1 || ((r.allowed >> op) & 1u) == 0 || bytes > r.length - offset) return 0;
+    if ((offset & r.page_mask) + bytes > r.page_mask + 1 || !r.timed) return 0;
+    status = kModeled;
+    return (((r.file_offset + offset) >> 12) << 1) + op + 1;
+}
+
+// Pass 1 leaves one 8-byte record per access in the caller's latency
+// buffer: the key of a timed access (below 2^54: pages are below 2^52), or
+// the status of any other access in the top byte.  Passes 3 and 5 read it
+// instead of classifying again; pass 5 overwrites it with the latency.
+constexpr u32 kStatusShift = 56;
+
+__device__ __forceinline__ u64 record_key(u64 rec)
+{
+    return rec < (u64{1} << kStatusShift) ? rec : 0;
+}
+
+__device__ __forceinline__ void cta_range(u64 tiles, u32 ctas, u64& t0, u64& t1)
+{
+    t0 = tiles * blockIdx.x / ctas;
+    t1 = tiles * (blockIdx.x + 1) / ctas;
+}
+
+__device__ __forceinline__ u32 tile_size(const EArgs& a, u64 t)
+{
+    const u64 start = t * kETile;
+    return a.n - start < kETile ? static_cast<u32>(a.n - start) : kETile;
 }
 
 __device__ __forceinline__ Burst thread_burst(const u64* key)
@@ -259,23 +319,58 @@ __device__ __forceinline__ Burst thread_burst(const u64* key)
 }
 
 // ------------------------------------------------------------ 1: burst sums
-__global__ void __launch_bounds__(kEThreads) emp_burst_kernel(const EArgs a)
+// `split` CTAs per range of the later passes (more loads in flight): CTA h
+// covers tiles [h * tiles / ctas1, (h + 1) * tiles / ctas1), and range g of
+// the later passes is exactly the union of CTAs g * split .. g * split + split - 1.
+struct RawTile {
+    u64 addr[kEItems];
+    u32 bytes[kEItems];
+    u32 op[kEItems];
+};
+
+__device__ __forceinline__ void load_raw(const EArgs& a, u64 start, u32 nt, RawTile& r)
+{
+#pragma unroll
+    for (u32 k = 0; k < kEItems; ++k) {
+        const u32 e = k * kEThreads + threadIdx.x;
+        if (e < nt) {
+            r.addr[k] = a.address[start + e];
+            r.bytes[k] = a.bytes[start + e];
+            r.op[k] = a.op[start + e];
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kEThreads, 3) emp_burst_kernel(const EArgs a)
 {
     __shared__ u64 s_key[kEPad];
     __shared__ Burst s_bt[kEWarps + 1];
     const u32 tid = threadIdx.x;
     u64 t0, t1;
-    cta_tiles(a, t0, t1);
+    cta_range(a.tiles, a.ctas1, t0, t1);
+    const bool single = a.dp.range_count == 1;
+    const KeyRange kr = single ? key_range(a.dp.ranges[0], a.ep.ok) : KeyRange{};
     Burst acc{0, 0, 0};
+    RawTile raw;
+    if (t0 < t1) load_raw(a, t0 * kETile, tile_size(a, t0), raw);
     for (u64 t = t0; t < t1; ++t) {
         const u64 start = t * kETile;
-        const u32 nt = a.n - start < kETile ? static_cast<u32>(a.n - start) : kETile;
-#pragma unroll 2
+        const u32 nt = tile_size(a, t);
+#pragma unroll
         for (u32 k = 0; k < kEItems; ++k) {
             const u32 e = k * kEThreads + tid;
-            u32 st;
-            s_key[pad(e)] = e < nt ? access_key(a, start + e, st) : 0;
+            u64 key = 0;
+            if (e < nt) {
+                u32 st;
+                key = single ? key_single(kr, raw.addr[k], raw.bytes[k], raw.op[k], st)
+                             : access_key(a, raw.addr[k], raw.bytes[k], raw.op[k], st);
+                // the record the later passes read instead of classifying again
+                a.latency[start + e] = key ? key : static_cast<u64>(st) << kStatusShift;
+            }
+            s_key[pad(e)] = key;
         }
+        // the next tile's loads overlap this tile's scan
+        if (t + 1 < t1) load_raw(a, start + kETile, tile_size(a, t + 1), raw);
         __syncthreads();
         u64 key[kEItems];
 #pragma unroll
@@ -296,33 +391,66 @@ __global__ void __launch_bounds__(kEThreads) emp_burst_kernel(const EArgs a)
 __global__ void __launch_bounds__(kScanThreads) emp_burst_scan_kernel(const EArgs a)
 {
     __shared__ Burst s_bt[kScanThreads / 32 + 1];
-    const u32 g = threadIdx.x;
+    const u32 h = threadIdx.x;
     Burst v{0, 0, 0};
-    if (g < a.ctas) {
-        const u64* w = a.words + 8ull * g;
+    if (h < a.ctas1) {
+        const u64* w = a.words + 8ull * h;
         v = Burst{w[0], w[1], static_cast<u32>(w[2])};
     }
     Burst total;
     const Burst pre = block_exclusive<kScanThreads>(v, Burst{0, 0, 0}, s_bt, total, burst_join);
     const u64 packed = a.state_in[1];
     const Burst st = burst_of_state(packed);
-    if (g < a.ctas) {
+    if (h < a.ctas1 && h % a.split == 0) {  // first pass-1 CTA of range g
         const Burst in = burst_join(st, pre);
-        a.words[8ull * g + 3] = in.last;
-        a.words[8ull * g + 4] = in.tail & ~kWhole;
+        const u64 g = h / a.split;
+        a.words[8 * g + 3] = in.last;
+        a.words[8 * g + 4] = in.tail & ~kWhole;
     }
-    if (g == 0) {
+    if (h == 0) {
         // no timed access: the state stays as it was, whatever it holds
         const Burst out = burst_join(st, total);
         a.words[kFinalWord] = total.first ? state_of(out.last, out.tail & ~kWhole) : packed;
     }
 }
 
-// One tile through shared memory: keys and arrivals staged (striped,
-// coalesced), then each thread's 8 consecutive accesses (blocked) get their
-// run lengths from the burst scan and their scaled services.
+// Passes 3 and 5 stage each tile's records and arrivals in shared memory
+// with cp.async, double-buffered: the next tile streams in while the current
+// one is scanned.  Layout of the dynamic shared memory: [2 buffers][records,
+// arrivals][kEPad] u64.
+__device__ __forceinline__ void cp_async8(void* smem_dst, const void* gmem_src)
+{
+    const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst), "l"(gmem_src));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+__device__ __forceinline__ void cp_async_wait_all()
+{
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+}
+
+constexpr u32 kStageBytes = 4u * kEPad * 8u;
+
+__device__ __forceinline__ void stage_tile(const EArgs& a, u64 start, u32 nt, u64* s_rec,
+                                           u64* s_arr)
+{
+#pragma unroll
+    for (u32 k = 0; k < kEItems; ++k) {
+        const u32 e = k * kEThreads + threadIdx.x;
+        if (e < nt) {
+            cp_async8(&s_rec[pad(e)], a.latency + start + e);
+            cp_async8(&s_arr[pad(e)], a.arrival + start + e);
+        } else {
+            s_rec[pad(e)] = 0;  // no access: no key
+        }
+    }
+    cp_async_commit();
+}
+
+// One staged tile, blocked phase: each thread's 8 consecutive accesses get
+// their run lengths from the burst scan and their scaled services.
 struct TileWork {
-    u64 key[kEItems];
+    u64 rec[kEItems];
     u64 arr[kEItems];
     i64 s[kEItems];
     u64 svc_sum;     // unscaled services of the thread's timed accesses
@@ -330,18 +458,20 @@ struct TileWork {
     Burst btotal;    // the tile's burst summary
 };
 
-__device__ __forceinline__ void tile_services(const EArgs& a, const u64* s_key, const u64* s_arr,
+__device__ __forceinline__ void tile_services(const EArgs& a, const u64* s_rec, const u64* s_arr,
                                               const u64* s_svc, Burst* s_bt, u64 in_key,
                                               u32 in_run, u32 nt, TileWork& w)
 {
     const u32 tid = threadIdx.x;
+    u64 key[kEItems];
 #pragma unroll
     for (u32 j = 0; j < kEItems; ++j) {
         const u32 e = tid * kEItems + j;
-        w.key[j] = s_key[pad(e)];
+        w.rec[j] = s_rec[pad(e)];
+        key[j] = record_key(w.rec[j]);
         w.arr[j] = e < nt ? s_arr[pad(e)] : 0;
     }
-    const Burst pre = block_exclusive<kEThreads>(thread_burst(w.key), Burst{0, 0, 0}, s_bt,
+    const Burst pre = block_exclusive<kEThreads>(thread_burst(key), Burst{0, 0, 0}, s_bt,
                                                  w.btotal, burst_join);
     const Burst in = burst_join(carried(in_key, in_run), pre);
     u64 last = in.last;
@@ -351,7 +481,7 @@ __device__ __forceinline__ void tile_services(const EArgs& a, const u64* s_key, 
 #pragma unroll
     for (u32 j = 0; j < kEItems; ++j) {
         w.s[j] = 0;
-        const u64 k = w.key[j];
+        const u64 k = key[j];
         if (!k) continue;
         run = last != 0 && k == last + 2 ? (run < kRunCap ? run + 1 : kRunCap) : 1u;
         last = k;
@@ -363,48 +493,45 @@ __device__ __forceinline__ void tile_services(const EArgs& a, const u64* s_key, 
 }
 
 // ---------------------------------------------------------- 3: tail summary
-__global__ void __launch_bounds__(kEThreads, 3) emp_reduce_kernel(const EArgs a)
+__global__ void __launch_bounds__(kEThreads, 2) emp_reduce_kernel(const EArgs a)
 {
-    __shared__ u64 s_key[kEPad];
-    __shared__ u64 s_arr[kEPad];
+    extern __shared__ __align__(16) u64 e_smem[];
     __shared__ u64 s_svc[kRunCap + 1];
     __shared__ Burst s_bt[kEWarps + 1];
     __shared__ MaxPlus s_mt[kEWarps + 1];
     const u32 tid = threadIdx.x;
     for (u32 r = tid; r <= kRunCap; r += kEThreads) s_svc[r] = a.ep.service[r];
     u64 t0, t1;
-    cta_tiles(a, t0, t1);
+    cta_range(a.tiles, a.ctas, t0, t1);
     const u64* cw = a.words + 8ull * blockIdx.x;
     u64 in_key = cw[3];
     u32 in_run = static_cast<u32>(cw[4]);
     MaxPlus acc{0, kNeg};
     bool unsorted = false, over = false;
-    for (u64 t = t0; t < t1; ++t) {
+    if (t0 < t1) stage_tile(a, t0 * kETile, tile_size(a, t0), e_smem, e_smem + kEPad);
+    u32 b = 0;
+    for (u64 t = t0; t < t1; ++t, b ^= 1u) {
         const u64 start = t * kETile;
-        const u32 nt = a.n - start < kETile ? static_cast<u32>(a.n - start) : kETile;
-#pragma unroll 2
-        for (u32 k = 0; k < kEItems; ++k) {
-            const u32 e = k * kEThreads + tid;
-            u64 key = 0;
-            if (e < nt) {
-                u32 st;
-                key = access_key(a, start + e, st);
-                s_arr[pad(e)] = a.arrival[start + e];
-            }
-            s_key[pad(e)] = key;
+        const u32 nt = tile_size(a, t);
+        u64* s_rec = e_smem + 2 * b * kEPad;
+        u64* s_arr = s_rec + kEPad;
+        cp_async_wait_all();
+        __syncthreads();  // tile t visible; everyone is done with the other buffer
+        if (t + 1 < t1) {
+            u64* n_rec = e_smem + 2 * (b ^ 1u) * kEPad;
+            stage_tile(a, start + kETile, tile_size(a, t + 1), n_rec, n_rec + kEPad);
         }
-        __syncthreads();
         // arrival order across the whole batch (and after the previous batch)
         u64 prev = tid > 0 ? s_arr[pad(tid * kEItems - 1)]
                            : (start > 0 ? a.arrival[start - 1] : *a.last_arrival);
         TileWork w;
-        tile_services(a, s_key, s_arr, s_svc, s_bt, in_key, in_run, nt, w);
+        tile_services(a, s_rec, s_arr, s_svc, s_bt, in_key, in_run, nt, w);
 #pragma unroll
         for (u32 j = 0; j < kEItems; ++j) {
             if (tid * kEItems + j >= nt) break;
             unsorted |= w.arr[j] < prev;
             prev = w.arr[j];
-            over |= w.key[j] != 0 && w.arr[j] >= kArrivalLimit;
+            over |= record_key(w.rec[j]) != 0 && w.arr[j] >= kArrivalLimit;
         }
         MaxPlus mtotal;
         block_exclusive<kEThreads>(w.own, MaxPlus{0, kNeg}, s_mt, mtotal, mp_join);
@@ -503,44 +630,38 @@ __device__ void flush_counts(DevCounters* c, u64 mod, u64 byp, u64 uns, u64 lat,
 }
 
 // ---------------------------------------------------------------- 5: replay
-__global__ void __launch_bounds__(kEThreads, 3) emp_replay_kernel(const EArgs a)
+__global__ void __launch_bounds__(kEThreads, 2) emp_replay_kernel(const EArgs a)
 {
-    __shared__ u64 s_key[kEPad];  // keys, then completion ticks
-    __shared__ u64 s_arr[kEPad];
+    extern __shared__ __align__(16) u64 e_smem[];  // records -> completion ticks
     __shared__ u64 s_svc[kRunCap + 1];
+    __shared__ u8 s_st[kETile];
     __shared__ Burst s_bt[kEWarps + 1];
     __shared__ MaxPlus s_mt[kEWarps + 1];
     if (*a.error) return;  // refused, or the sequential kernel times it
     const u32 tid = threadIdx.x;
     for (u32 r = tid; r <= kRunCap; r += kEThreads) s_svc[r] = a.ep.service[r];
     u64 t0, t1;
-    cta_tiles(a, t0, t1);
+    cta_range(a.tiles, a.ctas, t0, t1);
     const u64* cw = a.words + 8ull * blockIdx.x;
     u64 in_key = cw[3];
     u32 in_run = static_cast<u32>(cw[4]);
     i64 tail = static_cast<i64>(cw[7]);
     u64 n_mod = 0, n_byp = 0, n_uns = 0, lat = 0, mx = 0, svc = 0;
-    for (u64 t = t0; t < t1; ++t) {
+    if (t0 < t1) stage_tile(a, t0 * kETile, tile_size(a, t0), e_smem, e_smem + kEPad);
+    u32 b = 0;
+    for (u64 t = t0; t < t1; ++t, b ^= 1u) {
         const u64 start = t * kETile;
-        const u32 nt = a.n - start < kETile ? static_cast<u32>(a.n - start) : kETile;
-#pragma unroll 2
-        for (u32 k = 0; k < kEItems; ++k) {
-            const u32 e = k * kEThreads + tid;
-            u64 key = 0;
-            if (e < nt) {
-                u32 st;
-                key = access_key(a, start + e, st);
-                a.status[start + e] = static_cast<u8>(st);
-                n_mod += st == kModeled;
-                n_byp += st == kBypass;
-                n_uns += st != kModeled && st != kBypass;
-                s_arr[pad(e)] = a.arrival[start + e];
-            }
-            s_key[pad(e)] = key;
+        const u32 nt = tile_size(a, t);
+        u64* s_rec = e_smem + 2 * b * kEPad;
+        u64* s_arr = s_rec + kEPad;
+        cp_async_wait_all();
+        __syncthreads();  // tile t visible; everyone is done with the other buffer
+        if (t + 1 < t1) {
+            u64* n_rec = e_smem + 2 * (b ^ 1u) * kEPad;
+            stage_tile(a, start + kETile, tile_size(a, t + 1), n_rec, n_rec + kEPad);
         }
-        __syncthreads();
         TileWork w;
-        tile_services(a, s_key, s_arr, s_svc, s_bt, in_key, in_run, nt, w);
+        tile_services(a, s_rec, s_arr, s_svc, s_bt, in_key, in_run, nt, w);
         svc += w.svc_sum;
         MaxPlus mtotal;
         const MaxPlus pre = block_exclusive<kEThreads>(w.own, MaxPlus{0, kNeg}, s_mt, mtotal,
@@ -551,29 +672,37 @@ __global__ void __launch_bounds__(kEThreads, 3) emp_replay_kernel(const EArgs a)
             const u32 e = tid * kEItems + j;
             if (e >= nt) break;
             u64 d = w.arr[j];
-            if (w.key[j]) {
+            u32 st = static_cast<u32>(w.rec[j] >> kStatusShift);
+            if (record_key(w.rec[j])) {
                 x = imax(x, static_cast<i64>(w.arr[j])) + w.s[j];
                 d = static_cast<u64>(x);
                 lat += d - w.arr[j];
                 mx = d > mx ? d : mx;
+                st = kModeled;
+                ++n_mod;
+            } else if (st == kBypass) {
+                ++n_byp;
+            } else {
+                ++n_uns;
             }
-            s_key[pad(e)] = d;
+            s_rec[pad(e)] = d;
+            s_st[e] = static_cast<u8>(st);
         }
         __syncthreads();
-#pragma unroll 2
+#pragma unroll 4
         for (u32 k = 0; k < kEItems; ++k) {
             const u32 e = k * kEThreads + tid;
             if (e < nt) {
-                const u64 d = s_key[pad(e)];
+                const u64 d = s_rec[pad(e)];
                 a.done[start + e] = d;
                 a.latency[start + e] = d - s_arr[pad(e)];
+                a.status[start + e] = s_st[e];
             }
         }
         const Burst nb = burst_join(carried(in_key, in_run), w.btotal);
         in_key = nb.last;
         in_run = nb.tail & ~kWhole;
         tail = imax(tail + mtotal.s, mtotal.m);
-        __syncthreads();  // the next tile overwrites the staged arrays
     }
     flush_counts(a.counters, n_mod, n_byp, n_uns, lat, mx, svc);
 }
@@ -602,7 +731,7 @@ __global__ void emp_sequential_kernel(const EArgs a)
     unsigned long long n_mod = 0, n_byp = 0, n_uns = 0, lat = 0, mx = 0, svc_sum = 0;
     for (u64 i = 0; i < a.n; ++i) {
         u32 st;
-        const u64 key = access_key(a, i, st);
+        const u64 key = access_key(a, a.address[i], a.bytes[i], a.op[i], st);
         const u64 arr = a.arrival[i];
         a.status[i] = static_cast<u8>(st);
         if (!key) {
@@ -670,16 +799,24 @@ cudaError_t launch_empirical(const DecodeParams& dp, const EmpiricalParams& ep,
     a.status = io.status;
     a.n = io.n;
     a.tiles = (io.n + kETile - 1) / kETile;
+    for (auto k : {emp_reduce_kernel, emp_replay_kernel}) {
+        err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(kStageBytes));
+        if (err != cudaSuccess) return err;
+    }
     // one wave: as many CTAs as the replay kernel keeps resident
     static int resident = 0;
     if (resident == 0 &&
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, emp_replay_kernel, kEThreads, 0) !=
-            cudaSuccess)
-        resident = 2;
-    if (resident < 1) resident = 1;
+        (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, emp_replay_kernel, kEThreads,
+                                                       kStageBytes) != cudaSuccess ||
+         resident < 1))
+        resident = 1;
     const u64 want = static_cast<u64>(resident) * static_cast<u64>(sm_count > 0 ? sm_count : 148);
     a.ctas = static_cast<u32>(a.tiles < want ? a.tiles : want);
     if (a.ctas > kEmpMaxCtas) a.ctas = kEmpMaxCtas;
+    // pass 1 splits every range over up to 4 CTAs (its loads want more CTAs)
+    a.split = a.ctas ? std::min<u32>(4u, kEmpMaxCtas / a.ctas) : 1u;
+    a.ctas1 = a.ctas * a.split;
     a.words = s.words;
     a.error = s.error;
     a.last_arrival = s.last_arrival;
@@ -688,19 +825,19 @@ cudaError_t launch_empirical(const DecodeParams& dp, const EmpiricalParams& ep,
     a.state_out = s.state_out;
     if (!force_sequential && a.ctas > 0) {
         hooks(kSlotPass1, 0, stream);
-        emp_burst_kernel<<<a.ctas, kEThreads, 0, stream>>>(a);
+        emp_burst_kernel<<<a.ctas1, kEThreads, 0, stream>>>(a);
         hooks(kSlotPass1, 1, stream);
         hooks(kSlotScan, 0, stream);
         emp_burst_scan_kernel<<<1, kScanThreads, 0, stream>>>(a);
         hooks(kSlotScan, 1, stream);
         hooks(kSlotPass1, 0, stream);
-        emp_reduce_kernel<<<a.ctas, kEThreads, 0, stream>>>(a);
+        emp_reduce_kernel<<<a.ctas, kEThreads, kStageBytes, stream>>>(a);
         hooks(kSlotPass1, 1, stream);
         hooks(kSlotScan, 0, stream);
         emp_tail_scan_kernel<<<1, kScanThreads, 0, stream>>>(a);
         hooks(kSlotScan, 1, stream);
         hooks(kSlotPass2, 0, stream);
-        emp_replay_kernel<<<a.ctas, kEThreads, 0, stream>>>(a);
+        emp_replay_kernel<<<a.ctas, kEThreads, kStageBytes, stream>>>(a);
         hooks(kSlotPass2, 1, stream);
     }
     hooks(kSlotSequential, 0, stream);
