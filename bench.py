@@ -293,10 +293,20 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=8,
                     help="config-1 decode steps in the trace (8 = the full config; "
                          "fewer only for small profiling captures)")
+    ap.add_argument("--only-extra", choices=["empirical_vmem", "thermal_coupled"],
+                    help="run one secondary measurement alone and print its JSON "
+                         "(profiling captures); not a bench line")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
         return reference_arm(args)
+    if args.only_extra:
+        import torch
+        torch.cuda.set_device(0)
+        run = run_vmem if args.only_extra == "empirical_vmem" else run_c3
+        with tempfile.TemporaryDirectory() as tmp:
+            print_result(run(args, torch.device("cuda", 0), tmp))
+        return 0
 
     import torch
     import torch.distributed as dist
