@@ -115,6 +115,13 @@ class ThermalConfigV1(ctypes.Structure):
                 ("die_x1", vp), ("die_y0", vp), ("die_y1", vp)]
 
 
+class RetentionConfigV1(ctypes.Structure):
+    _fields_ = [("struct_size", u32), ("version", u32), ("ea_ev", dbl), ("tref_k", dbl),
+                ("period_ns", u64), ("initial_age_ns", u64), ("initial_wall_age_ns", u64),
+                ("epoch_ns", u64), ("initial_temperature_k", dbl),
+                ("refresh_trigger", u32), ("reserved", u32)]
+
+
 # Every exported function with its signature (restype, argtypes).
 SIGNATURES = {
     "hbfsim_abi_version": (u32, []),
@@ -154,6 +161,14 @@ SIGNATURES = {
     "hbfsim_advance_epoch_global_v1": (i32, [vp, dbl, vp, vp, vp]),
     "hbfsim_copy_die_activity_v1": (i32, [vp, vp, vp, vp]),
     "hbfsim_get_thermal_factors_v1": (i32, [vp, vp, vp, vp, vp]),
+    "hbfsim_retention_configure_v1": (i32, [vp, ctypes.POINTER(RetentionConfigV1)]),
+    "hbfsim_retention_blocks_v1": (u64, [vp]),
+    "hbfsim_retention_advance_v1": (i32, [vp, u64, vp, vp]),
+    "hbfsim_retention_due_v1": (i32, [vp, u64, vp, vp, u64, ctypes.POINTER(u64), vp]),
+    "hbfsim_retention_refresh_v1": (i32, [vp, vp, u64, vp]),
+    "hbfsim_retention_record_erase_v1": (i32, [vp, vp, u64, vp]),
+    "hbfsim_retention_record_programs_v1": (i32, [vp, vp, vp, vp, u64, vp]),
+    "hbfsim_get_retention_v1": (i32, [vp, vp, vp, vp, vp, u64, ctypes.POINTER(u64)]),
 }
 
 

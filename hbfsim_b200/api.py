@@ -372,3 +372,78 @@ class Context:
                                                       _ptr(lv)),
               "hbfsim_get_thermal_factors_v1")
         return r, t, a, lv
+
+    # ---- per-block retention-age ledger ---------------------------------
+    def retention_configure(self, ea_ev: float = 1.04, initial_temperature_k: float = 318.15,
+                            initial_age_ns: int = 0, initial_wall_age_ns: int = 0,
+                            epoch_ns: int = 0, refresh_trigger: str = "wall_only") -> int:
+        """Ledger over every block of the local channels (reliability.py
+        ReliabilityLedger); returns the block count."""
+        cfg = _lib.RetentionConfigV1(ctypes.sizeof(_lib.RetentionConfigV1), 1, float(ea_ev),
+                                     358.15, 86_400_000_000_000, int(initial_age_ns),
+                                     int(initial_wall_age_ns), int(epoch_ns),
+                                     float(initial_temperature_k),
+                                     {"wall_only": 0, "equivalent_age_or_wall": 1}[refresh_trigger],
+                                     0)
+        check(self._lib.hbfsim_retention_configure_v1(self.handle, ctypes.byref(cfg)),
+              "hbfsim_retention_configure_v1")
+        return self.retention_blocks()
+
+    def retention_blocks(self) -> int:
+        return int(self._lib.hbfsim_retention_blocks_v1(self.handle))
+
+    def retention_advance(self, end_ns: int, die_temp_k=None, stream=None) -> None:
+        """Age every block to end_ns: at the given per-local-die temperatures
+        (float64 device tensor), or at the midpoint of the thermal model's
+        die temperatures (None)."""
+        check(self._lib.hbfsim_retention_advance_v1(
+            self.handle, int(end_ns), None if die_temp_k is None else _ptr(die_temp_k),
+            ctypes.c_void_p(_stream_handle(stream))), "hbfsim_retention_advance_v1")
+
+    def retention_due(self, at_ns: int, stream=None):
+        """(block ids, reason bits) of the blocks due at at_ns, ascending."""
+        import torch
+        n = self.retention_blocks()
+        blocks = torch.empty(max(1, n), dtype=torch.int32, device="cuda")
+        reasons = torch.empty(max(1, n), dtype=torch.uint8, device="cuda")
+        count = ctypes.c_uint64()
+        check(self._lib.hbfsim_retention_due_v1(self.handle, int(at_ns), _ptr(blocks),
+                                                _ptr(reasons), n, ctypes.byref(count),
+                                                ctypes.c_void_p(_stream_handle(stream))),
+              "hbfsim_retention_due_v1")
+        k = int(count.value)
+        return (blocks[:k].cpu().numpy().view(np.uint32), reasons[:k].cpu().numpy())
+
+    def retention_refresh(self, blocks, stream=None) -> None:
+        """Committed refresh of the listed blocks (int32 device tensor)."""
+        check(self._lib.hbfsim_retention_refresh_v1(self.handle, _ptr(blocks), blocks.numel(),
+                                                    ctypes.c_void_p(_stream_handle(stream))),
+              "hbfsim_retention_refresh_v1")
+
+    def retention_record_erase(self, blocks, stream=None) -> None:
+        check(self._lib.hbfsim_retention_record_erase_v1(
+            self.handle, _ptr(blocks), blocks.numel(), ctypes.c_void_p(_stream_handle(stream))),
+            "hbfsim_retention_record_erase_v1")
+
+    def retention_record_programs(self, address, nbytes, op, stream=None) -> None:
+        check(self._lib.hbfsim_retention_record_programs_v1(
+            self.handle, _ptr(address), _ptr(nbytes), _ptr(op), address.numel(),
+            ctypes.c_void_p(_stream_handle(stream))), "hbfsim_retention_record_programs_v1")
+
+    def retention_state(self) -> dict:
+        """Host copies: age_ns, next_wall_due_ns, last_refresh_commit_ns,
+        program_started, program_completed, erase_started, erase_completed,
+        frontier_ns."""
+        n = self.retention_blocks()
+        age = np.zeros(n, np.float64)
+        due = np.zeros(n, np.uint64)
+        last = np.zeros(n, np.uint64)
+        counts = np.zeros(4 * n, np.uint32)
+        frontier = ctypes.c_uint64()
+        check(self._lib.hbfsim_get_retention_v1(self.handle, _ptr(age), _ptr(due), _ptr(last),
+                                                _ptr(counts), n, ctypes.byref(frontier)),
+              "hbfsim_get_retention_v1")
+        c = counts.reshape(4, n)
+        return {"age_ns": age, "next_wall_due_ns": due, "last_refresh_commit_ns": last,
+                "program_started": c[0], "program_completed": c[1], "erase_started": c[2],
+                "erase_completed": c[3], "frontier_ns": int(frontier.value)}

@@ -220,6 +220,8 @@ int configure_geometry(hbfsim_context* c, std::uint32_t stacks,
     if (p.capacity_bytes / stripe >= 0xffffffffull) return HBFSIM_UNSUPPORTED;
     if (cudaDeviceSynchronize() != cudaSuccess) return HBFSIM_CUDA_ERROR;
     free_geometry(c);
+    retention_destroy(c->retention);  // its blocks follow the geometry
+    c->retention = nullptr;
     c->stacks = stacks;
     c->stripe_bytes = stripe;
     c->shard_rank = rank;
@@ -681,6 +683,7 @@ void hbfsim_context_destroy(hbfsim_context* c)
     cudaDeviceSynchronize();
     if (c->thermal) thermal_destroy(c->thermal);
     if (c->capacity) capacity_destroy(c->capacity);
+    retention_destroy(c->retention);
     free_geometry(c);
     dfree(c->d_ranges);
     dfree(c->d_error);

@@ -11,8 +11,9 @@
 #include <vector>
 
 namespace hbfb {
-struct ThermalState;   // thermal.cu
-struct CapacityState;  // capacity.cu
+struct ThermalState;    // thermal.cu
+struct CapacityState;   // capacity.cu
+struct RetentionState;  // retention.cu
 }
 
 struct hbfsim_context {
@@ -95,6 +96,7 @@ struct hbfsim_context {
 
     hbfb::ThermalState* thermal = nullptr;
     hbfb::CapacityState* capacity = nullptr;  // Capacity-mode LRU (capacity.cu)
+    hbfb::RetentionState* retention = nullptr;  // per-block retention ledger (retention.cu)
     bool track_activity = false;  // accumulate per-die activity without thermal
 
     // launch profiling (event pairs per kernel slot)
@@ -113,6 +115,9 @@ namespace hbfb {
 // thermal.cu
 void thermal_destroy(ThermalState* t);
 void capacity_destroy(CapacityState* c);
+void retention_destroy(RetentionState* r);
+// Device array of the grid's per-die mean temperatures (global die g*D+d).
+const double* thermal_die_temperatures(const ThermalState* t);
 // Times media actions (device arrays) decoded against `ranges`, in batch
 // order whatever their arrivals; carries the context's timing state.
 int run_media_batch(hbfsim_context* c, const BatchIO& io, const DevRange* ranges,

@@ -62,6 +62,8 @@ struct ThermalState {
     std::uint64_t x_bound = 0, op_bound = 0, admit_bound = 0;
 };
 
+const double* thermal_die_temperatures(const ThermalState* t) { return t->d_die_temp; }
+
 void thermal_factor_arrays(ThermalState* t, std::uint32_t** refresh, std::uint32_t** throttle,
                            std::uint64_t** admit)
 {

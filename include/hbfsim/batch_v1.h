@@ -360,6 +360,72 @@ int hbfsim_get_channel_factors_v1(hbfsim_context* context,
                                   uint32_t* throttle_permille,
                                   uint64_t* admit_after_ns);
 
+/* ---- per-block retention-age ledger ----
+ * Replaces the reference's ReliabilityLedger
+ * (experiments/eq3_system_thermal/reliability.py:26-232) as
+ * run_maintenance_point.py:189, 225-234 drives it, for every physical block
+ * of the context's local channels (die model only).  Block id:
+ * ((local channel * D + die) * planes + plane) * blocks_per_plane + block,
+ * blocks_per_plane = ceil(capacity / (channels_total * D * planes * page)
+ * / pages_per_block).  All blocks share one accounted frontier. */
+#define HBFSIM_RETENTION_CONFIG_V1_VERSION 1u
+typedef struct hbfsim_retention_config_v1 {
+    uint32_t struct_size;
+    uint32_t version;
+    double ea_ev;                  /* 1.01, 1.04 or 1.08 (reliability.py:9)    */
+    double tref_k;                 /* fixed at 358.15 (reliability.py:41-43)  */
+    uint64_t period_ns;            /* fixed at 24 h (reliability.py:44-46)    */
+    uint64_t initial_age_ns;       /* initial_equivalent_age_ns               */
+    uint64_t initial_wall_age_ns;  /* at most period_ns                       */
+    uint64_t epoch_ns;             /* maintenance_epoch_ns: the start tick    */
+    double initial_temperature_k;  /* every die's temperature at the start    */
+    uint32_t refresh_trigger;      /* 0 wall_only, 1 equivalent_age_or_wall   */
+    uint32_t reserved;
+} hbfsim_retention_config_v1;
+
+int hbfsim_retention_configure_v1(hbfsim_context* context,
+                                  const hbfsim_retention_config_v1* config);
+/* Number of blocks in the ledger (0 when not configured). */
+uint64_t hbfsim_retention_blocks_v1(hbfsim_context* context);
+/* Ages every block from the frontier to end_ns (advance_temperature_many,
+ * reliability.py:109-135).  die_temp_k: device array of one temperature per
+ * local die (c*D+d), used as is; NULL: the thermal model's die means, at the
+ * midpoint of the previous and current value (run_maintenance_point.py:
+ * 229-234).  Asynchronous on `stream`. */
+int hbfsim_retention_advance_v1(hbfsim_context* context, uint64_t end_ns,
+                                const double* die_temp_k, void* stream);
+/* Blocks due at at_ns (due_reasons, reliability.py:76-88), ascending, with
+ * reason bits (1 WALL_24H_SCENARIO_CADENCE, 2 EQUIVALENT_AGE_24H_
+ * CONSERVATIVE_POLICY) into device arrays of `capacity` entries; *count
+ * (host) gets the number due, which may exceed capacity.  Synchronous. */
+int hbfsim_retention_due_v1(hbfsim_context* context, uint64_t at_ns,
+                            uint32_t* blocks, uint8_t* reasons,
+                            uint64_t capacity, uint64_t* count, void* stream);
+/* Committed refresh of the listed blocks (device array) at the frontier
+ * (record_refresh_terminal, reliability.py:172-187). */
+int hbfsim_retention_refresh_v1(hbfsim_context* context, const uint32_t* blocks,
+                                uint64_t count, void* stream);
+/* Completed erases of the listed blocks (_media_terminal, 138-159). */
+int hbfsim_retention_record_erase_v1(hbfsim_context* context,
+                                     const uint32_t* blocks, uint64_t count,
+                                     void* stream);
+/* Every modeled write of an access batch (device arrays) as one completed
+ * program of its block (record_program, reliability.py:161-165). */
+int hbfsim_retention_record_programs_v1(hbfsim_context* context,
+                                        const uint64_t* address,
+                                        const uint32_t* bytes,
+                                        const uint8_t* operation,
+                                        uint64_t count, void* stream);
+/* Host copies (NULL to skip): equivalent age (ns, fp64), next wall due,
+ * last committed refresh (UINT64_MAX: none), counts [4][blocks] (program
+ * started, program completed, erase started, erase completed), frontier.
+ * Returns HBFSIM_INVALID_ARGUMENT once after a device-side rejection (a
+ * temperature not finite and positive, a block id out of range). */
+int hbfsim_get_retention_v1(hbfsim_context* context, double* age_ns,
+                            uint64_t* next_wall_due_ns,
+                            uint64_t* last_refresh_commit_ns, uint32_t* counts,
+                            uint64_t blocks, uint64_t* frontier_ns);
+
 #ifdef __cplusplus
 }
 #endif

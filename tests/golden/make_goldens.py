@@ -14,6 +14,10 @@ Fixtures written:
                          fast-model traces, all computed by the reference's own
                          functions (src/cuda_runtime/device/hbf_device.cuh,
                          src/hybrid/calibrator.cpp).
+  retention_goldens.json per-block retention ages, due reasons, refreshes and
+                         program / erase counts from the reference
+                         ReliabilityLedger (experiments/eq3_system_thermal/
+                         reliability.py).
   thermal_goldens.json   layered RC grids built by the reference exporter
                          (tools/eq3_layered_export.py discretize()/network())
                          and advanced by the reference ThermalModel
@@ -158,6 +162,74 @@ def lru_goldens() -> None:
     (HERE / "lru_goldens.json").write_text(json.dumps(cases))
 
 
+def retention_goldens() -> None:
+    """Per-block ages, due reasons, committed refreshes and program / erase
+    counts from the reference ReliabilityLedger
+    (experiments/eq3_system_thermal/reliability.py), driven as
+    run_maintenance_point.py:189, 225-234 drives it: one cohort per die per
+    epoch at the midpoint of the die's previous and current temperature."""
+    sys.path.insert(0, str(REF / "experiments" / "eq3_system_thermal"))
+    from reliability import DAY_NS, ReliabilityLedger  # noqa: E402  (reference code)
+    hour = 3_600_000_000_000
+    rng = random.Random(11)
+    cases = []
+    for ea, trigger, age0, wall0, epoch0 in ((1.04, "wall_only", DAY_NS * 9, 0, 0),
+                                             (1.08, "equivalent_age_or_wall",
+                                              DAY_NS - hour, 0, 5_000),
+                                             (1.01, "equivalent_age_or_wall", 0,
+                                              DAY_NS // 2, 0)):
+        dies, per_die, t_init = 3, 4, 330.0
+        names = [f"d{d}/b{b}" for d in range(dies) for b in range(per_die)]
+        ledger = ReliabilityLedger({"ea_ev": ea, "refresh_trigger": trigger,
+                                    "initial_equivalent_age_ns": age0,
+                                    "initial_wall_age_ns": wall0,
+                                    "maintenance_epoch_ns": epoch0})
+        prev = [t_init] * dies
+        now = epoch0
+        steps = []
+        for epoch in range(14):
+            length = rng.choice([1_000_000, hour, 7 * hour, 123_456_789])
+            temps = [rng.uniform(300.0, 410.0) for _ in range(dies)]
+            for d in range(dies):
+                midpoint = (prev[d] + temps[d]) / 2
+                ledger.advance_temperature_many(names[d * per_die:(d + 1) * per_die], now,
+                                                now + length, midpoint)
+                prev[d] = temps[d]
+            now += length
+            programs = [rng.randrange(len(names)) for _ in range(rng.randrange(4))]
+            for b in programs:
+                ledger.record_program(names[b], now, True, f"p{epoch}.{b}")
+            erases = [rng.randrange(len(names)) for _ in range(rng.randrange(3))]
+            for b in erases:
+                ledger.record_erase(names[b], now, True, f"e{epoch}.{b}")
+            due = []
+            for n in names:
+                reasons = ledger.due_reasons(n, now)
+                due.append((1 if "WALL_24H_SCENARIO_CADENCE" in reasons else 0) |
+                           (2 if "EQUIVALENT_AGE_24H_CONSERVATIVE_POLICY" in reasons else 0))
+            refresh = [i for i in range(len(names)) if due[i] and rng.random() < 0.6]
+            for i in refresh:
+                ledger.record_refresh_terminal(names[i], now, True, f"m{epoch}.{i}")
+            blocks = ledger.snapshot()["blocks"]
+            rows = [blocks[n] for n in names]
+            steps.append({
+                "end_ns": now, "temps": temps, "programs": programs, "erases": erases,
+                "due": due, "refresh": refresh,
+                "age": [r["equivalent_age_ns"] for r in rows],
+                "next_due": [r["next_wall_due_ns"] for r in rows],
+                "last_commit": [-1 if r["last_refresh_commit_ns"] is None
+                                else r["last_refresh_commit_ns"] for r in rows],
+                "counts": [[r["program_phase_started_count"] for r in rows],
+                           [r["program_completed_count"] for r in rows],
+                           [r["erase_phase_started_count"] for r in rows],
+                           [r["erase_completed_count"] for r in rows]]})
+        cases.append({"ea_ev": ea, "refresh_trigger": trigger, "initial_age_ns": age0,
+                      "initial_wall_age_ns": wall0, "epoch_ns": epoch0, "dies": dies,
+                      "blocks_per_die": per_die, "initial_temperature_k": t_init,
+                      "steps": steps})
+    (HERE / "retention_goldens.json").write_text(json.dumps(cases))
+
+
 def main() -> int:
     if not REF_BIN.exists():
         print("build oracle/_ref/ref_goldens first (make -C oracle)", file=sys.stderr)
@@ -165,6 +237,7 @@ def main() -> int:
     device_goldens()
     thermal_goldens()
     lru_goldens()
+    retention_goldens()
     return 0
 
 

@@ -272,3 +272,37 @@ def test_empirical_fast_path_traces(golden_dir):
         assert np.all(status == 1)
         assert done.tolist() == [s[4] for s in steps]
         assert stats["fast_modeled_ns"] == sum(s[5] for s in steps) % (1 << 64)
+
+
+# ---- per-block retention ledger (experiments/eq3_system_thermal/reliability.py) ----
+
+def replay_retention(case):
+    """Replays one golden scenario through the oracle ledger; yields
+    (step, ledger, due blocks, due bits) after every epoch."""
+    import retention_oracle as ro
+    led = ro.Ledger(case["dies"], case["blocks_per_die"], case["ea_ev"], case["initial_age_ns"],
+                    case["initial_wall_age_ns"], case["epoch_ns"], case["refresh_trigger"],
+                    case["initial_temperature_k"])
+    for step in case["steps"]:
+        led.advance(step["end_ns"], step["temps"], midpoint=True)
+        led.program(step["programs"])
+        led.erase(step["erases"])
+        blocks, bits = led.due(step["end_ns"])
+        led.refresh(step["refresh"])
+        yield step, led, blocks, bits
+
+
+def test_retention_oracle_against_reference_ledger(golden_dir):
+    cases = json.loads((golden_dir / "retention_goldens.json").read_text())
+    assert len(cases) == 3
+    for case in cases:
+        n = case["dies"] * case["blocks_per_die"]
+        for step, led, blocks, bits in replay_retention(case):
+            want = np.zeros(n, np.uint8)
+            want[blocks] = bits
+            assert want.tolist() == step["due"]
+            assert led.age.tolist() == step["age"]          # bit-exact: same float steps
+            assert led.next_due.tolist() == step["next_due"]
+            assert [-1 if v == (1 << 64) - 1 else int(v) for v in led.last_commit] == \
+                step["last_commit"]
+            assert led.counts.tolist() == step["counts"]
