@@ -293,7 +293,7 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=8,
                     help="config-1 decode steps in the trace (8 = the full config; "
                          "fewer only for small profiling captures)")
-    ap.add_argument("--only-extra", choices=["empirical_vmem", "thermal_coupled"],
+    ap.add_argument("--only-extra", choices=["empirical_vmem", "thermal_coupled", "retention"],
                     help="run one secondary measurement alone and print its JSON "
                          "(profiling captures); not a bench line")
     args = ap.parse_args()
@@ -303,7 +303,8 @@ def main():
     if args.only_extra:
         import torch
         torch.cuda.set_device(0)
-        run = run_vmem if args.only_extra == "empirical_vmem" else run_c3
+        run = {"empirical_vmem": run_vmem, "thermal_coupled": run_c3,
+               "retention": run_retention}[args.only_extra]
         with tempfile.TemporaryDirectory() as tmp:
             print_result(run(args, torch.device("cuda", 0), tmp))
         return 0
@@ -564,7 +565,71 @@ def run_extras(args, device, tmp):
     out["thermal_step"] = th
     out["thermal_coupled"] = run_c3(args, device, tmp)
     out["empirical_vmem"] = run_vmem(args, device, tmp)
+    out["retention"] = run_retention(args, device, tmp)
     return out
+
+
+def retention_profile() -> dict:
+    """A die-model profile shaped like the reference's cd8p device (32
+    channels x 8 dies x 4 planes, 4 KiB pages, 256 pages per block) with
+    2 TiB of media: 2,097,152 blocks."""
+    from hbfsim_b200 import workloads as wl
+    p = wl.c0_profile()
+    p.update(name="bench-retention", capacity_bytes=2048 << 30, page_bytes=4096, channels=32,
+             dies_per_channel=8, planes_per_die=4, pages_per_block=256)
+    return p
+
+
+def run_retention(args, device, tmp):
+    """The per-block retention ledger over 2,097,152 blocks: epochs of one
+    hour at per-die temperatures, then the due query (stable compaction) of
+    the equivalent-age-or-wall trigger."""
+    import torch
+    from hbfsim_b200 import Context, workloads as wl
+    p = retention_profile()
+    w = wl.Workload("ret", p, 1, 4096, wl.RANGE_BASE, 1 << 30)
+    ctx = Context(w.write_profile(tmp), report_dir=f"{tmp}/report-ret", mode=3)
+    n = ctx.retention_configure(1.04, 330.0, refresh_trigger="equivalent_age_or_wall")
+    dies = p["channels"] * p["dies_per_channel"]
+    rng = np.random.default_rng(0)
+    temps = [torch.from_numpy(rng.uniform(320.0, 400.0, dies)).to(device) for _ in range(8)]
+    hour = 3_600_000_000_000
+    stream = torch.cuda.current_stream()
+    for k in range(3):
+        ctx.retention_advance((k + 1) * hour, temps[k], stream)
+    torch.cuda.synchronize()
+    steps = 50
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(steps):
+        ctx.retention_advance((k + 4) * hour, temps[k % 8], stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    adv_ms = e0.elapsed_time(e1) / steps
+    t0 = time.perf_counter()
+    due_blocks, _ = ctx.retention_due((steps + 3) * hour, stream)
+    due_ms = (time.perf_counter() - t0) * 1e3
+    ctx.close()
+    res = {"workload": "retention ledger: 2,097,152 blocks (32 ch x 8 dies x 4 planes x 2048 "
+                       "blocks), 1 h epochs at per-die temperatures, Ea 1.04 eV",
+           "blocks": n, "advance_ms_per_epoch": adv_ms,
+           "advance_gbs_16B_per_block": 16 * n / (adv_ms * 1e-3) / 1e9,
+           "due_query_ms_wall": due_ms, "due_blocks": int(due_blocks.size),
+           "value": n / (adv_ms * 1e-3), "unit": "block-epochs/s"}
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, str(REPO / "oracle"))
+        import retention_oracle as ro
+        led = ro.Ledger(dies, n // dies, 1.04, refresh_trigger="equivalent_age_or_wall",
+                        initial_temperature_k=330.0)
+        host = [t.cpu().numpy() for t in temps]
+        t0 = time.perf_counter()
+        for k in range(5):
+            led.advance((k + 1) * hour, host[k], midpoint=False)
+        dt = (time.perf_counter() - t0) / 5
+        res["cpu_baseline"] = {"value": n / dt, "unit": "block-epochs/s", "cores": 1,
+                               "kind": "port",
+                               "sample": "5 epochs of the same ledger, numpy per die cohort"}
+    return res
 
 
 def run_vmem(args, device, tmp):
