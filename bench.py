@@ -293,7 +293,8 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=8,
                     help="config-1 decode steps in the trace (8 = the full config; "
                          "fewer only for small profiling captures)")
-    ap.add_argument("--only-extra", choices=["empirical_vmem", "thermal_coupled", "retention"],
+    ap.add_argument("--only-extra", choices=["empirical_vmem", "thermal_coupled", "retention",
+                                             "prefetch_sweep"],
                     help="run one secondary measurement alone and print its JSON "
                          "(profiling captures); not a bench line")
     args = ap.parse_args()
@@ -304,7 +305,7 @@ def main():
         import torch
         torch.cuda.set_device(0)
         run = {"empirical_vmem": run_vmem, "thermal_coupled": run_c3,
-               "retention": run_retention}[args.only_extra]
+               "retention": run_retention, "prefetch_sweep": run_prefetch}[args.only_extra]
         with tempfile.TemporaryDirectory() as tmp:
             print_result(run(args, torch.device("cuda", 0), tmp))
         return 0
@@ -566,7 +567,63 @@ def run_extras(args, device, tmp):
     out["thermal_coupled"] = run_c3(args, device, tmp)
     out["empirical_vmem"] = run_vmem(args, device, tmp)
     out["retention"] = run_retention(args, device, tmp)
+    out["prefetch_sweep"] = run_prefetch(args, device, tmp)
     return out
+
+
+def run_prefetch(args, device, tmp):
+    """The prefetch-model sweep: 4,032 cells (the reference sweep's grid of
+    6 read latencies x 14 policies / accuracies, times lead distances 1-48)
+    on a 1,000,000-access MoE stream shaped like Qwen3-30B-A3B (48 layers,
+    128 experts, 8 per token, 2 pages per expert), one warp per cell."""
+    import torch
+    from hbfsim_b200 import prefetch_sweep
+    rng = np.random.default_rng(0)
+    tokens = 1_000_000 // (48 * 8 * 2) + 1
+    order = np.argsort(rng.random((tokens * 48, 128)), axis=1)[:, :8]
+    layer = np.tile(np.arange(48), tokens)[:, None]
+    base = (layer * 128 + order) * 2
+    pages = (base[:, :, None] + np.arange(2)).reshape(-1)[:1_000_000].astype(np.uint64)
+    dev = torch.from_numpy(pages.view(np.int64)).to(device)
+    cells = []
+    for lead in range(1, 49):
+        for read in (1_000, 2_000, 4_000, 5_000, 10_000, 20_000):
+            common = {"lead_distance": lead, "buffer_pages": 64, "max_in_flight": 32,
+                      "read_latency_ns": read, "compute_ns_per_access": 4_000, "seed": 7}
+            cells.append(dict(common, policy="none"))
+            cells.append(dict(common, policy="next_page"))
+            for acc in (0.0, 0.1, 0.2, 0.3, 0.4, 0.5, 0.6, 0.7, 0.8, 0.9, 0.95, 1.0):
+                cells.append(dict(common, policy="accuracy", accuracy=acc))
+    prefetch_sweep(dev[:10_000], cells[:8])  # warm up (module load, first launch)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    stats = prefetch_sweep(dev, cells)
+    dt = time.perf_counter() - t0
+    steps = len(cells) * pages.size
+    res = {"workload": f"{len(cells)} sweep cells on a 1,000,000-page MoE stream (Qwen3-30B-A3B "
+                       "shape), buffer 64 pages, 32 media reads in flight, 4 us compute per "
+                       "access",
+           "cells": len(cells), "accesses": int(pages.size), "seconds": dt,
+           "value": steps / dt, "unit": "cell-accesses/s",
+           # the group's no-prefetch cell sits 13 cells before its accuracy-1.0 cell
+           "best_speedup_over_no_prefetch": max(
+               stats[k - 13]["total_ns"] / s_["total_ns"] for k, s_ in enumerate(stats)
+               if cells[k]["policy"] == "accuracy" and cells[k]["accuracy"] == 1.0)}
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, str(REPO / "oracle"))
+        import hbf_oracle as ho
+        sample = [cells[k] for k in (2, 10, 13, 100)]
+        t0 = time.perf_counter()
+        for c in sample:
+            ho.prefetch_run(pages, {"policy": {"none": 0, "next_page": 1, "accuracy": 2}[c["policy"]],
+                                    "accuracy": c.get("accuracy", 1.0), "lead": c["lead_distance"],
+                                    "buffer": 64, "in_flight": 32, "read_ns": c["read_latency_ns"],
+                                    "compute_ns": 4_000, "seed": 7})
+        cdt = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": len(sample) * pages.size / cdt,
+                               "unit": "cell-accesses/s", "cores": 1, "kind": "port",
+                               "sample": "4 cells of the same sweep, single thread"}
+    return res
 
 
 def retention_profile() -> dict:

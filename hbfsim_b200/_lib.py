@@ -122,6 +122,18 @@ class RetentionConfigV1(ctypes.Structure):
                 ("refresh_trigger", u32), ("reserved", u32)]
 
 
+class PrefetchCellV1(ctypes.Structure):
+    _fields_ = [("policy", u32), ("lead_distance", u32), ("accuracy", dbl),
+                ("buffer_pages", u32), ("max_in_flight", u32), ("read_latency_ns", u64),
+                ("compute_ns_per_access", u64), ("seed", u64)]
+
+
+class PrefetchStatsV1(ctypes.Structure):
+    _fields_ = [("total_ns", u64), ("stall_ns", u64), ("demand_accesses", u64),
+                ("demand_misses", u64), ("prefetch_hits", u64), ("prefetch_issued", u64),
+                ("prefetch_wasted", u64)]
+
+
 # Every exported function with its signature (restype, argtypes).
 SIGNATURES = {
     "hbfsim_abi_version": (u32, []),
@@ -169,6 +181,7 @@ SIGNATURES = {
     "hbfsim_retention_record_erase_v1": (i32, [vp, vp, u64, vp]),
     "hbfsim_retention_record_programs_v1": (i32, [vp, vp, vp, vp, u64, vp]),
     "hbfsim_get_retention_v1": (i32, [vp, vp, vp, vp, vp, u64, ctypes.POINTER(u64)]),
+    "hbfsim_prefetch_sweep_v1": (i32, [vp, u64, vp, u32, vp, vp]),
 }
 
 

@@ -19,7 +19,9 @@ import numpy as np
 from . import _lib
 from ._lib import HbfsimError, check
 
-__all__ = ["Context", "HbfsimError", "BatchResult"]
+__all__ = ["Context", "HbfsimError", "BatchResult", "prefetch_sweep", "PREFETCH_POLICIES"]
+
+PREFETCH_POLICIES = {"none": 0, "next_page": 1, "accuracy": 2}
 
 
 @dataclass
@@ -447,3 +449,30 @@ class Context:
         return {"age_ns": age, "next_wall_due_ns": due, "last_refresh_commit_ns": last,
                 "program_started": c[0], "program_completed": c[1], "erase_started": c[2],
                 "erase_completed": c[3], "frontier_ns": int(frontier.value)}
+
+
+def prefetch_sweep(pages, cells, stream=None) -> list[dict]:
+    """The prefetch model (hbfsim::simulate_prefetch) for every cell on one
+    page stream (uint64/int64 device tensor).  A cell is a dict with keys
+    policy ("none" | "next_page" | "accuracy"), accuracy, lead_distance,
+    buffer_pages, max_in_flight, read_latency_ns, compute_ns_per_access,
+    seed (the reference's PrefetchConfig defaults fill missing keys).
+    Returns one stats dict per cell."""
+    lib = _lib.load()
+    n = len(cells)
+    arr = (_lib.PrefetchCellV1 * max(1, n))()
+    for k, c in enumerate(cells):
+        policy = c.get("policy", "none")
+        arr[k] = _lib.PrefetchCellV1(PREFETCH_POLICIES.get(policy, policy),
+                                     int(c.get("lead_distance", 1)),
+                                     float(c.get("accuracy", 1.0)),
+                                     int(c.get("buffer_pages", 64)),
+                                     int(c.get("max_in_flight", 32)),
+                                     int(c.get("read_latency_ns", 10_000)),
+                                     int(c.get("compute_ns_per_access", 0)),
+                                     int(c.get("seed", 1)))
+    out = (_lib.PrefetchStatsV1 * max(1, n))()
+    check(lib.hbfsim_prefetch_sweep_v1(_ptr(pages), pages.numel(), arr, n, out,
+                                       ctypes.c_void_p(_stream_handle(stream))),
+          "hbfsim_prefetch_sweep_v1")
+    return [{f: getattr(out[k], f) for f, _ in _lib.PrefetchStatsV1._fields_} for k in range(n)]

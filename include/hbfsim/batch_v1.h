@@ -426,6 +426,43 @@ int hbfsim_get_retention_v1(hbfsim_context* context, double* age_ns,
                             uint64_t* last_refresh_commit_ns, uint32_t* counts,
                             uint64_t blocks, uint64_t* frontier_ns);
 
+/* ---- prefetch model sweeps ----
+ * Replaces hbfsim::simulate_prefetch (src/prefetch/prefetch_model.cpp:117-195,
+ * include/hbfsim/prefetch_model.hpp:24-99) over many configurations at once:
+ * every cell walks the same page stream with its own policy, accuracy, lead
+ * distance, staging buffer, media concurrency, read latency, compute time
+ * per access and predictor seed.  Results equal the reference's, cell for
+ * cell. */
+typedef struct hbfsim_prefetch_cell_v1 {
+    uint32_t policy;                  /* 0 None, 1 NextPage, 2 Accuracy */
+    uint32_t lead_distance;
+    double accuracy;
+    uint32_t buffer_pages;
+    uint32_t max_in_flight;
+    uint64_t read_latency_ns;
+    uint64_t compute_ns_per_access;
+    uint64_t seed;
+} hbfsim_prefetch_cell_v1;
+
+typedef struct hbfsim_prefetch_stats_v1 {
+    uint64_t total_ns;
+    uint64_t stall_ns;
+    uint64_t demand_accesses;
+    uint64_t demand_misses;
+    uint64_t prefetch_hits;
+    uint64_t prefetch_issued;
+    uint64_t prefetch_wasted;
+} hbfsim_prefetch_stats_v1;
+
+/* pages: device array of `count` media pages in demand order; cells and
+ * out: host arrays of cell_count entries.  Synchronous on `stream`.
+ * HBFSIM_UNSUPPORTED for a staging buffer beyond about 8,000 pages or a
+ * stream of 2^32 - 2 accesses or more. */
+int hbfsim_prefetch_sweep_v1(const uint64_t* pages, uint64_t count,
+                             const hbfsim_prefetch_cell_v1* cells,
+                             uint32_t cell_count, hbfsim_prefetch_stats_v1* out,
+                             void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -742,3 +742,178 @@ int or_run_empirical_batch(const or_range* ranges, uint32_t count, const or_empi
     free(order);
     return 0;
 }
+
+/* ---- prefetch model ---- */
+
+/* The 64-bit Mersenne Twister of the C++ standard library (std::mt19937_64,
+ * Matsumoto & Nishimura 2000; parameters from the standard's [rand.predef])
+ * and the standard's generate_canonical for a double from one 64-bit draw,
+ * as std::uniform_real_distribution<double>(0, 1) uses it. */
+typedef struct or_mt64 {
+    uint64_t x[312];
+    uint32_t i;
+} or_mt64;
+
+static void or_mt64_seed(or_mt64* m, uint64_t seed)
+{
+    m->x[0] = seed;
+    for (uint32_t k = 1; k < 312; ++k)
+        m->x[k] = UINT64_C(6364136223846793005) * (m->x[k - 1] ^ (m->x[k - 1] >> 62)) + k;
+    m->i = 312;
+}
+
+static uint64_t or_mt64_next(or_mt64* m)
+{
+    if (m->i >= 312) {
+        for (uint32_t k = 0; k < 312; ++k) {
+            const uint64_t y = (m->x[k] & UINT64_C(0xFFFFFFFF80000000)) |
+                               (m->x[(k + 1) % 312] & UINT64_C(0x7FFFFFFF));
+            m->x[k] = m->x[(k + 156) % 312] ^ (y >> 1) ^
+                      ((y & 1) ? UINT64_C(0xB5026F5AA96619E9) : 0);
+        }
+        m->i = 0;
+    }
+    uint64_t y = m->x[m->i++];
+    y ^= (y >> 29) & UINT64_C(0x5555555555555555);
+    y ^= (y << 17) & UINT64_C(0x71D67FFFEDA60000);
+    y ^= (y << 37) & UINT64_C(0xFFF7EEE000000000);
+    y ^= y >> 43;
+    return y;
+}
+
+static double or_canonical(or_mt64* m)
+{
+    const double r = (double)or_mt64_next(m) / 18446744073709551616.0;
+    return r >= 1.0 ? 0x1.fffffffffffffp-1 : r;
+}
+
+/* prefetch_model.cpp:23-50: max_in_flight servers; a read issued at `now`
+ * takes the server that frees first, starts at max(now, free) and ends one
+ * read latency later.  A binary min-heap of free times. */
+typedef struct or_heap {
+    uint64_t* v;
+    uint32_t n;
+} or_heap;
+
+static uint64_t or_heap_pop_push(or_heap* h, uint64_t now, uint64_t latency)
+{
+    const uint64_t earliest = h->v[0];
+    const uint64_t done = (now > earliest ? now : earliest) + latency;
+    /* replace the root with `done` and sift down */
+    uint32_t k = 0;
+    for (;;) {
+        const uint32_t l = 2 * k + 1, r = l + 1;
+        uint32_t m = k;
+        uint64_t mv = done;
+        if (l < h->n && h->v[l] < mv) { m = l; mv = h->v[l]; }
+        if (r < h->n && h->v[r] < mv) { m = r; mv = h->v[r]; }
+        if (m == k) break;
+        h->v[k] = h->v[m];
+        k = m;
+    }
+    h->v[k] = done;
+    return done;
+}
+
+/* prefetch_model.cpp:52-104: pages fetched and not yet used, oldest first;
+ * inserting past capacity drops the oldest. */
+typedef struct or_staging {
+    uint64_t* page;
+    uint64_t* arrival;
+    uint32_t size, capacity;
+} or_staging;
+
+static int or_staging_find(const or_staging* b, uint64_t page)
+{
+    for (uint32_t k = 0; k < b->size; ++k)
+        if (b->page[k] == page) return (int)k;
+    return -1;
+}
+
+static uint64_t or_staging_insert(or_staging* b, uint64_t page, uint64_t arrival)
+{
+    b->page[b->size] = page;
+    b->arrival[b->size] = arrival;
+    ++b->size;
+    uint64_t evicted = 0;
+    while (b->size > b->capacity) {
+        memmove(b->page, b->page + 1, sizeof(uint64_t) * (b->size - 1));
+        memmove(b->arrival, b->arrival + 1, sizeof(uint64_t) * (b->size - 1));
+        --b->size;
+        ++evicted;
+    }
+    return evicted;
+}
+
+static uint64_t or_staging_take(or_staging* b, int k)
+{
+    const uint64_t arrival = b->arrival[k];
+    memmove(b->page + k, b->page + k + 1, sizeof(uint64_t) * (b->size - (uint32_t)k - 1));
+    memmove(b->arrival + k, b->arrival + k + 1,
+            sizeof(uint64_t) * (b->size - (uint32_t)k - 1));
+    --b->size;
+    return arrival;
+}
+
+/* prefetch_model.cpp:117-195 simulate_prefetch */
+int or_prefetch_run(const uint64_t* pages, uint64_t n, const or_prefetch_cell* c,
+                    or_prefetch_stats* s)
+{
+    memset(s, 0, sizeof *s);
+    s->demand_accesses = n;
+    if (n == 0) return 0;
+    or_heap media;
+    media.n = c->max_in_flight ? c->max_in_flight : 1;
+    media.v = (uint64_t*)calloc(media.n, sizeof(uint64_t));
+    or_staging buf;
+    buf.capacity = c->buffer_pages ? c->buffer_pages : 1;
+    buf.size = 0;
+    buf.page = (uint64_t*)malloc(sizeof(uint64_t) * (buf.capacity + 1));
+    buf.arrival = (uint64_t*)malloc(sizeof(uint64_t) * (buf.capacity + 1));
+    or_mt64* rng = (or_mt64*)malloc(sizeof(or_mt64));
+    if (!media.v || !buf.page || !buf.arrival || !rng) {
+        free(media.v); free(buf.page); free(buf.arrival); free(rng);
+        return -1;
+    }
+    or_mt64_seed(rng, c->seed);
+    uint64_t clock = 0;
+    uint64_t wrong = UINT64_C(1) << 60;
+    for (uint64_t i = 0; i < n; ++i) {
+        clock += c->compute_ns_per_access;
+        if (c->policy != 0 && c->lead_distance > 0) {
+            const uint64_t target = i + c->lead_distance;
+            int predict = 0;
+            uint64_t predicted = 0;
+            if (c->policy == 1) {
+                predicted = pages[i] + 1;
+                predict = 1;
+            } else if (target < n) {
+                predicted = or_canonical(rng) < c->accuracy ? pages[target] : wrong++;
+                predict = 1;
+            }
+            if (predict && or_staging_find(&buf, predicted) < 0) {
+                const uint64_t arrival = or_heap_pop_push(&media, clock, c->read_latency_ns);
+                s->prefetch_wasted += or_staging_insert(&buf, predicted, arrival);
+                ++s->prefetch_issued;
+            }
+        }
+        const int k = or_staging_find(&buf, pages[i]);
+        if (k >= 0) {
+            const uint64_t arrival = or_staging_take(&buf, k);
+            ++s->prefetch_hits;
+            if (arrival > clock) {
+                s->stall_ns += arrival - clock;
+                clock = arrival;
+            }
+        } else {
+            const uint64_t arrival = or_heap_pop_push(&media, clock, c->read_latency_ns);
+            ++s->demand_misses;
+            s->stall_ns += arrival - clock;
+            clock = arrival;
+        }
+    }
+    s->prefetch_wasted += buf.size;
+    s->total_ns = clock;
+    free(media.v); free(buf.page); free(buf.arrival); free(rng);
+    return 0;
+}

@@ -208,6 +208,34 @@ int or_run_empirical_batch(const or_range* ranges, uint32_t count, const or_empi
                            uint64_t* state, uint64_t* done, uint64_t* latency,
                            uint8_t* status, or_stats* stats);
 
+/* ---- prefetch model (src/prefetch/prefetch_model.cpp, include/hbfsim/
+ * prefetch_model.hpp): a discrete-event walk of a page stream with a
+ * prefetcher, a FIFO staging buffer and max_in_flight media servers. ---- */
+typedef struct or_prefetch_cell {
+    uint32_t policy;          /* 0 none, 1 next page, 2 accuracy */
+    uint32_t lead_distance;
+    double accuracy;
+    uint32_t buffer_pages;
+    uint32_t max_in_flight;
+    uint64_t read_latency_ns;
+    uint64_t compute_ns_per_access;
+    uint64_t seed;
+} or_prefetch_cell;
+
+typedef struct or_prefetch_stats {
+    uint64_t total_ns;
+    uint64_t stall_ns;
+    uint64_t demand_accesses;
+    uint64_t demand_misses;
+    uint64_t prefetch_hits;
+    uint64_t prefetch_issued;
+    uint64_t prefetch_wasted;
+} or_prefetch_stats;
+
+/* Returns 0, or -1 when memory runs out. */
+int or_prefetch_run(const uint64_t* pages, uint64_t n, const or_prefetch_cell* cell,
+                    or_prefetch_stats* stats);
+
 #ifdef __cplusplus
 }
 #endif

@@ -107,6 +107,8 @@ def _load() -> ctypes.CDLL:
     lib.or_empirical_control_valid.argtypes = [p]
     lib.or_empirical_request_service.restype = ctypes.c_int
     lib.or_empirical_request_service.argtypes = [p, u64, u64, u32, p, p, p]
+    lib.or_prefetch_run.restype = ctypes.c_int
+    lib.or_prefetch_run.argtypes = [p, u64, p, p]
     lib.or_run_empirical_batch.restype = ctypes.c_int
     lib.or_run_empirical_batch.argtypes = [p, u32, p, u32, u64, p, p, p, p, u64, p, p, p, p,
                                            p]
@@ -261,6 +263,29 @@ def run_empirical(ranges, count, e: Empirical, time_scale, request_timeout_ns, a
     if rc != 0:
         raise MemoryError("oracle allocation failed")
     return done, latency, status, {f: getattr(stats, f) for f, _ in Stats._fields_}
+
+
+class PrefetchCell(ctypes.Structure):
+    _fields_ = [("policy", ctypes.c_uint32), ("lead_distance", ctypes.c_uint32),
+                ("accuracy", ctypes.c_double), ("buffer_pages", ctypes.c_uint32),
+                ("max_in_flight", ctypes.c_uint32), ("read_latency_ns", ctypes.c_uint64),
+                ("compute_ns_per_access", ctypes.c_uint64), ("seed", ctypes.c_uint64)]
+
+
+PREFETCH_STATS = ("total_ns", "stall_ns", "demand_accesses", "demand_misses",
+                  "prefetch_hits", "prefetch_issued", "prefetch_wasted")
+
+
+def prefetch_run(pages: np.ndarray, cell: dict) -> tuple:
+    """The prefetch model on one cell; returns the 7 stats in PREFETCH_STATS
+    order."""
+    c = PrefetchCell(cell["policy"], cell["lead"], cell["accuracy"], cell["buffer"],
+                     cell["in_flight"], cell["read_ns"], cell["compute_ns"], cell["seed"])
+    out = (ctypes.c_uint64 * 7)()
+    pages = np.ascontiguousarray(pages, np.uint64)
+    if LIB.or_prefetch_run(_ptr(pages), pages.size, ctypes.byref(c), out) != 0:
+        raise MemoryError("oracle allocation failed")
+    return tuple(int(v) for v in out)
 
 
 def cores() -> int:

@@ -14,6 +14,9 @@ Fixtures written:
                          fast-model traces, all computed by the reference's own
                          functions (src/cuda_runtime/device/hbf_device.cuh,
                          src/hybrid/calibrator.cpp).
+  prefetch_goldens.json  statistics of the reference prefetch model
+                         (src/prefetch/prefetch_model.cpp, compiled from
+                         source) for sweep cells on four page streams.
   retention_goldens.json per-block retention ages, due reasons, refreshes and
                          program / erase counts from the reference
                          ReliabilityLedger (experiments/eq3_system_thermal/
@@ -42,6 +45,7 @@ HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
 REF = Path(os.environ.get("HBFSIM_REFERENCE", "/root/reference"))
 REF_BIN = REPO / "oracle" / "_ref" / "ref_goldens"
+REF_PREFETCH = REPO / "oracle" / "_ref" / "ref_prefetch"
 
 
 def load_exporter():
@@ -230,6 +234,63 @@ def retention_goldens() -> None:
     (HERE / "retention_goldens.json").write_text(json.dumps(cases))
 
 
+def prefetch_streams() -> dict:
+    """Page streams for the prefetch goldens: sequential, uniform random,
+    MoE-like (per token and layer, 4 of 16 experts, 2 pages each, shuffled)
+    and a small looping working set with noise."""
+    rng = random.Random(21)
+    streams = {"sequential": list(range(3000)),
+               "random": [rng.randrange(24000) for _ in range(3000)]}
+    moe = []
+    for _token in range(60):
+        for layer in range(6):
+            experts = list(range(16))
+            rng.shuffle(experts)
+            for e in experts[:4]:
+                base = (layer * 16 + e) * 2
+                moe += [base, base + 1]
+    streams["moe"] = moe
+    streams["loop"] = [(k % 50) if rng.random() < 0.85 else rng.randrange(10_000)
+                       for k in range(3000)]
+    return streams
+
+
+def prefetch_goldens() -> None:
+    """Statistics of the reference prefetch model
+    (src/prefetch/prefetch_model.cpp, compiled from source into
+    oracle/_ref/ref_prefetch) for cells across every policy and parameter,
+    on the streams above."""
+    rng = random.Random(5)
+    out = []
+    for name, pages in prefetch_streams().items():
+        cells = [(0, 1.0, 1, 64, 32, 10_000, 0, 1), (1, 1.0, 1, 64, 32, 10_000, 4_000, 1),
+                 (1, 1.0, 0, 64, 32, 10_000, 4_000, 1), (2, 0.5, 0, 64, 32, 5_000, 100, 3)]
+        if name == "sequential":  # the reference sweep's grid
+            for read in (1_000, 2_000, 4_000, 5_000, 10_000, 20_000):
+                cells.append((0, 0.0, 8, 64, 32, read, 4_000, 7))
+                cells.append((1, 0.0, 8, 64, 32, read, 4_000, 7))
+                for acc in (0.0, 0.1, 0.2, 0.3, 0.4, 0.5, 0.6, 0.7, 0.8, 0.9, 0.95, 1.0):
+                    cells.append((2, acc, 8, 64, 32, read, 4_000, 7))
+        for _ in range(60):
+            cells.append((rng.choice((0, 1, 2, 2, 2)), rng.choice((0.0, 0.3, 0.7, 0.95, 1.0)),
+                          rng.choice((1, 2, 8, 40, 500)), rng.choice((1, 3, 8, 64, 200)),
+                          rng.choice((1, 4, 32, 300)), rng.choice((700, 10_000, 20_000)),
+                          rng.choice((0, 50, 4_000)), rng.randrange(1 << 40)))
+        with tempfile.TemporaryDirectory() as tmp:
+            stream_path = Path(tmp) / "stream.bin"
+            stream_path.write_bytes(b"".join(int(p).to_bytes(8, "little") for p in pages))
+            cell_path = Path(tmp) / "cells.txt"
+            cell_path.write_text("".join(f"{c[0]} {c[1]!r} {c[2]} {c[3]} {c[4]} {c[5]} {c[6]} "
+                                         f"{c[7]}\n" for c in cells))
+            res = subprocess.run([str(REF_PREFETCH), str(stream_path), str(cell_path)],
+                                 check=True, capture_output=True, text=True).stdout
+        rows = [list(c) + [int(v) for v in line.split()]
+                for c, line in zip(cells, res.splitlines())]
+        assert len(rows) == len(cells)
+        out.append({"stream": name, "pages": pages, "cells": rows})
+    (HERE / "prefetch_goldens.json").write_text(json.dumps(out))
+
+
 def main() -> int:
     if not REF_BIN.exists():
         print("build oracle/_ref/ref_goldens first (make -C oracle)", file=sys.stderr)
@@ -238,6 +299,7 @@ def main() -> int:
     thermal_goldens()
     lru_goldens()
     retention_goldens()
+    prefetch_goldens()
     return 0
 
 

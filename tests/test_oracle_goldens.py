@@ -306,3 +306,25 @@ def test_retention_oracle_against_reference_ledger(golden_dir):
             assert [-1 if v == (1 << 64) - 1 else int(v) for v in led.last_commit] == \
                 step["last_commit"]
             assert led.counts.tolist() == step["counts"]
+
+
+# ---- prefetch model (src/prefetch/prefetch_model.cpp) ----
+
+PREFETCH_KEYS = ("policy", "accuracy", "lead", "buffer", "in_flight", "read_ns", "compute_ns",
+                 "seed")
+
+
+def test_prefetch_oracle_against_reference_model(golden_dir):
+    """The oracle's restatement (Mersenne Twister predictor draws, FIFO
+    staging buffer, min-heap media servers) against the reference model
+    compiled from its own source, cell for cell."""
+    streams = json.loads((golden_dir / "prefetch_goldens.json").read_text())
+    assert [s["stream"] for s in streams] == ["sequential", "random", "moe", "loop"]
+    cells = 0
+    for s in streams:
+        pages = np.array(s["pages"], np.uint64)
+        for row in s["cells"]:
+            got = ho.prefetch_run(pages, dict(zip(PREFETCH_KEYS, row[:8])))
+            assert list(got) == row[8:], (s["stream"], row[:8])
+            cells += 1
+    assert cells == 340
