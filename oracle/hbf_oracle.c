@@ -917,3 +917,251 @@ int or_prefetch_run(const uint64_t* pages, uint64_t n, const or_prefetch_cell* c
     free(media.v); free(buf.page); free(buf.arrival); free(rng);
     return 0;
 }
+
+/* ---- UCIe streaming link ---- */
+
+enum { OR_EV_ARRIVAL, OR_EV_FLIT, OR_EV_CONSUME, OR_EV_RETRY };
+
+typedef struct or_event {
+    uint64_t t;
+    uint64_t seq;      /* insertion order: equal times run in it (std::multimap) */
+    uint64_t id;
+    uint32_t kind, dir;
+    uint32_t count;    /* flit: messages it completes */
+    uint32_t grant;    /* flit: credit granules it returns */
+} or_event;
+
+typedef struct or_msg {
+    uint64_t id;
+    uint32_t remaining, emitted, started;
+} or_msg;
+
+typedef struct or_link {
+    const or_link_profile* p;
+    or_event* heap;
+    uint64_t heap_n, heap_cap, seq;
+    or_msg* queue[2];             /* rings of max_accepted: waiting to be sent */
+    uint64_t q_head[2], q_size[2];
+    uint64_t* sent[2];            /* rings: completed, waiting for delivery */
+    uint64_t s_head[2], s_size[2];
+    uint64_t now, cursor[2];
+    uint32_t credits[2];          /* 0 AR credits, 1 R credits */
+    uint32_t grant_pending[2];    /* 0 AR granules to return, 1 R granules */
+    uint64_t active[2];
+    int retry_pending[2];
+    uint64_t counters[2][8];
+    uint64_t flit_ns;
+    int error;
+} or_link;
+
+static int or_ev_less(const or_event* a, const or_event* b)
+{
+    return a->t < b->t || (a->t == b->t && a->seq < b->seq);
+}
+
+static void or_ev_push(or_link* L, or_event e)
+{
+    if (L->heap_n == L->heap_cap) {
+        const uint64_t cap = L->heap_cap ? 2 * L->heap_cap : 64;
+        or_event* h = (or_event*)realloc(L->heap, sizeof(or_event) * cap);
+        if (!h) { L->error = 1; return; }
+        L->heap = h;
+        L->heap_cap = cap;
+    }
+    e.seq = L->seq++;
+    uint64_t k = L->heap_n++;
+    while (k > 0) {
+        const uint64_t up = (k - 1) / 2;
+        if (!or_ev_less(&e, &L->heap[up])) break;
+        L->heap[k] = L->heap[up];
+        k = up;
+    }
+    L->heap[k] = e;
+}
+
+static or_event or_ev_pop(or_link* L)
+{
+    const or_event top = L->heap[0];
+    const or_event last = L->heap[--L->heap_n];
+    uint64_t k = 0;
+    for (;;) {
+        const uint64_t l = 2 * k + 1, r = l + 1;
+        uint64_t m = k;
+        const or_event* mv = &last;
+        if (l < L->heap_n && or_ev_less(&L->heap[l], mv)) { m = l; mv = &L->heap[l]; }
+        if (r < L->heap_n && or_ev_less(&L->heap[r], mv)) { m = r; mv = &L->heap[r]; }
+        if (m == k) break;
+        L->heap[k] = L->heap[m];
+        k = m;
+    }
+    if (L->heap_n) L->heap[k] = last;
+    return top;
+}
+
+static uint64_t or_add_time(or_link* L, uint64_t a, uint64_t b)
+{
+    if (a > UINT64_MAX - b) { L->error = 1; return UINT64_MAX; }
+    return a + b;
+}
+
+/* link.cpp:111-117 legal_grant: AoU grants are 1, 4, 8, ..., 128 granules */
+static uint32_t or_legal_grant(uint32_t pending)
+{
+    if (pending == 0) return 0;
+    if (pending < 4) return 1;
+    uint32_t grant = 4;
+    while (grant < 128 && grant * 2 <= pending) grant *= 2;
+    return grant;
+}
+
+static void or_retry(or_link* L, uint32_t d)
+{
+    /* the pending retry of a direction is always at its cursor: a second one
+     * at the same tick would run in the same step and change nothing */
+    if (L->retry_pending[d]) return;
+    L->retry_pending[d] = 1;
+    or_event e = {L->cursor[d], 0, 0, OR_EV_RETRY, d, 0, 0};
+    or_ev_push(L, e);
+}
+
+/* link.cpp:119-179 send_ready */
+static void or_send_ready(or_link* L, uint32_t d)
+{
+    uint32_t* credit = &L->credits[d];
+    uint32_t* pending = &L->grant_pending[1 - d];  /* reverse direction's granules */
+    if (L->cursor[d] > L->now) {
+        if (L->q_size[d] || *pending) or_retry(L, d);
+        return;
+    }
+    const uint64_t cap = L->p->max_accepted;
+    uint32_t used = 0, completed = 0;
+    while (L->q_size[d] && used < 48) {
+        or_msg* msg = &L->queue[d][L->q_head[d]];
+        if (!msg->started) {
+            const uint32_t full = d == 0 ? 3u : 14u;
+            if (*credit < full) break;
+            *credit -= full;   /* every granule is reserved at MsgStart */
+            msg->started = 1;
+        }
+        const uint32_t fragment = 48 - used < msg->remaining ? 48 - used : msg->remaining;
+        used += fragment;
+        msg->remaining -= fragment;
+        msg->emitted += fragment;
+        if (msg->remaining == 0) {
+            L->sent[d][(L->s_head[d] + L->s_size[d]) % cap] = msg->id;
+            ++L->s_size[d];
+            L->q_head[d] = (L->q_head[d] + 1) % cap;
+            --L->q_size[d];
+            ++completed;
+        }
+    }
+    const uint32_t grant = or_legal_grant(*pending);
+    if (used == 0 && grant == 0) return;
+    *pending -= grant;
+    L->cursor[d] = or_add_time(L, L->now, L->flit_ns);
+    const uint64_t delivery = or_add_time(L, L->cursor[d], L->p->propagation_ns);
+    or_event e = {delivery, 0, 0, OR_EV_FLIT, d, completed, grant};
+    or_ev_push(L, e);
+    if (L->q_size[d] || *pending) or_retry(L, d);
+    uint64_t* c = L->counters[d];
+    c[0] += 1;
+    c[1] += 256;
+    c[2] += 2;
+    c[3] += 4;
+    c[4] += 10;
+    c[5] += (uint64_t)used * 5;
+    c[6] += (uint64_t)(48 - used) * 5;
+    if (used == 0) c[7] += 1;
+}
+
+int or_link_run(const or_link_profile* p, const uint8_t* direction, const uint64_t* ready,
+                uint64_t m, uint64_t* delivered, or_link_result* out)
+{
+    or_link L;
+    memset(&L, 0, sizeof L);
+    memset(out, 0, sizeof *out);
+    L.p = p;
+    L.flit_ns = 32 / p->gt_per_second;   /* profile.cpp:63-67: 256 B at x64 */
+    L.credits[0] = p->initial_ar_granules;
+    L.credits[1] = p->initial_r_granules;
+    const uint64_t cap = p->max_accepted ? p->max_accepted : 1;
+    for (int d = 0; d < 2; ++d) {
+        L.queue[d] = (or_msg*)calloc(cap, sizeof(or_msg));
+        L.sent[d] = (uint64_t*)calloc(cap, sizeof(uint64_t));
+    }
+    /* deliveries of one step: (direction, id), consumed after the step */
+    uint64_t* step_id = (uint64_t*)malloc(sizeof(uint64_t) * 2 * cap);
+    uint32_t* step_dir = (uint32_t*)malloc(sizeof(uint32_t) * 2 * cap);
+    if (!L.queue[0] || !L.queue[1] || !L.sent[0] || !L.sent[1] || !step_id || !step_dir)
+        L.error = 1;
+    uint64_t next = 0;
+    while (!L.error) {
+        uint64_t t_event = L.heap_n ? L.heap[0].t : UINT64_MAX;
+        while (next < m) {
+            const uint32_t d = direction[next];
+            const uint64_t at = ready[next] > L.now ? ready[next] : L.now;
+            if (L.active[d] >= p->max_accepted || at > t_event) break;
+            or_event e = {at, 0, next + 1, OR_EV_ARRIVAL, d, 0, 0};   /* link.cpp:42-54 */
+            or_ev_push(&L, e);
+            ++L.active[d];
+            ++next;
+            if (at < t_event) t_event = at;
+        }
+        if (L.heap_n == 0) break;
+        /* link.cpp:181-227 step: every event at the earliest tick, in
+         * insertion order, then one send attempt per direction */
+        L.now = L.heap[0].t;
+        uint64_t n_step = 0;
+        while (L.heap_n && L.heap[0].t == L.now && !L.error) {
+            const or_event e = or_ev_pop(&L);
+            if (e.kind == OR_EV_ARRIVAL) {
+                or_msg* msg = &L.queue[e.dir][(L.q_head[e.dir] + L.q_size[e.dir]) % cap];
+                msg->id = e.id;
+                msg->remaining = e.dir == 0 ? 3u : 14u;
+                msg->emitted = 0;
+                msg->started = 0;
+                ++L.q_size[e.dir];
+            } else if (e.kind == OR_EV_FLIT) {
+                const uint32_t back = 1 - e.dir;   /* the grant returns the reverse credits */
+                const uint32_t maximum = back == 0 ? p->initial_ar_granules : p->initial_r_granules;
+                if (e.grant > maximum - L.credits[back]) { L.error = 1; break; }
+                L.credits[back] += e.grant;
+                for (uint32_t k = 0; k < e.count; ++k) {
+                    const uint64_t id = L.sent[e.dir][L.s_head[e.dir]];
+                    L.s_head[e.dir] = (L.s_head[e.dir] + 1) % cap;
+                    --L.s_size[e.dir];
+                    delivered[id - 1] = L.now;
+                    step_id[n_step] = id;
+                    step_dir[n_step] = e.dir;
+                    ++n_step;
+                }
+            } else if (e.kind == OR_EV_CONSUME) {
+                --L.active[e.dir];
+                uint32_t* pending = &L.grant_pending[e.dir];
+                const uint32_t amount = e.dir == 0 ? 3u : 14u;
+                if (*pending > 65535u - amount) { L.error = 1; break; }
+                *pending += amount;
+            } else {
+                L.retry_pending[e.dir] = 0;
+            }
+        }
+        if (L.error) break;
+        or_send_ready(&L, 0);
+        or_send_ready(&L, 1);
+        /* the driver consumes every delivery consume_ns after it (link.cpp:56-65) */
+        for (uint64_t k = 0; k < n_step; ++k) {
+            or_event e = {or_add_time(&L, L.now, p->consume_ns[step_dir[k]]), 0, step_id[k],
+                          OR_EV_CONSUME, step_dir[k], 0, 0};
+            or_ev_push(&L, e);
+        }
+    }
+    out->now = L.now;
+    out->ar_credits = L.credits[0];
+    out->r_credits = L.credits[1];
+    memcpy(out->counters, L.counters, sizeof L.counters);
+    free(L.heap);
+    for (int d = 0; d < 2; ++d) { free(L.queue[d]); free(L.sent[d]); }
+    free(step_id);
+    free(step_dir);
+    return L.error ? -1 : 0;
+}

@@ -236,6 +236,37 @@ typedef struct or_prefetch_stats {
 int or_prefetch_run(const uint64_t* pages, uint64_t n, const or_prefetch_cell* cell,
                     or_prefetch_stats* stats);
 
+/* ---- UCIe streaming link (src/ucie/link.cpp, include/hbfsim/ucie/link.hpp:
+ * Format 6 flits of 48 AoU granules, AR 3 / R 14 granules per message,
+ * credits returned as legal grants on the reverse direction's flits) under
+ * the batch driver: messages offered in input order, enqueued at
+ * max(ready, link time) once their direction has room and their ready time
+ * is not past the next event; each delivery consumed consume_ns[direction]
+ * later. ---- */
+typedef struct or_link_profile {
+    uint32_t gt_per_second;       /* 8, 16 or 32 */
+    uint32_t initial_ar_granules;
+    uint32_t initial_r_granules;
+    uint32_t max_accepted;
+    uint64_t propagation_ns;
+    uint64_t consume_ns[2];       /* 0 request (AR), 1 return (R) */
+} or_link_profile;
+
+typedef struct or_link_result {
+    /* per direction: flits, wire bytes, UCIe header bytes, CRC bytes, AoU
+     * header bytes, AoU message bytes, unused message bytes, credit-only flits */
+    uint64_t counters[2][8];
+    uint64_t now;
+    uint32_t ar_credits;
+    uint32_t r_credits;
+} or_link_result;
+
+/* direction[k] (0 AR, 1 R) and ready[k] (non-decreasing) of m messages;
+ * delivered[k] gets each message's delivery tick.  0, or -1 on a time or
+ * credit overflow (the reference throws) or when memory runs out. */
+int or_link_run(const or_link_profile* p, const uint8_t* direction, const uint64_t* ready,
+                uint64_t m, uint64_t* delivered, or_link_result* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -107,6 +107,8 @@ def _load() -> ctypes.CDLL:
     lib.or_empirical_control_valid.argtypes = [p]
     lib.or_empirical_request_service.restype = ctypes.c_int
     lib.or_empirical_request_service.argtypes = [p, u64, u64, u32, p, p, p]
+    lib.or_link_run.restype = ctypes.c_int
+    lib.or_link_run.argtypes = [p, p, p, u64, p, p]
     lib.or_prefetch_run.restype = ctypes.c_int
     lib.or_prefetch_run.argtypes = [p, u64, p, p]
     lib.or_run_empirical_batch.restype = ctypes.c_int
@@ -286,6 +288,33 @@ def prefetch_run(pages: np.ndarray, cell: dict) -> tuple:
     if LIB.or_prefetch_run(_ptr(pages), pages.size, ctypes.byref(c), out) != 0:
         raise MemoryError("oracle allocation failed")
     return tuple(int(v) for v in out)
+
+
+class LinkProfile(ctypes.Structure):
+    _fields_ = [("gt_per_second", ctypes.c_uint32), ("initial_ar_granules", ctypes.c_uint32),
+                ("initial_r_granules", ctypes.c_uint32), ("max_accepted", ctypes.c_uint32),
+                ("propagation_ns", ctypes.c_uint64), ("consume_ns", ctypes.c_uint64 * 2)]
+
+
+class LinkResult(ctypes.Structure):
+    _fields_ = [("counters", (ctypes.c_uint64 * 8) * 2), ("now", ctypes.c_uint64),
+                ("ar_credits", ctypes.c_uint32), ("r_credits", ctypes.c_uint32)]
+
+
+def link_run(profile: dict, direction: np.ndarray, ready: np.ndarray):
+    """The UCIe streaming link under the batch driver; returns (delivered
+    ticks, counters [2][8], now, ar_credits, r_credits)."""
+    p = LinkProfile(profile["gt"], profile["ar"], profile["r"], profile["accepted"],
+                    profile["prop"], (ctypes.c_uint64 * 2)(*profile["consume"]))
+    direction = np.ascontiguousarray(direction, np.uint8)
+    ready = np.ascontiguousarray(ready, np.uint64)
+    delivered = np.zeros(ready.size, np.uint64)
+    out = LinkResult()
+    if LIB.or_link_run(ctypes.byref(p), _ptr(direction), _ptr(ready), ready.size,
+                       _ptr(delivered), ctypes.byref(out)) != 0:
+        raise ValueError("link overflow")
+    counters = np.array([[out.counters[d][k] for k in range(8)] for d in range(2)], np.uint64)
+    return delivered, counters, out.now, out.ar_credits, out.r_credits
 
 
 def cores() -> int:

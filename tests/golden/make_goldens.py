@@ -14,6 +14,9 @@ Fixtures written:
                          fast-model traces, all computed by the reference's own
                          functions (src/cuda_runtime/device/hbf_device.cuh,
                          src/hybrid/calibrator.cpp).
+  link_goldens.json      delivery ticks, counters and credits of the reference
+                         UCIe streaming link (src/ucie/link.cpp, compiled
+                         from source) on message batches.
   prefetch_goldens.json  statistics of the reference prefetch model
                          (src/prefetch/prefetch_model.cpp, compiled from
                          source) for sweep cells on four page streams.
@@ -46,6 +49,7 @@ REPO = HERE.parent.parent
 REF = Path(os.environ.get("HBFSIM_REFERENCE", "/root/reference"))
 REF_BIN = REPO / "oracle" / "_ref" / "ref_goldens"
 REF_PREFETCH = REPO / "oracle" / "_ref" / "ref_prefetch"
+REF_LINK = REPO / "oracle" / "_ref" / "ref_link"
 
 
 def load_exporter():
@@ -291,6 +295,46 @@ def prefetch_goldens() -> None:
     (HERE / "prefetch_goldens.json").write_text(json.dumps(out))
 
 
+def link_goldens() -> None:
+    """Delivery ticks, byte and flit counters, credits and final tick of the
+    reference UCIe streaming link (src/ucie/link.cpp, compiled from source
+    into oracle/_ref/ref_link) under the batch driver, for profiles from the
+    reference's own link test (128 credits each, the minimum 3 / 14, a slow
+    consumer) and random ones, on message batches of mixed directions."""
+    rng = random.Random(31)
+    profiles = [dict(gt=16, ar=128, r=128, accepted=128, prop=0, consume=[0, 0]),
+                dict(gt=16, ar=3, r=14, accepted=4, prop=0, consume=[0, 0]),
+                dict(gt=16, ar=12, r=56, accepted=2, prop=0, consume=[0, 98]),
+                dict(gt=8, ar=12, r=56, accepted=4, prop=5, consume=[3, 40]),
+                dict(gt=32, ar=40, r=200, accepted=16, prop=1, consume=[0, 0])]
+    for _ in range(25):
+        profiles.append(dict(gt=rng.choice([8, 16, 32]), ar=rng.choice([3, 4, 12, 40, 128]),
+                             r=rng.choice([14, 20, 56, 200]),
+                             accepted=rng.choice([1, 2, 4, 16, 128]),
+                             prop=rng.choice([0, 1, 7, 100]),
+                             consume=[rng.choice([0, 0, 3, 50]), rng.choice([0, 2, 100, 1000])]))
+    cases = []
+    for k, prof in enumerate(profiles):
+        m = 17 if k == 0 else rng.randrange(1, 300)
+        share = rng.random()
+        direction = [0 if k == 0 else (1 if rng.random() < share else 0) for _ in range(m)]
+        ready, t = [], 0
+        for _ in range(m):
+            t += 0 if (k == 0 or rng.random() < 0.5) else rng.randrange(40)
+            ready.append(t)
+        text = (f"{prof['gt']} {prof['ar']} {prof['r']} {prof['accepted']} {prof['prop']} "
+                f"{prof['consume'][0]} {prof['consume'][1]} {m}\n" +
+                "".join(f"{d} {r}\n" for d, r in zip(direction, ready)))
+        out = subprocess.run([str(REF_LINK)], input=text, check=True, capture_output=True,
+                             text=True).stdout.split("\n")
+        cases.append({"profile": prof, "direction": direction, "ready": ready,
+                      "delivered": [int(v) for v in out[:m]],
+                      "counters": [[int(v) for v in out[m].split()],
+                                   [int(v) for v in out[m + 1].split()]],
+                      "tail": [int(v) for v in out[m + 2].split()]})
+    (HERE / "link_goldens.json").write_text(json.dumps(cases))
+
+
 def main() -> int:
     if not REF_BIN.exists():
         print("build oracle/_ref/ref_goldens first (make -C oracle)", file=sys.stderr)
@@ -300,6 +344,7 @@ def main() -> int:
     lru_goldens()
     retention_goldens()
     prefetch_goldens()
+    link_goldens()
     return 0
 
 

@@ -328,3 +328,19 @@ def test_prefetch_oracle_against_reference_model(golden_dir):
             assert list(got) == row[8:], (s["stream"], row[:8])
             cells += 1
     assert cells == 340
+
+
+# ---- UCIe streaming link (src/ucie/link.cpp) ----
+
+def test_link_oracle_against_reference_link(golden_dir):
+    """The oracle's restatement of the streaming link (event order, flit
+    packing, credit reservation and legal grants, retries) under the batch
+    driver, against the reference class compiled from its own source."""
+    cases = json.loads((golden_dir / "link_goldens.json").read_text())
+    assert len(cases) == 30
+    for k, c in enumerate(cases):
+        delivered, counters, now, ar, r = ho.link_run(c["profile"], np.array(c["direction"]),
+                                                      np.array(c["ready"]))
+        assert delivered.tolist() == c["delivered"], k
+        assert counters.tolist() == c["counters"], k
+        assert [ar, r, now] == c["tail"], k
