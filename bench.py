@@ -294,7 +294,7 @@ def main():
                     help="config-1 decode steps in the trace (8 = the full config; "
                          "fewer only for small profiling captures)")
     ap.add_argument("--only-extra", choices=["empirical_vmem", "thermal_coupled", "retention",
-                                             "prefetch_sweep"],
+                                             "prefetch_sweep", "ucie_link"],
                     help="run one secondary measurement alone and print its JSON "
                          "(profiling captures); not a bench line")
     args = ap.parse_args()
@@ -305,7 +305,8 @@ def main():
         import torch
         torch.cuda.set_device(0)
         run = {"empirical_vmem": run_vmem, "thermal_coupled": run_c3,
-               "retention": run_retention, "prefetch_sweep": run_prefetch}[args.only_extra]
+               "retention": run_retention, "prefetch_sweep": run_prefetch,
+               "ucie_link": run_link}[args.only_extra]
         with tempfile.TemporaryDirectory() as tmp:
             print_result(run(args, torch.device("cuda", 0), tmp))
         return 0
@@ -568,6 +569,53 @@ def run_extras(args, device, tmp):
     out["empirical_vmem"] = run_vmem(args, device, tmp)
     out["retention"] = run_retention(args, device, tmp)
     out["prefetch_sweep"] = run_prefetch(args, device, tmp)
+    out["ucie_link"] = run_link(args, device, tmp)
+    return out
+
+
+def run_link(args, device, tmp):
+    """UCIe streaming-link timing for 32,768 links (the reference's scenario
+    profile: x64 at 16 GT/s, 12 AR / 56 R credit granules, 4 messages in
+    flight per direction), each carrying 512 read requests (exponential gaps
+    of mean 8 ns) and their 512 returns 3 us later."""
+    import torch
+    from hbfsim_b200 import link_batch, link_profiles
+    links, per = 32768, 512
+    rng = np.random.default_rng(0)
+    req = np.cumsum(rng.exponential(8.0, (links, per)).astype(np.int64), axis=1)
+    ret = req + 3_000
+    ready = np.concatenate([req, ret], axis=1)
+    direction = np.concatenate([np.zeros((links, per), np.uint8), np.ones((links, per), np.uint8)],
+                               axis=1)
+    order = np.argsort(ready, axis=1, kind="stable")
+    ready = np.take_along_axis(ready, order, axis=1)
+    direction = np.take_along_axis(direction, order, axis=1)
+    offsets = np.arange(links + 1, dtype=np.uint64) * (2 * per)
+    prof = link_profiles(links)  # the reference LinkProfile's scenario values
+    d_ready = torch.from_numpy(ready.reshape(-1)).to(device)
+    d_dir = torch.from_numpy(direction.reshape(-1)).to(device)
+    link_batch(prof[:64], offsets[:65], d_dir, d_ready)  # warm up
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    delivered, res = link_batch(prof, offsets, d_dir, d_ready)
+    dt = time.perf_counter() - t0
+    messages = links * 2 * per
+    out = {"workload": f"{links} links x {2 * per} messages (AR + R), reference scenario profile",
+           "messages": messages, "seconds": dt, "value": messages / dt, "unit": "messages/s",
+           "refused_links": int((res["status"] != 0).sum()),
+           "flits_per_link": int(res["counters"][0, 0, 0] + res["counters"][0, 1, 0])}
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, str(REPO / "oracle"))
+        import hbf_oracle as ho
+        t0 = time.perf_counter()
+        sample = 64
+        for k in range(sample):
+            ho.link_run({"gt": 16, "ar": 12, "r": 56, "accepted": 4, "prop": 0,
+                         "consume": [0, 0]}, direction[k], ready[k].astype(np.uint64))
+        cdt = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": sample * 2 * per / cdt, "unit": "messages/s",
+                               "cores": 1, "kind": "port",
+                               "sample": f"{sample} of the links, single thread"}
     return out
 
 

@@ -4,7 +4,8 @@ The CUDA library libhbfsim_b200.so (hbfsim_b200/csrc) holds the kernels and
 the C ABI; this package is the Python host side.  Importing it does not load
 the library; `Context` does, and fails loudly if it is missing.
 """
-from .api import BatchResult, Context, HbfsimError, prefetch_sweep  # noqa: F401
+from .api import (BatchResult, Context, HbfsimError, link_batch, link_profiles,  # noqa: F401
+                  prefetch_sweep)
 from ._lib import (ACCESS_BYPASS, ACCESS_FOREIGN, ACCESS_MODELED,  # noqa: F401
                    ACCESS_UNSUPPORTED, MODEL_DIE, MODEL_FAST, MODEL_HYBRID,
                    MODEL_REFERENCE, RANGE_CAPACITY, RANGE_TIMING)

@@ -134,6 +134,17 @@ class PrefetchStatsV1(ctypes.Structure):
                 ("prefetch_wasted", u64)]
 
 
+class LinkProfileV1(ctypes.Structure):
+    _fields_ = [("gt_per_second", u32), ("initial_ar_granules", u32),
+                ("initial_r_granules", u32), ("max_accepted", u32), ("propagation_ns", u64),
+                ("consume_ns", u64 * 2)]
+
+
+class LinkResultV1(ctypes.Structure):
+    _fields_ = [("counters", (u64 * 8) * 2), ("now", u64), ("ar_credits", u32),
+                ("r_credits", u32), ("status", i32), ("reserved", u32)]
+
+
 # Every exported function with its signature (restype, argtypes).
 SIGNATURES = {
     "hbfsim_abi_version": (u32, []),
@@ -182,6 +193,7 @@ SIGNATURES = {
     "hbfsim_retention_record_programs_v1": (i32, [vp, vp, vp, vp, u64, vp]),
     "hbfsim_get_retention_v1": (i32, [vp, vp, vp, vp, vp, u64, ctypes.POINTER(u64)]),
     "hbfsim_prefetch_sweep_v1": (i32, [vp, u64, vp, u32, vp, vp]),
+    "hbfsim_link_batch_v1": (i32, [vp, u32, vp, vp, vp, vp, vp, vp]),  # arrays by address
 }
 
 

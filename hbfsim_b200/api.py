@@ -19,7 +19,8 @@ import numpy as np
 from . import _lib
 from ._lib import HbfsimError, check
 
-__all__ = ["Context", "HbfsimError", "BatchResult", "prefetch_sweep", "PREFETCH_POLICIES"]
+__all__ = ["Context", "HbfsimError", "BatchResult", "prefetch_sweep", "PREFETCH_POLICIES",
+           "link_batch", "link_profiles", "LINK_PROFILE_DTYPE", "LINK_RESULT_DTYPE"]
 
 PREFETCH_POLICIES = {"none": 0, "next_page": 1, "accuracy": 2}
 
@@ -476,3 +477,47 @@ def prefetch_sweep(pages, cells, stream=None) -> list[dict]:
                                        ctypes.c_void_p(_stream_handle(stream))),
           "hbfsim_prefetch_sweep_v1")
     return [{f: getattr(out[k], f) for f, _ in _lib.PrefetchStatsV1._fields_} for k in range(n)]
+
+
+LINK_PROFILE_DTYPE = np.dtype([("gt_per_second", "<u4"), ("initial_ar_granules", "<u4"),
+                               ("initial_r_granules", "<u4"), ("max_accepted", "<u4"),
+                               ("propagation_ns", "<u8"), ("consume_ns", "<u8", (2,))])
+LINK_RESULT_DTYPE = np.dtype([("counters", "<u8", (2, 8)), ("now", "<u8"),
+                              ("ar_credits", "<u4"), ("r_credits", "<u4"), ("status", "<i4"),
+                              ("reserved", "<u4")])
+
+
+def link_profiles(count: int, gt_per_second=16, initial_ar_granules=12, initial_r_granules=56,
+                  max_accepted=4, propagation_ns=0, consume_ns=(0, 0)) -> np.ndarray:
+    """A structured array of `count` link profiles (hbfsim_link_profile_v1),
+    every field a scalar or a per-link array; the defaults are the
+    reference LinkProfile's scenario values."""
+    p = np.zeros(count, LINK_PROFILE_DTYPE)
+    p["gt_per_second"] = gt_per_second
+    p["initial_ar_granules"] = initial_ar_granules
+    p["initial_r_granules"] = initial_r_granules
+    p["max_accepted"] = max_accepted
+    p["propagation_ns"] = propagation_ns
+    p["consume_ns"] = np.asarray(consume_ns, np.uint64)
+    return p
+
+
+def link_batch(profiles: np.ndarray, offsets, direction, ready, stream=None):
+    """UCIe streaming-link timing (hbfsim::ucie::StreamingLink) for a batch
+    of links.  profiles: structured array of LINK_PROFILE_DTYPE (see
+    link_profiles); offsets: links + 1 message offsets (host); direction
+    (uint8, 0 AR / 1 R) and ready (int64 ticks, non-decreasing per link):
+    device tensors.  Returns (delivered device tensor, structured array of
+    LINK_RESULT_DTYPE, one row per link)."""
+    import torch
+    lib = _lib.load()
+    profiles = np.ascontiguousarray(profiles, LINK_PROFILE_DTYPE)
+    n = profiles.size
+    off = np.ascontiguousarray(offsets, np.uint64)
+    delivered = torch.empty(max(1, int(off[-1])), dtype=torch.int64, device=ready.device)
+    res = np.zeros(max(1, n), LINK_RESULT_DTYPE)
+    check(lib.hbfsim_link_batch_v1(profiles.ctypes.data, n, off.ctypes.data, _ptr(direction),
+                                   _ptr(ready), _ptr(delivered), res.ctypes.data,
+                                   ctypes.c_void_p(_stream_handle(stream))),
+          "hbfsim_link_batch_v1")
+    return delivered[:int(off[-1])], res[:n]

@@ -17,7 +17,7 @@ LIB = PKG / "libhbfsim_b200.so"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 SOURCES = ["timing.cu", "empirical.cu", "context.cu", "thermal.cu", "capacity.cu",
-           "retention.cu", "prefetch.cu", "profile.cpp"]
+           "retention.cu", "prefetch.cu", "link.cu", "profile.cpp"]
 
 
 def sources() -> list[Path]:

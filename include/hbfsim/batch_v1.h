@@ -463,6 +463,46 @@ int hbfsim_prefetch_sweep_v1(const uint64_t* pages, uint64_t count,
                              uint32_t cell_count, hbfsim_prefetch_stats_v1* out,
                              void* stream);
 
+/* ---- UCIe streaming-link timing ----
+ * Replaces hbfsim::ucie::StreamingLink (src/ucie/link.cpp,
+ * include/hbfsim/ucie/link.hpp:54-113) for batches of independent links
+ * (one per stack, module or sweep cell), each driven as follows: its
+ * messages are offered in input order; the next one is enqueued at
+ * max(ready, the link's tick) once its direction has fewer than
+ * max_accepted messages in flight and its ready tick is not past the link's
+ * next event; after each step every delivered message is consumed
+ * consume_ns[direction] later.  Delivery ticks and counters equal the
+ * reference link's under that driver. */
+typedef struct hbfsim_link_profile_v1 {
+    uint32_t gt_per_second;        /* 8, 16 or 32 (x64 lanes)               */
+    uint32_t initial_ar_granules;  /* 3 .. 65535                            */
+    uint32_t initial_r_granules;   /* 14 .. 65535                           */
+    uint32_t max_accepted;         /* messages in flight per direction     */
+    uint64_t propagation_ns;       /* at most 1e9                           */
+    uint64_t consume_ns[2];        /* consumer delay: 0 AR, 1 R             */
+} hbfsim_link_profile_v1;
+
+typedef struct hbfsim_link_result_v1 {
+    /* per direction (0 AR, 1 R): flits, wire bytes, UCIe header bytes, CRC
+     * bytes, AoU header bytes, AoU message bytes, unused message bytes,
+     * credit-only flits (link.hpp:38-48 DirectionCounters) */
+    uint64_t counters[2][8];
+    uint64_t now;                  /* the link's last event tick           */
+    uint32_t ar_credits;
+    uint32_t r_credits;
+    int32_t status;                /* 0, or an hbfsim_error for this link  */
+    uint32_t reserved;
+} hbfsim_link_result_v1;
+
+/* links: count; profiles, offsets (links + 1, messages of link k are
+ * [offsets[k], offsets[k+1])) and results: host arrays; direction (0 AR,
+ * 1 R), ready (non-decreasing per link) and delivered: device arrays.
+ * Synchronous on `stream`. */
+int hbfsim_link_batch_v1(const hbfsim_link_profile_v1* profiles, uint32_t links,
+                         const uint64_t* offsets, const uint8_t* direction,
+                         const uint64_t* ready, uint64_t* delivered,
+                         hbfsim_link_result_v1* results, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -951,6 +951,7 @@ typedef struct or_link {
     int retry_pending[2];
     uint64_t counters[2][8];
     uint64_t flit_ns;
+    uint64_t heap_peak;
     int error;
 } or_link;
 
@@ -970,6 +971,7 @@ static void or_ev_push(or_link* L, or_event e)
     }
     e.seq = L->seq++;
     uint64_t k = L->heap_n++;
+    if (L->heap_n > L->heap_peak) L->heap_peak = L->heap_n;
     while (k > 0) {
         const uint64_t up = (k - 1) / 2;
         if (!or_ev_less(&e, &L->heap[up])) break;
@@ -1158,6 +1160,7 @@ int or_link_run(const or_link_profile* p, const uint8_t* direction, const uint64
     out->now = L.now;
     out->ar_credits = L.credits[0];
     out->r_credits = L.credits[1];
+    out->heap_peak = L.heap_peak;
     memcpy(out->counters, L.counters, sizeof L.counters);
     free(L.heap);
     for (int d = 0; d < 2; ++d) { free(L.queue[d]); free(L.sent[d]); }

@@ -259,6 +259,7 @@ typedef struct or_link_result {
     uint64_t now;
     uint32_t ar_credits;
     uint32_t r_credits;
+    uint64_t heap_peak;   /* most events pending at once (bounds the device heap) */
 } or_link_result;
 
 /* direction[k] (0 AR, 1 R) and ready[k] (non-decreasing) of m messages;

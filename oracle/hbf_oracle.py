@@ -298,7 +298,8 @@ class LinkProfile(ctypes.Structure):
 
 class LinkResult(ctypes.Structure):
     _fields_ = [("counters", (ctypes.c_uint64 * 8) * 2), ("now", ctypes.c_uint64),
-                ("ar_credits", ctypes.c_uint32), ("r_credits", ctypes.c_uint32)]
+                ("ar_credits", ctypes.c_uint32), ("r_credits", ctypes.c_uint32),
+                ("heap_peak", ctypes.c_uint64)]
 
 
 def link_run(profile: dict, direction: np.ndarray, ready: np.ndarray):
@@ -314,6 +315,7 @@ def link_run(profile: dict, direction: np.ndarray, ready: np.ndarray):
                        _ptr(delivered), ctypes.byref(out)) != 0:
         raise ValueError("link overflow")
     counters = np.array([[out.counters[d][k] for k in range(8)] for d in range(2)], np.uint64)
+    link_run.heap_peak = out.heap_peak
     return delivered, counters, out.now, out.ar_credits, out.r_credits
 
 
