@@ -119,3 +119,46 @@ def test_null_context_calls(lib):
     assert lib.hbfsim_map_file(None, b"x", 0, 1, None, ctypes.byref(out)) == 1
     assert out.value is None
     lib.hbfsim_context_destroy(None)
+
+
+def test_stateless_entry_argument_checks(lib):
+    """The prefetch-sweep and link-batch entries refuse bad arguments before
+    any device work (no GPU needed)."""
+    pf_cells = (_lib.PrefetchCellV1 * 2)()
+    pf_cells[0] = _lib.PrefetchCellV1(2, 1, 0.5, 64, 32, 1000, 0, 1)
+    pf_cells[1] = _lib.PrefetchCellV1(7, 1, 0.5, 64, 32, 1000, 0, 1)  # policy 7
+    out = (_lib.PrefetchStatsV1 * 2)()
+    assert lib.hbfsim_prefetch_sweep_v1(None, 10, pf_cells, 2, out, None) == 1  # no pages
+    assert lib.hbfsim_prefetch_sweep_v1(ctypes.c_void_p(8), 10, pf_cells, 2, out, None) == 1
+    assert lib.hbfsim_prefetch_sweep_v1(ctypes.c_void_p(8), 1 << 33, pf_cells, 1, out,
+                                        None) == 5  # 2^33 accesses: HBFSIM_UNSUPPORTED
+    assert lib.hbfsim_prefetch_sweep_v1(None, 0, pf_cells, 0, out, None) == 0
+    # zero accesses: every statistic 0, no device work
+    assert lib.hbfsim_prefetch_sweep_v1(None, 0, pf_cells, 1, out, None) == 0
+    assert out[0].total_ns == 0 and out[0].demand_accesses == 0
+
+    def link(gt=16, ar=12, r=56, accepted=4, prop=0):
+        return _lib.LinkProfileV1(gt, ar, r, accepted, prop, (ctypes.c_uint64 * 2)(0, 0))
+
+    offsets = (ctypes.c_uint64 * 2)(0, 0)
+    res = (_lib.LinkResultV1 * 1)()
+    for bad in (link(gt=64), link(ar=2), link(r=13), link(accepted=0), link(ar=70000),
+                link(prop=2_000_000_000)):
+        profiles = (_lib.LinkProfileV1 * 1)(bad)
+        assert lib.hbfsim_link_batch_v1(profiles, 1, offsets, None, None, None, res, None) == 1
+    assert lib.hbfsim_link_batch_v1(None, 0, None, None, None, None, None, None) == 0
+    offsets_bad = (ctypes.c_uint64 * 2)(0, 5)  # messages but no device arrays
+    profiles = (_lib.LinkProfileV1 * 1)(link())
+    assert lib.hbfsim_link_batch_v1(profiles, 1, offsets_bad, None, None, None, res, None) == 1
+
+
+def test_ledger_entries_without_a_ledger(lib):
+    assert lib.hbfsim_retention_blocks_v1(None) == 0
+    assert lib.hbfsim_retention_advance_v1(None, 0, None, None) == 1
+    count = ctypes.c_uint64()
+    assert lib.hbfsim_retention_due_v1(None, 0, None, None, 0, ctypes.byref(count), None) == 1
+    assert lib.hbfsim_retention_refresh_v1(None, None, 0, None) == 1
+    assert lib.hbfsim_get_retention_v1(None, None, None, None, None, 0, None) == 1
+    cfg = _lib.RetentionConfigV1(ctypes.sizeof(_lib.RetentionConfigV1), 1, 1.05, 358.15,
+                                 86_400_000_000_000, 0, 0, 0, 330.0, 0, 0)
+    assert lib.hbfsim_retention_configure_v1(None, ctypes.byref(cfg)) == 1
