@@ -367,7 +367,9 @@ int hbfsim_get_channel_factors_v1(hbfsim_context* context,
  * of the context's local channels (die model only).  Block id:
  * ((local channel * D + die) * planes + plane) * blocks_per_plane + block,
  * blocks_per_plane = ceil(capacity / (channels_total * D * planes * page)
- * / pages_per_block).  All blocks share one accounted frontier. */
+ * / pages_per_block).  All blocks share one accounted frontier.
+ * hbfsim_set_geometry_v1 drops the ledger (its blocks follow the geometry);
+ * configure it again afterwards. */
 #define HBFSIM_RETENTION_CONFIG_V1_VERSION 1u
 typedef struct hbfsim_retention_config_v1 {
     uint32_t struct_size;
