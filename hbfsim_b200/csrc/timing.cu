@@ -1046,11 +1046,18 @@ direct_replay_kernel(const PassArgs args)
 }
 
 // Range scan: incoming_b = R_{b-1} ... R_0 (state), one CTA per local
-// channel (channels are independent).  The CTA stages a chunk of its
-// channel's range aggregates in shared memory with coalesced loads; warp 0
-// then walks them, lane i holding state word i: one step is K shuffles and
-// K+1 max-plus terms per lane.  When the batch is accepted the CTA also adds
-// the activity pass 1 staged for its channel to the die counters.
+// channel (channels are independent).  Each range aggregate R is a max-plus
+// affine map x -> max(R[:, :K] + x, R[:, K]) (K state words).  The CTA's 8
+// warps split the ranges into 8 groups:
+//   A  each warp composes its group into one map (one lane per entry,
+//      clamping sums below -2^61 back to NEG so that they cannot overflow);
+//   B  warp 0 applies the 8 group maps to the carried state, giving each
+//      group its incoming state (and the batch's final state);
+//   C  each warp walks its group from that state (lane i = state word i,
+//      shuffles), writing every range's incoming state.
+// Aggregates are staged per warp in chunks of `chunk` with coalesced loads.
+// When the batch is accepted the CTA also adds the activity pass 1 staged
+// for its channel to the die counters.
 struct ScanArgs {
     const i64* agg;     // [ctas][C][K][K+1]
     i64* incoming;      // [ctas][C][K]
@@ -1061,7 +1068,7 @@ struct ScanArgs {
     const u64* arrival;
     u64 n;
     u32 ctas, C, K;
-    u32 chunk;          // aggregates staged per round
+    u32 chunk;          // aggregates staged per warp per round
     u32 dies;
     DevCounters* counters;
     const unsigned long long* act_stage;  // [C*D][2] or null
@@ -1069,11 +1076,23 @@ struct ScanArgs {
     unsigned long long* die_writes;
 };
 
-__global__ void __launch_bounds__(256) range_scan_kernel(const ScanArgs a)
+constexpr u32 kScanWarps = 8;
+
+__device__ __forceinline__ void stage_aggregates(const ScanArgs& a, u32 c, u32 b0, u32 nb,
+                                                 u32 per, i64* stage)
+{
+    const u32 lane = threadIdx.x & 31u;
+    for (u32 k = lane; k < nb * per; k += 32) {
+        const u32 b = k / per, w = k - b * per;
+        stage[k] = a.agg[(static_cast<u64>(b0 + b) * a.C + c) * per + w];
+    }
+    __syncwarp();
+}
+
+__global__ void __launch_bounds__(kScanWarps * 32) range_scan_kernel(const ScanArgs a)
 {
     extern __shared__ __align__(16) unsigned char smem[];
-    i64* s_r = reinterpret_cast<i64*>(smem);  // [chunk][K][K+1]
-    const u32 tid = threadIdx.x, lane = tid & 31u;
+    const u32 tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     const u32 c = blockIdx.x, K = a.K, KK = K + 1, per = K * KK;
     const u32 err = *a.error;
     if (!(err & kErrUnsorted) && (err & kErrNeedSeq)) return;  // sequential path
@@ -1086,27 +1105,80 @@ __global__ void __launch_bounds__(256) range_scan_kernel(const ScanArgs a)
         }
         return;
     }
-    i64 v = lane < K ? static_cast<i64>(a.state_in[row0 + lane]) : 0;
-    const u32 my_row = lane < K ? lane : 0u;
-    for (u32 b0 = 0; b0 < a.ctas; b0 += a.chunk) {
-        const u32 nb = a.ctas - b0 < a.chunk ? a.ctas - b0 : a.chunk;
-        __syncthreads();  // the previous chunk is consumed
-        for (u32 k = tid; k < nb * per; k += blockDim.x) {
-            const u32 b = k / per, w = k - b * per;
-            s_r[k] = a.agg[(static_cast<u64>(b0 + b) * a.C + c) * per + w];
-        }
-        __syncthreads();
-        if (tid < 32) {
-            for (u32 b = 0; b < nb; ++b) {
-                if (lane < K) a.incoming[(static_cast<u64>(b0 + b) * a.C + c) * K + lane] = v;
-                const i64* row = s_r + b * per + my_row * KK;
-                i64 best = row[K];
-                for (u32 j = 0; j < K; ++j) best = imax(best, row[j] + __shfl_sync(0xffffffffu, v, j));
-                if (lane < K) v = best;
+    const u32 n = a.ctas, span = a.chunk * per + per;
+    i64* stage = reinterpret_cast<i64*>(smem) + static_cast<u64>(warp) * span;
+    i64* comp = stage + static_cast<u64>(a.chunk) * per;  // the group's composite
+    i64* gin = reinterpret_cast<i64*>(smem) + static_cast<u64>(kScanWarps) * span;  // [8][K]
+    const u32 g0 = static_cast<u32>(static_cast<u64>(n) * warp / kScanWarps);
+    const u32 g1 = static_cast<u32>(static_cast<u64>(n) * (warp + 1) / kScanWarps);
+
+    // A: comp = R_{g1-1} o ... o R_{g0}
+    for (u32 b0 = g0; b0 < g1; b0 += a.chunk) {
+        const u32 nb = g1 - b0 < a.chunk ? g1 - b0 : a.chunk;
+        stage_aggregates(a, c, b0, nb, per, stage);
+        for (u32 b = 0; b < nb; ++b) {
+            const i64* R = stage + static_cast<u64>(b) * per;
+            if (b0 == g0 && b == 0) {
+                for (u32 e = lane; e < per; e += 32) comp[e] = R[e];
+                __syncwarp();
+                continue;
             }
+            i64 v[9];
+#pragma unroll
+            for (u32 t = 0; t < 9; ++t) {
+                const u32 e = lane + 32 * t;
+                if (e >= per) break;
+                const u32 i = e / KK, j = e - i * KK;
+                const i64* Ri = R + static_cast<u64>(i) * KK;
+                i64 best = j == K ? Ri[K] : kNeg;
+                for (u32 k = 0; k < K; ++k) best = imax(best, Ri[k] + comp[k * KK + j]);
+                v[t] = best < kNeg / 2 ? kNeg : best;
+            }
+            __syncwarp();
+#pragma unroll
+            for (u32 t = 0; t < 9; ++t) {
+                const u32 e = lane + 32 * t;
+                if (e >= per) break;
+                comp[e] = v[t];
+            }
+            __syncwarp();
         }
     }
-    if (tid < K) a.state_out[row0 + tid] = static_cast<u64>(v);
+    __syncthreads();
+
+    // B: incoming state of every group, and the batch's final state
+    const u32 my_row = lane < K ? lane : 0u;
+    if (warp == 0) {
+        i64 x = lane < K ? static_cast<i64>(a.state_in[row0 + lane]) : 0;
+        for (u32 w = 0; w < kScanWarps; ++w) {
+            if (lane < K) gin[w * K + lane] = x;
+            const u32 s0 = static_cast<u32>(static_cast<u64>(n) * w / kScanWarps);
+            const u32 s1 = static_cast<u32>(static_cast<u64>(n) * (w + 1) / kScanWarps);
+            if (s0 == s1) continue;
+            const i64* G = reinterpret_cast<i64*>(smem) + static_cast<u64>(w) * span +
+                           static_cast<u64>(a.chunk) * per + static_cast<u64>(my_row) * KK;
+            i64 best = G[K];
+            for (u32 j = 0; j < K; ++j) best = imax(best, G[j] + __shfl_sync(0xffffffffu, x, j));
+            if (lane < K) x = best;
+        }
+        if (lane < K) a.state_out[row0 + lane] = static_cast<u64>(x);
+    }
+    __syncthreads();
+
+    // C: every range's incoming state
+    i64 x = lane < K ? gin[warp * K + lane] : 0;
+    for (u32 b0 = g0; b0 < g1; b0 += a.chunk) {
+        const u32 nb = g1 - b0 < a.chunk ? g1 - b0 : a.chunk;
+        __syncwarp();  // the previous chunk is consumed
+        stage_aggregates(a, c, b0, nb, per, stage);
+        for (u32 b = 0; b < nb; ++b) {
+            if (lane < K) a.incoming[(static_cast<u64>(b0 + b) * a.C + c) * K + lane] = x;
+            const i64* row = stage + static_cast<u64>(b) * per + static_cast<u64>(my_row) * KK;
+            i64 best = row[K];
+            for (u32 j = 0; j < K; ++j) best = imax(best, row[j] + __shfl_sync(0xffffffffu, x, j));
+            if (lane < K) x = best;
+        }
+    }
     if (a.act_stage) {
         const u32 D = a.dies;
         for (u32 d = tid; d < D; d += blockDim.x) {
@@ -1474,15 +1546,18 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
         sa.act_stage = tp.act_stage;
         sa.die_read_bytes = tp.die_read_bytes;
         sa.die_writes = tp.die_writes;
-        const u32 per = 8 * plan.K * (plan.K + 1);
-        sa.chunk = (96u * 1024u) / per < plan.ctas ? (96u * 1024u) / per : plan.ctas;
-        const u32 scan_smem = sa.chunk * per;
+        // per warp: `chunk` staged aggregates and the group's composite
+        const u32 per = plan.K * (plan.K + 1);
+        const u32 group = (plan.ctas + kScanWarps - 1) / kScanWarps;
+        const u32 room = (96u * 1024u / 8u) / kScanWarps - per;
+        sa.chunk = std::max(1u, std::min(group, room / per));
+        const u32 scan_smem = 8u * (kScanWarps * (sa.chunk * per + per) + kScanWarps * plan.K);
         err = cudaFuncSetAttribute(range_scan_kernel,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(scan_smem));
         if (err != cudaSuccess) return err;
         hooks(kSlotScan, 0, stream);
-        range_scan_kernel<<<plan.C, 256, scan_smem, stream>>>(sa);
+        range_scan_kernel<<<plan.C, kScanWarps * 32, scan_smem, stream>>>(sa);
         hooks(kSlotScan, 1, stream);
         hooks(kSlotPass2, 0, stream);
         p2<<<plan.ctas, kThreads, plan.smem_bytes, stream>>>(a);
