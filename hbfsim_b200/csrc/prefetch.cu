@@ -13,7 +13,7 @@
 // buffer as slots {page, arrival, insertion number} with a stack of free
 // slots; one pass of ballots over the live slots finds the predicted page,
 // the demanded page and the oldest entry (a warp minimum of the insertion
-// numbers), which is dropped when an insertion overfills the buffer.  The media servers (prefetch_model.cpp:23-50) all take
+// numbers), which is dropped before an insertion into a full buffer.  The media servers (prefetch_model.cpp:23-50) all take
 // the same read latency and receive reads in non-decreasing issue time, so
 // the server that frees first for the j-th read is the one that served read
 // j - k: completion_j = max(issue_j, completion_{j-k}) + latency, a ring of
@@ -230,22 +230,11 @@ __global__ void __launch_bounds__(128) prefetch_sweep_kernel(const SweepArgs a)
             scanned = true;
             if (predict && pslot < 0) {
                 const u64 landed = media_issue(clock);
-                const u32 f = free_stack[free_top - 1];  // a free slot
-                --free_top;
-                __syncwarp();
-                if (lane == 0) {
-                    page[f] = predicted;
-                    arr[f] = landed;
-                    seq[f] = next_seq;
-                }
-                __syncwarp();
-                ++next_seq;
-                ++live;
-                hi = f + 1 > hi ? f + 1 : hi;
-                ++issued;
-                if (predicted == demand) dslot = static_cast<int>(f);
-                if (live > capacity) {
-                    // drop the oldest entry (live never exceeds capacity + 1)
+                if (live == capacity) {
+                    // full: drop the oldest entry first (the reference inserts,
+                    // then drops the oldest; the new page is never the oldest,
+                    // so the order does not matter), so that live entries fit
+                    // in `capacity` slots
                     const u32 oldest = __reduce_min_sync(kFull, best);
                     const u32 owner = __ffs(__ballot_sync(kFull, best == oldest)) - 1;
                     const u32 e = __shfl_sync(kFull, best_slot, owner);
@@ -260,6 +249,20 @@ __global__ void __launch_bounds__(128) prefetch_sweep_kernel(const SweepArgs a)
                     --live;
                     ++wasted;
                 }
+                const u32 f = free_stack[free_top - 1];  // a free slot
+                --free_top;
+                __syncwarp();
+                if (lane == 0) {
+                    page[f] = predicted;
+                    arr[f] = landed;
+                    seq[f] = next_seq;
+                }
+                __syncwarp();
+                ++next_seq;
+                ++live;
+                hi = f + 1 > hi ? f + 1 : hi;
+                ++issued;
+                if (predicted == demand) dslot = static_cast<int>(f);
             }
         }
         const int k = scanned ? dslot : buffer_find(page, seq, hi, demand);
@@ -325,7 +328,7 @@ extern "C" int hbfsim_prefetch_sweep_v1(const uint64_t* pages, uint64_t count,
         offset[k] = ring_words;
         ring_words += std::max<std::uint32_t>(1, cells[k].max_in_flight);
     }
-    const std::uint32_t slots = (max_buffer + 1 + 31) / 32 * 32;
+    const std::uint32_t slots = (max_buffer + 31) / 32 * 32;  // live entries never exceed the buffer
     const std::uint64_t warp_bytes = 8ull * (kMtWords + kRingSmem + 3ull * slots);
     if (warp_bytes > 200ull * 1024) return HBFSIM_UNSUPPORTED;  // buffer too large for a warp
     const std::uint32_t warps = static_cast<std::uint32_t>(
