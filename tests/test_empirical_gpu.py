@@ -244,3 +244,19 @@ def test_static_entry_point_matches(tmp_path):
            out[2].cpu().numpy())
     same(got, oracle.run(*arrays), "static entry")
     ctx.close()
+
+
+def test_element_offset_buffers(tmp_path):
+    """Inputs starting one element into their arrays (8-, 4- and 1-byte
+    offsets from the allocation): the same results as the oracle."""
+    import torch
+    setup = setup_for(wl.vmem_profile())
+    arrays = mixed(wl.vmem_trace(70_001, seed=12), np.random.default_rng(12))
+    ctx = make_context(setup, str(tmp_path))
+    dev = tuple(t[1:] for t in to_device(arrays))
+    out = ctx.submit(*dev)
+    torch.cuda.synchronize()
+    got = (out.done_ns.cpu().numpy().view(np.uint64), out.latency_ns.cpu().numpy().view(np.uint64),
+           out.status.cpu().numpy())
+    same(got, EmpiricalOracle(setup).run(*(a[1:] for a in arrays)), "offset buffers")
+    ctx.close()
