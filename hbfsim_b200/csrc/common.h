@@ -76,9 +76,19 @@ __device__ __forceinline__ u32 fastdiv_q(u32 n, const FastDiv& f)
 }
 #endif
 
+// The one registered range of a context that has exactly one, by value in
+// the kernel arguments so that its fields are read from the constant bank
+// instead of being held in registers across the decode loops.
+struct SingleRange {
+    u64 base, length, file_offset, page_mask;  // page_mask = page_bytes - 1
+    u32 allowed;  // DevRange::timing
+    u32 valid;    // 0: decode against `ranges`
+};
+
 struct DecodeParams {
     const DevRange* ranges;  // sorted by base
     u32 range_count;
+    SingleRange one;         // valid when ranges holds exactly one registered range
     u32 stripe_shift;
     u32 stacks;
     u32 dies;

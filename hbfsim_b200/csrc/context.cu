@@ -261,6 +261,11 @@ DecodeParams decode_params(const hbfsim_context* c)
     DecodeParams d{};
     d.ranges = c->d_ranges;
     d.range_count = static_cast<std::uint32_t>(c->ranges.size());
+    if (c->ranges.size() == 1) {
+        const DevRange& r = c->ranges[0];
+        d.one = SingleRange{r.base, r.length, r.file_offset, (u64{1} << r.reserved) - 1,
+                            r.timing, 1u};
+    }
     d.stripe_shift = log2u(c->stripe_bytes);
     d.stacks = c->stacks;
     d.dies = p.dies_per_channel;
@@ -464,6 +469,7 @@ int run_device_batch(hbfsim_context* c, const BatchIO& io, cudaStream_t stream,
     if (ranges) {
         dp.ranges = ranges;
         dp.range_count = range_count;
+        dp.one.valid = 0;
         tp.any_order = 1;
     }
     const cudaError_t err = launch_batch(dp, tp, io, plan, s, sequential, stream, c->hooks());
@@ -487,6 +493,7 @@ DecodeParams media_decode_params(const hbfsim_context* c, const DevRange* ranges
     DecodeParams dp = decode_params(c);
     dp.ranges = ranges;
     dp.range_count = range_count;
+    dp.one.valid = 0;
     return dp;
 }
 

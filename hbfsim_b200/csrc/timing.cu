@@ -91,18 +91,8 @@ __device__ __forceinline__ TimingDecoded classify_timing(const DecodeParams& p, 
 }
 
 // The same classification for a context with one registered range, its
-// record held in registers (hoisted out of the tile loop).
-struct RangeRegs {
-    u64 base, length, file_offset, page_mask;
-    u32 allowed;  // DevRange::timing
-};
-
-__device__ __forceinline__ RangeRegs range_regs(const DevRange& r)
-{
-    return RangeRegs{r.base, r.length, r.file_offset, (u64{1} << r.reserved) - 1, r.timing};
-}
-
-__device__ __forceinline__ TimingDecoded classify_single(const RangeRegs& r,
+// record passed by value in the kernel arguments.
+__device__ __forceinline__ TimingDecoded classify_single(const SingleRange& r,
                                                          const DecodeParams& p, u64 a,
                                                          u32 bytes, u32 op)
 {
@@ -291,6 +281,22 @@ struct DieRegs {
             if (d == static_cast<u32>(j)) die[j] = done;
         return done;
     }
+    // The same step with the arrival at -inf (the unit columns of pass 1):
+    // every state word is >= NEG, so max(NEG, chan) is chan.
+    __device__ __forceinline__ void step_unit(u32 info, const ChanInfo& ci)
+    {
+        const i64 x = static_cast<i64>(info & 0xffffffu);
+        const u32 d = (info >> 24) & 15u;
+        const i64 t = (info >> 28) & 1u ? ci.t_prog : ci.t_read;
+        i64 cur = die[0];
+#pragma unroll
+        for (int j = 1; j < D; ++j) cur = d == static_cast<u32>(j) ? die[j] : cur;
+        chan = imax(chan, cur) + x;
+        const i64 done = chan + t;
+#pragma unroll
+        for (int j = 0; j < D; ++j)
+            if (d == static_cast<u32>(j)) die[j] = done;
+    }
 };
 
 __device__ __forceinline__ u32 lane_id() { return threadIdx.x & 31u; }
@@ -367,6 +373,20 @@ struct Stats7 {
                        max = 0, fast = 0;
 };
 
+// 16-byte global -> shared copies that do not pass through registers: a
+// thread issues all of its copies of a tile before it waits for any, so the
+// tile costs one memory round trip instead of one per loop iteration.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
+{
+    const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(gmem_src));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+__device__ __forceinline__ void cp_async_wait_all()
+{
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+}
+
 // Stage one tile, decode it, and build the channel-sorted order in s.ord
 // with segment starts in s.seg (stable: warps own contiguous chunks, lanes
 // are ranked in index order with __match_any_sync).
@@ -386,12 +406,16 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
         uint4* d_arr = reinterpret_cast<uint4*>(s.arr);
         uint4* d_bytes = reinterpret_cast<uint4*>(s.bytes);
         uint4* d_op = reinterpret_cast<uint4*>(s.op);
+#pragma unroll 1
         for (u32 k = tid; k < T / 2; k += kThreads) {
-            d_addr[k] = __ldcs(g_addr + k);
-            d_arr[k] = __ldcs(g_arr + k);
+            cp_async16(d_addr + k, g_addr + k);
+            cp_async16(d_arr + k, g_arr + k);
         }
-        for (u32 k = tid; k < T / 4; k += kThreads) d_bytes[k] = __ldcs(g_bytes + k);
-        for (u32 k = tid; k < T / 16; k += kThreads) d_op[k] = __ldcs(g_op + k);
+#pragma unroll 1
+        for (u32 k = tid; k < T / 4; k += kThreads) cp_async16(d_bytes + k, g_bytes + k);
+        for (u32 k = tid; k < T / 16; k += kThreads) cp_async16(d_op + k, g_op + k);
+        cp_async_commit();
+        cp_async_wait_all();
     } else {
         for (u32 k = tid; k < nt; k += kThreads) {
             s.addr[k] = A.address[start + k];
@@ -405,8 +429,7 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
 
     DecodeParams dp = A.dp;
     if (dp.range_count <= kSmemRanges) dp.ranges = s.ranges;
-    const bool single = dp.range_count == 1;
-    const RangeRegs rr = single ? range_regs(dp.ranges[0]) : RangeRegs{};
+    const bool single = A.dp.one.valid != 0;
     const u32 chunk = T / kWarps;
     bool unsorted = false;
     u64 arr_max = 0;  // arrivals from 2^59 on take the sequential kernel
@@ -431,7 +454,7 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
             const u32 o = s.op[e];
             TimingDecoded d;
             if (MODEL == kModelDie) {
-                d = single ? classify_single(rr, dp, a, b, o) : classify_timing(dp, a, b, o);
+                d = single ? classify_single(A.dp.one, A.dp, a, b, o) : classify_timing(dp, a, b, o);
             } else {
                 const Decoded f = classify_decode(dp, a, b, o, false);
                 d = TimingDecoded{f.status, 0u, 0u};
@@ -869,11 +892,14 @@ direct_pass_kernel(const PassArgs args)
                 for (u32 k = first; k < last; ++k) reg[it].step(s.sarr[k], s.sinfo[k], ci);
             } else {
 #pragma unroll 4
-                for (u32 k = first; k < last; ++k) reg[it].step(kNeg, s.sinfo[k], ci);
+                for (u32 k = first; k < last; ++k) reg[it].step_unit(s.sinfo[k], ci);
             }
         }
         __syncthreads();
-        // snapshot column 0, then let die columns try to couple to it
+        // every 8th tile and after the last: snapshot column 0, then let the
+        // die columns try to couple to it (coupling is tested at any tile
+        // boundary; testing less often only replays a few more tiles)
+        if ((tt & 7u) != 7u && tt + 1 < A.tiles_per_cta && start + T < A.n) continue;
 #pragma unroll
         for (int it = 0; it < kItems; ++it) {
             if (!item_on[it] || item_r[it] != 0) continue;
@@ -921,16 +947,6 @@ direct_pass_kernel(const PassArgs args)
 // written -- the next tile's records and arrivals stream into the staging
 // buffers with cp.async.  The outputs of timed accesses are written in access
 // order (coalesced), their arrival re-read from global memory (in L2).
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
-{
-    const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(gmem_src));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-__device__ __forceinline__ void cp_async_wait_all()
-{
-    asm volatile("cp.async.wait_all;\n" ::: "memory");
-}
 
 // Stage tile [start, start + nt) (records from the latency buffer, arrivals):
 // asynchronously when the tile is full and the buffers are 16-byte aligned.
@@ -956,6 +972,8 @@ __device__ __forceinline__ void stage_records(const PassArgs& A, const TileSmem&
         }
     }
 }
+
+constexpr u32 kOutBatch = 8;  // tiles hold at most 2048 = 8 x kThreads accesses
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 3)
@@ -1024,21 +1042,47 @@ direct_replay_kernel(const PassArgs args)
             const u32 c = tid;
             const u32 first = s.seg[c] + c, last = s.seg[c + 1] + c;  // shifted segment
             const ChanInfo ci = s.chan[c];
+            // operands one step ahead; index `last` <= T + C - 1 stays inside
+            // the sorted arrays
+            i64 a_next = s.sarr[first];
+            u32 info_next = s.sinfo[first];
 #pragma unroll 4
-            for (u32 k = first; k < last; ++k) s.sarr[k] = reg.step(s.sarr[k], s.sinfo[k], ci);
+            for (u32 k = first; k < last; ++k) {
+                const i64 a = a_next;
+                const u32 info = info_next;
+                a_next = s.sarr[k + 1];
+                info_next = s.sinfo[k + 1];
+                s.sarr[k] = reg.step(a, info, ci);
+            }
         }
         __syncthreads();
-        // outputs of the timed accesses, in access order
-        for (u32 j = tid; j < nt; j += kThreads) {
-            const u32 k = slot_of[j];
-            if (k == 0xffffu) continue;
-            const u64 done = static_cast<u64>(s.sarr[k]);
-            const u64 lat = done - __ldcg(reinterpret_cast<const unsigned long long*>(A.arrival) +
-                                          start + j);
-            __stcs(reinterpret_cast<unsigned long long*>(A.done + start + j), done);
-            __stcs(reinterpret_cast<unsigned long long*>(A.latency + start + j), lat);
-            st.lat += lat;
-            st.max = done > st.max ? done : st.max;
+        // outputs of the timed accesses, in access order.  Their arrivals
+        // come from L2 (the staging buffer already holds the next tile): a
+        // thread loads a batch of them before it stores anything, so the
+        // loads overlap instead of each waiting behind the previous stores.
+        for (u32 j0 = tid; j0 < nt; j0 += kOutBatch * kThreads) {
+            u64 arr[kOutBatch];
+            u32 slot[kOutBatch];
+#pragma unroll
+            for (u32 i = 0; i < kOutBatch; ++i) {
+                const u32 j = j0 + i * kThreads;
+                slot[i] = j < nt ? slot_of[j] : 0xffffu;
+                arr[i] = slot[i] != 0xffffu
+                             ? __ldcg(reinterpret_cast<const unsigned long long*>(A.arrival) +
+                                      start + j)
+                             : 0ull;
+            }
+#pragma unroll
+            for (u32 i = 0; i < kOutBatch; ++i) {
+                if (slot[i] == 0xffffu) continue;
+                const u32 j = j0 + i * kThreads;
+                const u64 done = static_cast<u64>(s.sarr[slot[i]]);
+                const u64 lat = done - arr[i];
+                __stcs(reinterpret_cast<unsigned long long*>(A.done + start + j), done);
+                __stcs(reinterpret_cast<unsigned long long*>(A.latency + start + j), lat);
+                st.lat += lat;
+                st.max = done > st.max ? done : st.max;
+            }
         }
         // the next iteration's barrier keeps the sorted copy until this is done
     }
