@@ -133,6 +133,9 @@ struct TimingParams {
     // 1: the batch order need not follow the arrival order (media actions
     // whose arrival waits for an earlier action's completion)
     u32 any_order;
+    // < 32: every channel's transfer is (bytes + 2^x_shift - 1) >> x_shift
+    // ticks before scaling; 0xff: per channel (ChanInfo)
+    u32 x_shift;
 };
 
 // Device-side counters (one block of u64 per context).

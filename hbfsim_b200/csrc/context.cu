@@ -7,6 +7,7 @@
 #include "context.h"
 
 #include <algorithm>
+#include <numeric>
 #include <cerrno>
 #include <cstring>
 #include <limits>
@@ -176,6 +177,19 @@ int update_tables(hbfsim_context* c)
         c->t_max = std::max(c->t_max, ob);
         c->admit_max = std::max(c->admit_max, ab);
     }
+    // one shared bandwidth whose 1e9 / bw reduces to 1 / 2^s: the kernels
+    // take the shift from their arguments instead of the channel table
+    c->x_uniform_shift = 0xffu;
+    if (c->C > 0 && std::all_of(h_bw.begin(), h_bw.end(),
+                                [&](std::uint64_t v) { return v == h_bw[0]; })) {
+        const std::uint64_t g = std::gcd<std::uint64_t, std::uint64_t>(1000000000ull, h_bw[0]);
+        const std::uint64_t num = 1000000000ull / g, den = h_bw[0] / g;
+        if (num == 1 && (den & (den - 1)) == 0) {
+            std::uint32_t sh = 0;
+            while ((1ull << sh) < den) ++sh;
+            if (sh < 32) c->x_uniform_shift = sh;
+        }
+    }
     const std::size_t bytes = sizeof(std::uint64_t) * c->C;
     if (cudaMemcpyAsync(c->d_chan_bw, h_bw.data(), bytes, cudaMemcpyHostToDevice, c->stream) ||
         cudaMemcpyAsync(c->d_t_read, h_tr.data(), bytes, cudaMemcpyHostToDevice, c->stream) ||
@@ -325,6 +339,8 @@ TimingParams timing_params(const hbfsim_context* c)
     t.fast_service_read = std::max(x, p.read_latency_ns);   // hbf_device.cuh:797-817
     t.fast_service_prog = std::max(x, p.program_latency_ns);
     t.chan_bw = c->d_chan_bw;
+    // the thermal controller rewrites the bandwidth table on the device
+    t.x_shift = c->thermal ? 0xffu : c->x_uniform_shift;
     t.chan_t_read = c->d_t_read;
     t.chan_t_prog = c->d_t_prog;
     t.chan_admit = c->d_admit;

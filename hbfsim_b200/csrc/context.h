@@ -71,6 +71,9 @@ struct hbfsim_context {
     std::vector<std::uint32_t> throttle_permille;  // per stack
     std::vector<std::uint64_t> admit_after;        // per stack
     std::uint64_t x_max = 0;   // largest transfer tick of any access (scaled)
+    // every channel's transfer is (bytes + 2^x_shift - 1) >> x_shift (one
+    // bandwidth of 1e9 / 2^x_shift bytes per second); 0xff when not
+    std::uint32_t x_uniform_shift = 0xffu;
     std::uint64_t t_max = 0;   // largest die op tick (scaled, throttled)
     std::uint64_t admit_max = 0;
 

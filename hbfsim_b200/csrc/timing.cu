@@ -463,7 +463,13 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
             if (d.status == kModeled) {
                 key = MODEL == kModelDie ? d.local : 0u;
                 if (MODEL == kModelDie) {
-                    const u64 x = transfer_ticks(b, s.chan[key], A.tp.time_scale);
+                    const u32 xs = A.tp.x_shift;
+                    const u64 x =
+                        xs != kXDivide
+                            ? static_cast<u64>(static_cast<u32>(
+                                  (static_cast<u64>(b) + ((u64{1} << xs) - 1)) >> xs)) *
+                                  A.tp.time_scale
+                            : transfer_ticks(b, s.chan[key], A.tp.time_scale);
                     if (x > 0xffffffull) atomicOr(A.error, kErrNeedSeq);
                     info |= static_cast<u32>(x & 0xffffffull) | (d.die << 24);
                     if (activity) {
@@ -482,16 +488,20 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
             }
             s.bytes[e] = info;
             s.op[e] = static_cast<u8>(d.status);
+            s.key[e] = static_cast<u16>(key);
         }
+    }
+    __syncwarp();
+    // rank the warp's chunk 32 accesses at a time, in index order
+    for (u32 j = 0; j < chunk; j += 32) {
+        const u32 e = warp * chunk + j + lane;
+        const u32 key = e < nt ? static_cast<u32>(s.key[e]) : C;
         const u32 peers = __match_any_sync(0xffffffffu, key);
         const u32 before = __popc(peers & ((1u << lane) - 1u));
         const u32 base = s.wcnt[warp * (C + 1) + key];
         __syncwarp();
         if (before == 0) s.wcnt[warp * (C + 1) + key] = base + __popc(peers);
-        if (e < nt) {
-            s.key[e] = static_cast<u16>(key);
-            s.rank[e] = static_cast<u16>(base + before);
-        }
+        if (e < nt) s.rank[e] = static_cast<u16>(base + before);
         __syncwarp();
     }
     if (PASS == 1 && unsorted && !A.tp.any_order) atomicOr(A.error, kErrUnsorted);
