@@ -136,6 +136,9 @@ struct TimingParams {
     // < 32: every channel's transfer is (bytes + 2^x_shift - 1) >> x_shift
     // ticks before scaling; 0xff: per channel (ChanInfo)
     u32 x_shift;
+    // bound on one access's transfer plus die time (scaled ticks, including
+    // what the thermal controller may set); 0: unknown
+    i64 step_max;
 };
 
 // Device-side counters (one block of u64 per context).

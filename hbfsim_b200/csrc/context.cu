@@ -341,6 +341,9 @@ TimingParams timing_params(const hbfsim_context* c)
     t.chan_bw = c->d_chan_bw;
     // the thermal controller rewrites the bandwidth table on the device
     t.x_shift = c->thermal ? 0xffu : c->x_uniform_shift;
+    // x_max and t_max already cover the thermal controller's factors
+    t.step_max = c->x_max + c->t_max < (1ull << 40)
+                     ? static_cast<i64>(c->x_max + c->t_max) : 0;
     t.chan_t_read = c->d_t_read;
     t.chan_t_prog = c->d_t_prog;
     t.chan_admit = c->d_admit;

@@ -299,6 +299,95 @@ struct DieRegs {
     }
 };
 
+// Replay of one channel's shifted segment [first, last) in 32-bit words
+// relative to a base B: the same max-plus steps on one-instruction integer
+// max and add, so each step's dependency chain is a few cycles instead of
+// the 64-bit compare/select sequences.
+//   REAL   arrivals from sarr (non-decreasing in a sorted batch); otherwise
+//          the arrival is -inf (the unit columns of pass 1).
+//   WRITE  each completion tick goes back to sarr[k] (pass 2).
+// B = max(first arrival, chan): every max of the segment has an operand
+// >= B (an arrival, or chan, which never decreases), so state words below
+// B cannot win and are clamped to -1; a word that is still -1 at the end
+// was not touched and keeps its 64-bit value.  When the queue runs more
+// than 2^30 ahead of the first arrival, the segment's arrivals must all be
+// at or below B (then none of them wins and the unit step is exact);
+// otherwise the function declines.  Every word stays below
+// hi + (n + 1) * step_max, hi the largest starting word or arrival above B
+// and step_max a bound on one access's transfer plus die time; when that is
+// not below 2^31 the function returns false with `reg` unchanged and the
+// caller replays in 64 bits.
+template <int D, bool ARR, bool WRITE>
+__device__ __forceinline__ void rel32_loop(int& rc, int (&rd)[D], i64* sarr, const u32* sinfo,
+                                           u32 first, u32 last, i64 B, int t_read, int t_prog)
+{
+    // operands one step ahead; index `last` <= T + C - 1 stays inside the
+    // sorted arrays
+    i64 a_next = ARR ? sarr[first] : 0;
+    u32 info_next = sinfo[first];
+#pragma unroll 4
+    for (u32 k = first; k < last; ++k) {
+        const i64 a64 = a_next;
+        const u32 info = info_next;
+        if (ARR) a_next = sarr[k + 1];
+        info_next = sinfo[k + 1];
+        const int x = static_cast<int>(info & 0xffffffu);
+        const u32 d = (info >> 24) & 15u;
+        const int t = (info >> 28) & 1u ? t_prog : t_read;
+        int cur = rd[0];
+#pragma unroll
+        for (int j = 1; j < D; ++j) cur = d == static_cast<u32>(j) ? rd[j] : cur;
+        if (ARR) rc = max(max(static_cast<int>(a64 - B), rc), cur) + x;
+        else rc = max(rc, cur) + x;
+        const int done = rc + t;
+#pragma unroll
+        for (int j = 0; j < D; ++j)
+            if (d == static_cast<u32>(j)) rd[j] = done;
+        if (WRITE) sarr[k] = B + done;
+    }
+}
+
+template <int D, bool REAL, bool WRITE>
+__device__ __forceinline__ bool replay_rel32(DieRegs<D>& reg, i64* sarr, const u32* sinfo,
+                                             u32 first, u32 last, const ChanInfo& ci,
+                                             i64 step_max)
+{
+    constexpr i64 kWindow = i64{1} << 30;
+    if (reg.chan < kNeg / 2 && !REAL) return false;
+    bool arrivals = REAL;
+    i64 B = reg.chan, hi = 0;
+    if (REAL) {
+        const i64 a_first = sarr[first], a_last = sarr[last - 1];
+        B = imax(a_first, reg.chan);
+        if (B - a_first >= kWindow) {
+            if (a_last > B) return false;  // the arrivals overtake the queue inside the segment
+            arrivals = false;
+        }
+        hi = a_last - B;
+    }
+    int rc, rd[D];
+    {
+        const i64 v = reg.chan - B;
+        hi = imax(hi, v);
+        rc = v < 0 ? -1 : static_cast<int>(v);
+    }
+#pragma unroll
+    for (int j = 0; j < D; ++j) {
+        const i64 v = reg.die[j] - B;
+        hi = imax(hi, v);
+        rd[j] = v < 0 ? -1 : static_cast<int>(v);
+    }
+    if (hi + static_cast<i64>(last - first + 1) * step_max >= (i64{1} << 31)) return false;
+    const int t_read = static_cast<int>(ci.t_read), t_prog = static_cast<int>(ci.t_prog);
+    if (arrivals) rel32_loop<D, true, WRITE>(rc, rd, sarr, sinfo, first, last, B, t_read, t_prog);
+    else rel32_loop<D, false, WRITE>(rc, rd, sarr, sinfo, first, last, B, t_read, t_prog);
+    reg.chan = B + rc;
+#pragma unroll
+    for (int j = 0; j < D; ++j)
+        if (rd[j] >= 0) reg.die[j] = B + rd[j];
+    return true;
+}
+
 __device__ __forceinline__ u32 lane_id() { return threadIdx.x & 31u; }
 
 // Exclusive scan of `count` u32 values in shared memory by warp 0.
@@ -884,6 +973,9 @@ direct_pass_kernel(const PassArgs args)
     }
     __syncthreads();
     Stats7 st;
+    // 32-bit relative chains need arrivals that do not decrease (a batch
+    // that must follow the arrival order; pass 1 refuses it otherwise)
+    const bool rel32 = !A.tp.any_order && A.tp.step_max > 0;
 
     const u64 tile_first = static_cast<u64>(blockIdx.x) * A.tiles_per_cta;
     for (u32 tt = 0; tt < A.tiles_per_cta; ++tt) {
@@ -896,11 +988,19 @@ direct_pass_kernel(const PassArgs args)
             if (!item_on[it] || coupled[it]) continue;
             const u32 c = item_c[it];
             const u32 first = s.seg[c] + c, last = s.seg[c + 1] + c;  // shifted segment
+            if (first == last) continue;
             const ChanInfo ci = s.chan[c];
             if (item_r[it] == K) {
+                if (rel32 && replay_rel32<D, true, false>(reg[it], s.sarr, s.sinfo, first, last,
+                                                          ci, A.tp.step_max))
+                    continue;
 #pragma unroll 4
                 for (u32 k = first; k < last; ++k) reg[it].step(s.sarr[k], s.sinfo[k], ci);
             } else {
+                if (rel32 && item_r[it] == 0 &&
+                    replay_rel32<D, false, false>(reg[it], s.sarr, s.sinfo, first, last, ci,
+                                                  A.tp.step_max))
+                    continue;
 #pragma unroll 4
                 for (u32 k = first; k < last; ++k) reg[it].step_unit(s.sinfo[k], ci);
             }
@@ -1008,6 +1108,7 @@ direct_replay_kernel(const PassArgs args)
         for (int j = 0; j < D; ++j) reg.die[j] = cv[1 + j];
     }
     Stats7 st;
+    const bool rel32 = !A.tp.any_order && A.tp.step_max > 0;  // see direct_pass_kernel
     const u64 tile_first = static_cast<u64>(blockIdx.x) * A.tiles_per_cta;
     auto tile_size = [&](u64 start) -> u32 {
         return static_cast<u32>(A.n - start < T ? A.n - start : T);
@@ -1048,10 +1149,12 @@ direct_replay_kernel(const PassArgs args)
         // the staging buffers are free: stream the next tile in
         const u64 next = start + T;
         if (tt + 1 < A.tiles_per_cta && next < A.n) stage_records(A, s, next, tile_size(next));
-        if (chain) {
-            const u32 c = tid;
-            const u32 first = s.seg[c] + c, last = s.seg[c + 1] + c;  // shifted segment
-            const ChanInfo ci = s.chan[c];
+        const u32 c = tid;
+        const u32 first = chain ? s.seg[c] + c : 0u, last = chain ? s.seg[c + 1] + c : 0u;
+        const ChanInfo ci = chain ? s.chan[c] : ChanInfo{};
+        if (first < last &&
+            !(rel32 && replay_rel32<D, true, true>(reg, s.sarr, s.sinfo, first, last, ci,
+                                                   A.tp.step_max))) {
             // operands one step ahead; index `last` <= T + C - 1 stays inside
             // the sorted arrays
             i64 a_next = s.sarr[first];

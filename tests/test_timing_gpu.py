@@ -150,6 +150,39 @@ def test_saturating_sequential_path(tmp, model):
     assert np.array_equal(ctx.get_state(), ora.state)
 
 
+def test_deep_backlog_and_long_gaps(tmp):
+    """The chains replay a channel's accesses in 32-bit words relative to a
+    base while every word of the tile stays within 2^31 of it, else in 64
+    bits.  Three phases in one batch: 800,000 accesses (90 % writes) at one
+    arrival, whose die queues run seconds ahead of the arrivals (the unit
+    step once the queue is 2^30 past the arrivals); arrivals with a 3e9-tick
+    gap every 300 accesses (tiles span more than 2^31, and the arrivals
+    overtake the queue inside a segment); then the usual gaps."""
+    s = c0_setup(3, stacks=1)
+    ctx = make_context(s, tmp)
+    deep, gapped = 800_000, 150_000
+    n = deep + 2 * gapped
+    addr, nbytes, op, _ = wl.c0_trace(n, seed=21)
+    rng = np.random.default_rng(22)
+    op[:deep] = (rng.random(deep) < 0.9).astype(np.uint8)
+    gaps = np.zeros(n, np.uint64)
+    gaps[0] = 1000
+    gaps[deep:deep + gapped:300] = 3_000_000_000
+    gaps[deep + gapped:] = np.rint(rng.exponential(2.0, gapped)).astype(np.uint64)
+    arrival = np.cumsum(gaps, dtype=np.uint64)
+    ora = OracleRun(s)
+    want = ora.run(addr, nbytes, op, arrival, threads=4)
+    assert want[1][:deep].max() > (1 << 31)  # the queues outgrew the 32-bit window
+    assert_same(gpu_run(ctx, (addr, nbytes, op, arrival)), want, "backlog and gaps")
+    assert np.array_equal(ctx.get_state(), ora.state)
+    # the same accesses again, the carried state far ahead of the new arrivals
+    arrival2 = arrival + arrival[-1] + np.uint64(1)
+    want2 = ora.run(addr, nbytes, op, arrival2, threads=4)
+    assert_same(gpu_run(ctx, (addr, nbytes, op, arrival2)), want2, "second batch")
+    assert np.array_equal(ctx.get_state(), ora.state)
+    ctx.close()
+
+
 def test_refresh_throttle_admit_factors(tmp):
     s = c0_setup(3, stacks=2)
     ctx = make_context(s, tmp)
