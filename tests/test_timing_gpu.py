@@ -183,6 +183,41 @@ def test_deep_backlog_and_long_gaps(tmp):
     ctx.close()
 
 
+def test_chain_window_boundaries(tmp):
+    """Carried states placed around the edges of the 32-bit chain window:
+    channel c starts with its queue at first arrival + delta[c], deltas from
+    far below the arrivals to 2^32 above them, around 2^30 (where the
+    arrivals stop counting unless they overtake the queue) and 2^31 (where
+    the window ends).  Arrival jumps of 1.5e9 and 3e9 ticks inside tiles let
+    arrivals overtake the queues mid-segment.  Every channel's result must
+    equal the oracle's, whichever replay each segment takes."""
+    s = c0_setup(3, stacks=1)
+    ctx = make_context(s, tmp)
+    C, K = s.local_channels, s.k
+    a0 = 10**12
+    deltas = [-(2**31) - 5, -(2**30), -5, 0, 1, 2**20, 2**30 - 2, 2**30 - 1, 2**30, 2**30 + 1,
+              2**30 + 2**29, 2**31 - 2**25, 2**31 - 1, 2**31, 2**31 + 7, 2**32]
+    assert len(deltas) == C
+    state = np.zeros(C * K, np.uint64)
+    for c, dl in enumerate(deltas):
+        chan = a0 + dl
+        state[c * K] = chan
+        for j in range(1, K):
+            state[c * K + j] = max(0, chan + 1000 * j - 2000)
+    n = 20_000
+    addr, nbytes, op, _ = wl.c0_trace(n, seed=31)
+    arrival = a0 + np.arange(n, dtype=np.uint64)
+    arrival[5000:] += np.uint64(1_500_000_000)
+    arrival[12_000:] += np.uint64(3_000_000_000)
+    ctx.set_state(state)
+    ora = OracleRun(s)
+    ora.state[:] = state
+    want = ora.run(addr, nbytes, op, arrival)
+    assert_same(gpu_run(ctx, (addr, nbytes, op, arrival)), want, "window boundaries")
+    assert np.array_equal(ctx.get_state(), ora.state)
+    ctx.close()
+
+
 def test_refresh_throttle_admit_factors(tmp):
     s = c0_setup(3, stacks=2)
     ctx = make_context(s, tmp)
