@@ -646,16 +646,20 @@ def run_prefetch(args, device, tmp):
             cells.append(dict(common, policy="next_page"))
             for acc in (0.0, 0.1, 0.2, 0.3, 0.4, 0.5, 0.6, 0.7, 0.8, 0.9, 0.95, 1.0):
                 cells.append(dict(common, policy="accuracy", accuracy=acc))
-    prefetch_sweep(dev[:10_000], cells[:8])  # warm up (module load, first launch)
+    prefetch_sweep(dev, cells)  # warm up at full size (module load, first launch, clocks)
     torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    stats = prefetch_sweep(dev, cells)
-    dt = time.perf_counter() - t0
+    times = []
+    for _ in range(2):  # each call stages the cells, runs and reads the statistics back
+        t0 = time.perf_counter()
+        stats = prefetch_sweep(dev, cells)
+        times.append(time.perf_counter() - t0)
+    dt = min(times)
     steps = len(cells) * pages.size
     res = {"workload": f"{len(cells)} sweep cells on a 1,000,000-page MoE stream (Qwen3-30B-A3B "
                        "shape), buffer 64 pages, 32 media reads in flight, 4 us compute per "
                        "access",
            "cells": len(cells), "accesses": int(pages.size), "seconds": dt,
+           "seconds_all": times,
            "value": steps / dt, "unit": "cell-accesses/s",
            # the group's no-prefetch cell sits 13 cells before its accuracy-1.0 cell
            "best_speedup_over_no_prefetch": max(

@@ -40,8 +40,8 @@ struct RetentionState {
     std::uint64_t* d_last_commit = nullptr;  // last committed refresh (kNever: none)
     std::uint32_t* d_counts = nullptr;   // [4][blocks]: program started / completed,
                                          // erase started / completed
-    double* d_prev_temp = nullptr;       // per local die
-    double* d_rate = nullptr;            // per local die, this epoch
+    double* d_prev_temp = nullptr;       // per local die: the last epoch's temperature
+    double* d_prev_next = nullptr;       // per local die: this epoch's (swapped after it)
     std::uint32_t* d_error = nullptr;
     std::uint32_t* d_cta_counts = nullptr;
     std::uint32_t cta_capacity = 0;
@@ -93,13 +93,21 @@ __global__ void init_kernel(double* age, std::uint64_t* next_due, std::uint64_t*
     for (int k = 0; k < 4; ++k) counts[k * n + i] = 0;
 }
 
-// One Arrhenius rate per local die (the cohort of its blocks): at the
-// midpoint of the previous and current temperature, or at `temp` itself.
-struct RateArgs {
-    const double* temp;      // per local die, or per global die (global_index)
-    double* prev;            // per local die
-    double* rate;
-    std::uint32_t dies;      // local dies
+// One epoch of the ledger in one launch.  Each CTA ages kTile consecutive
+// blocks; first it computes the Arrhenius rate of every local die (the
+// cohort of its blocks) that its blocks belong to -- at the midpoint of the
+// previous and current temperature, or at the current one -- into shared
+// memory.  The CTA holding a die's first block also records that die's
+// temperature for the next epoch, in a second buffer that the host swaps
+// in after the launch, so no CTA reads a temperature another has replaced.
+struct AgeArgs {
+    const double* temp;         // per local die, or per global die (global_index)
+    const double* prev;         // per local die, the last epoch's
+    double* prev_next;          // per local die, written for the next epoch
+    double* age;
+    std::uint64_t n;            // blocks
+    std::uint64_t blocks_per_die;
+    double interval;            // end - start of the epoch, ns
     std::uint32_t D;
     std::uint32_t shard_rank, shard_count;
     std::uint32_t global_index;  // temp is indexed by global die (thermal model)
@@ -109,10 +117,8 @@ struct RateArgs {
     std::uint32_t* error;
 };
 
-__global__ void rate_kernel(const RateArgs a)
+__device__ __forceinline__ double die_rate(const AgeArgs& a, std::uint32_t i, bool owner)
 {
-    const std::uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= a.dies) return;
     std::uint32_t src = i;
     if (a.global_index) {
         const std::uint32_t c = i / a.D, d = i - c * a.D;
@@ -120,24 +126,36 @@ __global__ void rate_kernel(const RateArgs a)
     }
     const double cur = a.temp[src];
     const double t = a.midpoint ? __dadd_rn(a.prev[i], cur) / 2 : cur;
-    a.prev[i] = cur;
+    if (owner) a.prev_next[i] = cur;
     if (!(t > 0.0) || !isfinite(t)) {
         atomicOr(a.error, kErrTemperature);
-        a.rate[i] = 0.0;
-        return;
+        return 0.0;
     }
     // reliability.py:17-23, same operation order
-    a.rate[i] = exp(__dmul_rn(a.ea_over_kb, __dsub_rn(a.inv_tref, __ddiv_rn(1.0, t))));
+    return exp(__dmul_rn(a.ea_over_kb, __dsub_rn(a.inv_tref, __ddiv_rn(1.0, t))));
 }
 
-__global__ void age_kernel(double* age, const double* rate, std::uint64_t n,
-                           std::uint64_t blocks_per_die, double interval)
+__global__ void __launch_bounds__(kThreads) age_kernel(const AgeArgs a)
 {
-    const std::uint64_t i = static_cast<std::uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    // reliability.py:125-131: delta = (end - start) * rate; age += delta,
-    // rounded as two operations (no fused multiply-add)
-    age[i] = __dadd_rn(age[i], __dmul_rn(interval, rate[i / blocks_per_die]));
+    __shared__ double s_rate[kTile];
+    const std::uint64_t b0 = static_cast<std::uint64_t>(blockIdx.x) * kTile;
+    const std::uint64_t last = (b0 + kTile < a.n ? b0 + kTile : a.n) - 1;
+    const std::uint64_t d_lo = b0 / a.blocks_per_die, d_hi = last / a.blocks_per_die;
+    // a CTA's kTile blocks span at most kTile dies
+    for (std::uint64_t k = threadIdx.x; k <= d_hi - d_lo; k += kThreads) {
+        const std::uint64_t d = d_lo + k;
+        s_rate[k] = die_rate(a, static_cast<std::uint32_t>(d), d * a.blocks_per_die >= b0);
+    }
+    __syncthreads();
+#pragma unroll
+    for (std::uint32_t j = 0; j < kItems; ++j) {
+        const std::uint64_t i = b0 + j * kThreads + threadIdx.x;
+        if (i >= a.n) break;
+        // reliability.py:125-131: delta = (end - start) * rate; age +=
+        // delta, rounded as two operations (no fused multiply-add)
+        a.age[i] = __dadd_rn(a.age[i],
+                             __dmul_rn(a.interval, s_rate[i / a.blocks_per_die - d_lo]));
+    }
 }
 
 __device__ __forceinline__ std::uint32_t due_bits(const double* age,
@@ -336,7 +354,7 @@ void retention_destroy(RetentionState* r)
     rfree(r->d_last_commit);
     rfree(r->d_counts);
     rfree(r->d_prev_temp);
-    rfree(r->d_rate);
+    rfree(r->d_prev_next);
     rfree(r->d_error);
     rfree(r->d_cta_counts);
     rfree(r->d_count);
@@ -385,7 +403,7 @@ int hbfsim_retention_configure_v1(hbfsim_context* c, const hbfsim_retention_conf
     const std::uint32_t ctas = static_cast<std::uint32_t>((blocks + kTile - 1) / kTile);
     if (!ralloc(&r->d_age, blocks) || !ralloc(&r->d_next_due, blocks) ||
         !ralloc(&r->d_last_commit, blocks) || !ralloc(&r->d_counts, 4 * blocks) ||
-        !ralloc(&r->d_prev_temp, r->local_dies) || !ralloc(&r->d_rate, r->local_dies) ||
+        !ralloc(&r->d_prev_temp, r->local_dies) || !ralloc(&r->d_prev_next, r->local_dies) ||
         !ralloc(&r->d_error, 1) || !ralloc(&r->d_cta_counts, ctas) || !ralloc(&r->d_count, 1)) {
         retention_destroy(r);
         return HBFSIM_CUDA_ERROR;
@@ -428,25 +446,26 @@ int hbfsim_retention_advance_v1(hbfsim_context* c, uint64_t end_ns, const double
         thermal = true;
     }
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
-    RateArgs ra{};
-    ra.temp = temps;
-    ra.prev = r->d_prev_temp;
-    ra.rate = r->d_rate;
-    ra.dies = r->local_dies;
-    ra.D = c->D;
-    ra.shard_rank = c->shard_rank;
-    ra.shard_count = c->shard_count;
-    ra.global_index = thermal ? 1u : 0u;
-    ra.midpoint = thermal ? 1u : 0u;
-    ra.ea_over_kb = r->cfg.ea_ev / kKbEvPerK;
-    ra.inv_tref = 1.0 / r->cfg.tref_k;
-    ra.error = r->d_error;
-    rate_kernel<<<(r->local_dies + 255) / 256, 256, 0, s>>>(ra);
-    const std::uint64_t per_die = static_cast<std::uint64_t>(c->profile.planes_per_die) *
-                                  r->blocks_per_plane;
-    age_kernel<<<static_cast<unsigned>((r->blocks + 255) / 256), 256, 0, s>>>(
-        r->d_age, r->d_rate, r->blocks, per_die, static_cast<double>(end_ns - r->frontier_ns));
+    AgeArgs a{};
+    a.temp = temps;
+    a.prev = r->d_prev_temp;
+    a.prev_next = r->d_prev_next;
+    a.age = r->d_age;
+    a.n = r->blocks;
+    a.blocks_per_die = static_cast<std::uint64_t>(c->profile.planes_per_die) *
+                       r->blocks_per_plane;
+    a.interval = static_cast<double>(end_ns - r->frontier_ns);
+    a.D = c->D;
+    a.shard_rank = c->shard_rank;
+    a.shard_count = c->shard_count;
+    a.global_index = thermal ? 1u : 0u;
+    a.midpoint = thermal ? 1u : 0u;
+    a.ea_over_kb = r->cfg.ea_ev / kKbEvPerK;
+    a.inv_tref = 1.0 / r->cfg.tref_k;
+    a.error = r->d_error;
+    age_kernel<<<static_cast<unsigned>((r->blocks + kTile - 1) / kTile), kThreads, 0, s>>>(a);
     if (cudaGetLastError() != cudaSuccess) return HBFSIM_CUDA_ERROR;
+    std::swap(r->d_prev_temp, r->d_prev_next);
     r->frontier_ns = end_ns;
     return HBFSIM_OK;
 }
