@@ -1235,14 +1235,27 @@ struct ScanArgs {
 
 constexpr u32 kScanWarps = 8;
 
+// 8-byte global -> shared copy (cp.async.ca; both addresses 8-byte aligned).
+__device__ __forceinline__ void cp_async8(void* smem_dst, const void* gmem_src)
+{
+    const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst), "l"(gmem_src));
+}
+
+// A warp stages nb consecutive range aggregates of channel c.  The copies
+// do not pass through registers, so all of them are in flight before the
+// one wait (a load-then-store loop waits one memory round trip per
+// iteration: the compiler cannot move a load above the previous store).
 __device__ __forceinline__ void stage_aggregates(const ScanArgs& a, u32 c, u32 b0, u32 nb,
                                                  u32 per, i64* stage)
 {
     const u32 lane = threadIdx.x & 31u;
-    for (u32 k = lane; k < nb * per; k += 32) {
-        const u32 b = k / per, w = k - b * per;
-        stage[k] = a.agg[(static_cast<u64>(b0 + b) * a.C + c) * per + w];
+    for (u32 b = 0; b < nb; ++b) {
+        const i64* src = a.agg + (static_cast<u64>(b0 + b) * a.C + c) * per;
+        for (u32 w = lane; w < per; w += 32) cp_async8(stage + b * per + w, src + w);
     }
+    cp_async_commit();
+    cp_async_wait_all();
     __syncwarp();
 }
 
