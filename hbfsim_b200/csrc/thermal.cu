@@ -117,12 +117,24 @@ __device__ __forceinline__ void dmma_8x8x4(double& c0, double& c1, double a, dou
                  : "d"(a), "d"(b));
 }
 
+// 8-byte global -> shared copy that zero-fills when `bytes` is 0 (then
+// nothing is read at `gmem_src`).  A thread issues all of its copies of a K
+// step before it waits, so the step costs one memory round trip.
+__device__ __forceinline__ void cp_async8z(void* smem_dst, const void* gmem_src, unsigned bytes)
+{
+    const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(dst), "l"(gmem_src),
+                 "r"(bytes));
+}
+
 __global__ void __launch_bounds__(128) dgemm_kernel(int M, int N, int K, const double* A,
                                                     long long sa, int ta, const double* B,
                                                     long long sb, int tb, double* C, long long sc)
 {
-    __shared__ double as[kBK][kBM + 1];  // as[k][m] = op(A)(m, k)
-    __shared__ double bs[kBK][kBN + 1];  // bs[k][n] = op(B)(k, n)
+    // two K steps in shared memory: the next one streams in while the
+    // current one feeds the MMAs
+    __shared__ double as[2][kBK][kBM + 1];  // as[.][k][m] = op(A)(m, k)
+    __shared__ double bs[2][kBK][kBN + 1];  // bs[.][k][n] = op(B)(k, n)
     const double* a = A + sa * blockIdx.z;
     const double* b = B + sb * blockIdx.z;
     double* c = C + sc * blockIdx.z;
@@ -130,45 +142,60 @@ __global__ void __launch_bounds__(128) dgemm_kernel(int M, int N, int K, const d
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
     const int wm = (warp >> 1) * 16, wn = (warp & 1) * 16;
+    // global loads run along the contiguous dimension of each operand
+    auto stage = [&](int k0, int buf) {
+#pragma unroll
+        for (int idx = tid; idx < kBK * kBM; idx += 128) {
+            int m, k;
+            if (ta) { k = idx / kBM; m = idx % kBM; } else { m = idx / kBK; k = idx % kBK; }
+            const int gm = m0 + m, gk = k0 + k;
+            const bool in = gm < M && gk < K;
+            const double* src = in ? (ta ? a + static_cast<long long>(gk) * M + gm
+                                         : a + static_cast<long long>(gm) * K + gk)
+                                   : a;
+            cp_async8z(&as[buf][k][m], src, in ? 8u : 0u);
+        }
+#pragma unroll
+        for (int idx = tid; idx < kBK * kBN; idx += 128) {
+            int n, k;
+            if (tb) { n = idx / kBK; k = idx % kBK; } else { k = idx / kBN; n = idx % kBN; }
+            const int gn = n0 + n, gk = k0 + k;
+            const bool in = gk < K && gn < N;
+            const double* src = in ? (tb ? b + static_cast<long long>(gn) * K + gk
+                                         : b + static_cast<long long>(gk) * N + gn)
+                                   : b;
+            cp_async8z(&bs[buf][k][n], src, in ? 8u : 0u);
+        }
+        asm volatile("cp.async.commit_group;\n" ::);
+    };
     double acc[2][2][2];
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
         for (int j = 0; j < 2; ++j) acc[i][j][0] = acc[i][j][1] = 0.0;
-    for (int k0 = 0; k0 < K; k0 += kBK) {
-        // global loads run along the contiguous dimension of each operand
-#pragma unroll 4
-        for (int idx = tid; idx < kBK * kBM; idx += 128) {
-            int m, k;
-            if (ta) { k = idx / kBM; m = idx % kBM; } else { m = idx / kBK; k = idx % kBK; }
-            const int gm = m0 + m, gk = k0 + k;
-            as[k][m] = gm < M && gk < K ? (ta ? a[static_cast<long long>(gk) * M + gm]
-                                             : a[static_cast<long long>(gm) * K + gk])
-                                        : 0.0;
-        }
-#pragma unroll 4
-        for (int idx = tid; idx < kBK * kBN; idx += 128) {
-            int n, k;
-            if (tb) { n = idx / kBK; k = idx % kBK; } else { k = idx / kBN; n = idx % kBN; }
-            const int gn = n0 + n, gk = k0 + k;
-            bs[k][n] = gk < K && gn < N ? (tb ? b[static_cast<long long>(gn) * K + gk]
-                                             : b[static_cast<long long>(gk) * N + gn])
-                                        : 0.0;
+    stage(0, 0);
+    for (int k0 = 0, it = 0; k0 < K; k0 += kBK, ++it) {
+        const int cur = it & 1;
+        if (k0 + kBK < K) {
+            stage(k0 + kBK, cur ^ 1);
+            asm volatile("cp.async.wait_group 1;\n" ::: "memory");  // the current step landed
+        } else {
+            asm volatile("cp.async.wait_group 0;\n" ::: "memory");
         }
         __syncthreads();
 #pragma unroll
         for (int kk = 0; kk < kBK; kk += 4) {
             double fa[2], fb[2];
 #pragma unroll
-            for (int i = 0; i < 2; ++i) fa[i] = as[kk + t][wm + i * 8 + g];
+            for (int i = 0; i < 2; ++i) fa[i] = as[cur][kk + t][wm + i * 8 + g];
 #pragma unroll
-            for (int j = 0; j < 2; ++j) fb[j] = bs[kk + t][wn + j * 8 + g];
+            for (int j = 0; j < 2; ++j) fb[j] = bs[cur][kk + t][wn + j * 8 + g];
 #pragma unroll
             for (int i = 0; i < 2; ++i)
 #pragma unroll
                 for (int j = 0; j < 2; ++j) dmma_8x8x4(acc[i][j][0], acc[i][j][1], fa[i], fb[j]);
         }
-        __syncthreads();
+        __syncthreads();  // every warp is done with `cur` before it is refilled
     }
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
