@@ -92,6 +92,7 @@ __device__ __forceinline__ TimingDecoded classify_timing(const DecodeParams& p, 
 
 // The same classification for a context with one registered range, its
 // record passed by value in the kernel arguments.
+template <bool POW2 = false>
 __device__ __forceinline__ TimingDecoded classify_single(const SingleRange& r,
                                                          const DecodeParams& p, u64 a,
                                                          u32 bytes, u32 op)
@@ -109,7 +110,7 @@ __device__ __forceinline__ TimingDecoded classify_single(const SingleRange& r,
     if ((offset & r.page_mask) + bytes > r.page_mask + 1) return d;
     const u32 u = static_cast<u32>((r.file_offset + offset) >> p.stripe_shift);
     u32 g;
-    if (p.pow2) {
+    if (POW2 || p.pow2) {
         g = (u >> p.chan_shift) & p.chan_mask;
         d.die = (u >> p.die_shift) & p.die_mask;
         d.local = g >> p.shard_shift;
@@ -479,7 +480,9 @@ __device__ __forceinline__ void cp_async_wait_all()
 // Stage one tile, decode it, and build the channel-sorted order in s.ord
 // with segment starts in s.seg (stable: warps own contiguous chunks, lanes
 // are ranked in index order with __match_any_sync).
-template <int MODEL, int PASS, bool SORTED = false>
+// FAST: one registered range, power-of-two geometry, one transfer shift and
+// no activity counting, all known when the kernel is chosen.
+template <int MODEL, int PASS, bool SORTED = false, bool FAST = false>
 __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const TileSmem& s,
                                                       u64 start, u32 nt, bool activity,
                                                       Stats7& st)
@@ -543,7 +546,9 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
             const u32 o = s.op[e];
             TimingDecoded d;
             if (MODEL == kModelDie) {
-                d = single ? classify_single(A.dp.one, A.dp, a, b, o) : classify_timing(dp, a, b, o);
+                d = FAST ? classify_single<true>(A.dp.one, A.dp, a, b, o)
+                    : single ? classify_single(A.dp.one, A.dp, a, b, o)
+                             : classify_timing(dp, a, b, o);
             } else {
                 const Decoded f = classify_decode(dp, a, b, o, false);
                 d = TimingDecoded{f.status, 0u, 0u};
@@ -554,14 +559,14 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
                 if (MODEL == kModelDie) {
                     const u32 xs = A.tp.x_shift;
                     const u64 x =
-                        xs != kXDivide
+                        FAST || xs != kXDivide
                             ? static_cast<u64>(static_cast<u32>(
                                   (static_cast<u64>(b) + ((u64{1} << xs) - 1)) >> xs)) *
                                   A.tp.time_scale
                             : transfer_ticks(b, s.chan[key], A.tp.time_scale);
                     if (x > 0xffffffull) atomicOr(A.error, kErrNeedSeq);
                     info |= static_cast<u32>(x & 0xffffffull) | (d.die << 24);
-                    if (activity) {
+                    if (!FAST && activity) {
                         if (o) atomicAdd(&s.act[2 * (key * D + d.die) + 1], 1ull);
                         else atomicAdd(&s.act[2 * (key * D + d.die)],
                                        static_cast<unsigned long long>(b));
@@ -933,7 +938,7 @@ __device__ __forceinline__ bool try_couple(const i64* col0, const DieRegs<D>& v,
     return true;
 }
 
-template <int PASS, int D>
+template <int PASS, int D, bool FAST>
 __global__ void __launch_bounds__(kThreads, 3)
 direct_pass_kernel(const PassArgs args)
 {
@@ -947,7 +952,7 @@ direct_pass_kernel(const PassArgs args)
     i64* s_col0 = reinterpret_cast<i64*>(smem + A.off_pm);  // [C][K]
     // activity is counted where the access sizes are decoded (pass 1) and
     // staged until the range scan accepts the batch
-    const bool activity = A.tp.act_stage != nullptr;
+    const bool activity = !FAST && A.tp.act_stage != nullptr;
     prologue(A, s, true, activity, true);
 
     constexpr int kItems = 2;
@@ -982,7 +987,7 @@ direct_pass_kernel(const PassArgs args)
         const u64 start = (tile_first + tt) * T;
         if (start >= A.n) break;
         const u32 nt = static_cast<u32>(A.n - start < T ? A.n - start : T);
-        load_decode_partition<kModelDie, 1, true>(A, s, start, nt, activity, st);
+        load_decode_partition<kModelDie, 1, true, FAST>(A, s, start, nt, activity, st);
 #pragma unroll
         for (int it = 0; it < kItems; ++it) {
             if (!item_on[it] || coupled[it]) continue;
@@ -1684,11 +1689,26 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
         Kernel p1 = fast ? timing_pass_kernel<kModelFast, 1> : timing_pass_kernel<kModelDie, 1>;
         Kernel p2 = fast ? timing_pass_kernel<kModelFast, 2> : timing_pass_kernel<kModelDie, 2>;
         if (plan.direct) {
+            // the specialized decode: one range, power-of-two geometry, one
+            // transfer shift, no activity counting
+            const bool f = dp.one.valid && dp.pow2 && tp.x_shift != kXDivide && !tp.act_stage;
             switch (plan.dies) {
-            case 1: p1 = direct_pass_kernel<1, 1>; p2 = direct_replay_kernel<1>; break;
-            case 2: p1 = direct_pass_kernel<1, 2>; p2 = direct_replay_kernel<2>; break;
-            case 4: p1 = direct_pass_kernel<1, 4>; p2 = direct_replay_kernel<4>; break;
-            default: p1 = direct_pass_kernel<1, 8>; p2 = direct_replay_kernel<8>; break;
+            case 1:
+                p1 = f ? direct_pass_kernel<1, 1, true> : direct_pass_kernel<1, 1, false>;
+                p2 = direct_replay_kernel<1>;
+                break;
+            case 2:
+                p1 = f ? direct_pass_kernel<1, 2, true> : direct_pass_kernel<1, 2, false>;
+                p2 = direct_replay_kernel<2>;
+                break;
+            case 4:
+                p1 = f ? direct_pass_kernel<1, 4, true> : direct_pass_kernel<1, 4, false>;
+                p2 = direct_replay_kernel<4>;
+                break;
+            default:
+                p1 = f ? direct_pass_kernel<1, 8, true> : direct_pass_kernel<1, 8, false>;
+                p2 = direct_replay_kernel<8>;
+                break;
             }
         }
         for (auto k : {p1, p2}) {
