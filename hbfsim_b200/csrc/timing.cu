@@ -901,8 +901,10 @@ timing_pass_kernel(const PassArgs args)
 
 // ---------------------------------------------------------------------------
 // Direct kernels (die model, D dies known at compile time, enough channels
-// for parallelism): no pieces.  Pass 1 is direct_pass_kernel<1, D>, pass 2
-// direct_replay_kernel<D> below.
+// for parallelism): no pieces.  Pass 1 is direct_pass_kernel<1, D, FAST>
+// (FAST: the decode specialized for one range, power-of-two geometry, one
+// transfer shift and no activity counting), pass 2 direct_replay_kernel<D>
+// below.
 //
 // Pass 1: item (r, c) carries column r of channel c's range aggregate.  Items
 // are laid out r-major so that a warp holds one kind of column.  Column 0
