@@ -139,6 +139,8 @@ struct TimingParams {
     // bound on one access's transfer plus die time (scaled ticks, including
     // what the thermal controller may set); 0: unknown
     i64 step_max;
+    // 1: every admission tick is 0 and stays 0 (thermal bounds included)
+    u32 admit_zero;
 };
 
 // Device-side counters (one block of u64 per context).

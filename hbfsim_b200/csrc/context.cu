@@ -344,6 +344,7 @@ TimingParams timing_params(const hbfsim_context* c)
     // x_max and t_max already cover the thermal controller's factors
     t.step_max = c->x_max + c->t_max < (1ull << 40)
                      ? static_cast<i64>(c->x_max + c->t_max) : 0;
+    t.admit_zero = c->admit_max == 0 ? 1u : 0u;
     t.chan_t_read = c->d_t_read;
     t.chan_t_prog = c->d_t_prog;
     t.chan_admit = c->d_admit;

@@ -480,8 +480,9 @@ __device__ __forceinline__ void cp_async_wait_all()
 // Stage one tile, decode it, and build the channel-sorted order in s.ord
 // with segment starts in s.seg (stable: warps own contiguous chunks, lanes
 // are ranked in index order with __match_any_sync).
-// FAST: one registered range, power-of-two geometry, one transfer shift and
-// no activity counting, all known when the kernel is chosen.
+// FAST: one registered range, power-of-two geometry, one transfer shift, no
+// activity counting and no admission delay, all known when the kernel is
+// chosen.
 template <int MODEL, int PASS, bool SORTED = false, bool FAST = false>
 __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const TileSmem& s,
                                                       u64 start, u32 nt, bool activity,
@@ -538,7 +539,7 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
             u64 prev = __shfl_up_sync(0xffffffffu, arr, 1);
             if (lane == 0) prev = e > 0 ? s.arr[e - 1] : tile_prev;
             if (e < nt && arr < prev) unsorted = true;
-            arr_max = arr > arr_max ? arr : arr_max;
+            if (!FAST) arr_max = arr > arr_max ? arr : arr_max;
         }
         if (e < nt) {
             const u64 a = s.addr[e];
@@ -599,6 +600,9 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
         __syncwarp();
     }
     if (PASS == 1 && unsorted && !A.tp.any_order) atomicOr(A.error, kErrUnsorted);
+    // FAST batches must follow the arrival order (or are refused as
+    // unsorted), so the tile's last arrival is its largest
+    if (FAST && PASS == 1 && tid == 0 && nt > 0) arr_max = s.arr[nt - 1];
     if (PASS == 1 && arr_max >= kArrivalLimit) atomicOr(A.error, kErrNeedSeq);
     __syncthreads();
 
@@ -631,7 +635,9 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
                 const u32 info = s.bytes[e];
                 if (key < C) {
                     s.sinfo[pos + key] = info;
-                    s.sarr[pos + key] = imax(static_cast<i64>(s.arr[e]), s.chan[key].admit);
+                    // FAST: every admission tick is 0 and arrivals are below 2^59
+                    s.sarr[pos + key] = FAST ? static_cast<i64>(s.arr[e])
+                                             : imax(static_cast<i64>(s.arr[e]), s.chan[key].admit);
                 }
                 __stcs(reinterpret_cast<unsigned long long*>(A.latency + start + e),
                        static_cast<u64>(info) | (static_cast<u64>(pos) << 32) |
@@ -903,8 +909,8 @@ timing_pass_kernel(const PassArgs args)
 // Direct kernels (die model, D dies known at compile time, enough channels
 // for parallelism): no pieces.  Pass 1 is direct_pass_kernel<1, D, FAST>
 // (FAST: the decode specialized for one range, power-of-two geometry, one
-// transfer shift and no activity counting), pass 2 direct_replay_kernel<D>
-// below.
+// transfer shift, no activity counting and no admission delay), pass 2
+// direct_replay_kernel<D, NOADMIT> below.
 //
 // Pass 1: item (r, c) carries column r of channel c's range aggregate.  Items
 // are laid out r-major so that a warp holds one kind of column.  Column 0
@@ -1092,7 +1098,7 @@ __device__ __forceinline__ void stage_records(const PassArgs& A, const TileSmem&
 
 constexpr u32 kOutBatch = 8;  // tiles hold at most 2048 = 8 x kThreads accesses
 
-template <int D>
+template <int D, bool NOADMIT>
 __global__ void __launch_bounds__(kThreads, 3)
 direct_replay_kernel(const PassArgs args)
 {
@@ -1137,7 +1143,9 @@ direct_replay_kernel(const PassArgs args)
             if (status == kModeled) {
                 const u32 k = record_slot(r);
                 s.sinfo[k] = static_cast<u32>(r);
-                s.sarr[k] = imax(static_cast<i64>(arr), s.chan[r >> 56].admit);
+                // NOADMIT: every admission tick is 0 (arrivals are below 2^59)
+                s.sarr[k] = NOADMIT ? static_cast<i64>(arr)
+                                    : imax(static_cast<i64>(arr), s.chan[r >> 56].admit);
                 slot_of[j] = static_cast<u16>(k);
                 atomicAdd(&s.seg[r >> 56], 1u);
                 ++st.modeled;
@@ -1693,23 +1701,25 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
         if (plan.direct) {
             // the specialized decode: one range, power-of-two geometry, one
             // transfer shift, no activity counting
-            const bool f = dp.one.valid && dp.pow2 && tp.x_shift != kXDivide && !tp.act_stage;
+            const bool f = dp.one.valid && dp.pow2 && tp.x_shift != kXDivide && !tp.act_stage &&
+                           tp.admit_zero;
+            const bool z = tp.admit_zero != 0;
             switch (plan.dies) {
             case 1:
                 p1 = f ? direct_pass_kernel<1, 1, true> : direct_pass_kernel<1, 1, false>;
-                p2 = direct_replay_kernel<1>;
+                p2 = z ? direct_replay_kernel<1, true> : direct_replay_kernel<1, false>;
                 break;
             case 2:
                 p1 = f ? direct_pass_kernel<1, 2, true> : direct_pass_kernel<1, 2, false>;
-                p2 = direct_replay_kernel<2>;
+                p2 = z ? direct_replay_kernel<2, true> : direct_replay_kernel<2, false>;
                 break;
             case 4:
                 p1 = f ? direct_pass_kernel<1, 4, true> : direct_pass_kernel<1, 4, false>;
-                p2 = direct_replay_kernel<4>;
+                p2 = z ? direct_replay_kernel<4, true> : direct_replay_kernel<4, false>;
                 break;
             default:
                 p1 = f ? direct_pass_kernel<1, 8, true> : direct_pass_kernel<1, 8, false>;
-                p2 = direct_replay_kernel<8>;
+                p2 = z ? direct_replay_kernel<8, true> : direct_replay_kernel<8, false>;
                 break;
             }
         }
