@@ -535,9 +535,9 @@ __device__ __forceinline__ void load_decode_partition(const PassArgs& A, const T
         u32 key = C;
         const u64 arr = e < nt ? s.arr[e] : 0;
         if (PASS == 1) {
-            // previous arrival: the lane below, else the element before the chunk
-            u64 prev = __shfl_up_sync(0xffffffffu, arr, 1);
-            if (lane == 0) prev = e > 0 ? s.arr[e - 1] : tile_prev;
+            // previous arrival: the element before this one in the staged tile
+            // (for the tile's first, the arrival before the tile)
+            const u64 prev = e > 0 ? (e <= nt ? s.arr[e - 1] : 0) : tile_prev;
             if (e < nt && arr < prev) unsorted = true;
             if (!FAST) arr_max = arr > arr_max ? arr : arr_max;
         }
