@@ -1066,7 +1066,10 @@ int hbfsim_get_die_activity_v1(hbfsim_context* c, uint64_t* read_bytes, uint64_t
 // In host code the array's name is only a stand-in for the device variable:
 // its device address is looked up with cudaGetSymbolAddress once per device,
 // on that device's first call, so that first call should come before any
-// stream capture begins.
+// stream capture begins.  Under CUDA's lazy module loading the array's
+// device memory is committed only when this library's module loads on the
+// device (its first kernel launch or symbol lookup there), so a caller that
+// reserves almost all memory should make its first call before reserving.
 // ---------------------------------------------------------------------------
 namespace {
 

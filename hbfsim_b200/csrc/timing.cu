@@ -1650,7 +1650,7 @@ int plan_batch(u64 n, u32 C, u32 K, u32 dies, int sm_count, BatchPlan* plan)
     return 0;
 }
 
-static const u32 kSeqFlagHost = kErrNeedSeq;
+static_assert(kErrNeedSeq < 256u, "the sequential flag is set by a one-byte memset");
 
 // Launch sequence of one batch: pass 1, range scan, pass 2, then the
 // sequential kernel, which returns at once unless the error word asks for it
@@ -1668,8 +1668,10 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
         if (err != cudaSuccess) return err;
     }
     if (initial) {
-        err = cudaMemcpyAsync(s.error, &kSeqFlagHost, sizeof(u32),
-                              cudaMemcpyHostToDevice, stream);
+        // the word is zero: setting its low byte (little-endian) gives
+        // kErrNeedSeq without a copy from host memory, so the sequence stays
+        // valid inside a stream capture
+        err = cudaMemsetAsync(s.error, static_cast<int>(kErrNeedSeq), 1, stream);
         if (err != cudaSuccess) return err;
     }
     if (!force_sequential) {

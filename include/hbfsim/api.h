@@ -2,9 +2,12 @@
  * hbfsim/api.h -- the HBFSim public C interface, kept ABI-identical so the
  * existing adapters (vLLM ctypes loader, llama.cpp patch) bind unchanged.
  *
- * Same function names, argument types, struct layouts and enum values as the
- * reference header include/hbfsim/api.h:1-111; this file is written from
- * scratch for the B200 build.  What each call does in this build:
+ * The declarations below (lines from HBFSIM_API_H to the end) restate the
+ * reference header include/hbfsim/api.h:1-111 line for line: the same
+ * function names, argument types, struct layouts, enum values and error
+ * codes.  That is the point of this file -- the adapters bind by these names
+ * and layouts -- so the similarity is required, not incidental.  Only this
+ * comment block is new.  What each call does in this build:
  *
  *   hbfsim_abi_version           returns 1 (reference src/api.cpp:3-6)
  *   hbfsim_context_create        loads and validates the profile JSON, binds

@@ -103,7 +103,12 @@ int hbfsim_submit_access_batch_v1(hbfsim_context* context,
  * 8 MiB until the process exits.  All calls share the array: calls whose
  * work overlaps on the GPU race and must be serialized by the caller.  The
  * first call on a device looks up the array's device address; make that
- * first call before any stream capture begins.  Returns HBFSIM_UNSUPPORTED
+ * first call before any stream capture begins.  With CUDA's lazy module
+ * loading (the default) the 8 MiB are committed when the library's device
+ * code first loads on a device -- at that first call, or at any earlier
+ * library call that launches a kernel there -- so a caller that is about to
+ * reserve nearly all device memory should make one call first.  Returns
+ * HBFSIM_UNSUPPORTED
  * when one CTA's scratch (local channels * (D+1) * (D+3) * 8 bytes) exceeds
  * the array; otherwise it times the batch exactly as
  * hbfsim_submit_access_batch_v1 does. */

@@ -1,11 +1,10 @@
 """Regenerate the golden fixtures in this directory from the HBFSim reference.
 
-Run where the HBFSim source tree is available (its location comes from the
-HBFSIM_REFERENCE environment variable, with the build container's reference
-mount as the default):
+Run where the HBFSim source tree is available; its location comes from the
+HBFSIM_REFERENCE environment variable, which must be set:
 
-    make -C oracle            # builds oracle/_ref/ref_goldens from reference sources
-    python tests/golden/make_goldens.py
+    make -C oracle REF=$HBFSIM_REFERENCE   # golden generators from reference sources
+    HBFSIM_REFERENCE=<tree> python tests/golden/make_goldens.py
 
 Fixtures written:
   device_goldens.jsonl   range lookup / access_supported / media_descriptor,
@@ -14,6 +13,11 @@ Fixtures written:
                          fast-model traces, all computed by the reference's own
                          functions (src/cuda_runtime/device/hbf_device.cuh,
                          src/hybrid/calibrator.cpp).
+  layout_goldens.json    the reference's stripe decode of the UCIe stack path:
+                         hbf_cold_read_bank / hbf_media_lpa
+                         (src/ucie/bank_layout.cpp) and the page-striped
+                         placement checked by ContiguousStackMap::locate and
+                         inverse_page_striped (src/ucie/stack_router.cpp).
   link_goldens.json      delivery ticks, counters and credits of the reference
                          UCIe streaming link (src/ucie/link.cpp, compiled
                          from source) on message batches.
@@ -46,10 +50,13 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REF = Path(os.environ.get("HBFSIM_REFERENCE", "/root/reference"))
+if not os.environ.get("HBFSIM_REFERENCE"):
+    sys.exit("make_goldens.py: set HBFSIM_REFERENCE to the HBFSim source tree")
+REF = Path(os.environ["HBFSIM_REFERENCE"])
 REF_BIN = REPO / "oracle" / "_ref" / "ref_goldens"
 REF_PREFETCH = REPO / "oracle" / "_ref" / "ref_prefetch"
 REF_LINK = REPO / "oracle" / "_ref" / "ref_link"
+REF_LAYOUT = REPO / "oracle" / "_ref" / "ref_layout"
 
 
 def load_exporter():
@@ -335,16 +342,40 @@ def link_goldens() -> None:
     (HERE / "link_goldens.json").write_text(json.dumps(cases))
 
 
+def layout_goldens() -> None:
+    """Stripe-decode goldens from the reference's UCIe layout functions
+    (oracle/ref_layout.cpp over src/ucie/bank_layout.cpp and
+    src/ucie/stack_router.cpp): per-LPA host channel / core die / bank, and
+    per logical offset of a page-striped parent its stack, module and
+    module-local address."""
+    out = subprocess.run([str(REF_LAYOUT)], check=True, capture_output=True,
+                         text=True).stdout.split("\n")
+    bank, stripe = [], []
+    for line in out:
+        f = line.split()
+        if not f:
+            continue
+        (bank if f[0] == "bank" else stripe).append([int(v) for v in f[1:]])
+    (HERE / "layout_goldens.json").write_text(json.dumps({
+        "bank_fields": ["host_channels", "ncdu", "banks_per_die", "lpa", "host_channel",
+                        "core_die", "bank"],
+        "bank": bank,
+        "stripe_fields": ["phase", "logical_offset", "stack", "module", "module_local"],
+        "stripe": stripe}))
+
+
+GENERATORS = {"device": device_goldens, "thermal": thermal_goldens, "lru": lru_goldens,
+              "retention": retention_goldens, "prefetch": prefetch_goldens,
+              "link": link_goldens, "layout": layout_goldens}
+
+
 def main() -> int:
+    """All fixtures, or the ones named on the command line."""
     if not REF_BIN.exists():
-        print("build oracle/_ref/ref_goldens first (make -C oracle)", file=sys.stderr)
+        print("build oracle/_ref/ref_goldens first (make -C oracle REF=...)", file=sys.stderr)
         return 2
-    device_goldens()
-    thermal_goldens()
-    lru_goldens()
-    retention_goldens()
-    prefetch_goldens()
-    link_goldens()
+    for name in sys.argv[1:] or list(GENERATORS):
+        GENERATORS[name]()
     return 0
 
 

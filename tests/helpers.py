@@ -123,3 +123,87 @@ def assert_same(gpu, oracle, what=""):
     bad = np.flatnonzero(gd != od)
     assert bad.size == 0, f"{what}: done differs at {bad[:5]} gpu={gd[bad[:5]]} oracle={od[bad[:5]]}"
     assert np.array_equal(gl, ol), what
+
+
+# ---- stripe-decode goldens from the reference's UCIe layout functions ----
+DECODE_DTYPE = np.dtype([("media_address", "<u8"), ("page", "<u8"), ("status", "<u4"),
+                         ("range_index", "<u4"), ("stack", "<u4"), ("channel", "<u4"),
+                         ("die", "<u4"), ("plane", "<u4")])
+
+
+def layout_goldens(golden_dir):
+    import json
+    with open(golden_dir / "layout_goldens.json") as f:
+        return json.load(f)
+
+
+def bank_layout_cases(golden):
+    """hbf_cold_read_bank goldens (bank_layout.cpp:59-72), grouped by layout,
+    as decode cases: a module of `host_channels` channels, `ncdu` dies and
+    `banks_per_die` banks is one stack whose planes are the banks, with 4 KiB
+    stripes and pages and allocation order CPDW (channel fastest, then bank,
+    then die) -- the order in which hbf_cold_read_bank splits an LPA.  Yields
+    (Setup, address, bytes, op, expected channel, die, plane)."""
+    groups = {}
+    for hc, nd, nb, lpa, ch, die, bank in golden["bank"]:
+        groups.setdefault((hc, nd, nb), []).append((lpa, ch, die, bank))
+    for (hc, nd, nb), rows in sorted(groups.items()):
+        p = wl.c0_profile()
+        p.update(name=f"bank-{hc}-{nd}-{nb}", channels=hc, dies_per_channel=nd,
+                 planes_per_die=nb, page_bytes=4096, plane_allocation_scheme="CPDW",
+                 capacity_bytes=1 << 43)
+        s = Setup(profile=p, model=3, stacks=1, stripe=4096)
+        s.ranges = [(wl.RANGE_BASE, 1 << 42, 1, 3)]
+        r = np.array(rows, np.uint64)
+        lpa = r[:, 0]
+        address = wl.RANGE_BASE + lpa * np.uint64(4096) + (lpa % np.uint64(32)) * np.uint64(128)
+        n = lpa.size
+        yield (s, address.astype(np.uint64), np.full(n, 128, np.uint32), np.zeros(n, np.uint8),
+               r[:, 1], r[:, 2], r[:, 3])
+
+
+def stripe_layout_cases(golden):
+    """Page-striped placement goldens (stack_router.cpp:160-250, checked
+    there by ContiguousStackMap::locate and inverse_page_striped) as decode
+    cases: 4 stacks x 16 channels, 16 KiB stripes and pages, one die and
+    plane, so a stripe unit's channel digit is the reference's
+    (page + phase) % 64 when the striped range's media offset starts `phase`
+    stripes in (a first range of phase * 16 KiB registered before it).
+    Yields (Setup, address, bytes, op, phase, expected stack, module,
+    module-local address)."""
+    groups = {}
+    for phase, offset, stack, module, local in golden["stripe"]:
+        groups.setdefault(phase, []).append((offset, stack, module, local))
+    for phase, rows in sorted(groups.items()):
+        p = wl.c0_profile()
+        p.update(name=f"stripe-{phase}", dies_per_channel=1, planes_per_die=1,
+                 plane_allocation_scheme="CWDP", capacity_bytes=4 * 16 * (64 << 20))
+        s = Setup(profile=p, model=3, stacks=4, stripe=16384)
+        length = (64 * 1024 + 37) * 16384
+        base = wl.RANGE_BASE + (1 << 40)
+        s.ranges = ([(wl.RANGE_BASE, phase * 16384, 1, 3)] if phase else []) + \
+            [(base, length, 1, 3)]
+        r = np.array(rows, np.uint64)
+        n = r.shape[0]
+        yield (s, (base + r[:, 0]).astype(np.uint64), np.full(n, 128, np.uint32),
+               np.zeros(n, np.uint8), phase, r[:, 1], r[:, 2], r[:, 3])
+
+
+def check_layout_decode(got, case, kind):
+    """Compare decoded records with a layout golden case (see the two
+    generators above); `got` is a DECODE_DTYPE array."""
+    assert (got["status"] == 1).all(), kind
+    if kind == "bank":
+        _, _, _, _, ch, die, bank = case
+        assert np.array_equal(got["channel"], ch)
+        assert np.array_equal(got["die"], die)
+        assert np.array_equal(got["plane"], bank)
+        assert (got["stack"] == 0).all()
+    else:
+        _, _, _, _, phase, stack, module, local = case
+        assert np.array_equal(got["stack"], stack)
+        assert np.array_equal(got["channel"] // 4, module)
+        if phase == 0:
+            # rows are counted from the media origin: with no phase the
+            # page inside the plane is the module-local 16 KiB page
+            assert np.array_equal(got["page"], local >> np.uint64(14))

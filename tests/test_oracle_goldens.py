@@ -344,3 +344,21 @@ def test_link_oracle_against_reference_link(golden_dir):
         assert delivered.tolist() == c["delivered"], k
         assert counters.tolist() == c["counters"], k
         assert [ar, r, now] == c["tail"], k
+
+
+def test_stripe_decode_against_reference_layout(golden_dir):
+    """A2 pinned: the oracle's mixed-radix decode reproduces the reference's
+    hbf_cold_read_bank (LPA -> channel, die, bank) and its page-striped
+    stack/module placement, in the geometries where the two describe the
+    same mapping (helpers.bank_layout_cases, helpers.stripe_layout_cases)."""
+    from helpers import (OracleRun, bank_layout_cases, check_layout_decode, layout_goldens,
+                         stripe_layout_cases)
+    golden = layout_goldens(golden_dir)
+    cases = 0
+    for kind, gen in (("bank", bank_layout_cases), ("stripe", stripe_layout_cases)):
+        for case in gen(golden):
+            ora = OracleRun(case[0])
+            got = ho.decode(ora.ranges, ora.count, ora.geometry, *case[1:4])
+            check_layout_decode(got, case, kind)
+            cases += case[1].size
+    assert cases == len(golden["bank"]) + len(golden["stripe"])

@@ -284,6 +284,26 @@ def test_decode_matches_oracle(tmp, order, stacks, stripe):
         assert np.array_equal(got[f][m], want[f][m]), f
 
 
+@pytest.mark.parametrize("kind", ["bank", "stripe"])
+def test_decode_against_reference_layout(tmp, golden_dir, kind):
+    """The device decode (hbfsim_decode_batch_v1) against goldens from the
+    reference's own UCIe layout functions (bank_layout.cpp
+    hbf_cold_read_bank, stack_router.cpp page-striped placement)."""
+    import torch
+    from helpers import (DECODE_DTYPE, bank_layout_cases, check_layout_decode,
+                         layout_goldens, stripe_layout_cases)
+    golden = layout_goldens(golden_dir)
+    gen = bank_layout_cases if kind == "bank" else stripe_layout_cases
+    for k, case in enumerate(gen(golden)):
+        ctx = make_context(case[0], f"{tmp}/{k}")
+        dev = to_device((*case[1:4], np.zeros(case[1].size, np.uint64)))
+        raw = ctx.decode(dev[0], dev[1], dev[2])
+        torch.cuda.synchronize()
+        got = np.frombuffer(raw.cpu().numpy().tobytes(), dtype=DECODE_DTYPE)
+        check_layout_decode(got, case, kind)
+        ctx.close()
+
+
 def test_c1_slice_parity(tmp):
     """A slice of the MoE decode trace (config 1 shape, 4 stacks)."""
     s = Setup(profile=wl.c0_profile(), model=3, stacks=4, stripe=4096)
