@@ -186,6 +186,62 @@ def c0_trace(n: int = 1 << 20, seed: int = 0, range_length: int = 64 * GIB,
     return address, size.astype(np.uint32), op, arrival
 
 
+# ---------------------------------------------------------------------------
+# c3: the config-0 trace tiled to 100 ms of arrivals, driving a 9 x 128 x 128
+# fp64 grid (one logic layer under 8 NAND layers), 1 ms epochs, 45 C ambient;
+# per-die power 0.5 W idle + 2 nJ per 128-B read + 50 nJ per write; refresh
+# doubles every 10 C above 70 C, taken from channel bandwidth.
+C3_EPOCHS, C3_EPOCH_NS = 100, 1_000_000
+
+
+def c3_thermal(stacks: int = 1, channels: int = 16, dies: int = 4):
+    """Grid description, floorplan (die -> cell box), power, refresh and
+    throttle laws of config 3.  Channels form a square array of cell tiles;
+    die d of a channel heats NAND layers 1 + 2d and 2 + 2d (4 dies) -- with
+    8 dies, layer 1 + d."""
+    silicon = {"cv_j_m3_k": 1.66e6, "k_xyz_w_m_k": [148.0, 148.0, 148.0]}
+    nand = {"cv_j_m3_k": 1.75e6, "k_xyz_w_m_k": [110.0, 110.0, 35.0]}
+    grid = {"nx": 128, "ny": 128, "cell_m": 100e-6,
+            "layers": [dict(silicon, thickness_m=100e-6)] +
+                      [dict(nand, thickness_m=50e-6) for _ in range(8)],
+            "bottom": {"h_w_m2_k": 0.0, "ambient_k": 318.15},
+            "top": {"h_w_m2_k": 2.0e4, "ambient_k": 318.15}, "initial_k": 318.15}
+    total = stacks * channels
+    side = int(round(total ** 0.5))
+    while total % side:
+        side -= 1
+    tx, ty = 128 // side, 128 // (total // side)
+    per_layer = 8 // dies
+    n = total * dies
+    fp = {k: np.zeros(n, np.uint32) for k in ("z0", "z_count", "x0", "x1", "y0", "y1")}
+    for g in range(total):
+        for d in range(dies):
+            i = g * dies + d
+            fp["z0"][i], fp["z_count"][i] = 1 + per_layer * d, per_layer
+            fp["x0"][i], fp["x1"][i] = (g % side) * tx, (g % side) * tx + tx
+            fp["y0"][i], fp["y1"][i] = (g // side) * ty, (g // side) * ty + ty
+    power = {"idle_w": 0.5, "read_j_per_byte": 2e-9 / 128, "write_j_per_access": 50e-9}
+    refresh = {"onset_k": 343.15, "step_k": 10.0, "base_permille": 10, "cap_permille": 500}
+    throttle = {"light_k": 358.15, "severe_k": 368.15, "shutdown_k": 378.15,
+                "hysteresis_k": 2.0, "light_permille": 1500, "severe_permille": 3000}
+    return grid, fp, power, refresh, throttle
+
+
+def c3_trace(epochs: int = C3_EPOCHS, epoch_ns: int = C3_EPOCH_NS, seed: int = 0):
+    """The config-0 trace tiled in time until it covers `epochs` epochs:
+    (address, bytes, op, arrival) numpy arrays cut at the last epoch's end,
+    and the epoch boundaries as indices (cuts[k]..cuts[k+1] is epoch k)."""
+    a, b, o, t = c0_trace(1 << 20, seed=seed)
+    span = int(t[-1]) + 1
+    reps = -(-epochs * epoch_ns // span)
+    arrival = (np.tile(t, reps) +
+               np.repeat(np.arange(reps, dtype=np.uint64) * np.uint64(span), t.size))
+    cuts = np.searchsorted(arrival, np.arange(epochs + 1, dtype=np.uint64) * np.uint64(epoch_ns))
+    n = int(cuts[-1])
+    return ((np.tile(a, reps)[:n], np.tile(b, reps)[:n], np.tile(o, reps)[:n], arrival[:n]),
+            [int(c) for c in cuts])
+
+
 EXPERT_BYTES = 3 * 2048 * 768 * 2
 ATTN_BYTES = 4096 * 2048 * 2
 READ_BYTES = 1024

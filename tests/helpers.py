@@ -207,3 +207,17 @@ def check_layout_decode(got, case, kind):
             # rows are counted from the media origin: with no phase the
             # page inside the plane is the module-local 16 KiB page
             assert np.array_equal(got["page"], local >> np.uint64(14))
+
+
+def activity_of(setup, oracle, arrays, status):
+    """Per local (channel, die) read bytes and write count of the modeled
+    accesses, from the oracle's decode."""
+    address, nbytes, op, _ = arrays
+    dec = ho.decode(oracle.ranges, oracle.count, oracle.geometry, address, nbytes, op)
+    m = status == 1
+    dies = setup.profile["dies_per_channel"]
+    idx = (dec["channel"][m] // setup.shard_count) * dies + dec["die"][m]
+    size = setup.local_channels * dies
+    rb = np.bincount(idx, weights=np.where(op[m] == 0, nbytes[m], 0), minlength=size)
+    wr = np.bincount(idx, weights=(op[m] == 1), minlength=size)
+    return rb.astype(np.uint64), wr.astype(np.uint64)

@@ -14,7 +14,7 @@ import pytest
 
 import hbf_oracle as ho
 import thermal_oracle as to
-from helpers import OracleRun, Setup, gpu_run, make_context, assert_same
+from helpers import OracleRun, Setup, activity_of, assert_same, gpu_run, make_context
 from hbfsim_b200 import workloads as wl
 
 pytestmark = pytest.mark.gpu
@@ -128,20 +128,6 @@ def test_grid_and_controller_match_oracle(tmp_path):
         levels_seen.update(int(x) for x in lv)
     assert levels_seen == {0, 1, 2, 3}, levels_seen
     ctx.close()
-
-
-def activity_of(setup, oracle, arrays, status):
-    """Per local (channel, die) read bytes and write count of the modeled
-    accesses, from the oracle's decode."""
-    address, nbytes, op, _ = arrays
-    dec = ho.decode(oracle.ranges, oracle.count, oracle.geometry, address, nbytes, op)
-    m = status == 1
-    dies = setup.profile["dies_per_channel"]
-    idx = (dec["channel"][m] // setup.shard_count) * dies + dec["die"][m]
-    size = setup.local_channels * dies
-    rb = np.bincount(idx, weights=np.where(op[m] == 0, nbytes[m], 0), minlength=size)
-    wr = np.bincount(idx, weights=(op[m] == 1), minlength=size)
-    return rb.astype(np.uint64), wr.astype(np.uint64)
 
 
 def test_thermal_coupled_run(tmp_path):
