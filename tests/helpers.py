@@ -152,7 +152,9 @@ def bank_layout_cases(golden):
         p.update(name=f"bank-{hc}-{nd}-{nb}", channels=hc, dies_per_channel=nd,
                  planes_per_die=nb, page_bytes=4096, plane_allocation_scheme="CPDW",
                  capacity_bytes=1 << 43)
-        s = Setup(profile=p, model=3, stacks=1, stripe=4096)
+        # the decode is the same for every timing model; the die model keeps
+        # at most 15 dies per channel, so NCDU 16 decodes in a FAST context
+        s = Setup(profile=p, model=3 if nd <= 15 else 1, stacks=1, stripe=4096)
         s.ranges = [(wl.RANGE_BASE, 1 << 42, 1, 3)]
         r = np.array(rows, np.uint64)
         lpa = r[:, 0]
