@@ -946,56 +946,40 @@ __device__ __forceinline__ bool try_couple(const i64* col0, const DieRegs<D>& v,
     return true;
 }
 
-template <int PASS, int D, bool FAST>
-__global__ void __launch_bounds__(kThreads, 3)
-direct_pass_kernel(const PassArgs args)
-{
-    static_assert(PASS == 1, "pass 2 of the direct path is direct_replay_kernel");
-    extern __shared__ __align__(16) unsigned char smem[];
-    const PassArgs& A = args;
-    const u32 tid = threadIdx.x;
-    constexpr u32 K = D + 1, KK = D + 2;
-    const u32 T = A.T, C = A.C;
-    const TileSmem s = tile_views(smem, A, 1);
-    i64* s_col0 = reinterpret_cast<i64*>(smem + A.off_pm);  // [C][K]
-    // activity is counted where the access sizes are decoded (pass 1) and
-    // staged until the range scan accepts the batch
-    const bool activity = !FAST && A.tp.act_stage != nullptr;
-    prologue(A, s, true, activity, true);
-
-    constexpr int kItems = 2;
+// The column items of one CTA's range aggregate (pass 1 of the direct
+// path): thread tid holds items q = tid and tid + kThreads of the C x (K+1)
+// (r-major) column array.
+template <int D>
+struct ColumnItems {
+    static constexpr int kItems = 2;
+    static constexpr u32 K = D + 1, KK = D + 2;
     DieRegs<D> reg[kItems];
     u32 item_c[kItems], item_r[kItems];
     bool item_on[kItems], coupled[kItems];
     i64 delta[kItems];
-    i64* agg = A.agg + static_cast<u64>(blockIdx.x) * C * K * KK;
-#pragma unroll
-    for (int it = 0; it < kItems; ++it) {
-        const u32 q = tid + it * kThreads;
-        item_on[it] = q < C * KK;
-        item_r[it] = q / C;
-        item_c[it] = q % C;
-        coupled[it] = false;
-        delta[it] = 0;
-        if (!item_on[it]) continue;
-        // identity column e_r (r == K: no constant yet)
-        reg[it].chan = item_r[it] == 0 ? 0 : kNeg;
-#pragma unroll
-        for (int j = 0; j < D; ++j)
-            reg[it].die[j] = item_r[it] == static_cast<u32>(j + 1) ? 0 : kNeg;
-    }
-    __syncthreads();
-    Stats7 st;
-    // 32-bit relative chains need arrivals that do not decrease (a batch
-    // that must follow the arrival order; pass 1 refuses it otherwise)
-    const bool rel32 = !A.tp.any_order && A.tp.step_max > 0;
 
-    const u64 tile_first = static_cast<u64>(blockIdx.x) * A.tiles_per_cta;
-    for (u32 tt = 0; tt < A.tiles_per_cta; ++tt) {
-        const u64 start = (tile_first + tt) * T;
-        if (start >= A.n) break;
-        const u32 nt = static_cast<u32>(A.n - start < T ? A.n - start : T);
-        load_decode_partition<kModelDie, 1, true, FAST>(A, s, start, nt, activity, st);
+    __device__ __forceinline__ void init(u32 C)
+    {
+#pragma unroll
+        for (int it = 0; it < kItems; ++it) {
+            const u32 q = threadIdx.x + it * kThreads;
+            item_on[it] = q < C * KK;
+            item_r[it] = q / C;
+            item_c[it] = q % C;
+            coupled[it] = false;
+            delta[it] = 0;
+            if (!item_on[it]) continue;
+            // identity column e_r (r == K: no constant yet)
+            reg[it].chan = item_r[it] == 0 ? 0 : kNeg;
+#pragma unroll
+            for (int j = 0; j < D; ++j)
+                reg[it].die[j] = item_r[it] == static_cast<u32>(j + 1) ? 0 : kNeg;
+        }
+    }
+
+    // Replay the tile's channel-sorted segments into the items' columns.
+    __device__ __forceinline__ void replay(const TileSmem& s, bool rel32, i64 step_max)
+    {
 #pragma unroll
         for (int it = 0; it < kItems; ++it) {
             if (!item_on[it] || coupled[it]) continue;
@@ -1005,24 +989,25 @@ direct_pass_kernel(const PassArgs args)
             const ChanInfo ci = s.chan[c];
             if (item_r[it] == K) {
                 if (rel32 && replay_rel32<D, true, false>(reg[it], s.sarr, s.sinfo, first, last,
-                                                          ci, A.tp.step_max))
+                                                          ci, step_max))
                     continue;
 #pragma unroll 4
                 for (u32 k = first; k < last; ++k) reg[it].step(s.sarr[k], s.sinfo[k], ci);
             } else {
                 if (rel32 && item_r[it] == 0 &&
                     replay_rel32<D, false, false>(reg[it], s.sarr, s.sinfo, first, last, ci,
-                                                  A.tp.step_max))
+                                                  step_max))
                     continue;
 #pragma unroll 4
                 for (u32 k = first; k < last; ++k) reg[it].step_unit(s.sinfo[k], ci);
             }
         }
-        __syncthreads();
-        // every 8th tile and after the last: snapshot column 0, then let the
-        // die columns try to couple to it (coupling is tested at any tile
-        // boundary; testing less often only replays a few more tiles)
-        if ((tt & 7u) != 7u && tt + 1 < A.tiles_per_cta && start + T < A.n) continue;
+    }
+
+    // Snapshot column 0 into s_col0, then let the die columns try to couple
+    // to it.  Called by every thread (contains barriers).
+    __device__ __forceinline__ void couple(i64* s_col0)
+    {
 #pragma unroll
         for (int it = 0; it < kItems; ++it) {
             if (!item_on[it] || item_r[it] != 0) continue;
@@ -1040,25 +1025,265 @@ direct_pass_kernel(const PassArgs args)
         }
         __syncthreads();
     }
-    // s_col0 holds column 0 after the last tile of the range
+
+    // Write the CTA's range aggregate; s_col0 holds column 0 after the last
+    // tile of the range.
+    __device__ __forceinline__ void write(i64* agg, const i64* s_col0) const
+    {
 #pragma unroll
-    for (int it = 0; it < kItems; ++it) {
-        if (!item_on[it]) continue;
-        const u32 c = item_c[it], r = item_r[it];
-        i64* col = agg + static_cast<u64>(c) * K * KK + r;
-        if (coupled[it]) {
-            const i64* v0 = s_col0 + static_cast<u64>(c) * K;
+        for (int it = 0; it < kItems; ++it) {
+            if (!item_on[it]) continue;
+            const u32 c = item_c[it], r = item_r[it];
+            i64* col = agg + static_cast<u64>(c) * K * KK + r;
+            if (coupled[it]) {
+                const i64* v0 = s_col0 + static_cast<u64>(c) * K;
 #pragma unroll
-            for (int i = 0; i <= D; ++i) col[i * KK] = is_neg_inf(v0[i]) ? kNeg : v0[i] + delta[it];
-        } else {
-            col[0] = reg[it].chan;
+                for (int i = 0; i <= D; ++i)
+                    col[i * KK] = is_neg_inf(v0[i]) ? kNeg : v0[i] + delta[it];
+            } else {
+                col[0] = reg[it].chan;
 #pragma unroll
-            for (int j = 0; j < D; ++j) col[(j + 1) * KK] = reg[it].die[j];
+                for (int j = 0; j < D; ++j) col[(j + 1) * KK] = reg[it].die[j];
+            }
         }
     }
+};
+
+template <int PASS, int D, bool FAST>
+__global__ void __launch_bounds__(kThreads, 3)
+direct_pass_kernel(const PassArgs args)
+{
+    static_assert(PASS == 1, "pass 2 of the direct path is direct_replay_kernel");
+    extern __shared__ __align__(16) unsigned char smem[];
+    const PassArgs& A = args;
+    const u32 tid = threadIdx.x;
+    constexpr u32 K = D + 1, KK = D + 2;
+    const u32 T = A.T, C = A.C;
+    const TileSmem s = tile_views(smem, A, 1);
+    i64* s_col0 = reinterpret_cast<i64*>(smem + A.off_pm);  // [C][K]
+    // activity is counted where the access sizes are decoded (pass 1) and
+    // staged until the range scan accepts the batch
+    const bool activity = !FAST && A.tp.act_stage != nullptr;
+    prologue(A, s, true, activity, true);
+
+    ColumnItems<D> items;
+    items.init(C);
+    i64* agg = A.agg + static_cast<u64>(blockIdx.x) * C * K * KK;
+    __syncthreads();
+    Stats7 st;
+    // 32-bit relative chains need arrivals that do not decrease (a batch
+    // that must follow the arrival order; pass 1 refuses it otherwise)
+    const bool rel32 = !A.tp.any_order && A.tp.step_max > 0;
+
+    const u64 tile_first = static_cast<u64>(blockIdx.x) * A.tiles_per_cta;
+    for (u32 tt = 0; tt < A.tiles_per_cta; ++tt) {
+        const u64 start = (tile_first + tt) * T;
+        if (start >= A.n) break;
+        const u32 nt = static_cast<u32>(A.n - start < T ? A.n - start : T);
+        load_decode_partition<kModelDie, 1, true, FAST>(A, s, start, nt, activity, st);
+        items.replay(s, rel32, A.tp.step_max);
+        __syncthreads();
+        // every 8th tile and after the last: snapshot column 0, then let the
+        // die columns try to couple to it (coupling is tested at any tile
+        // boundary; testing less often only replays a few more tiles)
+        if ((tt & 7u) != 7u && tt + 1 < A.tiles_per_cta && start + T < A.n) continue;
+        items.couple(s_col0);
+    }
+    items.write(agg, s_col0);
     if (activity)
         for (u32 k = tid; k < 2 * C * D; k += kThreads)
             if (s.act[k]) atomicAdd(&A.tp.act_stage[k], s.act[k]);
+}
+
+// ---------------------------------------------------------------------------
+// Pass 1 of the direct path for the common case -- one registered range,
+// power-of-two geometry, one transfer shift, no activity counting and no
+// admission delay (the conditions of direct_pass_kernel's FAST instantiation)
+// -- restructured around the issue rate, which bounds that kernel:
+//   * the tile size is a compile-time 2048 (8 rounds of 32 accesses per
+//     warp), so every per-access loop unrolls and its shared-memory loads
+//     issue together instead of one round trip per iteration;
+//   * decode and warp ranking are one loop, and each access's channel, rank
+//     and status stay in registers until the sorted copy (no key / rank
+//     arrays in shared memory; the step info overwrites the staged size);
+//   * the segment offsets take two barriers (warp-shuffle scan of the
+//     per-channel totals) instead of four;
+//   * the decode drops what the host has proven for this context: a page's
+//     transfer times the scale fits the 24-bit field (the host sends the
+//     batch to the sequential kernel otherwise), and every admission tick
+//     is 0.
+// Outputs and aggregates are identical to direct_pass_kernel's, and so is
+// every record field pass 2 reads (the step info of an untimed access is 0
+// here).
+constexpr u32 kFastTile = 2048;
+constexpr u32 kFastRounds = kFastTile / kThreads;  // rounds of 32 per warp
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 3)
+direct_fast_kernel(const PassArgs args)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    const PassArgs& A = args;
+    const u32 tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
+    constexpr u32 K = D + 1, KK = D + 2, T = kFastTile;
+    const u32 C = A.C;
+    const TileSmem s = tile_views(smem, A, 1);
+    i64* s_col0 = reinterpret_cast<i64*>(smem + A.off_pm);  // [C][K]
+    u32* s_part = reinterpret_cast<u32*>(s.red);            // per-warp channel totals
+    prologue(A, s, true, false, false);
+
+    ColumnItems<D> items;
+    items.init(C);
+    i64* agg = A.agg + static_cast<u64>(blockIdx.x) * C * K * KK;
+    const bool rel32 = !A.tp.any_order && A.tp.step_max > 0;
+    const SingleRange rg = A.dp.one;
+    const u32 lanes_below = (1u << lane) - 1u;
+    u32* wc = s.wcnt + warp * (C + 1);
+    __syncthreads();
+
+    const u64 tile_first = static_cast<u64>(blockIdx.x) * A.tiles_per_cta;
+    for (u32 tt = 0; tt < A.tiles_per_cta; ++tt) {
+        const u64 start = (tile_first + tt) * T;
+        if (start >= A.n) break;
+        const u32 nt = static_cast<u32>(A.n - start < T ? A.n - start : T);
+        // ---- stage the tile (all copies in flight before the one wait)
+        if (nt == T && A.vec) {
+            const uint4* g_addr = reinterpret_cast<const uint4*>(A.address + start);
+            const uint4* g_arr = reinterpret_cast<const uint4*>(A.arrival + start);
+            const uint4* g_bytes = reinterpret_cast<const uint4*>(A.bytes + start);
+            const uint4* g_op = reinterpret_cast<const uint4*>(A.op + start);
+#pragma unroll
+            for (u32 k = tid; k < T / 2; k += kThreads) {
+                cp_async16(reinterpret_cast<uint4*>(s.addr) + k, g_addr + k);
+                cp_async16(reinterpret_cast<uint4*>(s.arr) + k, g_arr + k);
+            }
+#pragma unroll
+            for (u32 k = tid; k < T / 4; k += kThreads)
+                cp_async16(reinterpret_cast<uint4*>(s.bytes) + k, g_bytes + k);
+            if (tid < T / 16) cp_async16(reinterpret_cast<uint4*>(s.op) + tid, g_op + tid);
+            cp_async_commit();
+        } else {
+            for (u32 k = tid; k < nt; k += kThreads) {
+                s.addr[k] = A.address[start + k];
+                s.arr[k] = A.arrival[start + k];
+                s.bytes[k] = A.bytes[start + k];
+                s.op[k] = A.op[start + k];
+            }
+        }
+        for (u32 k = lane; k <= C; k += 32) wc[k] = 0;
+        const u64 tile_prev = tid == 0 ? (start > 0 ? A.arrival[start - 1] : *A.last_arrival) : 0;
+        cp_async_wait_all();
+        __syncthreads();
+
+        // ---- decode and rank, 8 rounds of 32 accesses per warp
+        u32 kr[kFastRounds];   // channel key | status << 8 | rank in warp << 16
+        bool unsorted = false;
+#pragma unroll
+        for (u32 j = 0; j < kFastRounds; ++j) {
+            const u32 e = warp * (T / kWarps) + j * 32 + lane;
+            u32 key = C, status = kUnsupported, info = 0;
+            if (e < nt) {
+                const u64 a = s.addr[e];
+                const u64 arr = s.arr[e];
+                const u64 prev = e > 0 ? s.arr[e - 1] : tile_prev;
+                unsorted |= arr < prev;
+                const u32 b = s.bytes[e];
+                const u32 o = s.op[e];
+                const u64 off = a - rg.base;  // wraps when a < base
+                if (b == 0) {                 // hbf_device.cu:997-1003
+                } else if (off >= rg.length) {
+                    // below the range: unsupported if it straddles into it
+                    status = a < rg.base && a <= ~u64{0} - b && rg.base < a + b ? kUnsupported
+                                                                                 : kBypass;
+                } else if (o <= 1 && ((rg.allowed >> o) & 1u) && b <= rg.length - off &&
+                           (off & rg.page_mask) + b <= rg.page_mask + 1) {
+                    const u32 u = static_cast<u32>((rg.file_offset + off) >> A.dp.stripe_shift);
+                    const u32 g = (u >> A.dp.chan_shift) & A.dp.chan_mask;
+                    if ((g & A.dp.shard_mask) == A.dp.shard_rank) {
+                        status = kModeled;
+                        key = g >> A.dp.shard_shift;
+                        const u32 xs = A.tp.x_shift;
+                        info = ((b + ((1u << xs) - 1u)) >> xs) * A.tp.time_scale |
+                               ((u >> A.dp.die_shift) & A.dp.die_mask) << 24 | (o & 1u) << 28;
+                    } else {
+                        status = kForeign;
+                    }
+                }
+            }
+            const u32 peers = __match_any_sync(0xffffffffu, key);
+            const u32 before = __popc(peers & lanes_below);
+            const u32 base = wc[key];
+            __syncwarp();
+            if (before == 0) wc[key] = base + __popc(peers);
+            __syncwarp();
+            kr[j] = key | status << 8 | (base + before) << 16;
+            if (e < nt) s.bytes[e] = info;  // step info (transfer | die << 24 | op << 28)
+        }
+        if (unsorted && !A.tp.any_order) atomicOr(A.error, kErrUnsorted);
+        if (tid == 0 && s.arr[nt - 1] >= kArrivalLimit) atomicOr(A.error, kErrNeedSeq);
+        __syncthreads();
+
+        // ---- segment offsets: channel c's segment starts after every
+        // smaller channel's accesses; within it, warp w's accesses follow
+        // the earlier warps'.
+        {
+            const u32 c = tid;
+            u32 tot = 0;
+            u32 pre[kWarps];
+            if (c < C) {
+#pragma unroll
+                for (u32 w = 0; w < kWarps; ++w) {
+                    pre[w] = tot;
+                    tot += s.wcnt[w * (C + 1) + c];
+                }
+            }
+            u32 incl = tot;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const u32 y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= static_cast<u32>(o)) incl += y;
+            }
+            if (lane == 31) s_part[warp] = incl;
+            __syncthreads();
+            if (c < C) {
+                u32 offset = incl - tot;
+                for (u32 w = 0; w < warp; ++w) offset += s_part[w];
+#pragma unroll
+                for (u32 w = 0; w < kWarps; ++w) s.wcnt[w * (C + 1) + c] = offset + pre[w];
+                s.seg[c] = offset;
+                if (c == C - 1) s.seg[C] = offset + tot;
+            }
+            __syncthreads();
+        }
+
+        // ---- channel-sorted copy (segment c shifted by c slots) and the
+        // per-access records for pass 2 (format at record_slot)
+#pragma unroll
+        for (u32 j = 0; j < kFastRounds; ++j) {
+            const u32 e = warp * (T / kWarps) + j * 32 + lane;
+            if (e >= nt) continue;
+            const u32 key = kr[j] & 0xffu;
+            const u32 info = s.bytes[e];
+            u32 pos = 0;
+            if (key < C) {
+                pos = wc[key] + (kr[j] >> 16);
+                s.sinfo[pos + key] = info;
+                s.sarr[pos + key] = static_cast<i64>(s.arr[e]);
+            }
+            __stcs(reinterpret_cast<unsigned long long*>(A.latency + start + e),
+                   static_cast<u64>(info) | static_cast<u64>(pos) << 32 |
+                       static_cast<u64>((kr[j] >> 8) & 0xffu) << 48 |
+                       static_cast<u64>(key) << 56);
+        }
+        __syncthreads();
+
+        // ---- chains
+        items.replay(s, rel32, A.tp.step_max);
+        __syncthreads();
+        if ((tt & 7u) != 7u && tt + 1 < A.tiles_per_cta && start + T < A.n) continue;
+        items.couple(s_col0);
+    }
+    items.write(agg, s_col0);
 }
 
 // ---------------------------------------------------------------------------
@@ -1705,22 +1930,27 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
             // transfer shift, no activity counting
             const bool f = dp.one.valid && dp.pow2 && tp.x_shift != kXDivide && !tp.act_stage &&
                            tp.admit_zero;
+            const bool f2 = f && plan.T == kFastTile;  // direct_fast_kernel's fixed tile
             const bool z = tp.admit_zero != 0;
             switch (plan.dies) {
             case 1:
-                p1 = f ? direct_pass_kernel<1, 1, true> : direct_pass_kernel<1, 1, false>;
+                p1 = f2  ? direct_fast_kernel<1>
+                     : f ? direct_pass_kernel<1, 1, true> : direct_pass_kernel<1, 1, false>;
                 p2 = z ? direct_replay_kernel<1, true> : direct_replay_kernel<1, false>;
                 break;
             case 2:
-                p1 = f ? direct_pass_kernel<1, 2, true> : direct_pass_kernel<1, 2, false>;
+                p1 = f2  ? direct_fast_kernel<2>
+                     : f ? direct_pass_kernel<1, 2, true> : direct_pass_kernel<1, 2, false>;
                 p2 = z ? direct_replay_kernel<2, true> : direct_replay_kernel<2, false>;
                 break;
             case 4:
-                p1 = f ? direct_pass_kernel<1, 4, true> : direct_pass_kernel<1, 4, false>;
+                p1 = f2  ? direct_fast_kernel<4>
+                     : f ? direct_pass_kernel<1, 4, true> : direct_pass_kernel<1, 4, false>;
                 p2 = z ? direct_replay_kernel<4, true> : direct_replay_kernel<4, false>;
                 break;
             default:
-                p1 = f ? direct_pass_kernel<1, 8, true> : direct_pass_kernel<1, 8, false>;
+                p1 = f2  ? direct_fast_kernel<8>
+                     : f ? direct_pass_kernel<1, 8, true> : direct_pass_kernel<1, 8, false>;
                 p2 = z ? direct_replay_kernel<8, true> : direct_replay_kernel<8, false>;
                 break;
             }
