@@ -154,6 +154,7 @@ struct PassArgs {
     u32 off_chan, off_act, off_red, off_ranges;
     u32 off_sarr[2], off_sinfo[2];  // direct kernel: channel-sorted arrays per pass
     u32 off_slot;                   // direct replay: sorted slot of each access
+    u32 off_dies[2];                // direct pass 1: die words of the 32-bit chains
     // global scratch
     i64* agg;        // [ctas][C][K][K+1]  (pass 1 out)
     i64* incoming;   // [ctas][C][K]       (pass 2 in, carried in place)
@@ -165,6 +166,7 @@ struct PassArgs {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+constexpr u32 kThreadsDie = kThreads;  // stride of the shared die words (rel32_loop)
 
 struct ChanInfo {  // per local channel, staged in shared memory
     i64 t_read;
@@ -303,7 +305,10 @@ struct DieRegs {
 // Replay of one channel's shifted segment [first, last) in 32-bit words
 // relative to a base B: the same max-plus steps on one-instruction integer
 // max and add, so each step's dependency chain is a few cycles instead of
-// the 64-bit compare/select sequences.
+// the 64-bit compare/select sequences.  The D die words live in shared
+// memory during the loop (`sd`: word j at sd[j * kThreads], one column per
+// thread, so a warp's accesses never share a bank): a step reads and writes
+// its die's word directly instead of selecting among D registers.
 //   REAL   arrivals from sarr (non-decreasing in a sorted batch); otherwise
 //          the arrival is -inf (the unit columns of pass 1).
 //   WRITE  each completion tick goes back to sarr[k] (pass 2).
@@ -318,12 +323,43 @@ struct DieRegs {
 // and step_max a bound on one access's transfer plus die time; when that is
 // not below 2^31 the function returns false with `reg` unchanged and the
 // caller replays in 64 bits.
-template <int D, bool ARR, bool WRITE>
-__device__ __forceinline__ void rel32_loop(int& rc, int (&rd)[D], i64* sarr, const u32* sinfo,
+template <bool ARR, bool WRITE>
+__device__ __forceinline__ void rel32_loop(int& rc, int* sd, i64* sarr, const u32* sinfo,
                                            u32 first, u32 last, i64 B, int t_read, int t_prog)
 {
     // operands one step ahead; index `last` <= T + C - 1 stays inside the
     // sorted arrays
+    i64 a_next = ARR ? sarr[first] : 0;
+    u32 info_next = sinfo[first];
+#pragma unroll 4
+    for (u32 k = first; k < last; ++k) {
+        const i64 a64 = a_next;
+        const u32 info = info_next;
+        if (ARR) a_next = sarr[k + 1];
+        info_next = sinfo[k + 1];
+        const int x = static_cast<int>(info & 0xffffffu);
+        int* slot = sd + ((info >> 24) & 15u) * kThreadsDie;
+        const int t = (info >> 28) & 1u ? t_prog : t_read;
+        const int cur = *slot;
+        if (ARR) rc = max(max(static_cast<int>(a64 - B), rc), cur) + x;
+        else rc = max(rc, cur) + x;
+        const int done = rc + t;
+        *slot = done;
+        if (WRITE) sarr[k] = B + done;
+    }
+}
+
+// The same steps with the D die words in registers (a select chain reads
+// the step's die word, predicated moves write it): more instructions per
+// step, but no shared-memory round trip on the loop-carried path.  Pass 2,
+// whose chains run on a quarter of the CTA's threads while the rest wait,
+// is bound by that path; pass 1, whose chains share the SMs with other
+// CTAs' decoding, by instructions.
+template <int D, bool ARR, bool WRITE>
+__device__ __forceinline__ void rel32_loop_regs(int& rc, int (&rd)[D], i64* sarr,
+                                                const u32* sinfo, u32 first, u32 last, i64 B,
+                                                int t_read, int t_prog)
+{
     i64 a_next = ARR ? sarr[first] : 0;
     u32 info_next = sinfo[first];
 #pragma unroll 4
@@ -348,10 +384,12 @@ __device__ __forceinline__ void rel32_loop(int& rc, int (&rd)[D], i64* sarr, con
     }
 }
 
-template <int D, bool REAL, bool WRITE>
-__device__ __forceinline__ bool replay_rel32(DieRegs<D>& reg, i64* sarr, const u32* sinfo,
-                                             u32 first, u32 last, const ChanInfo& ci,
-                                             i64 step_max)
+// SMEM: the die words in shared memory (rel32_loop) or registers
+// (rel32_loop_regs; `sd` unused).
+template <int D, bool REAL, bool WRITE, bool SMEM = true>
+__device__ __forceinline__ bool replay_rel32(DieRegs<D>& reg, int* sd, i64* sarr,
+                                             const u32* sinfo, u32 first, u32 last,
+                                             const ChanInfo& ci, i64 step_max)
 {
     constexpr i64 kWindow = i64{1} << 30;
     if (reg.chan < kNeg / 2 && !REAL) return false;
@@ -380,8 +418,19 @@ __device__ __forceinline__ bool replay_rel32(DieRegs<D>& reg, i64* sarr, const u
     }
     if (hi + static_cast<i64>(last - first + 1) * step_max >= (i64{1} << 31)) return false;
     const int t_read = static_cast<int>(ci.t_read), t_prog = static_cast<int>(ci.t_prog);
-    if (arrivals) rel32_loop<D, true, WRITE>(rc, rd, sarr, sinfo, first, last, B, t_read, t_prog);
-    else rel32_loop<D, false, WRITE>(rc, rd, sarr, sinfo, first, last, B, t_read, t_prog);
+    if constexpr (SMEM) {
+#pragma unroll
+        for (int j = 0; j < D; ++j) sd[j * kThreadsDie] = rd[j];
+        if (arrivals) rel32_loop<true, WRITE>(rc, sd, sarr, sinfo, first, last, B, t_read, t_prog);
+        else rel32_loop<false, WRITE>(rc, sd, sarr, sinfo, first, last, B, t_read, t_prog);
+#pragma unroll
+        for (int j = 0; j < D; ++j) rd[j] = sd[j * kThreadsDie];
+    } else {
+        if (arrivals)
+            rel32_loop_regs<D, true, WRITE>(rc, rd, sarr, sinfo, first, last, B, t_read, t_prog);
+        else
+            rel32_loop_regs<D, false, WRITE>(rc, rd, sarr, sinfo, first, last, B, t_read, t_prog);
+    }
     reg.chan = B + rc;
 #pragma unroll
     for (int j = 0; j < D; ++j)
@@ -978,7 +1027,8 @@ struct ColumnItems {
     }
 
     // Replay the tile's channel-sorted segments into the items' columns.
-    __device__ __forceinline__ void replay(const TileSmem& s, bool rel32, i64 step_max)
+    __device__ __forceinline__ void replay(const TileSmem& s, int* sd, bool rel32,
+                                           i64 step_max)
     {
 #pragma unroll
         for (int it = 0; it < kItems; ++it) {
@@ -988,15 +1038,15 @@ struct ColumnItems {
             if (first == last) continue;
             const ChanInfo ci = s.chan[c];
             if (item_r[it] == K) {
-                if (rel32 && replay_rel32<D, true, false>(reg[it], s.sarr, s.sinfo, first, last,
-                                                          ci, step_max))
+                if (rel32 && replay_rel32<D, true, false>(reg[it], sd, s.sarr, s.sinfo, first,
+                                                          last, ci, step_max))
                     continue;
 #pragma unroll 4
                 for (u32 k = first; k < last; ++k) reg[it].step(s.sarr[k], s.sinfo[k], ci);
             } else {
                 if (rel32 && item_r[it] == 0 &&
-                    replay_rel32<D, false, false>(reg[it], s.sarr, s.sinfo, first, last, ci,
-                                                  step_max))
+                    replay_rel32<D, false, false>(reg[it], sd, s.sarr, s.sinfo, first, last,
+                                                  ci, step_max))
                     continue;
 #pragma unroll 4
                 for (u32 k = first; k < last; ++k) reg[it].step_unit(s.sinfo[k], ci);
@@ -1069,6 +1119,7 @@ direct_pass_kernel(const PassArgs args)
     ColumnItems<D> items;
     items.init(C);
     i64* agg = A.agg + static_cast<u64>(blockIdx.x) * C * K * KK;
+    int* sd = reinterpret_cast<int*>(smem + A.off_dies[0]) + tid;
     __syncthreads();
     Stats7 st;
     // 32-bit relative chains need arrivals that do not decrease (a batch
@@ -1081,7 +1132,7 @@ direct_pass_kernel(const PassArgs args)
         if (start >= A.n) break;
         const u32 nt = static_cast<u32>(A.n - start < T ? A.n - start : T);
         load_decode_partition<kModelDie, 1, true, FAST>(A, s, start, nt, activity, st);
-        items.replay(s, rel32, A.tp.step_max);
+        items.replay(s, sd, rel32, A.tp.step_max);
         __syncthreads();
         // every 8th tile and after the last: snapshot column 0, then let the
         // die columns try to couple to it (coupling is tested at any tile
@@ -1108,6 +1159,9 @@ direct_pass_kernel(const PassArgs args)
 //     arrays in shared memory; the step info overwrites the staged size);
 //   * the segment offsets take two barriers (warp-shuffle scan of the
 //     per-channel totals) instead of four;
+//   * the channel-sorted copy has buffers of its own (layout_fast), so the
+//     next tile's inputs stream into the staging buffers while the chains
+//     run;
 //   * the decode drops what the host has proven for this context: a page's
 //     transfer times the scale fits the 24-bit field (the host sends the
 //     batch to the sequential kernel otherwise), and every admission tick
@@ -1138,15 +1192,13 @@ direct_fast_kernel(const PassArgs args)
     const bool rel32 = !A.tp.any_order && A.tp.step_max > 0;
     const SingleRange rg = A.dp.one;
     const u32 lanes_below = (1u << lane) - 1u;
+    int* sd = reinterpret_cast<int*>(smem + A.off_dies[0]) + tid;
     u32* wc = s.wcnt + warp * (C + 1);
     __syncthreads();
 
-    const u64 tile_first = static_cast<u64>(blockIdx.x) * A.tiles_per_cta;
-    for (u32 tt = 0; tt < A.tiles_per_cta; ++tt) {
-        const u64 start = (tile_first + tt) * T;
-        if (start >= A.n) break;
-        const u32 nt = static_cast<u32>(A.n - start < T ? A.n - start : T);
-        // ---- stage the tile (all copies in flight before the one wait)
+    // Stage tile [start, start + nt): full aligned tiles by cp.async (all
+    // copies in flight before any wait), others by plain copies.
+    auto stage = [&](u64 start, u32 nt) {
         if (nt == T && A.vec) {
             const uint4* g_addr = reinterpret_cast<const uint4*>(A.address + start);
             const uint4* g_arr = reinterpret_cast<const uint4*>(A.arrival + start);
@@ -1170,6 +1222,16 @@ direct_fast_kernel(const PassArgs args)
                 s.op[k] = A.op[start + k];
             }
         }
+    };
+    auto tile_size = [&](u64 start) -> u32 {
+        return static_cast<u32>(A.n - start < T ? A.n - start : T);
+    };
+    const u64 tile_first = static_cast<u64>(blockIdx.x) * A.tiles_per_cta;
+    if (tile_first * T < A.n) stage(tile_first * T, tile_size(tile_first * T));
+    for (u32 tt = 0; tt < A.tiles_per_cta; ++tt) {
+        const u64 start = (tile_first + tt) * T;
+        if (start >= A.n) break;
+        const u32 nt = tile_size(start);
         for (u32 k = lane; k <= C; k += 32) wc[k] = 0;
         const u64 tile_prev = tid == 0 ? (start > 0 ? A.arrival[start - 1] : *A.last_arrival) : 0;
         cp_async_wait_all();
@@ -1277,8 +1339,11 @@ direct_fast_kernel(const PassArgs args)
         }
         __syncthreads();
 
-        // ---- chains
-        items.replay(s, rel32, A.tp.step_max);
+        // ---- the staging buffers are free: stream the next tile in while
+        // the chains run
+        const u64 next = start + T;
+        if (tt + 1 < A.tiles_per_cta && next < A.n) stage(next, tile_size(next));
+        items.replay(s, sd, rel32, A.tp.step_max);
         __syncthreads();
         if ((tt & 7u) != 7u && tt + 1 < A.tiles_per_cta && start + T < A.n) continue;
         items.couple(s_col0);
@@ -1334,6 +1399,7 @@ direct_replay_kernel(const PassArgs args)
     const u32 T = A.T, C = A.C;
     const TileSmem s = tile_views(smem, A, 2);
     u16* slot_of = reinterpret_cast<u16*>(smem + A.off_slot);  // access -> sorted slot
+    int* sd = nullptr;  // pass 2 keeps its chains' die words in registers
     if (*A.error != 0) return;  // pass 1 refused or rerouted the batch
     prologue(A, s, true, false, false);
 
@@ -1393,7 +1459,7 @@ direct_replay_kernel(const PassArgs args)
         const u32 first = chain ? s.seg[c] + c : 0u, last = chain ? s.seg[c + 1] + c : 0u;
         const ChanInfo ci = chain ? s.chan[c] : ChanInfo{};
         if (first < last &&
-            !(rel32 && replay_rel32<D, true, true>(reg, s.sarr, s.sinfo, first, last, ci,
+            !(rel32 && replay_rel32<D, true, true, false>(reg, sd, s.sarr, s.sinfo, first, last, ci,
                                                    A.tp.step_max))) {
             // operands one step ahead; index `last` <= T + C - 1 stays inside
             // the sorted arrays
@@ -1787,12 +1853,16 @@ static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
         a.off_sinfo[0] = take(4 * (T + C));
         a.off_sarr[0] = a.off_addr;
         a.off_ord = 0;
+        // the chains' die words overlay the key and rank arrays, which are
+        // dead once the sorted copy is written
+        a.off_dies[0] = a.off_key;
         const u32 end1 = align_up(off, 16);
         // pass 2
         off = tail;
         a.off_sarr[1] = take(8 * (T + C));
         a.off_sinfo[1] = take(4 * (T + C));
         a.off_slot = take(2 * T);
+        a.off_dies[1] = 0;
         const u32 end2 = align_up(off, 16);
         return end1 > end2 ? end1 : end2;
     }
@@ -1816,6 +1886,44 @@ static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
     a.off_die = take(8 * D * kThreads);
     a.off_sarr[0] = a.off_sarr[1] = 0;
     a.off_sinfo[0] = a.off_sinfo[1] = 0;
+    return align_up(off, 16);
+}
+
+// Shared-memory layout of direct_fast_kernel (tile kFastTile): the staged
+// inputs, the channel-sorted copy in buffers of its own (so that the next
+// tile's inputs can stream in while the chains read the sorted copy),
+// per-warp counts, segment starts, the channel table, the column-0 snapshot.
+static u32 layout_fast(PassArgs& a, u32 C, u32 K)
+{
+    u32 off = 0;
+    auto take = [&](u32 bytes) {
+        off = align_up(off, 16);
+        const u32 at = off;
+        off += bytes;
+        return at;
+    };
+    const u32 T = kFastTile;
+    a.off_addr = take(8 * T);
+    a.off_arr = take(8 * T);
+    a.off_bytes = take(4 * T);
+    a.off_op = take(T);
+    a.off_sarr[0] = take(8 * (T + C));
+    a.off_sinfo[0] = take(4 * (T + C));
+    a.off_seg = take(4 * (C + 2));
+    a.off_chan = take(static_cast<u32>(sizeof(ChanInfo)) * C);
+    // per-warp counts, the segment scan's warp totals and the column-0
+    // snapshot, with the chains' die words over them (the counts and totals
+    // are dead once the sorted copy is written, the snapshot is taken after
+    // the chains)
+    const u32 wc_bytes = align_up(4 * kWarps * (C + 1), 16);
+    const u32 red_bytes = 8 * 8 * kWarps;
+    const u32 dies_bytes = 4 * (K - 1) * kThreads;
+    const u32 shared = wc_bytes + red_bytes + 8 * C * K;
+    a.off_wcnt = take(shared > dies_bytes ? shared : dies_bytes);
+    a.off_red = a.off_wcnt + wc_bytes;
+    a.off_pm = a.off_red + red_bytes;
+    a.off_dies[0] = a.off_wcnt;
+    a.off_key = a.off_rank = a.off_ord = a.off_act = a.off_ranges = 0;
     return align_up(off, 16);
 }
 
@@ -1925,12 +2033,14 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
         using Kernel = void (*)(const PassArgs);
         Kernel p1 = fast ? timing_pass_kernel<kModelFast, 1> : timing_pass_kernel<kModelDie, 1>;
         Kernel p2 = fast ? timing_pass_kernel<kModelFast, 2> : timing_pass_kernel<kModelDie, 2>;
+        bool fast_p1 = false;
         if (plan.direct) {
             // the specialized decode: one range, power-of-two geometry, one
             // transfer shift, no activity counting
             const bool f = dp.one.valid && dp.pow2 && tp.x_shift != kXDivide && !tp.act_stage &&
                            tp.admit_zero;
             const bool f2 = f && plan.T == kFastTile;  // direct_fast_kernel's fixed tile
+            fast_p1 = f2;
             const bool z = tp.admit_zero != 0;
             switch (plan.dies) {
             case 1:
@@ -1955,13 +2065,18 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
                 break;
             }
         }
-        for (auto k : {p1, p2}) {
-            err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(plan.smem_bytes));
-            if (err != cudaSuccess) return err;
-        }
+        // direct_fast_kernel runs on a layout of its own
+        PassArgs a1 = a;
+        u32 smem1 = plan.smem_bytes;
+        if (fast_p1) smem1 = layout_fast(a1, plan.C, plan.K);
+        err = cudaFuncSetAttribute(p1, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(smem1));
+        if (err != cudaSuccess) return err;
+        err = cudaFuncSetAttribute(p2, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(plan.smem_bytes));
+        if (err != cudaSuccess) return err;
         hooks(kSlotPass1, 0, stream);
-        p1<<<plan.ctas, kThreads, plan.smem_bytes, stream>>>(a);
+        p1<<<plan.ctas, kThreads, smem1, stream>>>(a1);
         hooks(kSlotPass1, 1, stream);
         ScanArgs sa{};
         sa.agg = s.agg;
