@@ -522,6 +522,298 @@ def run_extras(args, device, tmp):
     ctx = Context(w.write_profile(tmp), report_dir=f"{tmp}/report-c3", mode=3)
     ctx.set_geometry(1, STRIPE, 0, 1)
     stack, fp, power, refresh, throttle = wl.c3_thermal()
+    ctx.thermal_configure(stack, fp, power, refresh, throttle)
+    for _ in range(3):
+        ctx.advance_epoch(1e-3)
+    torch.cuda.synchronize()
+    ctx.kernel_times()
+    ctx.set_profiling(True)
+    steps = 100
+    for _ in range(steps):
+        ctx.advance_epoch(1e-3)
+    torch.cuda.synchronize()
+    kt = ctx.kernel_times()
+    ctx.set_profiling(False)
+    ctx.close()
+    cells = 128 * 128 * 9
+    step_ms = kt["thermal"][1] / max(1, kt["thermal"][0])
+    ctrl_ms = kt["controller"][1] / max(1, kt["controller"][0])
+    th = {"workload": "config-3 grid: 1 logic + 8 NAND layers x 128 x 128 cells, fp64, "
+                      "1 ms backward-Euler steps, 64 dies",
+          "cells": cells, "steps": steps, "ms_per_step": step_ms,
+          "controller_ms_per_epoch": ctrl_ms,
+          "cell_bytes_per_step": 16 * cells,
+          "achieved_gbs_16B_per_cell": 16 * cells / (step_ms * 1e-3) / 1e9}
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, str(REPO / "oracle"))
+        import thermal_oracle as to
+        grid = to.ThermalGrid(stack)
+        power = np.zeros(cells)
+        t0 = time.perf_counter()
+        grid.step(power, 1e-3)          # includes the sparse LU factorization
+        t1 = time.perf_counter()
+        for _ in range(3):
+            grid.step(power, 1e-3)
+        t2 = time.perf_counter()
+        th["cpu_baseline"] = {"ms_per_step": (t2 - t1) / 3 * 1e3,
+                              "factor_ms": (t1 - t0) * 1e3, "cores": 1, "kind": "port",
+                              "sample": "scipy splu factor once, then 3 solves"}
+    out["thermal_step"] = th
+    out["thermal_coupled"] = run_c3(args, device, tmp)
+    out["empirical_vmem"] = run_vmem(args, device, tmp)
+    out["retention"] = run_retention(args, device, tmp)
+    out["prefetch_sweep"] = run_prefetch(args, device, tmp)
+    out["ucie_link"] = run_link(args, device, tmp)
+    return out
+
+
+def run_link(args, device, tmp):
+    """UCIe streaming-link timing for 32,768 links (the reference's scenario
+    profile: x64 at 16 GT/s, 12 AR / 56 R credit granules, 4 messages in
+    flight per direction), each carrying 512 read requests (exponential gaps
+    of mean 8 ns) and their 512 returns 3 us later."""
+    import torch
+    from hbfsim_b200 import link_batch, link_profiles
+    links, per = 32768, 512
+    rng = np.random.default_rng(0)
+    req = np.cumsum(rng.exponential(8.0, (links, per)).astype(np.int64), axis=1)
+    ret = req + 3_000
+    ready = np.concatenate([req, ret], axis=1)
+    direction = np.concatenate([np.zeros((links, per), np.uint8), np.ones((links, per), np.uint8)],
+                               axis=1)
+    order = np.argsort(ready, axis=1, kind="stable")
+    ready = np.take_along_axis(ready, order, axis=1)
+    direction = np.take_along_axis(direction, order, axis=1)
+    offsets = np.arange(links + 1, dtype=np.uint64) * (2 * per)
+    prof = link_profiles(links)  # the reference LinkProfile's scenario values
+    d_ready = torch.from_numpy(ready.reshape(-1)).to(device)
+    d_dir = torch.from_numpy(direction.reshape(-1)).to(device)
+    link_batch(prof, offsets, d_dir, d_ready)  # warm up at full size
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(3):  # each call stages profiles, runs and reads the results back
+        t0 = time.perf_counter()
+        delivered, res = link_batch(prof, offsets, d_dir, d_ready)
+        times.append(time.perf_counter() - t0)
+    dt = float(np.median(times))
+    messages = links * 2 * per
+    out = {"workload": f"{links} links x {2 * per} messages (AR + R), reference scenario profile",
+           "messages": messages, "seconds": dt, "seconds_all": times, "value": messages / dt,
+           "unit": "messages/s",
+           "refused_links": int((res["status"] != 0).sum()),
+           "flits_per_link": int(res["counters"][0, 0, 0] + res["counters"][0, 1, 0])}
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, str(REPO / "oracle"))
+        import hbf_oracle as ho
+        t0 = time.perf_counter()
+        sample = 64
+        for k in range(sample):
+            ho.link_run({"gt": 16, "ar": 12, "r": 56, "accepted": 4, "prop": 0,
+                         "consume": [0, 0]}, direction[k], ready[k].astype(np.uint64))
+        cdt = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": sample * 2 * per / cdt, "unit": "messages/s",
+                               "cores": 1, "kind": "port",
+                               "sample": f"{sample} of the links, single thread"}
+    return out
+
+
+def run_prefetch(args, device, tmp):
+    """The prefetch-model sweep: 4,032 cells (the reference sweep's grid of
+    6 read latencies x 14 policies / accuracies, times lead distances 1-48)
+    on a 1,000,000-access MoE stream shaped like Qwen3-30B-A3B (48 layers,
+    128 experts, 8 per token, 2 pages per expert), one warp per cell."""
+    import torch
+    from hbfsim_b200 import prefetch_sweep
+    rng = np.random.default_rng(0)
+    tokens = 1_000_000 // (48 * 8 * 2) + 1
+    order = np.argsort(rng.random((tokens * 48, 128)), axis=1)[:, :8]
+    layer = np.tile(np.arange(48), tokens)[:, None]
+    base = (layer * 128 + order) * 2
+    pages = (base[:, :, None] + np.arange(2)).reshape(-1)[:1_000_000].astype(np.uint64)
+    dev = torch.from_numpy(pages.view(np.int64)).to(device)
+    cells = []
+    for lead in range(1, 49):
+        for read in (1_000, 2_000, 4_000, 5_000, 10_000, 20_000):
+            common = {"lead_distance": lead, "buffer_pages": 64, "max_in_flight": 32,
+                      "read_latency_ns": read, "compute_ns_per_access": 4_000, "seed": 7}
+            cells.append(dict(common, policy="none"))
+            cells.append(dict(common, policy="next_page"))
+            for acc in (0.0, 0.1, 0.2, 0.3, 0.4, 0.5, 0.6, 0.7, 0.8, 0.9, 0.95, 1.0):
+                cells.append(dict(common, policy="accuracy", accuracy=acc))
+    prefetch_sweep(dev, cells)  # warm up at full size (module load, first launch, clocks)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(2):  # each call stages the cells, runs and reads the statistics back
+        t0 = time.perf_counter()
+        stats = prefetch_sweep(dev, cells)
+        times.append(time.perf_counter() - t0)
+    dt = min(times)
+    steps = len(cells) * pages.size
+    res = {"workload": f"{len(cells)} sweep cells on a 1,000,000-page MoE stream (Qwen3-30B-A3B "
+                       "shape), buffer 64 pages, 32 media reads in flight, 4 us compute per "
+                       "access",
+           "cells": len(cells), "accesses": int(pages.size), "seconds": dt,
+           "seconds_all": times,
+           "value": steps / dt, "unit": "cell-accesses/s",
+           # the group's no-prefetch cell sits 13 cells before its accuracy-1.0 cell
+           "best_speedup_over_no_prefetch": max(
+               stats[k - 13]["total_ns"] / s_["total_ns"] for k, s_ in enumerate(stats)
+               if cells[k]["policy"] == "accuracy" and cells[k]["accuracy"] == 1.0)}
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, str(REPO / "oracle"))
+        import hbf_oracle as ho
+        sample = [cells[k] for k in (2, 10, 13, 100)]
+        t0 = time.perf_counter()
+        for c in sample:
+            ho.prefetch_run(pages, {"policy": {"none": 0, "next_page": 1, "accuracy": 2}[c["policy"]],
+                                    "accuracy": c.get("accuracy", 1.0), "lead": c["lead_distance"],
+                                    "buffer": 64, "in_flight": 32, "read_ns": c["read_latency_ns"],
+                                    "compute_ns": 4_000, "seed": 7})
+        cdt = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": len(sample) * pages.size / cdt,
+                               "unit": "cell-accesses/s", "cores": 1, "kind": "port",
+                               "sample": "4 cells of the same sweep, single thread"}
+    return res
+
+
+def retention_profile() -> dict:
+    """A die-model profile shaped like the reference's cd8p device (32
+    channels x 8 dies x 4 planes, 4 KiB pages, 256 pages per block) with
+    2 TiB of media: 2,097,152 blocks."""
+    from hbfsim_b200 import workloads as wl
+    p = wl.c0_profile()
+    p.update(name="bench-retention", capacity_bytes=2048 << 30, page_bytes=4096, channels=32,
+             dies_per_channel=8, planes_per_die=4, pages_per_block=256)
+    return p
+
+
+def run_retention(args, device, tmp):
+    """The per-block retention ledger over 2,097,152 blocks: epochs of one
+    hour at per-die temperatures, then the due query (stable compaction) of
+    the equivalent-age-or-wall trigger."""
+    import torch
+    from hbfsim_b200 import Context, workloads as wl
+    p = retention_profile()
+    w = wl.Workload("ret", p, 1, 4096, wl.RANGE_BASE, 1 << 30)
+    ctx = Context(w.write_profile(tmp), report_dir=f"{tmp}/report-ret", mode=3)
+    n = ctx.retention_configure(1.04, 330.0, refresh_trigger="equivalent_age_or_wall")
+    dies = p["channels"] * p["dies_per_channel"]
+    rng = np.random.default_rng(0)
+    temps = [torch.from_numpy(rng.uniform(320.0, 400.0, dies)).to(device) for _ in range(8)]
+    hour = 3_600_000_000_000
+    stream = torch.cuda.current_stream()
+    for k in range(3):
+        ctx.retention_advance((k + 1) * hour, temps[k], stream)
+    torch.cuda.synchronize()
+    steps = 50
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(steps):
+        ctx.retention_advance((k + 4) * hour, temps[k % 8], stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    adv_ms = e0.elapsed_time(e1) / steps
+    t0 = time.perf_counter()
+    due_blocks, _ = ctx.retention_due((steps + 3) * hour, stream)
+    due_ms = (time.perf_counter() - t0) * 1e3
+    ctx.close()
+    res = {"workload": "retention ledger: 2,097,152 blocks (32 ch x 8 dies x 4 planes x 2048 "
+                       "blocks), 1 h epochs at per-die temperatures, Ea 1.04 eV",
+           "blocks": n, "advance_ms_per_epoch": adv_ms,
+           "advance_gbs_16B_per_block": 16 * n / (adv_ms * 1e-3) / 1e9,
+           "due_query_ms_wall": due_ms, "due_blocks": int(due_blocks.size),
+           "value": n / (adv_ms * 1e-3), "unit": "block-epochs/s"}
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, str(REPO / "oracle"))
+        import retention_oracle as ro
+        led = ro.Ledger(dies, n // dies, 1.04, refresh_trigger="equivalent_age_or_wall",
+                        initial_temperature_k=330.0)
+        host = [t.cpu().numpy() for t in temps]
+        t0 = time.perf_counter()
+        for k in range(5):
+            led.advance((k + 1) * hour, host[k], midpoint=False)
+        dt = (time.perf_counter() - t0) / 5
+        res["cpu_baseline"] = {"value": n / dt, "unit": "block-epochs/s", "cores": 1,
+                               "kind": "port",
+                               "sample": "5 epochs of the same ledger, numpy per die cohort"}
+    return res
+
+
+def run_vmem(args, device, tmp):
+    """The FAST model with an empirical burst-curve profile (cd8p-shaped
+    curve, 4 KiB pages): one batch of 2^25 page accesses in sequential streaks
+    (mean 48 pages), timed from a reset state each step."""
+    import torch
+    from hbfsim_b200 import BatchResult, Context, workloads as wl
+    p = wl.vmem_profile()
+    w = wl.Workload("vmem", p, 1, 4096, wl.RANGE_BASE, 15 << 30)
+    ctx = Context(w.write_profile(tmp), report_dir=f"{tmp}/report-vmem", mode=1)
+    ctx.register_device(wl.RANGE_BASE, 15 << 30, 1, 3)
+    n = 1 << 25
+    host = wl.vmem_trace(n, seed=0)
+    dev = [torch.from_numpy(x.view(dt)).to(device)
+           for x, dt in zip(host, (np.int64, np.int32, np.uint8, np.int64))]
+    out = BatchResult(torch.empty(n, dtype=torch.int64, device=device),
+                      torch.empty(n, dtype=torch.int64, device=device),
+                      torch.empty(n, dtype=torch.uint8, device=device))
+    stream = torch.cuda.current_stream()
+    for _ in range(3):
+        ctx.reset_state(stream)
+        ctx.submit(*dev, out=out, stream=stream)
+    torch.cuda.synchronize()
+    ctx.kernel_times()
+    ctx.set_profiling(True)
+    times = []
+    for _ in range(10):
+        ctx.reset_state(stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        ctx.submit(*dev, out=out, stream=stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    kt = ctx.kernel_times()
+    ctx.set_profiling(False)
+    stats = ctx.batch_stats()
+    ctx.close()
+    ms = statistics.median(times)
+    res = {"workload": "empirical burst curve (cd8p-shaped, FAST model): 2^25 page accesses, "
+                       "sequential streaks of mean 48 pages, 5 percent write streaks",
+           "accesses": n, "ms_per_batch": ms, "value": n / (ms * 1e-3), "unit": "accesses/s",
+           "kernels": {k: {"launches": v[0], "avg_ms": v[1] / max(1, v[0])}
+                       for k, v in kt.items() if v[0]},
+           "achieved_gbs_38B_per_access": 38 * n / (ms * 1e-3) / 1e9,
+           "device_errors": stats["device_errors"]}
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, str(REPO / "oracle"))
+        import hbf_oracle as ho
+        m = 1 << 22
+        curve = p["empirical_vmem"]["read_curve"]
+        e = ho.make_empirical([c["pages"] for c in curve], [c["cumulative_ns"] for c in curve],
+                              p["program_latency_ns"])
+        ranges = ho.make_ranges([(wl.RANGE_BASE, 15 << 30, 0, 1, 1, 3, 4096)])
+        state = np.zeros(2, np.uint64)
+        t0 = time.perf_counter()
+        ho.run_empirical(ranges, 1, e, 1, 10**9, *(x[:m] for x in host), state)
+        dt = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": m / dt, "unit": "accesses/s", "cores": 1,
+                               "kind": "port", "sample": f"first {m} accesses, single thread"}
+    return res
+
+
+def run_c3(args, device, tmp):
+    """Config 3 at full size: the config-0 trace tiled to 100 ms of arrivals
+    (about 5e7 accesses), timed epoch by epoch (1 ms) with the factors the
+    previous epoch's temperatures produced; each epoch closes with one step of
+    the 9 x 128 x 128 fp64 grid and the refresh / throttle controller."""
+    import torch
+    from hbfsim_b200 import Context, workloads as wl
+    p = wl.c0_profile()
+    p["name"] = "bench-c3t"
+    w = wl.Workload("c3t", p, 1, STRIPE, wl.RANGE_BASE, 64 << 30)
+    ctx = Context(w.write_profile(tmp), report_dir=f"{tmp}/report-c3t", mode=3)
+    ctx.register_device(wl.RANGE_BASE, 64 << 30, 1, 3)
+    stack, fp, power, refresh, throttle = wl.c3_thermal()
 
     def configure():
         ctx.thermal_configure(stack, fp, power, refresh, throttle)
