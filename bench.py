@@ -288,13 +288,15 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-c4", action="store_true",
+                    help="skip the config-4 sharded run (runs at every N otherwise)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the secondary measurements (config-2 LRU, config-3 grid step)")
     ap.add_argument("--decode-steps", type=int, default=8,
                     help="config-1 decode steps in the trace (8 = the full config; "
                          "fewer only for small profiling captures)")
     ap.add_argument("--only-extra", choices=["empirical_vmem", "thermal_coupled", "retention",
-                                             "prefetch_sweep", "ucie_link"],
+                                             "prefetch_sweep", "ucie_link", "config4"],
                     help="run one secondary measurement alone and print its JSON "
                          "(profiling captures); not a bench line")
     args = ap.parse_args()
@@ -306,7 +308,8 @@ def main():
         torch.cuda.set_device(0)
         run = {"empirical_vmem": run_vmem, "thermal_coupled": run_c3,
                "retention": run_retention, "prefetch_sweep": run_prefetch,
-               "ucie_link": run_link}[args.only_extra]
+               "ucie_link": run_link,
+               "config4": lambda a, d, t: run_c4(a, d, t, 0, 1)}[args.only_extra]
         with tempfile.TemporaryDirectory() as tmp:
             print_result(run(args, torch.device("cuda", 0), tmp))
         return 0
@@ -426,6 +429,18 @@ def main():
         except Exception as e:  # a secondary measurement must not hide the headline line
             log(f"extras failed: {e!r}")
             extras = {"error": repr(e)}
+    if not args.no_extras and not args.no_c4:
+        # config 4 on every rank (its collectives need all of them); the
+        # headline's buffers go first
+        del address, nbytes, op, arrival, out
+        torch.cuda.empty_cache()
+        try:
+            c4 = run_c4(args, device, tmp, rank, world)
+        except Exception as e:
+            log(f"[rank {rank}] config 4 failed: {e!r}")
+            c4 = {"error": repr(e)}
+        if rank == 0:
+            extras = dict(extras or {}, config4=c4)
     if rank == 0:
         emit(args, world, n, ms_max, e2e_rate, same, kernels, launches, dominant, achieved,
              peak, peak_kind, traffic, alg, path_gbs, cpu, clocks, tot, extras)
@@ -894,6 +909,192 @@ def run_c3(args, device, tmp):
         res["graph_error"] = str(exc)[:200]
     ctx.close()
     return res
+
+
+def run_c4(args, device, tmp, rank: int, world: int):
+    """Config 4, strong scaling of one fixed trace: 2^32 accesses (60 % the
+    config-1 MoE expert reads, 40 % the config-2 paged-KV reads and
+    appends, interleaved by arrival over 100 ms) on 16 stacks x 16 channels
+    x 8 dies x 4 planes, channels sharded across the ranks (channel g on rank
+    g % world).  Each rank generates the trace on its GPU and keeps its own
+    accesses (untimed).  Timed: 100 epochs of 1 ms, each one batch of the
+    rank's accesses through the per-die model, then -- on every rank -- an
+    NCCL all-gather of every die's activity (one packed buffer), the
+    replicated 9 x 128 x 128 fp64 grid step and the controller deriving the
+    rank's refresh / throttle factors for the next epoch; after the last
+    epoch an all-reduce of the statistics.  `value` = 2^32 / the slowest
+    rank's device time.  The outputs of each epoch land in one buffer per
+    rank, reused by the next epoch (the statistics consume them)."""
+    import torch
+    import torch.distributed as dist
+    from hbfsim_b200 import BatchResult, Context, sharding, workloads as wl
+    t0 = time.perf_counter()
+    gen = wl.C4Trace(device)
+    p = wl.c4_profile()
+    p["name"] = "bench-c4"
+    unit = (p["page_bytes"] * p["channels"] * p["dies_per_channel"] * p["planes_per_die"] *
+            p["pages_per_block"])
+    p["capacity_bytes"] = -(-(wl.C4_MOE_LENGTH + gen.kv_length) // unit) * unit
+    w = wl.Workload("c4", p, wl.C4_STACKS, STRIPE, wl.RANGE_BASE, wl.C4_MOE_LENGTH)
+    ctx = Context(w.write_profile(tmp), report_dir=f"{tmp}/report-c4", mode=3)
+    ctx.set_geometry(wl.C4_STACKS, STRIPE, rank, world)
+    ctx.register_device(wl.RANGE_BASE, wl.C4_MOE_LENGTH, 1, 1)   # weights: read
+    ctx.register_device(wl.C4_KV_BASE, gen.kv_length, 1, 3)      # KV: read / append
+    channels, dies = wl.C4_STACKS * p["channels"], p["dies_per_channel"]
+    local = -(-channels // world)
+    grid, fp, power, refresh, throttle = wl.c3_thermal(wl.C4_STACKS, p["channels"], dies,
+                                                       cell_m=400e-6)
+
+    def configure():
+        ctx.thermal_configure(grid, fp, power, refresh, throttle)
+    configure()
+
+    def channel_of(a):  # the context's decode: 4 KiB stripes, channel digit fastest
+        kv = a >= wl.C4_KV_BASE
+        media = torch.where(kv, a - wl.C4_KV_BASE + wl.C4_MOE_LENGTH, a - wl.RANGE_BASE)
+        return (media >> 12) % channels
+
+    cap = gen.n if world == 1 else gen.n // world + gen.n // (50 * world) + (1 << 22)
+    address = torch.empty(cap, dtype=torch.int64, device=device)
+    nbytes = torch.empty(cap, dtype=torch.int32, device=device)
+    op = torch.empty(cap, dtype=torch.uint8, device=device)
+    arrival = torch.empty(cap, dtype=torch.int64, device=device)
+    n = 0
+    for a, b, o, t in gen.chunks(channel_of, lambda g: g % world == rank):
+        k = a.numel()
+        if n + k > cap:
+            raise RuntimeError("config-4 shard exceeds its buffer")
+        address[n:n + k], nbytes[n:n + k], op[n:n + k], arrival[n:n + k] = a, b, o, t
+        n += k
+    address, nbytes, op, arrival = address[:n], nbytes[:n], op[:n], arrival[:n]
+    epochs, epoch_ns = wl.C3_EPOCHS, wl.C3_EPOCH_NS
+    cuts = torch.searchsorted(arrival, torch.arange(epochs + 1, device=device,
+                                                    dtype=torch.int64) * epoch_ns).cpu().tolist()
+    cuts[-1] = n
+    biggest = max(cuts[k + 1] - cuts[k] for k in range(epochs))
+    out = BatchResult(torch.empty(biggest, dtype=torch.int64, device=device),
+                      torch.empty(biggest, dtype=torch.int64, device=device),
+                      torch.empty(biggest, dtype=torch.uint8, device=device))
+    torch.cuda.synchronize()
+    gen_s = time.perf_counter() - t0
+    log(f"[rank {rank}] config 4: {n} of {gen.n} accesses on {local} local channels, "
+        f"generated in {gen_s:.1f} s")
+    stream = torch.cuda.current_stream()
+
+    def epoch(k, marks=None):
+        lo, hi = cuts[k], cuts[k + 1]
+        if marks is not None:
+            marks[0].record(stream)
+        if hi > lo:
+            part = BatchResult(out.done_ns[:hi - lo], out.latency_ns[:hi - lo],
+                               out.status[:hi - lo])
+            ctx.submit(address[lo:hi], nbytes[lo:hi], op[lo:hi], arrival[lo:hi], part, stream)
+        if marks is not None:
+            marks[1].record(stream)
+        if world > 1:
+            rb, wr = sharding.gather_die_activity(ctx, local, dies, channels)
+            if marks is not None:
+                marks[2].record(stream)
+            ctx.advance_epoch_global(epoch_ns * 1e-9, rb, wr, stream)
+        else:
+            if marks is not None:
+                marks[2].record(stream)
+            ctx.advance_epoch(epoch_ns * 1e-9, stream)
+
+    def fresh():
+        torch.cuda.synchronize()
+        ctx.flush()
+        ctx.reset_state()
+        configure()
+        torch.cuda.synchronize()
+
+    # self-check on the rank's first epoch: one batch and the same accesses
+    # cut into 7 batches give identical ticks (the range scan carries the
+    # state exactly), and the checksum the run reports
+    fresh()
+    lo, hi = cuts[0], cuts[1]
+    one = ctx.submit(address[lo:hi], nbytes[lo:hi], op[lo:hi], arrival[lo:hi])
+    torch.cuda.synchronize()
+    fresh()
+    edges = [lo + (hi - lo) * j // 7 for j in range(8)]
+    split = [ctx.submit(address[a:b], nbytes[a:b], op[a:b], arrival[a:b])
+             for a, b in zip(edges[:-1], edges[1:])]
+    torch.cuda.synchronize()
+    same = all(torch.equal(torch.cat([getattr(r, f) for r in split]), getattr(one, f))
+               for f in ("done_ns", "latency_ns", "status"))
+    checksum = int((one.done_ns * 3 + one.latency_ns).sum().item()) & ((1 << 64) - 1)
+    modeled0 = int((one.status == 1).sum().item())
+    del one, split
+    # warm-up epochs, then a fresh state and grid
+    fresh()
+    for k in range(3):
+        epoch(k)
+    fresh()
+    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(epochs)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for k in range(epochs):
+        epoch(k, marks[k])
+    ctx.flush()  # waits for the stream; the counters are final
+    st = ctx.batch_stats()
+    totals = torch.tensor([st["modeled"], st["bypass"], st["unsupported"], st["foreign"]],
+                          dtype=torch.int64, device=device)
+    if world > 1:
+        dist.all_reduce(totals)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    phase = {"timing": 0.0, "all_gather": 0.0, "thermal": 0.0}
+    for k in range(epochs):
+        nxt = marks[k + 1][0] if k + 1 < epochs else e1
+        phase["timing"] += marks[k][0].elapsed_time(marks[k][1])
+        phase["all_gather"] += marks[k][1].elapsed_time(marks[k][2])
+        phase["thermal"] += marks[k][2].elapsed_time(nxt)
+    mine = torch.tensor([ms, phase["timing"], phase["all_gather"], phase["thermal"],
+                         float(n), float(checksum % (1 << 52)), float(same), float(modeled0)],
+                        dtype=torch.float64, device=device)
+    rows = [mine.clone() for _ in range(world)]
+    if world > 1:
+        dist.all_gather(rows, mine)
+    rows = [r.cpu().tolist() for r in rows]
+    ms_max = max(r[0] for r in rows)
+    tot = totals.cpu().tolist()
+    temps = ctx.die_temperatures(channels * dies)
+    _, _, _, levels = ctx.thermal_factors(local, wl.C4_STACKS)
+    ctx.close()
+    del address, nbytes, op, arrival, out
+    torch.cuda.empty_cache()
+    slowest = max(range(world), key=lambda r: rows[r][0])
+    ph = rows[slowest]
+    limiter = max((("timing kernels", ph[1]), ("activity all-gather", ph[2]),
+                   ("grid step and controller", ph[3])), key=lambda x: x[1])[0]
+    return {
+        "workload": "config 4: 2^32 accesses (60 % config-1 MoE expert reads, 40 % config-2 "
+                    "paged-KV reads / appends, interleaved by arrival over 100 ms) on 16 stacks "
+                    "x 16 channels x 8 dies x 4 planes, channels sharded over the ranks; 100 "
+                    "epochs of 1 ms with the die-activity all-gather, replicated 9 x 128 x 128 "
+                    "fp64 grid step and controller per epoch, stats all-reduce at the end",
+        "scaling": "strong", "accesses": gen.n, "epochs": epochs, "ms_total": ms_max,
+        "value": gen.n / (ms_max * 1e-3), "unit": "accesses/s",
+        "local_channels": local,
+        "per_rank": [{"rank": r, "ms": row[0], "accesses": int(row[4]),
+                      "timing_ms": row[1], "all_gather_ms": row[2], "thermal_ms": row[3],
+                      "epoch0_modeled": int(row[7]), "epoch0_checksum": int(row[5]),
+                      "epoch0_split_invariant": bool(row[6])} for r, row in enumerate(rows)],
+        "per_epoch_ms": {"timing": ph[1] / epochs, "all_gather": ph[2] / epochs,
+                         "thermal": ph[3] / epochs},
+        "limiter": limiter,
+        "statuses": {"modeled": tot[0], "bypass": tot[1], "unsupported": tot[2],
+                     "foreign": tot[3]},
+        "final_max_die_temp_k": float(temps.max()),
+        "final_throttle_level_max": int(levels.max()),
+        "generation_s": gen_s,
+    }
 
 
 def emit(args, world, n, ms_max, e2e_rate, same, kernels, launches, dominant, achieved,

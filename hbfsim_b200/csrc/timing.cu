@@ -995,6 +995,11 @@ __device__ __forceinline__ bool try_couple(const i64* col0, const DieRegs<D>& v,
     return true;
 }
 
+// Tiles after which the die columns try to couple to column 0: each of the
+// first 8 (short ranges couple early), then every 8th.  Coupling may be
+// tested at any tile boundary; testing less often only replays more tiles.
+__device__ __forceinline__ bool couple_now(u32 tt) { return tt < 8 || (tt & 7u) == 7u; }
+
 // The column items of one CTA's range aggregate (pass 1 of the direct
 // path): thread tid holds items q = tid and tid + kThreads of the C x (K+1)
 // (r-major) column array.
@@ -1044,9 +1049,10 @@ struct ColumnItems {
 #pragma unroll 4
                 for (u32 k = first; k < last; ++k) reg[it].step(s.sarr[k], s.sinfo[k], ci);
             } else {
-                if (rel32 && item_r[it] == 0 &&
-                    replay_rel32<D, false, false>(reg[it], sd, s.sarr, s.sinfo, first, last,
-                                                  ci, step_max))
+                // unit columns: column 0 and the die columns not yet coupled
+                // (a die column whose channel word is still -inf declines)
+                if (rel32 && replay_rel32<D, false, false>(reg[it], sd, s.sarr, s.sinfo, first,
+                                                           last, ci, step_max))
                     continue;
 #pragma unroll 4
                 for (u32 k = first; k < last; ++k) reg[it].step_unit(s.sinfo[k], ci);
@@ -1134,10 +1140,9 @@ direct_pass_kernel(const PassArgs args)
         load_decode_partition<kModelDie, 1, true, FAST>(A, s, start, nt, activity, st);
         items.replay(s, sd, rel32, A.tp.step_max);
         __syncthreads();
-        // every 8th tile and after the last: snapshot column 0, then let the
-        // die columns try to couple to it (coupling is tested at any tile
-        // boundary; testing less often only replays a few more tiles)
-        if ((tt & 7u) != 7u && tt + 1 < A.tiles_per_cta && start + T < A.n) continue;
+        // at the tiles couple_now picks and after the last: snapshot column 0,
+        // then let the die columns try to couple to it
+        if (!couple_now(tt) && tt + 1 < A.tiles_per_cta && start + T < A.n) continue;
         items.couple(s_col0);
     }
     items.write(agg, s_col0);
@@ -1167,8 +1172,8 @@ direct_pass_kernel(const PassArgs args)
 //     batch to the sequential kernel otherwise), and every admission tick
 //     is 0.
 // Outputs and aggregates are identical to direct_pass_kernel's, and so is
-// every record field pass 2 reads (the step info of an untimed access is 0
-// here).
+// every record field pass 2 reads (the step info of an untimed access is
+// not).
 constexpr u32 kFastTile = 2048;
 constexpr u32 kFastRounds = kFastTile / kThreads;  // rounds of 32 per warp
 
@@ -1251,26 +1256,28 @@ direct_fast_kernel(const PassArgs args)
                 unsorted |= arr < prev;
                 const u32 b = s.bytes[e];
                 const u32 o = s.op[e];
+                // classify_single, without branches: zero bytes
+                // (hbf_device.cu:997-1003), then the range (below it:
+                // unsupported if the access straddles into it, else bypass),
+                // the operation, the range end and the page (one page only;
+                // the host admits this kernel for pages up to 2^31 bytes)
                 const u64 off = a - rg.base;  // wraps when a < base
-                if (b == 0) {                 // hbf_device.cu:997-1003
-                } else if (off >= rg.length) {
-                    // below the range: unsupported if it straddles into it
-                    status = a < rg.base && a <= ~u64{0} - b && rg.base < a + b ? kUnsupported
-                                                                                 : kBypass;
-                } else if (o <= 1 && ((rg.allowed >> o) & 1u) && b <= rg.length - off &&
-                           (off & rg.page_mask) + b <= rg.page_mask + 1) {
-                    const u32 u = static_cast<u32>((rg.file_offset + off) >> A.dp.stripe_shift);
-                    const u32 g = (u >> A.dp.chan_shift) & A.dp.chan_mask;
-                    if ((g & A.dp.shard_mask) == A.dp.shard_rank) {
-                        status = kModeled;
-                        key = g >> A.dp.shard_shift;
-                        const u32 xs = A.tp.x_shift;
-                        info = ((b + ((1u << xs) - 1u)) >> xs) * A.tp.time_scale |
-                               ((u >> A.dp.die_shift) & A.dp.die_mask) << 24 | (o & 1u) << 28;
-                    } else {
-                        status = kForeign;
-                    }
-                }
+                const bool in = off < rg.length;
+                const u64 rem = rg.length - off;
+                const u32 pm = static_cast<u32>(rg.page_mask);
+                const bool ok = in & (b != 0u) & (o <= 1u) & (((rg.allowed >> (o & 1u)) & 1u) != 0u) &
+                                (static_cast<u64>(b) <= rem) &
+                                (b <= pm + 1u - (static_cast<u32>(off) & pm));
+                const bool straddles = (a < rg.base) & (a <= ~u64{0} - b) & (rg.base < a + b);
+                const u32 u = static_cast<u32>((rg.file_offset + off) >> A.dp.stripe_shift);
+                const u32 g = (u >> A.dp.chan_shift) & A.dp.chan_mask;
+                const bool mine = (g & A.dp.shard_mask) == A.dp.shard_rank;
+                status = ok ? (mine ? kModeled : kForeign)
+                            : (in | (b == 0u) | straddles ? kUnsupported : kBypass);
+                key = ok & mine ? g >> A.dp.shard_shift : C;
+                const u32 xs = A.tp.x_shift;
+                info = ((b + ((1u << xs) - 1u)) >> xs) * A.tp.time_scale |
+                       ((u >> A.dp.die_shift) & A.dp.die_mask) << 24 | (o & 1u) << 28;
             }
             const u32 peers = __match_any_sync(0xffffffffu, key);
             const u32 before = __popc(peers & lanes_below);
@@ -1345,7 +1352,7 @@ direct_fast_kernel(const PassArgs args)
         if (tt + 1 < A.tiles_per_cta && next < A.n) stage(next, tile_size(next));
         items.replay(s, sd, rel32, A.tp.step_max);
         __syncthreads();
-        if ((tt & 7u) != 7u && tt + 1 < A.tiles_per_cta && start + T < A.n) continue;
+        if (!couple_now(tt) && tt + 1 < A.tiles_per_cta && start + T < A.n) continue;
         items.couple(s_col0);
     }
     items.write(agg, s_col0);
@@ -2039,7 +2046,8 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
             // transfer shift, no activity counting
             const bool f = dp.one.valid && dp.pow2 && tp.x_shift != kXDivide && !tp.act_stage &&
                            tp.admit_zero;
-            const bool f2 = f && plan.T == kFastTile;  // direct_fast_kernel's fixed tile
+            // direct_fast_kernel: its fixed tile, pages up to 2^31 bytes
+            const bool f2 = f && plan.T == kFastTile && dp.one.page_mask < 0x80000000ull;
             fast_p1 = f2;
             const bool z = tp.admit_zero != 0;
             switch (plan.dies) {

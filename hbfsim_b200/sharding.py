@@ -62,28 +62,42 @@ def global_die_index(world: int, local_channels: int, dies: int, channels_total:
     return idx
 
 
+_INDEX_CACHE: dict = {}
+
+
+def _device_index(world: int, local_channels: int, dies: int, channels_total: int, device):
+    """global_die_index as a device tensor, built once per shape."""
+    import torch
+    key = (world, local_channels, dies, channels_total, str(device))
+    idx = _INDEX_CACHE.get(key)
+    if idx is None:
+        idx = torch.from_numpy(global_die_index(world, local_channels, dies,
+                                                channels_total)).to(device)
+        _INDEX_CACHE[key] = idx
+    return idx
+
+
 def gather_die_activity(ctx, local_channels: int, dies: int, channels_total: int,
                         group=None):
     """Device tensors (read bytes, writes) of every global die, from each
-    rank's activity since the last epoch (NCCL all-gather on GPU ranks).
+    rank's activity since the last epoch: one all-gather (NCCL on GPU ranks)
+    of the rank's [read bytes | writes] packed in one buffer, then one
+    gather into global die order with an index kept on the device.
     Everything runs on torch's current stream, after the batches submitted
     on it."""
     import torch
     import torch.distributed as dist
     world = dist.get_world_size(group)
     n = local_channels * dies
-    rb = torch.empty(n, dtype=torch.int64, device="cuda")
-    wr = torch.empty(n, dtype=torch.int64, device="cuda")
-    ctx.copy_die_activity(rb, wr, torch.cuda.current_stream())
-    gathered = []
-    for t in (rb, wr):
-        parts = [torch.empty_like(t) for _ in range(world)]
-        dist.all_gather(parts, t, group=group)
-        flat = torch.cat(parts)
-        idx = torch.from_numpy(global_die_index(world, local_channels, dies,
-                                                channels_total)).to(flat.device)
-        gathered.append(flat.index_select(0, idx).contiguous())
-    return gathered[0], gathered[1]
+    packed = torch.empty(2 * n, dtype=torch.int64, device="cuda")
+    ctx.copy_die_activity(packed[:n], packed[n:], torch.cuda.current_stream())
+    flat = torch.empty(world * 2 * n, dtype=torch.int64, device="cuda")
+    dist.all_gather_into_tensor(flat, packed, group=group)
+    idx = _device_index(world, local_channels, dies, channels_total, flat.device)
+    by_rank = flat.view(world, 2, n)
+    rb = by_rank[:, 0, :].reshape(-1).index_select(0, idx)
+    wr = by_rank[:, 1, :].reshape(-1).index_select(0, idx)
+    return rb, wr
 
 
 def advance_epoch_sharded(ctx, epoch_s: float, local_channels: int, dies: int,

@@ -194,14 +194,15 @@ def c0_trace(n: int = 1 << 20, seed: int = 0, range_length: int = 64 * GIB,
 C3_EPOCHS, C3_EPOCH_NS = 100, 1_000_000
 
 
-def c3_thermal(stacks: int = 1, channels: int = 16, dies: int = 4):
+def c3_thermal(stacks: int = 1, channels: int = 16, dies: int = 4, cell_m: float = 100e-6):
     """Grid description, floorplan (die -> cell box), power, refresh and
     throttle laws of config 3.  Channels form a square array of cell tiles;
     die d of a channel heats NAND layers 1 + 2d and 2 + 2d (4 dies) -- with
-    8 dies, layer 1 + d."""
+    8 dies, layer 1 + d.  `cell_m` is the cell pitch (100 um: one stack on a
+    12.8 mm square)."""
     silicon = {"cv_j_m3_k": 1.66e6, "k_xyz_w_m_k": [148.0, 148.0, 148.0]}
     nand = {"cv_j_m3_k": 1.75e6, "k_xyz_w_m_k": [110.0, 110.0, 35.0]}
-    grid = {"nx": 128, "ny": 128, "cell_m": 100e-6,
+    grid = {"nx": 128, "ny": 128, "cell_m": cell_m,
             "layers": [dict(silicon, thickness_m=100e-6)] +
                       [dict(nand, thickness_m=50e-6) for _ in range(8)],
             "bottom": {"h_w_m2_k": 0.0, "ambient_k": 318.15},
@@ -359,3 +360,120 @@ def _c2_step_torch(lengths, step, steps_total, layers, base, device):
     address = base + page * C2_PAGE
     op = (k == 0).to(torch.uint8)
     return address, torch.full((n,), C2_PAGE, dtype=torch.int32, device=device), op
+
+
+# ---------------------------------------------------------------------------
+# c4: 2^32 accesses on 16 stacks x 16 channels x 8 dies x 4 planes; 60 % the
+# MoE weight-streaming pattern (config 1's expert reads), 40 % the paged-KV
+# pattern (config 2's page reads and appends, here plain timed accesses of a
+# second range), interleaved by arrival.  Global access i is a MoE access
+# when i % 5 < 3 and a KV access otherwise, each stream consumed in its own
+# order; arrival(i) = floor(i * span / 2^32): the whole trace covers `span`
+# ns of simulated time (100 epochs of 1 ms, as config 3), about 43 accesses
+# per ns.  Channels are sharded across ranks (channel g on rank g % world),
+# and each rank keeps only its accesses: generation is replicated, no trace
+# record crosses between GPUs.
+C4_N = 1 << 32
+C4_STACKS = 16
+C4_SPAN_NS = C3_EPOCHS * C3_EPOCH_NS
+C4_MOE_LENGTH = 60 * GIB
+C4_KV_BASE = RANGE_BASE + 64 * GIB
+
+
+def c4_kv_length(lengths, steps_total: int) -> int:
+    """Bytes of the KV range: every (layer, sequence) region holds its
+    tokens plus the ones the run appends."""
+    room = int(np.asarray(lengths, np.int64).sum()) + len(lengths) * steps_total
+    return room * C2_LAYERS * C2_PAGE
+
+
+class C4Trace:
+    """Device-side generator of the config-4 trace, filtered to one rank's
+    channels.  `channel_of(address)` must give the global channel of an
+    address (the context's decode); `keep(channel)` selects the rank's."""
+
+    def __init__(self, device, seed: int = 0, n: int = C4_N, span_ns: int = C4_SPAN_NS):
+        self.device = device
+        self.n = n
+        self.span = span_ns
+        self.n_moe = 3 * (n // 5) + min(3, n % 5)
+        self.n_kv = n - self.n_moe
+        # MoE: config-1 expert segments (attention weights left out: they
+        # live in HBM), enough decode steps for the MoE share
+        per_step = 48 * 77 * (EXPERT_BYTES // READ_BYTES)
+        steps = self.n_moe // per_step + 2
+        bases, counts = c1_segments(seed=seed, steps=steps)
+        expert = bases >= RANGE_BASE
+        self.moe_bases, self.moe_counts = bases[expert], counts[expert]
+        while int(self.moe_counts.sum()) < self.n_moe:  # Zipf unions vary: top up
+            b, c = c1_segments(seed=seed + 1000 + steps, steps=4)
+            e = b >= RANGE_BASE
+            self.moe_bases = np.concatenate([self.moe_bases, b[e]])
+            self.moe_counts = np.concatenate([self.moe_counts, c[e]])
+            steps += 4
+        # KV: config-2 decode steps until the KV share is covered
+        self.lengths = c2_lengths(seed)
+        per = C2_LAYERS * (int(self.lengths.sum()) + 2 * C2_SEQS)
+        self.kv_steps = self.n_kv // per + 2
+        self.kv_length = c4_kv_length(self.lengths, self.kv_steps)
+
+    def _moe(self):
+        """MoE accesses in order, as (address, count) tensors per group of
+        segments."""
+        import torch
+        seg = 0
+        group = 4096
+        while seg < len(self.moe_bases):
+            b, c = self.moe_bases[seg:seg + group], self.moe_counts[seg:seg + group]
+            address, _, _, _ = expand_segments(b, c, device=self.device)
+            yield address, torch.full_like(address, READ_BYTES, dtype=torch.int32), \
+                torch.zeros_like(address, dtype=torch.uint8)
+            seg += group
+
+    def _kv(self):
+        for step in range(self.kv_steps):
+            yield c2_step(self.lengths, step, self.kv_steps, base=C4_KV_BASE,
+                          device=self.device)
+
+    def chunks(self, channel_of, keep, m: int = 1 << 22):
+        """Yields the rank's accesses (address, bytes, op, arrival) of
+        consecutive blocks of 5*m global indices."""
+        import torch
+        streams = {"moe": self._moe(), "kv": self._kv()}
+        bufs = {"moe": [], "kv": []}
+        have = {"moe": 0, "kv": 0}
+
+        def take(name, count):
+            while have[name] < count:
+                parts = next(streams[name])
+                bufs[name].append(parts)
+                have[name] += parts[0].numel()
+            cat = [torch.cat([p[k] for p in bufs[name]]) for k in range(3)]
+            out = [t[:count] for t in cat]
+            rest = [t[count:] for t in cat]
+            bufs[name] = [rest] if rest[0].numel() else []
+            have[name] -= count
+            return out
+
+        i0 = 0
+        while i0 < self.n:
+            blocks = min(m, (self.n - i0) // 5)
+            if blocks == 0:  # the tail: fewer than 5 accesses, MoE first
+                tail = self.n - i0
+                a, b, o = take("moe", min(3, tail))
+                if tail > 3:
+                    ka, kb, ko = take("kv", tail - 3)
+                    a, b, o = torch.cat([a, ka]), torch.cat([b, kb]), torch.cat([o, ko])
+                count = a.numel()
+            else:
+                ma, mb, mo = take("moe", 3 * blocks)
+                ka, kb, ko = take("kv", 2 * blocks)
+                a = torch.cat([ma.view(blocks, 3), ka.view(blocks, 2)], 1).view(-1)
+                b = torch.cat([mb.view(blocks, 3), kb.view(blocks, 2)], 1).view(-1)
+                o = torch.cat([mo.view(blocks, 3), ko.view(blocks, 2)], 1).view(-1)
+                count = 5 * blocks
+            idx = torch.arange(i0, i0 + count, dtype=torch.int64, device=self.device)
+            arrival = idx * self.span // self.n
+            mine = keep(channel_of(a))
+            yield a[mine], b[mine], o[mine], arrival[mine]
+            i0 += count
