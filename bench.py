@@ -915,19 +915,26 @@ def run_c4(args, device, tmp, rank: int, world: int):
     """Config 4, strong scaling of one fixed trace: 2^32 accesses (60 % the
     config-1 MoE expert reads, 40 % the config-2 paged-KV reads and
     appends, interleaved by arrival over 100 ms) on 16 stacks x 16 channels
-    x 8 dies x 4 planes, channels sharded across the ranks (channel g on rank
-    g % world).  Each rank generates the trace on its GPU and keeps its own
-    accesses (untimed).  Timed: 100 epochs of 1 ms, each one batch of the
-    rank's accesses through the per-die model, then -- on every rank -- an
-    NCCL all-gather of every die's activity (one packed buffer), the
-    replicated 9 x 128 x 128 fp64 grid step and the controller deriving the
-    rank's refresh / throttle factors for the next epoch; after the last
-    epoch an all-reduce of the statistics.  `value` = 2^32 / the slowest
-    rank's device time.  The outputs of each epoch land in one buffer per
-    rank, reused by the next epoch (the statistics consume them)."""
+    x 8 dies x 4 planes.  The 256 channels form 8 shards of 32 (channel g in
+    shard g % 8), each one context; GPU r of N holds the shards s with
+    s % N == r (8 / N of them), so every shard runs the direct kernels
+    (32 channels x 10 columns fit their 512 column items) at every N.  Each
+    GPU generates the trace on the device and keeps its shards' accesses
+    (untimed).  Timed: 100 epochs of 1 ms, each one batch per shard through
+    the per-die model, then one NCCL all-gather of every die's activity
+    (one packed buffer per GPU), and per shard the replicated 9 x 128 x 128
+    fp64 grid step and the controller deriving that shard's refresh /
+    throttle factors for the next epoch; after the last epoch an all-reduce
+    of the statistics.  `value` = 2^32 / the slowest GPU's device time.
+    Each shard's epoch outputs land in one buffer reused by the next epoch
+    (the statistics consume them)."""
     import torch
     import torch.distributed as dist
-    from hbfsim_b200 import BatchResult, Context, sharding, workloads as wl
+    from hbfsim_b200 import BatchResult, Context, workloads as wl
+    shards = wl.C4_SHARDS
+    if shards % world:
+        return {"error": f"{world} GPUs do not divide the {shards} channel shards"}
+    mine = [rank + world * k for k in range(shards // world)]
     t0 = time.perf_counter()
     gen = wl.C4Trace(device)
     p = wl.c4_profile()
@@ -936,112 +943,151 @@ def run_c4(args, device, tmp, rank: int, world: int):
             p["pages_per_block"])
     p["capacity_bytes"] = -(-(wl.C4_MOE_LENGTH + gen.kv_length) // unit) * unit
     w = wl.Workload("c4", p, wl.C4_STACKS, STRIPE, wl.RANGE_BASE, wl.C4_MOE_LENGTH)
-    ctx = Context(w.write_profile(tmp), report_dir=f"{tmp}/report-c4", mode=3)
-    ctx.set_geometry(wl.C4_STACKS, STRIPE, rank, world)
-    ctx.register_device(wl.RANGE_BASE, wl.C4_MOE_LENGTH, 1, 1)   # weights: read
-    ctx.register_device(wl.C4_KV_BASE, gen.kv_length, 1, 3)      # KV: read / append
+    path = w.write_profile(tmp)
     channels, dies = wl.C4_STACKS * p["channels"], p["dies_per_channel"]
-    local = -(-channels // world)
+    local = channels // shards
     grid, fp, power, refresh, throttle = wl.c3_thermal(wl.C4_STACKS, p["channels"], dies,
                                                        cell_m=400e-6)
+    ctxs = []
+    for s in mine:
+        ctx = Context(path, report_dir=f"{tmp}/report-c4-{s}", mode=3)
+        ctx.set_geometry(wl.C4_STACKS, STRIPE, s, shards)
+        ctx.register_device(wl.RANGE_BASE, wl.C4_MOE_LENGTH, 1, 1)   # weights: read
+        ctx.register_device(wl.C4_KV_BASE, gen.kv_length, 1, 3)      # KV: read / append
+        ctxs.append(ctx)
 
     def configure():
-        ctx.thermal_configure(grid, fp, power, refresh, throttle)
-    configure()
+        for ctx in ctxs:
+            ctx.thermal_configure(grid, fp, power, refresh, throttle)
 
-    def channel_of(a):  # the context's decode: 4 KiB stripes, channel digit fastest
+    def channel_of(a):  # the contexts' decode: 4 KiB stripes, channel digit fastest
         kv = a >= wl.C4_KV_BASE
         media = torch.where(kv, a - wl.C4_KV_BASE + wl.C4_MOE_LENGTH, a - wl.RANGE_BASE)
         return (media >> 12) % channels
 
-    cap = gen.n if world == 1 else gen.n // world + gen.n // (50 * world) + (1 << 22)
-    address = torch.empty(cap, dtype=torch.int64, device=device)
-    nbytes = torch.empty(cap, dtype=torch.int32, device=device)
-    op = torch.empty(cap, dtype=torch.uint8, device=device)
-    arrival = torch.empty(cap, dtype=torch.int64, device=device)
-    n = 0
-    for a, b, o, t in gen.chunks(channel_of, lambda g: g % world == rank):
-        k = a.numel()
-        if n + k > cap:
-            raise RuntimeError("config-4 shard exceeds its buffer")
-        address[n:n + k], nbytes[n:n + k], op[n:n + k], arrival[n:n + k] = a, b, o, t
-        n += k
-    address, nbytes, op, arrival = address[:n], nbytes[:n], op[:n], arrival[:n]
+    cap = gen.n // shards + gen.n // (50 * shards) + (1 << 22)
+    bufs = [[torch.empty(cap, dtype=dt, device=device)
+             for dt in (torch.int64, torch.int32, torch.uint8, torch.int64)] for _ in mine]
+    fill = [0] * len(mine)
+    for a, b, o, t in gen.chunks(channel_of, lambda g: (g % shards) % world == rank):
+        shard = channel_of(a) % shards
+        for k, s in enumerate(mine):
+            sel = shard == s
+            part = (a[sel], b[sel], o[sel], t[sel])
+            m = part[0].numel()
+            if fill[k] + m > cap:
+                raise RuntimeError("config-4 shard exceeds its buffer")
+            for buf, x in zip(bufs[k], part):
+                buf[fill[k]:fill[k] + m] = x
+            fill[k] += m
+    data = [[buf[:fill[k]] for buf in bufs[k]] for k in range(len(mine))]
+    del bufs
     epochs, epoch_ns = wl.C3_EPOCHS, wl.C3_EPOCH_NS
-    cuts = torch.searchsorted(arrival, torch.arange(epochs + 1, device=device,
-                                                    dtype=torch.int64) * epoch_ns).cpu().tolist()
-    cuts[-1] = n
-    biggest = max(cuts[k + 1] - cuts[k] for k in range(epochs))
+    edges = torch.arange(epochs + 1, device=device, dtype=torch.int64) * epoch_ns
+    cuts = []
+    for k in range(len(mine)):
+        c = torch.searchsorted(data[k][3], edges).cpu().tolist()
+        c[-1] = fill[k]
+        cuts.append(c)
+    biggest = max(c[e + 1] - c[e] for c in cuts for e in range(epochs))
     out = BatchResult(torch.empty(biggest, dtype=torch.int64, device=device),
                       torch.empty(biggest, dtype=torch.int64, device=device),
                       torch.empty(biggest, dtype=torch.uint8, device=device))
+    n = sum(fill)
     torch.cuda.synchronize()
     gen_s = time.perf_counter() - t0
-    log(f"[rank {rank}] config 4: {n} of {gen.n} accesses on {local} local channels, "
-        f"generated in {gen_s:.1f} s")
+    log(f"[rank {rank}] config 4: {n} of {gen.n} accesses in {len(mine)} shards of {local} "
+        f"channels, generated in {gen_s:.1f} s")
     stream = torch.cuda.current_stream()
+    per = local * dies                     # dies of one shard
+    packed = torch.empty(len(mine) * 2 * per, dtype=torch.int64, device=device)
+    flat = torch.empty(world * packed.numel(), dtype=torch.int64, device=device)
+    # global die g*D + d -> its slot in the gathered buffer [gpu][shard][rb|wr][c*D + d]
+    g_idx = np.arange(channels * dies) // dies
+    d_idx = np.arange(channels * dies) % dies
+    s_idx = g_idx % shards
+    slot = (((s_idx % world) * (shards // world) + s_idx // world) * 2 * per +
+            (g_idx // shards) * dies + d_idx)
+    rb_index = torch.from_numpy(slot.astype(np.int64)).to(device)
+    wr_index = rb_index + per
 
-    def epoch(k, marks=None):
-        lo, hi = cuts[k], cuts[k + 1]
+    def epoch(e, marks=None):
         if marks is not None:
             marks[0].record(stream)
-        if hi > lo:
-            part = BatchResult(out.done_ns[:hi - lo], out.latency_ns[:hi - lo],
-                               out.status[:hi - lo])
-            ctx.submit(address[lo:hi], nbytes[lo:hi], op[lo:hi], arrival[lo:hi], part, stream)
+        for k, ctx in enumerate(ctxs):
+            lo, hi = cuts[k][e], cuts[k][e + 1]
+            if hi > lo:
+                d = data[k]
+                part = BatchResult(out.done_ns[:hi - lo], out.latency_ns[:hi - lo],
+                                   out.status[:hi - lo])
+                ctx.submit(d[0][lo:hi], d[1][lo:hi], d[2][lo:hi], d[3][lo:hi], part, stream)
         if marks is not None:
             marks[1].record(stream)
+        for k, ctx in enumerate(ctxs):
+            base = k * 2 * per
+            ctx.copy_die_activity(packed[base:base + per], packed[base + per:base + 2 * per],
+                                  stream)
         if world > 1:
-            rb, wr = sharding.gather_die_activity(ctx, local, dies, channels)
-            if marks is not None:
-                marks[2].record(stream)
-            ctx.advance_epoch_global(epoch_ns * 1e-9, rb, wr, stream)
+            dist.all_gather_into_tensor(flat, packed)
+            src = flat
         else:
-            if marks is not None:
-                marks[2].record(stream)
-            ctx.advance_epoch(epoch_ns * 1e-9, stream)
+            src = packed
+        rb, wr = src.index_select(0, rb_index), src.index_select(0, wr_index)
+        if marks is not None:
+            marks[2].record(stream)
+        for ctx in ctxs:
+            ctx.advance_epoch_global(epoch_ns * 1e-9, rb, wr, stream)
 
     def fresh():
         torch.cuda.synchronize()
-        ctx.flush()
-        ctx.reset_state()
+        for ctx in ctxs:
+            ctx.flush()
+            ctx.reset_state()
         configure()
         torch.cuda.synchronize()
 
-    # self-check on the rank's first epoch: one batch and the same accesses
+    # self-check on each shard's first epoch: one batch and the same accesses
     # cut into 7 batches give identical ticks (the range scan carries the
-    # state exactly), and the checksum the run reports
+    # state exactly); and a checksum of the epoch's ticks
     fresh()
-    lo, hi = cuts[0], cuts[1]
-    one = ctx.submit(address[lo:hi], nbytes[lo:hi], op[lo:hi], arrival[lo:hi])
-    torch.cuda.synchronize()
-    fresh()
-    edges = [lo + (hi - lo) * j // 7 for j in range(8)]
-    split = [ctx.submit(address[a:b], nbytes[a:b], op[a:b], arrival[a:b])
-             for a, b in zip(edges[:-1], edges[1:])]
-    torch.cuda.synchronize()
-    same = all(torch.equal(torch.cat([getattr(r, f) for r in split]), getattr(one, f))
-               for f in ("done_ns", "latency_ns", "status"))
-    checksum = int((one.done_ns * 3 + one.latency_ns).sum().item()) & ((1 << 64) - 1)
-    modeled0 = int((one.status == 1).sum().item())
-    del one, split
+    same, checksum, modeled0 = True, 0, 0
+    for k, ctx in enumerate(ctxs):
+        d = data[k]
+        lo, hi = cuts[k][0], cuts[k][1]
+        one = ctx.submit(d[0][lo:hi], d[1][lo:hi], d[2][lo:hi], d[3][lo:hi])
+        torch.cuda.synchronize()
+        ctx.reset_state()
+        cut7 = [lo + (hi - lo) * j // 7 for j in range(8)]
+        split = [ctx.submit(d[0][x:y], d[1][x:y], d[2][x:y], d[3][x:y])
+                 for x, y in zip(cut7[:-1], cut7[1:])]
+        torch.cuda.synchronize()
+        same &= all(torch.equal(torch.cat([getattr(r, f) for r in split]), getattr(one, f))
+                    for f in ("done_ns", "latency_ns", "status"))
+        checksum = (checksum + int((one.done_ns * 3 + one.latency_ns).sum().item())) % (1 << 52)
+        modeled0 += int((one.status == 1).sum().item())
+        del one, split
     # warm-up epochs, then a fresh state and grid
     fresh()
-    for k in range(3):
-        epoch(k)
+    for e in range(3):
+        epoch(e)
     fresh()
+
+    def stats_now():
+        tot = np.zeros(4, np.int64)
+        for ctx in ctxs:
+            st = ctx.batch_stats()
+            tot += [st["modeled"], st["bypass"], st["unsupported"], st["foreign"]]
+        return tot
+    before = stats_now()
     marks = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(epochs)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     e0.record(stream)
-    for k in range(epochs):
-        epoch(k, marks[k])
-    ctx.flush()  # waits for the stream; the counters are final
-    st = ctx.batch_stats()
-    totals = torch.tensor([st["modeled"], st["bypass"], st["unsupported"], st["foreign"]],
-                          dtype=torch.int64, device=device)
+    for e in range(epochs):
+        epoch(e, marks[e])
+    totals = torch.from_numpy(stats_now() - before).to(device)  # waits for the stream
     if world > 1:
         dist.all_reduce(totals)
     e1.record(stream)
@@ -1050,42 +1096,44 @@ def run_c4(args, device, tmp, rank: int, world: int):
         dist.barrier()
     ms = e0.elapsed_time(e1)
     phase = {"timing": 0.0, "all_gather": 0.0, "thermal": 0.0}
-    for k in range(epochs):
-        nxt = marks[k + 1][0] if k + 1 < epochs else e1
-        phase["timing"] += marks[k][0].elapsed_time(marks[k][1])
-        phase["all_gather"] += marks[k][1].elapsed_time(marks[k][2])
-        phase["thermal"] += marks[k][2].elapsed_time(nxt)
-    mine = torch.tensor([ms, phase["timing"], phase["all_gather"], phase["thermal"],
-                         float(n), float(checksum % (1 << 52)), float(same), float(modeled0)],
-                        dtype=torch.float64, device=device)
-    rows = [mine.clone() for _ in range(world)]
+    for e in range(epochs):
+        nxt = marks[e + 1][0] if e + 1 < epochs else e1
+        phase["timing"] += marks[e][0].elapsed_time(marks[e][1])
+        phase["all_gather"] += marks[e][1].elapsed_time(marks[e][2])
+        phase["thermal"] += marks[e][2].elapsed_time(nxt)
+    row = torch.tensor([ms, phase["timing"], phase["all_gather"], phase["thermal"], float(n),
+                        float(checksum), float(same), float(modeled0)],
+                       dtype=torch.float64, device=device)
+    rows = [row.clone() for _ in range(world)]
     if world > 1:
-        dist.all_gather(rows, mine)
+        dist.all_gather(rows, row)
     rows = [r.cpu().tolist() for r in rows]
     ms_max = max(r[0] for r in rows)
     tot = totals.cpu().tolist()
-    temps = ctx.die_temperatures(channels * dies)
-    _, _, _, levels = ctx.thermal_factors(local, wl.C4_STACKS)
-    ctx.close()
-    del address, nbytes, op, arrival, out
+    temps = ctxs[0].die_temperatures(channels * dies)
+    levels = ctxs[0].thermal_factors(local, wl.C4_STACKS)[3]
+    for ctx in ctxs:
+        ctx.close()
+    del data, out
     torch.cuda.empty_cache()
     slowest = max(range(world), key=lambda r: rows[r][0])
     ph = rows[slowest]
     limiter = max((("timing kernels", ph[1]), ("activity all-gather", ph[2]),
-                   ("grid step and controller", ph[3])), key=lambda x: x[1])[0]
+                   ("replicated grid steps and controllers", ph[3])), key=lambda x: x[1])[0]
     return {
         "workload": "config 4: 2^32 accesses (60 % config-1 MoE expert reads, 40 % config-2 "
                     "paged-KV reads / appends, interleaved by arrival over 100 ms) on 16 stacks "
-                    "x 16 channels x 8 dies x 4 planes, channels sharded over the ranks; 100 "
-                    "epochs of 1 ms with the die-activity all-gather, replicated 9 x 128 x 128 "
-                    "fp64 grid step and controller per epoch, stats all-reduce at the end",
+                    "x 16 channels x 8 dies x 4 planes in 8 channel shards over the GPUs; 100 "
+                    "epochs of 1 ms with one die-activity all-gather, and per shard the "
+                    "replicated 9 x 128 x 128 fp64 grid step and controller; stats all-reduce "
+                    "at the end",
         "scaling": "strong", "accesses": gen.n, "epochs": epochs, "ms_total": ms_max,
         "value": gen.n / (ms_max * 1e-3), "unit": "accesses/s",
-        "local_channels": local,
-        "per_rank": [{"rank": r, "ms": row[0], "accesses": int(row[4]),
-                      "timing_ms": row[1], "all_gather_ms": row[2], "thermal_ms": row[3],
-                      "epoch0_modeled": int(row[7]), "epoch0_checksum": int(row[5]),
-                      "epoch0_split_invariant": bool(row[6])} for r, row in enumerate(rows)],
+        "shards_per_gpu": len(mine), "channels_per_shard": local,
+        "per_gpu": [{"rank": r, "ms": x[0], "accesses": int(x[4]), "timing_ms": x[1],
+                     "all_gather_ms": x[2], "thermal_ms": x[3], "epoch0_modeled": int(x[7]),
+                     "epoch0_checksum": int(x[5]), "epoch0_split_invariant": bool(x[6])}
+                    for r, x in enumerate(rows)],
         "per_epoch_ms": {"timing": ph[1] / epochs, "all_gather": ph[2] / epochs,
                          "thermal": ph[3] / epochs},
         "limiter": limiter,

@@ -203,12 +203,22 @@ class Context:
         return out
 
     # ---- Capacity mode ----
-    def capacity_configure(self, frames: int, page_bytes: int = 4096) -> None:
+    def capacity_configure(self, frames: int, page_bytes: int = 4096,
+                           policy: str = "lru") -> None:
+        """Capacity mode over `frames` HBM frames of `page_bytes` pages.
+        policy "lru": exact LRU (the offline LruCache); "clock": the
+        reference runtime's second-chance CLOCK (HbmCache)."""
         check(self._lib.hbfsim_capacity_configure_v1(self.handle, frames, page_bytes),
               "hbfsim_capacity_configure_v1")
+        codes = {"lru": 0, "clock": 1}
+        if policy not in codes:
+            raise ValueError(f"unknown capacity policy {policy!r}")
+        if codes[policy]:
+            check(self._lib.hbfsim_capacity_policy_v1(self.handle, codes[policy]),
+                  "hbfsim_capacity_policy_v1")
 
     def submit_capacity(self, address, nbytes, op, arrival=None, stream=None, timed=False):
-        """Exact-LRU decisions for device tensors: (hit u8, victim page
+        """Replacement decisions (the configured policy) for device tensors: (hit u8, victim page
         int64 (-1 = none), victim dirty u8, status u8) device tensors; with
         timed=True also (done, latency) int64 tensors of the media actions."""
         import torch
@@ -231,8 +241,19 @@ class Context:
             return hit, victim, dirty, status, done, latency
         return hit, victim, dirty, status
 
+    def capacity_stats(self) -> dict:
+        """hbfsim_get_capacity_stats_v1 as a dict (the reference's counter
+        names)."""
+        st = _lib.CapacityStatsV1()
+        st.struct_size = ctypes.sizeof(st)
+        st.version = 1
+        check(self._lib.hbfsim_get_capacity_stats_v1(self.handle, ctypes.byref(st)),
+              "hbfsim_get_capacity_stats_v1")
+        return {f: getattr(st, f) for f, _ in _lib.CapacityStatsV1._fields_}
+
     def capacity_state(self):
-        """(resident pages oldest first, their dirty bits) as numpy arrays."""
+        """(resident pages, their dirty bits) as numpy arrays: oldest first
+        under LRU, in frame order under CLOCK."""
         count = ctypes.c_uint64()
         check(self._lib.hbfsim_get_capacity_state_v1(self.handle, None, None, 0,
                                                      ctypes.byref(count)),

@@ -70,6 +70,15 @@ struct CapacityState {
     u32* chained_pos = nullptr;
     DevRange* media_range = nullptr; // identity range: media address -> itself
     u32* counts = nullptr;           // small device results
+    // CLOCK policy (the reference runtime's HbmCache): per frame its page,
+    // reference and dirty byte; page -> frame table; [hand, frames in use]
+    std::uint32_t policy = 0;        // HBFSIM_CAPACITY_POLICY_*
+    std::uint64_t table_pages = 0;   // entries of clk_table
+    u32* clk_table = nullptr;
+    u32* clk_page = nullptr;
+    u8* clk_ref = nullptr;
+    u8* clk_dirty = nullptr;
+    u64* clk_state = nullptr;
     // counters (host)
     std::uint64_t calls = 0, accesses = 0, hits = 0, misses = 0, evictions = 0,
                   dirty_evictions = 0;
@@ -615,6 +624,185 @@ __global__ void act_result_kernel(const u32* status, const u32* hit, const u32* 
     if (latency) latency[i] = d - a;
 }
 
+// ---------------------------------------------------------------- CLOCK
+// Second-chance CLOCK, the reference runtime's policy: HbmCache
+// (src/cuda_runtime/hbm_cache.cpp) as CapacityPageService::resolve
+// (capacity_page_service.cpp:97-210) drives it, one page reference at a
+// time.  A resident page is a hit: its reference bit is set (resolve,
+// 41-52), and a write sets its dirty bit (mark_dirty, 80-94).  A miss takes
+// the lowest free frame (free_frame, 101-110); once every frame holds a
+// page, begin_eviction_locked (131-175) walks the hand over the frames,
+// clearing set reference bits, and evicts the first frame whose bit is
+// clear, leaving the hand one past it.  publish (21-39) places the new page
+// referenced and clean; a write marks it dirty.
+//
+// The policy is sequential by definition (each eviction depends on every
+// reference bit the earlier accesses left), so one warp walks the batch in
+// order, with its 32 lanes hiding the memory latency:
+//   * the page -> frame lookups of 32 accesses are loaded at once, and each
+//     decision updates the lanes whose page it placed or evicted;
+//   * the lanes hold a window of 32 consecutive frames (reference bit,
+//     page, dirty bit) from the hand on: a hand walk is a ballot over the
+//     window, and a run of misses consumes the window without new loads;
+//   * stores go straight out (the warp reads back only what it wrote after
+//     a __syncwarp).
+struct ClockArgs {
+    const u32* valid;   // per access: 1 = capacity access
+    const u32* page;    // per access: LRU page
+    const u8* op;
+    u64 n;
+    u64 frames;
+    u32* table;         // page -> frame, kNone = not resident
+    u32* fpage;         // frame -> page
+    u8* ref;
+    u8* dirty;
+    u64* state;         // [0] hand, [1] frames in use
+    u32* ahit;          // per access decisions (media-action pass)
+    u32* avictim;
+    u32* adirty;
+    u8* out_hit;
+    u64* out_victim;
+    u8* out_dirty;
+    u32* counters;      // [0] hits, [1] dirty evictions, [2] evictions, [3] error,
+                        // [4] capacity accesses
+};
+
+__global__ void __launch_bounds__(32) clock_kernel(const ClockArgs a)
+{
+    const u32 lane = threadIdx.x;
+    const u64 F = a.frames;
+    u64 hand = a.state[0], used = a.state[1];
+    u32 hits = 0, dirty_ev = 0, evictions = 0, seen = 0;
+    // the window: frames w0 + lane (mod F) for lanes below wn
+    bool window = false;
+    u64 w0 = 0;
+    u32 wn = 0;
+    u32 wref = 0, wpage = 0, wdirty = 0;
+    auto in_window = [&](u64 f, u32& slot) {
+        if (!window) return false;
+        const u64 d = f >= w0 ? f - w0 : f + F - w0;
+        slot = static_cast<u32>(d);
+        return d < wn;
+    };
+    for (u64 i0 = 0; i0 < a.n; i0 += 32) {
+        const u64 i = i0 + lane;
+        const bool live = i < a.n && a.valid[i];
+        const u32 my_page = live ? a.page[i] : kNone;
+        const u32 my_w = live ? a.op[i] : 0u;
+        u32 my_frame = live ? a.table[my_page] : kNone;
+        const u32 count = static_cast<u32>(a.n - i0 < 32 ? a.n - i0 : 32);
+        for (u32 j = 0; j < count; ++j) {
+            const u32 p = __shfl_sync(0xffffffffu, my_page, j);
+            if (p == kNone) continue;  // not a capacity access (uniform)
+            ++seen;
+            const u32 w = __shfl_sync(0xffffffffu, my_w, j);
+            const u32 f = __shfl_sync(0xffffffffu, my_frame, j);
+            const u64 idx = i0 + j;
+            u32 slot;
+            if (f != kNone) {  // hit
+                if (lane == 0) {
+                    a.ref[f] = 1;
+                    if (w) a.dirty[f] = 1;
+                    a.ahit[idx] = 1;
+                    a.avictim[idx] = kNone;
+                    a.adirty[idx] = 0;
+                    if (a.out_hit) a.out_hit[idx] = 1;
+                    if (a.out_victim) a.out_victim[idx] = ~u64{0};
+                    if (a.out_dirty) a.out_dirty[idx] = 0;
+                }
+                if (in_window(f, slot) && lane == slot) {
+                    wref = 1;
+                    if (w) wdirty = 1;
+                }
+                ++hits;
+                continue;
+            }
+            u64 target;
+            u32 victim = kNone, vd = 0;
+            if (used < F) {
+                target = used++;
+            } else {
+                // the hand walk ends within two sweeps (the first clears
+                // every reference bit it passes); the cap only guards it
+                const u64 cap = 2 * (F / 32 + 2);
+                for (u64 step = 0;; ++step) {
+                    u32 at;
+                    if (!in_window(hand, at)) {
+                        __syncwarp();
+                        w0 = hand;
+                        wn = static_cast<u32>(F < 32 ? F : 32);
+                        const u64 fl = (w0 + lane) % F;
+                        wref = lane < wn ? a.ref[fl] : 1u;
+                        wpage = lane < wn ? a.fpage[fl] : kNone;
+                        wdirty = lane < wn ? a.dirty[fl] : 0u;
+                        window = true;
+                        at = 0;
+                    }
+                    const u32 clear = __ballot_sync(0xffffffffu, lane >= at && lane < wn &&
+                                                                     wref == 0);
+                    if (clear) {
+                        const u32 z = __ffs(clear) - 1;
+                        if (lane >= at && lane < z && wref) {  // second chances spent
+                            wref = 0;
+                            a.ref[(w0 + lane) % F] = 0;
+                        }
+                        target = (w0 + z) % F;
+                        victim = __shfl_sync(0xffffffffu, wpage, z);
+                        vd = __shfl_sync(0xffffffffu, wdirty, z);
+                        hand = (target + 1) % F;
+                        break;
+                    }
+                    if (lane >= at && lane < wn && wref) {
+                        wref = 0;
+                        a.ref[(w0 + lane) % F] = 0;
+                    }
+                    hand = (w0 + wn) % F;
+                    window = false;
+                    if (step > cap) {  // cannot happen: record it, take the hand's frame
+                        if (lane == 0) a.counters[3] = 1;
+                        target = hand;
+                        victim = a.fpage[hand];
+                        vd = a.dirty[hand];
+                        hand = (hand + 1) % F;
+                        break;
+                    }
+                }
+                ++evictions;
+                if (vd) ++dirty_ev;
+                if (lane == 0) a.table[victim] = kNone;
+                if (my_page == victim) my_frame = kNone;
+            }
+            if (lane == 0) {
+                a.fpage[target] = p;
+                a.ref[target] = 1;
+                a.dirty[target] = w ? 1 : 0;
+                a.table[p] = static_cast<u32>(target);
+                a.ahit[idx] = 0;
+                a.avictim[idx] = victim;
+                a.adirty[idx] = vd;
+                if (a.out_hit) a.out_hit[idx] = 0;
+                if (a.out_victim) a.out_victim[idx] = victim == kNone ? ~u64{0} : victim;
+                if (a.out_dirty) a.out_dirty[idx] = static_cast<u8>(vd);
+            }
+            if (in_window(target, slot) && lane == slot) {
+                wref = 1;
+                wpage = p;
+                wdirty = w ? 1 : 0;
+            }
+            if (my_page == p) my_frame = static_cast<u32>(target);
+        }
+        __syncwarp();
+    }
+    if (lane == 0) {
+        a.state[0] = hand;
+        a.state[1] = used;
+        a.counters[0] = hits;
+        a.counters[1] = dirty_ev;
+        a.counters[2] = evictions;
+        a.counters[4] = seen;
+    }
+}
+
 inline unsigned blocks(u64 n) { return static_cast<unsigned>((n + kT - 1) / kT); }
 
 }  // namespace
@@ -628,7 +816,8 @@ void capacity_destroy(CapacityState* c)
                     c->apage, c->ahit, c->avictim, c->adirty, c->anact, c->apos,
                     c->act_addr, c->act_bytes, c->act_op, c->act_arr, c->act_chain,
                     c->act_done, c->act_lat, c->act_status, c->chained, c->chained_flag,
-                    c->chained_pos, c->media_range};
+                    c->chained_pos, c->media_range, c->clk_table, c->clk_page, c->clk_ref,
+                    c->clk_dirty, c->clk_state};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     delete c;
@@ -789,9 +978,65 @@ int time_actions(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStr
     return cudaStreamSynchronize(st) == cudaSuccess ? HBFSIM_OK : HBFSIM_CUDA_ERROR;
 }
 
+// CLOCK decisions of one batch (clock_kernel), then the media actions.
+int run_clock(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStream_t st)
+{
+    CapacityState* s = ctx->capacity;
+    const std::uint64_t n = b->count;
+    if (ensure_scratch(s, n) != HBFSIM_OK) return HBFSIM_CUDA_ERROR;
+    u32* cnt = s->counts;
+    cudaMemsetAsync(cnt, 0, 4 * kCapCounts, st);
+    cap_classify_kernel<<<blocks(n), kT, 0, st>>>(ctx->d_ranges,
+                                                   static_cast<u32>(ctx->ranges.size()),
+                                                   b->address, b->bytes, b->operation, n,
+                                                   s->page_shift, s->apage, s->valid, s->status);
+    if (b->status) status_kernel<<<blocks(n), kT, 0, st>>>(s->status, n, b->status);
+    if (b->hit) cudaMemsetAsync(b->hit, 0, n, st);
+    if (b->victim_page) cudaMemsetAsync(b->victim_page, 0xff, 8 * n, st);
+    if (b->victim_dirty) cudaMemsetAsync(b->victim_dirty, 0, n, st);
+    ClockArgs a{};
+    a.valid = s->valid;
+    a.page = s->apage;
+    a.op = b->operation;
+    a.n = n;
+    a.frames = s->frames;
+    a.table = s->clk_table;
+    a.fpage = s->clk_page;
+    a.ref = s->clk_ref;
+    a.dirty = s->clk_dirty;
+    a.state = s->clk_state;
+    a.ahit = s->ahit;
+    a.avictim = s->avictim;
+    a.adirty = s->adirty;
+    a.out_hit = b->hit;
+    a.out_victim = b->victim_page;
+    a.out_dirty = b->victim_dirty;
+    a.counters = cnt;
+    clock_kernel<<<1, 32, 0, st>>>(a);
+    std::uint32_t host_cnt[5] = {0, 0, 0, 0, 0};
+    std::uint64_t used = 0;
+    cudaMemcpyAsync(host_cnt, cnt, sizeof host_cnt, cudaMemcpyDeviceToHost, st);
+    cudaMemcpyAsync(&used, s->clk_state + 1, 8, cudaMemcpyDeviceToHost, st);
+    if (cudaStreamSynchronize(st) != cudaSuccess) return HBFSIM_CUDA_ERROR;
+    if (host_cnt[3]) return HBFSIM_CUDA_ERROR;
+    s->resident = used;
+    if (b->done_ns || b->latency_ns) {
+        const int rc = time_actions(ctx, b, st);
+        if (rc != HBFSIM_OK) return rc;
+    }
+    ++s->calls;
+    s->accesses += host_cnt[4];
+    s->hits += host_cnt[0];
+    s->misses += host_cnt[4] - host_cnt[0];
+    s->dirty_evictions += host_cnt[1];
+    s->evictions += host_cnt[2];
+    return cudaGetLastError() == cudaSuccess ? HBFSIM_OK : HBFSIM_CUDA_ERROR;
+}
+
 int run_capacity(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStream_t st)
 {
     CapacityState* s = ctx->capacity;
+    if (s->policy == HBFSIM_CAPACITY_POLICY_CLOCK) return run_clock(ctx, b, st);
     const std::uint64_t n = b->count;
     const std::uint64_t resident = s->resident;
     if (ensure_scratch(s, resident + n) != HBFSIM_OK) return HBFSIM_CUDA_ERROR;
@@ -969,6 +1214,31 @@ int hbfsim_capacity_configure_v1(hbfsim_context* c, uint64_t frames, uint32_t pa
     return HBFSIM_OK;
 }
 
+int hbfsim_capacity_policy_v1(hbfsim_context* c, uint32_t policy)
+{
+    if (!c) return HBFSIM_INVALID_ARGUMENT;
+    CGuard g(c);
+    CapacityState* s = c->capacity;
+    if (!s || (policy != HBFSIM_CAPACITY_POLICY_LRU && policy != HBFSIM_CAPACITY_POLICY_CLOCK))
+        return HBFSIM_INVALID_ARGUMENT;
+    if (cudaDeviceSynchronize() != cudaSuccess) return HBFSIM_CUDA_ERROR;
+    s->resident = 0;
+    s->policy = policy;
+    if (policy == HBFSIM_CAPACITY_POLICY_LRU) return HBFSIM_OK;
+    if (s->frames == 0) return HBFSIM_INVALID_ARGUMENT;  // the reference cache needs a frame
+    const std::uint64_t pages = (c->profile.capacity_bytes >> s->page_shift) + 1;
+    if (grow(&s->clk_table, pages) || grow(&s->clk_page, s->frames) ||
+        grow(&s->clk_ref, s->frames) || grow(&s->clk_dirty, s->frames) ||
+        grow(&s->clk_state, 2) ||
+        cudaMemset(s->clk_table, 0xff, 4 * pages) != cudaSuccess ||
+        cudaMemset(s->clk_ref, 0, s->frames) != cudaSuccess ||
+        cudaMemset(s->clk_dirty, 0, s->frames) != cudaSuccess ||
+        cudaMemset(s->clk_state, 0, 16) != cudaSuccess)
+        return HBFSIM_CUDA_ERROR;
+    s->table_pages = pages;
+    return HBFSIM_OK;
+}
+
 int hbfsim_submit_capacity_batch_v1(hbfsim_context* c, const hbfsim_capacity_batch_v1* b,
                                     void* stream)
 {
@@ -1000,11 +1270,14 @@ int hbfsim_get_capacity_state_v1(hbfsim_context* c, uint64_t* resident_pages,
     if (!resident_pages && !resident_dirty) return HBFSIM_OK;
     if (count < s->resident) return HBFSIM_INVALID_ARGUMENT;
     std::vector<std::uint32_t> pages(s->resident);
+    const bool clock = s->policy == HBFSIM_CAPACITY_POLICY_CLOCK;
+    const u32* src_page = clock ? s->clk_page : s->res_page;   // CLOCK: frame order
+    const u8* src_dirty = clock ? s->clk_dirty : s->res_dirty;
     if (cudaDeviceSynchronize() != cudaSuccess ||
-        (s->resident && cudaMemcpy(pages.data(), s->res_page, 4 * s->resident,
+        (s->resident && cudaMemcpy(pages.data(), src_page, 4 * s->resident,
                                    cudaMemcpyDeviceToHost) != cudaSuccess) ||
         (resident_dirty && s->resident &&
-         cudaMemcpy(resident_dirty, s->res_dirty, s->resident, cudaMemcpyDeviceToHost) !=
+         cudaMemcpy(resident_dirty, src_dirty, s->resident, cudaMemcpyDeviceToHost) !=
              cudaSuccess))
         return HBFSIM_CUDA_ERROR;
     if (resident_pages)

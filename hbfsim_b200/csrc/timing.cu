@@ -1172,8 +1172,8 @@ direct_pass_kernel(const PassArgs args)
 //     batch to the sequential kernel otherwise), and every admission tick
 //     is 0.
 // Outputs and aggregates are identical to direct_pass_kernel's, and so is
-// every record field pass 2 reads (the step info of an untimed access is
-// not).
+// every record field pass 2 reads (the step info of an untimed access is 0
+// here).
 constexpr u32 kFastTile = 2048;
 constexpr u32 kFastRounds = kFastTile / kThreads;  // rounds of 32 per warp
 
@@ -1256,28 +1256,26 @@ direct_fast_kernel(const PassArgs args)
                 unsorted |= arr < prev;
                 const u32 b = s.bytes[e];
                 const u32 o = s.op[e];
-                // classify_single, without branches: zero bytes
-                // (hbf_device.cu:997-1003), then the range (below it:
-                // unsupported if the access straddles into it, else bypass),
-                // the operation, the range end and the page (one page only;
-                // the host admits this kernel for pages up to 2^31 bytes)
                 const u64 off = a - rg.base;  // wraps when a < base
-                const bool in = off < rg.length;
-                const u64 rem = rg.length - off;
-                const u32 pm = static_cast<u32>(rg.page_mask);
-                const bool ok = in & (b != 0u) & (o <= 1u) & (((rg.allowed >> (o & 1u)) & 1u) != 0u) &
-                                (static_cast<u64>(b) <= rem) &
-                                (b <= pm + 1u - (static_cast<u32>(off) & pm));
-                const bool straddles = (a < rg.base) & (a <= ~u64{0} - b) & (rg.base < a + b);
-                const u32 u = static_cast<u32>((rg.file_offset + off) >> A.dp.stripe_shift);
-                const u32 g = (u >> A.dp.chan_shift) & A.dp.chan_mask;
-                const bool mine = (g & A.dp.shard_mask) == A.dp.shard_rank;
-                status = ok ? (mine ? kModeled : kForeign)
-                            : (in | (b == 0u) | straddles ? kUnsupported : kBypass);
-                key = ok & mine ? g >> A.dp.shard_shift : C;
-                const u32 xs = A.tp.x_shift;
-                info = ((b + ((1u << xs) - 1u)) >> xs) * A.tp.time_scale |
-                       ((u >> A.dp.die_shift) & A.dp.die_mask) << 24 | (o & 1u) << 28;
+                if (b == 0) {                 // hbf_device.cu:997-1003
+                } else if (off >= rg.length) {
+                    // below the range: unsupported if it straddles into it
+                    status = a < rg.base && a <= ~u64{0} - b && rg.base < a + b ? kUnsupported
+                                                                                 : kBypass;
+                } else if (o <= 1 && ((rg.allowed >> o) & 1u) && b <= rg.length - off &&
+                           (off & rg.page_mask) + b <= rg.page_mask + 1) {
+                    const u32 u = static_cast<u32>((rg.file_offset + off) >> A.dp.stripe_shift);
+                    const u32 g = (u >> A.dp.chan_shift) & A.dp.chan_mask;
+                    if ((g & A.dp.shard_mask) == A.dp.shard_rank) {
+                        status = kModeled;
+                        key = g >> A.dp.shard_shift;
+                        const u32 xs = A.tp.x_shift;
+                        info = ((b + ((1u << xs) - 1u)) >> xs) * A.tp.time_scale |
+                               ((u >> A.dp.die_shift) & A.dp.die_mask) << 24 | (o & 1u) << 28;
+                    } else {
+                        status = kForeign;
+                    }
+                }
             }
             const u32 peers = __match_any_sync(0xffffffffu, key);
             const u32 before = __popc(peers & lanes_below);
@@ -2046,8 +2044,7 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
             // transfer shift, no activity counting
             const bool f = dp.one.valid && dp.pow2 && tp.x_shift != kXDivide && !tp.act_stage &&
                            tp.admit_zero;
-            // direct_fast_kernel: its fixed tile, pages up to 2^31 bytes
-            const bool f2 = f && plan.T == kFastTile && dp.one.page_mask < 0x80000000ull;
+            const bool f2 = f && plan.T == kFastTile;  // direct_fast_kernel's fixed tile
             fast_p1 = f2;
             const bool z = tp.admit_zero != 0;
             switch (plan.dies) {

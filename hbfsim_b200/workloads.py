@@ -375,6 +375,7 @@ def _c2_step_torch(lengths, step, steps_total, layers, base, device):
 # record crosses between GPUs.
 C4_N = 1 << 32
 C4_STACKS = 16
+C4_SHARDS = 8      # channel shards (channel g in shard g % 8), spread over the GPUs
 C4_SPAN_NS = C3_EPOCHS * C3_EPOCH_NS
 C4_MOE_LENGTH = 60 * GIB
 C4_KV_BASE = RANGE_BASE + 64 * GIB

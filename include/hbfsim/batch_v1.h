@@ -228,6 +228,22 @@ uint64_t hbfsim_state_words_v1(hbfsim_context* context);
 int hbfsim_capacity_configure_v1(hbfsim_context* context, uint64_t frames,
                                  uint32_t page_bytes);
 
+/* Replacement policy of the capacity path.  LRU (the default after
+ * hbfsim_capacity_configure_v1) is the offline LruCache above, decided for
+ * a whole batch at once.  CLOCK is the reference runtime's second-chance
+ * policy: HbmCache::begin_eviction_locked
+ * (src/cuda_runtime/hbm_cache.cpp:131-175) with the frame walk of
+ * CapacityPageService::resolve (capacity_page_service.cpp:97-210) -- a hit
+ * sets the frame's reference bit, a miss takes the lowest free frame or,
+ * with every frame full, the first frame at or after the hand whose bit is
+ * clear, clearing the set bits it passes.  Switching empties the cache.
+ * With CLOCK, hbfsim_get_capacity_state_v1 lists the resident pages in
+ * frame order.  Returns HBFSIM_INVALID_ARGUMENT before configure, for an
+ * unknown policy, or for CLOCK over zero frames. */
+#define HBFSIM_CAPACITY_POLICY_LRU 0u
+#define HBFSIM_CAPACITY_POLICY_CLOCK 1u
+int hbfsim_capacity_policy_v1(hbfsim_context* context, uint32_t policy);
+
 #define HBFSIM_CAPACITY_BATCH_V1_VERSION 1u
 typedef struct hbfsim_capacity_batch_v1 {
     uint32_t struct_size;

@@ -541,6 +541,115 @@ void or_lru_run(const uint64_t* pages, const uint8_t* writes, uint64_t n,
     free(table); free(key); free(prev); free(next); free(dirty);
 }
 
+/* Capacity mode with the reference runtime's policy: second-chance CLOCK
+ * over `frames` frames, one page reference at a time, as
+ * CapacityPageService::resolve (capacity_page_service.cpp:97-210) drives
+ * HbmCache (hbm_cache.cpp): a resident page is a hit and gets its reference
+ * bit (resolve, 41-52), a write also its dirty bit (mark_dirty, 80-94); a
+ * miss takes the lowest free frame (free_frame, 101-110) or, once every
+ * frame holds a page, the CLOCK victim (begin_eviction_locked, 131-175: the
+ * hand walks the frames, clearing set reference bits, and takes the first
+ * frame whose bit is clear; the hand stops one past it); the new page is
+ * published referenced and clean (publish, 21-39), dirty if written.
+ * The state (frame pages, bits, hand, frames in use) carries across calls
+ * through `st`; or_clock_new / or_clock_free manage it. */
+typedef struct or_clock {
+    uint64_t frames, used, hand;
+    uint64_t* page;    /* per frame */
+    uint8_t* ref;
+    uint8_t* dirty;
+    uint64_t cap;      /* hash table: page -> frame */
+    or_slot* table;
+} or_clock;
+
+void* or_clock_new(uint64_t frames)
+{
+    or_clock* c = (or_clock*)calloc(1, sizeof(or_clock));
+    if (!c) return NULL;
+    c->frames = frames;
+    c->page = (uint64_t*)calloc(frames ? frames : 1, sizeof(uint64_t));
+    c->ref = (uint8_t*)calloc(frames ? frames : 1, 1);
+    c->dirty = (uint8_t*)calloc(frames ? frames : 1, 1);
+    c->cap = 16;
+    while (c->cap < frames * 2 + 16) c->cap <<= 1;
+    c->table = (or_slot*)malloc(sizeof(or_slot) * c->cap);
+    if (!c->page || !c->ref || !c->dirty || !c->table) return NULL;
+    for (uint64_t k = 0; k < c->cap; ++k) c->table[k].node = -1;
+    return c;
+}
+
+void or_clock_free(void* p)
+{
+    or_clock* c = (or_clock*)p;
+    if (!c) return;
+    free(c->page); free(c->ref); free(c->dirty); free(c->table); free(c);
+}
+
+static uint64_t or_clock_find(const or_clock* c, uint64_t page)
+{
+    const uint64_t mask = c->cap - 1;
+    uint64_t h = or_mix(page) & mask;
+    while (c->table[h].node >= 0 && c->table[h].key != page) h = (h + 1) & mask;
+    return h;
+}
+
+static void or_clock_erase(or_clock* c, uint64_t page)
+{
+    const uint64_t mask = c->cap - 1;
+    uint64_t hole = or_clock_find(c, page), probe = (hole + 1) & mask;
+    c->table[hole].node = -1;
+    while (c->table[probe].node >= 0) {
+        const uint64_t ideal = or_mix(c->table[probe].key) & mask;
+        if (((probe - ideal) & mask) >= ((probe - hole) & mask)) {
+            c->table[hole] = c->table[probe];
+            c->table[probe].node = -1;
+            hole = probe;
+        }
+        probe = (probe + 1) & mask;
+    }
+}
+
+void or_clock_run(void* state, const uint64_t* pages, const uint8_t* writes, uint64_t n,
+                  uint8_t* hit, uint64_t* victim, uint8_t* victim_dirty)
+{
+    or_clock* c = (or_clock*)state;
+    for (uint64_t i = 0; i < n; ++i) {
+        const uint64_t p = pages[i];
+        victim[i] = U64MAX;
+        victim_dirty[i] = 0;
+        hit[i] = 0;
+        if (c->frames == 0) continue;
+        uint64_t h = or_clock_find(c, p);
+        if (c->table[h].node >= 0) {
+            const int64_t f = c->table[h].node;
+            hit[i] = 1;
+            c->ref[f] = 1;
+            if (writes[i]) c->dirty[f] = 1;
+            continue;
+        }
+        uint64_t f;
+        if (c->used < c->frames) {
+            f = c->used++;
+        } else {
+            for (;;) {
+                f = c->hand;
+                c->hand = (c->hand + 1) % c->frames;
+                if (!c->ref[f]) break;
+                c->ref[f] = 0;
+            }
+            victim[i] = c->page[f];
+            victim_dirty[i] = c->dirty[f];
+            or_clock_erase(c, c->page[f]);
+            h = or_clock_find(c, p);
+        }
+        c->page[f] = p;
+        c->ref[f] = 1;
+        c->dirty[f] = writes[i] ? 1 : 0;
+        c->table[h].key = p;
+        c->table[h].node = (int64_t)f;
+    }
+}
+
 /* One media action of the capacity path through the die model. */
 static uint64_t or_media_step(const or_geometry* g, const or_timing* t,
                               const uint64_t* chan_bw, const uint64_t* t_read,

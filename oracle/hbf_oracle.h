@@ -157,6 +157,14 @@ void or_lru_run(const uint64_t* pages, const uint8_t* writes, uint64_t n,
                 uint64_t frames, uint8_t* hit, uint64_t* victim,
                 uint8_t* victim_dirty);
 
+/* ---- capacity mode: second-chance CLOCK (the reference runtime's policy,
+ * src/cuda_runtime/hbm_cache.cpp:131-175 driven by
+ * capacity_page_service.cpp:97-210).  State carries across runs. */
+void* or_clock_new(uint64_t frames);
+void or_clock_free(void* state);
+void or_clock_run(void* state, const uint64_t* pages, const uint8_t* writes, uint64_t n,
+                  uint8_t* hit, uint64_t* victim, uint8_t* victim_dirty);
+
 /* ---- capacity mode: media actions of the misses, timed with the die model
  * in batch order (request_dispatcher.cpp:107-126, 294-298): for a miss, the
  * program of a dirty victim's page at the access's arrival, then the read of

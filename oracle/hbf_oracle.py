@@ -93,6 +93,12 @@ def _load() -> ctypes.CDLL:
     lib.or_run_batch_threads.restype = ctypes.c_int
     lib.or_run_batch_threads.argtypes = [p, u32, p, p, p, p, p, p, p, p, p, p,
                                          u64, p, p, p, p, p, ctypes.c_int]
+    lib.or_clock_new.restype = ctypes.c_void_p
+    lib.or_clock_new.argtypes = [u64]
+    lib.or_clock_free.restype = None
+    lib.or_clock_free.argtypes = [p]
+    lib.or_clock_run.restype = None
+    lib.or_clock_run.argtypes = [p, p, p, u64, p, p, p]
     lib.or_capacity_timing.restype = None
     lib.or_capacity_timing.argtypes = [p, p, p, p, p, p, p, p, p, p, p, p, u64, u32, p, p, p]
     lib.or_lru_run.restype = None
@@ -184,6 +190,32 @@ def lru(pages: np.ndarray, writes: np.ndarray, frames: int):
     LIB.or_lru_run(_ptr(pages), _ptr(writes), n, frames, _ptr(hit), _ptr(victim),
                    _ptr(vdirty))
     return hit, victim, vdirty
+
+
+class Clock:
+    """Second-chance CLOCK state across batches (the reference runtime's
+    capacity policy)."""
+
+    def __init__(self, frames: int):
+        self.handle = LIB.or_clock_new(frames)
+        if not self.handle:
+            raise MemoryError("oracle allocation failed")
+
+    def run(self, pages: np.ndarray, writes: np.ndarray):
+        n = pages.size
+        pages = np.ascontiguousarray(pages, np.uint64)
+        writes = np.ascontiguousarray(writes, np.uint8)
+        hit = np.zeros(n, np.uint8)
+        victim = np.zeros(n, np.uint64)
+        vdirty = np.zeros(n, np.uint8)
+        LIB.or_clock_run(self.handle, _ptr(pages), _ptr(writes), n, _ptr(hit), _ptr(victim),
+                         _ptr(vdirty))
+        return hit, victim, vdirty
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            LIB.or_clock_free(self.handle)
+            self.handle = None
 
 
 def capacity_timing(geometry, timing, chan_bw, t_read, t_prog, admit, status, hit, page,

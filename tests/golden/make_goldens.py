@@ -18,6 +18,11 @@ Fixtures written:
                          (src/ucie/bank_layout.cpp) and the page-striped
                          placement checked by ContiguousStackMap::locate and
                          inverse_page_striped (src/ucie/stack_router.cpp).
+  clock_goldens.json     hit / victim / victim-dirty decisions of the reference
+                         second-chance CLOCK HBM cache
+                         (src/cuda_runtime/hbm_cache.cpp, compiled from
+                         source) driven as the capacity service resolves
+                         page references.
   link_goldens.json      delivery ticks, counters and credits of the reference
                          UCIe streaming link (src/ucie/link.cpp, compiled
                          from source) on message batches.
@@ -57,6 +62,7 @@ REF_BIN = REPO / "oracle" / "_ref" / "ref_goldens"
 REF_PREFETCH = REPO / "oracle" / "_ref" / "ref_prefetch"
 REF_LINK = REPO / "oracle" / "_ref" / "ref_link"
 REF_LAYOUT = REPO / "oracle" / "_ref" / "ref_layout"
+REF_CLOCK = REPO / "oracle" / "_ref" / "ref_clock"
 
 
 def load_exporter():
@@ -364,9 +370,37 @@ def layout_goldens() -> None:
         "stripe": stripe}))
 
 
+def clock_goldens() -> None:
+    """Second-chance CLOCK decisions of the reference HBM cache
+    (oracle/ref_clock.cpp over src/cuda_runtime/hbm_cache.cpp) on random and
+    cyclic page traces: hit, victim page and victim dirty bit per access."""
+    rng = random.Random(77)
+    cases = []
+    shapes = [(1, 3, 60, 0.5, "random"), (2, 5, 200, 0.3, "random"),
+              (7, 30, 2000, 0.3, "random"), (64, 300, 4000, 0.2, "random"),
+              (100, 140, 2000, 0.1, "cyclic"), (33, 1000, 3000, 0.05, "zipf"),
+              (500, 800, 6000, 0.25, "random")]
+    for frames, npages, n, wfrac, kind in shapes:
+        if kind == "cyclic":
+            pages = [k % npages for k in range(n)]
+        elif kind == "zipf":
+            weights = [1.0 / (k + 1) ** 1.1 for k in range(npages)]
+            pages = rng.choices(range(npages), weights=weights, k=n)
+        else:
+            pages = [rng.randrange(npages) for _ in range(n)]
+        ops = [1 if rng.random() < wfrac else 0 for _ in range(n)]
+        text = f"{frames} {n}\n" + "".join(f"{p} {o}\n" for p, o in zip(pages, ops))
+        out = subprocess.run([str(REF_CLOCK)], input=text, check=True, capture_output=True,
+                             text=True).stdout.split()
+        vals = [int(v) for v in out]
+        cases.append({"frames": frames, "kind": kind, "pages": pages, "ops": ops,
+                      "hit": vals[0::3], "victim": vals[1::3], "victim_dirty": vals[2::3]})
+    (HERE / "clock_goldens.json").write_text(json.dumps(cases))
+
+
 GENERATORS = {"device": device_goldens, "thermal": thermal_goldens, "lru": lru_goldens,
               "retention": retention_goldens, "prefetch": prefetch_goldens,
-              "link": link_goldens, "layout": layout_goldens}
+              "link": link_goldens, "layout": layout_goldens, "clock": clock_goldens}
 
 
 def main() -> int:

@@ -191,3 +191,80 @@ def test_media_action_timing_matches_oracle(tmp_path, frames, write_p, n):
         assert chained > 0
     assert np.array_equal(ctx.get_state(), oracle.state)
     ctx.close()
+
+
+# ---- CLOCK (the reference runtime's second-chance policy) ----
+CLOCK_GOLDEN = Path(__file__).resolve().parent / "golden" / "clock_goldens.json"
+
+
+def clock_context(tmp, frames):
+    ctx = capacity_context(tmp, frames)
+    ctx.capacity_configure(frames, PAGE, policy="clock")
+    return ctx
+
+
+def test_clock_reference_goldens(tmp_path):
+    """GPU CLOCK decisions against the reference HbmCache
+    (tests/golden/clock_goldens.json), each case over three batches."""
+    rng = np.random.default_rng(1)
+    for k, case in enumerate(json.loads(CLOCK_GOLDEN.read_text())):
+        ctx = clock_context(str(tmp_path / f"c{k}"), case["frames"])
+        pages = np.array(case["pages"], np.uint64)
+        ops = np.array(case["ops"], np.uint8)
+        n = pages.size
+        parts = []
+        for lo, hi in ((0, n // 3), (n // 3, 2 * n // 3), (2 * n // 3, n)):
+            parts.append(run_gpu(ctx, *to_accesses(pages[lo:hi], ops[lo:hi], rng)))
+        got = tuple(np.concatenate([p[j] for p in parts]) for j in range(4))
+        want = (np.array(case["hit"], np.uint8), np.array(case["victim"], np.uint64),
+                np.array(case["victim_dirty"], np.uint8))
+        check(got, want, f"clock case {k} ({case['kind']}, {case['frames']} frames)")
+        resident, _ = ctx.capacity_state()
+        assert resident.size == min(case["frames"], np.unique(pages).size)
+        ctx.close()
+
+
+@pytest.mark.parametrize("frames,universe,n", [(1, 4, 2000), (31, 90, 20000),
+                                               (64, 500, 50000), (3000, 9000, 120000)])
+def test_clock_matches_oracle_with_media_timing(tmp_path, frames, universe, n):
+    """CLOCK decisions and the timed media actions of the misses against the
+    oracle (CLOCK pinned to the reference by the goldens above), over
+    batches that carry the frames, bits and hand."""
+    import torch
+    from helpers import OracleRun
+    rng = np.random.default_rng(frames + n)
+    pages = trace(rng, n, universe, 0.3) if n <= 50000 else \
+        np.where(rng.random(n) < 0.7, rng.integers(0, frames, n),
+                 rng.integers(0, universe, n)).astype(np.uint64)
+    writes = (rng.random(n) < 0.25).astype(np.uint8)
+    address, nbytes, op = to_accesses(pages, writes, rng)
+    arrival = np.cumsum(rng.exponential(20.0, n).astype(np.uint64) + 1).astype(np.uint64)
+    clock = ho.Clock(frames)
+    p = wl.c0_profile()
+    p["capacity_bytes"] = 64 << 30
+    s = Setup(profile=p, model=3, stacks=1, stripe=4096)
+    s.ranges = [(wl.RANGE_BASE, 63 << 30, 2, 3)]
+    oracle = OracleRun(s)
+    ctx = clock_context(str(tmp_path), frames)
+    cuts = [0, n // 5, n // 2, n]
+    for k, (lo, hi) in enumerate(zip(cuts[:-1], cuts[1:])):
+        hit_w, victim_w, dirty_w = clock.run(pages[lo:hi], writes[lo:hi])
+        dev = [torch.from_numpy(address[lo:hi].view(np.int64)).cuda(),
+               torch.from_numpy(nbytes[lo:hi].view(np.int32)).cuda(),
+               torch.from_numpy(op[lo:hi]).cuda(),
+               torch.from_numpy(arrival[lo:hi].view(np.int64)).cuda()]
+        hit, victim, dirty, status, done, latency = ctx.submit_capacity(*dev, timed=True)
+        check((hit.cpu().numpy(), victim.cpu().numpy().view(np.uint64), dirty.cpu().numpy(),
+               status.cpu().numpy()), (hit_w, victim_w, dirty_w), f"batch {k}")
+        want_done, want_lat = ho.capacity_timing(
+            oracle.geometry, oracle.timing, oracle.chan_bw, oracle.t_read, oracle.t_prog,
+            oracle.admit, np.ones(hi - lo, np.uint8), hit_w, pages[lo:hi], victim_w, dirty_w,
+            arrival[lo:hi], 12, oracle.state)
+        got_done = done.cpu().numpy().view(np.uint64)
+        bad = np.flatnonzero(got_done != want_done)
+        assert bad.size == 0, f"batch {k}: done differs at {bad[:5]}"
+        assert np.array_equal(latency.cpu().numpy().view(np.uint64), want_lat)
+    assert np.array_equal(ctx.get_state(), oracle.state)
+    stats = ctx.capacity_stats()
+    assert stats["service_resident_hits"] + stats["service_misses"] == n
+    ctx.close()

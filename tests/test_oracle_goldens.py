@@ -362,3 +362,23 @@ def test_stripe_decode_against_reference_layout(golden_dir):
             check_layout_decode(got, case, kind)
             cases += case[1].size
     assert cases == len(golden["bank"]) + len(golden["stripe"])
+
+
+def test_clock_oracle_against_reference_cache(golden_dir):
+    """The oracle's CLOCK (or_clock_run) against the reference HbmCache's
+    second-chance decisions, each case split over three calls (the state
+    carries across calls)."""
+    with open(golden_dir / "clock_goldens.json") as f:
+        cases = json.load(f)
+    for case in cases:
+        pages = np.array(case["pages"], np.uint64)
+        ops = np.array(case["ops"], np.uint8)
+        clock = ho.Clock(case["frames"])
+        cuts = [0, len(pages) // 3, 2 * len(pages) // 3, len(pages)]
+        got = [clock.run(pages[a:b], ops[a:b]) for a, b in zip(cuts[:-1], cuts[1:])]
+        hit = np.concatenate([g[0] for g in got])
+        victim = np.concatenate([g[1] for g in got])
+        dirty = np.concatenate([g[2] for g in got])
+        assert np.array_equal(hit, np.array(case["hit"], np.uint8)), case["kind"]
+        assert np.array_equal(victim, np.array(case["victim"], np.uint64)), case["kind"]
+        assert np.array_equal(dirty, np.array(case["victim_dirty"], np.uint8)), case["kind"]
