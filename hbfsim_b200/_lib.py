@@ -170,6 +170,7 @@ SIGNATURES = {
     "hbfsim_sample_batch_v1": (i32, [vp, vp, vp, vp, u64, vp, vp]),
     "hbfsim_capacity_configure_v1": (i32, [vp, u64, u32]),
     "hbfsim_capacity_policy_v1": (i32, [vp, u32]),
+    "hbfsim_get_capacity_rounds_v1": (i32, [vp, vp, vp, vp]),
     "hbfsim_submit_capacity_batch_v1": (i32, [vp, ctypes.POINTER(CapacityBatchV1), vp]),
     "hbfsim_get_capacity_state_v1": (i32, [vp, vp, vp, u64, ctypes.POINTER(u64)]),
     "hbfsim_set_channel_factors_v1": (i32, [vp, vp, vp, vp]),

@@ -241,6 +241,15 @@ class Context:
             return hit, victim, dirty, status, done, latency
         return hit, victim, dirty, status
 
+    def capacity_rounds(self):
+        """(fixed-point rounds, pieces, walked) of the last timed capacity
+        batch."""
+        r, p, w = ctypes.c_uint32(), ctypes.c_uint64(), ctypes.c_uint32()
+        check(self._lib.hbfsim_get_capacity_rounds_v1(self.handle, ctypes.byref(r),
+                                                      ctypes.byref(p), ctypes.byref(w)),
+              "hbfsim_get_capacity_rounds_v1")
+        return r.value, p.value, w.value
+
     def capacity_stats(self) -> dict:
         """hbfsim_get_capacity_stats_v1 as a dict (the reference's counter
         names)."""

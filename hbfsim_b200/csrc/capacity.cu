@@ -70,6 +70,14 @@ struct CapacityState {
     u32* chained_pos = nullptr;
     DevRange* media_range = nullptr; // identity range: media address -> itself
     u32* counts = nullptr;           // small device results
+    // what one timing batch of the media actions changes besides its
+    // outputs (counters, last arrival, die activity), saved before the
+    // fixed-point rounds and put back before each repeat
+    unsigned char* snap = nullptr;
+    std::uint64_t snap_bytes = 0;
+    std::uint32_t rounds_last = 0;   // rounds the last batch's fixed point took
+    std::uint32_t walked_last = 0;   // 1: it took the one-thread walk instead
+    std::uint64_t pieces_last = 0;   // pieces it ran in (0: settled in rounds)
     // CLOCK policy (the reference runtime's HbmCache): per frame its page,
     // reference and dirty byte; page -> frame table; [hand, frames in use]
     std::uint32_t policy = 0;        // HBFSIM_CAPACITY_POLICY_*
@@ -609,6 +617,23 @@ __global__ void chained_flag_kernel(const u32* chain, u64 count, u32* flag)
     if (k < count) flag[k] = chain[k] != kNone ? 1u : 0u;
 }
 
+// One fixed-point round: each chained read starts no earlier than its
+// program's completion.  Raises only ever increase an arrival (completions
+// are monotone in the arrivals), so max(current, completion) is the read's
+// arrival max(access arrival, completion).
+__global__ void raise_kernel(const u32* chained, u64 count, const u32* chain, const u64* done,
+                             u64* arrival, u32* changed)
+{
+    const u64 q = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (q >= count) return;
+    const u32 k = chained[q];
+    const u64 need = done[chain[k]];
+    if (need > arrival[k]) {
+        arrival[k] = need;
+        *changed = 1u;
+    }
+}
+
 // completion of each access: its read, or its arrival when served from HBM
 // (hit) or not a capacity access
 __global__ void act_result_kernel(const u32* status, const u32* hit, const u32* dirty,
@@ -817,7 +842,7 @@ void capacity_destroy(CapacityState* c)
                     c->act_addr, c->act_bytes, c->act_op, c->act_arr, c->act_chain,
                     c->act_done, c->act_lat, c->act_status, c->chained, c->chained_flag,
                     c->chained_pos, c->media_range, c->clk_table, c->clk_page, c->clk_ref,
-                    c->clk_dirty, c->clk_state};
+                    c->clk_dirty, c->clk_state, c->snap};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     delete c;
@@ -887,14 +912,9 @@ cudaError_t scan_add(CapacityState* s, const u32* in, u32* out, u64 n, bool incl
 
 bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
 
-constexpr std::uint64_t kMaxChainPieces = 4096;
-
 // Times the media actions of the batch's misses with the context's die
-// model, in batch order, and writes each access's completion.  Every chained
-// read starts a piece; pieces run back to back on the stream, and before
-// each one its chained read's arrival is raised to its program's
-// completion.  Beyond kMaxChainPieces chained reads, one thread walks all
-// actions instead (exact, slow).
+// model, in batch order, and writes each access's completion: one timing
+// batch of all actions per fixed-point round (below).
 int time_actions(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStream_t st)
 {
     CapacityState* s = ctx->capacity;
@@ -930,37 +950,125 @@ int time_actions(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStr
         std::uint32_t q = 0;
         cudaMemcpyAsync(&q, cnt + 9, 4, cudaMemcpyDeviceToHost, st);
         if (cudaStreamSynchronize(st) != cudaSuccess) return HBFSIM_CUDA_ERROR;
-        if (q <= kMaxChainPieces) {
+        BatchIO io{};
+        io.address = s->act_addr;
+        io.bytes = s->act_bytes;
+        io.op = s->act_op;
+        io.arrival = s->act_arr;
+        io.done = s->act_done;
+        io.latency = s->act_lat;
+        io.status = s->act_status;
+        io.n = actions;
+        io.aligned = aligned16(io.address) && aligned16(io.bytes) && aligned16(io.op) &&
+                     aligned16(io.arrival) && aligned16(io.done) && aligned16(io.latency) &&
+                     aligned16(io.status);
+        // Fixed point: time every action with the chained reads' current
+        // arrivals, raise each chained read to its program's completion,
+        // and repeat until no arrival moves.  Each round starts from the
+        // batch's initial die state (the timing kernels read one state
+        // buffer and write the other) and from the saved counters, last
+        // arrival and die activity, so the final round counts once.  The
+        // rounds converge to the one-at-a-time walk of the actions in batch
+        // order (every action depends only on earlier ones), but a raise
+        // can delay later programs of its channel and so move later chained
+        // reads: under a deep queue each round settles little more than one
+        // program.  After kMaxRounds the batch is timed in pieces instead:
+        // every chained read starts a piece, its arrival raised to its
+        // program's completion (computed by an earlier piece) just before
+        // the piece runs -- pieces in batch order, each in parallel.
+        constexpr std::uint32_t kMaxRounds = 3;
+        constexpr std::uint32_t kMaxPieces = 1u << 20;
+        const int cur0 = ctx->cur;
+        const std::uint64_t act_words = ctx->d_die_read_bytes ? 2ull * ctx->C * ctx->D : 0;
+        const std::uint64_t need = sizeof(DevCounters) + 8 + 8 * act_words;
+        if (need > s->snap_bytes) {
+            if (s->snap) cudaFree(s->snap);
+            s->snap = nullptr;
+            s->snap_bytes = 0;
+            if (cudaMalloc(&s->snap, need) != cudaSuccess) return HBFSIM_CUDA_ERROR;
+            s->snap_bytes = need;
+        }
+        unsigned char* snap_counters = s->snap;
+        unsigned char* snap_last = snap_counters + sizeof(DevCounters);
+        unsigned char* snap_act = snap_last + 8;
+        auto save = [&](bool restore) {
+            auto copy = [&](void* a, void* b, std::uint64_t bytes) {
+                cudaMemcpyAsync(restore ? a : b, restore ? b : a, bytes,
+                                cudaMemcpyDeviceToDevice, st);
+            };
+            copy(ctx->d_counters, snap_counters, sizeof(DevCounters));
+            copy(ctx->d_last_arrival, snap_last, 8);
+            if (act_words) {
+                copy(ctx->d_die_read_bytes, snap_act, 4 * act_words);
+                copy(ctx->d_die_writes, snap_act + 4 * act_words, 4 * act_words);
+            }
+        };
+        if (q) save(false);
+        bool converged = q == 0;
+        std::uint32_t round = 0;
+        for (; round < (q ? kMaxRounds : 1u); ++round) {
+            if (round) {
+                save(true);
+                ctx->cur = cur0;
+            }
+            const int rc = run_media_batch(ctx, io, s->media_range, 1, st);
+            if (rc != HBFSIM_OK) return rc;
+            if (!q) break;
+            cudaMemsetAsync(cnt + 10, 0, 4, st);
+            raise_kernel<<<blocks(q), kT, 0, st>>>(s->chained, q, s->act_chain, s->act_done,
+                                                   s->act_arr, cnt + 10);
+            std::uint32_t changed = 0;
+            cudaMemcpyAsync(&changed, cnt + 10, 4, cudaMemcpyDeviceToHost, st);
+            if (cudaStreamSynchronize(st) != cudaSuccess) return HBFSIM_CUDA_ERROR;
+            if (!changed) {
+                converged = true;
+                ++round;
+                break;
+            }
+        }
+        s->rounds_last = round;
+        s->walked_last = 0;
+        s->pieces_last = 0;
+        if (!converged && q <= kMaxPieces) {
+            save(true);
+            ctx->cur = cur0;
             std::vector<std::uint32_t> starts(q);
-            if (q && cudaMemcpy(starts.data(), s->chained, 4ull * q, cudaMemcpyDeviceToHost) !=
-                         cudaSuccess)
+            if (cudaMemcpy(starts.data(), s->chained, 4ull * q, cudaMemcpyDeviceToHost) !=
+                cudaSuccess)
                 return HBFSIM_CUDA_ERROR;
             std::vector<std::uint64_t> cuts{0};
             for (std::uint32_t v : starts)
                 if (v != 0) cuts.push_back(v);
             cuts.push_back(actions);
-            for (std::size_t p = 0; p + 1 < cuts.size(); ++p) {
-                const std::uint64_t lo = cuts[p], hi = cuts[p + 1];
+            for (std::size_t k = 0; k + 1 < cuts.size(); ++k) {
+                const std::uint64_t lo = cuts[k], hi = cuts[k + 1];
                 if (hi <= lo) continue;
                 if (launch_chain_fixup(s->act_arr, s->act_done, s->act_chain, lo, st) !=
                     cudaSuccess)
                     return HBFSIM_CUDA_ERROR;
-                BatchIO io{};
-                io.address = s->act_addr + lo;
-                io.bytes = s->act_bytes + lo;
-                io.op = s->act_op + lo;
-                io.arrival = s->act_arr + lo;
-                io.done = s->act_done + lo;
-                io.latency = s->act_lat + lo;
-                io.status = s->act_status + lo;
-                io.n = hi - lo;
-                io.aligned = aligned16(io.address) && aligned16(io.bytes) && aligned16(io.op) &&
-                             aligned16(io.arrival) && aligned16(io.done) &&
-                             aligned16(io.latency) && aligned16(io.status);
-                const int rc = run_media_batch(ctx, io, s->media_range, 1, st);
+                BatchIO piece = io;
+                piece.address = s->act_addr + lo;
+                piece.bytes = s->act_bytes + lo;
+                piece.op = s->act_op + lo;
+                piece.arrival = s->act_arr + lo;
+                piece.done = s->act_done + lo;
+                piece.latency = s->act_lat + lo;
+                piece.status = s->act_status + lo;
+                piece.n = hi - lo;
+                piece.aligned = aligned16(piece.address) && aligned16(piece.bytes) &&
+                                aligned16(piece.op) && aligned16(piece.arrival) &&
+                                aligned16(piece.done) && aligned16(piece.latency) &&
+                                aligned16(piece.status);
+                const int rc = run_media_batch(ctx, piece, s->media_range, 1, st);
                 if (rc != HBFSIM_OK) return rc;
+                ++s->pieces_last;
             }
-        } else {
+            converged = true;
+        }
+        if (!converged) {
+            s->walked_last = 1;
+            save(true);
+            ctx->cur = cur0;
             const DecodeParams dp = media_decode_params(ctx, s->media_range, 1);
             const std::uint64_t words = static_cast<std::uint64_t>(ctx->C) * ctx->K;
             if (launch_chain_sequential(dp, context_timing_params(ctx), s->act_addr,
@@ -1257,6 +1365,18 @@ int hbfsim_submit_capacity_batch_v1(hbfsim_context* c, const hbfsim_capacity_bat
     if (b->count == 0) return HBFSIM_OK;
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
     return run_capacity(c, b, s);
+}
+
+int hbfsim_get_capacity_rounds_v1(hbfsim_context* c, uint32_t* rounds, uint64_t* pieces,
+                                  uint32_t* walked)
+{
+    if (!c || !rounds || !pieces || !walked) return HBFSIM_INVALID_ARGUMENT;
+    CGuard g(c);
+    if (!c->capacity) return HBFSIM_INVALID_ARGUMENT;
+    *rounds = c->capacity->rounds_last;
+    *pieces = c->capacity->pieces_last;
+    *walked = c->capacity->walked_last;
+    return HBFSIM_OK;
 }
 
 int hbfsim_get_capacity_state_v1(hbfsim_context* c, uint64_t* resident_pages,

@@ -2324,8 +2324,9 @@ __global__ void chain_fixup_kernel(u64* arrival, const u64* done, const u32* cha
     }
 }
 
-// Exact fallback for batches with very many chained reads: one thread walks
-// every action in batch order with the saturating die model.
+// Exact fallback for media-action batches with more chained reads than the
+// piece path takes: one thread walks every action in batch order with the
+// saturating die model.
 __global__ void chain_sequential_kernel(const DecodeParams dp, const TimingParams tp,
                                         const u64* address, const u32* bytes, const u8* op,
                                         u64* arrival, const u32* chain, u64 n, u32 K,

@@ -272,12 +272,26 @@ typedef struct hbfsim_capacity_batch_v1 {
  * channel state: for each miss in batch order, the program of a dirty
  * victim's page at the access's arrival, then the read of the missed page
  * at max(arrival, program completion) (request_dispatcher.cpp:107-126,
- * 294-298); one LRU page each, at its media address.  A miss completes with
+ * 294-298); one LRU page each, at its media address.  The actions are timed
+ * in parallel, in rounds or pieces (hbfsim_get_capacity_rounds_v1).  A miss completes with
  * its read; hits (served from HBM) and non-capacity accesses complete at
  * their arrival. */
 int hbfsim_submit_capacity_batch_v1(hbfsim_context* context,
                                     const hbfsim_capacity_batch_v1* batch,
                                     void* stream);
+
+/* How the last timed batch resolved its chained reads (a miss's read that
+ * waits for its dirty victim's program).  First up to 3 *rounds: timing
+ * passes over all its media actions, each raising the chained reads to
+ * their programs' completions, until none moves (a fixed point, equal to
+ * timing the actions one at a time in batch order).  If that does not
+ * settle, *pieces > 0: the actions were timed in that many pieces, each
+ * starting at a chained read whose arrival its program's completion had
+ * raised.  *walked = 1: more than 2^20 chained reads, one thread walked the
+ * actions in order.  No counterpart in the reference, which times one
+ * request at a time. */
+int hbfsim_get_capacity_rounds_v1(hbfsim_context* context, uint32_t* rounds,
+                                  uint64_t* pieces, uint32_t* walked);
 
 /* The resident list, oldest first (host copies; NULL arrays return only
  * *resident). */

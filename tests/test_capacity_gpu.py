@@ -153,8 +153,10 @@ def test_statuses_and_page_numbering(tmp_path):
 @pytest.mark.parametrize("frames,write_p,n", [(256, 0.02, 60000), (64, 0.5, 30000)])
 def test_media_action_timing_matches_oracle(tmp_path, frames, write_p, n):
     """Misses become media actions timed with the die model: the program of
-    a dirty victim, then the chained read.  Few chained reads run as pieces
-    of the parallel path; many take the exact one-thread walk."""
+    a dirty victim, then the chained read.  All actions of a batch are timed
+    in parallel rounds that raise the chained reads to their programs'
+    completions until none moves, or else in pieces that start at the
+    chained reads."""
     import torch
     from helpers import OracleRun
     rng = np.random.default_rng(frames)
@@ -189,6 +191,57 @@ def test_media_action_timing_matches_oracle(tmp_path, frames, write_p, n):
         assert np.array_equal(latency, want_lat)
         chained = int((dirty_w[lo:hi] == 1).sum())
         assert chained > 0
+        rounds, pieces, walked = ctx.capacity_rounds()
+        assert rounds >= 2 and not walked
+    assert np.array_equal(ctx.get_state(), oracle.state)
+    ctx.close()
+
+
+def test_config2_timed_steps_full_size(tmp_path):
+    """Config 2 at full size: decode steps 0 and 1 of the Llama-3-8B-shaped
+    paged-KV trace (about 3.5e7 page references each; HBM holds 20 % of the
+    KV pages) through exact LRU with their media actions timed, bit-exact
+    against the oracle (LRU decisions, then every access's completion)."""
+    import torch
+    from helpers import OracleRun
+    lengths = wl.c2_lengths(0)
+    frames = wl.c2_frames(lengths)
+    p = wl.c0_profile()
+    p["capacity_bytes"] = 160 << 30
+    s = Setup(profile=p, model=3, stacks=1, stripe=4096)
+    s.ranges = [(wl.RANGE_BASE, 150 << 30, 2, 3)]
+    ctx = make_context(s, str(tmp_path))
+    ctx.capacity_configure(frames, PAGE)
+    oracle = OracleRun(s)
+    steps = [wl.c2_step(lengths, t, 256) for t in range(2)]
+    pages = [((a - np.uint64(wl.RANGE_BASE)) >> np.uint64(12)).astype(np.uint64)
+             for a, _, _ in steps]
+    ops = [o for _, _, o in steps]
+    want_all = ho.lru(np.concatenate(pages), np.concatenate(ops), frames)
+    start = 0
+    t0 = 0
+    for t, (address, nbytes, op) in enumerate(steps):
+        n = address.size
+        arrival = (np.uint64(t0) + np.arange(n, dtype=np.uint64)).astype(np.uint64)
+        t0 += n
+        want = tuple(w[start:start + n] for w in want_all)
+        start += n
+        dev = [torch.from_numpy(address.view(np.int64)).cuda(),
+               torch.from_numpy(nbytes.view(np.int32)).cuda(), torch.from_numpy(op).cuda(),
+               torch.from_numpy(arrival.view(np.int64)).cuda()]
+        hit, victim, dirty, status, done, latency = ctx.submit_capacity(*dev, timed=True)
+        check((hit.cpu().numpy(), victim.cpu().numpy().view(np.uint64), dirty.cpu().numpy(),
+               status.cpu().numpy()), want, f"step {t}")
+        want_done, want_lat = ho.capacity_timing(
+            oracle.geometry, oracle.timing, oracle.chan_bw, oracle.t_read, oracle.t_prog,
+            oracle.admit, np.ones(n, np.uint8), want[0], pages[t], want[1], want[2], arrival,
+            12, oracle.state)
+        got = done.cpu().numpy().view(np.uint64)
+        bad = np.flatnonzero(got != want_done)
+        assert bad.size == 0, f"step {t}: done differs at {bad[:5]}"
+        assert np.array_equal(latency.cpu().numpy().view(np.uint64), want_lat)
+        del dev, hit, victim, dirty, status, done, latency
+    assert int(want_all[2].sum()) > 0, "the steps evict dirty pages (chained reads)"
     assert np.array_equal(ctx.get_state(), oracle.state)
     ctx.close()
 
