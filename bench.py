@@ -301,7 +301,7 @@ def main():
                          "fewer only for small profiling captures)")
     ap.add_argument("--only-extra", choices=["empirical_vmem", "thermal_coupled", "retention",
                                              "prefetch_sweep", "ucie_link", "config4",
-                                             "capacity_lru"],
+                                             "capacity_lru", "linked_stage"],
                     help="run one secondary measurement alone and print its JSON "
                          "(profiling captures); not a bench line")
     args = ap.parse_args()
@@ -314,6 +314,7 @@ def main():
         run = {"empirical_vmem": run_vmem, "thermal_coupled": run_c3,
                "retention": run_retention, "prefetch_sweep": run_prefetch,
                "ucie_link": run_link, "capacity_lru": run_capacity_lru,
+               "linked_stage": run_linked,
                "config4": lambda a, d, t: run_c4(a, d, t, 0, 1)}[args.only_extra]
         with tempfile.TemporaryDirectory() as tmp:
             print_result(run(args, torch.device("cuda", 0), tmp))
@@ -541,6 +542,7 @@ def run_extras(args, device, tmp):
     out["retention"] = run_retention(args, device, tmp)
     out["prefetch_sweep"] = run_prefetch(args, device, tmp)
     out["ucie_link"] = run_link(args, device, tmp)
+    out["linked_stage"] = run_linked(args, device, tmp)
     return out
 
 
@@ -674,6 +676,47 @@ def run_link(args, device, tmp):
                                "cores": 1, "kind": "port",
                                "sample": f"{sample} of the links, single thread"}
     return out
+
+
+def run_linked(args, device, tmp):
+    """The access path with the UCIe link as a stage per stack: the full
+    config-0 trace (1,048,576 accesses, one stack) through the per-die model,
+    then its stack's StreamingLink (the reference scenario profile) carrying
+    per access an AR at its arrival and an R at its die completion; an access
+    completes with its R delivery."""
+    import torch
+    from hbfsim_b200 import Context, link_profiles, submit_linked, workloads as wl
+    p = wl.c0_profile()
+    p["name"] = "bench-linked"
+    length = p["capacity_bytes"] - (1 << 20)
+    w = wl.Workload("linked", p, 1, STRIPE, wl.RANGE_BASE, length)
+    ctx = Context(w.write_profile(tmp), report_dir=f"{tmp}/report-linked", mode=3)
+    ctx.register_device(wl.RANGE_BASE, length, 1, 3)
+    a, b, o, t = wl.c0_trace(1 << 20, seed=0, range_length=length)
+    dev = [torch.from_numpy(x.view(dt)).to(device) for x, dt in
+           zip((a, b, o, t), (np.int64, np.int32, np.uint8, np.int64))]
+    prof = link_profiles(1)
+    submit_linked(ctx, *dev, prof, 1)  # warm up
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(3):
+        ctx.reset_state()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        out, die, res, _ = submit_linked(ctx, *dev, prof, 1)
+        torch.cuda.synchronize()
+        times.append(time.perf_counter() - t0)
+    dt = float(np.median(times))
+    extra = (out.done_ns - die.done_ns).float()
+    ctx.close()
+    return {"workload": "config-0 trace (1,048,576 accesses, 1 stack): per-die model, then the "
+                        "stack's UCIe streaming link (x64 at 16 GT/s, 12 AR / 56 R credit "
+                        "granules, 4 in flight) with an AR and an R message per access",
+            "accesses": a.size, "messages": 2 * a.size, "seconds": dt, "value": a.size / dt,
+            "unit": "accesses/s (die model + link, wall time of the call)",
+            "link_delay_ns_mean": float(extra.mean().item()),
+            "link_delay_ns_max": float(extra.max().item()),
+            "note": "the link is one event walk per link (one GPU thread per stack)"}
 
 
 def run_prefetch(args, device, tmp):

@@ -551,3 +551,55 @@ def link_batch(profiles: np.ndarray, offsets, direction, ready, stream=None):
                                    ctypes.c_void_p(_stream_handle(stream))),
           "hbfsim_link_batch_v1")
     return delivered[:int(off[-1])], res[:n]
+
+
+def link_messages(stack, arrival, done, modeled, stacks: int):
+    """The UCIe messages of a timed batch (device tensors), per stack: for
+    every modeled access an AR (request, direction 0) ready at its arrival
+    and an R (response, direction 1) ready at its die completion, on the
+    link of its stack, each link's messages in ready order (an AR before an
+    R of the same tick, otherwise batch order).  Returns (offsets per link
+    (host, links + 1), direction, ready, access index) in link order."""
+    import torch
+    idx = torch.nonzero(modeled).flatten()
+    n = idx.numel()
+    st = stack[idx]
+    m_stack = torch.cat([st, st])
+    m_ready = torch.cat([arrival[idx], done[idx]])
+    m_dir = torch.cat([torch.zeros(n, dtype=torch.uint8, device=idx.device),
+                       torch.ones(n, dtype=torch.uint8, device=idx.device)])
+    m_idx = torch.cat([idx, idx])
+    order = torch.sort(m_ready, stable=True).indices
+    order = order[torch.sort(m_stack[order], stable=True).indices]
+    counts = torch.bincount(m_stack, minlength=stacks).cpu().numpy()
+    offsets = np.concatenate([[0], np.cumsum(counts)]).astype(np.uint64)
+    return offsets, m_dir[order].contiguous(), m_ready[order].contiguous(), m_idx[order]
+
+
+def submit_linked(ctx: "Context", address, nbytes, op, arrival, profiles: np.ndarray,
+                  stacks: int, stream=None):
+    """One batch through the per-die model and then each stack's UCIe
+    streaming link (hbfsim::ucie::StreamingLink, src/ucie/link.cpp), composed
+    per stack: the request of every modeled access crosses its stack's link
+    as an AR message at the access's arrival, and the response as an R
+    message once the die model has completed it; the access completes when
+    its R message is delivered.  Accesses the die model does not time keep
+    its outputs.  profiles: one link profile per stack (link_profiles).
+    Returns (BatchResult with the linked completions, the die model's
+    BatchResult, per-link LINK_RESULT_DTYPE rows, the AR delivery ticks per
+    access (-1 when not modeled))."""
+    import torch
+    die = ctx.submit(address, nbytes, op, arrival, stream=stream)
+    rec = ctx.decode(address, nbytes, op, stream)
+    stack = rec.view(torch.int32).view(-1, 10)[:, 6].to(torch.int64)
+    modeled = die.status == _lib.ACCESS_MODELED
+    offsets, direction, ready, index = link_messages(stack, arrival, die.done_ns, modeled,
+                                                     stacks)
+    delivered, res = link_batch(profiles, offsets, direction, ready, stream)
+    done = die.done_ns.clone()
+    ar = torch.full_like(die.done_ns, -1)
+    is_r = direction == 1
+    done[index[is_r]] = delivered[is_r]
+    ar[index[~is_r]] = delivered[~is_r]
+    out = BatchResult(done, done - arrival, die.status)
+    return out, die, res, ar

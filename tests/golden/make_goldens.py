@@ -23,6 +23,10 @@ Fixtures written:
                          (src/cuda_runtime/hbm_cache.cpp, compiled from
                          source) driven as the capacity service resolves
                          page references.
+  linked_goldens.json    the die model composed with each stack's UCIe link:
+                         AR at the arrival and R at the die completion of
+                         every access of a seeded trace, through the
+                         reference StreamingLink (src/ucie/link.cpp).
   link_goldens.json      delivery ticks, counters and credits of the reference
                          UCIe streaming link (src/ucie/link.cpp, compiled
                          from source) on message batches.
@@ -398,9 +402,79 @@ def clock_goldens() -> None:
     (HERE / "clock_goldens.json").write_text(json.dumps(cases))
 
 
+LINKED = {"n": 4000, "seed": 31, "stacks": 2,
+          "profile": {"gt": 16, "ar": 12, "r": 56, "accepted": 4, "prop": 7,
+                      "consume": [2, 3]}}
+
+
+def linked_messages(stack, arrival, done, modeled):
+    """Per stack, AR at the arrival and R at the die completion of every
+    modeled access, in ready order (AR first at equal ticks, then batch
+    order): [(direction, ready, access, kind)] per stack."""
+    out = {}
+    for i in range(len(stack)):
+        if not modeled[i]:
+            continue
+        out.setdefault(int(stack[i]), []).append((int(arrival[i]), 0, i))
+    for i in range(len(stack)):
+        if modeled[i]:
+            out[int(stack[i])].append((int(done[i]), 1, i))
+    return {k: sorted(v, key=lambda m: (m[0], m[1], m[2])) for k, v in out.items()}
+
+
+def linked_goldens() -> None:
+    """The die model followed by each stack's UCIe link: the oracle's die
+    completions of a seeded config-0-shaped trace on 2 stacks, then the
+    reference StreamingLink (oracle/_ref/ref_link, src/ucie/link.cpp
+    compiled from source) carrying per access an AR at its arrival and an R
+    at its die completion; the fixture holds every access's R and AR
+    delivery ticks."""
+    import numpy as np
+    sys.path.insert(0, str(REPO / "oracle"))
+    sys.path.insert(0, str(REPO))
+    import hbf_oracle as ho
+    from hbfsim_b200 import workloads as wl
+    cfg = LINKED
+    prof = wl.c0_profile()
+    length = prof["capacity_bytes"] - (1 << 20)
+    a, b, o, t = wl.c0_trace(cfg["n"], seed=cfg["seed"], range_length=length)
+    ranges = ho.make_ranges([(wl.RANGE_BASE, length, 0, 1, 1, 3, prof["page_bytes"])])
+    geom = ho.make_geometry(cfg["stacks"], prof["channels"], prof["dies_per_channel"],
+                            prof["planes_per_die"], 4096, prof["page_bytes"])
+    timing = ho.Timing(3, 1, prof["read_latency_ns"], prof["program_latency_ns"],
+                       prof["aggregate_bandwidth_bytes_per_s"], prof["page_bytes"])
+    chans = cfg["stacks"] * prof["channels"]
+    bw = prof["channel_width_bits"] * prof["channel_transfer_rate_mtps"] * 1_000_000 // 8
+    state = np.zeros(chans * (prof["dies_per_channel"] + 1), np.uint64)
+    done, _, status, _ = ho.run_batch(ranges, 1, geom, timing, np.full(chans, bw, np.uint64),
+                                      np.full(cfg["stacks"], prof["read_latency_ns"], np.uint64),
+                                      np.full(cfg["stacks"], prof["program_latency_ns"],
+                                              np.uint64), a, b, o, t, state)
+    dec = ho.decode(ranges, 1, geom, a, b, o)
+    msgs = linked_messages(dec["stack"], t, done, status == 1)
+    p = cfg["profile"]
+    linked = [int(x) for x in done]
+    ar = [-1] * cfg["n"]
+    for stack, m in sorted(msgs.items()):
+        text = (f"{p['gt']} {p['ar']} {p['r']} {p['accepted']} {p['prop']} "
+                f"{p['consume'][0]} {p['consume'][1]} {len(m)}\n" +
+                "".join(f"{d} {r}\n" for r, d, _ in m))
+        out = subprocess.run([str(REF_LINK)], input=text, check=True, capture_output=True,
+                             text=True).stdout.split("\n")
+        for (ready, d, i), tick in zip(m, out[:len(m)]):
+            if d == 1:
+                linked[i] = int(tick)
+            else:
+                ar[i] = int(tick)
+    (HERE / "linked_goldens.json").write_text(json.dumps(
+        dict(cfg, die_done=[int(x) for x in done], status=[int(x) for x in status],
+             linked_done=linked, ar_delivered=ar)))
+
+
 GENERATORS = {"device": device_goldens, "thermal": thermal_goldens, "lru": lru_goldens,
               "retention": retention_goldens, "prefetch": prefetch_goldens,
-              "link": link_goldens, "layout": layout_goldens, "clock": clock_goldens}
+              "link": link_goldens, "layout": layout_goldens, "clock": clock_goldens,
+              "linked": linked_goldens}
 
 
 def main() -> int:

@@ -223,3 +223,30 @@ def activity_of(setup, oracle, arrays, status):
     rb = np.bincount(idx, weights=np.where(op[m] == 0, nbytes[m], 0), minlength=size)
     wr = np.bincount(idx, weights=(op[m] == 1), minlength=size)
     return rb.astype(np.uint64), wr.astype(np.uint64)
+
+
+def oracle_linked(setup, oracle_run, arrays, profile: dict):
+    """The die model (the oracle run `oracle_run` of `setup`) composed with
+    each stack's UCIe link (the oracle's StreamingLink, or_link_run): per
+    modeled access an AR at its arrival and an R at its die completion on
+    its stack's link, in ready order (AR first at equal ticks, then batch
+    order).  Returns (linked done, die done, status, AR delivery or -1)."""
+    address, nbytes, op, arrival = arrays
+    done, _, status, _ = oracle_run.run(*arrays, threads=8)
+    dec = ho.decode(oracle_run.ranges, oracle_run.count, oracle_run.geometry, address, nbytes, op)
+    modeled = np.flatnonzero(status == 1)
+    linked = done.copy()
+    ar = np.full(done.size, -1, np.int64)
+    for stack in range(setup.stacks):
+        idx = modeled[dec["stack"][modeled] == stack]
+        if idx.size == 0:
+            continue
+        ready = np.concatenate([arrival[idx], done[idx]])
+        kind = np.concatenate([np.zeros(idx.size, np.uint8), np.ones(idx.size, np.uint8)])
+        who = np.concatenate([idx, idx])
+        order = np.lexsort((who, kind, ready))
+        delivered = ho.link_run(profile, kind[order], ready[order])[0]
+        r = kind[order] == 1
+        linked[who[order][r]] = delivered[r]
+        ar[who[order][~r]] = delivered[~r].astype(np.int64)
+    return linked, done, status, ar

@@ -93,3 +93,57 @@ def test_out_of_order_link_and_bad_profile():
     bad["profile"] = dict(cases[0]["profile"], gt=64)
     with pytest.raises(HbfsimError):
         run([bad])
+
+
+def _linked_gpu(tmp, stacks, arrays, profile):
+    from helpers import Setup, make_context, to_device
+    from hbfsim_b200 import submit_linked
+    from hbfsim_b200 import workloads as wl
+    p = wl.c0_profile()
+    s = Setup(profile=p, model=3, stacks=stacks, stripe=4096)
+    s.ranges = [(wl.RANGE_BASE, p["capacity_bytes"] - (1 << 20), 1, 3)]
+    ctx = make_context(s, tmp)
+    dev = to_device(arrays)
+    profs = link_profiles(stacks, profile["gt"], profile["ar"], profile["r"],
+                          profile["accepted"], profile["prop"], [profile["consume"]] * stacks)
+    out, die, res, ar = submit_linked(ctx, *dev, profs, stacks)
+    got = (out.done_ns.cpu().numpy().view(np.uint64), die.done_ns.cpu().numpy().view(np.uint64),
+           out.status.cpu().numpy(), ar.cpu().numpy())
+    assert (res["status"] == 0).all()
+    ctx.close()
+    return s, got
+
+
+def test_linked_stage_against_reference_link(tmp_path):
+    """Accesses through the die model and then their stack's UCIe link (AR
+    at the arrival, R at the die completion): every R and AR delivery equal
+    to the reference StreamingLink's on the same messages
+    (tests/golden/linked_goldens.json)."""
+    from hbfsim_b200 import workloads as wl
+    g = json.loads((GOLDEN.parent / "linked_goldens.json").read_text())
+    p = wl.c0_profile()
+    arrays = wl.c0_trace(g["n"], seed=g["seed"], range_length=p["capacity_bytes"] - (1 << 20))
+    _, (linked, done, status, ar) = _linked_gpu(str(tmp_path), g["stacks"], arrays,
+                                                g["profile"])
+    assert done.tolist() == g["die_done"]
+    assert status.tolist() == g["status"]
+    assert linked.tolist() == g["linked_done"]
+    assert ar.tolist() == g["ar_delivered"]
+
+
+def test_linked_stage_matches_oracle(tmp_path):
+    """A larger trace on 4 stacks (4 links), against the oracle's die model
+    and link composed the same way."""
+    from helpers import OracleRun, oracle_linked
+    from hbfsim_b200 import workloads as wl
+    p = wl.c0_profile()
+    arrays = wl.c0_trace(120_000, seed=8, range_length=p["capacity_bytes"] - (1 << 20))
+    profile = {"gt": 32, "ar": 12, "r": 56, "accepted": 8, "prop": 3, "consume": [0, 5]}
+    s, (linked, done, status, ar) = _linked_gpu(str(tmp_path), 4, arrays, profile)
+    want = oracle_linked(s, OracleRun(s), arrays, profile)
+    assert np.array_equal(done, want[1])
+    assert np.array_equal(status, want[2])
+    bad = np.flatnonzero(linked != want[0])
+    assert bad.size == 0, f"linked completion differs at {bad[:5]}"
+    assert np.array_equal(ar, want[3])
+    assert (linked >= done).all()

@@ -382,3 +382,22 @@ def test_clock_oracle_against_reference_cache(golden_dir):
         assert np.array_equal(hit, np.array(case["hit"], np.uint8)), case["kind"]
         assert np.array_equal(victim, np.array(case["victim"], np.uint64)), case["kind"]
         assert np.array_equal(dirty, np.array(case["victim_dirty"], np.uint8)), case["kind"]
+
+
+def test_linked_stage_oracle_against_reference_link(golden_dir):
+    """The die model followed by each stack's UCIe link, composed with the
+    oracle's link (or_link_run) the way tests/golden/linked_goldens.json
+    composes the reference StreamingLink: every access's R and AR delivery."""
+    from helpers import OracleRun, Setup, oracle_linked
+    from hbfsim_b200 import workloads as wl
+    with open(golden_dir / "linked_goldens.json") as f:
+        g = json.load(f)
+    p = wl.c0_profile()
+    s = Setup(profile=p, model=3, stacks=g["stacks"], stripe=4096)
+    s.ranges = [(wl.RANGE_BASE, p["capacity_bytes"] - (1 << 20), 1, 3)]
+    arrays = wl.c0_trace(g["n"], seed=g["seed"], range_length=p["capacity_bytes"] - (1 << 20))
+    linked, done, status, ar = oracle_linked(s, OracleRun(s), arrays, g["profile"])
+    assert done.tolist() == g["die_done"]
+    assert status.tolist() == g["status"]
+    assert linked.tolist() == g["linked_done"]
+    assert ar.tolist() == g["ar_delivered"]
