@@ -1177,7 +1177,7 @@ direct_pass_kernel(const PassArgs args)
 constexpr u32 kFastTile = 2048;
 constexpr u32 kFastRounds = kFastTile / kThreads;  // rounds of 32 per warp
 
-template <int D>
+template <int D, bool GENERAL = false>
 __global__ void __launch_bounds__(kThreads, 3)
 direct_fast_kernel(const PassArgs args)
 {
@@ -1190,6 +1190,10 @@ direct_fast_kernel(const PassArgs args)
     i64* s_col0 = reinterpret_cast<i64*>(smem + A.off_pm);  // [C][K]
     u32* s_part = reinterpret_cast<u32*>(s.red);            // per-warp channel totals
     prologue(A, s, true, false, false);
+    // GENERAL: the activity of this tile (layout_fast puts it beside the
+    // per-warp counts), flushed to the staging counters per tile
+    const bool activity = GENERAL && A.tp.act_stage != nullptr;
+    unsigned long long* act = reinterpret_cast<unsigned long long*>(smem + A.off_act);
 
     ColumnItems<D> items;
     items.init(C);
@@ -1232,12 +1236,15 @@ direct_fast_kernel(const PassArgs args)
         return static_cast<u32>(A.n - start < T ? A.n - start : T);
     };
     const u64 tile_first = static_cast<u64>(blockIdx.x) * A.tiles_per_cta;
-    if (tile_first * T < A.n) stage(tile_first * T, tile_size(tile_first * T));
+    if (!GENERAL && tile_first * T < A.n) stage(tile_first * T, tile_size(tile_first * T));
     for (u32 tt = 0; tt < A.tiles_per_cta; ++tt) {
         const u64 start = (tile_first + tt) * T;
         if (start >= A.n) break;
         const u32 nt = tile_size(start);
+        if (GENERAL) stage(start, nt);  // the chains' die words overlay the staged addresses
         for (u32 k = lane; k <= C; k += 32) wc[k] = 0;
+        if (activity)
+            for (u32 k = tid; k < 2 * C * D; k += kThreads) act[k] = 0;
         const u64 tile_prev = tid == 0 ? (start > 0 ? A.arrival[start - 1] : *A.last_arrival) : 0;
         cp_async_wait_all();
         __syncthreads();
@@ -1256,24 +1263,49 @@ direct_fast_kernel(const PassArgs args)
                 unsorted |= arr < prev;
                 const u32 b = s.bytes[e];
                 const u32 o = s.op[e];
-                const u64 off = a - rg.base;  // wraps when a < base
-                if (b == 0) {                 // hbf_device.cu:997-1003
-                } else if (off >= rg.length) {
-                    // below the range: unsupported if it straddles into it
-                    status = a < rg.base && a <= ~u64{0} - b && rg.base < a + b ? kUnsupported
-                                                                                 : kBypass;
-                } else if (o <= 1 && ((rg.allowed >> o) & 1u) && b <= rg.length - off &&
-                           (off & rg.page_mask) + b <= rg.page_mask + 1) {
-                    const u32 u = static_cast<u32>((rg.file_offset + off) >> A.dp.stripe_shift);
-                    const u32 g = (u >> A.dp.chan_shift) & A.dp.chan_mask;
-                    if ((g & A.dp.shard_mask) == A.dp.shard_rank) {
-                        status = kModeled;
-                        key = g >> A.dp.shard_shift;
+                if (GENERAL) {
+                    // the general classification (ranges read through the
+                    // cache), the channel's own transfer rate, activity
+                    const TimingDecoded d = rg.valid ? classify_single(rg, A.dp, a, b, o)
+                                                     : classify_timing(A.dp, a, b, o);
+                    status = d.status;
+                    if (d.status == kModeled) {
+                        key = d.local;
                         const u32 xs = A.tp.x_shift;
-                        info = ((b + ((1u << xs) - 1u)) >> xs) * A.tp.time_scale |
-                               ((u >> A.dp.die_shift) & A.dp.die_mask) << 24 | (o & 1u) << 28;
-                    } else {
-                        status = kForeign;
+                        const u64 x = xs != kXDivide
+                                          ? static_cast<u64>(static_cast<u32>(
+                                                (static_cast<u64>(b) + ((u64{1} << xs) - 1)) >> xs)) *
+                                                A.tp.time_scale
+                                          : transfer_ticks(b, s.chan[key], A.tp.time_scale);
+                        if (x > 0xffffffull) atomicOr(A.error, kErrNeedSeq);
+                        info = static_cast<u32>(x & 0xffffffull) | d.die << 24 | (o & 1u) << 28;
+                        if (activity) {
+                            if (o) atomicAdd(&act[2 * (key * D + d.die) + 1], 1ull);
+                            else atomicAdd(&act[2 * (key * D + d.die)],
+                                           static_cast<unsigned long long>(b));
+                        }
+                    }
+                } else {
+                    const u64 off = a - rg.base;  // wraps when a < base
+                    if (b == 0) {                 // hbf_device.cu:997-1003
+                    } else if (off >= rg.length) {
+                        // below the range: unsupported if it straddles into it
+                        status = a < rg.base && a <= ~u64{0} - b && rg.base < a + b
+                                     ? kUnsupported : kBypass;
+                    } else if (o <= 1 && ((rg.allowed >> o) & 1u) && b <= rg.length - off &&
+                               (off & rg.page_mask) + b <= rg.page_mask + 1) {
+                        const u32 u =
+                            static_cast<u32>((rg.file_offset + off) >> A.dp.stripe_shift);
+                        const u32 g = (u >> A.dp.chan_shift) & A.dp.chan_mask;
+                        if ((g & A.dp.shard_mask) == A.dp.shard_rank) {
+                            status = kModeled;
+                            key = g >> A.dp.shard_shift;
+                            const u32 xs = A.tp.x_shift;
+                            info = ((b + ((1u << xs) - 1u)) >> xs) * A.tp.time_scale |
+                                   ((u >> A.dp.die_shift) & A.dp.die_mask) << 24 | (o & 1u) << 28;
+                        } else {
+                            status = kForeign;
+                        }
                     }
                 }
             }
@@ -1335,7 +1367,8 @@ direct_fast_kernel(const PassArgs args)
             if (key < C) {
                 pos = wc[key] + (kr[j] >> 16);
                 s.sinfo[pos + key] = info;
-                s.sarr[pos + key] = static_cast<i64>(s.arr[e]);
+                s.sarr[pos + key] = GENERAL ? imax(static_cast<i64>(s.arr[e]), s.chan[key].admit)
+                                            : static_cast<i64>(s.arr[e]);
             }
             __stcs(reinterpret_cast<unsigned long long*>(A.latency + start + e),
                    static_cast<u64>(info) | static_cast<u64>(pos) << 32 |
@@ -1347,7 +1380,10 @@ direct_fast_kernel(const PassArgs args)
         // ---- the staging buffers are free: stream the next tile in while
         // the chains run
         const u64 next = start + T;
-        if (tt + 1 < A.tiles_per_cta && next < A.n) stage(next, tile_size(next));
+        if (!GENERAL && tt + 1 < A.tiles_per_cta && next < A.n) stage(next, tile_size(next));
+        if (activity)
+            for (u32 k = tid; k < 2 * C * D; k += kThreads)
+                if (act[k]) atomicAdd(&A.tp.act_stage[k], act[k]);
         items.replay(s, sd, rel32, A.tp.step_max);
         __syncthreads();
         if (!couple_now(tt) && tt + 1 < A.tiles_per_cta && start + T < A.n) continue;
@@ -1898,7 +1934,7 @@ static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
 // inputs, the channel-sorted copy in buffers of its own (so that the next
 // tile's inputs can stream in while the chains read the sorted copy),
 // per-warp counts, segment starts, the channel table, the column-0 snapshot.
-static u32 layout_fast(PassArgs& a, u32 C, u32 K)
+static u32 layout_fast(PassArgs& a, u32 C, u32 K, bool general = false)
 {
     u32 off = 0;
     auto take = [&](u32 bytes) {
@@ -1923,12 +1959,24 @@ static u32 layout_fast(PassArgs& a, u32 C, u32 K)
     const u32 wc_bytes = align_up(4 * kWarps * (C + 1), 16);
     const u32 red_bytes = 8 * 8 * kWarps;
     const u32 dies_bytes = 4 * (K - 1) * kThreads;
+    a.off_key = a.off_rank = a.off_ord = a.off_act = a.off_ranges = 0;
+    if (general) {
+        // no prefetch: the die words overlay the staged addresses (dead once
+        // decoded); the tile's activity (flushed before the chains) and the
+        // column-0 snapshot (taken after them) share a slot
+        const u32 pm_bytes = align_up(8 * C * K, 16), act_bytes = 16 * C * (K - 1);
+        a.off_wcnt = take(wc_bytes + red_bytes + (pm_bytes > act_bytes ? pm_bytes : act_bytes));
+        a.off_red = a.off_wcnt + wc_bytes;
+        a.off_pm = a.off_red + red_bytes;
+        a.off_act = a.off_pm;
+        a.off_dies[0] = a.off_addr;
+        return align_up(off, 16);
+    }
     const u32 shared = wc_bytes + red_bytes + 8 * C * K;
     a.off_wcnt = take(shared > dies_bytes ? shared : dies_bytes);
     a.off_red = a.off_wcnt + wc_bytes;
     a.off_pm = a.off_red + red_bytes;
     a.off_dies[0] = a.off_wcnt;
-    a.off_key = a.off_rank = a.off_ord = a.off_act = a.off_ranges = 0;
     return align_up(off, 16);
 }
 
@@ -2038,33 +2086,41 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
         using Kernel = void (*)(const PassArgs);
         Kernel p1 = fast ? timing_pass_kernel<kModelFast, 1> : timing_pass_kernel<kModelDie, 1>;
         Kernel p2 = fast ? timing_pass_kernel<kModelFast, 2> : timing_pass_kernel<kModelDie, 2>;
-        bool fast_p1 = false;
+        bool fast_p1 = false, general_p1 = false;
         if (plan.direct) {
             // the specialized decode: one range, power-of-two geometry, one
             // transfer shift, no activity counting
             const bool f = dp.one.valid && dp.pow2 && tp.x_shift != kXDivide && !tp.act_stage &&
                            tp.admit_zero;
             const bool f2 = f && plan.T == kFastTile;  // direct_fast_kernel's fixed tile
-            fast_p1 = f2;
+            // its general instantiation: any ranges, activity, admission
+            // delays and per-channel rates, for batches in arrival order
+            const bool g2 = !f2 && plan.T == kFastTile && !tp.any_order;
+            fast_p1 = f2 || g2;
+            general_p1 = g2;
             const bool z = tp.admit_zero != 0;
             switch (plan.dies) {
             case 1:
                 p1 = f2  ? direct_fast_kernel<1>
+                     : g2 ? direct_fast_kernel<1, true>
                      : f ? direct_pass_kernel<1, 1, true> : direct_pass_kernel<1, 1, false>;
                 p2 = z ? direct_replay_kernel<1, true> : direct_replay_kernel<1, false>;
                 break;
             case 2:
                 p1 = f2  ? direct_fast_kernel<2>
+                     : g2 ? direct_fast_kernel<2, true>
                      : f ? direct_pass_kernel<1, 2, true> : direct_pass_kernel<1, 2, false>;
                 p2 = z ? direct_replay_kernel<2, true> : direct_replay_kernel<2, false>;
                 break;
             case 4:
                 p1 = f2  ? direct_fast_kernel<4>
+                     : g2 ? direct_fast_kernel<4, true>
                      : f ? direct_pass_kernel<1, 4, true> : direct_pass_kernel<1, 4, false>;
                 p2 = z ? direct_replay_kernel<4, true> : direct_replay_kernel<4, false>;
                 break;
             default:
                 p1 = f2  ? direct_fast_kernel<8>
+                     : g2 ? direct_fast_kernel<8, true>
                      : f ? direct_pass_kernel<1, 8, true> : direct_pass_kernel<1, 8, false>;
                 p2 = z ? direct_replay_kernel<8, true> : direct_replay_kernel<8, false>;
                 break;
@@ -2073,7 +2129,7 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
         // direct_fast_kernel runs on a layout of its own
         PassArgs a1 = a;
         u32 smem1 = plan.smem_bytes;
-        if (fast_p1) smem1 = layout_fast(a1, plan.C, plan.K);
+        if (fast_p1) smem1 = layout_fast(a1, plan.C, plan.K, general_p1);
         err = cudaFuncSetAttribute(p1, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(smem1));
         if (err != cudaSuccess) return err;
