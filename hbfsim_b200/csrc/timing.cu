@@ -392,9 +392,29 @@ __device__ __forceinline__ bool replay_rel32(DieRegs<D>& reg, int* sd, i64* sarr
                                              const ChanInfo& ci, i64 step_max)
 {
     constexpr i64 kWindow = i64{1} << 30;
-    if (reg.chan < kNeg / 2 && !REAL) return false;
+    // Unit replay with the channel word at -inf (a die column before any
+    // access of its die): B is the smallest finite word instead, so every
+    // finite word starts at or above 0, and the -inf words start at
+    // kNegWord, far enough below 0 that the segment's steps cannot bring
+    // them near it (they stay -inf and keep their 64-bit value).  Nothing
+    // to do when every word is -inf.
+    constexpr int kNegWord = -(1 << 30);
+    const bool neg_chan = !REAL && reg.chan < kNeg / 2;
     bool arrivals = REAL;
     i64 B = reg.chan, hi = 0;
+    if (neg_chan) {
+        i64 lo = 0;
+        bool any = false;
+#pragma unroll
+        for (int j = 0; j < D; ++j) {
+            if (reg.die[j] < kNeg / 2) continue;
+            lo = any ? (reg.die[j] < lo ? reg.die[j] : lo) : reg.die[j];
+            any = true;
+        }
+        if (!any) return true;
+        if (static_cast<i64>(last - first + 1) * step_max >= (i64{1} << 29)) return false;
+        B = lo;
+    }
     if (REAL) {
         const i64 a_first = sarr[first], a_last = sarr[last - 1];
         B = imax(a_first, reg.chan);
@@ -405,16 +425,27 @@ __device__ __forceinline__ bool replay_rel32(DieRegs<D>& reg, int* sd, i64* sarr
         hi = a_last - B;
     }
     int rc, rd[D];
-    {
-        const i64 v = reg.chan - B;
-        hi = imax(hi, v);
-        rc = v < 0 ? -1 : static_cast<int>(v);
-    }
+    if (neg_chan) {
+        rc = kNegWord;
 #pragma unroll
-    for (int j = 0; j < D; ++j) {
-        const i64 v = reg.die[j] - B;
-        hi = imax(hi, v);
-        rd[j] = v < 0 ? -1 : static_cast<int>(v);
+        for (int j = 0; j < D; ++j) {
+            const bool fin = reg.die[j] >= kNeg / 2;
+            const i64 v = fin ? reg.die[j] - B : 0;
+            hi = imax(hi, v);
+            rd[j] = fin ? static_cast<int>(v) : kNegWord;
+        }
+    } else {
+        {
+            const i64 v = reg.chan - B;
+            hi = imax(hi, v);
+            rc = v < 0 ? -1 : static_cast<int>(v);
+        }
+#pragma unroll
+        for (int j = 0; j < D; ++j) {
+            const i64 v = reg.die[j] - B;
+            hi = imax(hi, v);
+            rd[j] = v < 0 ? -1 : static_cast<int>(v);
+        }
     }
     if (hi + static_cast<i64>(last - first + 1) * step_max >= (i64{1} << 31)) return false;
     const int t_read = static_cast<int>(ci.t_read), t_prog = static_cast<int>(ci.t_prog);
@@ -431,7 +462,7 @@ __device__ __forceinline__ bool replay_rel32(DieRegs<D>& reg, int* sd, i64* sarr
         else
             rel32_loop_regs<D, false, WRITE>(rc, rd, sarr, sinfo, first, last, B, t_read, t_prog);
     }
-    reg.chan = B + rc;
+    if (rc >= 0 || !neg_chan) reg.chan = B + rc;  // a -inf channel word stays -inf
 #pragma unroll
     for (int j = 0; j < D; ++j)
         if (rd[j] >= 0) reg.die[j] = B + rd[j];
@@ -1256,6 +1287,7 @@ direct_fast_kernel(const PassArgs args)
         for (u32 j = 0; j < kFastRounds; ++j) {
             const u32 e = warp * (T / kWarps) + j * 32 + lane;
             u32 key = C, status = kUnsupported, info = 0;
+            u32 act_slot = 0xffffffffu, act_add = 0;  // GENERAL: activity counter, amount
             if (e < nt) {
                 const u64 a = s.addr[e];
                 const u64 arr = s.arr[e];
@@ -1279,11 +1311,8 @@ direct_fast_kernel(const PassArgs args)
                                           : transfer_ticks(b, s.chan[key], A.tp.time_scale);
                         if (x > 0xffffffull) atomicOr(A.error, kErrNeedSeq);
                         info = static_cast<u32>(x & 0xffffffull) | d.die << 24 | (o & 1u) << 28;
-                        if (activity) {
-                            if (o) atomicAdd(&act[2 * (key * D + d.die) + 1], 1ull);
-                            else atomicAdd(&act[2 * (key * D + d.die)],
-                                           static_cast<unsigned long long>(b));
-                        }
+                        act_slot = 2 * (key * D + d.die) + (o & 1u);
+                        act_add = o & 1u ? 1u : b;
                     }
                 } else {
                     const u64 off = a - rg.base;  // wraps when a < base
@@ -1308,6 +1337,16 @@ direct_fast_kernel(const PassArgs args)
                         }
                     }
                 }
+            }
+            if (activity) {
+                // one shared-memory atomic per group of lanes with the same
+                // counter and amount (runs of accesses to one die would
+                // otherwise serialize on it)
+                const u64 tag = static_cast<u64>(act_add) << 32 | act_slot;
+                const u32 same = __match_any_sync(0xffffffffu, tag);
+                if (act_slot != 0xffffffffu && (same & lanes_below) == 0)
+                    atomicAdd(&act[act_slot], static_cast<unsigned long long>(act_add) *
+                                                   static_cast<unsigned long long>(__popc(same)));
             }
             const u32 peers = __match_any_sync(0xffffffffu, key);
             const u32 before = __popc(peers & lanes_below);
