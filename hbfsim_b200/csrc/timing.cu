@@ -1590,11 +1590,11 @@ direct_replay_kernel(const PassArgs args)
 
 // Range scan: incoming_b = R_{b-1} ... R_0 (state), one CTA per local
 // channel (channels are independent).  Each range aggregate R is a max-plus
-// affine map x -> max(R[:, :K] + x, R[:, K]) (K state words).  The CTA's 8
+// affine map x -> max(R[:, :K] + x, R[:, K]) (K state words).  The CTA's 32
 // warps split the ranges into 8 groups:
 //   A  each warp composes its group into one map (one lane per entry,
 //      clamping sums below -2^61 back to NEG so that they cannot overflow);
-//   B  warp 0 applies the 8 group maps to the carried state, giving each
+//   B  warp 0 applies the 32 group maps to the carried state, giving each
 //      group its incoming state (and the batch's final state);
 //   C  each warp walks its group from that state (lane i = state word i,
 //      shuffles), writing every range's incoming state.
@@ -1619,7 +1619,7 @@ struct ScanArgs {
     unsigned long long* die_writes;
 };
 
-constexpr u32 kScanWarps = 8;
+constexpr u32 kScanWarps = 32;
 
 // 8-byte global -> shared copy (cp.async.ca; both addresses 8-byte aligned).
 __device__ __forceinline__ void cp_async8(void* smem_dst, const void* gmem_src)
@@ -1664,7 +1664,7 @@ __global__ void __launch_bounds__(kScanWarps * 32) range_scan_kernel(const ScanA
     const u32 n = a.ctas, span = a.chunk * per + per;
     i64* stage = reinterpret_cast<i64*>(smem) + static_cast<u64>(warp) * span;
     i64* comp = stage + static_cast<u64>(a.chunk) * per;  // the group's composite
-    i64* gin = reinterpret_cast<i64*>(smem) + static_cast<u64>(kScanWarps) * span;  // [8][K]
+    i64* gin = reinterpret_cast<i64*>(smem) + static_cast<u64>(kScanWarps) * span;  // [warps][K]
     const u32 g0 = static_cast<u32>(static_cast<u64>(n) * warp / kScanWarps);
     const u32 g1 = static_cast<u32>(static_cast<u64>(n) * (warp + 1) / kScanWarps);
 
