@@ -87,6 +87,12 @@ struct CapacityState {
     u8* clk_ref = nullptr;
     u8* clk_dirty = nullptr;
     u64* clk_state = nullptr;
+    // single-pass scans (look-back): per tile a tagged status word, the
+    // tile ticket counter and an error word; the tag of the current scan
+    unsigned long long* lb_state = nullptr;
+    std::uint64_t lb_tiles = 0;
+    u32* lb_misc = nullptr;          // [0] ticket counter, [1] error
+    std::uint32_t lb_tag = 0;
     // counters (host)
     std::uint64_t calls = 0, accesses = 0, hits = 0, misses = 0, evictions = 0,
                   dirty_evictions = 0;
@@ -152,12 +158,103 @@ __device__ __forceinline__ u32 block_scan(u32 v, u32* total)
     return excl;
 }
 
-// Scan of one tile of kTile elements per CTA; tile totals to `sums`.
-template <class Op>
-__global__ void __launch_bounds__(kT) scan_tile_kernel(const u32* in, u32* out, u64 n, u32* sums,
-                                                       int inclusive)
+// ---------------------------------------------------------------- look-back
+// Single-pass scans (decoupled look-back, Merrill & Garland, "Single-pass
+// Parallel Prefix Scan with Decoupled Look-back", 2016).  Each CTA takes the
+// next tile ticket (so a tile only waits on tiles that already run), scans
+// its tile, publishes its aggregate, then walks back over its predecessors'
+// published words -- adding aggregates until it meets an inclusive prefix --
+// and publishes its own inclusive prefix.  A status word is
+//   tag << 34 | kind << 32 | value    (kind 1 aggregate, 2 inclusive)
+// with the scan's tag, so that words of earlier scans never match and the
+// array needs no clearing.  Every wait is bounded: after kLookbackSpins
+// polls the CTA records an error (the host reports it) and goes on.
+struct LookBack {
+    unsigned long long* state;
+    u32* misc;   // [0] ticket counter (reset by the last ticket), [1] error
+    u32 tag;
+    u32 tiles;
+};
+
+constexpr u32 kLookbackSpins = 1u << 22;
+
+__device__ __forceinline__ void lb_publish(const LookBack& lb, u32 tile, u32 kind, u32 value)
 {
-    const u64 base = static_cast<u64>(blockIdx.x) * kTile + threadIdx.x * kItems;
+    const unsigned long long w = static_cast<unsigned long long>(lb.tag) << 34 |
+                                 static_cast<unsigned long long>(kind) << 32 | value;
+    atomicExch(lb.state + tile, w);
+}
+
+// Exclusive prefix of `tile` under Op, called by one whole warp (the result
+// in every lane).  The warp reads a window of the 32 preceding status words
+// at once, lane k the word of tile - 1 - k; once all are published it folds
+// the aggregates up to the nearest inclusive prefix, or all 32 and moves the
+// window back.
+template <class Op>
+__device__ __forceinline__ u32 lb_prefix(const LookBack& lb, u32 tile)
+{
+    u32 prefix = Op::id;
+    int j = static_cast<int>(tile) - 1;
+    bool failed = false;
+    while (j >= 0) {
+        const int idx = j - static_cast<int>(lane());
+        u32 kind = 2u, value = Op::id;  // before tile 0: the identity, inclusive
+        if (idx >= 0) {
+            const volatile unsigned long long* w =
+                reinterpret_cast<volatile unsigned long long*>(lb.state + idx);
+            unsigned long long x = *w;
+            u32 spins = 0;
+            while (!((x >> 34) == lb.tag && ((x >> 32) & 3u) != 0)) {
+                if (++spins >= kLookbackSpins) {
+                    failed = true;
+                    break;
+                }
+                __nanosleep(32);
+                x = *w;
+            }
+            kind = failed ? 2u : static_cast<u32>((x >> 32) & 3u);
+            value = failed ? Op::id : static_cast<u32>(x);
+        }
+        const u32 incl = __ballot_sync(0xffffffffu, kind == 2u);
+        const u32 last = incl ? static_cast<u32>(__ffs(incl)) - 1u : 31u;
+        u32 v = lane() <= last ? value : Op::id;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v = Op::f(v, __shfl_xor_sync(0xffffffffu, v, o));
+        prefix = Op::f(v, prefix);
+        if (incl) break;
+        j -= 32;
+    }
+    if (__any_sync(0xffffffffu, failed) && lane() == 0) atomicExch(&lb.misc[1], 1u);
+    return prefix;
+}
+
+// The tile ticket of this CTA, broadcast through shared memory.  A ticket
+// past the last tile (a counter not reset) is recorded as an error; the
+// caller's CTA then does nothing.
+__device__ __forceinline__ u32 lb_ticket(const LookBack& lb, u32* slot)
+{
+    if (threadIdx.x == 0) {
+        const u32 t = atomicAdd(&lb.misc[0], 1u);
+        if (t >= lb.tiles) atomicExch(&lb.misc[1], 1u);
+        *slot = t;
+    }
+    __syncthreads();
+    return *slot;
+}
+
+__device__ __forceinline__ void lb_done(const LookBack& lb, u32 tile)
+{
+    if (threadIdx.x == 0 && tile + 1 == lb.tiles) lb.misc[0] = 0;  // every ticket is taken
+}
+
+template <class Op>
+__global__ void __launch_bounds__(kT) lb_scan_kernel(const u32* in, u32* out, u64 n,
+                                                     int inclusive, u32* total, LookBack lb)
+{
+    __shared__ u32 ticket, prefix_s;
+    const u32 tile = lb_ticket(lb, &ticket);
+    if (tile >= lb.tiles) return;
+    const u64 base = static_cast<u64>(tile) * kTile + threadIdx.x * kItems;
     u32 v[kItems];
     u32 run = Op::id;
 #pragma unroll
@@ -165,48 +262,31 @@ __global__ void __launch_bounds__(kT) scan_tile_kernel(const u32* in, u32* out, 
         v[k] = base + k < n ? in[base + k] : Op::id;
         run = Op::f(run, v[k]);
     }
-    u32 total;
-    u32 pre = block_scan<Op>(run, &total);
+    u32 agg;
+    u32 pre = block_scan<Op>(run, &agg);
+    if (threadIdx.x < 32) {
+        u32 prefix = Op::id;
+        if (tile == 0) {
+            if (threadIdx.x == 0) lb_publish(lb, 0, 2u, agg);
+        } else {
+            if (threadIdx.x == 0) lb_publish(lb, tile, 1u, agg);
+            prefix = lb_prefix<Op>(lb, tile);
+            if (threadIdx.x == 0) lb_publish(lb, tile, 2u, Op::f(prefix, agg));
+        }
+        if (threadIdx.x == 0) {
+            prefix_s = prefix;
+            if (total && tile + 1 == lb.tiles) *total = Op::f(prefix, agg);
+            lb_done(lb, tile);
+        }
+    }
+    __syncthreads();
+    pre = Op::f(prefix_s, pre);
 #pragma unroll
     for (u32 k = 0; k < kItems; ++k) {
         const u32 x = v[k];
         if (base + k < n) out[base + k] = inclusive ? Op::f(pre, x) : pre;
         pre = Op::f(pre, x);
     }
-    if (threadIdx.x == 0) sums[blockIdx.x] = total;
-}
-
-template <class Op>
-__global__ void __launch_bounds__(kT) scan_fix_kernel(u32* out, u64 n, const u32* offsets)
-{
-    const u64 base = static_cast<u64>(blockIdx.x) * kTile;
-    const u32 off = offsets[blockIdx.x];
-    for (u32 k = threadIdx.x; k < kTile; k += kT)
-        if (base + k < n) out[base + k] = Op::f(off, out[base + k]);
-}
-
-// Device-wide scan (exclusive or inclusive; in place allowed), recursive
-// over the tile sums.  `scratch` holds 2 words per tile per level.
-template <class Op>
-cudaError_t scan(const u32* in, u32* out, u64 n, bool inclusive, u32* scratch, cudaStream_t s)
-{
-    if (n == 0) return cudaSuccess;
-    const u64 tiles = (n + kTile - 1) / kTile;
-    u32* sums = scratch;
-    scan_tile_kernel<Op><<<static_cast<unsigned>(tiles), kT, 0, s>>>(in, out, n, sums,
-                                                                      inclusive ? 1 : 0);
-    if (tiles == 1) return cudaGetLastError();
-    // exclusive scan of the tile sums, then add them back
-    u32* sums_scanned = scratch + tiles;
-    const cudaError_t e = scan<Op>(sums, sums_scanned, tiles, false, scratch + 2 * tiles, s);
-    if (e != cudaSuccess) return e;
-    scan_fix_kernel<Op><<<static_cast<unsigned>(tiles), kT, 0, s>>>(out, n, sums_scanned);
-    return cudaGetLastError();
-}
-
-__global__ void total_kernel(const u32* excl_scan, const u32* in, u64 n, u32* total)
-{
-    if (threadIdx.x == 0 && blockIdx.x == 0) *total = n ? excl_scan[n - 1] + in[n - 1] : 0u;
 }
 
 // ---------------------------------------------------------------- classify
@@ -362,57 +442,121 @@ __global__ void value_kernel(const u32* prev, u64 m, u32* v)
     if (i < m) v[i] = prev[i] == kNone ? 0u : prev[i] + 1u;
 }
 
-__global__ void __launch_bounds__(kT) wm_zero_count_kernel(const u32* v, u64 m, u32 bit,
-                                                           u32* zeros)
+// Zeros of every bit over all values (order-independent: each level's
+// total zeros), one pass.
+__global__ void __launch_bounds__(kT) wm_bit_zeros_kernel(const u32* v, u64 m, u32 bits,
+                                                          u32* zeros)
 {
-    const u64 base = static_cast<u64>(blockIdx.x) * kTile;
-    u32 z = 0;
-    for (u32 k = threadIdx.x; k < kTile; k += kT)
-        if (base + k < m) z += ((v[base + k] >> bit) & 1u) == 0;
-    u32 total;
-    block_scan<AddOp>(z, &total);
-    if (threadIdx.x == 0) zeros[blockIdx.x] = total;
-}
-
-__global__ void __launch_bounds__(kT) wm_split_kernel(const u32* v, u64 m, u32 bit,
-                                                      const u32* zeros_before,
-                                                      const u32* total_zeros, u32* out,
-                                                      uint2* level)
-{
-    __shared__ u32 warp_ones[kT / 32];
-    const u64 base = static_cast<u64>(blockIdx.x) * kTile;
-    const u32 Z = *total_zeros;
-    u32 ob = static_cast<u32>(base) - zeros_before[blockIdx.x];  // ones before i
-    const u32 wid = threadIdx.x >> 5;
-    for (u32 round = 0; round < kItems; ++round) {
-        const u64 i = base + static_cast<u64>(round) * kT + threadIdx.x;
-        const bool on = i < m;
-        const u32 x = on ? v[i] : 0u;
-        const u32 b = (x >> bit) & 1u;
-        const u32 ones = __ballot_sync(0xffffffffu, on && b);
-        if (lane() == 0) warp_ones[wid] = __popc(ones);
-        __syncthreads();
-        u32 before_warp = 0, round_ones = 0;
-        for (u32 w2 = 0; w2 < kT / 32; ++w2) {
-            before_warp += w2 < wid ? warp_ones[w2] : 0u;
-            round_ones += warp_ones[w2];
-        }
-        const u32 word_rank = ob + before_warp;  // ones before this warp's 32 positions
-        const u32 o_rank = word_rank + __popc(ones & ((1u << lane()) - 1u));
-        if (on) {
-            if (b) out[Z + o_rank] = x;
-            else out[static_cast<u32>(i) - o_rank] = x;
-            if (lane() == 0) level[i >> 5] = make_uint2(ones, word_rank);
-        }
-        ob += round_ones;
-        __syncthreads();
+    u32 ones[32];
+#pragma unroll
+    for (int b = 0; b < 32; ++b) ones[b] = 0;
+    u32 seen = 0;
+    for (u64 i = static_cast<u64>(blockIdx.x) * blockDim.x + threadIdx.x; i < m;
+         i += static_cast<u64>(gridDim.x) * blockDim.x) {
+        const u32 x = v[i];
+        ++seen;
+#pragma unroll
+        for (int b = 0; b < 32; ++b) ones[b] += (x >> b) & 1u;
+    }
+#pragma unroll
+    for (int b = 0; b < 32; ++b) {
+        if (static_cast<u32>(b) >= bits) break;
+        u32 z = seen - ones[b];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) z += __shfl_down_sync(0xffffffffu, z, o);
+        if (lane() == 0 && z) atomicAdd(&zeros[b], z);
     }
 }
 
-// rank sentinel at position m when m is a multiple of 32
-__global__ void wm_sentinel_kernel(u64 m, const u32* total_zeros, uint2* level)
+// One wavelet level in one pass: each CTA (ticket order) loads its tile
+// (position base + r*kT + t in round r), takes per warp and round the ballot
+// of bit `bit` and ranks the ones inside the tile, gets the zeros before the
+// tile by look-back, and splits the tile stably through shared memory: its
+// zeros go on after the zeros of earlier tiles, its ones after the level's Z
+// zeros and the ones of earlier tiles, both as contiguous runs.  Each 32
+// positions get their level word (the bits, the ones before them); the last
+// tile writes the rank sentinel at position m when m is a multiple of 32.
+__global__ void __launch_bounds__(kT) wm_level_kernel(const u32* v, u64 m, u32 bit,
+                                                      const u32* total_zeros, u32* out,
+                                                      uint2* level, LookBack lb)
 {
-    if ((m & 31u) == 0) level[m >> 5] = make_uint2(0u, static_cast<u32>(m) - *total_zeros);
+    constexpr u32 kW = kT / 32;
+    static_assert(kItems * kW == 64, "two (round, warp) counts per lane of warp 0");
+    __shared__ u32 ticket, zeros_before_s, tile_zeros_s;
+    __shared__ u32 cnt[kItems * kW];  // ones per (round, warp), then their prefix
+    __shared__ u32 stage[kTile];
+    const u32 tile = lb_ticket(lb, &ticket);
+    if (tile >= lb.tiles) return;
+    const u64 base = static_cast<u64>(tile) * kTile;
+    const u32 valid = static_cast<u32>(m - base < kTile ? m - base : kTile);
+    const u32 wid = threadIdx.x >> 5;
+    u32 x[kItems], mask[kItems];
+#pragma unroll
+    for (u32 r = 0; r < kItems; ++r) {
+        const u32 k = r * kT + threadIdx.x;
+        x[r] = k < valid ? v[base + k] : 0u;
+    }
+#pragma unroll
+    for (u32 r = 0; r < kItems; ++r) {
+        const u32 k = r * kT + threadIdx.x;
+        mask[r] = __ballot_sync(0xffffffffu, k < valid && ((x[r] >> bit) & 1u));
+        if (lane() == 0) cnt[r * kW + wid] = __popc(mask[r]);
+    }
+    __syncthreads();
+    // tile-local exclusive prefix of the 64 counts (round-major: position
+    // order) by warp 0, then the zeros before the tile by look-back
+    if (wid == 0) {
+        const u32 c0 = cnt[2 * lane()], c1 = cnt[2 * lane() + 1];
+        u32 incl = c0 + c1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const u32 y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane() >= static_cast<u32>(o)) incl += y;
+        }
+        const u32 tz = valid - __shfl_sync(0xffffffffu, incl, 31);
+        const u32 excl = incl - c0 - c1;
+        __syncwarp();
+        cnt[2 * lane()] = excl;
+        cnt[2 * lane() + 1] = excl + c0;
+        u32 before = 0;
+        if (tile == 0) {
+            if (lane() == 0) lb_publish(lb, 0, 2u, tz);
+        } else {
+            if (lane() == 0) lb_publish(lb, tile, 1u, tz);
+            before = lb_prefix<AddOp>(lb, tile);
+            if (lane() == 0) lb_publish(lb, tile, 2u, before + tz);
+        }
+        if (lane() == 0) {
+            zeros_before_s = before;
+            tile_zeros_s = tz;
+            if (tile + 1 == lb.tiles && (m & 31u) == 0)
+                level[m >> 5] = make_uint2(0u, static_cast<u32>(m) - *total_zeros);
+            lb_done(lb, tile);
+        }
+    }
+    __syncthreads();
+    const u32 tz = tile_zeros_s;
+    const u32 ones_before_tile = static_cast<u32>(base) - zeros_before_s;
+    // the split tile in shared memory: zeros, then ones, each in order
+#pragma unroll
+    for (u32 r = 0; r < kItems; ++r) {
+        const u32 k = r * kT + threadIdx.x;
+        const u32 ob = cnt[r * kW + wid];  // ones of the tile before this warp's 32
+        if (k < valid) {
+            const u32 one_rank = ob + __popc(mask[r] & ((1u << lane()) - 1u));
+            stage[((x[r] >> bit) & 1u) ? tz + one_rank : k - one_rank] = x[r];
+            if (lane() == 0) level[(base + k) >> 5] = make_uint2(mask[r], ones_before_tile + ob);
+        }
+    }
+    __syncthreads();
+    const u32 Z = *total_zeros;
+    const u32 zeros_before = zeros_before_s;
+#pragma unroll
+    for (u32 r = 0; r < kItems; ++r) {
+        const u32 k = r * kT + threadIdx.x;
+        if (k < valid)
+            out[k < tz ? zeros_before + k : Z + ones_before_tile + (k - tz)] = stage[k];
+    }
 }
 
 __device__ __forceinline__ u32 rank1(const uint2* level, u32 x)
@@ -842,7 +986,7 @@ void capacity_destroy(CapacityState* c)
                     c->act_addr, c->act_bytes, c->act_op, c->act_arr, c->act_chain,
                     c->act_done, c->act_lat, c->act_status, c->chained, c->chained_flag,
                     c->chained_pos, c->media_range, c->clk_table, c->clk_page, c->clk_ref,
-                    c->clk_dirty, c->clk_state, c->snap};
+                    c->clk_dirty, c->clk_state, c->snap, c->lb_state, c->lb_misc};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     delete c;
@@ -876,38 +1020,76 @@ int ensure_scratch(CapacityState* s, std::uint64_t need)
     const std::uint64_t m = std::max<std::uint64_t>(need + need / 4, 1 << 16);
     const std::uint64_t words = m / 32 + 2;
     const std::uint64_t tiles = (m + kTile - 1) / kTile;
-    std::uint64_t sums = 0, t = tiles;
-    while (t > 1) {
-        sums += 2 * t + 2;
-        t = (t + kTile - 1) / kTile;
-    }
-    sums += 8 + 256 * tiles;  // radix histograms
     if (grow(&s->key, m) || grow(&s->w, m) || grow(&s->bidx, m) || grow(&s->sk, m) ||
         grow(&s->si, m) || grow(&s->tk, m) || grow(&s->ti, m) || grow(&s->prev, m) ||
         grow(&s->next, m) || grow(&s->cur, m) || grow(&s->nxt, m) ||
         grow(&s->levels, 32 * words) || grow(&s->hit, m) || grow(&s->a, m) ||
         grow(&s->b, m) || grow(&s->c, m) || grow(&s->d, m) || grow(&s->valid, m) ||
-        grow(&s->status, m) || grow(&s->tile_sums, 2 * (256 * tiles + sums)) ||
+        grow(&s->status, m) || grow(&s->tile_sums, 256 * tiles) ||
         grow(&s->apage, m) || grow(&s->ahit, m) || grow(&s->avictim, m) ||
         grow(&s->adirty, m) || grow(&s->anact, m) || grow(&s->apos, m))
         return HBFSIM_CUDA_ERROR;
-    s->tile_sums_words = 2 * (256 * tiles + sums);
+    s->tile_sums_words = 256 * tiles;
+    // look-back status words: the longest scan is over m values
+    if (grow(&s->lb_state, tiles + 1) || grow(&s->lb_misc, 4) ||
+        cudaMemset(s->lb_state, 0, 8 * (tiles + 1)) != cudaSuccess ||
+        cudaMemset(s->lb_misc, 0, 16) != cudaSuccess)
+        return HBFSIM_CUDA_ERROR;
+    s->lb_tiles = tiles + 1;
+    s->lb_tag = 0;
     s->capacity_m = m;
     return HBFSIM_OK;
+}
+
+// Single-pass scan of n values (exclusive or inclusive, in place allowed);
+// the total goes to *total_dev when given.
+template <class Op>
+cudaError_t lb_scan(CapacityState* s, const u32* in, u32* out, u64 n, bool inclusive,
+                    u32* total_dev, cudaStream_t st)
+{
+    if (n == 0) {
+        if (total_dev) return cudaMemsetAsync(total_dev, 0, 4, st);
+        return cudaSuccess;
+    }
+    const u64 tiles = (n + kTile - 1) / kTile;
+    if (tiles > s->lb_tiles) return cudaErrorInvalidValue;
+    if (++s->lb_tag >= (1u << 30)) {  // tags are 30 bits: start over on clean words
+        const cudaError_t e = cudaMemsetAsync(s->lb_state, 0, 8 * s->lb_tiles, st);
+        if (e != cudaSuccess) return e;
+        s->lb_tag = 1;
+    }
+    const LookBack lb{s->lb_state, s->lb_misc, s->lb_tag, static_cast<u32>(tiles)};
+    lb_scan_kernel<Op><<<static_cast<unsigned>(tiles), kT, 0, st>>>(in, out, n,
+                                                                   inclusive ? 1 : 0,
+                                                                   total_dev, lb);
+    return cudaGetLastError();
+}
+
+LookBack next_lookback(CapacityState* s, u64 tiles, cudaStream_t st)
+{
+    if (++s->lb_tag >= (1u << 30)) {
+        cudaMemsetAsync(s->lb_state, 0, 8 * s->lb_tiles, st);
+        s->lb_tag = 1;
+    }
+    return LookBack{s->lb_state, s->lb_misc, s->lb_tag, static_cast<u32>(tiles)};
+}
+
+// Reads device words to the host after the stream's work, with the
+// look-back error word (set when a wait gave up): HBFSIM_TIMEOUT then.
+int sync_read(CapacityState* s, void* dst, const void* src, std::size_t bytes, cudaStream_t st)
+{
+    u32 err = 0;
+    if (bytes) cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, st);
+    cudaMemcpyAsync(&err, s->lb_misc + 1, 4, cudaMemcpyDeviceToHost, st);
+    if (cudaStreamSynchronize(st) != cudaSuccess) return HBFSIM_CUDA_ERROR;
+    return err ? HBFSIM_TIMEOUT : HBFSIM_OK;
 }
 
 // exclusive (or inclusive) add-scan with the total written to *total_dev
 cudaError_t scan_add(CapacityState* s, const u32* in, u32* out, u64 n, bool inclusive,
                      u32* total_dev, cudaStream_t st)
 {
-    cudaError_t e = scan<AddOp>(in, out, n, inclusive, s->tile_sums, st);
-    if (e != cudaSuccess || !total_dev) return e;
-    if (inclusive) {
-        if (n) cudaMemcpyAsync(total_dev, out + n - 1, 4, cudaMemcpyDeviceToDevice, st);
-        return cudaGetLastError();
-    }
-    total_kernel<<<1, 32, 0, st>>>(out, in, n, total_dev);
-    return cudaGetLastError();
+    return lb_scan<AddOp>(s, in, out, n, inclusive, total_dev, st);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
@@ -923,8 +1105,8 @@ int time_actions(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStr
     act_count_kernel<<<blocks(n), kT, 0, st>>>(s->status, s->ahit, s->adirty, n, s->anact);
     scan_add(s, s->anact, s->apos, n, false, cnt + 8, st);
     std::uint32_t actions = 0;
-    cudaMemcpyAsync(&actions, cnt + 8, 4, cudaMemcpyDeviceToHost, st);
-    if (cudaStreamSynchronize(st) != cudaSuccess) return HBFSIM_CUDA_ERROR;
+    if (const int rc = sync_read(s, &actions, cnt + 8, 4, st)) return rc;
+    if (actions > 2 * n) return HBFSIM_CUDA_ERROR;  // a read, after a dirty victim's program
     if (actions > s->act_capacity) {
         const std::uint64_t cap = actions + actions / 4 + 1024;
         if (grow(&s->act_addr, cap) || grow(&s->act_bytes, cap) || grow(&s->act_op, cap) ||
@@ -948,8 +1130,8 @@ int time_actions(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStr
         compact_kernel<<<blocks(actions), kT, 0, st>>>(s->chained_flag, s->chained_pos, actions,
                                                        s->chained);
         std::uint32_t q = 0;
-        cudaMemcpyAsync(&q, cnt + 9, 4, cudaMemcpyDeviceToHost, st);
-        if (cudaStreamSynchronize(st) != cudaSuccess) return HBFSIM_CUDA_ERROR;
+        if (const int rc = sync_read(s, &q, cnt + 9, 4, st)) return rc;
+        if (q > actions) return HBFSIM_CUDA_ERROR;
         BatchIO io{};
         io.address = s->act_addr;
         io.bytes = s->act_bytes;
@@ -1158,8 +1340,8 @@ int run_capacity(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStr
                                                    s->page_shift, s->apage, s->valid, s->status);
     scan_add(s, s->valid, s->a, n, false, cnt + 0, st);
     std::uint32_t valid_total = 0;
-    cudaMemcpyAsync(&valid_total, cnt + 0, 4, cudaMemcpyDeviceToHost, st);
-    if (cudaStreamSynchronize(st) != cudaSuccess) return HBFSIM_CUDA_ERROR;
+    if (const int rc = sync_read(s, &valid_total, cnt + 0, 4, st)) return rc;
+    if (valid_total > n) return HBFSIM_CUDA_ERROR;
     const std::uint64_t m = resident + valid_total;
     if (b->status) status_kernel<<<blocks(n), kT, 0, st>>>(s->status, n, b->status);
     // 2. the sequence: resident list, then the capacity accesses
@@ -1183,10 +1365,10 @@ int run_capacity(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStr
     cudaMemcpyAsync(s->sk, s->key, 4 * m, cudaMemcpyDeviceToDevice, st);
     iota_kernel<<<blocks(m), kT, 0, st>>>(s->si, m);
     u32 *ik = s->sk, *iv = s->si, *ok = s->tk, *ov = s->ti;
-    u32* hist = s->tile_sums + s->tile_sums_words / 2;
+    u32* hist = s->tile_sums;  // radix histograms [256][tiles]
     for (std::uint32_t shift = 0; shift < key_bits; shift += 8) {
         radix_hist_kernel<<<tiles, kT, 0, st>>>(ik, m, shift, hist, tiles);
-        scan<AddOp>(hist, hist, 256ull * tiles, false, s->tile_sums, st);
+        lb_scan<AddOp>(s, hist, hist, 256ull * tiles, false, nullptr, st);
         radix_scatter_kernel<<<tiles, kT, 0, st>>>(ik, iv, m, shift, hist, tiles, ok, ov);
         std::swap(ik, ok);
         std::swap(iv, ov);
@@ -1201,13 +1383,11 @@ int run_capacity(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStr
     value_kernel<<<blocks(m), kT, 0, st>>>(s->prev, m, s->cur);
     u32* zeros_dev = cnt + 16;  // per level
     u32 *wc = s->cur, *wn = s->nxt;
+    wm_bit_zeros_kernel<<<std::min<u32>(tiles, 4 * 148), kT, 0, st>>>(wc, m, vbits, zeros_dev);
     for (int l = static_cast<int>(vbits) - 1; l >= 0; --l) {
-        wm_zero_count_kernel<<<tiles, kT, 0, st>>>(wc, m, static_cast<u32>(l), s->d);
-        scan_add(s, s->d, s->c, tiles, false, zeros_dev + l, st);
         uint2* level = s->levels + static_cast<std::uint64_t>(l) * words;
-        wm_split_kernel<<<tiles, kT, 0, st>>>(wc, m, static_cast<u32>(l), s->c, zeros_dev + l,
-                                              wn, level);
-        wm_sentinel_kernel<<<1, 1, 0, st>>>(m, zeros_dev + l, level);
+        wm_level_kernel<<<tiles, kT, 0, st>>>(wc, m, static_cast<u32>(l), zeros_dev + l, wn,
+                                              level, next_lookback(s, tiles, st));
         std::swap(wc, wn);
     }
     // 6. hits, distinct pages before each access, evicting misses
@@ -1225,8 +1405,8 @@ int run_capacity(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStr
     u32* write_mark = ov;
     dirty_marks_kernel<<<blocks(m), kT, 0, st>>>(ik, iv, s->hit, s->w, m, start_mark,
                                                  write_mark);
-    scan<MaxOp>(start_mark, start_mark, m, true, s->tile_sums, st);
-    scan<MaxOp>(write_mark, write_mark, m, true, s->tile_sums, st);
+    lb_scan<MaxOp>(s, start_mark, start_mark, m, true, nullptr, st);
+    lb_scan<MaxOp>(s, write_mark, write_mark, m, true, nullptr, st);
     dirty_kernel<<<blocks(m), kT, 0, st>>>(iv, start_mark, write_mark, m, s->b);
     // 9. per-access outputs
     OutArgs oa{};
@@ -1254,8 +1434,8 @@ int run_capacity(hbfsim_context* ctx, const hbfsim_capacity_batch_v1* b, cudaStr
     live_kernel<<<blocks(m), kT, 0, st>>>(s->next, m, s->a);
     scan_add(s, s->a, s->cur, m, false, cnt + 7, st);
     std::uint32_t host_cnt[kCapCounts];
-    cudaMemcpyAsync(host_cnt, cnt, 4 * kCapCounts, cudaMemcpyDeviceToHost, st);
-    if (cudaStreamSynchronize(st) != cudaSuccess) return HBFSIM_CUDA_ERROR;
+    if (const int rc = sync_read(s, host_cnt, cnt, 4 * kCapCounts, st)) return rc;
+    if (host_cnt[7] > m) return HBFSIM_CUDA_ERROR;
     const std::uint32_t live_total = host_cnt[7];
     const std::uint32_t keep =
         static_cast<std::uint32_t>(std::min<std::uint64_t>(live_total, s->frames));
