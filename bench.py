@@ -519,7 +519,11 @@ def run_extras(args, device, tmp):
     th = {"workload": "config-3 grid: 1 logic + 8 NAND layers x 128 x 128 cells, fp64, "
                       "1 ms backward-Euler steps, 64 dies",
           "cells": cells, "steps": steps, "ms_per_step": step_ms,
-          "controller_ms_per_epoch": ctrl_ms,
+          "controller_ms_per_epoch": ctrl_ms if kt["controller"][0] else None,
+          "kernel": ("thermal_epoch_kernel: one cooperative launch per epoch (rhs, 4 fp64 "
+                     "DCT GEMMs staged by bulk copies, tridiagonal solves, die means, "
+                     "controller)" if not kt["controller"][0] else
+                     "rhs, 4 dgemm, tridiag, die means, then the controller kernel"),
           "cell_bytes_per_step": 16 * cells,
           "achieved_gbs_16B_per_cell": 16 * cells / (step_ms * 1e-3) / 1e9}
     if not args.no_cpu_baseline:

@@ -164,6 +164,7 @@ struct DevCounters {
 enum DeviceError : u32 {
     kErrUnsorted = 1u,
     kErrNeedSeq = 2u,
+    kErrWait = 4u,  // a bounded device wait gave up (fused thermal step)
 };
 constexpr u64 kArrivalLimit = u64{1} << 59;
 

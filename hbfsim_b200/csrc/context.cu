@@ -645,6 +645,12 @@ int hbfsim_flush(hbfsim_context* c)
         return HBFSIM_CUDA_ERROR;
     if (k.errors > c->errors_reported) {
         c->errors_reported = k.errors;
+        if (k.error_code & kErrWait) {  // a bounded wait of the fused thermal step ran out
+            thermal_reset_barrier(c->thermal);
+            k.error_code &= ~static_cast<unsigned long long>(kErrWait);
+            cudaMemcpy(&c->d_counters->error_code, &k.error_code, 8, cudaMemcpyHostToDevice);
+            return HBFSIM_TIMEOUT;
+        }
         return HBFSIM_INVALID_ARGUMENT;  // a batch was refused (unsorted arrivals)
     }
     return HBFSIM_OK;

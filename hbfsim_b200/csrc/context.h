@@ -121,6 +121,7 @@ void capacity_destroy(CapacityState* c);
 void retention_destroy(RetentionState* r);
 // Device array of the grid's per-die mean temperatures (global die g*D+d).
 const double* thermal_die_temperatures(const ThermalState* t);
+void thermal_reset_barrier(ThermalState* t);
 // Times media actions (device arrays) decoded against `ranges`, in batch
 // order whatever their arrivals; carries the context's timing state.
 int run_media_batch(hbfsim_context* c, const BatchIO& io, const DevRange* ranges,

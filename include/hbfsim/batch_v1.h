@@ -352,7 +352,11 @@ int hbfsim_thermal_configure_v1(hbfsim_context* context,
 /* Closes one epoch of `epoch_s` seconds: die activity recorded by the batches
  * since the previous epoch becomes power, the grid takes one backward-Euler
  * step, and the refresh / throttle factors of the next epoch are derived from
- * the new die temperatures.  Activity counters are then cleared. */
+ * the new die temperatures.  Activity counters are then cleared.
+ * On grids whose sides are multiples of 4 and up to about 150 cells the whole
+ * close is one cooperative kernel (capturable in a CUDA graph); its waits
+ * are bounded, and one that gives up makes the next hbfsim_flush return
+ * HBFSIM_TIMEOUT (the epoch's temperatures and factors are then unspecified). */
 int hbfsim_advance_epoch_v1(hbfsim_context* context, double epoch_s,
                             void* stream);
 
