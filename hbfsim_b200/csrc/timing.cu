@@ -175,29 +175,36 @@ struct ChanInfo {  // per local channel, staged in shared memory
     u64 bw;
     u32 x_add;     // transfer = (bytes + x_add) >> x_shift, x_add = 2^x_shift - 1,
     u32 x_shift;   // when 1e9 / bw reduces to 1 / 2^x_shift; else x_shift = kXDivide
+                   // and x_add holds 1 / bw as an fp32 (the quotient's estimate)
 };
+
+constexpr u32 kXDivide = 0xffu;
 
 // ceil(bytes * 1e9 / bw) * time_scale for one access of a channel.  An
 // access never exceeds its page (access_supported), and the host admits the
 // parallel path only when a page's transfer times the scale stays below
-// 2^24, so the plain product is exact here.
-__device__ __noinline__ u64 transfer_ticks_div(u32 bytes, u64 bw)
-{
-    return ceil_div_u64(static_cast<u64>(bytes) * 1000000000ull, bw);
-}
-
-constexpr u32 kXDivide = 0xffu;
+// 2^24, so the plain product is exact here.  Per-channel rates are mostly
+// 1e9 * 2^k bytes per second (a shift); otherwise the quotient q of
+// n = bytes * 1e9 by bw is estimated as n * r in fp64, r = 1 / bw rounded
+// to fp32 (relative error 2^-24, plus 2^-52 for the product), so for every
+// q below 2^23 the estimate is within 0.6 of the quotient and one step of
+// the exact remainder test settles it; larger estimates take the division.
+__device__ __noinline__ u64 transfer_ticks_div(u64 n, u64 d) { return ceil_div_u64(n, d); }
 
 __device__ __forceinline__ u64 transfer_ticks(u32 bytes, const ChanInfo& ci, u32 scale)
 {
-    // the division stays out of line: per-channel rates are almost always
-    // 1e9 / 2^k bytes per second.  bytes < 2^32, so the quotient fits 32 bits.
     const uint2 code = *reinterpret_cast<const uint2*>(&ci.x_add);
     if (code.y != kXDivide) {
         const u32 x = static_cast<u32>((static_cast<u64>(bytes) + code.x) >> code.y);
         return static_cast<u64>(x) * scale;
     }
-    return transfer_ticks_div(bytes, ci.bw) * scale;
+    const u64 n = static_cast<u64>(bytes) * 1000000000ull, d = ci.bw;
+    const double r = static_cast<double>(__uint_as_float(code.x));
+    u64 q = static_cast<u64>(static_cast<double>(n) * r);
+    if (q >= (u64{1} << 23)) return transfer_ticks_div(n, d) * scale;
+    if (q * d > n) --q;                 // now q * d <= n
+    else if (n - q * d >= d) ++q;       // now n - q * d < d
+    return (q + (q * d != n ? 1u : 0u)) * scale;
 }
 
 __device__ ChanInfo stage_channel(const TimingParams& tp, u32 c, bool die)
@@ -208,13 +215,13 @@ __device__ ChanInfo stage_channel(const TimingParams& tp, u32 c, bool die)
     ci.t_prog = tp.chan_t_prog[c];
     ci.admit = tp.chan_admit[c];
     ci.bw = tp.chan_bw[c];
-    // reduce 1e9 / bw: exact shift when the quotient is 1 / 2^s
-    u64 a = 1000000000ull, b = ci.bw;
-    while (b) { const u64 r = a % b; a = b; b = r; }
-    const u64 num = 1000000000ull / a, den = ci.bw / a;
+    // 1e9 / bw is 1 / 2^s exactly when bw = 1e9 * 2^s
     ci.x_shift = kXDivide;
-    ci.x_add = 0;
-    if (num == 1 && (den & (den - 1)) == 0 && 63 - __clzll(den) < 32) {
+    ci.x_add = __float_as_uint(ci.bw ? static_cast<float>(1.0 / static_cast<double>(ci.bw))
+                                     : 0.0f);
+    const u64 den = ci.bw / 1000000000ull;
+    if (ci.bw % 1000000000ull == 0 && den != 0 && (den & (den - 1)) == 0 &&
+        63 - __clzll(den) < 32) {
         ci.x_shift = 63 - __clzll(den);
         ci.x_add = static_cast<u32>((u64{1} << ci.x_shift) - 1);
     }

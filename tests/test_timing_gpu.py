@@ -233,6 +233,34 @@ def test_refresh_throttle_admit_factors(tmp):
     assert np.array_equal(r, refresh) and np.array_equal(t, throttle) and np.array_equal(a, admit)
 
 
+def test_transfer_quotients_every_size_and_rate(tmp):
+    """ceil(bytes * 1e9 / bw) for channel rates that are not 1e9 * 2^k: the
+    quotient is estimated with the channel's fp64 reciprocal and settled with
+    the remainder.  Every access size from 1 byte to a whole page on channels
+    whose refresh shares (0..900 permille) leave odd rates (refresh 0 keeps
+    the shift path), against the oracle's integer division."""
+    s = c0_setup(3, stacks=2)
+    ctx = make_context(s, tmp)
+    rng = np.random.default_rng(77)
+    refresh = rng.integers(0, 901, s.local_channels).astype(np.uint32)
+    refresh[:4] = [0, 1, 500, 900]
+    ctx.set_channel_factors(refresh, None, None)
+    page = s.profile["page_bytes"]
+    n = 60_000
+    size = np.concatenate([np.arange(1, page + 1), rng.integers(1, page + 1, n - page)])
+    size = size[:n].astype(np.uint32)
+    pages = rng.integers(0, (64 * GIB) // page, n, dtype=np.int64)
+    address = (wl.RANGE_BASE + pages * page).astype(np.uint64)
+    op = (rng.random(n) < 0.1).astype(np.uint8)
+    arrival = np.cumsum(rng.integers(0, 40, n)).astype(np.uint64)
+    arrays = (address, size, op, arrival)
+    ora = OracleRun(s, refresh, None, None)
+    want = ora.run(*arrays)
+    assert (want[2] == 1).all()
+    assert_same(gpu_run(ctx, arrays), want, "transfer quotients")
+    ctx.close()
+
+
 def test_channel_shards_partition_the_trace(tmp):
     """Each shard times only its channels; the union equals the unsharded run."""
     arrays = wl.c0_trace(30000, seed=12)
