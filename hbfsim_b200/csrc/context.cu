@@ -213,6 +213,7 @@ void free_geometry(hbfsim_context* c)
     dfree(c->d_act_stage);
     dfree(c->d_agg);
     dfree(c->d_incoming);
+    dfree(c->d_scan_groups);
     c->scratch_ctas = 0;
 }
 
@@ -468,9 +469,11 @@ int run_device_batch(hbfsim_context* c, const BatchIO& io, cudaStream_t stream,
     if (plan.ctas > c->scratch_ctas) {
         dfree(c->d_agg);
         dfree(c->d_incoming);
+        dfree(c->d_scan_groups);
         const std::uint64_t ctas = std::max<std::uint64_t>(plan.ctas, 2ull * c->sm_count);
         if (dalloc(&c->d_agg, ctas * c->C * c->K * (c->K + 1)) ||
-            dalloc(&c->d_incoming, ctas * c->C * c->K)) {
+            dalloc(&c->d_incoming, ctas * c->C * c->K) ||
+            dalloc(&c->d_scan_groups, lb_group_words(ctas, c->C, c->K))) {
             c->scratch_ctas = 0;
             return HBFSIM_CUDA_ERROR;
         }
@@ -479,6 +482,8 @@ int run_device_batch(hbfsim_context* c, const BatchIO& io, cudaStream_t stream,
     BatchScratch s{};
     s.agg = c->d_agg;
     s.incoming = c->d_incoming;
+    s.scan_groups = c->d_scan_groups;
+    s.scan_lb = c->d_scan_lb;
     s.error = c->d_error;
     s.last_arrival = c->d_last_arrival;
     s.counters = c->d_counters;
@@ -558,10 +563,12 @@ int hbfsim_context_create(const hbfsim_options* options, hbfsim_context** out)
         cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
         dalloc(&c->d_error, 1) || dalloc(&c->d_last_arrival, 1) || dalloc(&c->d_counters, 1) ||
         dalloc(&c->d_sample_seq, 1) ||
-        dalloc(&c->d_sample_counts, hbfsim_context::kSampleCtas)) {
+        dalloc(&c->d_sample_counts, hbfsim_context::kSampleCtas) ||
+        dalloc(&c->d_scan_lb, 2 + kLbFlagWords)) {
         hbfsim_context_destroy(c);
         return HBFSIM_CUDA_ERROR;
     }
+    cudaMemset(c->d_scan_lb, 0, 4 * (2 + kLbFlagWords));
     cudaMemset(c->d_error, 0, sizeof(std::uint32_t));
     cudaMemset(c->d_last_arrival, 0, sizeof(std::uint64_t));
     cudaMemset(c->d_counters, 0, sizeof(DevCounters));
@@ -724,6 +731,7 @@ void hbfsim_context_destroy(hbfsim_context* c)
     dfree(c->d_counters);
     dfree(c->d_sample_seq);
     dfree(c->d_sample_counts);
+    dfree(c->d_scan_lb);
     dfree(c->d_emp_service);
     dfree(c->d_emp_words);
     for (auto& p : c->d_stage) {
@@ -1081,6 +1089,10 @@ namespace {
 
 constexpr std::size_t kStaticScratchBytes = std::size_t{8} << 20;
 constexpr std::size_t kStaticErrorBytes = 256;  // error word, padded
+// then the look-back scan's counters and flags at a fixed address (zero as
+// the array is, and left zero by every scan)
+constexpr std::size_t kStaticLbBytes = (4 * (2 + kLbFlagWords) + 255) / 256 * 256;
+constexpr std::size_t kStaticHeadBytes = kStaticErrorBytes + kStaticLbBytes;
 constexpr int kMaxDevices = 64;
 
 }  // namespace
@@ -1147,10 +1159,13 @@ extern "C" int hbfsim_submit_access_batch_static_v1(hbfsim_context* c,
     // its incoming state.  Fewer CTAs cover longer ranges; results do not
     // depend on how the batch is split.  A shape whose single CTA does not
     // fit is refused.
+    // (plus, per group of 32 CTAs, the look-back scan's group words)
     const std::uint64_t words_per_cta =
         static_cast<std::uint64_t>(c->C) * c->K * (c->K + 1) + static_cast<std::uint64_t>(c->C) * c->K;
+    const std::uint64_t group_words = lb_group_words(1, c->C, c->K);
+    const std::uint64_t avail = (kStaticScratchBytes - kStaticHeadBytes) / 8;
     const std::uint64_t max_ctas =
-        (kStaticScratchBytes - kStaticErrorBytes) / (8 * words_per_cta);
+        avail > group_words ? (avail - group_words) / (words_per_cta + group_words / 32 + 1) : 0;
     if (max_ctas == 0) return HBFSIM_UNSUPPORTED;
     if (plan.ctas > max_ctas) {
         const std::uint64_t tiles = (io.n + plan.T - 1) / plan.T;
@@ -1161,8 +1176,10 @@ extern "C" int hbfsim_submit_access_batch_static_v1(hbfsim_context* c,
     auto* bytes = static_cast<unsigned char*>(base);
     BatchScratch s{};
     s.error = reinterpret_cast<std::uint32_t*>(bytes);
-    s.agg = reinterpret_cast<i64*>(bytes + kStaticErrorBytes);
+    s.agg = reinterpret_cast<i64*>(bytes + kStaticHeadBytes);
     s.incoming = s.agg + static_cast<std::uint64_t>(plan.ctas) * c->C * c->K * (c->K + 1);
+    s.scan_groups = s.incoming + static_cast<std::uint64_t>(plan.ctas) * c->C * c->K;
+    s.scan_lb = reinterpret_cast<std::uint32_t*>(bytes + kStaticErrorBytes);
     s.last_arrival = c->d_last_arrival;
     s.counters = c->d_counters;
     s.state_in = c->d_state[c->cur];

@@ -52,6 +52,8 @@ struct hbfsim_context {
     // per-batch scratch
     hbfb::i64* d_agg = nullptr;
     hbfb::i64* d_incoming = nullptr;
+    hbfb::i64* d_scan_groups = nullptr;     // look-back range scan: group maps and states
+    std::uint32_t* d_scan_lb = nullptr;     // its counters and flags (zero between scans)
     std::uint64_t scratch_ctas = 0;
     std::uint32_t* d_error = nullptr;
     std::uint64_t* d_last_arrival = nullptr;

@@ -1756,6 +1756,244 @@ __global__ void __launch_bounds__(kScanWarps * 32) range_scan_kernel(const ScanA
     }
 }
 
+// ---------------------------------------------------------------------------
+// Range scan over several CTAs per channel (decoupled look-back).  CTA
+// (group g, channel c) -- taken in ticket order, so every group it waits on
+// is already running -- owns ranges [g R, (g + 1) R) of channel c, R =
+// kLbWarps * m, m per warp:
+//   A  each warp composes its m range maps (kept staged for C);
+//   P  the warps' maps form an inclusive prefix (Hillis-Steele, 3 rounds);
+//      the last is the group's map, published as an aggregate (flag 1);
+//   L  warp 0 walks back over the preceding groups of channel c, composing
+//      their published maps until it meets a group that published its
+//      outgoing state (flag 2), and applies the composite to it: the group's
+//      incoming state; it publishes its own outgoing state (flag 2);
+//   C  each warp applies the prefix of the warps before it and walks its
+//      ranges, writing every range's incoming state.
+// Flags live at a fixed address and are cleared by the last CTA to finish;
+// waits are bounded (a wait error is counted and the scan goes on).
+constexpr u32 kLbWarps = 8;
+constexpr u32 kLbRangesPerWarp = 4;
+constexpr u32 kLbRanges = kLbWarps * kLbRangesPerWarp;  // ranges per group
+constexpr u32 kLbSpins = 1u << 22;
+
+struct LbScanArgs {
+    i64* gmap;     // [groups][C][K][K+1] published group maps
+    i64* gstate;   // [groups][C][K] published outgoing states
+    u32* ctr;      // ticket and done counters, then the flags [groups][C]: 0, 1 map,
+    u32 groups;    //   2 outgoing state (zero between scans)
+};
+
+// Out = Post o Pre (Pre first) for maps x -> max(M[:, :K] + x, M[:, K]),
+// one warp, entries strided over the lanes; sums below -2^61 clamp to NEG.
+__device__ __forceinline__ void compose_maps(i64* out, const i64* post, const i64* pre, u32 K)
+{
+    const u32 lane = threadIdx.x & 31u, KK = K + 1, per = K * KK;
+    i64 v[3];
+#pragma unroll
+    for (u32 t = 0; t < 3; ++t) {
+        const u32 e = lane + 32 * t;
+        v[t] = 0;
+        if (e >= per) continue;
+        const u32 i = e / KK, j = e - i * KK;
+        const i64* Pi = post + static_cast<u64>(i) * KK;
+        i64 best = j == K ? Pi[K] : kNeg;
+        for (u32 k = 0; k < K; ++k) best = imax(best, Pi[k] + pre[k * KK + j]);
+        v[t] = best < kNeg / 2 ? kNeg : best;
+    }
+    __syncwarp();
+#pragma unroll
+    for (u32 t = 0; t < 3; ++t) {
+        const u32 e = lane + 32 * t;
+        if (e < per) out[e] = v[t];
+    }
+    __syncwarp();
+}
+
+// x -> M(x), lane i < K holding word i (all lanes call)
+__device__ __forceinline__ i64 apply_map(const i64* M, i64 x, u32 K)
+{
+    const u32 lane = threadIdx.x & 31u, row = lane < K ? lane : 0u;
+    const i64* r = M + static_cast<u64>(row) * (K + 1);
+    i64 best = r[K];
+    for (u32 j = 0; j < K; ++j) best = imax(best, r[j] + __shfl_sync(0xffffffffu, x, j));
+    return lane < K ? best : x;
+}
+
+__device__ __forceinline__ void identity_map(i64* M, u32 K)
+{
+    const u32 lane = threadIdx.x & 31u, KK = K + 1;
+    for (u32 e = lane; e < K * KK; e += 32) {
+        const u32 i = e / KK, j = e - i * KK;
+        M[e] = i == j ? 0 : kNeg;
+    }
+    __syncwarp();
+}
+
+__global__ void __launch_bounds__(kLbWarps * 32) range_scan_lb_kernel(const ScanArgs a,
+                                                                      const LbScanArgs b)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ u32 s_ticket, s_last;
+    const u32 tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+    const u32 K = a.K, KK = K + 1, per = K * KK, C = a.C;
+    const u32 err = *a.error;
+    if (!(err & kErrUnsorted) && (err & kErrNeedSeq)) return;  // sequential path
+    if (err & kErrUnsorted) {  // refused: keep the state
+        for (u32 c = blockIdx.x; c < C; c += gridDim.x)
+            for (u32 k = tid; k < K; k += blockDim.x)
+                a.state_out[static_cast<u64>(c) * K + k] = a.state_in[static_cast<u64>(c) * K + k];
+        if (blockIdx.x == 0 && tid == 0) {
+            atomicAdd(&a.counters->errors, 1ull);
+            atomicOr(&a.counters->error_code, static_cast<unsigned long long>(err));
+        }
+        return;
+    }
+    u32* ticket = b.ctr;
+    u32* flags = b.ctr + 2;
+    if (tid == 0) s_ticket = atomicAdd(ticket, 1u);
+    __syncthreads();
+    const u32 t = s_ticket;
+    const u32 g = t / C, c = t % C;
+    i64* stage = reinterpret_cast<i64*>(smem) + static_cast<u64>(warp) * kLbRangesPerWarp * per;
+    i64* pm = reinterpret_cast<i64*>(smem) + static_cast<u64>(kLbWarps) * kLbRangesPerWarp * per;
+    i64* pm2 = pm + static_cast<u64>(kLbWarps) * per;        // prefix double buffer
+    i64* acc = pm2 + static_cast<u64>(kLbWarps) * per;       // look-back composite (warp 0)
+    i64* tmp = acc + per;                                    // a fetched map
+    i64* gin = tmp + per;                                    // [warps][K] incoming states
+    const u32 n = a.ctas;
+    const u32 w0 = g * kLbRanges + warp * kLbRangesPerWarp;
+    const u32 w1 = w0 + kLbRangesPerWarp < n ? w0 + kLbRangesPerWarp : n;
+    const u32 nb = w0 < n ? w1 - w0 : 0u;
+    bool failed = false;
+
+    // A: the warp's map R_{w1-1} o ... o R_{w0}
+    if (nb) stage_aggregates(a, c, w0, nb, per, stage);
+    i64* mine = pm + static_cast<u64>(warp) * per;
+    if (nb == 0) {
+        identity_map(mine, K);
+    } else {
+        for (u32 e = lane; e < per; e += 32) mine[e] = stage[e];
+        __syncwarp();
+        for (u32 k = 1; k < nb; ++k) compose_maps(mine, stage + static_cast<u64>(k) * per, mine, K);
+    }
+    __syncthreads();
+    // P: inclusive prefix over the warps
+    i64 *cur = pm, *nxt = pm2;
+    for (u32 d = 1; d < kLbWarps; d <<= 1) {
+        i64* o = nxt + static_cast<u64>(warp) * per;
+        const i64* m = cur + static_cast<u64>(warp) * per;
+        if (warp >= d) {
+            compose_maps(o, m, cur + static_cast<u64>(warp - d) * per, K);
+        } else {
+            for (u32 e = lane; e < per; e += 32) o[e] = m[e];
+            __syncwarp();
+        }
+        __syncthreads();
+        i64* sw = cur;
+        cur = nxt;
+        nxt = sw;
+    }
+    const i64* group_map = cur + static_cast<u64>(kLbWarps - 1) * per;
+    u32* my_flag = flags + g * C + c;
+    // L: the group's incoming state
+    if (warp == 0) {
+        i64 x = 0;
+        if (g == 0) {
+            x = lane < K ? static_cast<i64>(a.state_in[static_cast<u64>(c) * K + lane]) : 0;
+        } else {
+            i64* slot = b.gmap + (static_cast<u64>(g) * C + c) * per;
+            for (u32 e = lane; e < per; e += 32) slot[e] = group_map[e];
+            __syncwarp();
+            if (lane == 0) {
+                __threadfence();
+                atomicExch(my_flag, 1u);
+            }
+            identity_map(acc, K);
+            for (int j = static_cast<int>(g) - 1; j >= 0; --j) {
+                const u32* f = flags + static_cast<u32>(j) * C + c;
+                u32 fv = 0;
+                if (lane == 0) {
+                    for (u32 spins = 0;; ++spins) {
+                        fv = *reinterpret_cast<const volatile u32*>(f);
+                        if (fv != 0) break;
+                        if (spins >= kLbSpins) break;
+                        __nanosleep(32);
+                    }
+                    __threadfence();
+                }
+                fv = __shfl_sync(0xffffffffu, fv, 0);
+                __threadfence();  // every lane reads the published words after the flag
+                if (fv == 0) {  // gave up: carry on from the carried state
+                    failed = true;
+                    x = lane < K ? static_cast<i64>(a.state_in[static_cast<u64>(c) * K + lane]) : 0;
+                    break;
+                }
+                if (fv == 2) {
+                    const i64 y = lane < K ? __ldcg(b.gstate + (static_cast<u64>(j) * C + c) * K + lane)
+                                           : 0;
+                    x = apply_map(acc, y, K);
+                    break;
+                }
+                const i64* src = b.gmap + (static_cast<u64>(j) * C + c) * per;
+                for (u32 e = lane; e < per; e += 32) tmp[e] = __ldcg(src + e);
+                __syncwarp();
+                compose_maps(acc, acc, tmp, K);
+            }
+        }
+        if (lane < K) gin[lane] = x;
+        // outgoing state of the group
+        const i64 out = apply_map(group_map, x, K);
+        if (lane < K) b.gstate[(static_cast<u64>(g) * C + c) * K + lane] = out;
+        __syncwarp();
+        if (lane == 0) {
+            __threadfence();
+            atomicExch(my_flag, 2u);
+        }
+        if ((g + 1) * kLbRanges >= n && lane < K) a.state_out[static_cast<u64>(c) * K + lane] = out;
+        if (failed && lane == 0) {
+            atomicAdd(&a.counters->errors, 1ull);
+            atomicOr(&a.counters->error_code, static_cast<unsigned long long>(kErrWait));
+        }
+    }
+    __syncthreads();
+    // C: every range's incoming state
+    {
+        i64 x = lane < K ? gin[lane] : 0;
+        if (warp > 0) x = apply_map(cur + static_cast<u64>(warp - 1) * per, x, K);
+        for (u32 k = 0; k < nb; ++k) {
+            if (lane < K) a.incoming[(static_cast<u64>(w0 + k) * C + c) * K + lane] = x;
+            x = apply_map(stage + static_cast<u64>(k) * per, x, K);
+        }
+    }
+    if (g == 0 && a.act_stage) {
+        const u32 D = a.dies;
+        for (u32 d = tid; d < D; d += blockDim.x) {
+            const u64 k = static_cast<u64>(c) * D + d;
+            a.die_read_bytes[k] += a.act_stage[2 * k];
+            a.die_writes[k] += a.act_stage[2 * k + 1];
+        }
+    }
+    if (t == 0 && tid == 0) {
+        if (a.n) *a.last_arrival = a.arrival[a.n - 1];
+        atomicAdd(&a.counters->batches, 1ull);
+    }
+    // the last CTA to finish clears the flags and counters for the next scan
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        s_last = atomicAdd(ticket + 1, 1u) == b.groups * C - 1 ? 1u : 0u;
+    }
+    __syncthreads();
+    if (s_last) {
+        for (u32 k = tid; k < b.groups * C; k += blockDim.x) flags[k] = 0;
+        if (tid == 0) {
+            ticket[0] = 0;
+            ticket[1] = 0;
+        }
+    }
+}
+
 // Exact sequential fallback with the reference's saturating unsigned
 // arithmetic, for batches whose ticks may approach 2^64.  One thread per
 // local channel walks the whole batch in order.
@@ -2207,14 +2445,31 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
         const u32 group = (plan.ctas + kScanWarps - 1) / kScanWarps;
         const u32 room = (96u * 1024u / 8u) / kScanWarps - per;
         sa.chunk = std::max(1u, std::min(group, room / per));
-        const u32 scan_smem = 8u * (kScanWarps * (sa.chunk * per + per) + kScanWarps * plan.K);
-        err = cudaFuncSetAttribute(range_scan_kernel,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   static_cast<int>(scan_smem));
-        if (err != cudaSuccess) return err;
-        hooks(kSlotScan, 0, stream);
-        range_scan_kernel<<<plan.C, kScanWarps * 32, scan_smem, stream>>>(sa);
-        hooks(kSlotScan, 1, stream);
+        const u32 groups = (plan.ctas + kLbRanges - 1) / kLbRanges;
+        if (s.scan_lb && s.scan_groups && static_cast<u64>(groups) * plan.C <= kLbFlagWords) {
+            // several CTAs per channel, chained by look-back
+            LbScanArgs lb{};
+            lb.gmap = s.scan_groups;
+            lb.gstate = s.scan_groups + static_cast<u64>(groups) * plan.C * per;
+            lb.ctr = s.scan_lb;
+            lb.groups = groups;
+            const u32 lb_smem =
+                8u * (kLbWarps * kLbRangesPerWarp * per + 2 * kLbWarps * per + 2 * per +
+                      kLbWarps * plan.K);
+            hooks(kSlotScan, 0, stream);
+            range_scan_lb_kernel<<<groups * plan.C, kLbWarps * 32, lb_smem, stream>>>(sa, lb);
+            hooks(kSlotScan, 1, stream);
+        } else {
+            const u32 scan_smem =
+                8u * (kScanWarps * (sa.chunk * per + per) + kScanWarps * plan.K);
+            err = cudaFuncSetAttribute(range_scan_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(scan_smem));
+            if (err != cudaSuccess) return err;
+            hooks(kSlotScan, 0, stream);
+            range_scan_kernel<<<plan.C, kScanWarps * 32, scan_smem, stream>>>(sa);
+            hooks(kSlotScan, 1, stream);
+        }
         hooks(kSlotPass2, 0, stream);
         p2<<<plan.ctas, kThreads, plan.smem_bytes, stream>>>(a);
         hooks(kSlotPass2, 1, stream);

@@ -33,7 +33,22 @@ struct BatchScratch {
     DevCounters* counters;
     const u64* state_in;
     u64* state_out;
+    // range scan by look-back (optional: null selects one CTA per channel):
+    // group maps and states, lb_group_words(ctas, C, K) words; and the
+    // counters and flags, 2 + kLbFlagWords words at a fixed address, zero
+    // before the first batch (each scan leaves them zero)
+    i64* scan_groups = nullptr;
+    u32* scan_lb = nullptr;
 };
+
+constexpr u32 kLbFlagWords = 16384;  // groups x local channels of one scan, at most
+
+// Words of the look-back scan's group maps and states for `ctas` ranges
+// (groups of 32 ranges).
+inline u64 lb_group_words(u64 ctas, u64 C, u64 K)
+{
+    return (ctas + 31) / 32 * C * (K * (K + 1) + K);
+}
 
 // Optional launch markers (profiling): mark(slot, 0) before a launch and
 // mark(slot, 1) after it, on the launching stream.

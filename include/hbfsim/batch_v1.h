@@ -109,9 +109,10 @@ int hbfsim_submit_access_batch_v1(hbfsim_context* context,
  * library call that launches a kernel there -- so a caller that is about to
  * reserve nearly all device memory should make one call first.  Returns
  * HBFSIM_UNSUPPORTED
- * when one CTA's scratch (local channels * (D+1) * (D+3) * 8 bytes) exceeds
- * the array; otherwise it times the batch exactly as
- * hbfsim_submit_access_batch_v1 does. */
+ * when one CTA's scratch (local channels * (D+1) * (D+3) * 8 bytes, plus the
+ * range scan's 64 KiB of flags and its per-group words) exceeds the array;
+ * otherwise it times the batch exactly as hbfsim_submit_access_batch_v1
+ * does. */
 int hbfsim_submit_access_batch_static_v1(hbfsim_context* context,
                                          const hbfsim_access_batch_v1* batch,
                                          void* stream);
