@@ -155,6 +155,7 @@ struct PassArgs {
     u32 off_sarr[2], off_sinfo[2];  // direct kernel: channel-sorted arrays per pass
     u32 off_slot;                   // direct replay: sorted slot of each access
     u32 off_dies[2];                // direct pass 1: die words of the 32-bit chains
+    u32 off_xtab;                   // general direct pass 1: transfer ticks of pow2 sizes
     // global scratch
     i64* agg;        // [ctas][C][K][K+1]  (pass 1 out)
     i64* incoming;   // [ctas][C][K]       (pass 2 in, carried in place)
@@ -179,6 +180,9 @@ struct ChanInfo {  // per local channel, staged in shared memory
 };
 
 constexpr u32 kXDivide = 0xffu;
+// per-channel transfer ticks of the power-of-two sizes 2^kXTabMin ..
+// 2^(kXTabMin + kXTabSizes - 1), tabulated by the general pass-1 kernel
+constexpr u32 kXTabMin = 4, kXTabSizes = 12;
 
 // ceil(bytes * 1e9 / bw) * time_scale for one access of a channel.  An
 // access never exceeds its page (access_supported), and the host admits the
@@ -1227,7 +1231,12 @@ direct_fast_kernel(const PassArgs args)
     const TileSmem s = tile_views(smem, A, 1);
     i64* s_col0 = reinterpret_cast<i64*>(smem + A.off_pm);  // [C][K]
     u32* s_part = reinterpret_cast<u32*>(s.red);            // per-warp channel totals
-    prologue(A, s, true, false, false);
+    // GENERAL with several ranges: the range records in shared memory
+    // (layout_fast reserves them when the batch has at most kSmemRanges)
+    const bool smem_ranges = GENERAL && A.off_ranges != 0;
+    prologue(A, s, true, false, smem_ranges);
+    DecodeParams dpl = A.dp;
+    if (smem_ranges) dpl.ranges = s.ranges;
     // GENERAL: the activity of this tile (layout_fast puts it beside the
     // per-warp counts), flushed to the staging counters per tile
     const bool activity = GENERAL && A.tp.act_stage != nullptr;
@@ -1242,6 +1251,18 @@ direct_fast_kernel(const PassArgs args)
     int* sd = reinterpret_cast<int*>(smem + A.off_dies[0]) + tid;
     u32* wc = s.wcnt + warp * (C + 1);
     __syncthreads();
+    // GENERAL at odd channel rates: each channel's transfer ticks of the
+    // power-of-two access sizes, so that those take no division
+    u32* xtab = GENERAL && A.off_xtab && A.tp.x_shift == kXDivide
+                    ? reinterpret_cast<u32*>(smem + A.off_xtab) : nullptr;
+    if (xtab) {
+        for (u32 k = tid; k < C * kXTabSizes; k += kThreads) {
+            const u64 x = transfer_ticks(1u << (kXTabMin + k % kXTabSizes), s.chan[k / kXTabSizes],
+                                         A.tp.time_scale);
+            xtab[k] = x > 0xffffffffull ? 0xffffffffu : static_cast<u32>(x);
+        }
+        __syncthreads();
+    }
 
     // Stage tile [start, start + nt): full aligned tiles by cp.async (all
     // copies in flight before any wait), others by plain copies.
@@ -1306,15 +1327,18 @@ direct_fast_kernel(const PassArgs args)
                     // the general classification (ranges read through the
                     // cache), the channel's own transfer rate, activity
                     const TimingDecoded d = rg.valid ? classify_single(rg, A.dp, a, b, o)
-                                                     : classify_timing(A.dp, a, b, o);
+                                                     : classify_timing(dpl, a, b, o);
                     status = d.status;
                     if (d.status == kModeled) {
                         key = d.local;
                         const u32 xs = A.tp.x_shift;
+                        const u32 k = __ffs(b) - 1 - kXTabMin;  // a power-of-two size's slot
                         const u64 x = xs != kXDivide
                                           ? static_cast<u64>(static_cast<u32>(
                                                 (static_cast<u64>(b) + ((u64{1} << xs) - 1)) >> xs)) *
                                                 A.tp.time_scale
+                                      : xtab && (b & (b - 1)) == 0 && k < kXTabSizes
+                                          ? static_cast<u64>(xtab[key * kXTabSizes + k])
                                           : transfer_ticks(b, s.chan[key], A.tp.time_scale);
                         if (x > 0xffffffull) atomicOr(A.error, kErrNeedSeq);
                         info = static_cast<u32>(x & 0xffffffull) | d.die << 24 | (o & 1u) << 28;
@@ -1347,8 +1371,9 @@ direct_fast_kernel(const PassArgs args)
             }
             if (activity) {
                 // one shared-memory atomic per group of lanes with the same
-                // counter and amount (runs of accesses to one die would
-                // otherwise serialize on it)
+                // counter (runs of accesses to one die would otherwise
+                // serialize on it), carrying the group's sum (a page's
+                // bytes times 32 at most: no overflow)
                 const u64 tag = static_cast<u64>(act_add) << 32 | act_slot;
                 const u32 same = __match_any_sync(0xffffffffu, tag);
                 if (act_slot != 0xffffffffu && (same & lanes_below) == 0)
@@ -2218,7 +2243,10 @@ static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
 // inputs, the channel-sorted copy in buffers of its own (so that the next
 // tile's inputs can stream in while the chains read the sorted copy),
 // per-warp counts, segment starts, the channel table, the column-0 snapshot.
-static u32 layout_fast(PassArgs& a, u32 C, u32 K, bool general = false)
+// dynamic shared memory of a pass-1 CTA that leaves room for 3 per SM
+constexpr u32 kFastSmemBudget = 76800;
+
+static u32 layout_fast(PassArgs& a, u32 C, u32 K, bool general = false, u32 ranges = 0)
 {
     u32 off = 0;
     auto take = [&](u32 bytes) {
@@ -2254,6 +2282,12 @@ static u32 layout_fast(PassArgs& a, u32 C, u32 K, bool general = false)
         a.off_pm = a.off_red + red_bytes;
         a.off_act = a.off_pm;
         a.off_dies[0] = a.off_addr;
+        if (ranges > 1 && ranges <= kSmemRanges)
+            a.off_ranges = take(static_cast<u32>(sizeof(DevRange)) * ranges);
+        // the transfer table, where it leaves room for 3 CTAs per SM
+        a.off_xtab = 0;
+        if (align_up(off, 16) + 4 * C * kXTabSizes <= kFastSmemBudget)
+            a.off_xtab = take(4 * C * kXTabSizes);
         return align_up(off, 16);
     }
     const u32 shared = wc_bytes + red_bytes + 8 * C * K;
@@ -2413,7 +2447,9 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
         // direct_fast_kernel runs on a layout of its own
         PassArgs a1 = a;
         u32 smem1 = plan.smem_bytes;
-        if (fast_p1) smem1 = layout_fast(a1, plan.C, plan.K, general_p1);
+        if (fast_p1)
+            smem1 = layout_fast(a1, plan.C, plan.K, general_p1,
+                                dp.one.valid ? 0u : dp.range_count);
         err = cudaFuncSetAttribute(p1, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(smem1));
         if (err != cudaSuccess) return err;

@@ -44,6 +44,8 @@ def _submit(lib, ctx, fn_name, dev):
 
 STATIC_BYTES = 8 << 20      # the array's size (csrc/context.cu kStaticScratchBytes)
 STATIC_ERROR_BYTES = 256    # its padded error word
+# then the range scan's counters and flags (2 + 16384 words, padded to 256 B)
+STATIC_HEAD_BYTES = STATIC_ERROR_BYTES + (4 * (2 + 16384) + 255) // 256 * 256
 
 
 def _compare(lib, setup, arrays, tmp_path):
@@ -83,12 +85,13 @@ def test_static_entry_matches_allocating_entry(tmp_path, model, dies, stacks, n,
     arrays = wl.c0_trace(n, seed=77 + n, range_length=p["capacity_bytes"] - (1 << 20))
     if stacks == 4:
         # 64 local channels, K = 9 state words: one CTA needs
-        # C*K*(K+1) + C*K words, so the array holds at most `fits` CTAs,
+        # C*K*(K+1) + C*K words (and a share of the scan's group words), so
+        # the array holds at most `fits` CTAs,
         # while the plan asks for 2 per SM (the piece kernel, C*(K+1) > 512)
         # once a call has that many tiles of at most 2048 accesses: the grid
         # of both calls must shrink
         C, K = 16 * stacks, dies + 1
-        fits = (STATIC_BYTES - STATIC_ERROR_BYTES) // (8 * (C * K * (K + 1) + C * K))
+        fits = (STATIC_BYTES - STATIC_HEAD_BYTES) // (8 * (C * K * (K + 1) + C * K))
         sms = torch.cuda.get_device_properties(0).multi_processor_count
         smaller_call = n - n * 3 // 5
         assert -(-smaller_call // 2048) >= 2 * sms > fits
