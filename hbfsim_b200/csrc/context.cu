@@ -471,9 +471,10 @@ int run_device_batch(hbfsim_context* c, const BatchIO& io, cudaStream_t stream,
         dfree(c->d_incoming);
         dfree(c->d_scan_groups);
         const std::uint64_t ctas = std::max<std::uint64_t>(plan.ctas, 2ull * c->sm_count);
-        if (dalloc(&c->d_agg, ctas * c->C * c->K * (c->K + 1)) ||
-            dalloc(&c->d_incoming, ctas * c->C * c->K) ||
-            dalloc(&c->d_scan_groups, lb_group_words(ctas, c->C, c->K))) {
+        const std::uint64_t ranges = 2 * ctas;  // a CTA may time its tile's halves
+        if (dalloc(&c->d_agg, ranges * c->C * c->K * (c->K + 1)) ||
+            dalloc(&c->d_incoming, ranges * c->C * c->K) ||
+            dalloc(&c->d_scan_groups, lb_group_words(ranges, c->C, c->K))) {
             c->scratch_ctas = 0;
             return HBFSIM_CUDA_ERROR;
         }
@@ -484,6 +485,7 @@ int run_device_batch(hbfsim_context* c, const BatchIO& io, cudaStream_t stream,
     s.incoming = c->d_incoming;
     s.scan_groups = c->d_scan_groups;
     s.scan_lb = c->d_scan_lb;
+    s.ranges_capacity = 2 * c->scratch_ctas;
     s.error = c->d_error;
     s.last_arrival = c->d_last_arrival;
     s.counters = c->d_counters;
@@ -1180,6 +1182,7 @@ extern "C" int hbfsim_submit_access_batch_static_v1(hbfsim_context* c,
     s.incoming = s.agg + static_cast<std::uint64_t>(plan.ctas) * c->C * c->K * (c->K + 1);
     s.scan_groups = s.incoming + static_cast<std::uint64_t>(plan.ctas) * c->C * c->K;
     s.scan_lb = reinterpret_cast<std::uint32_t*>(bytes + kStaticErrorBytes);
+    s.ranges_capacity = plan.ctas;  // one range per CTA here
     s.last_arrival = c->d_last_arrival;
     s.counters = c->d_counters;
     s.state_in = c->d_state[c->cur];

@@ -156,6 +156,9 @@ struct PassArgs {
     u32 off_slot;                   // direct replay: sorted slot of each access
     u32 off_dies[2];                // direct pass 1: die words of the 32-bit chains
     u32 off_xtab;                   // general direct pass 1: transfer ticks of pow2 sizes
+    u32 off_mid;                    // halves: each channel's split point (pass 1)
+    u32 off_half;                   // halves: first-half accesses per channel (pass 2)
+    u32 halves;                     // one tile per CTA, its two halves separate ranges
     // global scratch
     i64* agg;        // [ctas][C][K][K+1]  (pass 1 out)
     i64* incoming;   // [ctas][C][K]       (pass 2 in, carried in place)
@@ -1050,17 +1053,21 @@ struct ColumnItems {
     static constexpr int kItems = 2;
     static constexpr u32 K = D + 1, KK = D + 2;
     DieRegs<D> reg[kItems];
-    u32 item_c[kItems], item_r[kItems];
+    u32 item_c[kItems], item_r[kItems], item_p[kItems];
     bool item_on[kItems], coupled[kItems];
     i64 delta[kItems];
 
-    __device__ __forceinline__ void init(u32 C)
+    // parts = 2: each channel's segment is split at the first access of the
+    // tile's second half, and each half is a range of its own (one tile
+    // per CTA, 2 C (K+1) <= kThreads items)
+    __device__ __forceinline__ void init(u32 C, u32 parts = 1)
     {
 #pragma unroll
         for (int it = 0; it < kItems; ++it) {
             const u32 q = threadIdx.x + it * kThreads;
-            item_on[it] = q < C * KK;
-            item_r[it] = q / C;
+            item_on[it] = q < parts * C * KK;
+            item_p[it] = q / (C * KK);
+            item_r[it] = q % (C * KK) / C;
             item_c[it] = q % C;
             coupled[it] = false;
             delta[it] = 0;
@@ -1073,15 +1080,20 @@ struct ColumnItems {
         }
     }
 
-    // Replay the tile's channel-sorted segments into the items' columns.
+    // Replay the tile's channel-sorted segments into the items' columns
+    // (`mid`: each channel's split point, with parts = 2).
     __device__ __forceinline__ void replay(const TileSmem& s, int* sd, bool rel32,
-                                           i64 step_max)
+                                           i64 step_max, const u32* mid = nullptr)
     {
 #pragma unroll
         for (int it = 0; it < kItems; ++it) {
             if (!item_on[it] || coupled[it]) continue;
             const u32 c = item_c[it];
-            const u32 first = s.seg[c] + c, last = s.seg[c + 1] + c;  // shifted segment
+            u32 first = s.seg[c] + c, last = s.seg[c + 1] + c;  // shifted segment
+            if (mid) {
+                if (item_p[it] == 0) last = mid[c] + c;
+                else first = mid[c] + c;
+            }
             if (first == last) continue;
             const ChanInfo ci = s.chan[c];
             if (item_r[it] == K) {
@@ -1104,12 +1116,12 @@ struct ColumnItems {
 
     // Snapshot column 0 into s_col0, then let the die columns try to couple
     // to it.  Called by every thread (contains barriers).
-    __device__ __forceinline__ void couple(i64* s_col0)
+    __device__ __forceinline__ void couple(i64* s_col0, u32 C)
     {
 #pragma unroll
         for (int it = 0; it < kItems; ++it) {
             if (!item_on[it] || item_r[it] != 0) continue;
-            i64* v0 = s_col0 + static_cast<u64>(item_c[it]) * K;
+            i64* v0 = s_col0 + static_cast<u64>(item_p[it] * C + item_c[it]) * K;
             v0[0] = reg[it].chan;
 #pragma unroll
             for (int j = 0; j < D; ++j) v0[1 + j] = reg[it].die[j];
@@ -1118,23 +1130,23 @@ struct ColumnItems {
 #pragma unroll
         for (int it = 0; it < kItems; ++it) {
             if (!item_on[it] || coupled[it] || item_r[it] == 0 || item_r[it] == K) continue;
-            coupled[it] = try_couple<D>(s_col0 + static_cast<u64>(item_c[it]) * K, reg[it],
-                                        delta[it]);
+            coupled[it] = try_couple<D>(
+                s_col0 + static_cast<u64>(item_p[it] * C + item_c[it]) * K, reg[it], delta[it]);
         }
         __syncthreads();
     }
 
-    // Write the CTA's range aggregate; s_col0 holds column 0 after the last
-    // tile of the range.
-    __device__ __forceinline__ void write(i64* agg, const i64* s_col0) const
+    // Write the CTA's range aggregates (agg: the first of them, parts of C
+    // channels each); s_col0 holds column 0 after the last tile of the range.
+    __device__ __forceinline__ void write(i64* agg, const i64* s_col0, u32 C) const
     {
 #pragma unroll
         for (int it = 0; it < kItems; ++it) {
             if (!item_on[it]) continue;
-            const u32 c = item_c[it], r = item_r[it];
-            i64* col = agg + static_cast<u64>(c) * K * KK + r;
+            const u32 c = item_c[it], r = item_r[it], pc = item_p[it] * C + c;
+            i64* col = agg + static_cast<u64>(pc) * K * KK + r;
             if (coupled[it]) {
-                const i64* v0 = s_col0 + static_cast<u64>(c) * K;
+                const i64* v0 = s_col0 + static_cast<u64>(pc) * K;
 #pragma unroll
                 for (int i = 0; i <= D; ++i)
                     col[i * KK] = is_neg_inf(v0[i]) ? kNeg : v0[i] + delta[it];
@@ -1185,9 +1197,9 @@ direct_pass_kernel(const PassArgs args)
         // at the tiles couple_now picks and after the last: snapshot column 0,
         // then let the die columns try to couple to it
         if (!couple_now(tt) && tt + 1 < A.tiles_per_cta && start + T < A.n) continue;
-        items.couple(s_col0);
+        items.couple(s_col0, C);
     }
-    items.write(agg, s_col0);
+    items.write(agg, s_col0, C);
     if (activity)
         for (u32 k = tid; k < 2 * C * D; k += kThreads)
             if (s.act[k]) atomicAdd(&A.tp.act_stage[k], s.act[k]);
@@ -1242,9 +1254,12 @@ direct_fast_kernel(const PassArgs args)
     const bool activity = GENERAL && A.tp.act_stage != nullptr;
     unsigned long long* act = reinterpret_cast<unsigned long long*>(smem + A.off_act);
 
+    // halves: one tile per CTA, two ranges (the tile's halves) per CTA
+    const u32 parts = A.halves ? 2u : 1u;
+    u32* s_mid = A.halves ? reinterpret_cast<u32*>(smem + A.off_mid) : nullptr;
     ColumnItems<D> items;
-    items.init(C);
-    i64* agg = A.agg + static_cast<u64>(blockIdx.x) * C * K * KK;
+    items.init(C, parts);
+    i64* agg = A.agg + static_cast<u64>(blockIdx.x) * parts * C * K * KK;
     const bool rel32 = !A.tp.any_order && A.tp.step_max > 0;
     const SingleRange rg = A.dp.one;
     const u32 lanes_below = (1u << lane) - 1u;
@@ -1422,6 +1437,8 @@ direct_fast_kernel(const PassArgs args)
                 for (u32 w = 0; w < kWarps; ++w) s.wcnt[w * (C + 1) + c] = offset + pre[w];
                 s.seg[c] = offset;
                 if (c == C - 1) s.seg[C] = offset + tot;
+                // the split point: warps kWarps/2.. hold the tile's second half
+                if (s_mid) s_mid[c] = offset + pre[kWarps / 2];
             }
             __syncthreads();
         }
@@ -1455,12 +1472,12 @@ direct_fast_kernel(const PassArgs args)
         if (activity)
             for (u32 k = tid; k < 2 * C * D; k += kThreads)
                 if (act[k]) atomicAdd(&A.tp.act_stage[k], act[k]);
-        items.replay(s, sd, rel32, A.tp.step_max);
+        items.replay(s, sd, rel32, A.tp.step_max, s_mid);
         __syncthreads();
         if (!couple_now(tt) && tt + 1 < A.tiles_per_cta && start + T < A.n) continue;
-        items.couple(s_col0);
+        items.couple(s_col0, C);
     }
-    items.write(agg, s_col0);
+    items.write(agg, s_col0, C);
 }
 
 // ---------------------------------------------------------------------------
@@ -1500,7 +1517,7 @@ __device__ __forceinline__ void stage_records(const PassArgs& A, const TileSmem&
 
 constexpr u32 kOutBatch = 8;  // tiles hold at most 2048 = 8 x kThreads accesses
 
-template <int D, bool NOADMIT>
+template <int D, bool NOADMIT, bool HALVES = false>
 __global__ void __launch_bounds__(kThreads, 3)
 direct_replay_kernel(const PassArgs args)
 {
@@ -1515,10 +1532,14 @@ direct_replay_kernel(const PassArgs args)
     if (*A.error != 0) return;  // pass 1 refused or rerouted the batch
     prologue(A, s, true, false, false);
 
+    // halves: threads c and C + c replay channel c's first and second half
+    // of the (one) tile, each from its own incoming state
+    constexpr u32 parts = HALVES ? 2u : 1u;
+    u32* s_half = HALVES ? reinterpret_cast<u32*>(smem + A.off_half) : nullptr;
     DieRegs<D> reg;
-    const bool chain = tid < C;
+    const bool chain = tid < parts * C;
     if (chain) {
-        const i64* cv = A.incoming + (static_cast<u64>(blockIdx.x) * C + tid) * K;
+        const i64* cv = A.incoming + (static_cast<u64>(blockIdx.x) * parts * C + tid) * K;
         reg.chan = cv[0];
 #pragma unroll
         for (int j = 0; j < D; ++j) reg.die[j] = cv[1 + j];
@@ -1536,6 +1557,8 @@ direct_replay_kernel(const PassArgs args)
         const u32 nt = tile_size(start);
         cp_async_wait_all();
         for (u32 c = tid; c <= C; c += kThreads) s.seg[c] = 0;
+        if (HALVES)
+            for (u32 c = tid; c < C; c += kThreads) s_half[c] = 0;
         __syncthreads();
         // unpack: sorted copy, access -> slot, statuses, untimed outputs
         for (u32 j = tid; j < nt; j += kThreads) {
@@ -1551,6 +1574,7 @@ direct_replay_kernel(const PassArgs args)
                                     : imax(static_cast<i64>(arr), s.chan[r >> 56].admit);
                 slot_of[j] = static_cast<u16>(k);
                 atomicAdd(&s.seg[r >> 56], 1u);
+                if (HALVES && j < T / 2) atomicAdd(&s_half[r >> 56], 1u);
                 ++st.modeled;
             } else {
                 slot_of[j] = 0xffffu;
@@ -1567,8 +1591,12 @@ direct_replay_kernel(const PassArgs args)
         // the staging buffers are free: stream the next tile in
         const u64 next = start + T;
         if (tt + 1 < A.tiles_per_cta && next < A.n) stage_records(A, s, next, tile_size(next));
-        const u32 c = tid;
-        const u32 first = chain ? s.seg[c] + c : 0u, last = chain ? s.seg[c + 1] + c : 0u;
+        const u32 c = HALVES ? tid % C : tid, part = HALVES ? tid / C : 0u;
+        u32 first = chain ? s.seg[c] + c : 0u, last = chain ? s.seg[c + 1] + c : 0u;
+        if (HALVES && chain) {
+            if (part == 0) last = s.seg[c] + s_half[c] + c;
+            else first = s.seg[c] + s_half[c] + c;
+        }
         const ChanInfo ci = chain ? s.chan[c] : ChanInfo{};
         if (first < last &&
             !(rel32 && replay_rel32<D, true, true, false>(reg, sd, s.sarr, s.sinfo, first, last, ci,
@@ -1789,10 +1817,12 @@ __global__ void __launch_bounds__(kScanWarps * 32) range_scan_kernel(const ScanA
 //   A  each warp composes its m range maps (kept staged for C);
 //   P  the warps' maps form an inclusive prefix (Hillis-Steele, 3 rounds);
 //      the last is the group's map, published as an aggregate (flag 1);
-//   L  warp 0 walks back over the preceding groups of channel c, composing
-//      their published maps until it meets a group that published its
-//      outgoing state (flag 2), and applies the composite to it: the group's
-//      incoming state; it publishes its own outgoing state (flag 2);
+//   L  warp 0 reads the flags of the preceding groups of channel c at once
+//      (one lane per group, at most 31), starts from the nearest group that
+//      published its outgoing state (flag 2; before group 0, the carried
+//      state) and applies the published maps of the groups after it, fetched
+//      together: the group's incoming state; it publishes its own outgoing
+//      state (flag 2);
 //   C  each warp applies the prefix of the warps before it and walks its
 //      ranges, writing every range's incoming state.
 // Flags live at a fixed address and are cleared by the last CTA to finish;
@@ -1801,6 +1831,7 @@ constexpr u32 kLbWarps = 8;
 constexpr u32 kLbRangesPerWarp = 4;
 constexpr u32 kLbRanges = kLbWarps * kLbRangesPerWarp;  // ranges per group
 constexpr u32 kLbSpins = 1u << 22;
+constexpr u32 kLbMaxGroups = 32;  // groups of one channel (the look-back window)
 
 struct LbScanArgs {
     i64* gmap;     // [groups][C][K][K+1] published group maps
@@ -1883,9 +1914,8 @@ __global__ void __launch_bounds__(kLbWarps * 32) range_scan_lb_kernel(const Scan
     i64* stage = reinterpret_cast<i64*>(smem) + static_cast<u64>(warp) * kLbRangesPerWarp * per;
     i64* pm = reinterpret_cast<i64*>(smem) + static_cast<u64>(kLbWarps) * kLbRangesPerWarp * per;
     i64* pm2 = pm + static_cast<u64>(kLbWarps) * per;        // prefix double buffer
-    i64* acc = pm2 + static_cast<u64>(kLbWarps) * per;       // look-back composite (warp 0)
-    i64* tmp = acc + per;                                    // a fetched map
-    i64* gin = tmp + per;                                    // [warps][K] incoming states
+    i64* maps = pm2 + static_cast<u64>(kLbWarps) * per;      // look-back: fetched maps
+    i64* gin = maps + static_cast<u64>(kLbMaxGroups - 1) * per;  // [warps][K] incoming states
     const u32 n = a.ctas;
     const u32 w0 = g * kLbRanges + warp * kLbRangesPerWarp;
     const u32 w1 = w0 + kLbRangesPerWarp < n ? w0 + kLbRangesPerWarp : n;
@@ -1934,37 +1964,36 @@ __global__ void __launch_bounds__(kLbWarps * 32) range_scan_lb_kernel(const Scan
                 __threadfence();
                 atomicExch(my_flag, 1u);
             }
-            identity_map(acc, K);
-            for (int j = static_cast<int>(g) - 1; j >= 0; --j) {
-                const u32* f = flags + static_cast<u32>(j) * C + c;
-                u32 fv = 0;
-                if (lane == 0) {
-                    for (u32 spins = 0;; ++spins) {
-                        fv = *reinterpret_cast<const volatile u32*>(f);
-                        if (fv != 0) break;
-                        if (spins >= kLbSpins) break;
-                        __nanosleep(32);
-                    }
-                    __threadfence();
+            // the window of preceding groups (at most 31): lane k watches
+            // group g - 1 - k, and a lane before group 0 stands for the
+            // carried state; the nearest group that published its
+            // outgoing state starts the walk, the maps of the groups after
+            // it are fetched at once and applied in order
+            const int j = static_cast<int>(g) - 1 - static_cast<int>(lane);
+            u32 fv = 2;
+            if (j >= 0) {
+                const volatile u32* f = flags + static_cast<u32>(j) * C + c;
+                fv = *f;
+                for (u32 spins = 0; fv == 0 && spins < kLbSpins; ++spins) {
+                    __nanosleep(32);
+                    fv = *f;
                 }
-                fv = __shfl_sync(0xffffffffu, fv, 0);
-                __threadfence();  // every lane reads the published words after the flag
-                if (fv == 0) {  // gave up: carry on from the carried state
-                    failed = true;
-                    x = lane < K ? static_cast<i64>(a.state_in[static_cast<u64>(c) * K + lane]) : 0;
-                    break;
-                }
-                if (fv == 2) {
-                    const i64 y = lane < K ? __ldcg(b.gstate + (static_cast<u64>(j) * C + c) * K + lane)
-                                           : 0;
-                    x = apply_map(acc, y, K);
-                    break;
-                }
-                const i64* src = b.gmap + (static_cast<u64>(j) * C + c) * per;
-                for (u32 e = lane; e < per; e += 32) tmp[e] = __ldcg(src + e);
-                __syncwarp();
-                compose_maps(acc, acc, tmp, K);
             }
+            __threadfence();  // the published words after the flags
+            failed = __any_sync(0xffffffffu, fv == 0);
+            const u32 have = __ballot_sync(0xffffffffu, fv == 2);
+            const u32 kstar = failed ? 31u : static_cast<u32>(__ffs(have)) - 1u;
+            const int jstar = failed ? -1 : static_cast<int>(g) - 1 - static_cast<int>(kstar);
+            if (lane < K)
+                x = jstar >= 0 ? __ldcg(b.gstate + (static_cast<u64>(jstar) * C + c) * K + lane)
+                               : static_cast<i64>(a.state_in[static_cast<u64>(c) * K + lane]);
+            const u32 count = failed ? 0u : kstar;  // groups jstar + 1 .. g - 1
+            for (u32 w = lane; w < count * per; w += 32) {
+                const u32 q = w / per, e = w - q * per;
+                maps[w] = __ldcg(b.gmap + ((static_cast<u64>(jstar) + 1 + q) * C + c) * per + e);
+            }
+            __syncwarp();
+            for (u32 q = 0; q < count; ++q) x = apply_map(maps + static_cast<u64>(q) * per, x, K);
         }
         if (lane < K) gin[lane] = x;
         // outgoing state of the group
@@ -2212,6 +2241,7 @@ static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
         a.off_sarr[1] = take(8 * (T + C));
         a.off_sinfo[1] = take(4 * (T + C));
         a.off_slot = take(2 * T);
+        a.off_half = take(4 * C);
         a.off_dies[1] = 0;
         const u32 end2 = align_up(off, 16);
         return end1 > end2 ? end1 : end2;
@@ -2246,7 +2276,8 @@ static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
 // dynamic shared memory of a pass-1 CTA that leaves room for 3 per SM
 constexpr u32 kFastSmemBudget = 76800;
 
-static u32 layout_fast(PassArgs& a, u32 C, u32 K, bool general = false, u32 ranges = 0)
+static u32 layout_fast(PassArgs& a, u32 C, u32 K, bool general = false, u32 ranges = 0,
+                       bool halves = false)
 {
     u32 off = 0;
     auto take = [&](u32 bytes) {
@@ -2271,12 +2302,14 @@ static u32 layout_fast(PassArgs& a, u32 C, u32 K, bool general = false, u32 rang
     const u32 wc_bytes = align_up(4 * kWarps * (C + 1), 16);
     const u32 red_bytes = 8 * 8 * kWarps;
     const u32 dies_bytes = 4 * (K - 1) * kThreads;
+    const u32 col0_bytes = 8 * C * K * (halves ? 2 : 1);  // a snapshot per range
     a.off_key = a.off_rank = a.off_ord = a.off_act = a.off_ranges = 0;
+    a.off_mid = halves ? take(4 * C) : 0;
     if (general) {
         // no prefetch: the die words overlay the staged addresses (dead once
         // decoded); the tile's activity (flushed before the chains) and the
         // column-0 snapshot (taken after them) share a slot
-        const u32 pm_bytes = align_up(8 * C * K, 16), act_bytes = 16 * C * (K - 1);
+        const u32 pm_bytes = align_up(col0_bytes, 16), act_bytes = 16 * C * (K - 1);
         a.off_wcnt = take(wc_bytes + red_bytes + (pm_bytes > act_bytes ? pm_bytes : act_bytes));
         a.off_red = a.off_wcnt + wc_bytes;
         a.off_pm = a.off_red + red_bytes;
@@ -2290,7 +2323,7 @@ static u32 layout_fast(PassArgs& a, u32 C, u32 K, bool general = false, u32 rang
             a.off_xtab = take(4 * C * kXTabSizes);
         return align_up(off, 16);
     }
-    const u32 shared = wc_bytes + red_bytes + 8 * C * K;
+    const u32 shared = wc_bytes + red_bytes + col0_bytes;
     a.off_wcnt = take(shared > dies_bytes ? shared : dies_bytes);
     a.off_red = a.off_wcnt + wc_bytes;
     a.off_pm = a.off_red + red_bytes;
@@ -2444,12 +2477,36 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
                 break;
             }
         }
+        // One tile per CTA and few column items: the tile's halves are
+        // ranges of their own, so that twice the items and chains (pass 1
+        // and pass 2) each walk half a segment.
+        const bool halves = fast_p1 && plan.tiles_per_cta == 1 &&
+                            2 * plan.C * (plan.K + 1) <= static_cast<u32>(kThreads) &&
+                            s.ranges_capacity >= 2ull * plan.ctas;
+        a.halves = halves ? 1u : 0u;
+        if (halves) {
+            const bool z = tp.admit_zero != 0;
+            switch (plan.dies) {
+            case 1:
+                p2 = z ? direct_replay_kernel<1, true, true> : direct_replay_kernel<1, false, true>;
+                break;
+            case 2:
+                p2 = z ? direct_replay_kernel<2, true, true> : direct_replay_kernel<2, false, true>;
+                break;
+            case 4:
+                p2 = z ? direct_replay_kernel<4, true, true> : direct_replay_kernel<4, false, true>;
+                break;
+            default:
+                p2 = z ? direct_replay_kernel<8, true, true> : direct_replay_kernel<8, false, true>;
+                break;
+            }
+        }
         // direct_fast_kernel runs on a layout of its own
         PassArgs a1 = a;
         u32 smem1 = plan.smem_bytes;
         if (fast_p1)
             smem1 = layout_fast(a1, plan.C, plan.K, general_p1,
-                                dp.one.valid ? 0u : dp.range_count);
+                                dp.one.valid ? 0u : dp.range_count, halves);
         err = cudaFuncSetAttribute(p1, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(smem1));
         if (err != cudaSuccess) return err;
@@ -2468,7 +2525,7 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
         sa.last_arrival = s.last_arrival;
         sa.arrival = io.arrival;
         sa.n = io.n;
-        sa.ctas = plan.ctas;
+        sa.ctas = halves ? 2 * plan.ctas : plan.ctas;  // ranges
         sa.C = plan.C;
         sa.K = plan.K;
         sa.counters = s.counters;
@@ -2478,11 +2535,12 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
         sa.die_writes = tp.die_writes;
         // per warp: `chunk` staged aggregates and the group's composite
         const u32 per = plan.K * (plan.K + 1);
-        const u32 group = (plan.ctas + kScanWarps - 1) / kScanWarps;
+        const u32 group = (sa.ctas + kScanWarps - 1) / kScanWarps;
         const u32 room = (96u * 1024u / 8u) / kScanWarps - per;
         sa.chunk = std::max(1u, std::min(group, room / per));
-        const u32 groups = (plan.ctas + kLbRanges - 1) / kLbRanges;
-        if (s.scan_lb && s.scan_groups && static_cast<u64>(groups) * plan.C <= kLbFlagWords) {
+        const u32 groups = (sa.ctas + kLbRanges - 1) / kLbRanges;
+        if (s.scan_lb && s.scan_groups && groups <= kLbMaxGroups &&
+            static_cast<u64>(groups) * plan.C <= kLbFlagWords) {
             // several CTAs per channel, chained by look-back
             LbScanArgs lb{};
             lb.gmap = s.scan_groups;
@@ -2490,8 +2548,12 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
             lb.ctr = s.scan_lb;
             lb.groups = groups;
             const u32 lb_smem =
-                8u * (kLbWarps * kLbRangesPerWarp * per + 2 * kLbWarps * per + 2 * per +
-                      kLbWarps * plan.K);
+                8u * (kLbWarps * kLbRangesPerWarp * per + 2 * kLbWarps * per +
+                      (kLbMaxGroups - 1) * per + kLbWarps * plan.K);
+            err = cudaFuncSetAttribute(range_scan_lb_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(lb_smem));
+            if (err != cudaSuccess) return err;
             hooks(kSlotScan, 0, stream);
             range_scan_lb_kernel<<<groups * plan.C, kLbWarps * 32, lb_smem, stream>>>(sa, lb);
             hooks(kSlotScan, 1, stream);

@@ -39,6 +39,8 @@ struct BatchScratch {
     // before the first batch (each scan leaves them zero)
     i64* scan_groups = nullptr;
     u32* scan_lb = nullptr;
+    // ranges agg / incoming / scan_groups can hold (a CTA may time two)
+    u64 ranges_capacity = 0;
 };
 
 constexpr u32 kLbFlagWords = 16384;  // groups x local channels of one scan, at most
