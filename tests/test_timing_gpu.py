@@ -373,17 +373,22 @@ def test_host_buffer_path_matches_device_path(tmp):
     assert_same((out.done_ns, out.latency_ns, out.status), want, "host path")
 
 
-@pytest.mark.parametrize("dies,stacks", [(1, 1), (2, 2), (3, 1), (8, 1), (4, 16), (8, 4)])
-def test_kernel_variants(tmp, dies, stacks):
+@pytest.mark.parametrize("dies,stacks,channels", [(1, 1, 16), (2, 2, 16), (3, 1, 16), (8, 1, 16),
+                                                  (4, 16, 16), (8, 4, 16), (8, 1, 8),
+                                                  (4, 1, 4)])
+def test_kernel_variants(tmp, dies, stacks, channels):
     """Direct (register) kernels for D in {1,2,4,8} with few channels, piece
-    kernels for other D or many channels: all bit-exact."""
+    kernels for other D or many channels: all bit-exact.  With one tile per
+    CTA and 2 C (D + 2) <= 256 (D = 8 on 8 channels, D = 4 on 4, D = 1 and 2
+    on 16) each tile's halves are timed as two ranges."""
     p = wl.c0_profile()
     p["dies_per_channel"] = dies
-    p["capacity_bytes"] = p["page_bytes"] * 16 * dies * 4 * 256 * 64
+    p["channels"] = channels
+    p["capacity_bytes"] = p["page_bytes"] * channels * dies * 4 * 256 * 64
     s = Setup(profile=p, model=3, stacks=stacks, stripe=4096)
     s.ranges = [(wl.RANGE_BASE, p["capacity_bytes"] - (1 << 20), 1, 3)]
     ctx = make_context(s, tmp)
-    arrays = wl.c0_trace(60000, seed=dies * 10 + stacks,
+    arrays = wl.c0_trace(60000, seed=dies * 10 + stacks + channels,
                          range_length=p["capacity_bytes"] - (1 << 20))
     ora = OracleRun(s)
     assert_same(gpu_run(ctx, arrays), ora.run(*arrays, threads=4), f"D={dies} S={stacks}")
