@@ -2225,6 +2225,10 @@ static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
         a.off_bytes = take(4 * T);
         a.off_key = take(2 * T);
         a.off_rank = take(2 * T);
+        // the chains' die words (below) overlay the key and rank arrays;
+        // short tiles leave them less room than the words need
+        const u32 dies_bytes = 4 * (K - 1) * kThreadsDie;
+        if (4 * T < dies_bytes) take(dies_bytes - 4 * T);
         a.off_wcnt = take(4 * kWarps * (C + 1));
         a.off_act = take(16 * C * D);
         a.off_ranges = take(static_cast<u32>(sizeof(DevRange)) * kSmemRanges);
@@ -2366,6 +2370,13 @@ int plan_batch(u64 n, u32 C, u32 K, u32 dies, int sm_count, BatchPlan* plan)
             else if (T > 512) T /= 2;
             else return -1;
         }
+    }
+    // small batches: shorter tiles (down to 256 accesses, one per thread),
+    // so that at least one runs per SM (a tile's time is latency-bound;
+    // media-action pieces are a few thousand accesses)
+    while (T > 256 && (n + T - 1) / T < static_cast<u64>(sm_count)) {
+        T /= 2;
+        if (direct) L = T;
     }
     const u64 tiles = (n + T - 1) / T;
     const u64 max_ctas = static_cast<u64>(sm_count) * per_sm;
