@@ -315,37 +315,30 @@ __global__ void tridiag_kernel(const double* rhs, int nx, int ny, int nz, const 
     tridiag_mode(m, rhs, nx, ny, nz, base, gx, gy, gz, lx, ly, out, false);
 }
 
-// Mean temperature of global die d over its own cell list, by one CTA of
-// kDieThreads threads (fixed summation order: strided partial sums, then a
-// tree); `red` holds kDieThreads doubles.
-constexpr int kDieThreads = 128;
-
+// Mean temperature of global die d over its own cell list, by one warp
+// (fixed summation order: lane-strided partial sums, then a shuffle tree).
 __device__ __forceinline__ void die_mean(int d, const double* t, const int* die_start,
                                          const int* die_list, const double* die_cells,
-                                         double* red, double* mean_out)
+                                         double* mean_out)
 {
+    const int lane = threadIdx.x & 31;
     double s = 0.0;
-    for (int k = die_start[d] + threadIdx.x; k < die_start[d + 1]; k += kDieThreads)
-        s += t[die_list[k]];
-    red[threadIdx.x] = s;
-    __syncthreads();
-    for (int o = kDieThreads / 2; o > 0; o >>= 1) {
-        if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
-        __syncthreads();
-    }
-    if (threadIdx.x == 0) mean_out[d] = die_cells[d] > 0 ? red[0] / die_cells[d] : 0.0;
-    __syncthreads();
+    for (int k = die_start[d] + lane; k < die_start[d + 1]; k += 32) s += t[die_list[k]];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_down_sync(0xffffffffu, s, o);
+    if (lane == 0) mean_out[d] = die_cells[d] > 0 ? s / die_cells[d] : 0.0;
 }
 
-__global__ void __launch_bounds__(kDieThreads) die_temp_kernel(const double* t,
-                                                               const int* die_start,
-                                                               const int* die_list, int dies,
-                                                               const double* die_cells,
-                                                               double* mean_out)
+constexpr int kDieWarps = 4;  // warps (dies) per CTA of die_temp_kernel
+
+__global__ void __launch_bounds__(kDieWarps * 32) die_temp_kernel(const double* t,
+                                                                const int* die_start,
+                                                                const int* die_list, int dies,
+                                                                const double* die_cells,
+                                                                double* mean_out)
 {
-    __shared__ double red[kDieThreads];
-    if (static_cast<int>(blockIdx.x) < dies)
-        die_mean(blockIdx.x, t, die_start, die_list, die_cells, red, mean_out);
+    const int d = blockIdx.x * kDieWarps + (threadIdx.x >> 5);
+    if (d < dies) die_mean(d, t, die_start, die_list, die_cells, mean_out);
 }
 
 struct ControllerArgs {
@@ -723,9 +716,7 @@ __global__ void __launch_bounds__(kEpochThreads) thermal_epoch_kernel(const Epoc
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ unsigned long long dbar, cbar[4];
     __shared__ int failed, pending, cpend;
-    __shared__ double red[kDieThreads];
     __shared__ double cdt[32], gbtb[32], base[32];  // per layer
-    static_assert(kDieThreads == kEpochThreads, "die means use the CTA");
     const int tid = threadIdx.x;
     const int Kmax = e.nx > e.ny ? e.nx : e.ny;
     const int panel = kBM * a_row(Kmax);
@@ -808,9 +799,11 @@ __global__ void __launch_bounds__(kEpochThreads) thermal_epoch_kernel(const Epoc
     epoch_gemm(gemm[3], cslot + 3 * panel, dslot, sync_of(3));
     grid_barrier(e.bar, &failed);
     // 6. die means
-    if (!failed)
-        for (int d = blockIdx.x; d < e.dies; d += gridDim.x)
-            die_mean(d, e.t, e.die_start, e.die_list, e.die_cells, red, e.die_temp);
+    if (!failed) {
+        const int warps = kEpochThreads / 32;
+        for (int d = blockIdx.x * warps + (tid >> 5); d < e.dies; d += gridDim.x * warps)
+            die_mean(d, e.t, e.die_start, e.die_list, e.die_cells, e.die_temp);
+    }
     grid_barrier(e.bar, &failed);
     // 7. the controller, on CTA 0
     if (blockIdx.x == 0 && !failed) controller_body(e.ctl);
@@ -973,9 +966,9 @@ int advance(hbfsim_context* c, double epoch_s, const unsigned long long* rb,
     // inverse: W0_z = Qy W1_z, then T = W0 Qx^T
     dgemm(t->ny, t->nx, t->ny, t->d_qy, 0, 0, t->d_w1, plane, 0, t->d_w0, plane, t->nz, s);
     dgemm(t->nz * t->ny, t->nx, t->nx, t->d_w0, 0, 0, t->d_qx, 0, 1, t->d_t, 0, 1, s);
-    die_temp_kernel<<<t->dies_total, kDieThreads, 0, s>>>(t->d_t, t->d_die_start, t->d_die_list,
-                                                   static_cast<int>(t->dies_total),
-                                                   t->d_die_cells, t->d_die_temp);
+    die_temp_kernel<<<(t->dies_total + kDieWarps - 1) / kDieWarps, kDieWarps * 32, 0, s>>>(
+        t->d_t, t->d_die_start, t->d_die_list, static_cast<int>(t->dies_total), t->d_die_cells,
+        t->d_die_temp);
     hooks(kSlotThermal, 1, s);
     hooks(kSlotController, 0, s);
     controller_kernel<<<1, 1024, 0, s>>>(a);
