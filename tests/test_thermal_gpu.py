@@ -72,9 +72,12 @@ def thresholds_from(trajectory):
             "light_permille": 1250, "severe_permille": 2000}
 
 
-def test_grid_and_controller_match_oracle(tmp_path):
+@pytest.mark.parametrize("nx,ny", [(16, 16), (18, 18)])
+def test_grid_and_controller_match_oracle(tmp_path, nx, ny):
+    """The epoch step as one cooperative kernel (sides multiples of 4) and as
+    separate launches (18 x 18): grid, die means and factors."""
     import torch
-    stacks, dies, nx, ny = 2, 4, 16, 16
+    stacks, dies = 2, 4
     setup = make(tmp_path, stacks)
     channels = stacks * setup.profile["channels"]
     n_dies = channels * dies
