@@ -1649,9 +1649,10 @@ direct_replay_kernel(const PassArgs args)
 }
 
 // Range scan: incoming_b = R_{b-1} ... R_0 (state), one CTA per local
-// channel (channels are independent).  Each range aggregate R is a max-plus
-// affine map x -> max(R[:, :K] + x, R[:, K]) (K state words).  The CTA's 32
-// warps split the ranges into 8 groups:
+// channel (channels are independent); range_scan_lb_kernel below replaces
+// it whenever a channel's ranges fit 32 groups of 32.  Each range aggregate
+// R is a max-plus affine map x -> max(R[:, :K] + x, R[:, K]) (K state
+// words).  The CTA's 32 warps split the ranges into 32 groups, one each:
 //   A  each warp composes its group into one map (one lane per entry,
 //      clamping sums below -2^61 back to NEG so that they cannot overflow);
 //   B  warp 0 applies the 32 group maps to the carried state, giving each
