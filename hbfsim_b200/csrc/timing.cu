@@ -128,6 +128,104 @@ __device__ __forceinline__ TimingDecoded classify_single(const SingleRange& r,
     return d;
 }
 
+// The exact sequential walk with the reference's saturating unsigned
+// arithmetic, for one local channel c: the batch in order, the accesses of
+// channel c timed, the untimed ones written by channel 0's thread.
+template <int MODEL>
+__device__ void sequential_walk(const DecodeParams& dp, const TimingParams& tp,
+                                const u64* address, const u32* bytes, const u8* op,
+                                const u64* arrival, u64* done_out, u64* latency, u8* status,
+                                u64 n, u32 K, const u64* state_in, u64* state_out,
+                                u64* last_arrival, DevCounters* counters, u32 c)
+{
+    struct {
+        const DecodeParams& dp;
+        const TimingParams& tp;
+        const u64* address;
+        const u32* bytes;
+        const u8* op;
+        const u64* arrival;
+        u64* done;
+        u64* latency;
+        u8* status;
+        u64 n;
+        u32 K;
+        const u64* state_in;
+        u64* state_out;
+        u64* last_arrival;
+        DevCounters* counters;
+    } a{dp, tp, address, bytes, op, arrival, done_out, latency, status, n, K, state_in,
+        state_out, last_arrival, counters};
+    u64 st[17];
+    for (u32 k = 0; k < a.K; ++k) st[k] = a.state_in[static_cast<u64>(c) * a.K + k];
+    unsigned long long n_mod = 0, n_byp = 0, n_uns = 0, n_for = 0, lat = 0,
+                       mx = 0, fast = 0;
+    for (u64 i = 0; i < a.n; ++i) {
+        const u64 arr = a.arrival[i];
+        const Decoded d = classify_decode(a.dp, a.address[i], a.bytes[i], a.op[i],
+                                          MODEL == kModelDie);
+        const u32 key = MODEL == kModelDie ? d.local : 0u;
+        if (d.status != kModeled) {
+            if (c == 0) {
+                a.done[i] = arr;
+                a.latency[i] = 0;
+                a.status[i] = static_cast<u8>(d.status);
+                if (d.status == kBypass) ++n_byp;
+                else if (d.status == kForeign) ++n_for;
+                else ++n_uns;
+            }
+            continue;
+        }
+        if (key != c) continue;
+        u64 done;
+        if (MODEL == kModelFast) {
+            const u64 x = static_cast<u64>(a.tp.fast_x);  // host: already saturated
+            const u64 lat_op = static_cast<u64>(a.op[i] ? a.tp.fast_l_prog : a.tp.fast_l_read);
+            const u64 s = st[0] > arr ? st[0] : arr;
+            st[0] = sat_add_u64(s, x);
+            const u64 lt = sat_add_u64(arr, lat_op);
+            done = lt > st[0] ? lt : st[0];
+            fast += a.op[i] ? a.tp.fast_service_prog : a.tp.fast_service_read;
+        } else {
+            const u64 bw = a.tp.chan_bw[c];
+            const u64 num = static_cast<u64>(a.bytes[i]) * 1000000000ull;
+            const u64 x = sat_mul_u64(num / bw + (num % bw != 0), a.tp.time_scale);
+            const u64 top = static_cast<u64>(a.op[i] ? a.tp.chan_t_prog[c] : a.tp.chan_t_read[c]);
+            u64 s = arr;
+            const u64 admit = static_cast<u64>(a.tp.chan_admit[c]);
+            if (admit > s) s = admit;
+            if (st[0] > s) s = st[0];
+            if (st[1 + d.die] > s) s = st[1 + d.die];
+            st[0] = sat_add_u64(s, x);
+            st[1 + d.die] = sat_add_u64(st[0], top);
+            done = st[1 + d.die];
+            if (a.tp.die_read_bytes) {  // this thread owns channel c's dies
+                const u64 k = static_cast<u64>(c) * a.tp.dies + d.die;
+                if (a.op[i]) a.tp.die_writes[k] += 1;
+                else a.tp.die_read_bytes[k] += a.bytes[i];
+            }
+        }
+        a.done[i] = done;
+        a.latency[i] = done - arr;
+        a.status[i] = kModeled;
+        ++n_mod;
+        lat += done - arr;
+        mx = done > mx ? done : mx;
+    }
+    for (u32 k = 0; k < a.K; ++k) a.state_out[static_cast<u64>(c) * a.K + k] = st[k];
+    atomicAdd(&a.counters->modeled, n_mod);
+    if (c == 0) {
+        atomicAdd(&a.counters->bypass, n_byp);
+        atomicAdd(&a.counters->foreign, n_for);
+        atomicAdd(&a.counters->unsupported, n_uns);
+        atomicAdd(&a.counters->batches, 1ull);
+        if (a.n) *a.last_arrival = a.arrival[a.n - 1];
+    }
+    atomicAdd(&a.counters->latency_sum, lat);
+    atomicAdd(&a.counters->fast_modeled_ns, fast);
+    atomicMax(&a.counters->max_done, mx);
+}
+
 // ---------------------------------------------------------------- kernels
 struct PassArgs {
     DecodeParams dp;
@@ -166,6 +264,7 @@ struct PassArgs {
     const u64* last_arrival;  // last arrival of the previous batch
     const u64* state_in;      // carried state (checked against the tick limit)
     DevCounters* counters;
+    u64* state_out;           // direct pass 2: the sequential walk's final state
 };
 
 constexpr int kThreads = 256;
@@ -1517,7 +1616,7 @@ __device__ __forceinline__ void stage_records(const PassArgs& A, const TileSmem&
 
 constexpr u32 kOutBatch = 8;  // tiles hold at most 2048 = 8 x kThreads accesses
 
-template <int D, bool NOADMIT, bool HALVES = false>
+template <int D, bool NOADMIT, bool HALVES = false, bool WALK = false>
 __global__ void __launch_bounds__(kThreads, 3)
 direct_replay_kernel(const PassArgs args)
 {
@@ -1529,7 +1628,16 @@ direct_replay_kernel(const PassArgs args)
     const TileSmem s = tile_views(smem, A, 2);
     u16* slot_of = reinterpret_cast<u16*>(smem + A.off_slot);  // access -> sorted slot
     int* sd = nullptr;  // pass 2 keeps its chains' die words in registers
-    if (*A.error != 0) return;  // pass 1 refused or rerouted the batch
+    if (const u32 err = *A.error) {
+        // pass 1 refused the batch, or rerouted it to the exact sequential
+        // walk; WALK (small batches, where a launch of its own costs as much
+        // as the pass): CTA 0 runs that walk here, one thread per channel
+        if (WALK && !(err & kErrUnsorted) && (err & kErrNeedSeq) && blockIdx.x == 0 && tid < C)
+            sequential_walk<kModelDie>(A.dp, A.tp, A.address, A.bytes, A.op, A.arrival, A.done,
+                                       A.latency, A.status, A.n, K, A.state_in, A.state_out,
+                                       const_cast<u64*>(A.last_arrival), A.counters, tid);
+        return;
+    }
     prologue(A, s, true, false, false);
 
     // halves: threads c and C + c replay channel c's first and second half
@@ -2077,74 +2185,9 @@ __global__ void sequential_kernel(const SeqArgs a)
     const u32 c = blockIdx.x * blockDim.x + threadIdx.x;
     const u32 flags = *a.error;
     if ((flags & kErrUnsorted) || !(flags & kErrNeedSeq) || c >= a.C) return;
-    u64 st[17];
-    for (u32 k = 0; k < a.K; ++k) st[k] = a.state_in[static_cast<u64>(c) * a.K + k];
-    unsigned long long n_mod = 0, n_byp = 0, n_uns = 0, n_for = 0, lat = 0,
-                       mx = 0, fast = 0;
-    for (u64 i = 0; i < a.n; ++i) {
-        const u64 arr = a.arrival[i];
-        const Decoded d = classify_decode(a.dp, a.address[i], a.bytes[i], a.op[i],
-                                          MODEL == kModelDie);
-        const u32 key = MODEL == kModelDie ? d.local : 0u;
-        if (d.status != kModeled) {
-            if (c == 0) {
-                a.done[i] = arr;
-                a.latency[i] = 0;
-                a.status[i] = static_cast<u8>(d.status);
-                if (d.status == kBypass) ++n_byp;
-                else if (d.status == kForeign) ++n_for;
-                else ++n_uns;
-            }
-            continue;
-        }
-        if (key != c) continue;
-        u64 done;
-        if (MODEL == kModelFast) {
-            const u64 x = static_cast<u64>(a.tp.fast_x);  // host: already saturated
-            const u64 lat_op = static_cast<u64>(a.op[i] ? a.tp.fast_l_prog : a.tp.fast_l_read);
-            const u64 s = st[0] > arr ? st[0] : arr;
-            st[0] = sat_add_u64(s, x);
-            const u64 lt = sat_add_u64(arr, lat_op);
-            done = lt > st[0] ? lt : st[0];
-            fast += a.op[i] ? a.tp.fast_service_prog : a.tp.fast_service_read;
-        } else {
-            const u64 bw = a.tp.chan_bw[c];
-            const u64 num = static_cast<u64>(a.bytes[i]) * 1000000000ull;
-            const u64 x = sat_mul_u64(num / bw + (num % bw != 0), a.tp.time_scale);
-            const u64 top = static_cast<u64>(a.op[i] ? a.tp.chan_t_prog[c] : a.tp.chan_t_read[c]);
-            u64 s = arr;
-            const u64 admit = static_cast<u64>(a.tp.chan_admit[c]);
-            if (admit > s) s = admit;
-            if (st[0] > s) s = st[0];
-            if (st[1 + d.die] > s) s = st[1 + d.die];
-            st[0] = sat_add_u64(s, x);
-            st[1 + d.die] = sat_add_u64(st[0], top);
-            done = st[1 + d.die];
-            if (a.tp.die_read_bytes) {  // this thread owns channel c's dies
-                const u64 k = static_cast<u64>(c) * a.tp.dies + d.die;
-                if (a.op[i]) a.tp.die_writes[k] += 1;
-                else a.tp.die_read_bytes[k] += a.bytes[i];
-            }
-        }
-        a.done[i] = done;
-        a.latency[i] = done - arr;
-        a.status[i] = kModeled;
-        ++n_mod;
-        lat += done - arr;
-        mx = done > mx ? done : mx;
-    }
-    for (u32 k = 0; k < a.K; ++k) a.state_out[static_cast<u64>(c) * a.K + k] = st[k];
-    atomicAdd(&a.counters->modeled, n_mod);
-    if (c == 0) {
-        atomicAdd(&a.counters->bypass, n_byp);
-        atomicAdd(&a.counters->foreign, n_for);
-        atomicAdd(&a.counters->unsupported, n_uns);
-        atomicAdd(&a.counters->batches, 1ull);
-        if (a.n) *a.last_arrival = a.arrival[a.n - 1];
-    }
-    atomicAdd(&a.counters->latency_sum, lat);
-    atomicAdd(&a.counters->fast_modeled_ns, fast);
-    atomicMax(&a.counters->max_done, mx);
+    sequential_walk<MODEL>(a.dp, a.tp, a.address, a.bytes, a.op, a.arrival, a.done, a.latency,
+                           a.status, a.n, a.K, a.state_in, a.state_out, a.last_arrival,
+                           a.counters, c);
 }
 
 // Decode-only kernel (A1 + A2), one thread per access.
@@ -2404,6 +2447,22 @@ static_assert(kErrNeedSeq < 256u, "the sequential flag is set by a one-byte mems
 // Launch sequence of one batch: pass 1, range scan, pass 2, then the
 // sequential kernel, which returns at once unless the error word asks for it
 // (set by the host when its tick bound fails, or by pass 1 on the device).
+using PassKernel = void (*)(const PassArgs);
+
+// The pass-2 instantiation for admit-free batches (z), tile halves and the
+// walk in pass 2.
+template <int D>
+static PassKernel pick_replay(bool z, bool halves, bool walk)
+{
+    if (walk)
+        return z ? (halves ? direct_replay_kernel<D, true, true, true>
+                           : direct_replay_kernel<D, true, false, true>)
+                 : (halves ? direct_replay_kernel<D, false, true, true>
+                           : direct_replay_kernel<D, false, false, true>);
+    return z ? (halves ? direct_replay_kernel<D, true, true> : direct_replay_kernel<D, true>)
+             : (halves ? direct_replay_kernel<D, false, true> : direct_replay_kernel<D, false>);
+}
+
 cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
                          const BatchIO& io, const BatchPlan& plan,
                          const BatchScratch& s, bool force_sequential,
@@ -2423,6 +2482,7 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
         err = cudaMemsetAsync(s.error, static_cast<int>(kErrNeedSeq), 1, stream);
         if (err != cudaSuccess) return err;
     }
+    bool walk = false;
     if (!force_sequential) {
         PassArgs a{};
         layout(a, plan.T, plan.L, plan.C, plan.K, tp.dies, plan.group_channels,
@@ -2445,6 +2505,7 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
         a.last_arrival = s.last_arrival;
         a.state_in = s.state_in;
         a.counters = s.counters;
+        a.state_out = s.state_out;
         const bool fast = tp.model == kModelFast;
         using Kernel = void (*)(const PassArgs);
         Kernel p1 = fast ? timing_pass_kernel<kModelFast, 1> : timing_pass_kernel<kModelDie, 1>;
@@ -2496,21 +2557,16 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
                             2 * plan.C * (plan.K + 1) <= static_cast<u32>(kThreads) &&
                             s.ranges_capacity >= 2ull * plan.ctas;
         a.halves = halves ? 1u : 0u;
-        if (halves) {
+        // small batches: pass 2 also runs the sequential walk when it is
+        // needed, instead of a separate launch after it
+        walk = plan.direct && plan.tiles_per_cta == 1;
+        if (plan.direct) {
             const bool z = tp.admit_zero != 0;
             switch (plan.dies) {
-            case 1:
-                p2 = z ? direct_replay_kernel<1, true, true> : direct_replay_kernel<1, false, true>;
-                break;
-            case 2:
-                p2 = z ? direct_replay_kernel<2, true, true> : direct_replay_kernel<2, false, true>;
-                break;
-            case 4:
-                p2 = z ? direct_replay_kernel<4, true, true> : direct_replay_kernel<4, false, true>;
-                break;
-            default:
-                p2 = z ? direct_replay_kernel<8, true, true> : direct_replay_kernel<8, false, true>;
-                break;
+            case 1: p2 = pick_replay<1>(z, halves, walk); break;
+            case 2: p2 = pick_replay<2>(z, halves, walk); break;
+            case 4: p2 = pick_replay<4>(z, halves, walk); break;
+            default: p2 = pick_replay<8>(z, halves, walk); break;
             }
         }
         // direct_fast_kernel runs on a layout of its own
@@ -2584,6 +2640,9 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
         p2<<<plan.ctas, kThreads, plan.smem_bytes, stream>>>(a);
         hooks(kSlotPass2, 1, stream);
     }
+    // the direct pass 2 runs the sequential walk itself when the batch needs
+    // it; the other paths launch it (it returns at once unless needed)
+    if (walk) return cudaGetLastError();
     SeqArgs q{};
     q.dp = dp;
     q.tp = tp;
