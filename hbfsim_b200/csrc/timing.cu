@@ -1342,6 +1342,39 @@ direct_fast_kernel(const PassArgs args)
     const TileSmem s = tile_views(smem, A, 1);
     i64* s_col0 = reinterpret_cast<i64*>(smem + A.off_pm);  // [C][K]
     u32* s_part = reinterpret_cast<u32*>(s.red);            // per-warp channel totals
+    // Stage tile [start, start + nt): full aligned tiles by cp.async (all
+    // copies in flight before any wait), others by plain copies.
+    auto stage = [&](u64 start, u32 nt) {
+        if (nt == T && A.vec) {
+            const uint4* g_addr = reinterpret_cast<const uint4*>(A.address + start);
+            const uint4* g_arr = reinterpret_cast<const uint4*>(A.arrival + start);
+            const uint4* g_bytes = reinterpret_cast<const uint4*>(A.bytes + start);
+            const uint4* g_op = reinterpret_cast<const uint4*>(A.op + start);
+#pragma unroll
+            for (u32 k = tid; k < T / 2; k += kThreads) {
+                cp_async16(reinterpret_cast<uint4*>(s.addr) + k, g_addr + k);
+                cp_async16(reinterpret_cast<uint4*>(s.arr) + k, g_arr + k);
+            }
+#pragma unroll
+            for (u32 k = tid; k < T / 4; k += kThreads)
+                cp_async16(reinterpret_cast<uint4*>(s.bytes) + k, g_bytes + k);
+            if (tid < T / 16) cp_async16(reinterpret_cast<uint4*>(s.op) + tid, g_op + tid);
+            cp_async_commit();
+        } else {
+            for (u32 k = tid; k < nt; k += kThreads) {
+                s.addr[k] = A.address[start + k];
+                s.arr[k] = A.arrival[start + k];
+                s.bytes[k] = A.bytes[start + k];
+                s.op[k] = A.op[start + k];
+            }
+        }
+    };
+    auto tile_size = [&](u64 start) -> u32 {
+        return static_cast<u32>(A.n - start < T ? A.n - start : T);
+    };
+    // the CTA's first tile streams in while the prologue runs
+    const u64 tile_first = static_cast<u64>(blockIdx.x) * A.tiles_per_cta;
+    if (tile_first * T < A.n) stage(tile_first * T, tile_size(tile_first * T));
     // GENERAL with several ranges: the range records in shared memory
     // (layout_fast reserves them when the batch has at most kSmemRanges)
     const bool smem_ranges = GENERAL && A.off_ranges != 0;
@@ -1378,43 +1411,13 @@ direct_fast_kernel(const PassArgs args)
         __syncthreads();
     }
 
-    // Stage tile [start, start + nt): full aligned tiles by cp.async (all
-    // copies in flight before any wait), others by plain copies.
-    auto stage = [&](u64 start, u32 nt) {
-        if (nt == T && A.vec) {
-            const uint4* g_addr = reinterpret_cast<const uint4*>(A.address + start);
-            const uint4* g_arr = reinterpret_cast<const uint4*>(A.arrival + start);
-            const uint4* g_bytes = reinterpret_cast<const uint4*>(A.bytes + start);
-            const uint4* g_op = reinterpret_cast<const uint4*>(A.op + start);
-#pragma unroll
-            for (u32 k = tid; k < T / 2; k += kThreads) {
-                cp_async16(reinterpret_cast<uint4*>(s.addr) + k, g_addr + k);
-                cp_async16(reinterpret_cast<uint4*>(s.arr) + k, g_arr + k);
-            }
-#pragma unroll
-            for (u32 k = tid; k < T / 4; k += kThreads)
-                cp_async16(reinterpret_cast<uint4*>(s.bytes) + k, g_bytes + k);
-            if (tid < T / 16) cp_async16(reinterpret_cast<uint4*>(s.op) + tid, g_op + tid);
-            cp_async_commit();
-        } else {
-            for (u32 k = tid; k < nt; k += kThreads) {
-                s.addr[k] = A.address[start + k];
-                s.arr[k] = A.arrival[start + k];
-                s.bytes[k] = A.bytes[start + k];
-                s.op[k] = A.op[start + k];
-            }
-        }
-    };
-    auto tile_size = [&](u64 start) -> u32 {
-        return static_cast<u32>(A.n - start < T ? A.n - start : T);
-    };
-    const u64 tile_first = static_cast<u64>(blockIdx.x) * A.tiles_per_cta;
-    if (!GENERAL && tile_first * T < A.n) stage(tile_first * T, tile_size(tile_first * T));
     for (u32 tt = 0; tt < A.tiles_per_cta; ++tt) {
         const u64 start = (tile_first + tt) * T;
         if (start >= A.n) break;
         const u32 nt = tile_size(start);
-        if (GENERAL) stage(start, nt);  // the chains' die words overlay the staged addresses
+        // GENERAL: the chains' die words overlay the staged addresses, so
+        // later tiles are staged here, not during the previous chains
+        if (GENERAL && tt > 0) stage(start, nt);
         for (u32 k = lane; k <= C; k += 32) wc[k] = 0;
         if (activity)
             for (u32 k = tid; k < 2 * C * D; k += kThreads) act[k] = 0;
