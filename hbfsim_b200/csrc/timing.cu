@@ -255,7 +255,6 @@ struct PassArgs {
     u32 off_dies[2];                // direct pass 1: die words of the 32-bit chains
     u32 off_xtab;                   // general direct pass 1: transfer ticks of pow2 sizes
     u32 off_mid;                    // halves: each channel's split point (pass 1)
-    u32 off_half;                   // halves: first-half accesses per channel (pass 2)
     u32 halves;                     // one tile per CTA, its two halves separate ranges
     // global scratch
     i64* agg;        // [ctas][C][K][K+1]  (pass 1 out)
@@ -1156,9 +1155,9 @@ struct ColumnItems {
     bool item_on[kItems], coupled[kItems];
     i64 delta[kItems];
 
-    // parts = 2: each channel's segment is split at the first access of the
-    // tile's second half, and each half is a range of its own (one tile
-    // per CTA, 2 C (K+1) <= kThreads items)
+    // parts = 2: each channel's segment is split in the middle (the first
+    // half rounded up), and each half is a range of its own (one tile per
+    // CTA, 2 C (K+1) <= kThreads items)
     __device__ __forceinline__ void init(u32 C, u32 parts = 1)
     {
 #pragma unroll
@@ -1539,8 +1538,8 @@ direct_fast_kernel(const PassArgs args)
                 for (u32 w = 0; w < kWarps; ++w) s.wcnt[w * (C + 1) + c] = offset + pre[w];
                 s.seg[c] = offset;
                 if (c == C - 1) s.seg[C] = offset + tot;
-                // the split point: warps kWarps/2.. hold the tile's second half
-                if (s_mid) s_mid[c] = offset + pre[kWarps / 2];
+                // the split point: the middle of the channel's segment
+                if (s_mid) s_mid[c] = offset + (tot + 1) / 2;
             }
             __syncthreads();
         }
@@ -1643,10 +1642,9 @@ direct_replay_kernel(const PassArgs args)
     }
     prologue(A, s, true, false, false);
 
-    // halves: threads c and C + c replay channel c's first and second half
-    // of the (one) tile, each from its own incoming state
+    // halves: threads c and C + c replay the first and second half of
+    // channel c's segment of the (one) tile, each from its own incoming state
     constexpr u32 parts = HALVES ? 2u : 1u;
-    u32* s_half = HALVES ? reinterpret_cast<u32*>(smem + A.off_half) : nullptr;
     DieRegs<D> reg;
     const bool chain = tid < parts * C;
     if (chain) {
@@ -1668,8 +1666,6 @@ direct_replay_kernel(const PassArgs args)
         const u32 nt = tile_size(start);
         cp_async_wait_all();
         for (u32 c = tid; c <= C; c += kThreads) s.seg[c] = 0;
-        if (HALVES)
-            for (u32 c = tid; c < C; c += kThreads) s_half[c] = 0;
         __syncthreads();
         // unpack: sorted copy, access -> slot, statuses, untimed outputs
         for (u32 j = tid; j < nt; j += kThreads) {
@@ -1685,7 +1681,6 @@ direct_replay_kernel(const PassArgs args)
                                     : imax(static_cast<i64>(arr), s.chan[r >> 56].admit);
                 slot_of[j] = static_cast<u16>(k);
                 atomicAdd(&s.seg[r >> 56], 1u);
-                if (HALVES && j < T / 2) atomicAdd(&s_half[r >> 56], 1u);
                 ++st.modeled;
             } else {
                 slot_of[j] = 0xffffu;
@@ -1705,8 +1700,10 @@ direct_replay_kernel(const PassArgs args)
         const u32 c = HALVES ? tid % C : tid, part = HALVES ? tid / C : 0u;
         u32 first = chain ? s.seg[c] + c : 0u, last = chain ? s.seg[c + 1] + c : 0u;
         if (HALVES && chain) {
-            if (part == 0) last = s.seg[c] + s_half[c] + c;
-            else first = s.seg[c] + s_half[c] + c;
+            // the middle of the channel's segment, as pass 1 split it
+            const u32 mid = s.seg[c] + (s.seg[c + 1] - s.seg[c] + 1) / 2 + c;
+            if (part == 0) last = mid;
+            else first = mid;
         }
         const ChanInfo ci = chain ? s.chan[c] : ChanInfo{};
         if (first < last &&
@@ -2292,7 +2289,6 @@ static u32 layout(PassArgs& a, u32 T, u32 L, u32 C, u32 K, u32 dies,
         a.off_sarr[1] = take(8 * (T + C));
         a.off_sinfo[1] = take(4 * (T + C));
         a.off_slot = take(2 * T);
-        a.off_half = take(4 * C);
         a.off_dies[1] = 0;
         const u32 end2 = align_up(off, 16);
         return end1 > end2 ? end1 : end2;
@@ -2553,9 +2549,9 @@ cudaError_t launch_batch(const DecodeParams& dp, const TimingParams& tp,
                 break;
             }
         }
-        // One tile per CTA and few column items: the tile's halves are
-        // ranges of their own, so that twice the items and chains (pass 1
-        // and pass 2) each walk half a segment.
+        // One tile per CTA and few column items: each channel's segment is
+        // timed as two ranges (its halves), so that twice the items and
+        // chains (pass 1 and pass 2) each walk half a segment.
         const bool halves = fast_p1 && plan.tiles_per_cta == 1 &&
                             2 * plan.C * (plan.K + 1) <= static_cast<u32>(kThreads) &&
                             s.ranges_capacity >= 2ull * plan.ctas;
