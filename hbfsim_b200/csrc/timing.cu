@@ -2097,9 +2097,26 @@ __global__ void __launch_bounds__(kLbWarps * 32) range_scan_lb_kernel(const Scan
                 x = jstar >= 0 ? __ldcg(b.gstate + (static_cast<u64>(jstar) * C + c) * K + lane)
                                : static_cast<i64>(a.state_in[static_cast<u64>(c) * K + lane]);
             const u32 count = failed ? 0u : kstar;  // groups jstar + 1 .. g - 1
-            for (u32 w = lane; w < count * per; w += 32) {
-                const u32 q = w / per, e = w - q * per;
-                maps[w] = __ldcg(b.gmap + ((static_cast<u64>(jstar) + 1 + q) * C + c) * per + e);
+            // all of their maps in flight before one wait (one L2 round trip,
+            // not one per word the lane copies; from the far die's L2 a round
+            // trip costs about a microsecond): 16-byte copies, a map being
+            // K (K + 1) words (an even count), when the maps start on a
+            // 16-byte boundary (the static entry's scratch may put them 8
+            // bytes off it: plain loads then)
+            if ((reinterpret_cast<std::uintptr_t>(b.gmap) & 15u) == 0) {
+                const u32 halves = per / 2;
+                for (u32 w = lane; w < count * halves; w += 32) {
+                    const u32 q = w / halves, e = 2 * (w - q * halves);
+                    cp_async16(maps + static_cast<u64>(q) * per + e,
+                               b.gmap + ((static_cast<u64>(jstar) + 1 + q) * C + c) * per + e);
+                }
+                cp_async_commit();
+                cp_async_wait_all();
+            } else {
+                for (u32 w = lane; w < count * per; w += 32) {
+                    const u32 q = w / per, e = w - q * per;
+                    maps[w] = __ldcg(b.gmap + ((static_cast<u64>(jstar) + 1 + q) * C + c) * per + e);
+                }
             }
             __syncwarp();
             for (u32 q = 0; q < count; ++q) x = apply_map(maps + static_cast<u64>(q) * per, x, K);
