@@ -2097,12 +2097,12 @@ __global__ void __launch_bounds__(kLbWarps * 32) range_scan_lb_kernel(const Scan
                 x = jstar >= 0 ? __ldcg(b.gstate + (static_cast<u64>(jstar) * C + c) * K + lane)
                                : static_cast<i64>(a.state_in[static_cast<u64>(c) * K + lane]);
             const u32 count = failed ? 0u : kstar;  // groups jstar + 1 .. g - 1
-            // all of their maps in flight before one wait (one L2 round trip,
-            // not one per word the lane copies; from the far die's L2 a round
-            // trip costs about a microsecond): 16-byte copies, a map being
-            // K (K + 1) words (an even count), when the maps start on a
-            // 16-byte boundary (the static entry's scratch may put them 8
-            // bytes off it: plain loads then)
+            // all of their maps in flight before one wait: one L2 round trip
+            // instead of one per word the lane copies, which had made this
+            // fetch the slowest step of the scan's late groups.  16-byte
+            // copies (a map is K (K + 1) words, an even count) when the maps
+            // start on a 16-byte boundary; the static entry's scratch may put
+            // them 8 bytes off it, and plain loads take that case.
             if ((reinterpret_cast<std::uintptr_t>(b.gmap) & 15u) == 0) {
                 const u32 halves = per / 2;
                 for (u32 w = lane; w < count * halves; w += 32) {
